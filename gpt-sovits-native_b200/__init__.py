@@ -1,0 +1,175 @@
+"""gsv_b200 — Python view of libgsvk.so, the B200 build of the GPT-SoVITS-native
+`src/kern` GEMM/GEMV hot path.
+
+Everything here is a thin ctypes layer over the C ABI declared in
+include/gsvk.h; all arithmetic happens in the CUDA kernels of libgsvk.so.
+There is no CPU fallback: if libgsvk.so is missing or no sm_100 device is
+present, calls raise.
+
+Tensors are torch CUDA tensors (torch is used for device memory and streams
+only).  fp16 bit patterns travel as torch.float16 tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_char, c_double, c_float, c_int, c_size_t, c_void_p
+
+from . import workloads  # noqa: F401  (seeded synthetic inputs)
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libgsvk.so")
+
+ACT_NONE, ACT_RELU, ACT_GELU_ERF, ACT_LEAKY = 0, 1, 2, 3
+STATUS = {0: "OK", -1: "INVALID", -2: "ALIGN", -3: "CUDA", -4: "TIMEOUT", -5: "UNSUPPORTED",
+          -6: "NOMEM", -7: "NODEV"}
+
+
+class GsvkError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"gsvk error {code} ({STATUS.get(code, '?')}): {msg}")
+        self.code = code
+
+
+_lib = None
+
+# name -> (restype, argtypes); the exported surface of include/gsvk.h.
+_vp, _sz = c_void_p, c_size_t
+SIGNATURES = {
+    "gsvk_version": (c_int, []),
+    "gsvk_last_error": (ctypes.c_char_p, []),
+    "gsvk_device_init": (c_int, [c_int]),
+    "gsvk_available": (c_int, []),
+    "gsvk_f32_to_f16": (c_int, [_vp, _vp, _sz, _vp]),
+    "gsvk_f16_to_f32": (c_int, [_vp, _vp, _sz, _vp]),
+    "gsvk_gemv_f16w_f32acc": (c_int, [_vp, _vp, _vp, _sz, _sz, _vp]),
+    "gsvk_gemv_f16x_fmlal": (c_int, [_vp, _vp, _vp, _sz, _sz, _vp]),
+    "gsvk_gemv_ex": (c_int, [_vp, _vp, c_int, _vp, _vp, _sz, _sz, _vp, _vp, c_int, c_float, _vp]),
+    "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
+    "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
+    "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
+}
+
+
+def lib():
+    """Load libgsvk.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} not built: run `make -C {_HERE}` "
+                              "(or __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().gsvk_last_error().decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        raise GsvkError(rc, last_error())
+
+
+def device_init(device: int = 0) -> None:
+    check(lib().gsvk_device_init(device))
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("gsvk takes CUDA tensors")
+    if not t.is_contiguous():
+        raise ValueError("gsvk takes contiguous tensors")
+    return t.data_ptr()
+
+
+def _stream(stream):
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+# ---------------------------------------------------------------------- a4
+def f32_to_f16(src, dst=None, stream=None):
+    import torch
+
+    dst = dst if dst is not None else torch.empty(src.shape, dtype=torch.float16, device=src.device)
+    check(lib().gsvk_f32_to_f16(_ptr(src), _ptr(dst), src.numel(), _stream(stream)))
+    return dst
+
+
+def f16_to_f32(src, dst=None, stream=None):
+    import torch
+
+    dst = dst if dst is not None else torch.empty(src.shape, dtype=torch.float32, device=src.device)
+    check(lib().gsvk_f16_to_f32(_ptr(src), _ptr(dst), src.numel(), _stream(stream)))
+    return dst
+
+
+# ------------------------------------------------------------------ a1, a2
+def gemv_f16w_f32acc(w, x, y=None, stream=None):
+    """kern::gemv_f16w_f32acc: y[out] = W[out,in] (fp16) . x[in] (fp32)."""
+    import torch
+
+    out_, in_ = w.shape
+    y = y if y is not None else torch.empty(out_, dtype=torch.float32, device=w.device)
+    check(lib().gsvk_gemv_f16w_f32acc(_ptr(w), _ptr(x), _ptr(y), out_, in_, _stream(stream)))
+    return y
+
+
+def gemv_f16x_fmlal(w, xh, y=None, stream=None):
+    """kern::gemv_f16x_fmlal: fp16 x, fp32 accumulate."""
+    import torch
+
+    out_, in_ = w.shape
+    y = y if y is not None else torch.empty(out_, dtype=torch.float32, device=w.device)
+    check(lib().gsvk_gemv_f16x_fmlal(_ptr(w), _ptr(xh), _ptr(y), out_, in_, _stream(stream)))
+    return y
+
+
+def gemv_ex(w, x, bias=None, residual=None, act=ACT_NONE, slope=0.0, y=None, y_f16=None,
+            stream=None):
+    import torch
+
+    out_, in_ = w.shape
+    if y is None and y_f16 is None:
+        y = torch.empty(out_, dtype=torch.float32, device=w.device)
+    check(lib().gsvk_gemv_ex(_ptr(w), _ptr(x), int(x.dtype == torch.float16), _ptr(y), _ptr(y_f16),
+                             out_, in_, _ptr(bias), _ptr(residual), act, slope, _stream(stream)))
+    return y if y is not None else y_f16
+
+
+# --------------------------------------------------------------------- a22
+def layernorm_rows(x, g, b, eps, y=None, stream=None):
+    import torch
+
+    n = x.shape[-1]
+    y = y if y is not None else torch.empty_like(x)
+    check(lib().gsvk_layernorm_rows(_ptr(x), _ptr(g), _ptr(b), _ptr(y), x.numel() // n, n, eps,
+                                    _stream(stream)))
+    return y
+
+
+def softmax_rows(x, y=None, stream=None):
+    import torch
+
+    n = x.shape[-1]
+    y = y if y is not None else torch.empty_like(x)
+    check(lib().gsvk_softmax_rows(_ptr(x), _ptr(y), x.numel() // n, n, _stream(stream)))
+    return y
+
+
+def activation(x, act, slope=0.0, y=None, stream=None):
+    import torch
+
+    y = y if y is not None else torch.empty_like(x)
+    check(lib().gsvk_activation(_ptr(x), _ptr(y), x.numel(), act, slope, _stream(stream)))
+    return y

@@ -1,0 +1,79 @@
+// common.cuh — shared host/device helpers for the sm_100a kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gsvk.h"
+
+namespace gsvk {
+
+// ------------------------------------------------------------------ host side
+// Records a printf-style message as the calling thread's last error and
+// returns `code` (used as `return fail(GSVK_ERR_INVALID, "...")`).
+int fail(int code, const char* fmt, ...);
+// Converts a CUDA error into GSVK_ERR_CUDA with context; GSVK_OK otherwise.
+int check_cuda(cudaError_t e, const char* what);
+// cudaGetLastError after a launch.
+int check_launch(const char* kernel);
+// Device properties of the device current on the calling thread.
+int sm_count();
+
+inline cudaStream_t as_cuda(gsvk_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline unsigned ceil_div(size_t a, size_t b) { return static_cast<unsigned>((a + b - 1) / b); }
+
+// ---------------------------------------------------------------- device side
+__device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+__device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
+
+// Streaming 128-bit load that bypasses L1 allocation (weights are read once
+// per launch; keeping them out of L1 leaves it to the reused activations).
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// 8 packed fp16 (one uint4) -> 8 fp32.
+__device__ __forceinline__ void unpack8(const uint4& v, float* f) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Epilogue activation (GSVK_ACT_*), identical expressions to the reference:
+// relu kern.cpp:85, gelu_erf bert_ops.hpp:25, leaky nn_ops.hpp:48.
+__device__ __forceinline__ float apply_act(float v, int act, float slope) {
+  switch (act) {
+    case GSVK_ACT_RELU: return v > 0.f ? v : 0.f;
+    case GSVK_ACT_GELU_ERF: return 0.5f * v * (1.f + erff(v * 0.70710678118654752440f));
+    case GSVK_ACT_LEAKY: return v < 0.f ? v * slope : v;
+    default: return v;
+  }
+}
+
+}  // namespace gsvk

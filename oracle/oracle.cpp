@@ -1,0 +1,718 @@
+// oracle.cpp — CPU restatement of the reference `src/kern` hot path and its
+// callers.  TEST INFRASTRUCTURE: the parity checker and the timed CPU
+// baseline; the CUDA product path never links it.
+//
+// Built with -ffp-contract=off so that every fused multiply-add below is an
+// explicit fmaf() exactly where the reference issues one (vfmaq_f32 /
+// vfmlalq_*), and every separate multiply/add is rounded separately where the
+// reference rounds separately (vmulq_f32 + vaddq_f32).
+//
+// NEON horizontal sums (vaddvq_f32) are restated as (l0 + l1) + (l2 + l3),
+// the AArch64 FADDP pairwise order.
+#include "oracle.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <condition_variable>
+#include <cstring>
+#include <functional>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+namespace {
+
+// ---------------------------------------------------------------- fp16 bits
+inline float h2f(uint16_t b) {
+  _Float16 h;
+  std::memcpy(&h, &b, 2);
+  return static_cast<float>(h);
+}
+inline uint16_t f2h(float v) {
+  const _Float16 h = static_cast<_Float16>(v);  // IEEE RNE
+  uint16_t b;
+  std::memcpy(&b, &h, 2);
+  return b;
+}
+inline float round_f16(float v) { return h2f(f2h(v)); }
+
+inline float vaddv4(const float* l) { return (l[0] + l[1]) + (l[2] + l[3]); }
+
+// ---------------------------------------------------------------- thread pool
+// Persistent workers pulling fixed-size chunks; the restatement of
+// rt::parallel_for (runtime/threadpool.hpp:141).  Results never depend on the
+// partition: every output element is computed by exactly one chunk with a
+// fixed arithmetic order.
+class Pool {
+ public:
+  ~Pool() { resize(0); }
+
+  void resize(int n) {
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      quit_ = true;
+      ++gen_;
+    }
+    cv_.notify_all();
+    for (auto& t : th_) t.join();
+    th_.clear();
+    quit_ = false;
+    nthreads_ = std::max(1, n);
+    for (int i = 1; i < nthreads_; ++i) th_.emplace_back([this] { loop(); });
+  }
+  int size() const { return nthreads_; }
+
+  void run(size_t n, size_t grain, const std::function<void(size_t, size_t)>& fn) {
+    if (n == 0) return;
+    if (grain == 0) grain = 1;
+    if (nthreads_ <= 1 || n <= grain) {
+      fn(0, n);
+      return;
+    }
+    std::unique_lock<std::mutex> call_lk(call_mu_);
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      fn_ = &fn;
+      n_ = n;
+      grain_ = grain;
+      next_.store(0);
+      active_ = static_cast<int>(th_.size());
+      ++gen_;
+    }
+    cv_.notify_all();
+    work();
+    std::unique_lock<std::mutex> lk(mu_);
+    done_cv_.wait(lk, [this] { return active_ == 0; });
+    fn_ = nullptr;
+  }
+
+ private:
+  void work() {
+    for (;;) {
+      const size_t b = next_.fetch_add(grain_);
+      if (b >= n_) break;
+      (*fn_)(b, std::min(n_, b + grain_));
+    }
+  }
+  void loop() {
+    uint64_t seen = 0;
+    {
+      std::unique_lock<std::mutex> lk(mu_);
+      seen = gen_;
+    }
+    for (;;) {
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return gen_ != seen; });
+        seen = gen_;
+        if (quit_) return;
+      }
+      work();
+      std::unique_lock<std::mutex> lk(mu_);
+      if (--active_ == 0) done_cv_.notify_all();
+    }
+  }
+
+  std::vector<std::thread> th_;
+  std::mutex mu_, call_mu_;
+  std::condition_variable cv_, done_cv_;
+  const std::function<void(size_t, size_t)>* fn_ = nullptr;
+  size_t n_ = 0, grain_ = 1;
+  std::atomic<size_t> next_{0};
+  int active_ = 0;
+  uint64_t gen_ = 0;
+  bool quit_ = false;
+  int nthreads_ = 1;
+};
+
+Pool& pool() {
+  static Pool p;
+  return p;
+}
+
+// Row-band split over all workers: grain = ceil(rows / workers)
+// (gemv.cpp:117-126, gemv_fmlal.cpp:117-129).
+void row_bands(size_t rows, const std::function<void(size_t, size_t)>& fn) {
+  const size_t workers = static_cast<size_t>(pool().size());
+  const size_t grain = (rows + workers - 1) / workers;
+  pool().run(rows, grain, fn);
+}
+
+// ------------------------------------------------ gemv_f16w_f32acc (gemv.cpp)
+// gemv.cpp:36-109: 4 rows at a time, each row with two 4-lane accumulators
+// fed by FMA over 8-element chunks, scalar FMA tail.
+void gemv_f16w_rows(const uint16_t* w, const float* x, float* y, size_t rb,
+                    size_t re, size_t in) {
+  const size_t vec_end = in & ~size_t{7};
+  size_t r = rb;
+  for (; r + 4 <= re; r += 4) {
+    float acc[4][8];
+    for (auto& a : acc)
+      for (float& v : a) v = 0.f;
+    for (size_t i = 0; i < vec_end; i += 8) {
+      for (int q = 0; q < 4; ++q) {
+        const uint16_t* wr = w + (r + q) * in + i;
+        for (int l = 0; l < 8; ++l) acc[q][l] = std::fmaf(h2f(wr[l]), x[i + l], acc[q][l]);
+      }
+    }
+    float s[4];
+    for (int q = 0; q < 4; ++q) {
+      float t[4];
+      for (int l = 0; l < 4; ++l) t[l] = acc[q][l] + acc[q][4 + l];  // vaddq
+      s[q] = vaddv4(t);
+    }
+    for (size_t i = vec_end; i < in; ++i)
+      for (int q = 0; q < 4; ++q) s[q] = std::fmaf(h2f(w[(r + q) * in + i]), x[i], s[q]);
+    for (int q = 0; q < 4; ++q) y[r + q] = s[q];
+  }
+  for (; r < re; ++r) {
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const uint16_t* wr = w + r * in;
+    for (size_t i = 0; i < vec_end; i += 8)
+      for (int l = 0; l < 8; ++l) a[l] = std::fmaf(h2f(wr[i + l]), x[i + l], a[l]);
+    float s = vaddv4(a) + vaddv4(a + 4);
+    for (size_t i = vec_end; i < in; ++i) s = std::fmaf(h2f(wr[i]), x[i], s);
+    y[r] = s;
+  }
+}
+
+// ------------------------------------------- gemv_f16x_fmlal (gemv_fmlal.cpp)
+// gemv_fmlal.cpp:40-109: 8 accumulators x 4 lanes over 64-element steps; each
+// accumulator takes the low then the high half of its 8-element slice.
+float row_dot_fmlal(const uint16_t* wr, const uint16_t* xh, size_t in) {
+  const size_t vec_end = in & ~size_t{63};
+  float a[8][4];
+  for (auto& v : a)
+    for (float& z : v) z = 0.f;
+  size_t i = 0;
+  for (; i < vec_end; i += 64) {
+    for (int j = 0; j < 8; ++j) {
+      const size_t o = i + 8 * j;
+      for (int l = 0; l < 4; ++l) a[j][l] = std::fmaf(h2f(wr[o + l]), h2f(xh[o + l]), a[j][l]);
+      for (int l = 0; l < 4; ++l)
+        a[j][l] = std::fmaf(h2f(wr[o + 4 + l]), h2f(xh[o + 4 + l]), a[j][l]);
+    }
+  }
+  float s = vaddv4(a[0]);
+  for (int j = 1; j < 8; ++j) s = s + vaddv4(a[j]);
+  for (; i < in; ++i) s = s + h2f(wr[i]) * h2f(xh[i]);  // exact product
+  return s;
+}
+
+// -------------------------------------------- gemm_f16x_fmlal tile4 kernel
+// gemv_fmlal.cpp:140-185: per (m, n) one 4-lane accumulator; 8-element K
+// steps (low then high half), the K tail accumulated into lane 0.
+void gemm_f16_tile4(const uint16_t* a, const uint16_t* b, float* c, size_t M,
+                    size_t N, size_t K) {
+  const size_t vec_end = K & ~size_t{7};
+  for (size_t m = 0; m < M; ++m) {
+    const uint16_t* ar = a + m * K;
+    for (size_t n = 0; n < N; ++n) {
+      const uint16_t* br = b + n * K;
+      float acc[4] = {0, 0, 0, 0};
+      for (size_t k = 0; k < vec_end; k += 8) {
+        for (int l = 0; l < 4; ++l) acc[l] = std::fmaf(h2f(ar[k + l]), h2f(br[k + l]), acc[l]);
+        for (int l = 0; l < 4; ++l)
+          acc[l] = std::fmaf(h2f(ar[k + 4 + l]), h2f(br[k + 4 + l]), acc[l]);
+      }
+      for (size_t k = vec_end; k < K; ++k) acc[0] = acc[0] + h2f(ar[k]) * h2f(br[k]);
+      c[m * N + n] = vaddv4(acc);
+    }
+  }
+}
+
+// fp32 dot with one FMA chain (the restated sgemm kernel).
+inline float dot_f32_f16w(const uint16_t* w, const float* x, size_t n) {
+  float s = 0.f;
+  for (size_t i = 0; i < n; ++i) s = std::fmaf(h2f(w[i]), x[i], s);
+  return s;
+}
+
+// --------------------------------------------------------- T2S attention dots
+// t2s_engine.cpp:69-99 dot_f16kv: 4 accumulators x 4 lanes over 16-element
+// chunks, tree (a0+a1)+(a2+a3), then (s0+s2)+(s1+s3).
+float dot_f16kv(const float* q, const uint16_t* k16, size_t HD) {
+  float a[4][4];
+  for (auto& v : a)
+    for (float& z : v) z = 0.f;
+  size_t e = 0;
+  for (; e + 16 <= HD; e += 16)
+    for (int j = 0; j < 4; ++j)
+      for (int l = 0; l < 4; ++l)
+        a[j][l] = std::fmaf(q[e + 4 * j + l], h2f(k16[e + 4 * j + l]), a[j][l]);
+  float s[4];
+  for (int l = 0; l < 4; ++l) s[l] = (a[0][l] + a[1][l]) + (a[2][l] + a[3][l]);
+  float dot = (s[0] + s[2]) + (s[1] + s[3]);
+  for (; e < HD; ++e) dot = std::fmaf(q[e], h2f(k16[e]), dot);
+  return dot;
+}
+
+// t2s_engine.cpp:126-145 accum_f16kv: ov += p * v with separate mul and add.
+void accum_f16kv(float* ov, const uint16_t* v16, float p, size_t HD) {
+  for (size_t e = 0; e < HD; ++e) {
+    const float t = p * h2f(v16[e]);
+    ov[e] = ov[e] + t;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+void ora_set_threads(int n) { pool().resize(n); }
+int ora_get_threads(void) { return pool().size(); }
+
+void ora_f32_to_f16(const float* src, uint16_t* dst, size_t n) {
+  for (size_t i = 0; i < n; ++i) dst[i] = f2h(src[i]);
+}
+void ora_f16_to_f32(const uint16_t* src, float* dst, size_t n) {
+  for (size_t i = 0; i < n; ++i) dst[i] = h2f(src[i]);
+}
+
+void ora_gemv_f16w_f32acc_ref(const uint16_t* w, const float* x, float* y, size_t out,
+                              size_t in) {
+  for (size_t r = 0; r < out; ++r) {
+    float s = 0.f;
+    for (size_t i = 0; i < in; ++i) s = s + h2f(w[r * in + i]) * x[i];
+    y[r] = s;
+  }
+}
+
+void ora_gemv_f16w_f32acc(const uint16_t* w, const float* x, float* y, size_t out, size_t in) {
+  if (out * in < (size_t{1} << 18)) {  // gemv.cpp:114
+    gemv_f16w_rows(w, x, y, 0, out, in);
+    return;
+  }
+  row_bands(out, [&](size_t b, size_t e) { gemv_f16w_rows(w, x, y, b, e, in); });
+}
+
+void ora_gemv_f16x_fmlal(const uint16_t* w, const uint16_t* xh, float* y, size_t out,
+                         size_t in) {
+  if (out * in < (size_t{1} << 18)) {  // gemv_fmlal.cpp:116
+    for (size_t r = 0; r < out; ++r) y[r] = row_dot_fmlal(w + r * in, xh, in);
+    return;
+  }
+  row_bands(out, [&](size_t b, size_t e) {
+    for (size_t r = b; r < e; ++r) y[r] = row_dot_fmlal(w + r * in, xh, in);
+  });
+}
+
+void ora_gemm_f16x_fmlal(const uint16_t* a, const uint16_t* b, float* c, size_t M, size_t N,
+                         size_t K) {
+  if (M * N * K < (size_t{1} << 20)) {  // gemv_fmlal.cpp:190
+    gemm_f16_tile4(a, b, c, M, N, K);
+    return;
+  }
+  const size_t workers = static_cast<size_t>(pool().size());
+  size_t mblock = (M + workers - 1) / workers;
+  mblock = (mblock + 3) & ~size_t{3};  // gemv_fmlal.cpp:197
+  pool().run(M, mblock, [&](size_t mb, size_t me) {
+    gemm_f16_tile4(a + mb * K, b, c + mb * N, me - mb, N, K);
+  });
+}
+
+void ora_sgemm(char transa, char transb, int M, int N, int K, float alpha, const float* A,
+               int lda, const float* B, int ldb, float beta, float* C, int ldc) {
+  const bool ta = transa == 'T' || transa == 't';
+  const bool tb = transb == 'T' || transb == 't';
+  pool().run(static_cast<size_t>(M), 1, [&](size_t mb, size_t me) {
+    for (size_t i = mb; i < me; ++i)
+      for (int j = 0; j < N; ++j) {
+        float s = 0.f;
+        for (int k = 0; k < K; ++k) {
+          const float av = ta ? A[static_cast<size_t>(k) * lda + i] : A[i * lda + k];
+          const float bv = tb ? B[static_cast<size_t>(j) * ldb + k] : B[static_cast<size_t>(k) * ldb + j];
+          s = std::fmaf(av, bv, s);
+        }
+        float& cv = C[i * ldc + j];
+        cv = beta == 0.f ? alpha * s : alpha * s + beta * cv;
+      }
+  });
+}
+
+// ----------------------------------------------------------------- primitives
+void ora_layernorm(const float* x, const float* g, const float* b, float* y, size_t n,
+                   double eps) {
+  const size_t vec_end = n & ~size_t{7};
+  float s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0}, q0[4] = {0, 0, 0, 0}, q1[4] = {0, 0, 0, 0};
+  size_t i = 0;
+  for (; i < vec_end; i += 8)
+    for (int l = 0; l < 4; ++l) {
+      s0[l] = s0[l] + x[i + l];
+      s1[l] = s1[l] + x[i + 4 + l];
+      q0[l] = std::fmaf(x[i + l], x[i + l], q0[l]);
+      q1[l] = std::fmaf(x[i + 4 + l], x[i + 4 + l], q1[l]);
+    }
+  double sum = static_cast<double>(vaddv4(s0) + vaddv4(s1));
+  double sqsum = static_cast<double>(vaddv4(q0) + vaddv4(q1));
+  for (; i < n; ++i) {
+    sum += x[i];
+    sqsum += static_cast<double>(x[i]) * x[i];
+  }
+  const double dn = static_cast<double>(n);
+  const float mean = static_cast<float>(sum / dn);
+  float var = static_cast<float>(sqsum / dn - static_cast<double>(mean) * mean);
+  if (!(var >= 0.0f)) {  // kern.cpp:45-52 two-pass fallback
+    double s2 = 0;
+    for (size_t j = 0; j < n; ++j) {
+      const double d = static_cast<double>(x[j]) - mean;
+      s2 += d * d;
+    }
+    var = static_cast<float>(s2 / dn);
+  }
+  const float rstd = static_cast<float>(1.0 / std::sqrt(static_cast<double>(var) + eps));
+  for (size_t j = 0; j < n; ++j) y[j] = std::fmaf((x[j] - mean) * rstd, g[j], b[j]);
+}
+
+void ora_rmsnorm(const float* x, const float* g, float* y, size_t n, double eps) {
+  const size_t vec_end = n & ~size_t{7};
+  float s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+  size_t i = 0;
+  for (; i < vec_end; i += 8)
+    for (int l = 0; l < 4; ++l) {
+      s0[l] = std::fmaf(x[i + l], x[i + l], s0[l]);
+      s1[l] = std::fmaf(x[i + 4 + l], x[i + 4 + l], s1[l]);
+    }
+  float ss = vaddv4(s0) + vaddv4(s1);
+  for (; i < n; ++i) ss = ss + x[i] * x[i];
+  const float inv_rms = static_cast<float>(1.0 / std::sqrt(ss / static_cast<double>(n) + eps));
+  for (size_t j = 0; j < n; ++j) y[j] = x[j] * inv_rms * g[j];
+}
+
+void ora_softmax(const float* x, float* y, size_t n) {
+  float m = x[0];
+  for (size_t i = 1; i < n; ++i) m = m < x[i] ? x[i] : m;
+  float sum = 0.f;
+  for (size_t i = 0; i < n; ++i) {
+    const float e = std::exp(x[i] - m);
+    y[i] = e;
+    sum = sum + e;
+  }
+  const float inv = 1.0f / sum;
+  for (size_t i = 0; i < n; ++i) y[i] = y[i] * inv;
+}
+
+void ora_relu(const float* x, float* y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = x[i] > 0.0f ? x[i] : 0.0f;
+}
+void ora_silu(const float* x, float* y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = x[i] / (1.0f + std::exp(-x[i]));
+}
+void ora_gelu_erf(const float* x, float* y, size_t n) {
+  for (size_t i = 0; i < n; ++i) y[i] = 0.5f * x[i] * (1.f + std::erf(x[i] * 0.70710678118654752440f));
+}
+void ora_leaky_relu(const float* x, float* y, size_t n, float slope) {
+  for (size_t i = 0; i < n; ++i) y[i] = x[i] < 0.f ? x[i] * slope : x[i];
+}
+
+static void apply_act(float* v, size_t n, int act, float slope) {
+  switch (act) {
+    case ORA_ACT_RELU: ora_relu(v, v, n); break;
+    case ORA_ACT_GELU_ERF: ora_gelu_erf(v, v, n); break;
+    case ORA_ACT_LEAKY: ora_leaky_relu(v, v, n, slope); break;
+    default: break;
+  }
+}
+
+void ora_linear_f16(const float* x, size_t T, size_t in, const uint16_t* w, size_t out,
+                    const float* bias, int act, float slope, float* y) {
+  std::vector<uint16_t> xh(T * in);
+  ora_f32_to_f16(x, xh.data(), T * in);
+  ora_gemm_f16x_fmlal(xh.data(), w, y, T, out, in);
+  if (bias)
+    for (size_t t = 0; t < T; ++t)
+      for (size_t o = 0; o < out; ++o) y[t * out + o] = y[t * out + o] + bias[o];
+  apply_act(y, T * out, act, slope);
+}
+
+// ---------------------------------------------------------------- convolutions
+void ora_conv1d(const float* x, size_t Ci, size_t T, const uint16_t* w, const float* bias,
+                size_t Co, size_t k, size_t dil, int round_in, float* y) {
+  const size_t K = Ci * k;
+  const long long pad_l = static_cast<long long>((k - 1) * dil) / 2;  // conv1d.hpp:165
+  // im2col col[(i*k+kk), t] (conv1d.hpp:166-176), optionally fp16-rounded.
+  std::vector<float> col(K * T);
+  for (size_t i = 0; i < Ci; ++i)
+    for (size_t kk = 0; kk < k; ++kk)
+      for (size_t t = 0; t < T; ++t) {
+        const long long src = static_cast<long long>(t) + static_cast<long long>(kk * dil) - pad_l;
+        float v = (src >= 0 && src < static_cast<long long>(T)) ? x[i * T + src] : 0.f;
+        col[(i * k + kk) * T + t] = round_in ? round_f16(v) : v;
+      }
+  std::vector<float> wf(Co * K);
+  ora_f16_to_f32(w, wf.data(), Co * K);
+  pool().run(Co, 1, [&](size_t cb, size_t ce) {
+    std::vector<float> acc(T);
+    for (size_t o = cb; o < ce; ++o) {
+      std::fill(acc.begin(), acc.end(), 0.f);
+      for (size_t kk = 0; kk < K; ++kk) {
+        const float wv = wf[o * K + kk];
+        const float* cr = col.data() + kk * T;
+        for (size_t t = 0; t < T; ++t) acc[t] = std::fmaf(wv, cr[t], acc[t]);
+      }
+      const float bv = bias ? bias[o] : 0.f;
+      for (size_t t = 0; t < T; ++t) y[o * T + t] = acc[t] + bv;  // add_bias (conv1d.hpp:196)
+    }
+  });
+}
+
+void ora_convt1d(const float* x, size_t Ci, size_t T, const uint16_t* w, const float* bias,
+                 size_t Co, size_t k, size_t u, int round_in, float* y) {
+  const long long pad = static_cast<long long>((k - u) / 2);  // conv1d.hpp:263
+  const size_t Tout = T * u;
+  std::vector<float> xr(Ci * T);
+  for (size_t i = 0; i < Ci * T; ++i) xr[i] = round_in ? round_f16(x[i]) : x[i];
+  // phase weights wd[d][o][i] = W[i,o,d] (conv1d.hpp:226-232)
+  std::vector<float> wd(k * Co * Ci);
+  for (size_t d = 0; d < k; ++d)
+    for (size_t o = 0; o < Co; ++o)
+      for (size_t i = 0; i < Ci; ++i) wd[(d * Co + o) * Ci + i] = h2f(w[(i * Co + o) * k + d]);
+  pool().run(Co, 1, [&](size_t cb, size_t ce) {
+    std::vector<float> tmp(T);
+    for (size_t o = cb; o < ce; ++o) {
+      float* yr = y + o * Tout;
+      std::fill(yr, yr + Tout, 0.f);  // y.reset (conv1d.hpp:265)
+      for (size_t d = 0; d < k; ++d) {
+        // phase GEMM row: tmp[j] = sum_i wd[d][o][i] * x[i][j]
+        std::fill(tmp.begin(), tmp.end(), 0.f);
+        for (size_t i = 0; i < Ci; ++i) {
+          const float wv = wd[(d * Co + o) * Ci + i];
+          const float* xi = xr.data() + i * T;
+          for (size_t j = 0; j < T; ++j) tmp[j] = std::fmaf(wv, xi[j], tmp[j]);
+        }
+        // scatter_raw (conv1d.hpp:347-359)
+        for (size_t j = 0; j < T; ++j) {
+          const long long opos = static_cast<long long>(j * u + d) - pad;
+          if (opos < 0 || opos >= static_cast<long long>(Tout)) continue;
+          yr[opos] = yr[opos] + tmp[j];
+        }
+      }
+      const float bv = bias ? bias[o] : 0.f;
+      for (size_t t = 0; t < Tout; ++t) yr[t] = yr[t] + bv;
+    }
+  });
+}
+
+size_t ora_decoder_out_len(const ora_decoder_cfg* cfg, size_t T) {
+  size_t t = T;
+  for (int s = 0; s < cfg->n_stages; ++s) t *= static_cast<size_t>(cfg->up_rate[s]);
+  return t;
+}
+
+void ora_decoder_forward(const ora_decoder_cfg* cfg, const uint16_t* const* w,
+                         const float* const* b, const float* z, size_t T, int round_in,
+                         float* wav) {
+  size_t C = static_cast<size_t>(cfg->ch0);
+  size_t L = T;
+  std::vector<float> x(C * L);
+  ora_conv1d(z, cfg->in_ch, T, w[0], b[0], C, cfg->conv_pre_k, 1, round_in, x.data());
+  const float kInv = 1.f / 3.f;
+  for (int s = 0; s < cfg->n_stages; ++s) {
+    const size_t base = 1 + static_cast<size_t>(s) * 19;
+    ora_leaky_relu(x.data(), x.data(), x.size(), cfg->lrelu_slope);
+    const size_t Cn = C / 2, Ln = L * cfg->up_rate[s];
+    std::vector<float> xu(Cn * Ln);
+    ora_convt1d(x.data(), C, L, w[base], b[base], Cn, cfg->up_k[s], cfg->up_rate[s], round_in,
+                xu.data());
+    C = Cn;
+    L = Ln;
+    std::vector<float> sum(C * L), cur(C * L), tin(C * L), ta(C * L), tb(C * L);
+    for (int j = 0; j < 3; ++j) {  // dec.hpp:303-335 serial resblock path
+      cur = xu;
+      for (int p = 0; p < 3; ++p) {
+        const size_t i1 = base + 1 + j * 6 + p * 2;
+        ora_leaky_relu(cur.data(), tin.data(), cur.size(), cfg->lrelu_slope);
+        ora_conv1d(tin.data(), C, L, w[i1], b[i1], C, cfg->res_k[j], cfg->res_dil[p], round_in,
+                   ta.data());
+        ora_leaky_relu(ta.data(), ta.data(), ta.size(), cfg->lrelu_slope);
+        ora_conv1d(ta.data(), C, L, w[i1 + 1], b[i1 + 1], C, cfg->res_k[j], 1, round_in,
+                   tb.data());
+        for (size_t i = 0; i < cur.size(); ++i) cur[i] = cur[i] + tb[i];
+      }
+      if (j == 0)
+        for (size_t i = 0; i < sum.size(); ++i) sum[i] = cur[i] * kInv;
+      else
+        for (size_t i = 0; i < sum.size(); ++i) sum[i] = sum[i] + cur[i] * kInv;
+    }
+    x.swap(sum);
+  }
+  ora_leaky_relu(x.data(), x.data(), x.size(), cfg->post_slope);
+  const size_t ip = 1 + static_cast<size_t>(cfg->n_stages) * 19;
+  ora_conv1d(x.data(), C, L, w[ip], b[ip], 1, cfg->conv_post_k, 1, round_in, wav);
+  for (size_t t = 0; t < L; ++t) wav[t] = std::tanh(wav[t]);
+}
+
+// ------------------------------------------------------------------------ T2S
+void ora_t2s_pe_row(int d_model, size_t pos, float* pe) {
+  const size_t D = static_cast<size_t>(d_model);
+  const float log_inc = static_cast<float>(-std::log(10000.0) / static_cast<double>(D));
+  const float p = static_cast<float>(pos);
+  for (size_t d = 0; d < D; d += 2) {
+    const float div = std::exp(static_cast<float>(d) * log_inc);
+    pe[d] = std::sin(p * div);
+    pe[d + 1] = std::cos(p * div);
+  }
+}
+
+void ora_t2s_decode_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l, float* x,
+                          size_t pos, uint16_t* kc, uint16_t* vc) {
+  const size_t D = dm->d_model, H = dm->n_heads, HD = D / H, F = dm->ffn;
+  const size_t len = pos + 1;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(HD));
+  std::vector<float> qkv(3 * D), attn(D, 0.f), xb(D), h(D), ff(F), sc(len);
+  std::vector<uint16_t> xh(std::max(D, F));
+  // QKV: FMLAL GEMV on fp16(x) + bias (t2s_engine.cpp:1044-1050)
+  ora_f32_to_f16(x, xh.data(), D);
+  ora_gemv_f16x_fmlal(w->wqkv + l * 3 * D * D, xh.data(), qkv.data(), 3 * D, D);
+  for (size_t j = 0; j < 3 * D; ++j) qkv[j] = qkv[j] + w->bqkv[l * 3 * D + j];
+  ora_f32_to_f16(qkv.data() + D, kc + pos * D, D);       // :1053-1055
+  ora_f32_to_f16(qkv.data() + 2 * D, vc + pos * D, D);
+  for (size_t hh = 0; hh < H; ++hh) {  // :1062-1087
+    const float* qv = qkv.data() + hh * HD;
+    for (size_t k = 0; k < len; ++k) sc[k] = dot_f16kv(qv, kc + k * D + hh * HD, HD) * scale;
+    ora_softmax(sc.data(), sc.data(), len);
+    float* ov = attn.data() + hh * HD;
+    for (size_t k = 0; k < len; ++k) accum_f16kv(ov, vc + k * D + hh * HD, sc[k], HD);
+  }
+  // out proj + bias + residual + LN1 (:1089-1099)
+  ora_f32_to_f16(attn.data(), xh.data(), D);
+  ora_gemv_f16x_fmlal(w->wout + l * D * D, xh.data(), xb.data(), D, D);
+  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + w->bout[l * D + i];
+  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + x[i];
+  ora_layernorm(xb.data(), w->n1g + l * D, w->n1b + l * D, xb.data(), D, dm->ln_eps);
+  h = xb;
+  // FFN: W1 FMLAL + bias + ReLU, W2 on fp32 activations + bias + residual, LN2
+  ora_f32_to_f16(xb.data(), xh.data(), D);
+  ora_gemv_f16x_fmlal(w->w1 + l * F * D, xh.data(), ff.data(), F, D);
+  for (size_t i = 0; i < F; ++i) ff[i] = ff[i] + w->b1[l * F + i];
+  ora_relu(ff.data(), ff.data(), F);
+  ora_gemv_f16w_f32acc(w->w2 + l * D * F, ff.data(), xb.data(), D, F);
+  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + w->b2[l * D + i];
+  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + h[i];
+  ora_layernorm(xb.data(), w->n2g + l * D, w->n2b + l * D, x, D, dm->ln_eps);
+}
+
+void ora_t2s_prefill_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l, float* x,
+                           size_t S, size_t pos, size_t text_len, uint16_t* kc, uint16_t* vc) {
+  const size_t D = dm->d_model, H = dm->n_heads, HD = D / H, F = dm->ffn;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(HD));
+  std::vector<float> qkv(S * 3 * D), attn(S * D, 0.f), tmp(S * D), ff(S * F);
+  ora_linear_f16(x, S, D, w->wqkv + l * 3 * D * D, 3 * D, w->bqkv + l * 3 * D, ORA_ACT_NONE, 0.f,
+                 qkv.data());
+  for (size_t t = 0; t < S; ++t) {
+    ora_f32_to_f16(qkv.data() + t * 3 * D + D, kc + (pos + t) * D, D);
+    ora_f32_to_f16(qkv.data() + t * 3 * D + 2 * D, vc + (pos + t) * D, D);
+  }
+  pool().run(S * H, 1, [&](size_t wb, size_t we) {
+    std::vector<float> sc(pos + S), pr(pos + S);
+    std::vector<size_t> keys(pos + S);
+    for (size_t item = wb; item < we; ++item) {
+      const size_t hh = item / S, q = item % S;
+      size_t n = 0;
+      for (size_t k = 0; k < pos; ++k) keys[n++] = k;
+      for (size_t k = 0; k < S; ++k)
+        if (k < text_len || k <= q) keys[n++] = pos + k;  // t2s_engine.cpp:947-949
+      const float* qv = qkv.data() + q * 3 * D + hh * HD;
+      for (size_t i = 0; i < n; ++i) sc[i] = dot_f16kv(qv, kc + keys[i] * D + hh * HD, HD) * scale;
+      ora_softmax(sc.data(), pr.data(), n);
+      float* ov = attn.data() + q * D + hh * HD;
+      for (size_t i = 0; i < n; ++i) accum_f16kv(ov, vc + keys[i] * D + hh * HD, pr[i], HD);
+    }
+  });
+  ora_linear_f16(attn.data(), S, D, w->wout + l * D * D, D, nullptr, ORA_ACT_NONE, 0.f, tmp.data());
+  for (size_t i = 0; i < S * D; ++i) x[i] = x[i] + (tmp[i] + w->bout[l * D + i % D]);
+  for (size_t t = 0; t < S; ++t)
+    ora_layernorm(x + t * D, w->n1g + l * D, w->n1b + l * D, x + t * D, D, dm->ln_eps);
+  ora_linear_f16(x, S, D, w->w1 + l * F * D, F, w->b1 + l * F, ORA_ACT_RELU, 0.f, ff.data());
+  ora_linear_f16(ff.data(), S, F, w->w2 + l * D * F, D, nullptr, ORA_ACT_NONE, 0.f, tmp.data());
+  for (size_t i = 0; i < S * D; ++i) x[i] = x[i] + (tmp[i] + w->b2[l * D + i % D]);
+  for (size_t t = 0; t < S; ++t)
+    ora_layernorm(x + t * D, w->n2g + l * D, w->n2b + l * D, x + t * D, D, dm->ln_eps);
+}
+
+int ora_t2s_greedy_sample(float* lg, int V, const int32_t* hist, size_t n_hist,
+                          int eos_allowed, int* raw_argmax) {
+  const int limit = eos_allowed ? V : V - 1;
+  std::vector<unsigned char> mark(static_cast<size_t>(V), 0);
+  for (size_t i = 0; i < n_hist; ++i) {
+    const int c = hist[i];
+    if (c < 0 || c >= limit || mark[c]) continue;
+    mark[c] = 1;
+    float& v = lg[c];
+    v = v < 0.f ? v * 1.35f : v / 1.35f;
+  }
+  if (raw_argmax) {
+    int best = 0;
+    float bv = lg[0];
+    for (int c = 1; c < V; ++c)
+      if (lg[c] > bv) {
+        bv = lg[c];
+        best = c;
+      }
+    *raw_argmax = best;
+  }
+  int best = 0;
+  float bv = lg[0];
+  for (int c = 1; c < limit; ++c)
+    if (lg[c] > bv) {
+      bv = lg[c];
+      best = c;
+    }
+  return best;
+}
+
+int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
+                     uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt, size_t P,
+                     size_t max_steps, int stop_on_eos, int32_t* tokens_out,
+                     float* margins_out) {
+  const size_t D = dm->d_model, L = dm->n_layers, V = dm->vocab;
+  const int eos = static_cast<int>(V) - 1;
+  if (P == 0 || prefix + P + max_steps > cap) return -1;
+  std::vector<float> xy(P * D), pe(D), x1(D), logits(V);
+  for (size_t t = 0; t < P; ++t) {  // t2s_engine.cpp:1785-1790
+    ora_t2s_pe_row(dm->d_model, t, pe.data());
+    const uint16_t* er = w->audio_emb + static_cast<size_t>(prompt[t]) * D;
+    for (size_t d = 0; d < D; ++d) xy[t * D + d] = std::fmaf(dm->alpha_audio, pe[d], h2f(er[d]));
+  }
+  for (size_t l = 0; l < L; ++l)
+    ora_t2s_prefill_layer(dm, w, static_cast<int>(l), xy.data(), P, prefix, 0, kc + l * cap * D,
+                          vc + l * cap * D);
+  ora_gemv_f16w_f32acc(w->wpred, xy.data() + (P - 1) * D, logits.data(), V, D);
+  std::vector<int32_t> hist(prompt, prompt + P);
+  size_t cur = prefix + P;
+  int n_out = 0;
+  for (size_t idx = 0; idx < max_steps; ++idx) {
+    const bool eos_allowed = idx >= 11;  // kEosMaskSteps
+    int raw = -1;
+    const int s = ora_t2s_greedy_sample(logits.data(), static_cast<int>(V), hist.data(),
+                                        hist.size(), eos_allowed, &raw);
+    if (margins_out) {
+      const int limit = eos_allowed ? static_cast<int>(V) : static_cast<int>(V) - 1;
+      float second = -INFINITY;
+      for (int c = 0; c < limit; ++c)
+        if (c != s && logits[c] > second) second = logits[c];
+      margins_out[idx] = logits[s] - second;
+    }
+    bool stop = false;
+    if (stop_on_eos && eos_allowed && s == eos) {
+      stop = true;
+    } else {
+      tokens_out[n_out++] = s;
+      hist.push_back(s);
+    }
+    if (idx + 1 == max_steps) stop = true;
+    if (stop) break;
+    ora_t2s_pe_row(dm->d_model, P + idx, pe.data());  // :1865-1869
+    const uint16_t* er = w->audio_emb + static_cast<size_t>(s) * D;
+    for (size_t d = 0; d < D; ++d) x1[d] = std::fmaf(dm->alpha_audio, pe[d], h2f(er[d]));
+    for (size_t l = 0; l < L; ++l)
+      ora_t2s_decode_layer(dm, w, static_cast<int>(l), x1.data(), cur, kc + l * cap * D,
+                           vc + l * cap * D);
+    ora_gemv_f16w_f32acc(w->wpred, x1.data(), logits.data(), V, D);
+    ++cur;
+  }
+  return n_out;
+}
+
+}  // extern "C"

@@ -1,0 +1,55 @@
+"""The C-ABI library loads and exports every symbol include/gsvk.h declares;
+host-side argument validation (no device needed for the rejected calls)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_symbols():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for fn in os.listdir(inc):
+        if fn.endswith(".h"):
+            src = open(os.path.join(inc, fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(gsvk_[a-z0-9_]+)\s*\(", src))
+    return names
+
+
+def test_library_exports_every_declared_symbol(gsv):
+    L = gsv.lib()
+    missing = [n for n in sorted(declared_symbols()) if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header(gsv):
+    assert declared_symbols() <= set(gsv.SIGNATURES), declared_symbols() - set(gsv.SIGNATURES)
+
+
+def test_version_and_error_text(gsv):
+    assert gsv.lib().gsvk_version() >= 100
+    assert isinstance(gsv.last_error(), str)
+
+
+def test_invalid_arguments_rejected_before_launch(gsv):
+    L = gsv.lib()
+    # null pointers / zero sizes are rejected on the host: no launch happens
+    assert L.gsvk_gemv_f16w_f32acc(None, None, None, 4, 4, None) == -1
+    assert "null" in gsv.last_error()
+    assert L.gsvk_gemv_ex(None, None, 0, None, None, 0, 0, None, None, 0, 0.0, None) == -1
+    assert L.gsvk_layernorm_rows(None, None, None, None, 1, 1, 1e-5, None) == -1
+    assert L.gsvk_activation(None, None, 1, 9, 0.0, None) == -1
+
+
+def test_device_init_without_gpu_fails_cleanly(gsv):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    rc = gsv.lib().gsvk_device_init(0)
+    assert rc == -7  # GSVK_ERR_NODEV
+    assert gsv.lib().gsvk_available() == 0

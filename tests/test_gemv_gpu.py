@@ -1,0 +1,134 @@
+"""GPU parity: decode GEMV (a1, a2), conversions (a4) and support primitives
+(a22) through the C-ABI, against the CPU oracle and the reference goldens.
+
+Tolerances: GEMV against the oracle 2e-5 peak-normalised (test_kern.cpp:104,
+the reference's own gate for reordered fp32 sums) and cos >= 1-1e-10;
+conversions bit-exact; LayerNorm 1e-5 and softmax 1e-6 as the golden tests.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def dev_f16(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.float16)).cuda()
+
+
+def dev_f32(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def rel_err(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return np.abs(got - want).max() / max(np.abs(want).max(), 1e-30)
+
+
+def cos_sim(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+@pytest.mark.parametrize("tag", ["gemv_a", "gemv_b"])
+def test_gemv_golden(dev, golden, tag):
+    w, x, y = golden[f"{tag}_w"], golden[f"{tag}_x"], golden[f"{tag}_y"]
+    got = dev.gemv_f16w_f32acc(dev_f16(w), dev_f32(x)).cpu().numpy()
+    assert rel_err(got, y) <= 2e-5
+    assert cos_sim(got, y) >= 1 - 1e-12
+
+
+T2S_SHAPES = [(1536, 512), (512, 512), (2048, 512), (512, 2048), (1025, 512)]
+ODD_SHAPES = [(17, 131), (3, 8), (1, 1), (64, 7), (33, 131), (4099, 136)]
+
+
+@pytest.mark.parametrize("out_,in_", T2S_SHAPES + ODD_SHAPES + [(24 * 2048, 512)])
+def test_gemv_f32x_matches_oracle(dev, ora, out_, in_):
+    rng = np.random.default_rng(out_ + 3 * in_)
+    w = dev.workloads._f16(rng.standard_normal((out_, in_), dtype=np.float32) * 0.02)
+    x = rng.standard_normal(in_, dtype=np.float32)
+    got = dev.gemv_f16w_f32acc(dev_f16(w), dev_f32(x)).cpu().numpy()
+    ref = ora.gemv_f16w_f32acc(w, x)
+    assert rel_err(got, ref) <= 2e-5
+    assert cos_sim(got, ref) >= 1 - 1e-10
+
+
+@pytest.mark.parametrize("out_,in_", T2S_SHAPES + ODD_SHAPES)
+def test_gemv_f16x_matches_oracle(dev, ora, out_, in_):
+    rng = np.random.default_rng(7 * out_ + in_)
+    w = dev.workloads._f16(rng.standard_normal((out_, in_), dtype=np.float32) * 0.02)
+    xh = dev.workloads._f16(rng.standard_normal(in_, dtype=np.float32))
+    got = dev.gemv_f16x_fmlal(dev_f16(w), dev_f16(xh)).cpu().numpy()
+    ref = ora.gemv_f16x_fmlal(w, xh)
+    assert rel_err(got, ref) <= 2e-5
+
+
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_gemv_fused_epilogue(dev, ora, act):
+    rng = np.random.default_rng(act)
+    out_, in_ = 2048, 512
+    w = dev.workloads._f16(rng.standard_normal((out_, in_), dtype=np.float32) * 0.02)
+    x = rng.standard_normal(in_, dtype=np.float32)
+    b = rng.standard_normal(out_, dtype=np.float32) * 0.1
+    r = rng.standard_normal(out_, dtype=np.float32)
+    yh = torch.empty(out_, dtype=torch.float16, device="cuda")
+    y = dev.gemv_ex(dev_f16(w), dev_f32(x), bias=dev_f32(b), residual=dev_f32(r), act=act,
+                    slope=0.1, y_f16=yh)
+    acc = ora.gemv_f16w_f32acc(w, x) + b
+    acts = {0: lambda v: v, 1: ora.relu, 2: ora.gelu_erf, 3: lambda v: ora.leaky_relu(v, 0.1)}
+    ref = acts[act](acc.astype(np.float32)) + r
+    assert rel_err(y.cpu().numpy(), ref) <= 2e-5
+    np.testing.assert_array_equal(yh.cpu().numpy(), y.cpu().numpy().astype(np.float16))
+
+
+def test_gemv_rejects_bad_args(dev):
+    w = torch.zeros(4, 4, dtype=torch.float16, device="cuda")
+    assert dev.lib().gsvk_gemv_f16w_f32acc(w.data_ptr(), None, None, 4, 4, None) == -1
+    with pytest.raises(dev.GsvkError):
+        dev.gemv_f16w_f32acc(w, torch.zeros(0, device="cuda"))
+    rc = dev.lib().gsvk_gemv_f16w_f32acc(w.data_ptr(), w.data_ptr(), None, 4, 4, None)
+    assert rc == -1
+
+
+def test_f32_f16_conversions_bit_exact(dev, ora):
+    rng = np.random.default_rng(9)
+    x = np.concatenate([rng.standard_normal(10001, dtype=np.float32) * 100,
+                        np.array([1.0 + 2 ** -11, 65520.0, -0.0, 1e-8, 6.1e-5], np.float32)])
+    h = dev.f32_to_f16(dev_f32(x)).cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(h, ora.f32_to_f16(x))
+    back = dev.f16_to_f32(dev_f16(h)).cpu().numpy()
+    np.testing.assert_array_equal(back, ora.f16_to_f32(h))
+
+
+def test_layernorm_golden_and_oracle(dev, ora, golden):
+    x, g, b = golden["ln_x"], golden["ln_g"], golden["ln_b"]
+    got = dev.layernorm_rows(dev_f32(x), dev_f32(g), dev_f32(b), 1e-5).cpu().numpy()
+    assert rel_err(got, golden["ln_y"]) <= 1e-5
+    big = np.random.default_rng(1).standard_normal((64, 1024), dtype=np.float32) * 3 + 1
+    gg = np.random.default_rng(2).standard_normal(1024, dtype=np.float32)
+    bb = np.random.default_rng(3).standard_normal(1024, dtype=np.float32)
+    got = dev.layernorm_rows(dev_f32(big), dev_f32(gg), dev_f32(bb), 1e-12).cpu().numpy()
+    assert rel_err(got, ora.layernorm(big, gg, bb, 1e-12)) <= 1e-5
+
+
+def test_layernorm_in_place(dev, ora, golden):
+    x, g, b = golden["ln_x"], golden["ln_g"], golden["ln_b"]
+    t = dev_f32(x)
+    dev.layernorm_rows(t, dev_f32(g), dev_f32(b), 1e-5, y=t)
+    assert rel_err(t.cpu().numpy(), golden["ln_y"]) <= 1e-5
+
+
+def test_softmax_golden(dev, golden):
+    got = dev.softmax_rows(dev_f32(golden["sm_x"])).cpu().numpy()
+    assert rel_err(got, golden["sm_y"]) <= 1e-6
+    np.testing.assert_allclose(got.astype(np.float64).sum(-1), 1.0, atol=1e-6)
+
+
+def test_activations(dev, ora, golden):
+    v = golden["act_v"]
+    assert np.array_equal(dev.activation(dev_f32(v), 1).cpu().numpy(), golden["act_relu"])
+    assert rel_err(dev.activation(dev_f32(v), 2).cpu().numpy(), ora.gelu_erf(v)) <= 1e-6
+    np.testing.assert_array_equal(dev.activation(dev_f32(v), 3, 0.1).cpu().numpy(),
+                                  ora.leaky_relu(v, 0.1))
