@@ -40,6 +40,9 @@ SIGNATURES = {
     "gsvk_last_error": (ctypes.c_char_p, []),
     "gsvk_device_init": (c_int, [c_int]),
     "gsvk_available": (c_int, []),
+    "gsvk_device_status": (c_int, [c_int]),
+    "gsvk_gemm_f16": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
+    "gsvk_gemm_f16_ex": (c_int, [_vp, _vp]),
     "gsvk_f32_to_f16": (c_int, [_vp, _vp, _sz, _vp]),
     "gsvk_f16_to_f32": (c_int, [_vp, _vp, _sz, _vp]),
     "gsvk_gemv_f16w_f32acc": (c_int, [_vp, _vp, _vp, _sz, _sz, _vp]),
@@ -85,8 +88,8 @@ def _ptr(t):
         return None
     if not t.is_cuda:
         raise ValueError("gsvk takes CUDA tensors")
-    if not t.is_contiguous():
-        raise ValueError("gsvk takes contiguous tensors")
+    if t.dim() > 0 and t.stride(-1) != 1:
+        raise ValueError("gsvk takes tensors with unit inner stride")
     return t.data_ptr()
 
 
@@ -140,11 +143,48 @@ def gemv_ex(w, x, bias=None, residual=None, act=ACT_NONE, slope=0.0, y=None, y_f
     import torch
 
     out_, in_ = w.shape
-    if y is None and y_f16 is None:
+    if y is None:
         y = torch.empty(out_, dtype=torch.float32, device=w.device)
     check(lib().gsvk_gemv_ex(_ptr(w), _ptr(x), int(x.dtype == torch.float16), _ptr(y), _ptr(y_f16),
                              out_, in_, _ptr(bias), _ptr(residual), act, slope, _stream(stream)))
-    return y if y is not None else y_f16
+    return y
+
+
+# ------------------------------------------------------------- a3, a6, a9
+class GemmArgs(ctypes.Structure):
+    _fields_ = [("a", _vp), ("lda", _sz), ("b", _vp), ("ldb", _sz), ("M", _sz), ("N", _sz),
+                ("K", _sz), ("bias", _vp), ("residual", _vp), ("ld_res", _sz), ("c", _vp),
+                ("ldc", _sz), ("c_f16", _vp), ("ldc_f16", _sz), ("act", c_int), ("slope", c_float),
+                ("alpha", c_float)]
+
+
+def device_status(reset: bool = True) -> int:
+    """0, or GSVK_ERR_TIMEOUT (-4) if a bounded device wait gave up."""
+    return lib().gsvk_device_status(int(reset))
+
+
+def gemm_f16(a, b, c=None, stream=None):
+    """kern::gemm_f16x_fmlal: C[M,N] = A[M,K] . B[N,K]^T (fp16 in, fp32 out)."""
+    import torch
+
+    M, K = a.shape
+    N = b.shape[0]
+    c = c if c is not None else torch.empty(M, N, dtype=torch.float32, device=a.device)
+    check(lib().gsvk_gemm_f16(_ptr(a), _ptr(b), _ptr(c), M, N, K, _stream(stream)))
+    return c
+
+
+def gemm_ex(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, c=None,
+            c_f16=None, stream=None):
+    """C = act(alpha * A.B^T + bias) + residual -> fp32 c and/or fp16 c_f16."""
+    M, K = a.shape
+    N = b.shape[0]
+    g = GemmArgs(_ptr(a), a.stride(0), _ptr(b), b.stride(0), M, N, K, _ptr(bias), _ptr(residual),
+                 0 if residual is None else residual.stride(0), _ptr(c),
+                 0 if c is None else c.stride(0), _ptr(c_f16),
+                 0 if c_f16 is None else c_f16.stride(0), act, slope, alpha)
+    check(lib().gsvk_gemm_f16_ex(ctypes.byref(g), _stream(stream)))
+    return c if c is not None else c_f16
 
 
 # --------------------------------------------------------------------- a22

@@ -21,7 +21,9 @@ int check_launch(const char* kernel);
 int sm_count();
 
 inline cudaStream_t as_cuda(gsvk_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__host__ __device__ inline bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
 inline unsigned ceil_div(size_t a, size_t b) { return static_cast<unsigned>((a + b - 1) / b); }
 
 // ---------------------------------------------------------------- device side

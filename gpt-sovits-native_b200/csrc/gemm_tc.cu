@@ -1,0 +1,445 @@
+// gemm_tc.cu — tcgen05 / TMA tensor-core GEMM (see gemm_tc.cuh for the
+// algorithm and roles) and its C-ABI entry points:
+//   gsvk_gemm_f16 / gsvk_gemm_f16_ex      (kern::gemm_f16x_fmlal, accel::DenseF16 view)
+//   gsvk_conv1d_f16 / gsvk_convt1d_f16    (sovits::Conv1d / ConvT1d as implicit GEMM)
+#include <algorithm>
+
+#include "gemm_tc.cuh"
+#include "gsvk_internal.hpp"
+
+namespace gsvk {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 192;
+constexpr int kSmemBudget = 200 * 1024;
+
+struct TapPlan {
+  int ntaps, q0, qmax, a_mul, a_off, b_first, b_step, o_mul, o_off;
+};
+
+__device__ __forceinline__ TapPlan plan_for(const TcProblem& p, int phase) {
+  TapPlan t;
+  if (!p.convt) {
+    t.ntaps = p.taps;
+    t.q0 = 0;
+    t.qmax = p.M - 1;
+    t.a_mul = p.dil;
+    t.a_off = -p.pad;
+    t.b_first = 0;
+    t.b_step = 1;
+    t.o_mul = 1;
+    t.o_off = 0;
+  } else {
+    const int u = p.dil, k = p.taps, r = phase;
+    t.ntaps = (k - r + u - 1) / u;
+    const int num = p.pad - r;
+    t.q0 = num > 0 ? (num + u - 1) / u : 0;
+    const int top = p.out_rows - 1 + p.pad - r;
+    t.qmax = top >= 0 ? top / u : -1;
+    t.a_mul = -1;
+    t.a_off = 0;
+    t.b_first = r;
+    t.b_step = u;
+    t.o_mul = u;
+    t.o_off = r - p.pad;
+  }
+  return t;
+}
+
+__device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int n0, int N,
+                                        const uint32_t* r) {
+  float v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]) * e.alpha;
+  const bool full = (n0 + 16 <= N);
+  if (e.bias) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (full || n0 + j < N) v[j] = v[j] + __ldg(e.bias + n0 + j);
+  }
+  if (e.act != GSVK_ACT_NONE) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j], e.act, e.slope);
+  }
+  if (e.residual) {
+    const float* rr = e.residual + orow * e.ld_res + n0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (full || n0 + j < N) v[j] = fmaf(e.res_scale, rr[j], v[j]);
+  }
+  if (e.c32) {
+    float* dst = e.c32 + orow * e.ld_c32 + n0;
+    if (full && aligned16(dst)) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) dst[j] = v[j];
+    }
+  }
+  if (e.c16) {
+    uint16_t* dst = e.c16 + orow * e.ld_c16 + n0;
+    if (full && aligned16(dst)) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pk[j] = f2h(v[2 * j]) | (static_cast<uint32_t>(f2h(v[2 * j + 1])) << 16);
+      reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    } else {
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) dst[j] = f2h(v[j]);
+    }
+  }
+  if (e.c16_act) {
+    uint16_t* dst = e.c16_act + orow * e.ld_c16_act + n0;
+    if (full && aligned16(dst)) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        pk[j] = f2h(apply_act(v[2 * j], e.act2, e.slope2)) |
+                (static_cast<uint32_t>(f2h(apply_act(v[2 * j + 1], e.act2, e.slope2))) << 16);
+      reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    } else {
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) dst[j] = f2h(apply_act(v[j], e.act2, e.slope2));
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcProblem p, const TcEpilogue e, int stages, uint32_t* status) {
+  constexpr uint32_t kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+  const int bk = p.bk;
+  const uint32_t swz_bytes = static_cast<uint32_t>(bk) * 2;          // 32, 64 or 128
+  const uint32_t swz_code = swz_bytes == 128 ? 2u : (swz_bytes == 64 ? 4u : 6u);
+  const uint32_t a_bytes = kBM * swz_bytes, b_bytes = BN * swz_bytes;
+  const uint32_t sbo = 8 * swz_bytes;                                  // 8-row atom stride
+  const int ksteps = bk / 16;
+  constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + static_cast<size_t>(stages) * a_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + static_cast<size_t>(stages) * b_bytes);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (p.M + kBM - 1) / kBM, n_tiles = (p.N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles * p.phases;
+  const int kpt = (p.kc + bk - 1) / bk;  // k-blocks per tap
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int phase = tile / (m_tiles * n_tiles);
+        const int rem = tile - phase * m_tiles * n_tiles;
+        const int mt = rem / n_tiles, nt = rem - (rem / n_tiles) * n_tiles;
+        const TapPlan tp = plan_for(p, phase);
+        for (int t = 0; t < tp.ntaps && ok; ++t) {
+          const int a_row = tp.q0 + mt * kBM + tp.a_mul * t + tp.a_off;
+          const int b_row = (tp.b_first + tp.b_step * t) * p.b_tap_rows + nt * BN;
+          for (int kb = 0; kb < kpt; ++kb, ++it) {
+            const int s = it % stages;
+            const uint32_t ph = static_cast<uint32_t>(it / stages) & 1u;
+            if (!mbar_wait(&empty[s], ph ^ 1u, status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
+            tma_load_2d(sA + static_cast<size_t>(s) * a_bytes, &tmA, &full[s], kb * bk, a_row);
+            tma_load_2d(sB + static_cast<size_t>(s) * b_bytes, &tmB, &full[s], kb * bk, b_row);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------------- MMA issuer
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++tl) {
+        const int phase = tile / (m_tiles * n_tiles);
+        const TapPlan tp = plan_for(p, phase);
+        const int acc = tl & 1;
+        const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+        const int nk = tp.ntaps * kpt;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int s = it % stages;
+          const uint32_t ph = static_cast<uint32_t>(it / stages) & 1u;
+          if (!mbar_wait(&full[s], ph, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + static_cast<size_t>(s) * a_bytes);
+          const uint32_t b_base = smem_u32(sB + static_cast<size_t>(s) * b_bytes);
+          for (int j = 0; j < ksteps; ++j) {
+            const uint64_t ad = smem_desc(a_base + 32u * j, sbo, swz_code);
+            const uint64_t bd = smem_desc(b_base + 32u * j, sbo, swz_code);
+            tc_mma_f16(d_tmem, ad, bd, idesc, (kk | j) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    int tl = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tl) {
+      const int phase = tile / (m_tiles * n_tiles);
+      const int rem = tile - phase * m_tiles * n_tiles;
+      const int mt = rem / n_tiles, nt = rem - (rem / n_tiles) * n_tiles;
+      const TapPlan tp = plan_for(p, phase);
+      const int acc = tl & 1;
+      const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
+      if (!mbar_wait(&tfull[acc], aph, status)) break;
+      tc_fence_after();
+      const int i = mt * kBM + quarter * 32 + lane;
+      const int q = tp.q0 + i;
+      const bool row_ok = (i < p.M) && (q <= tp.qmax);
+      const long long orow = static_cast<long long>(q) * tp.o_mul + tp.o_off;
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
+        tmem_ld_wait();
+        if (row_ok && nt * BN + c0 < p.N) store16(e, orow, nt * BN + c0, p.N, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int BN>
+int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
+              const TcEpilogue& e, cudaStream_t st) {
+  const int stage_bytes = (kBM + BN) * p.bk * 2;
+  int stages = kSmemBudget / stage_bytes;
+  stages = std::max(2, std::min(stages, 8));
+  const size_t smem = 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * stages + 4) * 8 + 16;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<BN>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemBudget + 4096),
+                        "cudaFuncSetAttribute(gemm_tc)");
+    if (rc) return rc;
+    attr_set[dev] = true;
+  }
+  const long long tiles = static_cast<long long>((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) *
+                          p.phases;
+  const int grid = static_cast<int>(std::min<long long>(tiles, sm_count()));
+  gemm_tc_kernel<BN><<<grid, kThreads, smem, st>>>(ta, tb, p, e, stages, device_status());
+  return check_launch("gemm_tc_kernel");
+}
+
+// CUDA-core path for shapes the TMA descriptors cannot express: one thread
+// per (row, 16-column group), fp32 FMA over K, the same epilogue.
+__global__ void gemm_simt_kernel(const uint16_t* __restrict__ a, long long lda,
+                                 const uint16_t* __restrict__ b, long long ldb, int M, int N, int K,
+                                 const TcEpilogue e) {
+  const int groups = (N + 15) / 16;
+  const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (idx >= static_cast<long long>(M) * groups) return;
+  const int m = static_cast<int>(idx / groups), g = static_cast<int>(idx % groups);
+  uint32_t r[16];
+  const uint16_t* ar = a + m * lda;
+  for (int j = 0; j < 16; ++j) {
+    const int n = g * 16 + j;
+    float acc = 0.f;
+    if (n < N) {
+      const uint16_t* br = b + n * ldb;
+      for (int k = 0; k < K; ++k) acc = fmaf(h2f(ar[k]), h2f(br[k]), acc);
+    }
+    r[j] = __float_as_uint(acc);
+  }
+  store16(e, m, g * 16, N, r);
+}
+
+int pick_bk(long long kc) {
+  if (kc <= 16) return 16;
+  if (kc <= 32) return 32;
+  return 64;
+}
+
+CUtensorMapSwizzle swizzle_for(int bk) {
+  return bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                  : (bk == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+}  // namespace
+
+int make_kmajor_map(CUtensorMap* map, const uint16_t* base, long long rows, long long kc,
+                    long long ld, int box_rows, int bk) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(kc), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 2};
+  const uint32_t box[2] = {static_cast<uint32_t>(bk), static_cast<uint32_t>(box_rows)};
+  return encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t*>(base), dims,
+                      strides, box, swizzle_for(bk));
+}
+
+int tc_pick_bn(long long M, long long N) {
+  if (N <= 16) return 16;
+  if (N <= 32) return 32;
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  const long long m_tiles = (M + kBM - 1) / kBM;
+  // 256-wide tiles halve A re-reads; keep them only while they still fill the GPU.
+  return (m_tiles * ((N + 255) / 256) >= sm_count()) ? 256 : 128;
+}
+
+int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b,
+           long long b_rows, long long ldb, TcProblem p, const TcEpilogue& e, int bn,
+           cudaStream_t st) {
+  if (!gsvk_available()) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
+  if (p.kc % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0)
+    return fail(GSVK_ERR_ALIGN, "tensor-core path needs K and leading dims multiple of 8");
+  if (!aligned16(a) || !aligned16(b))
+    return fail(GSVK_ERR_ALIGN, "tensor-core path needs 16-byte aligned A and B");
+  if (p.M <= 0 || p.N <= 0 || p.kc <= 0 || p.taps <= 0)
+    return fail(GSVK_ERR_INVALID, "empty GEMM");
+  p.bk = pick_bk(p.kc);
+  if (bn == 0) bn = tc_pick_bn(p.M, p.N);
+  CUtensorMap ta, tb;
+  int rc = make_kmajor_map(&ta, a, a_rows, p.kc, lda, kBM, p.bk);
+  if (rc) return rc;
+  rc = make_kmajor_map(&tb, b, b_rows, p.kc, ldb, bn, p.bk);
+  if (rc) return rc;
+  switch (bn) {
+    case 16: return launch_bn<16>(ta, tb, p, e, st);
+    case 32: return launch_bn<32>(ta, tb, p, e, st);
+    case 64: return launch_bn<64>(ta, tb, p, e, st);
+    case 128: return launch_bn<128>(ta, tb, p, e, st);
+    case 256: return launch_bn<256>(ta, tb, p, e, st);
+    default: return fail(GSVK_ERR_INVALID, "bad BN %d", bn);
+  }
+}
+
+int simt_gemm(const gsvk_gemm_args* g, const TcEpilogue& e, cudaStream_t st) {
+  const long long groups = (static_cast<long long>(g->N) + 15) / 16;
+  const long long threads = static_cast<long long>(g->M) * groups;
+  gemm_simt_kernel<<<static_cast<unsigned>((threads + 127) / 128), 128, 0, st>>>(
+      g->a, (long long)g->lda, g->b, (long long)g->ldb, (int)g->M, (int)g->N, (int)g->K, e);
+  return check_launch("gemm_simt_kernel");
+}
+
+TcEpilogue make_epilogue() {
+  TcEpilogue e{};
+  e.alpha = 1.f;
+  e.res_scale = 1.f;
+  return e;
+}
+
+}  // namespace gsvk
+
+using namespace gsvk;
+
+extern "C" {
+
+int gsvk_gemm_f16(const uint16_t* a, const uint16_t* b, float* c, size_t M, size_t N, size_t K,
+                  gsvk_stream_t stream) {
+  gsvk_gemm_args g{};
+  g.a = a;
+  g.lda = K;
+  g.b = b;
+  g.ldb = K;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.c = c;
+  g.ldc = N;
+  g.alpha = 1.f;
+  return gsvk_gemm_f16_ex(&g, stream);
+}
+
+int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
+  if (!g || !g->a || !g->b || (!g->c && !g->c_f16) || g->M == 0 || g->N == 0 || g->K == 0)
+    return fail(GSVK_ERR_INVALID, "gemm: null pointer or zero size");
+  if (g->M > 0x7fffffff || g->N > 0x7fffffff || g->K > 0x7fffffff)
+    return fail(GSVK_ERR_UNSUPPORTED, "gemm: size > 2^31");
+  if (g->lda < g->K || g->ldb < g->K) return fail(GSVK_ERR_INVALID, "gemm: lda/ldb < K");
+  if (g->act < GSVK_ACT_NONE || g->act > GSVK_ACT_LEAKY) return fail(GSVK_ERR_INVALID, "bad act");
+  TcEpilogue e = make_epilogue();
+  e.bias = g->bias;
+  e.residual = g->residual;
+  e.ld_res = g->ld_res ? (long long)g->ld_res : (long long)g->N;
+  e.c32 = g->c;
+  e.ld_c32 = g->ldc ? (long long)g->ldc : (long long)g->N;
+  e.c16 = g->c_f16;
+  e.ld_c16 = g->ldc_f16 ? (long long)g->ldc_f16 : (long long)g->N;
+  e.act = g->act;
+  e.slope = g->slope;
+  e.alpha = g->alpha == 0.f ? 1.f : g->alpha;
+  if (g->K % 8 != 0 || g->lda % 8 != 0 || g->ldb % 8 != 0 || !aligned16(g->a) ||
+      !aligned16(g->b))
+    return simt_gemm(g, e, as_cuda(stream));  // odd K (conv K=7/9, test shapes)
+  TcProblem p{};
+  p.M = (int)g->M;
+  p.N = (int)g->N;
+  p.kc = (int)g->K;
+  p.taps = 1;
+  p.dil = 1;
+  p.pad = 0;
+  p.b_tap_rows = 0;
+  p.convt = 0;
+  p.phases = 1;
+  p.out_rows = (int)g->M;
+  return tc_run(g->a, (long long)g->M, (long long)g->lda, g->b, (long long)g->N,
+                (long long)g->ldb, p, e, 0, as_cuda(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,56 @@
+// gemm_tc.cuh — warp-specialised persistent tensor-core GEMM for sm_100a.
+//
+//   C[row(i), n] = epi( sum_{t < taps} sum_k A[i + a_shift(t), k] * B[b_row(t) + n, k] )
+//
+// A (activations) and B (weights) are fp16, K-major (row-major [rows, K]),
+// fetched by TMA into swizzled shared-memory stages; tcgen05.mma
+// (cta_group::1, kind::f16, M = 128, N = BN, K = 16) accumulates fp32 in TMEM;
+// the epilogue warps read TMEM with tcgen05.ld and apply bias / activation /
+// residual before storing fp32 and/or fp16.
+//
+// The "taps" loop turns the same mainloop into:
+//   plain GEMM          taps = 1, a_shift = 0, b_row = 0
+//   conv1d (implicit)   tap t: a_shift = t*dil - pad, b_row = t*Co   (A = x[T, Ci] channels-last,
+//                        B = W[k][Co][Ci]); rows outside [0, T) come back as zeros from TMA
+//   ConvTranspose1d     phase r, tap m: a_shift = -m, b_row = (r + m*u)*Co,
+//                        output row = q*u + r - pad with q = i + q0(r)   (polyphase, no scatter)
+//
+// Roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and TMEM
+// owner, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+// Two TMEM accumulators let the epilogue of tile i overlap the mainloop of
+// tile i+1.  Every mbarrier wait is bounded (see tma.cuh).
+#pragma once
+
+#include "tma.cuh"
+
+namespace gsvk {
+
+struct TcEpilogue {
+  const float* bias;      // [N] or null
+  const float* residual;  // fp32 [rows, ld_res] at the output row, or null
+  float* c32;             // fp32 output or null
+  uint16_t* c16;          // fp16 output or null
+  uint16_t* c16_act;      // optional second fp16 output = act2(value)
+  long long ld_c32, ld_c16, ld_res, ld_c16_act;
+  int act;                // applied to alpha*acc + bias, before the residual add
+  float slope;
+  int act2;               // activation for c16_act
+  float slope2;
+  float alpha;
+  float res_scale;        // y = act(alpha*acc + bias) + res_scale * residual
+};
+
+struct TcProblem {
+  int M;            // tile-space rows (per phase)
+  int N;            // output columns
+  int kc;           // K per tap
+  int bk;           // K elements per stage: 16, 32 or 64 (swizzle 32/64/128 B)
+  int taps;         // conv taps (plain GEMM: 1)
+  int dil, pad;     // conv: a_shift(t) = t*dil - pad
+  int b_tap_rows;   // rows of B per tap (Co)
+  int convt;        // 1: ConvTranspose1d polyphase mode (taps = kernel k, dil = u)
+  int phases;       // ConvT: u phases; otherwise 1
+  int out_rows;     // valid output rows (ConvT: T*u; others: M)
+};
+
+}  // namespace gsvk

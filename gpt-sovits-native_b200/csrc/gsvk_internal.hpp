@@ -1,0 +1,32 @@
+// gsvk_internal.hpp — declarations shared between the library's translation
+// units (not part of the public ABI).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+
+namespace gsvk {
+
+// Per-device status word written by bounded device-side waits (DEV_TIMEOUT).
+uint32_t* device_status();
+
+// K-major (row-major [rows, kc], leading dimension ld elements) fp16 tensor
+// map with a box of bk x box_rows and the swizzle matching bk.
+int make_kmajor_map(CUtensorMap* map, const uint16_t* base, long long rows, long long kc,
+                    long long ld, int box_rows, int bk);
+int tc_pick_bn(long long M, long long N);
+// Launches the tensor-core kernel for problem p (bn = 0 picks the tile width).
+int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b,
+           long long b_rows, long long ldb, TcProblem p, const TcEpilogue& e, int bn,
+           cudaStream_t st);
+TcEpilogue make_epilogue();
+// CUDA-core fallback for shapes the TMA path cannot express (K or leading
+// dimensions not multiples of 8, unaligned bases).
+int simt_gemm(const gsvk_gemm_args* g, const TcEpilogue& e, cudaStream_t st);
+int gemv_ex(const uint16_t* w, const void* x, int x_is_f16, float* y, uint16_t* yh, size_t out,
+            size_t in, const float* bias, const float* residual, int act, float slope,
+            cudaStream_t st);
+
+}  // namespace gsvk

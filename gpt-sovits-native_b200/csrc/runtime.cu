@@ -7,7 +7,7 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "tma.cuh"
+#include "gsvk_internal.hpp"
 
 namespace gsvk {
 
@@ -18,6 +18,7 @@ thread_local int g_ready_device = -1;
 struct DeviceInfo {
   int sms = 0;
   int major = 0, minor = 0;
+  uint32_t* status = nullptr;  // device word written by bounded waits
 };
 DeviceInfo g_info[64];
 std::mutex g_init_mu;
@@ -54,6 +55,12 @@ int sm_count() {
 }
 
 bool tma_encode_available() { return g_encode_tiled != nullptr; }
+
+uint32_t* device_status() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return (dev >= 0 && dev < 64) ? g_info[dev].status : nullptr;
+}
 
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base,
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
@@ -96,6 +103,13 @@ int gsvk_device_init(int device) {
                 prop.major, prop.minor);
   std::lock_guard<std::mutex> lk(g_init_mu);
   g_info[device].sms = prop.multiProcessorCount;
+  if (!g_info[device].status) {
+    // One-time allocation at initialisation (never on the hot path).
+    rc = check_cuda(cudaMalloc(&g_info[device].status, 256), "cudaMalloc(status)");
+    if (rc) return rc;
+    rc = check_cuda(cudaMemset(g_info[device].status, 0, 256), "cudaMemset(status)");
+    if (rc) return rc;
+  }
   g_info[device].major = prop.major;
   g_info[device].minor = prop.minor;
   if (!g_encode_tiled) {
@@ -110,6 +124,19 @@ int gsvk_device_init(int device) {
   }
   g_ready_device = device;
   return GSVK_OK;
+}
+
+int gsvk_device_status(int reset) {
+  uint32_t* st = device_status();
+  if (!st) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
+  uint32_t v = 0;
+  int rc = check_cuda(cudaMemcpy(&v, st, 4, cudaMemcpyDeviceToHost), "read device status");
+  if (rc) return rc;
+  if (reset) {
+    rc = check_cuda(cudaMemset(st, 0, 4), "reset device status");
+    if (rc) return rc;
+  }
+  return v == DEV_OK ? GSVK_OK : GSVK_ERR_TIMEOUT;
 }
 
 int gsvk_available(void) {

@@ -25,9 +25,10 @@ int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, voi
 // Device status words written by bounded waits (one per launch site).
 enum : uint32_t { DEV_OK = 0, DEV_TIMEOUT = 1 };
 
-// Spin budget of one bounded wait: ~2^26 polls (several hundred ms on a
-// B200 at any clock), far above any legitimate wait in these kernels.
-constexpr uint32_t kSpinLimit = 1u << 26;
+// Spin budget of one bounded wait: 2^22 polls of mbarrier.try_wait (each
+// poll may suspend briefly; the budget is seconds), far above any
+// legitimate wait in these kernels.
+constexpr uint32_t kSpinLimit = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -58,6 +58,10 @@ const char* gsvk_last_error(void);
 int gsvk_device_init(int device);
 /* 1 when gsvk_device_init succeeded on the current device. */
 int gsvk_available(void);
+/* Reads (and optionally clears) the current device's status word written by
+ * bounded device-side waits; synchronous.  GSVK_ERR_TIMEOUT when a kernel
+ * gave up waiting since the last reset. */
+int gsvk_device_status(int reset);
 
 /* ---- fp16 conversion (a4) ---------------------------------------------- */
 /* kern::f32_to_f16 (gemv_fmlal.hpp:16): round-to-nearest-even. */
@@ -80,6 +84,32 @@ int gsvk_gemv_f16x_fmlal(const uint16_t* w, const uint16_t* xh, float* y, size_t
 int gsvk_gemv_ex(const uint16_t* w, const void* x, int x_is_f16, float* y, uint16_t* y_f16,
                  size_t out, size_t in, const float* bias, const float* residual, int act,
                  float slope, gsvk_stream_t stream);
+
+/* ---- tensor-core GEMM (a3, a6, a9) -------------------------------------- */
+/* kern::gemm_f16x_fmlal (gemv_fmlal.hpp:36): C[M,N] = A[M,K] . B[N,K]^T,
+ * fp16 A/B row-major, fp32 C row-major.  tcgen05 + TMA when K and the
+ * leading dimensions are multiples of 8 (16-byte rows), a CUDA-core kernel
+ * otherwise (same results within fp32 rounding). */
+int gsvk_gemm_f16(const uint16_t* a, const uint16_t* b, float* c, size_t M, size_t N, size_t K,
+                  gsvk_stream_t stream);
+
+/* Fused form: C = act(alpha * A.B^T + bias) + residual, written as fp32
+ * and/or fp16.  Covers accel::DenseF16::forward on a view (accel.hpp:70-78)
+ * and bert::Linear::forward (bert_ops.hpp:225-258) with their bias / GELU /
+ * residual loops folded into the epilogue.  Zero leading dimensions mean
+ * "dense" (K for A/B, N for C / residual). */
+typedef struct {
+  const uint16_t* a; size_t lda;     /* [M, K] fp16 */
+  const uint16_t* b; size_t ldb;     /* [N, K] fp16 (weights, [out, in]) */
+  size_t M, N, K;
+  const float* bias;                 /* [N] or NULL */
+  const float* residual; size_t ld_res; /* fp32 [M, N] or NULL */
+  float* c; size_t ldc;              /* fp32 output or NULL */
+  uint16_t* c_f16; size_t ldc_f16;   /* fp16 output or NULL */
+  int act; float slope;              /* GSVK_ACT_* */
+  float alpha;                       /* 0 is read as 1 */
+} gsvk_gemm_args;
+int gsvk_gemm_f16_ex(const gsvk_gemm_args* args, gsvk_stream_t stream);
 
 /* ---- support primitives (a22) ------------------------------------------ */
 /* kern::layernorm (kern.cpp:27) applied to `rows` rows of n. y may equal x. */

@@ -1,0 +1,120 @@
+"""GPU parity for the tensor-core GEMM (a3, a6, a9) through the C-ABI.
+
+Gates (stated per test):
+  * the reference's own gemm test (test_kern.cpp:145-196):
+        |acc - got| <= 1e-4 (1 + |acc|)  against an fp64 dot of the fp16 inputs;
+  * the AMX-vs-FMLAL gate (test_kern.cpp:282-320): cos >= 0.9999, max|d|/max|ref| <= 1e-3;
+  * the north-star bound for fused fp16-output GEMMs: max relative error <= 1e-2.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def h(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.float16)).cuda()
+
+
+def f(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def rand16(rng, shape, scale):
+    return (rng.uniform(-1, 1, size=shape).astype(np.float32) * scale).astype(np.float16).view(np.uint16)
+
+
+def exact(a, b):
+    return a.view(np.float16).astype(np.float64) @ b.view(np.float16).astype(np.float64).T
+
+
+GEMM_SHAPES = [(8, 1024, 1024), (32, 4096, 1024), (14, 768, 768), (96, 200, 9),
+               (2048, 50, 1024), (17, 31, 7), (1, 1, 1), (64, 3, 1536)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_f16_reference_cases(dev, M, N, K):
+    """test_kern.cpp:145-196 shapes and tolerance (odd K runs the CUDA-core kernel)."""
+    rng = np.random.default_rng(M * 7 + N * 13 + K)
+    a, b = rand16(rng, (M, K), 0.5), rand16(rng, (N, K), 0.5)
+    got = dev.gemm_f16(h(a), h(b)).cpu().numpy().astype(np.float64)
+    acc = exact(a, b)
+    bad = np.abs(acc - got) > 1e-4 * (1.0 + np.abs(acc))
+    assert not bad.any(), f"{bad.sum()} mismatches, worst {np.abs(acc - got).max():.3g}"
+    assert dev.device_status() == 0
+
+
+EDGE = [(1, 16, 64), (127, 17, 64), (129, 33, 72), (300, 64, 16), (300, 48, 32), (256, 128, 128),
+        (200, 200, 520), (513, 256, 256), (130, 384, 1024), (64, 1000, 512), (1000, 24, 24)]
+
+
+@pytest.mark.parametrize("M,N,K", EDGE)
+def test_gemm_edges_match_oracle(dev, ora, M, N, K):
+    rng = np.random.default_rng(M + 31 * N + 7 * K)
+    a, b = rand16(rng, (M, K), 1.0), rand16(rng, (N, K), 0.05)
+    got = dev.gemm_f16(h(a), h(b)).cpu().numpy()
+    ref = ora.gemm_f16x_fmlal(a, b)
+    acc = exact(a, b)
+    assert np.all(np.abs(acc - got) <= 1e-4 * (1.0 + np.abs(acc)))
+    assert np.abs(got - ref).max() <= 1e-3 * np.abs(ref).max()
+
+
+def test_gemm_config1_ffn_up(dev, ora):
+    """Y = ReLU(X W^T + b), X[128,512] U(-1,1), W[2048,512] N(0,0.02),
+    b N(0,0.01), fp16 output; max relative error <= 1e-2 against the oracle."""
+    x, w, b = dev.workloads.gemm_ffn_up()
+    yh = torch.empty(128, 2048, dtype=torch.float16, device="cuda")
+    dev.gemm_ex(h(x), h(w), bias=f(b), act=dev.ACT_RELU, c_f16=yh)
+    got = yh.float().cpu().numpy()
+    ref = ora.linear_f16(ora.f16_to_f32(x), w, b, ora.ACT_RELU)
+    err = np.abs(got - ref)
+    assert err.max() <= 1e-2 * np.abs(ref).max()
+    # fp16 rounding of the output is the only loss beyond fp32 reordering
+    assert np.all(err <= 2.0 ** -10 * np.abs(ref) + 1e-4)
+
+
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_gemm_fused_epilogue(dev, ora, act):
+    rng = np.random.default_rng(100 + act)
+    M, N, K = 300, 384, 256
+    a, w = rand16(rng, (M, K), 1.0), rand16(rng, (N, K), 0.05)
+    bias = rng.standard_normal(N).astype(np.float32) * 0.1
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    c = torch.empty(M, N, device="cuda")
+    c16 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    dev.gemm_ex(h(a), h(w), bias=f(bias), residual=f(res), act=act, slope=0.1, c=c, c_f16=c16)
+    ref = ora.linear_f16(ora.f16_to_f32(a), w, bias, act, 0.1) + res
+    got = c.cpu().numpy()
+    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
+    np.testing.assert_array_equal(c16.cpu().numpy(), got.astype(np.float16))
+
+
+def test_gemm_strided_operands(dev, ora):
+    """Leading dimensions larger than K (sub-matrix views, e.g. per-head slices)."""
+    rng = np.random.default_rng(5)
+    M, N, K, lda, ldb = 200, 96, 64, 192, 136
+    A = rand16(rng, (M, lda), 1.0)
+    B = rand16(rng, (N, ldb), 0.1)
+    ta, tb = h(A)[:, 32:32 + K], h(B)[:, 8:8 + K]
+    c = torch.empty(M, N, device="cuda")
+    dev.gemm_ex(ta, tb, c=c)
+    ref = exact(np.ascontiguousarray(A[:, 32:32 + K]), np.ascontiguousarray(B[:, 8:8 + K]))
+    assert np.abs(c.cpu().numpy() - ref).max() <= 1e-4 * (1 + np.abs(ref).max())
+
+
+@pytest.mark.parametrize("name", ["bert", "hubert"])
+def test_gemm_encoder_shapes_vs_torch_fp32(dev, name):
+    """Config 4 FFN-up shape per encoder against a torch fp32 GEMM of the same
+    fp16 values (AMX gate: cos >= 0.9999, max|d|/max|ref| <= 1e-3)."""
+    e = dev.workloads.ENCODERS[name]
+    M, H, Fd = e["batch"] * e["seq"], e["hidden"], e["ffn"]
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(M, H, device="cuda", generator=g).half()
+    w = (torch.randn(Fd, H, device="cuda", generator=g) * 0.02).half()
+    got = dev.gemm_f16(x, w)
+    ref = x.float() @ w.float().T
+    d = (got - ref).abs().max().item() / ref.abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(got.flatten().double(), ref.flatten().double(), dim=0)
+    assert d <= 1e-3 and cos.item() >= 0.9999
+    assert dev.device_status() == 0
