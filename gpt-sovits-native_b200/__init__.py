@@ -48,6 +48,13 @@ SIGNATURES = {
     "gsvk_gemv_f16w_f32acc": (c_int, [_vp, _vp, _vp, _sz, _sz, _vp]),
     "gsvk_gemv_f16x_fmlal": (c_int, [_vp, _vp, _vp, _sz, _sz, _vp]),
     "gsvk_gemv_ex": (c_int, [_vp, _vp, c_int, _vp, _vp, _sz, _sz, _vp, _vp, c_int, c_float, _vp]),
+    "gsvk_t2s_create": (c_int, [_vp, _vp, _vp]),
+    "gsvk_t2s_destroy": (c_int, [_vp]),
+    "gsvk_t2s_load_kv": (c_int, [_vp, _vp, _vp, _sz, _sz, _vp]),
+    "gsvk_t2s_prefill": (c_int, [_vp, _vp, _sz, _sz, _sz, _vp]),
+    "gsvk_t2s_generate": (c_int, [_vp, _sz, _vp, _sz, _sz, c_int, _vp, _vp, _vp, _vp]),
+    "gsvk_t2s_generate_device": (c_int, [_vp, _sz, _vp, _sz, _sz, c_int, _vp, _vp, _vp, _vp]),
+    "gsvk_t2s_read_logits": (c_int, [_vp, _vp]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -213,3 +220,84 @@ def activation(x, act, slope=0.0, y=None, stream=None):
     y = y if y is not None else torch.empty_like(x)
     check(lib().gsvk_activation(_ptr(x), _ptr(y), x.numel(), act, slope, _stream(stream)))
     return y
+
+
+# ------------------------------------------------------------ a16 - a19: T2S
+class T2SConfig(ctypes.Structure):
+    _fields_ = [("n_layers", c_int), ("d_model", c_int), ("n_heads", c_int), ("ffn", c_int),
+                ("vocab", c_int), ("ln_eps", c_float), ("alpha_audio", c_float), ("cap", c_int)]
+
+
+class T2SHostWeights(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("wqkv", "bqkv", "wout", "bout", "w1", "b1", "w2", "b2",
+                                   "n1g", "n1b", "n2g", "n2b", "wpred", "audio_emb")]
+
+
+class T2S:
+    """Device T2S engine (ar::T2SEngine).  `model` is a dict of numpy arrays in
+    the reference layouts (see workloads.t2s_model)."""
+
+    def __init__(self, model: dict, cap: int):
+        import numpy as np
+
+        self.model = model
+        self.cap = cap
+        self._keep = {k: np.ascontiguousarray(v) for k, v in model.items()
+                      if isinstance(v, np.ndarray)}
+        cfg = T2SConfig(model["n_layers"], model["d_model"], model["n_heads"], model["ffn"],
+                        model["vocab"], model["ln_eps"], model["alpha_audio"], cap)
+        w = T2SHostWeights(*[self._keep[n].ctypes.data for n in (
+            "wqkv", "bqkv", "wout", "bout", "w1", "b1", "w2", "b2", "n1g", "n1b", "n2g", "n2b",
+            "wpred", "audio_emb")])
+        h = c_void_p()
+        check(lib().gsvk_t2s_create(ctypes.byref(cfg), ctypes.byref(w), ctypes.byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().gsvk_t2s_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_kv(self, k, v, prefix: int, stream=None):
+        """k, v: host uint16 [L, rows, D] (pinned torch tensors or numpy)."""
+        rows = k.shape[1]
+        kp = k.ctypes.data if hasattr(k, "ctypes") else k.data_ptr()
+        vp = v.ctypes.data if hasattr(v, "ctypes") else v.data_ptr()
+        check(lib().gsvk_t2s_load_kv(self.h, kp, vp, prefix, rows, _stream(stream)))
+
+    def prefill(self, x, pos: int, text_len: int = 0, stream=None):
+        check(lib().gsvk_t2s_prefill(self.h, _ptr(x), x.shape[0], pos, text_len, _stream(stream)))
+        return x
+
+    def generate(self, prefix: int, prompt, max_steps: int, stop_on_eos: bool = True,
+                 stream=None):
+        """Host prompt (int32 numpy) -> (tokens, margins) numpy arrays."""
+        import numpy as np
+
+        pr = np.ascontiguousarray(prompt, np.int32)
+        toks = np.zeros(max(1, max_steps), np.int32)
+        margins = np.zeros(max(1, max_steps), np.float32)
+        n = c_int(0)
+        check(lib().gsvk_t2s_generate(self.h, prefix, pr.ctypes.data, pr.size, max_steps,
+                                      int(stop_on_eos), toks.ctypes.data, margins.ctypes.data,
+                                      ctypes.byref(n), _stream(stream)))
+        return toks[:n.value], margins[:max_steps]
+
+    def generate_device(self, prefix: int, prompt_dev, max_steps: int, tokens_dev, n_out_dev,
+                        stop_on_eos: bool = True, margins_dev=None, stream=None):
+        check(lib().gsvk_t2s_generate_device(self.h, prefix, _ptr(prompt_dev), prompt_dev.numel(),
+                                             max_steps, int(stop_on_eos), _ptr(tokens_dev),
+                                             _ptr(n_out_dev), _ptr(margins_dev), _stream(stream)))
+
+    def read_logits(self):
+        import numpy as np
+
+        out = np.zeros(self.model["vocab"], np.float32)
+        check(lib().gsvk_t2s_read_logits(self.h, out.ctypes.data))
+        return out

@@ -1,0 +1,130 @@
+// canon.cuh — the canonical T2S arithmetic, reproduced bit for bit.
+//
+// The reference leaves the association of its sums to NEON register blocking
+// (and Accelerate); the T2S path here fixes one order and evaluates it
+// identically on the CPU oracle and on the device, so that greedy token
+// streams are identical by construction, not by luck of the logit margins:
+//   dot32     the gemv_fmlal.cpp:40-109 association: 32 accumulators (8 groups
+//             x 4 lanes) over 64-element steps, low then high half of each
+//             8-element slice; group sums (a0+a1)+(a2+a3); groups added in
+//             order.  One accumulator per lane of a warp.
+//   dot_kv    dot_f16kv (t2s_engine.cpp:69-99): 4 x 4 accumulators over
+//             16-element steps, (a0+a1)+(a2+a3) per lane, (s0+s2)+(s1+s3).
+//   ln_canon  kern.cpp:27-58: 8-lane fp32 sums, fp64 mean / biased variance.
+//   exp_det   Cody-Waite reduction + degree-7 Taylor polynomial (within 2 ulp
+//             of expf), used by the chunked softmax.
+// Every multiply feeding an add that the order keeps separate is written with
+// __fmul_rn / __fadd_rn so that the compiler cannot contract it into an FMA.
+#pragma once
+
+#include "common.cuh"
+
+namespace gsvk {
+
+__device__ __forceinline__ float exp_det(float x) {
+  if (x < -87.0f) return 0.0f;
+  if (x > 88.0f) return __int_as_float(0x7f800000);
+  const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+  float r = fmaf(n, -0.693359375f, x);
+  r = fmaf(n, 2.12194440e-4f, r);
+  float p = 1.98412698e-4f;
+  p = fmaf(p, r, 1.38888889e-3f);
+  p = fmaf(p, r, 8.33333333e-3f);
+  p = fmaf(p, r, 4.16666667e-2f);
+  p = fmaf(p, r, 1.66666667e-1f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int ni = static_cast<int>(n);
+  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+// Canonical dot of an fp16 row with fp32 activations, one warp; every lane
+// returns the same value.  w and x may live in shared or global memory.
+__device__ __forceinline__ float warp_dot32(const uint16_t* w, const float* x, int n) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+  const int vec_end = n & ~63;
+  float acc = 0.f;
+  for (int i = 0; i < vec_end; i += 64) {
+    acc = fmaf(h2f(w[i + o0]), x[i + o0], acc);
+    acc = fmaf(h2f(w[i + o0 + 4]), x[i + o0 + 4], acc);
+  }
+  const float t = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+  const float u = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+  float s = __shfl_sync(0xffffffffu, u, 0);
+#pragma unroll
+  for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __shfl_sync(0xffffffffu, u, 4 * j));
+  for (int i = vec_end; i < n; ++i) s = fmaf(h2f(w[i]), x[i], s);
+  return s;
+}
+
+// Canonical q . k over HD dims by a 16-lane group (lanes g*16 .. g*16+15 of a
+// warp); q_reg[c] holds q[16c + (lane & 15)].  Lane (lane & 15) == 0 of the
+// group ends with the result (others hold partial combinations).
+template <int HD>
+__device__ __forceinline__ float group16_dot_kv(const float* q_reg, const uint16_t* krow) {
+  const int L = threadIdx.x & 15;
+  float a = 0.f;
+#pragma unroll
+  for (int c = 0; c < HD / 16; ++c) a = fmaf(q_reg[c], h2f(krow[16 * c + L]), a);
+  const float t = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+  const float u = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 8));
+  const float v = __fadd_rn(u, __shfl_xor_sync(0xffffffffu, u, 2));
+  return __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+}
+
+// LayerNorm of n values held in shared memory `buf`, in place, whole block.
+// scratch: >= 18 floats of shared memory.
+__device__ __forceinline__ void ln_canon(float* buf, const float* g, const float* b, int n,
+                                         double eps, float* scratch) {
+  const int tid = threadIdx.x;
+  const int vec_end = n & ~7;
+  if (tid < 16) {
+    const int l = tid & 7;
+    float a = 0.f;
+    if (tid < 8) {
+      for (int i = l; i < vec_end; i += 8) a = __fadd_rn(a, buf[i]);
+    } else {
+      for (int i = l; i < vec_end; i += 8) a = fmaf(buf[i], buf[i], a);
+    }
+    scratch[tid] = a;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const float* f = scratch;
+    const float s = __fadd_rn(__fadd_rn(__fadd_rn(f[0], f[1]), __fadd_rn(f[2], f[3])),
+                              __fadd_rn(__fadd_rn(f[4], f[5]), __fadd_rn(f[6], f[7])));
+    const float q = __fadd_rn(__fadd_rn(__fadd_rn(f[8], f[9]), __fadd_rn(f[10], f[11])),
+                              __fadd_rn(__fadd_rn(f[12], f[13]), __fadd_rn(f[14], f[15])));
+    double sum = static_cast<double>(s), sq = static_cast<double>(q);
+    for (int i = vec_end; i < n; ++i) {
+      const double xv = static_cast<double>(buf[i]);
+      sum = __dadd_rn(sum, xv);
+      sq = __dadd_rn(sq, __dmul_rn(xv, xv));
+    }
+    const double dn = static_cast<double>(n);
+    const float mean = static_cast<float>(__ddiv_rn(sum, dn));
+    const double md = static_cast<double>(mean);
+    float var = static_cast<float>(__dsub_rn(__ddiv_rn(sq, dn), __dmul_rn(md, md)));
+    if (!(var >= 0.0f)) {
+      double s2 = 0.0;
+      for (int i = 0; i < n; ++i) {
+        const double d = __dsub_rn(static_cast<double>(buf[i]), md);
+        s2 = __dadd_rn(s2, __dmul_rn(d, d));
+      }
+      var = static_cast<float>(__ddiv_rn(s2, dn));
+    }
+    const float rstd = static_cast<float>(
+        __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(static_cast<double>(var), eps))));
+    scratch[16] = mean;
+    scratch[17] = rstd;
+  }
+  __syncthreads();
+  const float mean = scratch[16], rstd = scratch[17];
+  for (int i = tid; i < n; i += blockDim.x)
+    buf[i] = fmaf(__fmul_rn(__fsub_rn(buf[i], mean), rstd), g[i], b[i]);
+  __syncthreads();
+}
+
+}  // namespace gsvk

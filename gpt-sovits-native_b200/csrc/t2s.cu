@@ -1,0 +1,1016 @@
+// t2s.cu — the T2S autoregressive transformer on the device
+// (GPT-SoVITS-native src/ar/t2s_engine.cpp), post-LN, fused QKV, ReLU FFN.
+//
+// All arithmetic follows the canonical association of canon.cuh, which the
+// CPU oracle evaluates identically: decode is bit-exact against it.
+//
+// Prefill (block_prefill_impl, t2s_engine.cpp:881-1034): per layer, four
+// canonical-order GEMMs (one warp per 4x4 output tile, fused bias / ReLU /
+// residual), a KV append, the chunked-softmax attention and two LayerNorms.
+//
+// Decode (block_decode_impl + greedy_sample + the generate loop,
+// t2s_engine.cpp:1036-1119, 1594-1636, 1839-1900): ONE persistent cooperative
+// kernel runs every step of the generation.  Per layer it has five phases
+// separated by grid barriers:
+//   P1  x = LN2(prev) ; q|k|v = Wqkv . f16(x) + b ; k, v -> fp16 KV slot
+//   P2  attention partials per (head, key chunk)  (split-K softmax)
+//   P3  combine partials ; hpre = Wout . f16(attn) + b + x
+//   P4  h = LN1(hpre) ; ff = relu(W1 . f16(h) + b)
+//   P5  xpre = W2 . ff + b + h          (fp32 activations, as the reference)
+// then logits = Wpred . LN2(xpre) and every CTA redundantly applies the
+// repetition penalty and takes the argmax, so the next token's embedding
+// needs no extra barrier.  Each CTA owns fixed row slices of every weight
+// matrix and streams them into shared memory one layer ahead with bulk
+// copies, so HBM streaming overlaps the barrier latency chain.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "canon.cuh"
+#include "gsvk_internal.hpp"
+
+struct gsvk_t2s;
+
+namespace gsvk {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kChunk = 128;      // softmax chunk (slots), fixed by the canonical order
+constexpr int kMaxChunks = 128;  // chunks per head (cap <= 16384 slots)
+constexpr uint32_t kGridSpin = 1u << 23;
+
+struct T2SDev {
+  int L, D, H, F, V, cap, HD;
+  float eps, alpha, scale;
+  const uint16_t *wqkv, *wout, *w1, *w2, *wpred, *emb;
+  const float *bqkv, *bout, *b1, *b2, *n1g, *n1b, *n2g, *n2b, *pe;
+  uint16_t *kc, *vc;
+  float *q, *part, *hpre, *ff, *xpre, *logits;
+  unsigned* bar;
+  uint32_t* status;
+};
+
+struct DecodeArgs {
+  int pos0;       // KV slot of the first decoded token
+  int pe0;        // position-encoding index of the first decoded token (= P)
+  int max_steps;
+  int stop_on_eos;
+  const int32_t* hist;
+  int n_hist;
+  int32_t* tokens;
+  int* n_out;
+  float* margins;
+  // shared-memory plan (identical in every CTA)
+  int mq, mo, m1, m2, ml;  // max rows per CTA of qkv / out / w1 / w2 / logits
+  uint32_t layer_bytes;
+};
+
+__host__ __device__ inline int row_lo(int rows, int g, int c) {
+  return static_cast<int>(static_cast<long long>(rows) * c / g);
+}
+
+// ----------------------------------------------------------- block helpers
+__device__ __forceinline__ float blk_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : -INFINITY;
+  return warp_max(t);
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier on a monotonically increasing counter (reset by the host
+// before each launch).  Bounded: on timeout, or when another CTA has already
+// flagged one, it returns false and the kernel winds down.
+__device__ bool grid_sync(unsigned* bar, unsigned& epoch, uint32_t* status, int* flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ++epoch;
+    const unsigned target = epoch * gridDim.x;
+    __threadfence();
+    atomicAdd(bar, 1u);
+    int ok = 1;
+    for (uint32_t i = 0;; ++i) {
+      const unsigned v = ld_acquire(bar);
+      if (static_cast<int>(v - target) >= 0) break;
+      if ((i & 1023u) == 1023u && *reinterpret_cast<volatile uint32_t*>(status) != 0) {
+        ok = 0;
+        break;
+      }
+      if (i > kGridSpin) {
+        atomicExch(status, DEV_TIMEOUT);
+        ok = 0;
+        break;
+      }
+    }
+    __threadfence();
+    *flag = ok;
+  }
+  __syncthreads();
+  return *flag != 0;
+}
+
+// One attention chunk of the canonical softmax for head h: slots [k0, k1) of
+// a token-major fp16 cache (row stride D).  Stages the chunk's K and V rows
+// in shared memory, computes the scores with group16_dot_kv, the chunk max,
+// exp_det weights, and the two sequential sums (l by thread 0, o by warp 1,
+// one lane per dimension).  Writes {m, l, o[HD]} to dst.  Whole block.
+template <int HD>
+__device__ void attn_chunk(const float* qv, const uint16_t* kcache, const uint16_t* vcache, int D,
+                           int k0, int k1, float scale, uint16_t* kst, uint16_t* vst, float* sc,
+                           float* red, float* dst) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nk = k1 - k0;
+  constexpr int kV = HD / 8;  // uint4 per row slice
+  for (int i = tid; i < nk * kV; i += blockDim.x) {
+    const int key = i / kV, part = i - (i / kV) * kV;
+    const size_t off = static_cast<size_t>(k0 + key) * D;
+    reinterpret_cast<uint4*>(kst)[i] = __ldcg(reinterpret_cast<const uint4*>(kcache + off) + part);
+    reinterpret_cast<uint4*>(vst)[i] = __ldcg(reinterpret_cast<const uint4*>(vcache + off) + part);
+  }
+  float q_reg[HD / 16];
+#pragma unroll
+  for (int c = 0; c < HD / 16; ++c) q_reg[c] = __ldcg(qv + 16 * c + (lane & 15));
+  __syncthreads();
+  const int groups = blockDim.x >> 4, g = tid >> 4;
+  for (int base = 0; base < nk; base += groups) {
+    const int key = base + g;
+    const int kk = key < nk ? key : nk - 1;
+    const float d = group16_dot_kv<HD>(q_reg, kst + kk * HD);
+    if ((tid & 15) == 0 && key < nk) sc[key] = __fmul_rn(d, scale);
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int k = tid; k < nk; k += blockDim.x) mx = fmaxf(mx, sc[k]);
+  mx = blk_max(mx, red);
+  for (int k = tid; k < nk; k += blockDim.x) sc[k] = exp_det(__fsub_rn(sc[k], mx));
+  __syncthreads();
+  if (tid == 0) {
+    float l = 0.f;
+    for (int k = 0; k < nk; ++k) l = __fadd_rn(l, sc[k]);
+    dst[0] = mx;
+    dst[1] = l;
+  } else if (warp == 1) {
+    float o0 = 0.f, o1 = 0.f;
+    for (int k = 0; k < nk; ++k) {
+      const float p = sc[k];
+      o0 = __fadd_rn(o0, __fmul_rn(p, h2f(vst[k * HD + lane])));
+      if (HD > 32) o1 = __fadd_rn(o1, __fmul_rn(p, h2f(vst[k * HD + 32 + lane])));
+    }
+    dst[2 + lane] = o0;
+    if (HD > 32) dst[2 + 32 + lane] = o1;
+  }
+  __syncthreads();
+}
+
+// Combine nch chunk records {m, l, o[HD]} (stride HD+2) of one head; one
+// warp, every lane returns dims lane (and lane+32).
+template <int HD>
+__device__ __forceinline__ void attn_combine(const float* rec, int nch, bool cg, float* out0,
+                                             float* out1) {
+  const int lane = threadIdx.x & 31;
+  auto rd = [cg](const float* p) { return cg ? __ldcg(p) : *p; };
+  float M = -INFINITY;
+  for (int c = 0; c < nch; ++c) M = fmaxf(M, rd(rec + c * (HD + 2)));
+  float L = 0.f, O0 = 0.f, O1 = 0.f;
+  for (int c = 0; c < nch; ++c) {
+    const float* r = rec + c * (HD + 2);
+    const float w = exp_det(__fsub_rn(rd(r), M));
+    L = __fadd_rn(L, __fmul_rn(rd(r + 1), w));
+    O0 = __fadd_rn(O0, __fmul_rn(rd(r + 2 + lane), w));
+    if (HD > 32) O1 = __fadd_rn(O1, __fmul_rn(rd(r + 2 + 32 + lane), w));
+  }
+  const float inv = __fdiv_rn(1.0f, L);
+  *out0 = __fmul_rn(O0, inv);
+  *out1 = HD > 32 ? __fmul_rn(O1, inv) : 0.f;
+}
+
+struct Slices {
+  int q0, q1, o0, o1, a0, a1, b0, b1, l0, l1;
+};
+
+__device__ Slices my_slices(const T2SDev& m) {
+  const int G = gridDim.x, c = blockIdx.x;
+  Slices s;
+  s.q0 = row_lo(3 * m.D, G, c);
+  s.q1 = row_lo(3 * m.D, G, c + 1);
+  s.o0 = row_lo(m.D, G, c);
+  s.o1 = row_lo(m.D, G, c + 1);
+  s.a0 = row_lo(m.F, G, c);
+  s.a1 = row_lo(m.F, G, c + 1);
+  s.b0 = row_lo(m.D, G, c);
+  s.b1 = row_lo(m.D, G, c + 1);
+  s.l0 = row_lo(m.V, G, c);
+  s.l1 = row_lo(m.V, G, c + 1);
+  return s;
+}
+
+// Thread 0 only: stream this CTA's slices of layer l into `buf`.
+__device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slices& s, int l,
+                               uint8_t* buf, uint64_t* bar) {
+  const size_t D = m.D, F = m.F;
+  const uint32_t bq = (s.q1 - s.q0) * D * 2, bo = (s.o1 - s.o0) * D * 2,
+                 b1 = (s.a1 - s.a0) * D * 2, b2 = (s.b1 - s.b0) * F * 2;
+  mbar_arrive_expect_tx(bar, bq + bo + b1 + b2);
+  uint8_t* p = buf;
+  if (bq) bulk_load(p, m.wqkv + (static_cast<size_t>(l) * 3 * D + s.q0) * D, bq, bar);
+  p = buf + static_cast<size_t>(a.mq) * D * 2;
+  if (bo) bulk_load(p, m.wout + (static_cast<size_t>(l) * D + s.o0) * D, bo, bar);
+  p += static_cast<size_t>(a.mo) * D * 2;
+  if (b1) bulk_load(p, m.w1 + (static_cast<size_t>(l) * F + s.a0) * D, b1, bar);
+  p += static_cast<size_t>(a.m1) * D * 2;
+  if (b2) bulk_load(p, m.w2 + (static_cast<size_t>(l) * D + s.b0) * F, b2, bar);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m, const DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                             ~static_cast<uintptr_t>(127));
+  const int D = m.D, F = m.F, V = m.V, H = m.H, L = m.L;
+  uint8_t* wbuf[2] = {smem, smem + a.layer_bytes};
+  uint16_t* wlog = reinterpret_cast<uint16_t*>(smem + 2 * static_cast<size_t>(a.layer_bytes));
+  uint16_t* kst = wlog + static_cast<size_t>(a.ml) * D;   // [kChunk][HD] staged K
+  uint16_t* vst = kst + kChunk * HD;                      // [kChunk][HD] staged V
+  float* xs = reinterpret_cast<float*>(vst + kChunk * HD); // layer input x
+  float* hs = xs + D;                                     // LN1 output h
+  float* act = hs + D;                                    // operand, max(D, F)
+  float* sc = act + (F > D ? F : D);                      // chunk scores / weights
+  float* red = sc + kChunk;                               // 64 floats
+  int* flag = reinterpret_cast<int*>(red + 64);
+  int* tokp = flag + 4;
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(tokp + 4);
+  uint8_t* seen = reinterpret_cast<uint8_t*>(mbar + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+  const Slices s = my_slices(m);
+  unsigned epoch = 0;
+  uint32_t uses[2] = {0, 0};
+  const int eos = V - 1;
+
+  for (int c = tid; c < V; c += kThreads) seen[c] = 0;
+  __syncthreads();
+  for (int i = tid; i < a.n_hist; i += kThreads) {
+    const int t = a.hist[i];
+    if (t >= 0 && t < V) seen[t] = 1;
+  }
+  if (tid == 0) {
+    mbar_init(&mbar[0], 1);
+    mbar_init(&mbar[1], 1);
+    mbar_init(&mbar[2], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t bl = (s.l1 - s.l0) * D * 2;
+    mbar_arrive_expect_tx(&mbar[2], bl);
+    if (bl) bulk_load(wlog, m.wpred + static_cast<size_t>(s.l0) * D, bl, &mbar[2]);
+    // the global layer sequence g = 0, 1, 2, ... runs layer g % L from buffer g & 1
+    prefetch_layer(m, a, s, 0, wbuf[0], &mbar[0]);
+    prefetch_layer(m, a, s, 1 % L, wbuf[1], &mbar[1]);
+  }
+  uint32_t pending[2] = {1u, 1u};
+  unsigned gl = 0;
+  bool alive = mbar_wait(&mbar[2], 0, m.status);
+
+  int n_out = 0;
+  for (int idx = 0; idx < a.max_steps && alive; ++idx) {
+    // ------------------------------------------------ greedy sample (all CTAs)
+    // t2s_engine.cpp:1594-1636: penalty once per distinct history token,
+    // EOS excluded while idx < 11, first maximum wins.
+    const int eos_allowed = idx >= 11;
+    const int limit = eos_allowed ? V : V - 1;
+    float bv = -INFINITY, sv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = tid; c < limit; c += kThreads) {
+      float v = __ldcg(m.logits + c);
+      if (seen[c]) v = v < 0.f ? __fmul_rn(v, 1.35f) : __fdiv_rn(v, 1.35f);
+      if (v > bv || (v == bv && c < bi)) {
+        sv = bv;
+        bv = v;
+        bi = c;
+      } else if (v > sv) {
+        sv = v;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const float os = __shfl_xor_sync(0xffffffffu, sv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        sv = fmaxf(os, bv);
+        bv = ov;
+        bi = oi;
+      } else {
+        sv = fmaxf(sv, ov);
+      }
+    }
+    __syncthreads();
+    if (lane == 0) {
+      red[warp] = bv;
+      red[kWarps + warp] = sv;
+      reinterpret_cast<int*>(red + 2 * kWarps)[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float B = red[0], S = red[kWarps];
+      int I = reinterpret_cast<int*>(red + 2 * kWarps)[0];
+      for (int w = 1; w < kWarps; ++w) {
+        const float ov = red[w], os = red[kWarps + w];
+        const int oi = reinterpret_cast<int*>(red + 2 * kWarps)[w];
+        if (ov > B || (ov == B && oi < I)) {
+          S = fmaxf(os, B);
+          B = ov;
+          I = oi;
+        } else {
+          S = fmaxf(S, ov);
+        }
+      }
+      tokp[0] = I;
+      if (blockIdx.x == 0 && a.margins) a.margins[idx] = __fsub_rn(B, S);
+    }
+    __syncthreads();
+    const int tok = tokp[0];
+    bool stop = false;
+    if (a.stop_on_eos && eos_allowed && tok == eos) {
+      stop = true;
+    } else {
+      if (blockIdx.x == 0 && tid == 0) a.tokens[n_out] = tok;
+      ++n_out;
+      if (tid == 0) seen[tok] = 1;
+    }
+    if (idx + 1 == a.max_steps) stop = true;
+    __syncthreads();
+    if (stop) break;
+
+    // ------------------------------------- next input: emb[tok] + alpha*PE
+    const int pos = a.pos0 + idx;
+    const int len = pos + 1;
+    {
+      const uint16_t* er = m.emb + static_cast<size_t>(tok) * D;
+      const float* pr = m.pe + static_cast<size_t>(a.pe0 + idx) * D;
+      for (int i = tid; i < D; i += kThreads) xs[i] = fmaf(m.alpha, pr[i], h2f(er[i]));
+    }
+    __syncthreads();
+    const int nch = (len + kChunk - 1) / kChunk;
+
+    for (int l = 0; l < L && alive; ++l, ++gl) {
+      const int b = static_cast<int>(gl & 1u);
+      const uint16_t* Wq = reinterpret_cast<const uint16_t*>(wbuf[b]);
+      const uint16_t* Wo = Wq + static_cast<size_t>(a.mq) * D;
+      const uint16_t* W1 = Wo + static_cast<size_t>(a.mo) * D;
+      const uint16_t* W2 = W1 + static_cast<size_t>(a.m1) * D;
+      // ---------------------------------------------------------------- P1
+      if (l > 0) {
+        for (int i = tid; i < D; i += kThreads) xs[i] = __ldcg(m.xpre + i);
+        __syncthreads();
+        ln_canon(xs, m.n2g + static_cast<size_t>(l - 1) * D, m.n2b + static_cast<size_t>(l - 1) * D,
+                 D, m.eps, red);
+      }
+      for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(xs[i]));
+      if (!mbar_wait(&mbar[b], uses[b] & 1u, m.status)) {
+        alive = false;
+        break;
+      }
+      ++uses[b];
+      pending[b] = 0;
+      __syncthreads();
+      {
+        uint16_t* kl = m.kc + (static_cast<size_t>(l) * m.cap + pos) * D;
+        uint16_t* vl = m.vc + (static_cast<size_t>(l) * m.cap + pos) * D;
+        const float* bq = m.bqkv + static_cast<size_t>(l) * 3 * D;
+        for (int r = s.q0 + warp; r < s.q1; r += kWarps) {
+          const float acc = warp_dot32(Wq + static_cast<size_t>(r - s.q0) * D, act, D);
+          if (lane == 0) {
+            const float v = __fadd_rn(acc, bq[r]);
+            if (r < D)
+              m.q[r] = v;
+            else if (r < 2 * D)
+              kl[r - D] = f2h(v);
+            else
+              vl[r - 2 * D] = f2h(v);
+          }
+        }
+      }
+      if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      // ---------------------------------------------------------------- P2
+      for (int item = blockIdx.x; item < H * nch; item += G) {
+        const int h = item / nch, c = item - (item / nch) * nch;
+        const int k0 = c * kChunk, k1 = min(len, k0 + kChunk);
+        attn_chunk<HD>(m.q + h * HD, m.kc + static_cast<size_t>(l) * m.cap * D + h * HD,
+                       m.vc + static_cast<size_t>(l) * m.cap * D + h * HD, D, k0, k1, m.scale, kst,
+                       vst, sc, red, m.part + (static_cast<size_t>(h) * kMaxChunks + c) * (HD + 2));
+      }
+      if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      // ---------------------------------------------------------------- P3
+      for (int h = warp; h < H; h += kWarps) {
+        float o0, o1;
+        attn_combine<HD>(m.part + static_cast<size_t>(h) * kMaxChunks * (HD + 2), nch, true, &o0,
+                         &o1);
+        act[h * HD + lane] = h2f(f2h(o0));
+        if (HD > 32) act[h * HD + 32 + lane] = h2f(f2h(o1));
+      }
+      __syncthreads();
+      {
+        const float* bo = m.bout + static_cast<size_t>(l) * D;
+        for (int r = s.o0 + warp; r < s.o1; r += kWarps) {
+          const float acc = warp_dot32(Wo + static_cast<size_t>(r - s.o0) * D, act, D);
+          if (lane == 0) m.hpre[r] = __fadd_rn(__fadd_rn(acc, bo[r]), xs[r]);
+        }
+      }
+      if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      // ---------------------------------------------------------------- P4
+      for (int i = tid; i < D; i += kThreads) hs[i] = __ldcg(m.hpre + i);
+      __syncthreads();
+      ln_canon(hs, m.n1g + static_cast<size_t>(l) * D, m.n1b + static_cast<size_t>(l) * D, D, m.eps,
+               red);
+      for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(hs[i]));
+      __syncthreads();
+      {
+        const float* bb = m.b1 + static_cast<size_t>(l) * F;
+        for (int r = s.a0 + warp; r < s.a1; r += kWarps) {
+          const float acc = warp_dot32(W1 + static_cast<size_t>(r - s.a0) * D, act, D);
+          if (lane == 0) {
+            const float v = __fadd_rn(acc, bb[r]);
+            m.ff[r] = v > 0.f ? v : 0.f;
+          }
+        }
+      }
+      if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      // ---------------------------------------------------------------- P5
+      for (int i = tid; i < F; i += kThreads) act[i] = __ldcg(m.ff + i);
+      __syncthreads();
+      {
+        const float* bb = m.b2 + static_cast<size_t>(l) * D;
+        for (int r = s.b0 + warp; r < s.b1; r += kWarps) {
+          const float acc = warp_dot32(W2 + static_cast<size_t>(r - s.b0) * F, act, F);
+          if (lane == 0) m.xpre[r] = __fadd_rn(__fadd_rn(acc, bb[r]), hs[r]);
+        }
+      }
+      __syncthreads();  // every warp is done with wbuf[b]
+      if (tid == 0) {
+        prefetch_layer(m, a, s, (l + 2) % L, wbuf[b], &mbar[b]);  // global layer gl + 2
+        pending[b] = 1;
+      }
+      if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+    }
+    if (!alive) break;
+    // ---------------------------------------------------------------- logits
+    for (int i = tid; i < D; i += kThreads) xs[i] = __ldcg(m.xpre + i);
+    __syncthreads();
+    ln_canon(xs, m.n2g + static_cast<size_t>(L - 1) * D, m.n2b + static_cast<size_t>(L - 1) * D, D,
+             m.eps, red);
+    for (int r = s.l0 + warp; r < s.l1; r += kWarps) {
+      const float acc = warp_dot32(wlog + static_cast<size_t>(r - s.l0) * D, xs, D);
+      if (lane == 0) m.logits[r] = acc;
+    }
+    if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+  }
+  // Drain bulk copies still in flight before the CTA exits.
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b)
+      if (pending[b]) mbar_wait(&mbar[b], uses[b] & 1u, m.status);
+    if (blockIdx.x == 0 && a.n_out) *a.n_out = n_out;
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------ prefill kernels
+__global__ void embed_kernel(const int32_t* __restrict__ ids, int P, const uint16_t* __restrict__ emb,
+                             const float* __restrict__ pe, int pe0, float alpha, int D,
+                             float* __restrict__ x, uint16_t* __restrict__ x16) {
+  const int t = blockIdx.x;
+  const uint16_t* er = emb + static_cast<size_t>(ids[t]) * D;
+  const float* pr = pe + static_cast<size_t>(pe0 + t) * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float v = fmaf(alpha, pr[i], h2f(er[i]));
+    x[static_cast<size_t>(t) * D + i] = v;
+    x16[static_cast<size_t>(t) * D + i] = f2h(v);
+  }
+}
+
+__global__ void kv_append_kernel(const float* __restrict__ qkv, int S, int D, uint16_t* kc,
+                                 uint16_t* vc, int pos) {
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    kc[static_cast<size_t>(pos + t) * D + i] = f2h(qkv[static_cast<size_t>(t) * 3 * D + D + i]);
+    vc[static_cast<size_t>(pos + t) * D + i] = f2h(qkv[static_cast<size_t>(t) * 3 * D + 2 * D + i]);
+  }
+}
+
+// C[m, n] = epi(dot32(B[n], A[m])), A and B fp16 row-major; one warp per 4x4
+// output tile, each output's 32 canonical accumulators spread over the lanes.
+// epi: + bias[n], ReLU, + residual[m, n], stored as fp32 and/or fp16.
+__global__ void __launch_bounds__(256) canon_gemm_kernel(
+    const uint16_t* __restrict__ A, int lda, const uint16_t* __restrict__ B, int ldb, int M, int N,
+    int K, const float* __restrict__ bias, int relu, const float* __restrict__ res, int ldr,
+    float* __restrict__ c32, int ldc, uint16_t* __restrict__ c16, int ldc16) {
+  const int lane = threadIdx.x & 31;
+  const long long wid = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 5;
+  const int n_tiles = (N + 3) / 4;
+  const long long mt = wid / n_tiles;
+  const int nt = static_cast<int>(wid - mt * n_tiles);
+  if (mt * 4 >= M) return;
+  int mr[4], nr[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    mr[i] = min(static_cast<int>(mt * 4) + i, M - 1);
+    nr[i] = min(nt * 4 + i, N - 1);
+  }
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+  const int vec_end = K & ~63;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int k = 0; k < vec_end; k += 64) {
+    float alo[4], ahi[4], blo[4], bhi[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint16_t* ar = A + static_cast<size_t>(mr[i]) * lda + k + o0;
+      alo[i] = h2f(ar[0]);
+      ahi[i] = h2f(ar[4]);
+      const uint16_t* br = B + static_cast<size_t>(nr[i]) * ldb + k + o0;
+      blo[i] = h2f(br[0]);
+      bhi[i] = h2f(br[4]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[i][j] = fmaf(blo[j], alo[i], acc[i][j]);
+        acc[i][j] = fmaf(bhi[j], ahi[i], acc[i][j]);
+      }
+  }
+  float outv = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = acc[i][j];
+      const float t = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+      const float u = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+      float sum = __shfl_sync(0xffffffffu, u, 0);
+#pragma unroll
+      for (int g = 1; g < 8; ++g) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, u, 4 * g));
+      for (int k = vec_end; k < K; ++k)
+        sum = fmaf(h2f(B[static_cast<size_t>(nr[j]) * ldb + k]), h2f(A[static_cast<size_t>(mr[i]) * lda + k]), sum);
+      if (lane == i * 4 + j) outv = sum;
+    }
+  if (lane < 16) {
+    const int i = lane >> 2, j = lane & 3;
+    const int mm = static_cast<int>(mt * 4) + i, nn = nt * 4 + j;
+    if (mm < M && nn < N) {
+      float v = outv;
+      if (bias) v = __fadd_rn(v, bias[nn]);
+      if (relu) v = v > 0.f ? v : 0.f;
+      if (res) v = __fadd_rn(v, res[static_cast<size_t>(mm) * ldr + nn]);
+      if (c32) c32[static_cast<size_t>(mm) * ldc + nn] = v;
+      if (c16) c16[static_cast<size_t>(mm) * ldc16 + nn] = f2h(v);
+    }
+  }
+}
+
+// y[r] = dot32(W[r], x) with fp32 x (logits head), one warp per row.
+__global__ void canon_gemv_kernel(const uint16_t* __restrict__ w, const float* __restrict__ x,
+                                  float* __restrict__ y, int out, int in) {
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (r >= out) return;
+  const float acc = warp_dot32(w + static_cast<size_t>(r) * in, x, in);
+  if ((threadIdx.x & 31) == 0) y[r] = acc;
+}
+
+// Masked prefill attention (t2s_engine.cpp:944-979) in the canonical chunked
+// softmax: query q of the block sees slots [0, pos + max(text_len, q+1)).
+template <int HD>
+__global__ void __launch_bounds__(128) prefill_attn_kernel(
+    const float* __restrict__ qkv, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
+    int D, int pos, int text_len, float scale, uint16_t* __restrict__ out16) {
+  extern __shared__ uint8_t psm[];
+  uint16_t* kst = reinterpret_cast<uint16_t*>(psm);
+  uint16_t* vst = kst + kChunk * HD;
+  float* sc = reinterpret_cast<float*>(vst + kChunk * HD);
+  float* red = sc + kChunk;
+  float* rec = red + 64;  // [nch][HD + 2]
+  const int q = blockIdx.x, h = blockIdx.y;
+  const int n = pos + max(text_len, q + 1);
+  const int nch = (n + kChunk - 1) / kChunk;
+  const float* qv = qkv + static_cast<size_t>(q) * 3 * D + h * HD;
+  for (int c = 0; c < nch; ++c)
+    attn_chunk<HD>(qv, kc + h * HD, vc + h * HD, D, c * kChunk, min(n, (c + 1) * kChunk), scale, kst,
+                   vst, sc, red, rec + c * (HD + 2));
+  if (threadIdx.x < 32) {
+    float o0, o1;
+    attn_combine<HD>(rec, nch, false, &o0, &o1);
+    out16[static_cast<size_t>(q) * D + h * HD + threadIdx.x] = f2h(o0);
+    if (HD > 32) out16[static_cast<size_t>(q) * D + h * HD + 32 + threadIdx.x] = f2h(o1);
+  }
+}
+
+// Row LayerNorm (kern.cpp:27-58, canonical order) writing fp32 and fp16.
+__global__ void __launch_bounds__(256) ln_rows_canon_kernel(
+    const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
+    float* __restrict__ y, uint16_t* __restrict__ y16, int n, double eps) {
+  __shared__ float scratch[32];
+  __shared__ float buf[4096];
+  const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) buf[i] = xr[i];
+  __syncthreads();
+  ln_canon(buf, g, b, n, eps, scratch);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    y[static_cast<size_t>(blockIdx.x) * n + i] = buf[i];
+    y16[static_cast<size_t>(blockIdx.x) * n + i] = f2h(buf[i]);
+  }
+}
+
+int canon_gemm(const uint16_t* A, int lda, const uint16_t* B, int ldb, int M, int N, int K,
+               const float* bias, int relu, const float* res, int ldr, float* c32, int ldc,
+               uint16_t* c16, int ldc16, cudaStream_t st) {
+  const long long warps = static_cast<long long>((M + 3) / 4) * ((N + 3) / 4);
+  canon_gemm_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, st>>>(
+      A, lda, B, ldb, M, N, K, bias, relu, res, ldr, c32, ldc, c16, ldc16);
+  return check_launch("canon_gemm_kernel");
+}
+}  // namespace
+
+// --------------------------------------------------------------- host engine
+struct T2SEngine {
+  int L, D, H, F, V, cap;
+  float eps, alpha;
+  T2SDev dev{};
+  int G = 0;                 // decode CTAs
+  int HD = 0;
+  DecodeArgs plan{};
+  size_t decode_smem = 0;
+  size_t attn_smem = 0;      // prefill attention dynamic shared memory
+  const void* decode_fn = nullptr;
+  const void* attn_fn = nullptr;
+  // device allocations
+  void* weights = nullptr;   // one block: all fp16 weights + fp32 vectors + PE table
+  void* scratch = nullptr;
+  int32_t* d_prompt = nullptr;
+  int32_t* d_tokens = nullptr;
+  int* d_nout = nullptr;
+  float* d_margins = nullptr;
+  // prefill buffers
+  float *px = nullptr, *pqkv = nullptr, *phpre = nullptr;
+  uint16_t *px16 = nullptr, *pattn16 = nullptr, *pff16 = nullptr;
+};
+
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// PE row as the reference computes it (t2s_engine.cpp:711-720).
+void pe_row_host(int D, size_t pos, float* pe) {
+  const float log_inc = static_cast<float>(-std::log(10000.0) / static_cast<double>(D));
+  const float p = static_cast<float>(pos);
+  for (int d = 0; d < D; d += 2) {
+    const float div = std::exp(static_cast<float>(d) * log_inc);
+    pe[d] = std::sin(p * div);
+    pe[d + 1] = std::cos(p * div);
+  }
+}
+
+}  // namespace
+
+}  // namespace gsvk
+
+using namespace gsvk;
+
+struct gsvk_t2s : gsvk::T2SEngine {};
+
+extern "C" {
+
+int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, gsvk_t2s_t* out) {
+  if (!cfg || !w || !out) return fail(GSVK_ERR_INVALID, "t2s_create: null argument");
+  *out = nullptr;
+  if (!gsvk_available()) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
+  const int L = cfg->n_layers, D = cfg->d_model, H = cfg->n_heads, F = cfg->ffn, V = cfg->vocab;
+  const int cap = cfg->cap;
+  if (L <= 0 || D <= 0 || H <= 0 || F <= 0 || V <= 1 || cap <= 0 || D % H != 0)
+    return fail(GSVK_ERR_INVALID, "t2s_create: bad dimensions");
+  const int HD = D / H;
+  if ((HD != 32 && HD != 64) || D % 8 != 0 || F % 8 != 0 || D > 4096 || F > 16384)
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s_create: head_dim must be 32 or 64, D,F multiples of 8");
+  if (cap > kMaxChunks * kChunk) return fail(GSVK_ERR_UNSUPPORTED, "t2s_create: cap too large");
+  if (!w->wqkv || !w->bqkv || !w->wout || !w->bout || !w->w1 || !w->b1 || !w->w2 || !w->b2 ||
+      !w->n1g || !w->n1b || !w->n2g || !w->n2b || !w->wpred || !w->audio_emb)
+    return fail(GSVK_ERR_INVALID, "t2s_create: null weight");
+  auto* e = new gsvk_t2s();
+  e->L = L; e->D = D; e->H = H; e->F = F; e->V = V; e->cap = cap;
+  e->eps = cfg->ln_eps; e->alpha = cfg->alpha_audio;
+
+  // ---- weights: fp16 matrices, fp32 vectors, PE table (one allocation)
+  const size_t nqkv = (size_t)L * 3 * D * D, nout = (size_t)L * D * D, n1 = (size_t)L * F * D,
+               n2 = (size_t)L * D * F, npred = (size_t)V * D, nemb = (size_t)V * D;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+  const size_t o_wqkv = take(nqkv * 2), o_wout = take(nout * 2), o_w1 = take(n1 * 2),
+               o_w2 = take(n2 * 2), o_pred = take(npred * 2), o_emb = take(nemb * 2);
+  const size_t o_bqkv = take((size_t)L * 3 * D * 4), o_bout = take((size_t)L * D * 4),
+               o_b1 = take((size_t)L * F * 4), o_b2 = take((size_t)L * D * 4),
+               o_n1g = take((size_t)L * D * 4), o_n1b = take((size_t)L * D * 4),
+               o_n2g = take((size_t)L * D * 4), o_n2b = take((size_t)L * D * 4),
+               o_pe = take((size_t)cap * D * 4);
+  if (cudaMalloc(&e->weights, off) != cudaSuccess) {
+    cudaGetLastError();
+    delete e;
+    return fail(GSVK_ERR_NOMEM, "t2s_create: weights (%zu bytes)", off);
+  }
+  uint8_t* base = static_cast<uint8_t*>(e->weights);
+  struct Up { size_t o; const void* src; size_t bytes; };
+  std::vector<float> pe((size_t)cap * D);
+  for (int p = 0; p < cap; ++p) pe_row_host(D, p, pe.data() + (size_t)p * D);
+  const Up ups[] = {{o_wqkv, w->wqkv, nqkv * 2}, {o_wout, w->wout, nout * 2}, {o_w1, w->w1, n1 * 2},
+                    {o_w2, w->w2, n2 * 2}, {o_pred, w->wpred, npred * 2}, {o_emb, w->audio_emb, nemb * 2},
+                    {o_bqkv, w->bqkv, (size_t)L * 3 * D * 4}, {o_bout, w->bout, (size_t)L * D * 4},
+                    {o_b1, w->b1, (size_t)L * F * 4}, {o_b2, w->b2, (size_t)L * D * 4},
+                    {o_n1g, w->n1g, (size_t)L * D * 4}, {o_n1b, w->n1b, (size_t)L * D * 4},
+                    {o_n2g, w->n2g, (size_t)L * D * 4}, {o_n2b, w->n2b, (size_t)L * D * 4},
+                    {o_pe, pe.data(), (size_t)cap * D * 4}};
+  for (const Up& u : ups) {
+    int rc = check_cuda(cudaMemcpy(base + u.o, u.src, u.bytes, cudaMemcpyHostToDevice), "t2s upload");
+    if (rc) { gsvk_t2s_destroy(e); return rc; }
+  }
+  T2SDev& d = e->dev;
+  d.L = L; d.D = D; d.H = H; d.F = F; d.V = V; d.cap = cap; d.HD = HD;
+  d.eps = cfg->ln_eps; d.alpha = cfg->alpha_audio;
+  d.scale = 1.0f / std::sqrt(static_cast<float>(HD));
+  d.wqkv = reinterpret_cast<const uint16_t*>(base + o_wqkv);
+  d.wout = reinterpret_cast<const uint16_t*>(base + o_wout);
+  d.w1 = reinterpret_cast<const uint16_t*>(base + o_w1);
+  d.w2 = reinterpret_cast<const uint16_t*>(base + o_w2);
+  d.wpred = reinterpret_cast<const uint16_t*>(base + o_pred);
+  d.emb = reinterpret_cast<const uint16_t*>(base + o_emb);
+  d.bqkv = reinterpret_cast<const float*>(base + o_bqkv);
+  d.bout = reinterpret_cast<const float*>(base + o_bout);
+  d.b1 = reinterpret_cast<const float*>(base + o_b1);
+  d.b2 = reinterpret_cast<const float*>(base + o_b2);
+  d.n1g = reinterpret_cast<const float*>(base + o_n1g);
+  d.n1b = reinterpret_cast<const float*>(base + o_n1b);
+  d.n2g = reinterpret_cast<const float*>(base + o_n2g);
+  d.n2b = reinterpret_cast<const float*>(base + o_n2b);
+  d.pe = reinterpret_cast<const float*>(base + o_pe);
+
+  // ---- KV cache + decode scratch + prefill buffers (one allocation)
+  off = 0;
+  const size_t o_kc = take((size_t)L * cap * D * 2), o_vc = take((size_t)L * cap * D * 2),
+               o_q = take((size_t)D * 4), o_part = take((size_t)H * kMaxChunks * (HD + 2) * 4),
+               o_hpre = take((size_t)D * 4), o_ff = take((size_t)F * 4), o_xpre = take((size_t)D * 4),
+               o_logits = take((size_t)V * 4), o_bar = take(256), o_prompt = take((size_t)cap * 4),
+               o_tok = take((size_t)cap * 4), o_nout = take(256), o_marg = take((size_t)cap * 4),
+               o_px = take((size_t)cap * D * 4), o_pqkv = take((size_t)cap * 3 * D * 4),
+               o_phpre = take((size_t)cap * D * 4), o_px16 = take((size_t)cap * D * 2),
+               o_pattn = take((size_t)cap * D * 2), o_pff = take((size_t)cap * F * 2);
+  if (cudaMalloc(&e->scratch, off) != cudaSuccess) {
+    cudaGetLastError();
+    gsvk_t2s_destroy(e);
+    return fail(GSVK_ERR_NOMEM, "t2s_create: scratch (%zu bytes)", off);
+  }
+  uint8_t* sb = static_cast<uint8_t*>(e->scratch);
+  if (int rc = check_cuda(cudaMemset(sb, 0, off), "t2s scratch memset")) {
+    gsvk_t2s_destroy(e);
+    return rc;
+  }
+  d.kc = reinterpret_cast<uint16_t*>(sb + o_kc);
+  d.vc = reinterpret_cast<uint16_t*>(sb + o_vc);
+  d.q = reinterpret_cast<float*>(sb + o_q);
+  d.part = reinterpret_cast<float*>(sb + o_part);
+  d.hpre = reinterpret_cast<float*>(sb + o_hpre);
+  d.ff = reinterpret_cast<float*>(sb + o_ff);
+  d.xpre = reinterpret_cast<float*>(sb + o_xpre);
+  d.logits = reinterpret_cast<float*>(sb + o_logits);
+  d.bar = reinterpret_cast<unsigned*>(sb + o_bar);
+  d.status = device_status();
+  e->d_prompt = reinterpret_cast<int32_t*>(sb + o_prompt);
+  e->d_tokens = reinterpret_cast<int32_t*>(sb + o_tok);
+  e->d_nout = reinterpret_cast<int*>(sb + o_nout);
+  e->d_margins = reinterpret_cast<float*>(sb + o_marg);
+  e->px = reinterpret_cast<float*>(sb + o_px);
+  e->pqkv = reinterpret_cast<float*>(sb + o_pqkv);
+  e->phpre = reinterpret_cast<float*>(sb + o_phpre);
+  e->px16 = reinterpret_cast<uint16_t*>(sb + o_px16);
+  e->pattn16 = reinterpret_cast<uint16_t*>(sb + o_pattn);
+  e->pff16 = reinterpret_cast<uint16_t*>(sb + o_pff);
+
+  // ---- decode launch plan: one CTA per SM, weight slices sized for the
+  // largest CTA, two layer buffers + the persistent logits slice.
+  int G = sm_count();
+  auto ceil_rows = [&](int rows) { return (rows + G - 1) / G; };
+  DecodeArgs& a = e->plan;
+  a.mq = ceil_rows(3 * D);
+  a.mo = ceil_rows(D);
+  a.m1 = ceil_rows(F);
+  a.m2 = ceil_rows(D);
+  a.ml = ceil_rows(V);
+  a.layer_bytes = static_cast<uint32_t>(align_up(
+      ((size_t)a.mq * D + (size_t)a.mo * D + (size_t)a.m1 * D + (size_t)a.m2 * F) * 2, 128));
+  const size_t floats = (size_t)D * 2 + std::max(D, F) + kChunk + 64;
+  e->decode_smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 +
+                   2 * (size_t)kChunk * HD * 2 + floats * 4 + 8 * 4 + 4 * 8 + align_up(V, 16) + 64;
+  e->attn_smem = 2 * (size_t)kChunk * HD * 2 + ((size_t)kChunk + 64) * 4 +
+                 (size_t)kMaxChunks * (HD + 2) * 4;
+  e->HD = HD;
+  e->decode_fn = HD == 32 ? (const void*)t2s_decode_kernel<32> : (const void*)t2s_decode_kernel<64>;
+  e->attn_fn = HD == 32 ? (const void*)prefill_attn_kernel<32> : (const void*)prefill_attn_kernel<64>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int max_optin = 0;
+  cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e->decode_smem > (size_t)max_optin || e->attn_smem > (size_t)max_optin) {
+    gsvk_t2s_destroy(e);
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s kernels need %zu / %zu B shared memory",
+                e->decode_smem, e->attn_smem);
+  }
+  if (int rc = check_cuda(cudaFuncSetAttribute(e->decode_fn,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)e->decode_smem),
+                          "cudaFuncSetAttribute(t2s_decode)")) {
+    gsvk_t2s_destroy(e);
+    return rc;
+  }
+  if (int rc = check_cuda(cudaFuncSetAttribute(e->attn_fn,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)e->attn_smem),
+                          "cudaFuncSetAttribute(prefill_attn)")) {
+    gsvk_t2s_destroy(e);
+    return rc;
+  }
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->decode_fn, kThreads, e->decode_smem);
+  if (per_sm < 1) {
+    gsvk_t2s_destroy(e);
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s decode kernel does not fit an SM");
+  }
+  e->G = G;
+  *out = e;
+  return GSVK_OK;
+}
+
+int gsvk_t2s_destroy(gsvk_t2s_t h) {
+  if (!h) return GSVK_OK;
+  if (h->weights) cudaFree(h->weights);
+  if (h->scratch) cudaFree(h->scratch);
+  delete h;
+  return GSVK_OK;
+}
+
+int gsvk_t2s_load_kv(gsvk_t2s_t h, const uint16_t* k_host, const uint16_t* v_host, size_t prefix,
+                     size_t src_rows, gsvk_stream_t stream) {
+  if (!h || (prefix && (!k_host || !v_host))) return fail(GSVK_ERR_INVALID, "t2s_load_kv: null");
+  if (prefix > (size_t)h->cap || src_rows < prefix)
+    return fail(GSVK_ERR_INVALID, "t2s_load_kv: prefix %zu exceeds cache", prefix);
+  const size_t row = (size_t)h->D * 2;
+  for (int l = 0; l < h->L && prefix; ++l) {
+    int rc = check_cuda(cudaMemcpyAsync(h->dev.kc + (size_t)l * h->cap * h->D,
+                                        k_host + (size_t)l * src_rows * h->D, prefix * row,
+                                        cudaMemcpyHostToDevice, as_cuda(stream)),
+                        "t2s_load_kv k");
+    if (rc) return rc;
+    rc = check_cuda(cudaMemcpyAsync(h->dev.vc + (size_t)l * h->cap * h->D,
+                                    v_host + (size_t)l * src_rows * h->D, prefix * row,
+                                    cudaMemcpyHostToDevice, as_cuda(stream)),
+                    "t2s_load_kv v");
+    if (rc) return rc;
+  }
+  return GSVK_OK;
+}
+
+int gsvk_t2s_prefill(gsvk_t2s_t h, float* x, size_t S, size_t pos, size_t text_len,
+                     gsvk_stream_t stream) {
+  if (!h || !x || S == 0) return fail(GSVK_ERR_INVALID, "t2s_prefill: null or empty");
+  if (pos + S > (size_t)h->cap) return fail(GSVK_ERR_INVALID, "t2s_prefill: exceeds cache");
+  const T2SDev& d = h->dev;
+  const int D = h->D, F = h->F;
+  cudaStream_t st = as_cuda(stream);
+  int rc = gsvk_f32_to_f16(x, h->px16, S * D, stream);
+  if (rc) return rc;
+  for (int l = 0; l < h->L; ++l) {
+    // QKV: qkv = f16(x) . Wqkv^T + b
+    if ((rc = canon_gemm(h->px16, D, d.wqkv + (size_t)l * 3 * D * D, D, (int)S, 3 * D, D,
+                         d.bqkv + (size_t)l * 3 * D, 0, nullptr, 0, h->pqkv, 3 * D, nullptr, 0, st)))
+      return rc;
+    uint16_t* kl = d.kc + (size_t)l * h->cap * D;
+    uint16_t* vl = d.vc + (size_t)l * h->cap * D;
+    kv_append_kernel<<<(unsigned)S, 256, 0, st>>>(h->pqkv, (int)S, D, kl, vl, (int)pos);
+    if ((rc = check_launch("kv_append_kernel"))) return rc;
+    {
+      dim3 grid((unsigned)S, (unsigned)h->H);
+      int Di = D, posi = (int)pos, tl = (int)text_len;
+      float sc = d.scale;
+      const float* qkv = h->pqkv;
+      uint16_t* o16 = h->pattn16;
+      void* args[] = {&qkv, &kl, &vl, &Di, &posi, &tl, &sc, &o16};
+      if ((rc = check_cuda(cudaLaunchKernel(h->attn_fn, grid, dim3(128), args, h->attn_smem, st),
+                           "prefill_attn_kernel")))
+        return rc;
+    }
+    // out-proj + bias + residual(x) -> hpre ; x = LN1(hpre)
+    if ((rc = canon_gemm(h->pattn16, D, d.wout + (size_t)l * D * D, D, (int)S, D, D,
+                         d.bout + (size_t)l * D, 0, x, D, h->phpre, D, nullptr, 0, st)))
+      return rc;
+    ln_rows_canon_kernel<<<(unsigned)S, kThreads, 0, st>>>(h->phpre, d.n1g + (size_t)l * D,
+                                                         d.n1b + (size_t)l * D, x, h->px16, D, h->eps);
+    if ((rc = check_launch("ln_rows_canon_kernel"))) return rc;
+    // FFN: ff16 = relu(f16(x) . W1^T + b1) ; hpre = f16(ff) . W2^T + b2 + x ; x = LN2(hpre)
+    if ((rc = canon_gemm(h->px16, D, d.w1 + (size_t)l * F * D, D, (int)S, F, D,
+                         d.b1 + (size_t)l * F, 1, nullptr, 0, nullptr, 0, h->pff16, F, st)))
+      return rc;
+    if ((rc = canon_gemm(h->pff16, F, d.w2 + (size_t)l * D * F, F, (int)S, D, F,
+                         d.b2 + (size_t)l * D, 0, x, D, h->phpre, D, nullptr, 0, st)))
+      return rc;
+    ln_rows_canon_kernel<<<(unsigned)S, kThreads, 0, st>>>(h->phpre, d.n2g + (size_t)l * D,
+                                                         d.n2b + (size_t)l * D, x, h->px16, D, h->eps);
+    if ((rc = check_launch("ln_rows_canon_kernel"))) return rc;
+  }
+  return GSVK_OK;
+}
+
+int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
+                             size_t max_steps, int stop_on_eos, int32_t* tokens_dev,
+                             int* n_out_dev, float* margins_dev, gsvk_stream_t stream) {
+  if (!h || !prompt_dev || P == 0 || !tokens_dev || !n_out_dev)
+    return fail(GSVK_ERR_INVALID, "t2s_generate: null argument or empty prompt");
+  if (prefix + P + max_steps > (size_t)h->cap)
+    return fail(GSVK_ERR_INVALID, "t2s_generate: prefix+P+steps=%zu exceeds cap %d",
+                prefix + P + max_steps, h->cap);
+  const T2SDev& d = h->dev;
+  cudaStream_t st = as_cuda(stream);
+  const int D = h->D;
+  embed_kernel<<<(unsigned)P, 256, 0, st>>>(prompt_dev, (int)P, d.emb, d.pe, 0, h->alpha, D, h->px,
+                                           h->px16);
+  int rc = check_launch("embed_kernel");
+  if (rc) return rc;
+  if ((rc = gsvk_t2s_prefill(h, h->px, P, prefix, 0, stream))) return rc;
+  // first logits from the last prompt row (fp32 activations, t2s_engine.cpp:703-707)
+  canon_gemv_kernel<<<(unsigned)((h->V * 32 + 255) / 256), 256, 0, st>>>(
+      d.wpred, h->px + (P - 1) * D, d.logits, h->V, D);
+  if ((rc = check_launch("canon_gemv_kernel"))) return rc;
+  if ((rc = check_cuda(cudaMemsetAsync(d.bar, 0, 4, st), "reset grid barrier"))) return rc;
+  if ((rc = check_cuda(cudaMemsetAsync(n_out_dev, 0, 4, st), "reset n_out"))) return rc;
+  if (max_steps == 0) return GSVK_OK;
+  DecodeArgs a = h->plan;
+  a.pos0 = (int)(prefix + P);
+  a.pe0 = (int)P;
+  a.max_steps = (int)max_steps;
+  a.stop_on_eos = stop_on_eos;
+  a.hist = prompt_dev;
+  a.n_hist = (int)P;
+  a.tokens = tokens_dev;
+  a.n_out = n_out_dev;
+  a.margins = margins_dev;
+  T2SDev dv = d;
+  void* args[] = {&dv, &a};
+  return check_cuda(cudaLaunchCooperativeKernel(h->decode_fn, dim3(h->G), dim3(kThreads),
+                                                args, h->decode_smem, st),
+                    "t2s_decode_kernel (cooperative launch)");
+}
+
+int gsvk_t2s_generate(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_host, size_t P,
+                      size_t max_steps, int stop_on_eos, int32_t* tokens_host, float* margins_host,
+                      int* n_out, gsvk_stream_t stream) {
+  if (!h || !prompt_host || !tokens_host || !n_out) return fail(GSVK_ERR_INVALID, "t2s_generate: null");
+  if (P > (size_t)h->cap) return fail(GSVK_ERR_INVALID, "t2s_generate: prompt longer than cache");
+  cudaStream_t st = as_cuda(stream);
+  int rc = check_cuda(cudaMemcpyAsync(h->d_prompt, prompt_host, P * 4, cudaMemcpyHostToDevice, st),
+                      "prompt upload");
+  if (rc) return rc;
+  rc = gsvk_t2s_generate_device(h, prefix, h->d_prompt, P, max_steps, stop_on_eos, h->d_tokens,
+                                h->d_nout, margins_host ? h->d_margins : nullptr, stream);
+  if (rc) return rc;
+  int n = 0;
+  if ((rc = check_cuda(cudaMemcpyAsync(&n, h->d_nout, 4, cudaMemcpyDeviceToHost, st), "n_out")))
+    return rc;
+  if ((rc = check_cuda(cudaStreamSynchronize(st), "t2s_generate sync"))) return rc;
+  if (n < 0 || (size_t)n > max_steps) return fail(GSVK_ERR_CUDA, "t2s_generate: bad count %d", n);
+  *n_out = n;
+  if (n && (rc = check_cuda(cudaMemcpy(tokens_host, h->d_tokens, (size_t)n * 4,
+                                       cudaMemcpyDeviceToHost), "tokens download")))
+    return rc;
+  if (margins_host && max_steps &&
+      (rc = check_cuda(cudaMemcpy(margins_host, h->d_margins, max_steps * 4, cudaMemcpyDeviceToHost),
+                       "margins download")))
+    return rc;
+  return gsvk_device_status(1);
+}
+
+int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out) {
+  if (!h || !host_out) return fail(GSVK_ERR_INVALID, "t2s_read_logits: null");
+  return check_cuda(cudaMemcpy(host_out, h->dev.logits, (size_t)h->V * 4, cudaMemcpyDeviceToHost),
+                    "logits download");
+}
+
+}  // extern "C"

@@ -172,3 +172,16 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t M, uint32_t N) {
 }
 
 }  // namespace gsvk
+
+namespace gsvk {
+// 1D bulk copy global -> this CTA's shared memory (16-byte aligned, size a
+// multiple of 16), completion counted in bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+}  // namespace gsvk

@@ -122,6 +122,58 @@ int gsvk_softmax_rows(const float* x, float* y, size_t rows, size_t n,
 int gsvk_activation(const float* x, float* y, size_t n, int act, float slope,
                     gsvk_stream_t stream);
 
+/* ---- T2S autoregressive transformer (a16-a19) -------------------------- */
+/* Replaces ar::T2SEngine (t2s_engine.hpp:86-220): weights registered once
+ * (the analogue of the reference's load + amx_pack), KV cache and every
+ * workspace owned by the handle. */
+typedef struct gsvk_t2s* gsvk_t2s_t;
+typedef struct {
+  int n_layers, d_model, n_heads, ffn, vocab; /* 24, 512, 16, 2048, 1025 */
+  float ln_eps;                               /* 1e-5 */
+  float alpha_audio;                          /* ar_audio_position.alpha */
+  int cap;                                    /* KV slots (prefix + prompt + steps) */
+} gsvk_t2s_config;
+/* HOST pointers, layouts of the reference's .gsv tensors (t2s_engine.cpp:606-627):
+ * fp16 [L][3D][D] in_proj, [L][D][D] out_proj, [L][F][D] linear1,
+ * [L][D][F] linear2, [V][D] predict_layer and audio embedding; fp32 biases
+ * and LayerNorm affine parameters. */
+typedef struct {
+  const uint16_t* wqkv; const float* bqkv;
+  const uint16_t* wout; const float* bout;
+  const uint16_t* w1;   const float* b1;
+  const uint16_t* w2;   const float* b2;
+  const float* n1g; const float* n1b;
+  const float* n2g; const float* n2b;
+  const uint16_t* wpred;
+  const uint16_t* audio_emb;
+} gsvk_t2s_host_weights;
+int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, gsvk_t2s_t* out);
+int gsvk_t2s_destroy(gsvk_t2s_t h);
+/* Copies a KV prefix (HOST, fp16 [L][src_rows][D] for K and V) into slots
+ * [0, prefix) of every layer's cache. */
+int gsvk_t2s_load_kv(gsvk_t2s_t h, const uint16_t* k_host, const uint16_t* v_host, size_t prefix,
+                     size_t src_rows, gsvk_stream_t stream);
+/* block_prefill (t2s_engine.cpp:881-1034) over all layers, in place on the
+ * DEVICE rows x[S][D] (fp32), writing K/V into slots pos..pos+S-1.  Query q
+ * sees slots below pos, the first text_len block slots and block slots <= q. */
+int gsvk_t2s_prefill(gsvk_t2s_t h, float* x, size_t S, size_t pos, size_t text_len,
+                     gsvk_stream_t stream);
+/* generate (t2s_engine.cpp:1740-1900) over a cache whose slots [0, prefix)
+ * are loaded: prompt prefill at prefix.., greedy decode with repetition
+ * penalty 1.35 and the 11-step EOS mask.  stop_on_eos = 0 decodes through
+ * EOS (fixed-length runs).  HOST prompt and outputs; synchronous.  margins
+ * (optional, max_steps floats) receives top1 - top2 of each step's
+ * penalised logits. */
+int gsvk_t2s_generate(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_host, size_t P,
+                      size_t max_steps, int stop_on_eos, int32_t* tokens_host,
+                      float* margins_host, int* n_out, gsvk_stream_t stream);
+/* Same with DEVICE prompt / outputs, asynchronous on `stream`. */
+int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
+                             size_t max_steps, int stop_on_eos, int32_t* tokens_dev,
+                             int* n_out_dev, float* margins_dev, gsvk_stream_t stream);
+/* The logits the last step sampled from (raw, before the penalty); synchronous. */
+int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -83,7 +83,7 @@ def lib():
             "ora_t2s_decode_layer": (None, [vp, vp, c_int, vp, sz, vp, vp]),
             "ora_t2s_prefill_layer": (None, [vp, vp, c_int, vp, sz, sz, sz, vp, vp]),
             "ora_t2s_greedy_sample": (c_int, [vp, c_int, vp, sz, c_int, vp]),
-            "ora_t2s_generate": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp, vp]),
+            "ora_t2s_generate": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp, vp, vp]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(L, name)
@@ -301,16 +301,21 @@ def t2s_greedy_sample(logits: np.ndarray, history: np.ndarray, eos_allowed: bool
 
 
 def t2s_generate(model: dict, kcache: np.ndarray, vcache: np.ndarray, prefix: int,
-                 prompt: np.ndarray, max_steps: int, stop_on_eos: bool = True):
-    """kcache/vcache: [L, cap, D] uint16 (modified in place).  Returns (tokens, margins)."""
+                 prompt: np.ndarray, max_steps: int, stop_on_eos: bool = True,
+                 with_logits: bool = False):
+    """kcache/vcache: [L, cap, D] uint16 (modified in place).  Returns (tokens, margins)
+    or (tokens, margins, last_logits)."""
     d, w = t2s_structs(model)
     cap = kcache.shape[1]
     pr = np.ascontiguousarray(prompt, np.int32)
     toks = np.zeros(max_steps, dtype=np.int32)
     margins = np.zeros(max_steps, dtype=np.float32)
+    logits = np.zeros(model["vocab"], dtype=np.float32)
     n = lib().ora_t2s_generate(ctypes.byref(d), ctypes.byref(w), _p(kcache), _p(vcache), cap,
                                prefix, _p(pr), pr.size, max_steps, int(stop_on_eos), _p(toks),
-                               _p(margins))
+                               _p(margins), _p(logits))
     if n < 0:
         raise ValueError("ora_t2s_generate: cache too small")
+    if with_logits:
+        return toks[:n], margins, logits
     return toks[:n], margins

@@ -196,8 +196,62 @@ float row_dot_fmlal(const uint16_t* wr, const uint16_t* xh, size_t in) {
   }
   float s = vaddv4(a[0]);
   for (int j = 1; j < 8; ++j) s = s + vaddv4(a[j]);
-  for (; i < in; ++i) s = s + h2f(wr[i]) * h2f(xh[i]);  // exact product
+  for (; i < in; ++i) s = std::fmaf(h2f(wr[i]), h2f(xh[i]), s);  // exact product, one rounding
   return s;
+}
+
+// The same association with fp32 activations: the canonical order of every
+// T2S dot product (GEMV and prefill GEMM alike), so that the device kernels can
+// reproduce each sum bit for bit (32 accumulators = 32 lanes of a warp).
+float dot32(const uint16_t* wr, const float* x, size_t in) {
+  const size_t vec_end = in & ~size_t{63};
+  float a[8][4];
+  for (auto& v : a)
+    for (float& z : v) z = 0.f;
+  size_t i = 0;
+  for (; i < vec_end; i += 64)
+    for (int j = 0; j < 8; ++j) {
+      const size_t o = i + 8 * j;
+      for (int l = 0; l < 4; ++l) a[j][l] = std::fmaf(h2f(wr[o + l]), x[o + l], a[j][l]);
+      for (int l = 0; l < 4; ++l) a[j][l] = std::fmaf(h2f(wr[o + 4 + l]), x[o + 4 + l], a[j][l]);
+    }
+  float s = vaddv4(a[0]);
+  for (int j = 1; j < 8; ++j) s = s + vaddv4(a[j]);
+  for (; i < in; ++i) s = std::fmaf(h2f(wr[i]), x[i], s);
+  return s;
+}
+
+// y[r] = dot32(W[r], x) over row bands.
+void gemv32(const uint16_t* w, const float* x, float* y, size_t out, size_t in) {
+  row_bands(out, [&](size_t b, size_t e) {
+    for (size_t r = b; r < e; ++r) y[r] = dot32(w + r * in, x, in);
+  });
+}
+
+// Deterministic exp for the softmax: Cody-Waite reduction x = n ln2 + r with
+// the two-constant split of ln 2, then the degree-7 Taylor polynomial of e^r
+// (|r| <= ln2/2, truncation < 6e-9 relative) in Horner form, scaled by 2^n
+// through the exponent field.  Written with explicit fmaf so the CUDA build
+// produces the same bits; within 2 ulp of libm expf.
+float exp_det(float x) {
+  if (x < -87.0f) return 0.0f;
+  if (x > 88.0f) return INFINITY;
+  const float n = std::rint(x * 1.44269504088896341f);
+  float r = std::fmaf(n, -0.693359375f, x);
+  r = std::fmaf(n, 2.12194440e-4f, r);
+  float p = 1.98412698e-4f;
+  p = std::fmaf(p, r, 1.38888889e-3f);
+  p = std::fmaf(p, r, 8.33333333e-3f);
+  p = std::fmaf(p, r, 4.16666667e-2f);
+  p = std::fmaf(p, r, 1.66666667e-1f);
+  p = std::fmaf(p, r, 0.5f);
+  p = std::fmaf(p, r, 1.0f);
+  p = std::fmaf(p, r, 1.0f);
+  const int ni = static_cast<int>(n);
+  uint32_t bits = static_cast<uint32_t>(ni + 127) << 23;
+  float scale;
+  std::memcpy(&scale, &bits, 4);
+  return p * scale;
 }
 
 // -------------------------------------------- gemm_f16x_fmlal tile4 kernel
@@ -254,6 +308,66 @@ void accum_f16kv(float* ov, const uint16_t* v16, float p, size_t HD) {
     const float t = p * h2f(v16[e]);
     ov[e] = ov[e] + t;
   }
+}
+
+constexpr size_t kAttnChunk = 128;
+
+// Attention of one query row q (fp32, one head) over key/value slots
+// [0, n) of a token-major fp16 cache (t2s_engine.cpp:1062-1087): scores
+// dot_f16kv * scale, stable softmax, probability-weighted sum of V.  The
+// softmax is associated in fixed chunks of 128 slots from slot 0 (per chunk
+// max m_c, sum l_c of exp(s - m_c) and o_c = sum exp(s - m_c) v, each a
+// sequential sum in slot order; then chunk weights exp(m_c - M)), the order a
+// split-K device kernel reproduces exactly; it equals the reference's softmax
+// up to reassociation.  out receives HD values.
+void attend_canon(const float* q, const uint16_t* kc, const uint16_t* vc, size_t D, size_t n,
+                  size_t HD, float scale, float* out) {
+  const size_t nch = (n + kAttnChunk - 1) / kAttnChunk;
+  std::vector<float> mc(nch), lc(nch), oc(nch * HD, 0.f), sc(kAttnChunk);
+  for (size_t c = 0; c < nch; ++c) {
+    const size_t k0 = c * kAttnChunk, k1 = std::min(n, k0 + kAttnChunk);
+    float m = -INFINITY;
+    for (size_t k = k0; k < k1; ++k) {
+      sc[k - k0] = dot_f16kv(q, kc + k * D, HD) * scale;
+      m = m < sc[k - k0] ? sc[k - k0] : m;
+    }
+    float l = 0.f;
+    float* o = oc.data() + c * HD;
+    for (size_t k = k0; k < k1; ++k) {
+      const float e = exp_det(sc[k - k0] - m);
+      l = l + e;
+      accum_f16kv(o, vc + k * D, e, HD);
+    }
+    mc[c] = m;
+    lc[c] = l;
+  }
+  float M = -INFINITY;
+  for (size_t c = 0; c < nch; ++c) M = M < mc[c] ? mc[c] : M;
+  float L = 0.f;
+  for (size_t e = 0; e < HD; ++e) out[e] = 0.f;
+  for (size_t c = 0; c < nch; ++c) {
+    const float w = exp_det(mc[c] - M);
+    L = L + lc[c] * w;
+    for (size_t e = 0; e < HD; ++e) out[e] = out[e] + oc[c * HD + e] * w;
+  }
+  const float inv = 1.0f / L;
+  for (size_t e = 0; e < HD; ++e) out[e] = out[e] * inv;
+}
+
+// y[T,out] = act(dot32(W[o], f16(x[t])) + b) (prefill projections).
+void linear_canon(const float* x, size_t T, size_t in, const uint16_t* w, size_t out,
+                  const float* bias, bool relu, float* y) {
+  std::vector<float> xr(T * in);
+  for (size_t i = 0; i < T * in; ++i) xr[i] = round_f16(x[i]);
+  pool().run(T * out, 64, [&](size_t b, size_t e) {
+    for (size_t idx = b; idx < e; ++idx) {
+      const size_t t = idx / out, o = idx % out;
+      float v = dot32(w + o * in, xr.data() + t * in, in);
+      if (bias) v = v + bias[o];
+      if (relu) v = v > 0.f ? v : 0.f;
+      y[idx] = v;
+    }
+  });
 }
 
 }  // namespace
@@ -555,41 +669,37 @@ void ora_t2s_pe_row(int d_model, size_t pos, float* pe) {
   }
 }
 
+// T2S layers.  Every dot product uses the canonical dot32 association and
+// attention the chunked softmax of attend_canon; LayerNorm is kern.cpp:27-58.
 void ora_t2s_decode_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l, float* x,
                           size_t pos, uint16_t* kc, uint16_t* vc) {
   const size_t D = dm->d_model, H = dm->n_heads, HD = D / H, F = dm->ffn;
   const size_t len = pos + 1;
   const float scale = 1.0f / std::sqrt(static_cast<float>(HD));
-  std::vector<float> qkv(3 * D), attn(D, 0.f), xb(D), h(D), ff(F), sc(len);
-  std::vector<uint16_t> xh(std::max(D, F));
-  // QKV: FMLAL GEMV on fp16(x) + bias (t2s_engine.cpp:1044-1050)
-  ora_f32_to_f16(x, xh.data(), D);
-  ora_gemv_f16x_fmlal(w->wqkv + l * 3 * D * D, xh.data(), qkv.data(), 3 * D, D);
+  std::vector<float> qkv(3 * D), attn(D), xb(D), h(D), ff(F), xr(std::max(D, F));
+  // QKV on fp16(x) + bias (t2s_engine.cpp:1044-1050, GEMV16: gemv_fmlal.cpp:113)
+  for (size_t i = 0; i < D; ++i) xr[i] = round_f16(x[i]);
+  gemv32(w->wqkv + l * 3 * D * D, xr.data(), qkv.data(), 3 * D, D);
   for (size_t j = 0; j < 3 * D; ++j) qkv[j] = qkv[j] + w->bqkv[l * 3 * D + j];
   ora_f32_to_f16(qkv.data() + D, kc + pos * D, D);       // :1053-1055
   ora_f32_to_f16(qkv.data() + 2 * D, vc + pos * D, D);
-  for (size_t hh = 0; hh < H; ++hh) {  // :1062-1087
-    const float* qv = qkv.data() + hh * HD;
-    for (size_t k = 0; k < len; ++k) sc[k] = dot_f16kv(qv, kc + k * D + hh * HD, HD) * scale;
-    ora_softmax(sc.data(), sc.data(), len);
-    float* ov = attn.data() + hh * HD;
-    for (size_t k = 0; k < len; ++k) accum_f16kv(ov, vc + k * D + hh * HD, sc[k], HD);
+  for (size_t hh = 0; hh < H; ++hh)  // :1062-1087
+    attend_canon(qkv.data() + hh * HD, kc + hh * HD, vc + hh * HD, D, len, HD, scale,
+                 attn.data() + hh * HD);
+  // out proj on fp16(attn) + bias + residual, LN1 (:1089-1099)
+  for (size_t i = 0; i < D; ++i) xr[i] = round_f16(attn[i]);
+  gemv32(w->wout + l * D * D, xr.data(), xb.data(), D, D);
+  for (size_t i = 0; i < D; ++i) xb[i] = (xb[i] + w->bout[l * D + i]) + x[i];
+  ora_layernorm(xb.data(), w->n1g + l * D, w->n1b + l * D, h.data(), D, dm->ln_eps);
+  // FFN: W1 on fp16(h) + bias, ReLU; W2 on fp32 ff + bias + residual h; LN2
+  for (size_t i = 0; i < D; ++i) xr[i] = round_f16(h[i]);
+  gemv32(w->w1 + l * F * D, xr.data(), ff.data(), F, D);
+  for (size_t i = 0; i < F; ++i) {
+    const float v = ff[i] + w->b1[l * F + i];
+    ff[i] = v > 0.f ? v : 0.f;
   }
-  // out proj + bias + residual + LN1 (:1089-1099)
-  ora_f32_to_f16(attn.data(), xh.data(), D);
-  ora_gemv_f16x_fmlal(w->wout + l * D * D, xh.data(), xb.data(), D, D);
-  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + w->bout[l * D + i];
-  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + x[i];
-  ora_layernorm(xb.data(), w->n1g + l * D, w->n1b + l * D, xb.data(), D, dm->ln_eps);
-  h = xb;
-  // FFN: W1 FMLAL + bias + ReLU, W2 on fp32 activations + bias + residual, LN2
-  ora_f32_to_f16(xb.data(), xh.data(), D);
-  ora_gemv_f16x_fmlal(w->w1 + l * F * D, xh.data(), ff.data(), F, D);
-  for (size_t i = 0; i < F; ++i) ff[i] = ff[i] + w->b1[l * F + i];
-  ora_relu(ff.data(), ff.data(), F);
-  ora_gemv_f16w_f32acc(w->w2 + l * D * F, ff.data(), xb.data(), D, F);
-  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + w->b2[l * D + i];
-  for (size_t i = 0; i < D; ++i) xb[i] = xb[i] + h[i];
+  gemv32(w->w2 + l * D * F, ff.data(), xb.data(), D, F);
+  for (size_t i = 0; i < D; ++i) xb[i] = (xb[i] + w->b2[l * D + i]) + h[i];
   ora_layernorm(xb.data(), w->n2g + l * D, w->n2b + l * D, x, D, dm->ln_eps);
 }
 
@@ -597,36 +707,29 @@ void ora_t2s_prefill_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int
                            size_t S, size_t pos, size_t text_len, uint16_t* kc, uint16_t* vc) {
   const size_t D = dm->d_model, H = dm->n_heads, HD = D / H, F = dm->ffn;
   const float scale = 1.0f / std::sqrt(static_cast<float>(HD));
-  std::vector<float> qkv(S * 3 * D), attn(S * D, 0.f), tmp(S * D), ff(S * F);
-  ora_linear_f16(x, S, D, w->wqkv + l * 3 * D * D, 3 * D, w->bqkv + l * 3 * D, ORA_ACT_NONE, 0.f,
-                 qkv.data());
+  std::vector<float> qkv(S * 3 * D), attn(S * D), tmp(S * D), ff(S * F);
+  linear_canon(x, S, D, w->wqkv + l * 3 * D * D, 3 * D, w->bqkv + l * 3 * D, false, qkv.data());
   for (size_t t = 0; t < S; ++t) {
     ora_f32_to_f16(qkv.data() + t * 3 * D + D, kc + (pos + t) * D, D);
     ora_f32_to_f16(qkv.data() + t * 3 * D + 2 * D, vc + (pos + t) * D, D);
   }
+  // Query q sees slots [0, pos) and block slots [0, max(text_len, q+1)):
+  // the text-prefix / causal mask of t2s_engine.cpp:944-979 as one range.
   pool().run(S * H, 1, [&](size_t wb, size_t we) {
-    std::vector<float> sc(pos + S), pr(pos + S);
-    std::vector<size_t> keys(pos + S);
     for (size_t item = wb; item < we; ++item) {
       const size_t hh = item / S, q = item % S;
-      size_t n = 0;
-      for (size_t k = 0; k < pos; ++k) keys[n++] = k;
-      for (size_t k = 0; k < S; ++k)
-        if (k < text_len || k <= q) keys[n++] = pos + k;  // t2s_engine.cpp:947-949
-      const float* qv = qkv.data() + q * 3 * D + hh * HD;
-      for (size_t i = 0; i < n; ++i) sc[i] = dot_f16kv(qv, kc + keys[i] * D + hh * HD, HD) * scale;
-      ora_softmax(sc.data(), pr.data(), n);
-      float* ov = attn.data() + q * D + hh * HD;
-      for (size_t i = 0; i < n; ++i) accum_f16kv(ov, vc + keys[i] * D + hh * HD, pr[i], HD);
+      const size_t n = pos + std::max(text_len, q + 1);
+      attend_canon(qkv.data() + q * 3 * D + hh * HD, kc + hh * HD, vc + hh * HD, D, n, HD, scale,
+                   attn.data() + q * D + hh * HD);
     }
   });
-  ora_linear_f16(attn.data(), S, D, w->wout + l * D * D, D, nullptr, ORA_ACT_NONE, 0.f, tmp.data());
-  for (size_t i = 0; i < S * D; ++i) x[i] = x[i] + (tmp[i] + w->bout[l * D + i % D]);
+  linear_canon(attn.data(), S, D, w->wout + l * D * D, D, nullptr, false, tmp.data());
+  for (size_t i = 0; i < S * D; ++i) x[i] = (tmp[i] + w->bout[l * D + i % D]) + x[i];
   for (size_t t = 0; t < S; ++t)
     ora_layernorm(x + t * D, w->n1g + l * D, w->n1b + l * D, x + t * D, D, dm->ln_eps);
-  ora_linear_f16(x, S, D, w->w1 + l * F * D, F, w->b1 + l * F, ORA_ACT_RELU, 0.f, ff.data());
-  ora_linear_f16(ff.data(), S, F, w->w2 + l * D * F, D, nullptr, ORA_ACT_NONE, 0.f, tmp.data());
-  for (size_t i = 0; i < S * D; ++i) x[i] = x[i] + (tmp[i] + w->b2[l * D + i % D]);
+  linear_canon(x, S, D, w->w1 + l * F * D, F, w->b1 + l * F, true, ff.data());
+  linear_canon(ff.data(), S, F, w->w2 + l * D * F, D, nullptr, false, tmp.data());
+  for (size_t i = 0; i < S * D; ++i) x[i] = (tmp[i] + w->b2[l * D + i % D]) + x[i];
   for (size_t t = 0; t < S; ++t)
     ora_layernorm(x + t * D, w->n2g + l * D, w->n2b + l * D, x + t * D, D, dm->ln_eps);
 }
@@ -665,7 +768,7 @@ int ora_t2s_greedy_sample(float* lg, int V, const int32_t* hist, size_t n_hist,
 int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
                      uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt, size_t P,
                      size_t max_steps, int stop_on_eos, int32_t* tokens_out,
-                     float* margins_out) {
+                     float* margins_out, float* last_logits) {
   const size_t D = dm->d_model, L = dm->n_layers, V = dm->vocab;
   const int eos = static_cast<int>(V) - 1;
   if (P == 0 || prefix + P + max_steps > cap) return -1;
@@ -678,12 +781,13 @@ int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t*
   for (size_t l = 0; l < L; ++l)
     ora_t2s_prefill_layer(dm, w, static_cast<int>(l), xy.data(), P, prefix, 0, kc + l * cap * D,
                           vc + l * cap * D);
-  ora_gemv_f16w_f32acc(w->wpred, xy.data() + (P - 1) * D, logits.data(), V, D);
+  gemv32(w->wpred, xy.data() + (P - 1) * D, logits.data(), V, D);  // fp32 activations
   std::vector<int32_t> hist(prompt, prompt + P);
   size_t cur = prefix + P;
   int n_out = 0;
   for (size_t idx = 0; idx < max_steps; ++idx) {
     const bool eos_allowed = idx >= 11;  // kEosMaskSteps
+    if (last_logits) std::memcpy(last_logits, logits.data(), V * sizeof(float));
     int raw = -1;
     const int s = ora_t2s_greedy_sample(logits.data(), static_cast<int>(V), hist.data(),
                                         hist.size(), eos_allowed, &raw);
@@ -709,7 +813,7 @@ int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t*
     for (size_t l = 0; l < L; ++l)
       ora_t2s_decode_layer(dm, w, static_cast<int>(l), x1.data(), cur, kc + l * cap * D,
                            vc + l * cap * D);
-    ora_gemv_f16w_f32acc(w->wpred, x1.data(), logits.data(), V, D);
+    gemv32(w->wpred, x1.data(), logits.data(), V, D);
     ++cur;
   }
   return n_out;

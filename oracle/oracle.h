@@ -140,7 +140,21 @@ typedef struct {
 /* t2s_engine.cpp:711-720  sinusoidal position row, fp32 expressions. */
 void ora_t2s_pe_row(int d_model, size_t pos, float* pe);
 
-/* t2s_engine.cpp:1036-1119 with KV16 && GEMV16 (the `--fp16-all` mode):
+/* T2S numerics.  The reference leaves the association of its sums to NEON
+ * register blocking and Accelerate; this oracle fixes ONE canonical order that
+ * the device kernels reproduce bit for bit:
+ *   - every dot product: the gemv_fmlal.cpp:40-109 order (8 x 4 accumulators
+ *     over 64-element steps, low then high half, vaddv per group, groups summed
+ *     in order), for fp16 and fp32 activations alike;
+ *   - LayerNorm: kern.cpp:27-58 (8-lane fp32 sums, fp64 combine);
+ *   - attention scores: dot_f16kv (t2s_engine.cpp:69-99);
+ *   - softmax: chunks of 128 slots (sequential sums inside a chunk, chunk
+ *     weights exp(m_c - M)) with a deterministic Cody-Waite/Taylor exp within
+ *     2 ulp of expf.
+ * Rounding points are the reference's: fp16(x) before QKV, out-proj and W1
+ * (GEMV16), fp16 K/V storage (KV16), fp32 activations into W2 and the logits.
+ *
+ * t2s_engine.cpp:1036-1119 with KV16 && GEMV16 (the `--fp16-all` mode):
  * one post-LN decode layer over x[D] in place; appends k/v at slot pos into
  * kcache/vcache (token-major [cap][D] fp16) and attends over [0, pos]. */
 void ora_t2s_decode_layer(const ora_t2s_dims* d, const ora_t2s_weights* w,
@@ -151,7 +165,8 @@ void ora_t2s_decode_layer(const ora_t2s_dims* d, const ora_t2s_weights* w,
  * pos..pos+S-1.  Query q sees every slot below pos, the first text_len
  * slots of the block, and block slots <= q (pos == 0 reproduces the
  * reference's text-prefix mask exactly).  All four projections take
- * fp16-rounded activations (the accelerated-panel semantics). */
+ * fp16-rounded activations (the DenseF16 view / accelerated-panel semantics,
+ * accel.hpp:70-78). */
 void ora_t2s_prefill_layer(const ora_t2s_dims* d, const ora_t2s_weights* w,
                            int layer, float* x, size_t S, size_t pos,
                            size_t text_len, uint16_t* kcache,
@@ -168,12 +183,13 @@ int ora_t2s_greedy_sample(float* logits, int vocab, const int32_t* history,
  * cap >= prefix + P + max_steps.  stop_on_eos = 0 keeps decoding through
  * EOS (fixed-length benchmark runs).  Returns the number of sampled tokens
  * written to tokens_out; margins_out (optional) receives per-step
- * top1 - top2 of the penalised logits. */
+ * top1 - top2 of the penalised logits; last_logits (optional, vocab floats)
+ * the raw logits the final step sampled from. */
 int ora_t2s_generate(const ora_t2s_dims* d, const ora_t2s_weights* w,
                      uint16_t* kcache, uint16_t* vcache, size_t cap,
                      size_t prefix, const int32_t* prompt, size_t P,
                      size_t max_steps, int stop_on_eos, int32_t* tokens_out,
-                     float* margins_out);
+                     float* margins_out, float* last_logits);
 
 #ifdef __cplusplus
 }
