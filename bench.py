@@ -1,0 +1,398 @@
+#!/usr/bin/env python3
+"""Benchmark driver: one JSON line on rank 0.
+
+Default workload (the metric's T2S decode): batch-1
+greedy decode of the 24-layer d=512 T2S transformer, KV prefix of 256 slots,
+64-token prompt, 500 tokens per utterance.  A "step" is one utterance: prompt
+prefill + 500 greedy steps.  Multi-GPU runs are replicas (one utterance per
+GPU per step, no collective on the data path): value = tokens of all ranks /
+max-over-ranks time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gsvk|reference]
+                  [--workload t2s_decode_b1|gemm_ffn_up]
+
+--impl reference times the reference's CPU arithmetic for the same workload on
+the host cores (the oracle restatement; the reference itself targets Apple
+NEON/Accelerate and does not build on x86).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+T2S_STEPS = 500
+T2S_PREFIX = 256
+T2S_PROMPT = 64
+L2_BYTES = 126 * 1024 * 1024
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((int(parts[0]), float(parts[1]), float(parts[2]), parts[4:]))
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        max_mhz = max(r[2] for r in rows)
+        loaded = [r for r in rows if r[1] >= 0.5 * r[2]] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3][1:5])
+                          if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[1] for r in loaded), "sm_max_mhz": max_mhz,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------- distributed
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return rank, local, world
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world <= 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(v)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def dist_close(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------- CPU baseline (oracle)
+def t2s_cpu_sample(n_decode=12, threads=None):
+    """Time the oracle restatement of the T2S generate on the host cores:
+    the 64-token prompt prefill, then n_decode decode steps; extrapolate to the
+    500-token utterance.  Returns (tokens_per_s, ms_per_utterance, threads, sample)."""
+    import oracle
+
+    g = __import__("__graft_entry__").package()
+    threads = threads or (os.cpu_count() or 1)
+    oracle.build()
+    oracle.set_threads(threads)
+    m, k0, v0, prompt = g.workloads.t2s_decode_b1(steps=n_decode + 1)
+    t0 = time.perf_counter()
+    oracle.t2s_generate(m, k0.copy(), v0.copy(), T2S_PREFIX, prompt, 1, False)
+    t_pf = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    oracle.t2s_generate(m, k0.copy(), v0.copy(), T2S_PREFIX, prompt, n_decode + 1, False)
+    t_all = time.perf_counter() - t0
+    per_tok = max(1e-9, (t_all - t_pf) / n_decode)
+    full = t_pf + (T2S_STEPS - 1) * per_tok
+    sample = (f"oracle T2S generate, 24 layers: 64-token prompt prefill ({t_pf*1e3:.0f} ms) + "
+              f"{n_decode} decode steps ({per_tok*1e3:.1f} ms/token), extrapolated to the "
+              f"500-token utterance; {threads} threads")
+    return T2S_STEPS / full, full * 1e3, threads, sample
+
+
+# ------------------------------------------------------------ T2S workload
+def t2s_algorithmic_bytes(model, steps):
+    """HBM bytes the decode kernel must move: per decode pass all weights
+    (24 x 6,291,456 + logits 1,049,600 B) + K/V reads over len slots
+    (49,152 B per slot) + K/V writes (49,152 B)."""
+    L, D, F, V = model["n_layers"], model["d_model"], model["ffn"], model["vocab"]
+    w = L * (3 * D * D + D * D + 2 * F * D) * 2 + V * D * 2
+    kv_slot = L * 2 * D * 2
+    total = 0
+    for i in range(steps - 1):  # the last step only samples
+        length = T2S_PREFIX + T2S_PROMPT + i + 1
+        total += w + kv_slot * length + kv_slot
+    return total
+
+
+def run_t2s(args, rank, local, world):
+    import numpy as np
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    m, k0, v0, _ = g.workloads.t2s_decode_b1()
+    prompt = g.workloads.t2s_prompt(T2S_PROMPT, m["vocab"], seed=rank)  # one utterance per rank
+    cap = T2S_PREFIX + T2S_PROMPT + T2S_STEPS
+    eng = g.T2S(m, cap)
+    k_pin = torch.from_numpy(k0[:, :T2S_PREFIX].copy()).pin_memory()
+    v_pin = torch.from_numpy(v0[:, :T2S_PREFIX].copy()).pin_memory()
+    eng.load_kv(k_pin.numpy(), v_pin.numpy(), T2S_PREFIX)
+    prompt_dev = torch.from_numpy(prompt).to(dev)
+    toks = torch.zeros(T2S_STEPS, dtype=torch.int32, device=dev)
+    nout = torch.zeros(1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        eng.prompt(T2S_PREFIX, prompt_dev)
+        eng.decode(T2S_PREFIX, prompt_dev, T2S_STEPS, toks, nout, stop_on_eos=False)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    assert g.device_status() == 0
+
+    # ---- device-resident timing (value) + per-launch decode kernel events
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    start.record(stream)
+    for i in range(args.steps):
+        eng.prompt(T2S_PREFIX, prompt_dev)
+        ev[i][0].record(stream)
+        eng.decode(T2S_PREFIX, prompt_dev, T2S_STEPS, toks, nout, stop_on_eos=False)
+        ev[i][1].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    barrier(world)
+    t_total = start.elapsed_time(end) * 1e-3
+    t_dec = statistics.mean(a.elapsed_time(b) for a, b in ev) * 1e-3
+    assert int(nout.item()) == T2S_STEPS and g.device_status() == 0
+    t_max = max_over_ranks(t_total, world)
+    t_dec_max = max_over_ranks(t_dec, world)
+
+    # ---- end to end through the C-ABI with host buffers (e2e)
+    h2d = k_pin.numel() * 2 * 2 + prompt.nbytes
+    d2h = T2S_STEPS * 4 + 4
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.load_kv(k_pin.numpy(), v_pin.numpy(), T2S_PREFIX)
+        out, _ = eng.generate(T2S_PREFIX, prompt, T2S_STEPS, stop_on_eos=False)
+        assert len(out) == T2S_STEPS
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    launches = eng.launches_per_generate() * args.steps
+    eng.close()
+
+    tokens = T2S_STEPS * args.steps * world
+    hbm, _, peak_kind = measured_peaks()
+    alg = t2s_algorithmic_bytes(m, T2S_STEPS)
+    achieved = alg / t_dec_max / 1e9
+    line = {
+        "metric": "T2S decode tokens/s (batch 1 per GPU, 500 greedy tokens per utterance)",
+        "value": tokens / t_max,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": t_max / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 weights/KV, f32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV prefix, uniform prompt ids)",
+        "config": {"workload": "t2s_decode_b1 (BASELINE configs[1])",
+                   "model": "T2S 24L d512 16h ffn2048 vocab1025 post-LN",
+                   "global_batch": world, "seq_len": T2S_STEPS, "kv_prefix": T2S_PREFIX,
+                   "prompt": T2S_PROMPT, "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2: 152 MB of weights streamed per token"},
+        "e2e": {"value": tokens / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "t2s_decode_kernel", "achieved": achieved,
+                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg,
+                     "launch_ms": t_dec_max * 1e3},
+    }
+    if clk:
+        line["clocks"] = clk
+    return line
+
+
+# ------------------------------------------------------------ GEMM config 1
+def run_gemm1(args, rank, local, world):
+    import numpy as np
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    x, w, b = g.workloads.gemm_ffn_up(seed=rank)
+    # rotate enough independent copies that the working set exceeds L2
+    copies = 64
+    xs = [torch.from_numpy(x.view(np.float16)).to(dev) for _ in range(copies)]
+    ws = [torch.from_numpy(w.view(np.float16)).to(dev) for _ in range(copies)]
+    bd = torch.from_numpy(b).to(dev)
+    ys = [torch.empty(128, 2048, dtype=torch.float16, device=dev) for _ in range(copies)]
+    iters = 200
+    for i in range(args.warmup * 10):
+        g.gemm_ex(xs[i % copies], ws[i % copies], bias=bd, act=g.ACT_RELU, c_f16=ys[i % copies])
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler()
+    barrier(world)
+    clocks.start()
+    start.record(stream)
+    for s in range(args.steps):
+        for i in range(iters):
+            j = (s * iters + i) % copies
+            g.gemm_ex(xs[j], ws[j], bias=bd, act=g.ACT_RELU, c_f16=ys[j])
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    t = max_over_ranks(start.elapsed_time(end) * 1e-3, world)
+    flops = 2 * 128 * 2048 * 512 * iters * args.steps * world
+    _, tf, kind = measured_peaks()
+    achieved = flops / world / t / 1e12
+    line = {"metric": "GEMM TFLOP/s (Y = ReLU(X W^T + b), 128x2048x512, fp16 out)",
+            "value": flops / t / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, f32 accumulate, f16 out",
+            "data": "synthetic", "config": {"workload": "gemm_ffn_up (BASELINE configs[0])",
+                                            "iters_per_step": iters,
+                                            "l2": f"{copies} rotated X/W copies"},
+            "gpu_launches": iters * args.steps,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf, "unit": "TFLOP/s",
+                         "frac": achieved / tf, "peak_source": kind, "traffic": None}}
+    if clk:
+        line["clocks"] = clk
+    return line
+
+
+WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1}
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU arithmetic (oracle restatement) on the host cores."""
+    if rank != 0:
+        return None
+    if args.workload != "t2s_decode_b1":
+        return {"impl": "reference", "unavailable": "reference arm implemented for t2s_decode_b1"}
+    vals, mss = [], []
+    for _ in range(args.warmup):
+        t2s_cpu_sample(n_decode=4)
+    for _ in range(args.steps):
+        v, ms, threads, sample = t2s_cpu_sample(n_decode=8)
+        vals.append(v)
+        mss.append(ms)
+    v = statistics.mean(vals)
+    return {"metric": "T2S decode tokens/s (batch 1 per GPU, 500 greedy tokens per utterance)",
+            "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(mss),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 weights/KV, f32 accumulate", "data": "synthetic",
+            "config": {"workload": "t2s_decode_b1 (BASELINE configs[1])"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="gsvk", choices=["gsvk", "reference"])
+    ap.add_argument("--workload", default="t2s_decode_b1", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    rank, local, world = dist_setup(args.gpus)
+    try:
+        line = WORKLOADS[args.workload](args, rank, local, world)
+    finally:
+        pass
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "t2s_decode_b1":
+        v, ms, threads, sample = t2s_cpu_sample()
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": sample}
+    dist_close(world)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

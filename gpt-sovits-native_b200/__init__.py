@@ -55,6 +55,11 @@ SIGNATURES = {
     "gsvk_t2s_generate": (c_int, [_vp, _sz, _vp, _sz, _sz, c_int, _vp, _vp, _vp, _vp]),
     "gsvk_t2s_generate_device": (c_int, [_vp, _sz, _vp, _sz, _sz, c_int, _vp, _vp, _vp, _vp]),
     "gsvk_t2s_read_logits": (c_int, [_vp, _vp]),
+    "gsvk_t2s_prompt": (c_int, [_vp, _sz, _vp, _sz, _vp]),
+    "gsvk_t2s_decode": (c_int, [_vp, _sz, _vp, _sz, _sz, c_int, _vp, _vp, _vp, _vp]),
+    "gsvk_t2s_launches_per_generate": (c_int, [_vp]),
+    "gsvk_t2s_set_trace": (c_int, [_vp, c_int]),
+    "gsvk_t2s_read_trace": (c_int, [_vp, _vp, _sz]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -294,6 +299,32 @@ class T2S:
         check(lib().gsvk_t2s_generate_device(self.h, prefix, _ptr(prompt_dev), prompt_dev.numel(),
                                              max_steps, int(stop_on_eos), _ptr(tokens_dev),
                                              _ptr(n_out_dev), _ptr(margins_dev), _stream(stream)))
+
+    def prompt(self, prefix: int, prompt_dev, stream=None):
+        check(lib().gsvk_t2s_prompt(self.h, prefix, _ptr(prompt_dev), prompt_dev.numel(),
+                                    _stream(stream)))
+
+    def decode(self, prefix: int, prompt_dev, max_steps: int, tokens_dev, n_out_dev,
+               stop_on_eos: bool = True, margins_dev=None, stream=None):
+        check(lib().gsvk_t2s_decode(self.h, prefix, _ptr(prompt_dev), prompt_dev.numel(),
+                                    max_steps, int(stop_on_eos), _ptr(tokens_dev), _ptr(n_out_dev),
+                                    _ptr(margins_dev), _stream(stream)))
+
+    TRACE_STEPS, TRACE_STRIDE = 4, 16 + 16 * 64
+
+    def set_trace(self, on: bool = True):
+        check(lib().gsvk_t2s_set_trace(self.h, int(on)))
+
+    def read_trace(self):
+        """[4, 1040] device-clock ns per phase boundary (see gsvk.h)."""
+        import numpy as np
+
+        out = np.zeros(self.TRACE_STEPS * self.TRACE_STRIDE, np.uint64)
+        check(lib().gsvk_t2s_read_trace(self.h, out.ctypes.data, out.size))
+        return out.reshape(self.TRACE_STEPS, self.TRACE_STRIDE)
+
+    def launches_per_generate(self) -> int:
+        return lib().gsvk_t2s_launches_per_generate(self.h)
 
     def read_logits(self):
         import numpy as np

@@ -46,6 +46,7 @@ __device__ __forceinline__ float warp_dot32(const uint16_t* w, const float* x, i
   const int o0 = 8 * (lane >> 2) + (lane & 3);
   const int vec_end = n & ~63;
   float acc = 0.f;
+#pragma unroll 4
   for (int i = 0; i < vec_end; i += 64) {
     acc = fmaf(h2f(w[i + o0]), x[i + o0], acc);
     acc = fmaf(h2f(w[i + o0 + 4]), x[i + o0 + 4], acc);
@@ -75,18 +76,28 @@ __device__ __forceinline__ float group16_dot_kv(const float* q_reg, const uint16
 }
 
 // LayerNorm of n values held in shared memory `buf`, in place, whole block.
-// scratch: >= 18 floats of shared memory.
+// scratch: >= 18 floats of shared memory.  Threads 0-7 run the 8 sum chains,
+// 8-15 the 8 sum-of-squares chains (each in element order, loads hoisted 8
+// at a time); thread 0 then forms mean / variance / rstd in fp64.
 __device__ __forceinline__ void ln_canon(float* buf, const float* g, const float* b, int n,
                                          double eps, float* scratch) {
   const int tid = threadIdx.x;
   const int vec_end = n & ~7;
   if (tid < 16) {
     const int l = tid & 7;
+    const bool sq = tid >= 8;
     float a = 0.f;
-    if (tid < 8) {
-      for (int i = l; i < vec_end; i += 8) a = __fadd_rn(a, buf[i]);
-    } else {
-      for (int i = l; i < vec_end; i += 8) a = fmaf(buf[i], buf[i], a);
+    int i = l;
+    for (; i + 56 < vec_end; i += 64) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = buf[i + 8 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a = sq ? fmaf(v[u], v[u], a) : __fadd_rn(a, v[u]);
+    }
+    for (; i < vec_end; i += 8) {
+      const float v = buf[i];
+      a = sq ? fmaf(v, v, a) : __fadd_rn(a, v);
     }
     scratch[tid] = a;
   }
@@ -104,16 +115,20 @@ __device__ __forceinline__ void ln_canon(float* buf, const float* g, const float
       sq = __dadd_rn(sq, __dmul_rn(xv, xv));
     }
     const double dn = static_cast<double>(n);
-    const float mean = static_cast<float>(__ddiv_rn(sum, dn));
+    // x / 2^k == x * 2^-k exactly: skip the fp64 divide for power-of-two n
+    const bool pow2 = (n & (n - 1)) == 0;
+    const double inv_n = pow2 ? 1.0 / dn : 0.0;
+    const float mean = static_cast<float>(pow2 ? __dmul_rn(sum, inv_n) : __ddiv_rn(sum, dn));
     const double md = static_cast<double>(mean);
-    float var = static_cast<float>(__dsub_rn(__ddiv_rn(sq, dn), __dmul_rn(md, md)));
+    const double ex2 = pow2 ? __dmul_rn(sq, inv_n) : __ddiv_rn(sq, dn);
+    float var = static_cast<float>(__dsub_rn(ex2, __dmul_rn(md, md)));
     if (!(var >= 0.0f)) {
       double s2 = 0.0;
       for (int i = 0; i < n; ++i) {
         const double d = __dsub_rn(static_cast<double>(buf[i]), md);
         s2 = __dadd_rn(s2, __dmul_rn(d, d));
       }
-      var = static_cast<float>(__ddiv_rn(s2, dn));
+      var = static_cast<float>(pow2 ? __dmul_rn(s2, inv_n) : __ddiv_rn(s2, dn));
     }
     const float rstd = static_cast<float>(
         __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(static_cast<double>(var), eps))));
@@ -125,6 +140,64 @@ __device__ __forceinline__ void ln_canon(float* buf, const float* g, const float
   for (int i = tid; i < n; i += blockDim.x)
     buf[i] = fmaf(__fmul_rn(__fsub_rn(buf[i], mean), rstd), g[i], b[i]);
   __syncthreads();
+}
+
+// Two canonical dots sharing x (independent chains interleaved for ILP).
+__device__ __forceinline__ void warp_dot32x2(const uint16_t* w0, const uint16_t* w1,
+                                             const float* x, int n, float* r0, float* r1) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+  const int vec_end = n & ~63;
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < vec_end; i += 64) {
+    const float xl = x[i + o0], xh = x[i + o0 + 4];
+    a0 = fmaf(h2f(w0[i + o0]), xl, a0);
+    a1 = fmaf(h2f(w1[i + o0]), xl, a1);
+    a0 = fmaf(h2f(w0[i + o0 + 4]), xh, a0);
+    a1 = fmaf(h2f(w1[i + o0 + 4]), xh, a1);
+  }
+  float t0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
+  float t1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+  t0 = __fadd_rn(t0, __shfl_xor_sync(0xffffffffu, t0, 2));
+  t1 = __fadd_rn(t1, __shfl_xor_sync(0xffffffffu, t1, 2));
+  float s0 = __shfl_sync(0xffffffffu, t0, 0), s1 = __shfl_sync(0xffffffffu, t1, 0);
+#pragma unroll
+  for (int j = 1; j < 8; ++j) {
+    s0 = __fadd_rn(s0, __shfl_sync(0xffffffffu, t0, 4 * j));
+    s1 = __fadd_rn(s1, __shfl_sync(0xffffffffu, t1, 4 * j));
+  }
+  for (int i = vec_end; i < n; ++i) {
+    s0 = fmaf(h2f(w0[i]), x[i], s0);
+    s1 = fmaf(h2f(w1[i]), x[i], s1);
+  }
+  *r0 = s0;
+  *r1 = s1;
+}
+
+// Canonical q . k (dot_f16kv order) by ONE thread: 4 x 4 accumulators over
+// 16-element steps, (a0+a1)+(a2+a3) per lane, then (s0+s2)+(s1+s3).
+template <int HD>
+__device__ __forceinline__ float thread_dot_kv(const float* q, const uint4* krow) {
+  float a[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int l = 0; l < 4; ++l) a[j][l] = 0.f;
+#pragma unroll
+  for (int e = 0; e < HD; e += 16) {
+    float kf[16];
+    unpack8(krow[e / 8], kf);
+    unpack8(krow[e / 8 + 1], kf + 8);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int l = 0; l < 4; ++l) a[j][l] = fmaf(q[e + 4 * j + l], kf[4 * j + l], a[j][l]);
+  }
+  float s[4];
+#pragma unroll
+  for (int l = 0; l < 4; ++l) s[l] = __fadd_rn(__fadd_rn(a[0][l], a[1][l]), __fadd_rn(a[2][l], a[3][l]));
+  return __fadd_rn(__fadd_rn(s[0], s[2]), __fadd_rn(s[1], s[3]));
 }
 
 }  // namespace gsvk

@@ -37,8 +37,9 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kChunk = 128;      // softmax chunk (slots), fixed by the canonical order
-constexpr int kMaxChunks = 128;  // chunks per head (cap <= 16384 slots)
+constexpr int kChunk = 64;       // softmax chunk (slots), fixed by the canonical order
+constexpr int kMaxChunks = 256;  // chunks per head (cap <= 16384 slots)
+constexpr int kSlots = kThreads / 64;  // concurrent attention chunks per CTA
 constexpr uint32_t kGridSpin = 1u << 23;
 
 struct T2SDev {
@@ -65,21 +66,24 @@ struct DecodeArgs {
   // shared-memory plan (identical in every CTA)
   int mq, mo, m1, m2, ml;  // max rows per CTA of qkv / out / w1 / w2 / logits
   uint32_t layer_bytes;
+  int stage_floats;  // shared floats for chunk records (P3); 0 = read them from global
+  // optional phase trace: CTA 0 writes %globaltimer (ns) at every phase
+  // boundary of the first kTraceSteps steps, kTraceStride slots per step
+  unsigned long long* trace;
 };
+
+constexpr int kTraceSteps = 4;
+constexpr int kTraceStride = 16 + 16 * 64;
 
 __host__ __device__ inline int row_lo(int rows, int g, int c) {
   return static_cast<int>(static_cast<long long>(rows) * c / g);
 }
 
 // ----------------------------------------------------------- block helpers
-__device__ __forceinline__ float blk_max(float v, float* red) {
-  v = warp_max(v);
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();
-  if (lane == 0) red[w] = v;
-  __syncthreads();
-  float t = lane < nw ? red[lane] : -INFINITY;
-  return warp_max(t);
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
 }
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -119,79 +123,141 @@ __device__ bool grid_sync(unsigned* bar, unsigned& epoch, uint32_t* status, int*
   return *flag != 0;
 }
 
-// One attention chunk of the canonical softmax for head h: slots [k0, k1) of
-// a token-major fp16 cache (row stride D).  Stages the chunk's K and V rows
-// in shared memory, computes the scores with group16_dot_kv, the chunk max,
-// exp_det weights, and the two sequential sums (l by thread 0, o by warp 1,
-// one lane per dimension).  Writes {m, l, o[HD]} to dst.  Whole block.
-template <int HD>
-__device__ void attn_chunk(const float* qv, const uint16_t* kcache, const uint16_t* vcache, int D,
-                           int k0, int k1, float scale, uint16_t* kst, uint16_t* vst, float* sc,
-                           float* red, float* dst) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nk = k1 - k0;
-  constexpr int kV = HD / 8;  // uint4 per row slice
-  for (int i = tid; i < nk * kV; i += blockDim.x) {
-    const int key = i / kV, part = i - (i / kV) * kV;
-    const size_t off = static_cast<size_t>(k0 + key) * D;
-    reinterpret_cast<uint4*>(kst)[i] = __ldcg(reinterpret_cast<const uint4*>(kcache + off) + part);
-    reinterpret_cast<uint4*>(vst)[i] = __ldcg(reinterpret_cast<const uint4*>(vcache + off) + part);
-  }
-  float q_reg[HD / 16];
-#pragma unroll
-  for (int c = 0; c < HD / 16; ++c) q_reg[c] = __ldcg(qv + 16 * c + (lane & 15));
-  __syncthreads();
-  const int groups = blockDim.x >> 4, g = tid >> 4;
-  for (int base = 0; base < nk; base += groups) {
-    const int key = base + g;
-    const int kk = key < nk ? key : nk - 1;
-    const float d = group16_dot_kv<HD>(q_reg, kst + kk * HD);
-    if ((tid & 15) == 0 && key < nk) sc[key] = __fmul_rn(d, scale);
-  }
-  __syncthreads();
-  float mx = -INFINITY;
-  for (int k = tid; k < nk; k += blockDim.x) mx = fmaxf(mx, sc[k]);
-  mx = blk_max(mx, red);
-  for (int k = tid; k < nk; k += blockDim.x) sc[k] = exp_det(__fsub_rn(sc[k], mx));
-  __syncthreads();
-  if (tid == 0) {
-    float l = 0.f;
-    for (int k = 0; k < nk; ++k) l = __fadd_rn(l, sc[k]);
-    dst[0] = mx;
-    dst[1] = l;
-  } else if (warp == 1) {
-    float o0 = 0.f, o1 = 0.f;
-    for (int k = 0; k < nk; ++k) {
-      const float p = sc[k];
-      o0 = __fadd_rn(o0, __fmul_rn(p, h2f(vst[k * HD + lane])));
-      if (HD > 32) o1 = __fadd_rn(o1, __fmul_rn(p, h2f(vst[k * HD + 32 + lane])));
-    }
-    dst[2 + lane] = o0;
-    if (HD > 32) dst[2 + 32 + lane] = o1;
-  }
-  __syncthreads();
+__device__ __forceinline__ void slot_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
 }
 
-// Combine nch chunk records {m, l, o[HD]} (stride HD+2) of one head; one
-// warp, every lane returns dims lane (and lane+32).
+// Floats of shared memory one attention slot uses: q[64], e[64], red[8],
+// staged V rows (64 x HD halves).
+template <int HD>
+__host__ __device__ constexpr int slot_floats() {
+  return 64 + 64 + 8 + kChunk * HD / 2;
+}
+
+// One 64-slot chunk [k0, k1) of the canonical softmax for one head, by a
+// slot of 64 threads (two warps, named barrier `bar_id`): thread t scores key
+// k0 + t with the dot_f16kv order (its K row read straight into registers),
+// stages its V row, then the slot forms the chunk max, exp_det weights and the
+// two sequential sums (l, and o one dimension per lane).  dst <- {m, l, o[HD]}.
+template <int HD>
+__device__ void attn_chunk_slot(const float* qg, bool q_global, const uint16_t* kcache,
+                                const uint16_t* vcache, int D, int k0, int k1, float scale,
+                                float* sm, int bar_id, float* dst) {
+  float* ew = sm + 64;
+  float* red = sm + 128;
+  uint16_t* vst = reinterpret_cast<uint16_t*>(sm + 136);
+  const int t = threadIdx.x & 63, lane = t & 31, w = t >> 5;
+  const int nk = k1 - k0;
+  constexpr int kV = HD / 8;
+  // every global load of the chunk in flight at once: q (broadcast), K row, V row
+  float q[HD];
+  uint4 kr[kV], vr[kV];
+  const int kk = t < nk ? t : 0;
+  const uint4* ks = reinterpret_cast<const uint4*>(kcache + static_cast<size_t>(k0 + kk) * D);
+  const uint4* vs = reinterpret_cast<const uint4*>(vcache + static_cast<size_t>(k0 + kk) * D);
+#pragma unroll
+  for (int p = 0; p < HD / 4; ++p) {
+    const float4 v = q_global ? __ldcg(reinterpret_cast<const float4*>(qg) + p)
+                              : reinterpret_cast<const float4*>(qg)[p];
+    q[4 * p] = v.x;
+    q[4 * p + 1] = v.y;
+    q[4 * p + 2] = v.z;
+    q[4 * p + 3] = v.w;
+  }
+#pragma unroll
+  for (int p = 0; p < kV; ++p) {
+    kr[p] = __ldcg(ks + p);
+    vr[p] = __ldcg(vs + p);
+  }
+#pragma unroll
+  for (int p = 0; p < kV; ++p) reinterpret_cast<uint4*>(vst + t * HD)[p] = vr[p];
+  float score = -INFINITY;
+  if (t < nk) score = __fmul_rn(thread_dot_kv<HD>(q, kr), scale);
+  float mx = warp_max(score);
+  if (lane == 0) red[w] = mx;
+  slot_sync(bar_id);
+  mx = fmaxf(red[0], red[1]);
+  ew[t] = t < nk ? exp_det(__fsub_rn(score, mx)) : 0.f;
+  slot_sync(bar_id);
+  // o: dimension d = 32*w + lane (HD = 64) or lane (HD = 32, warp 0);
+  // l: warp 1 lane 0.
+  float o = 0.f, l = 0.f;
+  const bool do_o = (HD == 64) || (w == 0);
+  const bool do_l = (w == 1 && lane == 0);
+  const int d = (HD == 64 ? 32 * w : 0) + lane;
+  int k = 0;
+  for (; k + 8 <= nk; k += 8) {
+    float e8[8], v8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      e8[u] = ew[k + u];
+      v8[u] = do_o ? h2f(vst[(k + u) * HD + d]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (do_o) o = __fadd_rn(o, __fmul_rn(e8[u], v8[u]));
+      if (do_l) l = __fadd_rn(l, e8[u]);
+    }
+  }
+  for (; k < nk; ++k) {
+    const float e = ew[k];
+    if (do_o) o = __fadd_rn(o, __fmul_rn(e, h2f(vst[k * HD + d])));
+    if (do_l) l = __fadd_rn(l, e);
+  }
+  if (do_o) dst[4 + d] = o;
+  if (do_l) {
+    dst[0] = mx;
+    dst[1] = l;
+  }
+  slot_sync(bar_id);
+}
+
+// Chunk records are {m, l, pad, pad, o[HD]}: HD + 4 floats, 16-byte aligned.
+template <int HD>
+__host__ __device__ constexpr int rec_floats() {
+  return HD + 4;
+}
+
+// Combine nch chunk records of one head; one warp, every lane returns dims
+// lane (and lane+32).
 template <int HD>
 __device__ __forceinline__ void attn_combine(const float* rec, int nch, bool cg, float* out0,
                                              float* out1) {
   const int lane = threadIdx.x & 31;
   auto rd = [cg](const float* p) { return cg ? __ldcg(p) : *p; };
   float M = -INFINITY;
-  for (int c = 0; c < nch; ++c) M = fmaxf(M, rd(rec + c * (HD + 2)));
+  for (int c = 0; c < nch; ++c) M = fmaxf(M, rd(rec + c * rec_floats<HD>()));
   float L = 0.f, O0 = 0.f, O1 = 0.f;
   for (int c = 0; c < nch; ++c) {
-    const float* r = rec + c * (HD + 2);
+    const float* r = rec + c * rec_floats<HD>();
     const float w = exp_det(__fsub_rn(rd(r), M));
     L = __fadd_rn(L, __fmul_rn(rd(r + 1), w));
-    O0 = __fadd_rn(O0, __fmul_rn(rd(r + 2 + lane), w));
-    if (HD > 32) O1 = __fadd_rn(O1, __fmul_rn(rd(r + 2 + 32 + lane), w));
+    O0 = __fadd_rn(O0, __fmul_rn(rd(r + 4 + lane), w));
+    if (HD > 32) O1 = __fadd_rn(O1, __fmul_rn(rd(r + 4 + 32 + lane), w));
   }
   const float inv = __fdiv_rn(1.0f, L);
   *out0 = __fmul_rn(O0, inv);
   *out1 = HD > 32 ? __fmul_rn(O1, inv) : 0.f;
+}
+
+// dst[0, n) <- src (global, written by other CTAs), n a multiple of 4: every
+// thread issues all of its float4 loads before the first store.
+template <int MAXV>
+__device__ __forceinline__ void load_vec(float* dst, const float* src, int n) {
+  const int nv = n >> 2;
+  float4 r[MAXV];
+#pragma unroll
+  for (int u = 0; u < MAXV; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    if (i < nv) r[u] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+  }
+#pragma unroll
+  for (int u = 0; u < MAXV; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    if (i < nv) reinterpret_cast<float4*>(dst)[i] = r[u];
+  }
+  for (int i = threadIdx.x + MAXV * kThreads; i < nv; i += kThreads)
+    reinterpret_cast<float4*>(dst)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
 }
 
 struct Slices {
@@ -239,9 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   const int D = m.D, F = m.F, V = m.V, H = m.H, L = m.L;
   uint8_t* wbuf[2] = {smem, smem + a.layer_bytes};
   uint16_t* wlog = reinterpret_cast<uint16_t*>(smem + 2 * static_cast<size_t>(a.layer_bytes));
-  uint16_t* kst = wlog + static_cast<size_t>(a.ml) * D;   // [kChunk][HD] staged K
-  uint16_t* vst = kst + kChunk * HD;                      // [kChunk][HD] staged V
-  float* xs = reinterpret_cast<float*>(vst + kChunk * HD); // layer input x
+  float* slots = reinterpret_cast<float*>(wlog + static_cast<size_t>(a.ml) * D);  // attention
+  float* stage = slots + kSlots * slot_floats<HD>();      // staged chunk records
+  float* xs = stage + a.stage_floats;                     // layer input x
   float* hs = xs + D;                                     // LN1 output h
   float* act = hs + D;                                    // operand, max(D, F)
   float* sc = act + (F > D ? F : D);                      // chunk scores / weights
@@ -284,7 +350,14 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   bool alive = mbar_wait(&mbar[2], 0, m.status);
 
   int n_out = 0;
+  unsigned long long* tr = nullptr;
+#define GSVK_TR(slot)                                   \
+  do {                                                  \
+    if (tr && tid == 0) tr[(slot)] = global_ns();       \
+  } while (0)
   for (int idx = 0; idx < a.max_steps && alive; ++idx) {
+    tr = (a.trace && blockIdx.x == 0 && idx < kTraceSteps) ? a.trace + idx * kTraceStride : nullptr;
+    GSVK_TR(0);
     // ------------------------------------------------ greedy sample (all CTAs)
     // t2s_engine.cpp:1594-1636: penalty once per distinct history token,
     // EOS excluded while idx < 11, first maximum wins.
@@ -352,6 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
     }
     if (idx + 1 == a.max_steps) stop = true;
     __syncthreads();
+    GSVK_TR(1);
     if (stop) break;
 
     // ------------------------------------- next input: emb[tok] + alpha*PE
@@ -373,12 +447,13 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       const uint16_t* W2 = W1 + static_cast<size_t>(a.m1) * D;
       // ---------------------------------------------------------------- P1
       if (l > 0) {
-        for (int i = tid; i < D; i += kThreads) xs[i] = __ldcg(m.xpre + i);
+        load_vec<2>(xs, m.xpre, D);
         __syncthreads();
         ln_canon(xs, m.n2g + static_cast<size_t>(l - 1) * D, m.n2b + static_cast<size_t>(l - 1) * D,
                  D, m.eps, red);
       }
       for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(xs[i]));
+      GSVK_TR(16 + 16 * l + 10);
       if (!mbar_wait(&mbar[b], uses[b] & 1u, m.status)) {
         alive = false;
         break;
@@ -386,40 +461,100 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       ++uses[b];
       pending[b] = 0;
       __syncthreads();
+      GSVK_TR(16 + 16 * l + 11);
       {
         uint16_t* kl = m.kc + (static_cast<size_t>(l) * m.cap + pos) * D;
         uint16_t* vl = m.vc + (static_cast<size_t>(l) * m.cap + pos) * D;
         const float* bq = m.bqkv + static_cast<size_t>(l) * 3 * D;
-        for (int r = s.q0 + warp; r < s.q1; r += kWarps) {
-          const float acc = warp_dot32(Wq + static_cast<size_t>(r - s.q0) * D, act, D);
-          if (lane == 0) {
-            const float v = __fadd_rn(acc, bq[r]);
-            if (r < D)
-              m.q[r] = v;
-            else if (r < 2 * D)
-              kl[r - D] = f2h(v);
-            else
-              vl[r - 2 * D] = f2h(v);
+        auto put = [&](int r, float acc) {
+          const float v = __fadd_rn(acc, bq[r]);
+          if (r < D)
+            m.q[r] = v;
+          else if (r < 2 * D)
+            kl[r - D] = f2h(v);
+          else
+            vl[r - 2 * D] = f2h(v);
+        };
+        for (int r = s.q0 + 2 * warp; r < s.q1; r += 2 * kWarps) {
+          if (r + 1 < s.q1) {
+            float a0, a1;
+            warp_dot32x2(Wq + static_cast<size_t>(r - s.q0) * D,
+                         Wq + static_cast<size_t>(r + 1 - s.q0) * D, act, D, &a0, &a1);
+            if (lane == 0) {
+              put(r, a0);
+              put(r + 1, a1);
+            }
+          } else {
+            const float a0 = warp_dot32(Wq + static_cast<size_t>(r - s.q0) * D, act, D);
+            if (lane == 0) put(r, a0);
           }
         }
       }
+      GSVK_TR(16 + 16 * l + 0);
       if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      GSVK_TR(16 + 16 * l + 1);
       // ---------------------------------------------------------------- P2
-      for (int item = blockIdx.x; item < H * nch; item += G) {
-        const int h = item / nch, c = item - (item / nch) * nch;
-        const int k0 = c * kChunk, k1 = min(len, k0 + kChunk);
-        attn_chunk<HD>(m.q + h * HD, m.kc + static_cast<size_t>(l) * m.cap * D + h * HD,
-                       m.vc + static_cast<size_t>(l) * m.cap * D + h * HD, D, k0, k1, m.scale, kst,
-                       vst, sc, red, m.part + (static_cast<size_t>(h) * kMaxChunks + c) * (HD + 2));
+      {
+        const int slot = tid >> 6;
+        float* sm = slots + slot * slot_floats<HD>();
+        for (int base = blockIdx.x * kSlots; base < H * nch; base += G * kSlots) {
+          const int item = base + slot;
+          if (item >= H * nch) break;
+          const int h = item / nch, c = item - (item / nch) * nch;
+          const int k0 = c * kChunk, k1 = min(len, k0 + kChunk);
+          attn_chunk_slot<HD>(m.q + h * HD, true, m.kc + static_cast<size_t>(l) * m.cap * D + h * HD,
+                              m.vc + static_cast<size_t>(l) * m.cap * D + h * HD, D, k0, k1, m.scale,
+                              sm, 1 + slot,
+                              m.part + (static_cast<size_t>(h) * kMaxChunks + c) * rec_floats<HD>());
+        }
       }
+      GSVK_TR(16 + 16 * l + 2);
       if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      GSVK_TR(16 + 16 * l + 3);
       // ---------------------------------------------------------------- P3
-      for (int h = warp; h < H; h += kWarps) {
-        float o0, o1;
-        attn_combine<HD>(m.part + static_cast<size_t>(h) * kMaxChunks * (HD + 2), nch, true, &o0,
-                         &o1);
-        act[h * HD + lane] = h2f(f2h(o0));
-        if (HD > 32) act[h * HD + 32 + lane] = h2f(f2h(o1));
+      {
+        // each warp stages the records of its own heads (all loads in flight at once)
+        const int rec4 = nch * rec_floats<HD>() / 4;
+        const bool staged = kWarps * 2 * rec4 * 4 <= a.stage_floats && H <= 2 * kWarps;
+        float* wst = stage + warp * 2 * rec4 * 4;
+        if (staged) {
+          constexpr int kMaxU = 16;
+          float4 r[kMaxU];
+          const int n4 = (H > kWarps ? 2 : 1) * rec4;
+#pragma unroll
+          for (int u = 0; u < kMaxU; ++u) {
+            const int i = lane + 32 * u;
+            if (i < n4) {
+              const int hh = warp + (i / rec4) * kWarps, j = i - (i / rec4) * rec4;
+              r[u] = hh < H ? __ldcg(reinterpret_cast<const float4*>(
+                                  m.part + static_cast<size_t>(hh) * kMaxChunks * rec_floats<HD>()) + j)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kMaxU; ++u) {
+            const int i = lane + 32 * u;
+            if (i < n4) reinterpret_cast<float4*>(wst)[i] = r[u];
+          }
+          for (int i = lane + 32 * kMaxU; i < n4; i += 32) {
+            const int hh = warp + (i / rec4) * kWarps, j = i - (i / rec4) * rec4;
+            reinterpret_cast<float4*>(wst)[i] =
+                hh < H ? __ldcg(reinterpret_cast<const float4*>(
+                             m.part + static_cast<size_t>(hh) * kMaxChunks * rec_floats<HD>()) + j)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          __syncwarp();
+        }
+        for (int h = warp, k = 0; h < H; h += kWarps, ++k) {
+          float o0, o1;
+          if (staged)
+            attn_combine<HD>(wst + k * rec4 * 4, nch, false, &o0, &o1);
+          else
+            attn_combine<HD>(m.part + static_cast<size_t>(h) * kMaxChunks * rec_floats<HD>(), nch,
+                             true, &o0, &o1);
+          act[h * HD + lane] = h2f(f2h(o0));
+          if (HD > 32) act[h * HD + 32 + lane] = h2f(f2h(o1));
+        }
       }
       __syncthreads();
       {
@@ -429,28 +564,45 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
           if (lane == 0) m.hpre[r] = __fadd_rn(__fadd_rn(acc, bo[r]), xs[r]);
         }
       }
+      GSVK_TR(16 + 16 * l + 4);
       if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      GSVK_TR(16 + 16 * l + 5);
       // ---------------------------------------------------------------- P4
-      for (int i = tid; i < D; i += kThreads) hs[i] = __ldcg(m.hpre + i);
+      load_vec<2>(hs, m.hpre, D);
       __syncthreads();
       ln_canon(hs, m.n1g + static_cast<size_t>(l) * D, m.n1b + static_cast<size_t>(l) * D, D, m.eps,
                red);
       for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(hs[i]));
       __syncthreads();
+      GSVK_TR(16 + 16 * l + 12);
       {
         const float* bb = m.b1 + static_cast<size_t>(l) * F;
-        for (int r = s.a0 + warp; r < s.a1; r += kWarps) {
-          const float acc = warp_dot32(W1 + static_cast<size_t>(r - s.a0) * D, act, D);
-          if (lane == 0) {
-            const float v = __fadd_rn(acc, bb[r]);
-            m.ff[r] = v > 0.f ? v : 0.f;
+        auto put = [&](int r, float acc) {
+          const float v = __fadd_rn(acc, bb[r]);
+          m.ff[r] = v > 0.f ? v : 0.f;
+        };
+        for (int r = s.a0 + 2 * warp; r < s.a1; r += 2 * kWarps) {
+          if (r + 1 < s.a1) {
+            float a0, a1;
+            warp_dot32x2(W1 + static_cast<size_t>(r - s.a0) * D,
+                         W1 + static_cast<size_t>(r + 1 - s.a0) * D, act, D, &a0, &a1);
+            if (lane == 0) {
+              put(r, a0);
+              put(r + 1, a1);
+            }
+          } else {
+            const float a0 = warp_dot32(W1 + static_cast<size_t>(r - s.a0) * D, act, D);
+            if (lane == 0) put(r, a0);
           }
         }
       }
+      GSVK_TR(16 + 16 * l + 6);
       if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      GSVK_TR(16 + 16 * l + 7);
       // ---------------------------------------------------------------- P5
-      for (int i = tid; i < F; i += kThreads) act[i] = __ldcg(m.ff + i);
+      load_vec<4>(act, m.ff, F);
       __syncthreads();
+      GSVK_TR(16 + 16 * l + 13);
       {
         const float* bb = m.b2 + static_cast<size_t>(l) * D;
         for (int r = s.b0 + warp; r < s.b1; r += kWarps) {
@@ -463,11 +615,13 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
         prefetch_layer(m, a, s, (l + 2) % L, wbuf[b], &mbar[b]);  // global layer gl + 2
         pending[b] = 1;
       }
+      GSVK_TR(16 + 16 * l + 8);
       if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      GSVK_TR(16 + 16 * l + 9);
     }
     if (!alive) break;
     // ---------------------------------------------------------------- logits
-    for (int i = tid; i < D; i += kThreads) xs[i] = __ldcg(m.xpre + i);
+    load_vec<2>(xs, m.xpre, D);
     __syncthreads();
     ln_canon(xs, m.n2g + static_cast<size_t>(L - 1) * D, m.n2b + static_cast<size_t>(L - 1) * D, D,
              m.eps, red);
@@ -475,8 +629,11 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       const float acc = warp_dot32(wlog + static_cast<size_t>(r - s.l0) * D, xs, D);
       if (lane == 0) m.logits[r] = acc;
     }
+    GSVK_TR(2);
     if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+    GSVK_TR(3);
   }
+#undef GSVK_TR
   // Drain bulk copies still in flight before the CTA exits.
   if (tid == 0) {
     for (int b = 0; b < 2; ++b)
@@ -594,23 +751,24 @@ __global__ void canon_gemv_kernel(const uint16_t* __restrict__ w, const float* _
 
 // Masked prefill attention (t2s_engine.cpp:944-979) in the canonical chunked
 // softmax: query q of the block sees slots [0, pos + max(text_len, q+1)).
+// One CTA per (query, head); its four 64-thread slots take the chunks in
+// turn, then warp 0 combines the chunk records in order.
 template <int HD>
-__global__ void __launch_bounds__(128) prefill_attn_kernel(
+__global__ void __launch_bounds__(kThreads) prefill_attn_kernel(
     const float* __restrict__ qkv, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
     int D, int pos, int text_len, float scale, uint16_t* __restrict__ out16) {
-  extern __shared__ uint8_t psm[];
-  uint16_t* kst = reinterpret_cast<uint16_t*>(psm);
-  uint16_t* vst = kst + kChunk * HD;
-  float* sc = reinterpret_cast<float*>(vst + kChunk * HD);
-  float* red = sc + kChunk;
-  float* rec = red + 64;  // [nch][HD + 2]
+  extern __shared__ float psm[];
+  float* rec = psm + kSlots * slot_floats<HD>();  // [nch][rec_floats]
   const int q = blockIdx.x, h = blockIdx.y;
   const int n = pos + max(text_len, q + 1);
   const int nch = (n + kChunk - 1) / kChunk;
   const float* qv = qkv + static_cast<size_t>(q) * 3 * D + h * HD;
-  for (int c = 0; c < nch; ++c)
-    attn_chunk<HD>(qv, kc + h * HD, vc + h * HD, D, c * kChunk, min(n, (c + 1) * kChunk), scale, kst,
-                   vst, sc, red, rec + c * (HD + 2));
+  const int slot = threadIdx.x >> 6;
+  for (int c = slot; c < nch; c += kSlots)
+    attn_chunk_slot<HD>(qv, false, kc + h * HD, vc + h * HD, D, c * kChunk,
+                        min(n, (c + 1) * kChunk), scale, psm + slot * slot_floats<HD>(), 1 + slot,
+                        rec + c * rec_floats<HD>());
+  __syncthreads();
   if (threadIdx.x < 32) {
     float o0, o1;
     attn_combine<HD>(rec, nch, false, &o0, &o1);
@@ -664,6 +822,8 @@ struct T2SEngine {
   int32_t* d_tokens = nullptr;
   int* d_nout = nullptr;
   float* d_margins = nullptr;
+  unsigned long long* d_trace = nullptr;
+  bool trace_on = false;
   // prefill buffers
   float *px = nullptr, *pqkv = nullptr, *phpre = nullptr;
   uint16_t *px16 = nullptr, *pattn16 = nullptr, *pff16 = nullptr;
@@ -768,13 +928,14 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   // ---- KV cache + decode scratch + prefill buffers (one allocation)
   off = 0;
   const size_t o_kc = take((size_t)L * cap * D * 2), o_vc = take((size_t)L * cap * D * 2),
-               o_q = take((size_t)D * 4), o_part = take((size_t)H * kMaxChunks * (HD + 2) * 4),
+               o_q = take((size_t)D * 4), o_part = take((size_t)H * kMaxChunks * (HD + 4) * 4),
                o_hpre = take((size_t)D * 4), o_ff = take((size_t)F * 4), o_xpre = take((size_t)D * 4),
                o_logits = take((size_t)V * 4), o_bar = take(256), o_prompt = take((size_t)cap * 4),
                o_tok = take((size_t)cap * 4), o_nout = take(256), o_marg = take((size_t)cap * 4),
                o_px = take((size_t)cap * D * 4), o_pqkv = take((size_t)cap * 3 * D * 4),
                o_phpre = take((size_t)cap * D * 4), o_px16 = take((size_t)cap * D * 2),
-               o_pattn = take((size_t)cap * D * 2), o_pff = take((size_t)cap * F * 2);
+               o_pattn = take((size_t)cap * D * 2), o_pff = take((size_t)cap * F * 2),
+               o_trace = take((size_t)kTraceSteps * kTraceStride * 8);
   if (cudaMalloc(&e->scratch, off) != cudaSuccess) {
     cudaGetLastError();
     gsvk_t2s_destroy(e);
@@ -805,6 +966,7 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   e->px16 = reinterpret_cast<uint16_t*>(sb + o_px16);
   e->pattn16 = reinterpret_cast<uint16_t*>(sb + o_pattn);
   e->pff16 = reinterpret_cast<uint16_t*>(sb + o_pff);
+  e->d_trace = reinterpret_cast<unsigned long long*>(sb + o_trace);
 
   // ---- decode launch plan: one CTA per SM, weight slices sized for the
   // largest CTA, two layer buffers + the persistent logits slice.
@@ -818,11 +980,13 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   a.ml = ceil_rows(V);
   a.layer_bytes = static_cast<uint32_t>(align_up(
       ((size_t)a.mq * D + (size_t)a.mo * D + (size_t)a.m1 * D + (size_t)a.m2 * F) * 2, 128));
-  const size_t floats = (size_t)D * 2 + std::max(D, F) + kChunk + 64;
-  e->decode_smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 +
-                   2 * (size_t)kChunk * HD * 2 + floats * 4 + 8 * 4 + 4 * 8 + align_up(V, 16) + 64;
-  e->attn_smem = 2 * (size_t)kChunk * HD * 2 + ((size_t)kChunk + 64) * 4 +
-                 (size_t)kMaxChunks * (HD + 2) * 4;
+  const size_t slot_f = (size_t)kSlots * (HD == 32 ? slot_floats<32>() : slot_floats<64>());
+  const size_t max_nch = ((size_t)cap + kChunk - 1) / kChunk;
+  a.stage_floats = (int)std::min<size_t>((size_t)2 * kWarps * max_nch * (HD + 4), 16384);
+  const size_t floats = slot_f + a.stage_floats + (size_t)D * 2 + std::max(D, F) + kChunk + 64;
+  e->decode_smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 + floats * 4 + 8 * 4 +
+                   4 * 8 + align_up(V, 16) + 64;
+  e->attn_smem = (slot_f + max_nch * (HD + 4)) * 4;
   e->HD = HD;
   e->decode_fn = HD == 32 ? (const void*)t2s_decode_kernel<32> : (const void*)t2s_decode_kernel<64>;
   e->attn_fn = HD == 32 ? (const void*)prefill_attn_kernel<32> : (const void*)prefill_attn_kernel<64>;
@@ -914,7 +1078,7 @@ int gsvk_t2s_prefill(gsvk_t2s_t h, float* x, size_t S, size_t pos, size_t text_l
       const float* qkv = h->pqkv;
       uint16_t* o16 = h->pattn16;
       void* args[] = {&qkv, &kl, &vl, &Di, &posi, &tl, &sc, &o16};
-      if ((rc = check_cuda(cudaLaunchKernel(h->attn_fn, grid, dim3(128), args, h->attn_smem, st),
+      if ((rc = check_cuda(cudaLaunchKernel(h->attn_fn, grid, dim3(kThreads), args, h->attn_smem, st),
                            "prefill_attn_kernel")))
         return rc;
     }
@@ -939,14 +1103,11 @@ int gsvk_t2s_prefill(gsvk_t2s_t h, float* x, size_t S, size_t pos, size_t text_l
   return GSVK_OK;
 }
 
-int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
-                             size_t max_steps, int stop_on_eos, int32_t* tokens_dev,
-                             int* n_out_dev, float* margins_dev, gsvk_stream_t stream) {
-  if (!h || !prompt_dev || P == 0 || !tokens_dev || !n_out_dev)
-    return fail(GSVK_ERR_INVALID, "t2s_generate: null argument or empty prompt");
-  if (prefix + P + max_steps > (size_t)h->cap)
-    return fail(GSVK_ERR_INVALID, "t2s_generate: prefix+P+steps=%zu exceeds cap %d",
-                prefix + P + max_steps, h->cap);
+int gsvk_t2s_prompt(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
+                    gsvk_stream_t stream) {
+  if (!h || !prompt_dev || P == 0) return fail(GSVK_ERR_INVALID, "t2s_prompt: null or empty");
+  if (prefix + P > (size_t)h->cap)
+    return fail(GSVK_ERR_INVALID, "t2s_prompt: prefix+P=%zu exceeds cap %d", prefix + P, h->cap);
   const T2SDev& d = h->dev;
   cudaStream_t st = as_cuda(stream);
   const int D = h->D;
@@ -955,10 +1116,23 @@ int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_
   int rc = check_launch("embed_kernel");
   if (rc) return rc;
   if ((rc = gsvk_t2s_prefill(h, h->px, P, prefix, 0, stream))) return rc;
-  // first logits from the last prompt row (fp32 activations, t2s_engine.cpp:703-707)
+  // first logits from the last prompt row, fp32 activations (t2s_engine.cpp:703-707, 1806)
   canon_gemv_kernel<<<(unsigned)((h->V * 32 + 255) / 256), 256, 0, st>>>(
       d.wpred, h->px + (P - 1) * D, d.logits, h->V, D);
-  if ((rc = check_launch("canon_gemv_kernel"))) return rc;
+  return check_launch("canon_gemv_kernel");
+}
+
+int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
+                    size_t max_steps, int stop_on_eos, int32_t* tokens_dev, int* n_out_dev,
+                    float* margins_dev, gsvk_stream_t stream) {
+  if (!h || !prompt_dev || P == 0 || !tokens_dev || !n_out_dev)
+    return fail(GSVK_ERR_INVALID, "t2s_decode: null argument or empty prompt");
+  if (prefix + P + max_steps > (size_t)h->cap)
+    return fail(GSVK_ERR_INVALID, "t2s_decode: prefix+P+steps=%zu exceeds cap %d",
+                prefix + P + max_steps, h->cap);
+  const T2SDev& d = h->dev;
+  cudaStream_t st = as_cuda(stream);
+  int rc;
   if ((rc = check_cuda(cudaMemsetAsync(d.bar, 0, 4, st), "reset grid barrier"))) return rc;
   if ((rc = check_cuda(cudaMemsetAsync(n_out_dev, 0, 4, st), "reset n_out"))) return rc;
   if (max_steps == 0) return GSVK_OK;
@@ -972,11 +1146,32 @@ int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_
   a.tokens = tokens_dev;
   a.n_out = n_out_dev;
   a.margins = margins_dev;
+  a.trace = h->trace_on ? h->d_trace : nullptr;
   T2SDev dv = d;
   void* args[] = {&dv, &a};
   return check_cuda(cudaLaunchCooperativeKernel(h->decode_fn, dim3(h->G), dim3(kThreads),
                                                 args, h->decode_smem, st),
                     "t2s_decode_kernel (cooperative launch)");
+}
+
+int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
+                             size_t max_steps, int stop_on_eos, int32_t* tokens_dev,
+                             int* n_out_dev, float* margins_dev, gsvk_stream_t stream) {
+  if (!h || !prompt_dev || P == 0 || !tokens_dev || !n_out_dev)
+    return fail(GSVK_ERR_INVALID, "t2s_generate: null argument or empty prompt");
+  if (prefix + P + max_steps > (size_t)h->cap)
+    return fail(GSVK_ERR_INVALID, "t2s_generate: prefix+P+steps=%zu exceeds cap %d",
+                prefix + P + max_steps, h->cap);
+  int rc = gsvk_t2s_prompt(h, prefix, prompt_dev, P, stream);
+  if (rc) return rc;
+  return gsvk_t2s_decode(h, prefix, prompt_dev, P, max_steps, stop_on_eos, tokens_dev, n_out_dev,
+                         margins_dev, stream);
+}
+
+int gsvk_t2s_launches_per_generate(gsvk_t2s_t h) {
+  // embed + per layer (4 GEMMs, KV append, attention, 2 LayerNorms) + logits
+  // GEMV + the decode kernel
+  return h ? 1 + 8 * h->L + 1 + 1 : 0;
 }
 
 int gsvk_t2s_generate(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_host, size_t P,
@@ -1005,6 +1200,23 @@ int gsvk_t2s_generate(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_host, s
                        "margins download")))
     return rc;
   return gsvk_device_status(1);
+}
+
+int gsvk_t2s_set_trace(gsvk_t2s_t h, int enable) {
+  if (!h) return fail(GSVK_ERR_INVALID, "t2s_set_trace: null handle");
+  h->trace_on = enable != 0;
+  if (h->trace_on)
+    return check_cuda(cudaMemset(h->d_trace, 0, (size_t)kTraceSteps * kTraceStride * 8),
+                      "trace reset");
+  return GSVK_OK;
+}
+
+int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n) {
+  if (!h || !host_out) return fail(GSVK_ERR_INVALID, "t2s_read_trace: null");
+  const size_t total = (size_t)kTraceSteps * kTraceStride;
+  return check_cuda(cudaMemcpy(host_out, h->d_trace, (n < total ? n : total) * 8,
+                               cudaMemcpyDeviceToHost),
+                    "trace download");
 }
 
 int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out) {

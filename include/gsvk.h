@@ -167,10 +167,31 @@ int gsvk_t2s_prefill(gsvk_t2s_t h, float* x, size_t S, size_t pos, size_t text_l
 int gsvk_t2s_generate(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_host, size_t P,
                       size_t max_steps, int stop_on_eos, int32_t* tokens_host,
                       float* margins_host, int* n_out, gsvk_stream_t stream);
-/* Same with DEVICE prompt / outputs, asynchronous on `stream`. */
+/* The two halves of generate, DEVICE prompt, asynchronous on `stream`:
+ * gsvk_t2s_prompt embeds the prompt (audio embedding + alpha * PE), runs the
+ * prefill at slots prefix.. and computes the first logits;
+ * gsvk_t2s_decode runs the whole greedy loop in one persistent kernel. */
+int gsvk_t2s_prompt(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
+                    gsvk_stream_t stream);
+int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
+                    size_t max_steps, int stop_on_eos, int32_t* tokens_dev, int* n_out_dev,
+                    float* margins_dev, gsvk_stream_t stream);
+/* Kernel launches one generate issues (prompt + decode). */
+int gsvk_t2s_launches_per_generate(gsvk_t2s_t h);
+/* Same as gsvk_t2s_generate with DEVICE prompt / outputs, asynchronous. */
 int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
                              size_t max_steps, int stop_on_eos, int32_t* tokens_dev,
                              int* n_out_dev, float* margins_dev, gsvk_stream_t stream);
+/* Phase trace of the decode kernel (the reference's GSV_AR_TIMING probe,
+ * t2s_engine.cpp:1906-1925, at phase granularity): when enabled, CTA 0
+ * records the device clock (ns) at every phase boundary of the first 4 steps
+ * of the next decode: per step 1040 slots, [0] step start, [1] sampled,
+ * [2] logits done, [3] after the logits barrier, [16 + 16*l + 2*k] phase k of
+ * layer l done, [.. + 1] its barrier passed, [16 + 16*l + 10..13] P1 after
+ * LayerNorm, P1 after the weight wait, P4 after LayerNorm, P5 after the
+ * activation load.  read_trace is synchronous. */
+int gsvk_t2s_set_trace(gsvk_t2s_t h, int enable);
+int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n);
 /* The logits the last step sampled from (raw, before the penalty); synchronous. */
 int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out);
 

@@ -310,12 +310,12 @@ void accum_f16kv(float* ov, const uint16_t* v16, float p, size_t HD) {
   }
 }
 
-constexpr size_t kAttnChunk = 128;
+constexpr size_t kAttnChunk = 64;
 
 // Attention of one query row q (fp32, one head) over key/value slots
 // [0, n) of a token-major fp16 cache (t2s_engine.cpp:1062-1087): scores
 // dot_f16kv * scale, stable softmax, probability-weighted sum of V.  The
-// softmax is associated in fixed chunks of 128 slots from slot 0 (per chunk
+// softmax is associated in fixed chunks of 64 slots from slot 0 (per chunk
 // max m_c, sum l_c of exp(s - m_c) and o_c = sum exp(s - m_c) v, each a
 // sequential sum in slot order; then chunk weights exp(m_c - M)), the order a
 // split-K device kernel reproduces exactly; it equals the reference's softmax

@@ -148,7 +148,7 @@ void ora_t2s_pe_row(int d_model, size_t pos, float* pe);
  *     in order), for fp16 and fp32 activations alike;
  *   - LayerNorm: kern.cpp:27-58 (8-lane fp32 sums, fp64 combine);
  *   - attention scores: dot_f16kv (t2s_engine.cpp:69-99);
- *   - softmax: chunks of 128 slots (sequential sums inside a chunk, chunk
+ *   - softmax: chunks of 64 slots (sequential sums inside a chunk, chunk
  *     weights exp(m_c - M)) with a deterministic Cody-Waite/Taylor exp within
  *     2 ulp of expf.
  * Rounding points are the reference's: fp16(x) before QKV, out-proj and W1
