@@ -60,6 +60,8 @@ SIGNATURES = {
     "gsvk_t2s_launches_per_generate": (c_int, [_vp]),
     "gsvk_t2s_set_trace": (c_int, [_vp, c_int]),
     "gsvk_t2s_read_trace": (c_int, [_vp, _vp, _sz]),
+    "gsvk_attention_workspace_floats": (_sz, [_sz, _sz, _sz]),
+    "gsvk_attention_decode": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp, _vp, _vp]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -197,6 +199,26 @@ def gemm_ex(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, 
                  0 if c_f16 is None else c_f16.stride(0), act, slope, alpha)
     check(lib().gsvk_gemm_f16_ex(ctypes.byref(g), _stream(stream)))
     return c if c is not None else c_f16
+
+
+# ------------------------------------------------------- decode attention
+def attention_workspace_floats(length: int, n_heads: int, head_dim: int) -> int:
+    return lib().gsvk_attention_workspace_floats(length, n_heads, head_dim)
+
+
+def attention_decode(q, kcache, vcache, length: int, n_heads: int, head_dim: int, scale: float,
+                     out=None, workspace=None, stream=None):
+    """One decode step of multi-head attention over a token-major fp16 cache."""
+    import torch
+
+    out = out if out is not None else torch.empty(n_heads * head_dim, device=q.device)
+    if workspace is None:
+        workspace = torch.empty(attention_workspace_floats(length, n_heads, head_dim),
+                                device=q.device)
+    check(lib().gsvk_attention_decode(_ptr(q), _ptr(kcache), _ptr(vcache), length, n_heads,
+                                      head_dim, kcache.stride(0), scale, _ptr(out),
+                                      _ptr(workspace), _stream(stream)))
+    return out
 
 
 # --------------------------------------------------------------------- a22

@@ -777,6 +777,35 @@ __global__ void __launch_bounds__(kThreads) prefill_attn_kernel(
   }
 }
 
+// Standalone decode attention (gsvk_attention_decode): stage 1 computes one
+// canonical 64-slot chunk record per (head, chunk) item, four items per CTA.
+template <int HD>
+__global__ void __launch_bounds__(kThreads) attn_chunks_kernel(
+    const float* __restrict__ q, const uint16_t* __restrict__ kc, const uint16_t* __restrict__ vc,
+    int len, int H, int D, float scale, float* __restrict__ rec) {
+  extern __shared__ float asm_[];
+  const int nch = (len + kChunk - 1) / kChunk;
+  const int slot = threadIdx.x >> 6;
+  const int item = blockIdx.x * kSlots + slot;
+  if (item >= H * nch) return;  // whole slot exits together (slot-local barriers only)
+  const int h = item / nch, c = item - (item / nch) * nch;
+  attn_chunk_slot<HD>(q + h * HD, true, kc + h * HD, vc + h * HD, D, c * kChunk,
+                      min(len, (c + 1) * kChunk), scale, asm_ + slot * slot_floats<HD>(), 1 + slot,
+                      rec + static_cast<size_t>(item) * rec_floats<HD>());
+}
+
+// Stage 2: one warp per head combines its chunk records in order.
+template <int HD>
+__global__ void attn_combine_kernel(const float* __restrict__ rec, int len, int H,
+                                    float* __restrict__ out) {
+  const int nch = (len + kChunk - 1) / kChunk;
+  const int h = blockIdx.x;
+  float o0, o1;
+  attn_combine<HD>(rec + static_cast<size_t>(h) * nch * rec_floats<HD>(), nch, true, &o0, &o1);
+  out[h * HD + threadIdx.x] = o0;
+  if (HD > 32) out[h * HD + 32 + threadIdx.x] = o1;
+}
+
 // Row LayerNorm (kern.cpp:27-58, canonical order) writing fp32 and fp16.
 __global__ void __launch_bounds__(256) ln_rows_canon_kernel(
     const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ b,
@@ -1223,6 +1252,41 @@ int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out) {
   if (!h || !host_out) return fail(GSVK_ERR_INVALID, "t2s_read_logits: null");
   return check_cuda(cudaMemcpy(host_out, h->dev.logits, (size_t)h->V * 4, cudaMemcpyDeviceToHost),
                     "logits download");
+}
+
+size_t gsvk_attention_workspace_floats(size_t len, size_t n_heads, size_t head_dim) {
+  return n_heads * ((len + kChunk - 1) / kChunk) * (head_dim + 4);
+}
+
+int gsvk_attention_decode(const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                          size_t len, size_t n_heads, size_t head_dim, size_t row_stride,
+                          float scale, float* out, float* workspace, gsvk_stream_t stream) {
+  if (!q || !kcache || !vcache || !out || !workspace || len == 0 || n_heads == 0)
+    return fail(GSVK_ERR_INVALID, "attention_decode: null pointer or zero size");
+  if (head_dim != 32 && head_dim != 64)
+    return fail(GSVK_ERR_UNSUPPORTED, "attention_decode: head_dim must be 32 or 64");
+  if (row_stride < n_heads * head_dim || row_stride % 8 != 0 || len > (1u << 24))
+    return fail(GSVK_ERR_INVALID, "attention_decode: bad row stride or length");
+  if (!aligned16(q) || !aligned16(kcache) || !aligned16(vcache))
+    return fail(GSVK_ERR_ALIGN, "attention_decode: q, K and V need 16-byte alignment");
+  cudaStream_t st = as_cuda(stream);
+  const int L = (int)len, H = (int)n_heads, D = (int)row_stride;
+  const int items = H * ((L + kChunk - 1) / kChunk);
+  const unsigned grid = (unsigned)((items + kSlots - 1) / kSlots);
+  if (head_dim == 32) {
+    const size_t sm = (size_t)kSlots * slot_floats<32>() * 4;
+    attn_chunks_kernel<32><<<grid, kThreads, sm, st>>>(q, kcache, vcache, L, H, D, scale, workspace);
+    int rc = check_launch("attn_chunks_kernel");
+    if (rc) return rc;
+    attn_combine_kernel<32><<<(unsigned)H, 32, 0, st>>>(workspace, L, H, out);
+  } else {
+    const size_t sm = (size_t)kSlots * slot_floats<64>() * 4;
+    attn_chunks_kernel<64><<<grid, kThreads, sm, st>>>(q, kcache, vcache, L, H, D, scale, workspace);
+    int rc = check_launch("attn_chunks_kernel");
+    if (rc) return rc;
+    attn_combine_kernel<64><<<(unsigned)H, 32, 0, st>>>(workspace, L, H, out);
+  }
+  return check_launch("attn_combine_kernel");
 }
 
 }  // extern "C"

@@ -122,6 +122,19 @@ int gsvk_softmax_rows(const float* x, float* y, size_t rows, size_t n,
 int gsvk_activation(const float* x, float* y, size_t n, int act, float slope,
                     gsvk_stream_t stream);
 
+/* ---- decode attention (a17 support op) ---------------------------------- */
+/* The per-head attention of one decode step (t2s_engine.cpp:1062-1087):
+ *   out[h] = softmax(q[h] . K[0:len, h]^T * scale) . V[0:len, h]
+ * over a token-major fp16 cache whose rows hold row_stride halves (head h at
+ * column h*head_dim).  Canonical chunked softmax (64-slot chunks, the T2S
+ * decode kernel's order: bit-identical results).  q and out are fp32
+ * [n_heads * head_dim]; head_dim 32 or 64.  workspace: DEVICE floats, at least
+ * gsvk_attention_workspace_floats(len, n_heads, head_dim) of them. */
+size_t gsvk_attention_workspace_floats(size_t len, size_t n_heads, size_t head_dim);
+int gsvk_attention_decode(const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                          size_t len, size_t n_heads, size_t head_dim, size_t row_stride,
+                          float scale, float* out, float* workspace, gsvk_stream_t stream);
+
 /* ---- T2S autoregressive transformer (a16-a19) -------------------------- */
 /* Replaces ar::T2SEngine (t2s_engine.hpp:86-220): weights registered once
  * (the analogue of the reference's load + amx_pack), KV cache and every

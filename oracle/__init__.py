@@ -83,6 +83,7 @@ def lib():
             "ora_t2s_decode_layer": (None, [vp, vp, c_int, vp, sz, vp, vp]),
             "ora_t2s_prefill_layer": (None, [vp, vp, c_int, vp, sz, sz, sz, vp, vp]),
             "ora_t2s_greedy_sample": (c_int, [vp, c_int, vp, sz, c_int, vp]),
+            "ora_attention_decode": (None, [vp, vp, vp, sz, sz, sz, sz, c_float, vp]),
             "ora_t2s_generate": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp, vp, vp]),
         }
         for name, (res, args) in sigs.items():
@@ -290,6 +291,15 @@ def t2s_prefill_layer(model: dict, layer: int, x: np.ndarray, pos: int, text_len
     d, w = t2s_structs(model)
     lib().ora_t2s_prefill_layer(ctypes.byref(d), ctypes.byref(w), layer, _p(x), x.shape[0], pos,
                                 text_len, _p(kc), _p(vc))
+
+
+def attention_decode(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, length: int, n_heads: int,
+                     head_dim: int, scale: float) -> np.ndarray:
+    """q [H*HD] fp32; kc/vc [slots, row_stride] fp16 bits."""
+    out = np.zeros(n_heads * head_dim, np.float32)
+    lib().ora_attention_decode(_p(np.ascontiguousarray(q, np.float32)), _p(kc), _p(vc), length,
+                               n_heads, head_dim, kc.shape[1], scale, _p(out))
+    return out
 
 
 def t2s_greedy_sample(logits: np.ndarray, history: np.ndarray, eos_allowed: bool):

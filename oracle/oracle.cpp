@@ -734,6 +734,14 @@ void ora_t2s_prefill_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int
     ora_layernorm(x + t * D, w->n2g + l * D, w->n2b + l * D, x + t * D, D, dm->ln_eps);
 }
 
+void ora_attention_decode(const float* q, const uint16_t* kc, const uint16_t* vc, size_t len,
+                          size_t n_heads, size_t head_dim, size_t row_stride, float scale,
+                          float* out) {
+  for (size_t h = 0; h < n_heads; ++h)
+    attend_canon(q + h * head_dim, kc + h * head_dim, vc + h * head_dim, row_stride, len,
+                 head_dim, scale, out + h * head_dim);
+}
+
 int ora_t2s_greedy_sample(float* lg, int V, const int32_t* hist, size_t n_hist,
                           int eos_allowed, int* raw_argmax) {
   const int limit = eos_allowed ? V : V - 1;

@@ -172,6 +172,13 @@ void ora_t2s_prefill_layer(const ora_t2s_dims* d, const ora_t2s_weights* w,
                            size_t text_len, uint16_t* kcache,
                            uint16_t* vcache);
 
+/* t2s_engine.cpp:1062-1087  one query per head over slots [0, len) of a
+ * token-major fp16 cache (rows of row_stride halves, head h at column
+ * h*head_dim), canonical chunked softmax; out [n_heads*head_dim]. */
+void ora_attention_decode(const float* q, const uint16_t* kc, const uint16_t* vc, size_t len,
+                          size_t n_heads, size_t head_dim, size_t row_stride, float scale,
+                          float* out);
+
 /* t2s_engine.cpp:1594-1636  repetition penalty 1.35 once per distinct
  * history token, EOS column excluded while !eos_allowed, argmax. */
 int ora_t2s_greedy_sample(float* logits, int vocab, const int32_t* history,
