@@ -62,6 +62,9 @@ SIGNATURES = {
     "gsvk_t2s_read_trace": (c_int, [_vp, _vp, _sz]),
     "gsvk_attention_workspace_floats": (_sz, [_sz, _sz, _sz]),
     "gsvk_attention_decode": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp, _vp, _vp]),
+    "gsvk_attention_decode_noalloc_max_floats": (_sz, []),
+    "gsvk_attention_decode_noalloc": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp,
+                                              _vp]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),

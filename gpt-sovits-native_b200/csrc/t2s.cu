@@ -23,6 +23,7 @@
 // matrix and streams them into shared memory one layer ahead with bulk
 // copies, so HBM streaming overlaps the barrier latency chain.
 #include <cmath>
+#include <mutex>
 #include <cstring>
 #include <vector>
 
@@ -1287,6 +1288,67 @@ int gsvk_attention_decode(const float* q, const uint16_t* kcache, const uint16_t
     attn_combine_kernel<64><<<(unsigned)H, 32, 0, st>>>(workspace, L, H, out);
   }
   return check_launch("attn_combine_kernel");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode attention.
+//
+// For callers that must not allocate device memory at all: code running
+// under an external allocator that owns every byte of device memory (a host
+// framework's memory pool, a fixed-budget embedded deployment), or code that
+// may not touch the CUDA allocator on its call path.  The chunk records that
+// gsvk_attention_decode keeps in a caller-provided workspace live here in a
+// fixed file-scope device array instead.  Every GPU that loads this library
+// holds this array (1 MiB) until the process exits.
+namespace {
+
+constexpr size_t kNoAllocAttnFloats = 262144;  // 1 MiB of fp32 chunk records
+static __device__ __align__(256) float g_noalloc_attn_scratch[kNoAllocAttnFloats];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};  // device address of the array, per device
+
+}  // namespace
+
+extern "C" {
+
+size_t gsvk_attention_decode_noalloc_max_floats(void) { return kNoAllocAttnFloats; }
+
+int gsvk_attention_decode_noalloc(const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                                  size_t len, size_t n_heads, size_t head_dim, size_t row_stride,
+                                  float scale, float* out, gsvk_stream_t stream) {
+  if (head_dim == 32 || head_dim == 64) {
+    const size_t need = gsvk_attention_workspace_floats(len, n_heads, head_dim);
+    if (need > kNoAllocAttnFloats)
+      return fail(GSVK_ERR_UNSUPPORTED,
+                  "attention_decode_noalloc: needs %zu scratch floats, the static array holds "
+                  "%zu (n_heads * ceil(len/64) * (head_dim+4) must not exceed it)",
+                  need, kNoAllocAttnFloats);
+  }
+  int dev = -1;
+  int rc = check_cuda(cudaGetDevice(&dev), "attention_decode_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(GSVK_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  float* scratch = nullptr;
+  {
+    // One-time set-up per device, with that device current: host code cannot
+    // use the array's name as a device address, so resolve it here.
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_attn_scratch),
+                      "attention_decode_noalloc: cudaGetSymbolAddress");
+      if (rc) return rc;
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  // Same kernels as gsvk_attention_decode; the records it reads are all
+  // written earlier in the same call, so nothing needs clearing between calls.
+  return gsvk_attention_decode(q, kcache, vcache, len, n_heads, head_dim, row_stride, scale, out,
+                               scratch, stream);
 }
 
 }  // extern "C"

@@ -135,6 +135,24 @@ int gsvk_attention_decode(const float* q, const uint16_t* kcache, const uint16_t
                           size_t len, size_t n_heads, size_t head_dim, size_t row_stride,
                           float scale, float* out, float* workspace, gsvk_stream_t stream);
 
+/* Allocation-free form of gsvk_attention_decode, for callers that cannot
+ * allocate device memory (a host framework whose pool owns all device
+ * memory, a fixed-budget deployment, a call path that must not touch the CUDA
+ * allocator).  No counterpart in the reference, whose CPU kernels keep their
+ * scratch in thread-local vectors.  The chunk records live in one static
+ * device array of gsvk_attention_decode_noalloc_max_floats() floats (1 MiB),
+ * held by every GPU that loads the library until the process exits; requests
+ * needing more (n_heads * ceil(len/64) * (head_dim+4) floats) return
+ * GSVK_ERR_UNSUPPORTED.  The first call on a device resolves the array's
+ * device address; make that first call before any stream capture.  All calls
+ * on a device share the array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller.  Results
+ * are bit-identical to gsvk_attention_decode. */
+size_t gsvk_attention_decode_noalloc_max_floats(void);
+int gsvk_attention_decode_noalloc(const float* q, const uint16_t* kcache, const uint16_t* vcache,
+                                  size_t len, size_t n_heads, size_t head_dim, size_t row_stride,
+                                  float scale, float* out, gsvk_stream_t stream);
+
 /* ---- T2S autoregressive transformer (a16-a19) -------------------------- */
 /* Replaces ar::T2SEngine (t2s_engine.hpp:86-220): weights registered once
  * (the analogue of the reference's load + amx_pack), KV cache and every
