@@ -364,6 +364,7 @@ def run_reference(args, rank, world):
 
 
 def main():
+    global T2S_STEPS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -371,8 +372,11 @@ def main():
     ap.add_argument("--impl", default="gsvk", choices=["gsvk", "reference"])
     ap.add_argument("--workload", default="t2s_decode_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=T2S_STEPS,
+                    help="tokens per utterance (default 500; smaller only for profiling captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    T2S_STEPS = args.decode_steps
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
