@@ -20,7 +20,7 @@ from . import workloads  # noqa: F401  (seeded synthetic inputs)
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libgsvk.so")
 
-ACT_NONE, ACT_RELU, ACT_GELU_ERF, ACT_LEAKY = 0, 1, 2, 3
+ACT_NONE, ACT_RELU, ACT_GELU_ERF, ACT_LEAKY, ACT_TANH = 0, 1, 2, 3, 4
 STATUS = {0: "OK", -1: "INVALID", -2: "ALIGN", -3: "CUDA", -4: "TIMEOUT", -5: "UNSUPPORTED",
           -6: "NOMEM", -7: "NODEV"}
 
@@ -65,6 +65,17 @@ SIGNATURES = {
     "gsvk_attention_decode_noalloc_max_floats": (_sz, []),
     "gsvk_attention_decode_noalloc": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp,
                                               _vp]),
+    "gsvk_conv1d_pack_weight": (c_int, [_vp, _sz, _sz, _sz, _vp, _vp]),
+    "gsvk_convt1d_pack_weight": (c_int, [_vp, _sz, _sz, _sz, _vp, _vp]),
+    "gsvk_conv1d_f16": (c_int, [_vp, _vp]),
+    "gsvk_convt1d_f16": (c_int, [_vp, _vp]),
+    "gsvk_channels_to_rows_f16": (c_int, [_vp, _sz, _sz, _vp, _vp]),
+    "gsvk_rows_to_channels_f32": (c_int, [_vp, _sz, _sz, _vp, _vp]),
+    "gsvk_decoder_out_len": (_sz, [_vp, _sz]),
+    "gsvk_decoder_create": (c_int, [_vp, _vp, _vp, _vp]),
+    "gsvk_decoder_destroy": (c_int, [_vp]),
+    "gsvk_decoder_forward": (c_int, [_vp, _vp, _sz, _vp, _vp]),
+    "gsvk_decoder_launches": (c_int, [_vp]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -357,3 +368,122 @@ class T2S:
         out = np.zeros(self.model["vocab"], np.float32)
         check(lib().gsvk_t2s_read_logits(self.h, out.ctypes.data))
         return out
+
+
+# ---------------------------------------------------------- a12 - a15: SoVITS
+class ConvArgs(ctypes.Structure):
+    _fields_ = [("x", _vp), ("T", _sz), ("ci", _sz), ("w", _vp), ("co", _sz), ("k", _sz),
+                ("dil", _sz), ("bias", _vp), ("residual", _vp), ("res_scale", c_float),
+                ("act", c_int), ("slope", c_float), ("y", _vp), ("y_f16", _vp),
+                ("y_f16_act", _vp), ("act2", c_int), ("slope2", c_float)]
+
+
+def pack_conv_weight(w_torch, transpose=False, stream=None):
+    """fp16 torch-layout weight (CUDA) -> packed [k][co][ci]."""
+    import torch
+
+    if transpose:
+        ci, co, k = w_torch.shape
+    else:
+        co, ci, k = w_torch.shape
+    out = torch.empty(k, co, ci, dtype=torch.float16, device=w_torch.device)
+    fn = lib().gsvk_convt1d_pack_weight if transpose else lib().gsvk_conv1d_pack_weight
+    a, b = (ci, co) if transpose else (co, ci)
+    check(fn(_ptr(w_torch), a, b, k, _ptr(out), _stream(stream)))
+    return out
+
+
+def conv1d(x16, wp, bias=None, dil=1, transpose=False, residual=None, res_scale=1.0,
+           act=ACT_NONE, slope=0.0, y=None, y_f16=None, y_f16_act=None, act2=ACT_NONE,
+           slope2=0.0, stream=None):
+    """Channels-last conv (x16 [T, ci] fp16, wp packed [k, co, ci]); transpose=True
+    runs ConvTranspose1d with stride `dil`."""
+    import torch
+
+    T, ci = x16.shape
+    k, co, ci2 = wp.shape
+    assert ci == ci2
+    t_out = T * dil if transpose else T
+    if y is None and y_f16 is None and y_f16_act is None:
+        y = torch.empty(t_out, co, device=x16.device)
+    a = ConvArgs(_ptr(x16), T, ci, _ptr(wp), co, k, dil, _ptr(bias), _ptr(residual), res_scale,
+                 act, slope, _ptr(y), _ptr(y_f16), _ptr(y_f16_act), act2, slope2)
+    fn = lib().gsvk_convt1d_f16 if transpose else lib().gsvk_conv1d_f16
+    check(fn(ctypes.byref(a), _stream(stream)))
+    return y
+
+
+def channels_to_rows_f16(x, stream=None):
+    import torch
+
+    C, T = x.shape
+    y = torch.empty(T, C, dtype=torch.float16, device=x.device)
+    check(lib().gsvk_channels_to_rows_f16(_ptr(x), C, T, _ptr(y), _stream(stream)))
+    return y
+
+
+def rows_to_channels_f32(x, stream=None):
+    import torch
+
+    T, C = x.shape
+    y = torch.empty(C, T, device=x.device)
+    check(lib().gsvk_rows_to_channels_f32(_ptr(x), T, C, _ptr(y), _stream(stream)))
+    return y
+
+
+class DecoderConfig(ctypes.Structure):
+    _fields_ = [("n_stages", c_int), ("in_ch", c_int), ("ch0", c_int), ("conv_pre_k", c_int),
+                ("conv_post_k", c_int), ("up_rate", c_int * 8), ("up_k", c_int * 8),
+                ("res_k", c_int * 3), ("res_dil", c_int * 3), ("lrelu_slope", c_float),
+                ("post_slope", c_float), ("max_frames", c_int)]
+
+
+class Decoder:
+    """Device HiFi-GAN generator (sovits::Generator).  ws/bs: host numpy weights
+    in the documented order (workloads.decoder_weights)."""
+
+    def __init__(self, cfg: dict, ws, bs, max_frames: int):
+        import numpy as np
+
+        c = DecoderConfig()
+        c.n_stages, c.in_ch, c.ch0 = cfg["n_stages"], cfg["in_ch"], cfg["ch0"]
+        c.conv_pre_k, c.conv_post_k = cfg["conv_pre_k"], cfg["conv_post_k"]
+        for i in range(cfg["n_stages"]):
+            c.up_rate[i], c.up_k[i] = cfg["up_rate"][i], cfg["up_k"][i]
+        for i in range(3):
+            c.res_k[i], c.res_dil[i] = cfg["res_k"][i], cfg["res_dil"][i]
+        c.lrelu_slope, c.post_slope, c.max_frames = cfg["lrelu_slope"], cfg["post_slope"], max_frames
+        self.cfg = c
+        self._ws = [np.ascontiguousarray(w) for w in ws]
+        self._bs = [None if b is None else np.ascontiguousarray(b, np.float32) for b in bs]
+        wp = (c_void_p * len(ws))(*[w.ctypes.data for w in self._ws])
+        bp = (c_void_p * len(bs))(*[None if b is None else b.ctypes.data for b in self._bs])
+        h = c_void_p()
+        check(lib().gsvk_decoder_create(ctypes.byref(c), wp, bp, ctypes.byref(h)))
+        self.h = h
+
+    def out_len(self, T: int) -> int:
+        return lib().gsvk_decoder_out_len(ctypes.byref(self.cfg), T)
+
+    def forward(self, z, wav=None, stream=None):
+        """z: CUDA fp32 [in_ch, T] -> wav CUDA fp32 [T * prod(up_rate)]."""
+        import torch
+
+        T = z.shape[1]
+        wav = wav if wav is not None else torch.empty(self.out_len(T), device=z.device)
+        check(lib().gsvk_decoder_forward(self.h, _ptr(z), T, _ptr(wav), _stream(stream)))
+        return wav
+
+    def launches(self) -> int:
+        return lib().gsvk_decoder_launches(self.h)
+
+    def close(self):
+        if self.h:
+            lib().gsvk_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

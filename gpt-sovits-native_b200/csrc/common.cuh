@@ -68,12 +68,13 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Epilogue activation (GSVK_ACT_*), identical expressions to the reference:
-// relu kern.cpp:85, gelu_erf bert_ops.hpp:25, leaky nn_ops.hpp:48.
+// relu kern.cpp:85, gelu_erf bert_ops.hpp:25, leaky nn_ops.hpp:48, tanh dec.hpp:344.
 __device__ __forceinline__ float apply_act(float v, int act, float slope) {
   switch (act) {
     case GSVK_ACT_RELU: return v > 0.f ? v : 0.f;
     case GSVK_ACT_GELU_ERF: return 0.5f * v * (1.f + erff(v * 0.70710678118654752440f));
     case GSVK_ACT_LEAKY: return v < 0.f ? v * slope : v;
+    case GSVK_ACT_TANH: return tanhf(v);
     default: return v;
   }
 }

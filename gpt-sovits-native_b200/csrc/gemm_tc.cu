@@ -412,7 +412,7 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   if (g->M > 0x7fffffff || g->N > 0x7fffffff || g->K > 0x7fffffff)
     return fail(GSVK_ERR_UNSUPPORTED, "gemm: size > 2^31");
   if (g->lda < g->K || g->ldb < g->K) return fail(GSVK_ERR_INVALID, "gemm: lda/ldb < K");
-  if (g->act < GSVK_ACT_NONE || g->act > GSVK_ACT_LEAKY) return fail(GSVK_ERR_INVALID, "bad act");
+  if (g->act < GSVK_ACT_NONE || g->act > GSVK_ACT_TANH) return fail(GSVK_ERR_INVALID, "bad act");
   TcEpilogue e = make_epilogue();
   e.bias = g->bias;
   e.residual = g->residual;

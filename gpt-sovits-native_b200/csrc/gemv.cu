@@ -207,7 +207,7 @@ int gsvk_gemv_f16x_fmlal(const uint16_t* w, const uint16_t* xh, float* y, size_t
 int gsvk_gemv_ex(const uint16_t* w, const void* x, int x_is_f16, float* y, uint16_t* y_f16,
                  size_t out, size_t in, const float* bias, const float* residual, int act,
                  float slope, gsvk_stream_t stream) {
-  if (act < GSVK_ACT_NONE || act > GSVK_ACT_LEAKY) return fail(GSVK_ERR_INVALID, "gemv: bad act");
+  if (act < GSVK_ACT_NONE || act > GSVK_ACT_TANH) return fail(GSVK_ERR_INVALID, "gemv: bad act");
   return gemv_ex(w, x, x_is_f16, y, y_f16, out, in, bias, residual, act, slope, as_cuda(stream));
 }
 

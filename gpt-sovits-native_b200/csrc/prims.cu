@@ -126,7 +126,7 @@ int gsvk_softmax_rows(const float* x, float* y, size_t rows, size_t n, gsvk_stre
 int gsvk_activation(const float* x, float* y, size_t n, int act, float slope,
                     gsvk_stream_t stream) {
   if (!x || !y) return fail(GSVK_ERR_INVALID, "activation: null pointer");
-  if (act < GSVK_ACT_NONE || act > GSVK_ACT_LEAKY) return fail(GSVK_ERR_INVALID, "bad act");
+  if (act < GSVK_ACT_NONE || act > GSVK_ACT_TANH) return fail(GSVK_ERR_INVALID, "bad act");
   if (n == 0) return GSVK_OK;
   const size_t cap = static_cast<size_t>(sm_count()) * 8;
   size_t g = (n + 255) / 256;

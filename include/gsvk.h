@@ -45,7 +45,8 @@ enum {
   GSVK_ACT_NONE = 0,
   GSVK_ACT_RELU = 1,     /* kern.cpp:85 relu */
   GSVK_ACT_GELU_ERF = 2, /* bert_ops.hpp:25 gelu_erf */
-  GSVK_ACT_LEAKY = 3     /* nn_ops.hpp:48 leaky_relu(slope) */
+  GSVK_ACT_LEAKY = 3,    /* nn_ops.hpp:48 leaky_relu(slope) */
+  GSVK_ACT_TANH = 4      /* dec.hpp:344 output tanh */
 };
 
 /* ---- library ---------------------------------------------------------- */
@@ -110,6 +111,68 @@ typedef struct {
   float alpha;                       /* 0 is read as 1 */
 } gsvk_gemm_args;
 int gsvk_gemm_f16_ex(const gsvk_gemm_args* args, gsvk_stream_t stream);
+
+/* ---- SoVITS convolutions (a12-a14) -------------------------------------- */
+/* Activations are channels-last rows: x[T][ci] fp16 (the transpose of the
+ * reference's channel-major Tensor2D, sovits_types.hpp), ci a multiple of 8.
+ * Weights are packed once to tap-major [k][co][ci] fp16 by the pack entry
+ * points below (the reference's ConvT phase layout, conv1d.hpp:226-232).
+ * The epilogue writes y = act(conv + bias) + res_scale * residual as fp32
+ * (y), fp16 (y_f16) and/or fp16 of act2(y) (y_f16_act), all [T_out][co]. */
+typedef struct {
+  const uint16_t* x; size_t T; size_t ci;
+  const uint16_t* w; size_t co; size_t k;
+  size_t dil;              /* conv1d: dilation (1 = plain); convt1d: stride u */
+  const float* bias;       /* [co] or NULL */
+  const float* residual;   /* fp32 [T_out][co] or NULL (may alias y) */
+  float res_scale;
+  int act; float slope;
+  float* y; uint16_t* y_f16; uint16_t* y_f16_act;
+  int act2; float slope2;
+} gsvk_conv_args;
+/* torch Conv1d weight [co][ci][k] -> packed [k][co][ci] (DEVICE buffers). */
+int gsvk_conv1d_pack_weight(const uint16_t* w_torch, size_t co, size_t ci, size_t k,
+                            uint16_t* packed, gsvk_stream_t stream);
+/* torch ConvTranspose1d weight [ci][co][k] -> packed [k][co][ci]. */
+int gsvk_convt1d_pack_weight(const uint16_t* w_torch, size_t ci, size_t co, size_t k,
+                             uint16_t* packed, gsvk_stream_t stream);
+/* sovits::Conv1d::forward (conv1d.hpp:109-194): same padding (k-1)*dil/2,
+ * implicit GEMM on the tensor cores (no im2col buffer); T_out = T. */
+int gsvk_conv1d_f16(const gsvk_conv_args* args, gsvk_stream_t stream);
+/* sovits::ConvT1d::forward (conv1d.hpp:250-359): ConvTranspose1d(k, stride u,
+ * pad (k-u)/2), polyphase implicit GEMM writing every output phase directly;
+ * T_out = T * u.  Requires k >= u and k - u even. */
+int gsvk_convt1d_f16(const gsvk_conv_args* args, gsvk_stream_t stream);
+/* Layout helpers: channel-major fp32 [C][T] <-> channels-last rows. */
+int gsvk_channels_to_rows_f16(const float* x, size_t C, size_t T, uint16_t* y,
+                              gsvk_stream_t stream);
+int gsvk_rows_to_channels_f32(const float* x, size_t T, size_t C, float* y, gsvk_stream_t stream);
+
+/* ---- SoVITS HiFi-GAN generator (a15) ------------------------------------ */
+/* sovits::Generator::forward (dec.hpp:265-345) without the cond(ge) term:
+ * conv_pre -> n_stages x [lrelu -> ConvT -> mean of 3 ResBlock1] -> lrelu
+ * (post_slope) -> conv_post -> tanh.  Weights (HOST, torch layouts, fp16)
+ * in the order: [0] conv_pre; per stage s: [1+19s] ups[s], then resblock j
+ * pair p: [1+19s+1+6j+2p] convs1[p], [+1] convs2[p]; [1+19*n_stages]
+ * conv_post.  Biases fp32 (NULL allowed).  max_frames bounds T. */
+typedef struct gsvk_decoder* gsvk_decoder_t;
+typedef struct {
+  int n_stages, in_ch, ch0, conv_pre_k, conv_post_k;
+  int up_rate[8], up_k[8];
+  int res_k[3], res_dil[3];
+  float lrelu_slope, post_slope;
+  int max_frames;
+} gsvk_decoder_config;
+size_t gsvk_decoder_out_len(const gsvk_decoder_config* cfg, size_t T);
+int gsvk_decoder_create(const gsvk_decoder_config* cfg, const uint16_t* const* w_host,
+                        const float* const* b_host, gsvk_decoder_t* out);
+int gsvk_decoder_destroy(gsvk_decoder_t h);
+/* z: DEVICE fp32 [in_ch][T] (channel-major, the reference layout);
+ * wav: DEVICE fp32 [T * prod(up_rate)]. */
+int gsvk_decoder_forward(gsvk_decoder_t h, const float* z, size_t T, float* wav,
+                         gsvk_stream_t stream);
+/* Kernel launches issued by the last gsvk_decoder_forward. */
+int gsvk_decoder_launches(gsvk_decoder_t h);
 
 /* ---- support primitives (a22) ------------------------------------------ */
 /* kern::layernorm (kern.cpp:27) applied to `rows` rows of n. y may equal x. */

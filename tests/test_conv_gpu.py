@@ -1,0 +1,116 @@
+"""GPU parity of the SoVITS convolutions (a12-a14) and generator (a15).
+
+Per layer the device and the oracle see the same fp16 inputs and weights; the
+tensor-core accumulation order is the only difference, so the bar is the
+reference's own AMX-versus-FMLAL gate (test_kern.cpp:282-320):
+cos >= 0.9999 and max|d| / max|ref| <= 1e-3.  Through the whole generator the
+per-layer fp16 roundings of activations can flip where the fp32 sums differ
+in the last bit; the end-to-end bar is the north-star 1e-2 relative error.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def f16(a):
+    return np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
+
+
+def to_dev16(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.float16)).cuda()
+
+
+def gate(got, ref, rel=1e-3, min_cos=0.9999):
+    got = np.asarray(got, np.float64).ravel()
+    ref = np.asarray(ref, np.float64).ravel()
+    d = np.abs(got - ref).max() / np.abs(ref).max()
+    c = got @ ref / np.sqrt((got @ got) * (ref @ ref))
+    assert d <= rel and c >= min_cos, f"max rel {d:.3e}, cos {c:.8f}"
+
+
+CONV_CASES = [(192, 512, 37, 7, 1), (256, 256, 100, 3, 5), (128, 128, 150, 11, 3),
+              (16, 16, 500, 7, 5), (32, 32, 300, 11, 1), (16, 1, 200, 7, 1), (64, 48, 129, 3, 1),
+              (24, 24, 64, 3, 3)]
+
+
+@pytest.mark.parametrize("Ci,Co,T,k,dil", CONV_CASES)
+def test_conv1d_matches_oracle(dev, ora, Ci, Co, T, k, dil):
+    rng = np.random.default_rng(Ci * 7 + Co + T)
+    x = rng.standard_normal((Ci, T)).astype(np.float32)
+    w = f16(rng.standard_normal((Co, Ci, k)) * 0.05)
+    b = (rng.standard_normal(Co) * 0.1).astype(np.float32)
+    ref = ora.conv1d(x, w, b, dil, round_in=True)  # [Co, T]
+    wp = dev.pack_conv_weight(to_dev16(w))
+    y = dev.conv1d(to_dev16(f16(x.T)), wp, torch.from_numpy(b).cuda(), dil=dil)
+    gate(y.cpu().numpy().T, ref)
+    assert dev.device_status() == 0
+
+
+CONVT_CASES = [(512, 256, 13, 16, 10), (256, 128, 40, 16, 8), (128, 64, 100, 8, 2),
+               (64, 32, 200, 2, 2), (32, 16, 300, 2, 2), (768, 384, 7, 20, 10), (16, 8, 33, 4, 2)]
+
+
+@pytest.mark.parametrize("Ci,Co,T,k,u", CONVT_CASES)
+def test_convt1d_matches_oracle(dev, ora, Ci, Co, T, k, u):
+    rng = np.random.default_rng(Ci + 3 * Co + T + k)
+    x = rng.standard_normal((Ci, T)).astype(np.float32)
+    w = f16(rng.standard_normal((Ci, Co, k)) * 0.05)
+    b = (rng.standard_normal(Co) * 0.1).astype(np.float32)
+    ref = ora.convt1d(x, w, b, u, round_in=True)  # [Co, T*u]
+    wp = dev.pack_conv_weight(to_dev16(w), transpose=True)
+    y = dev.conv1d(to_dev16(f16(x.T)), wp, torch.from_numpy(b).cuda(), dil=u, transpose=True)
+    assert y.shape == (T * u, Co)
+    gate(y.cpu().numpy().T, ref)
+
+
+def test_conv_fused_epilogue_residual_and_second_output(dev, ora):
+    """The resblock c2 step: cur = cur + conv(t) + b, and lrelu(cur) in fp16."""
+    rng = np.random.default_rng(11)
+    C, T, k = 64, 257, 7
+    t = rng.standard_normal((C, T)).astype(np.float32)
+    cur = rng.standard_normal((T, C)).astype(np.float32)
+    w = f16(rng.standard_normal((C, C, k)) * 0.05)
+    b = (rng.standard_normal(C) * 0.1).astype(np.float32)
+    ref = cur + ora.conv1d(t, w, b, 1, round_in=True).T
+    wp = dev.pack_conv_weight(to_dev16(w))
+    cur_d = torch.from_numpy(cur).cuda()
+    act16 = torch.empty(T, C, dtype=torch.float16, device="cuda")
+    dev.conv1d(to_dev16(f16(t.T)), wp, torch.from_numpy(b).cuda(), residual=cur_d, y=cur_d,
+               y_f16_act=act16, act2=dev.ACT_LEAKY, slope2=0.1)
+    got = cur_d.cpu().numpy()
+    gate(got, ref)
+    np.testing.assert_array_equal(act16.cpu().numpy(),
+                                  ora.leaky_relu(got, 0.1).astype(np.float16))
+
+
+def test_conv_rejects_unaligned_channels(dev):
+    x = torch.zeros(10, 12, dtype=torch.float16, device="cuda")
+    wp = torch.zeros(3, 8, 12, dtype=torch.float16, device="cuda")
+    with pytest.raises(dev.GsvkError) as ei:
+        dev.conv1d(x, wp)
+    assert ei.value.code == -2
+
+
+def test_layout_round_trip(dev, ora):
+    x = np.random.default_rng(2).standard_normal((37, 1001)).astype(np.float32)
+    rows = dev.channels_to_rows_f16(torch.from_numpy(x).cuda())
+    np.testing.assert_array_equal(rows.cpu().numpy().view(np.uint16), ora.f32_to_f16(x.T.copy()))
+    back = dev.rows_to_channels_f32(rows.float())
+    np.testing.assert_array_equal(back.cpu().numpy(), ora.f16_to_f32(ora.f32_to_f16(x)))
+
+
+@pytest.mark.parametrize("which,T", [("config5", 12), ("reference_v2", 6)])
+def test_decoder_matches_oracle(dev, ora, which, T):
+    W = dev.workloads
+    cfg = W.DECODER if which == "config5" else W.DECODER_REF
+    ws, bs = W.decoder_weights(cfg, seed=3)  # N(0, 0.01), the configs' distribution
+    z = W.decoder_latent(T, cfg, seed=1)
+    ref = ora.decoder_forward(ora.decoder_cfg(**cfg), ws, bs, z, round_in=True)
+    dec = dev.Decoder(cfg, ws, bs, max_frames=T)
+    wav = dec.forward(torch.from_numpy(z).cuda()).cpu().numpy()
+    dec.close()
+    assert wav.shape == ref.shape
+    gate(wav, ref, rel=1e-2, min_cos=0.999)
+    assert dev.device_status() == 0
