@@ -334,7 +334,75 @@ def run_gemm1(args, rank, local, world):
     return line
 
 
-WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1}
+# ------------------------------------------------------- SoVITS decoder (5)
+def run_decoder(args, rank, local, world):
+    import numpy as np
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    cfg = g.workloads.DECODER
+    T = 500
+    ws, bs = g.workloads.decoder_weights(cfg, seed=0)
+    z = g.workloads.decoder_latent(T, cfg, seed=rank)  # one utterance per GPU
+    dec = g.Decoder(cfg, ws, bs, max_frames=T)
+    zd = torch.from_numpy(z).to(dev)
+    wav = torch.empty(dec.out_len(T), device=dev)
+    for _ in range(args.warmup):
+        dec.forward(zd, wav)
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler()
+    barrier(world)
+    clocks.start()
+    start.record(stream)
+    for _ in range(args.steps):
+        dec.forward(zd, wav)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    t = max_over_ranks(start.elapsed_time(end) * 1e-3 / args.steps, world)
+    # e2e: host latent in, host waveform out
+    z_pin = torch.from_numpy(z).pin_memory()
+    w_pin = torch.empty(wav.numel(), pin_memory=True)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        zd.copy_(z_pin, non_blocking=True)
+        dec.forward(zd, wav)
+        w_pin.copy_(wav, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e-3 / args.steps, world)
+    flops = 2 * g.workloads.decoder_macs(cfg, T)
+    launches = dec.launches()
+    dec.close()
+    _, tf, kind = measured_peaks()
+    line = {"metric": "SoVITS decoder TFLOP/s (192x500 latent -> 320,000 samples per utterance)",
+            "value": flops * world / t / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 activations/weights, f32 accumulate and residual",
+            "data": "synthetic (N(0,0.01) weights, N(0,1) latent)",
+            "config": {"workload": "sovits_decoder (BASELINE configs[4])", "frames": T,
+                       "samples": int(wav.numel()), "global_batch": world,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "activations 20-40 MB per layer at the late stages, > L2 per step"},
+            "e2e": {"value": flops * world / t_e2e / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": z.nbytes, "d2h_bytes_per_step": int(wav.numel()) * 4},
+            "gpu_launches": launches * args.steps,
+            "roofline": {"bound": "tensor", "achieved": flops / t / 1e12, "peak": tf,
+                         "unit": "TFLOP/s", "frac": flops / t / 1e12 / tf, "peak_source": kind,
+                         "traffic": None, "note": "whole generator; late stages are HBM-bound"}}
+    if clk:
+        line["clocks"] = clk
+    return line
+
+
+WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder": run_decoder}
 
 
 def run_reference(args, rank, world):
