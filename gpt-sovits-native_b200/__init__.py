@@ -76,6 +76,8 @@ SIGNATURES = {
     "gsvk_decoder_destroy": (c_int, [_vp]),
     "gsvk_decoder_forward": (c_int, [_vp, _vp, _sz, _vp, _vp]),
     "gsvk_decoder_launches": (c_int, [_vp]),
+    "gsvk_sgemm": (c_int, [c_char, c_char, c_int, c_int, c_int, c_float, _vp, c_int, _vp, c_int,
+                           c_float, _vp, c_int, _vp]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -233,6 +235,15 @@ def attention_decode(q, kcache, vcache, length: int, n_heads: int, head_dim: int
                                       head_dim, kcache.stride(0), scale, _ptr(out),
                                       _ptr(workspace), _stream(stream)))
     return out
+
+
+# ---------------------------------------------------------------------- a5
+def sgemm(ta: str, tb: str, M: int, N: int, K: int, alpha: float, A, lda: int, B, ldb: int,
+          beta: float, C, ldc: int, stream=None):
+    """accel::sgemm on device fp32 buffers (row-major, cblas semantics)."""
+    check(lib().gsvk_sgemm(ta.encode(), tb.encode(), M, N, K, alpha, _ptr(A), lda, _ptr(B), ldb,
+                           beta, _ptr(C), ldc, _stream(stream)))
+    return C
 
 
 # --------------------------------------------------------------------- a22

@@ -112,6 +112,13 @@ typedef struct {
 } gsvk_gemm_args;
 int gsvk_gemm_f16_ex(const gsvk_gemm_args* args, gsvk_stream_t stream);
 
+/* ---- fp32 GEMM (a5) ------------------------------------------------------ */
+/* accel::sgemm (accel.hpp:27): row-major C = alpha op(A) op(B) + beta C with
+ * transa/transb 'N' or 'T'; beta == 0 never reads C.  fp32 on CUDA cores. */
+int gsvk_sgemm(char transa, char transb, int M, int N, int K, float alpha, const float* A,
+               int lda, const float* B, int ldb, float beta, float* C, int ldc,
+               gsvk_stream_t stream);
+
 /* ---- SoVITS convolutions (a12-a14) -------------------------------------- */
 /* Activations are channels-last rows: x[T][ci] fp16 (the transpose of the
  * reference's channel-major Tensor2D, sovits_types.hpp), ci a multiple of 8.

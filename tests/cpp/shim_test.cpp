@@ -1,0 +1,103 @@
+// C++ drop-in check: the reference's test_accel.cpp cases restated over the
+// gsv::kern::cuda shim (device buffers), built against libgsvk.so.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "gsv_kern_cuda.hpp"
+
+namespace gk = gsv::kern::cuda;
+
+static unsigned long long g_s = 0x9e3779b97f4a7c15ull;
+static float rnd() {  // xorshift in [-1, 1) (test_kern.cpp:83-92 generator)
+  g_s ^= g_s << 13;
+  g_s ^= g_s >> 7;
+  g_s ^= g_s << 17;
+  return static_cast<float>(static_cast<long long>(g_s >> 40) / static_cast<double>(1ull << 23)) - 1.f;
+}
+
+template <class T>
+static T* dev(const std::vector<T>& h) {
+  T* d = nullptr;
+  cudaMalloc(&d, h.size() * sizeof(T));
+  cudaMemcpy(d, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice);
+  return d;
+}
+template <class T>
+static std::vector<T> host(const T* d, size_t n) {
+  std::vector<T> h(n);
+  cudaMemcpy(h.data(), d, n * sizeof(T), cudaMemcpyDeviceToHost);
+  return h;
+}
+
+int main() {
+  gk::init(0);
+  int fails = 0;
+  // sgemm_matches_naive_loop (test_accel.cpp:102-133)
+  {
+    const int M = 5, N = 7, K = 3;
+    std::vector<float> A(M * K), B(K * N), C(M * N, std::nanf(""));
+    for (auto& v : A) v = rnd();
+    for (auto& v : B) v = rnd();
+    float *dA = dev(A), *dB = dev(B), *dC = dev(C);
+    gk::accel::sgemm('N', 'N', M, N, K, 1.f, dA, K, dB, N, 0.f, dC, N);
+    auto got = host(dC, M * N);
+    for (int i = 0; i < M; ++i)
+      for (int j = 0; j < N; ++j) {
+        double acc = 0;
+        for (int k = 0; k < K; ++k) acc += A[i * K + k] * B[k * N + j];
+        if (std::fabs(got[i * N + j] - acc) > 1e-5) ++fails;
+      }
+    std::vector<float> P(K * M), Q(N * K), C2(M * N, 0.5f);
+    for (auto& v : P) v = rnd();
+    for (auto& v : Q) v = rnd();
+    float *dP = dev(P), *dQ = dev(Q), *dC2 = dev(C2);
+    gk::accel::sgemm('T', 'T', M, N, K, 2.f, dP, M, dQ, K, 1.f, dC2, N);
+    got = host(dC2, M * N);
+    for (int i = 0; i < M; ++i)
+      for (int j = 0; j < N; ++j) {
+        double acc = 0;
+        for (int k = 0; k < K; ++k) acc += P[k * M + i] * Q[j * K + k];
+        if (std::fabs(got[i * N + j] - (2.0 * acc + 0.5)) > 1e-5) ++fails;
+      }
+  }
+  // DenseF16 view rows == GEMV rows on fp16 activations (test_accel.cpp:135-158)
+  {
+    const size_t out = 128, in = 96, T = 17;
+    std::vector<uint16_t> w(out * in), xh(T * in);
+    for (auto& v : w) {
+      const _Float16 h = static_cast<_Float16>(rnd() * 0.05f);
+      std::memcpy(&v, &h, 2);
+    }
+    std::vector<float> x(T * in);
+    for (auto& v : x) v = rnd();
+    uint16_t* dw = dev(w);
+    float* dx = dev(x);
+    uint16_t* dxh = dev(xh);
+    float* dy = dev(std::vector<float>(T * out));
+    float* dyr = dev(std::vector<float>(out));
+    gk::accel::DenseF16 d = gk::accel::DenseF16::view_f16(dw, out, in);
+    d.forward(dx, T, dy, dxh);
+    auto y = host(dy, T * out);
+    for (size_t t = 0; t < T; ++t) {
+      gk::gemv_f16x_fmlal(dw, dxh + t * in, dyr, out, in);
+      auto yr = host(dyr, out);
+      float peak = 0;
+      for (float v : yr) peak = std::fmax(peak, std::fabs(v));
+      for (size_t o = 0; o < out; ++o)
+        if (std::fabs(y[t * out + o] - yr[o]) > 1e-5f * peak) ++fails;
+    }
+  }
+  // error path: a bad transpose flag throws
+  try {
+    gk::accel::sgemm('X', 'N', 1, 1, 1, 1.f, nullptr, 1, nullptr, 1, 0.f, nullptr, 1);
+    ++fails;
+  } catch (const std::runtime_error&) {
+  }
+  cudaDeviceSynchronize();
+  std::printf("shim_test: %s (%d failures)\n", fails ? "FAIL" : "PASS", fails);
+  return fails ? 1 : 0;
+}

@@ -118,3 +118,37 @@ def test_gemm_encoder_shapes_vs_torch_fp32(dev, name):
     cos = torch.nn.functional.cosine_similarity(got.flatten().double(), ref.flatten().double(), dim=0)
     assert d <= 1e-3 and cos.item() >= 0.9999
     assert dev.device_status() == 0
+
+
+# ------------------------------------------------------------------ a5 sgemm
+def test_sgemm_matches_naive_loop(dev, ora):
+    """test_accel.cpp:102-133: NN with NaN in C (beta = 0 must not read it) and TT
+    with alpha = 2, beta = 1; |d| <= 1e-5."""
+    rng = np.random.default_rng(7)
+    M, N, K = 5, 7, 3
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    C = torch.full((M, N), float("nan"), device="cuda")
+    dev.sgemm("N", "N", M, N, K, 1.0, f(A), K, f(B), N, 0.0, C, N)
+    np.testing.assert_allclose(C.cpu().numpy(), A.astype(np.float64) @ B, atol=1e-5)
+    P = rng.uniform(-1, 1, (K, M)).astype(np.float32)
+    Q = rng.uniform(-1, 1, (N, K)).astype(np.float32)
+    C = torch.full((M, N), 0.5, device="cuda")
+    dev.sgemm("T", "T", M, N, K, 2.0, f(P), M, f(Q), K, 1.0, C, N)
+    np.testing.assert_allclose(C.cpu().numpy(), 2.0 * (P.T.astype(np.float64) @ Q.T) + 0.5,
+                               atol=1e-5)
+
+
+@pytest.mark.parametrize("ta,tb,M,N,K", [("N", "T", 17, 128, 96), ("N", "N", 300, 129, 257),
+                                         ("T", "N", 64, 65, 1000), ("T", "T", 1, 1025, 512)])
+def test_sgemm_against_oracle(dev, ora, ta, tb, M, N, K):
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((K, M) if ta == "T" else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb == "T" else (K, N)).astype(np.float32)
+    lda, ldb = A.shape[1], B.shape[1]
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    ref = C0.copy()
+    ora.sgemm(ta, tb, M, N, K, 0.5, A, lda, B, ldb, 2.0, ref, N)
+    C = f(C0)
+    dev.sgemm(ta, tb, M, N, K, 0.5, f(A), lda, f(B), ldb, 2.0, C, N)
+    np.testing.assert_allclose(C.cpu().numpy(), ref, atol=1e-4, rtol=1e-5)
