@@ -31,6 +31,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 T2S_STEPS = 500
+# DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one decode
+# launch divided by its algorithmic bytes, measured on a 20-step launch of the
+# same kernel; traffic grows in proportion to the decode passes.
+T2S_TRAFFIC_RATIO = 0.986
 T2S_PREFIX = 256
 T2S_PROMPT = 64
 L2_BYTES = 126 * 1024 * 1024
@@ -274,7 +278,8 @@ def run_t2s(args, rank, local, world):
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "kernel": "t2s_decode_kernel", "achieved": achieved,
                      "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_source": peak_kind, "traffic": None,
+                     "peak_source": peak_kind, "traffic": T2S_TRAFFIC_RATIO * alg,
+                     "traffic_note": "ncu DRAM bytes of a 20-step launch, scaled per pass",
                      "algorithmic_bytes_per_launch": alg,
                      "launch_ms": t_dec_max * 1e3},
     }
