@@ -78,6 +78,10 @@ SIGNATURES = {
     "gsvk_decoder_launches": (c_int, [_vp]),
     "gsvk_sgemm": (c_int, [c_char, c_char, c_int, c_int, c_int, c_float, _vp, c_int, _vp, c_int,
                            c_float, _vp, c_int, _vp]),
+    "gsvk_encoder_create": (c_int, [_vp, _vp, _vp]),
+    "gsvk_encoder_destroy": (c_int, [_vp]),
+    "gsvk_encoder_forward": (c_int, [_vp, _vp, _sz, _sz, _vp, _vp]),
+    "gsvk_encoder_launches": (c_int, [_vp]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -491,6 +495,54 @@ class Decoder:
     def close(self):
         if self.h:
             lib().gsvk_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------ a20, a21: encoders
+class EncoderConfig(ctypes.Structure):
+    _fields_ = [("layers", c_int), ("hidden", c_int), ("heads", c_int), ("ffn", c_int),
+                ("eps", c_double), ("max_batch", c_int), ("max_seq", c_int)]
+
+
+class EncoderHostWeights(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("wqkv", "bqkv", "wo", "bo", "ln1g", "ln1b", "wi", "bi", "wf",
+                                   "bf", "ln2g", "ln2b")]
+
+
+class Encoder:
+    """Device encoder stack (BERT / HuBERT); model from workloads.encoder_model."""
+
+    NAMES = ("wqkv", "bqkv", "wo", "bo", "ln1g", "ln1b", "wi", "bi", "wf", "bf", "ln2g", "ln2b")
+
+    def __init__(self, model: dict, max_batch: int, max_seq: int):
+        import numpy as np
+
+        self._keep = {n: np.ascontiguousarray(model[n]) for n in self.NAMES}
+        cfg = EncoderConfig(model["layers"], model["hidden"], model["heads"], model["ffn"],
+                            model["eps"], max_batch, max_seq)
+        w = EncoderHostWeights(*[self._keep[n].ctypes.data for n in self.NAMES])
+        h = c_void_p()
+        check(lib().gsvk_encoder_create(ctypes.byref(cfg), ctypes.byref(w), ctypes.byref(h)))
+        self.h = h
+
+    def forward(self, x, batch: int, seq: int, valid=None, stream=None):
+        """x: CUDA fp32 [batch*seq, hidden], updated in place."""
+        check(lib().gsvk_encoder_forward(self.h, _ptr(x), batch, seq, _ptr(valid),
+                                         _stream(stream)))
+        return x
+
+    def launches(self) -> int:
+        return lib().gsvk_encoder_launches(self.h)
+
+    def close(self):
+        if self.h:
+            lib().gsvk_encoder_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -1,0 +1,365 @@
+// encoder.cu — post-LN transformer encoder stack: RoBERTa-large (BertLayer,
+// bert_ops.hpp:347-400) and HuBERT-base (hubert.cpp:590-730) share it.
+//
+// Per layer, all products on the tensor-core kernel (gemm_tc.cuh):
+//   qkv16 = f16(x) . Wqkv^T + b                   (q, k, v Linear fused, fp16 out)
+//   S     = (Q_h K_h^T) * 1/sqrt(dh)              (batched over utterance x head)
+//   P     = softmax(S + key mask) -> fp16         (bert_ops.hpp:28-43, :373-374)
+//   ctx16 = P . V_h                               (batched; V_h^T packed per head)
+//   y     = ctx16 . Wo^T + b + x ; x1 = LN(y)     (residual fused in the epilogue)
+//   mid16 = GELU(x1 . Wi^T + b)                   (GELU fused)
+//   f     = mid16 . Wf^T + b + x1 ; x = LN(f)
+// The reference runs q/k/v and the attention products in fp32 (sgemm); here
+// they are fp16 operands with fp32 accumulation, checked against the oracle
+// at the encoder tolerance.
+#include <cmath>
+#include <vector>
+
+#include "gsvk_internal.hpp"
+
+struct gsvk_encoder;
+
+namespace gsvk {
+
+namespace {
+
+// Row softmax of S (fp32, ld) with keys >= valid masked by finfo.min, written
+// as fp16 P (ld) with the padding columns [T, ldp) zeroed.  One warp per row.
+__global__ void enc_softmax_kernel(const float* __restrict__ S, int ld, int rows, int T, int H,
+                                   const int* __restrict__ valid, uint16_t* __restrict__ P) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int b = row / (H * T);
+  const int nv = valid ? valid[b] : T;
+  const float* s = S + static_cast<size_t>(row) * ld;
+  float v[8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int j = lane + 32 * u;
+    float x = -INFINITY;
+    if (j < T) {
+      x = s[j];
+      if (j >= nv) x = x + -3.40282347e+38f;
+    }
+    v[u] = x;
+    mx = fmaxf(mx, x);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int j = lane + 32 * u;
+    const float e = j < T ? expf(v[u] - mx) : 0.f;
+    v[u] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.f / sum;
+  uint16_t* p = P + static_cast<size_t>(row) * ld;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int j = lane + 32 * u;
+    if (j < ld) p[j] = j < T ? f2h(v[u] * inv) : 0;
+  }
+}
+
+// V_h^T per (utterance, head): vt[(b*H + h)*dh + d][j] = V[b*T + j][h*dh + d],
+// zero for j in [T, ldt).
+__global__ void enc_vt_kernel(const uint16_t* __restrict__ qkv, int C, int T, int H, int dh,
+                              int ldt, uint16_t* __restrict__ vt) {
+  __shared__ uint16_t tile[32][33];
+  const int bh = blockIdx.z, b = bh / H, h = bh - (bh / H) * H;
+  const int j0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int j = j0 + i, d = d0 + threadIdx.x;
+    tile[i][threadIdx.x] = (j < T && d < dh)
+                               ? qkv[(static_cast<size_t>(b) * T + j) * 3 * C + 2 * C + h * dh + d]
+                               : 0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int d = d0 + i, j = j0 + threadIdx.x;
+    if (d < dh && j < ldt)
+      vt[(static_cast<size_t>(bh) * dh + d) * ldt + j] = tile[threadIdx.x][i];
+  }
+}
+
+// Row LayerNorm (biased variance, fp64 combine) writing fp32 and fp16.
+__global__ void enc_ln_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                              const float* __restrict__ bta, float* __restrict__ y,
+                              uint16_t* __restrict__ y16, int n, double eps) {
+  __shared__ double sh[32];
+  const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
+  float s = 0.f, q = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xr[i];
+    s += v;
+    q = fmaf(v, v, q);
+  }
+  double ds = warp_sum_d(static_cast<double>(s)), dq = warp_sum_d(static_cast<double>(q));
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sh[w] = ds;
+    sh[16 + w] = dq;
+  }
+  __syncthreads();
+  ds = lane < nw ? sh[lane] : 0.0;
+  dq = lane < nw ? sh[16 + lane] : 0.0;
+  ds = warp_sum_d(ds);
+  dq = warp_sum_d(dq);
+  const double dn = n;
+  const float mean = static_cast<float>(ds / dn);
+  float var = static_cast<float>(dq / dn - static_cast<double>(mean) * mean);
+  if (!(var >= 0.f)) var = 0.f;
+  const float rstd = static_cast<float>(1.0 / sqrt(static_cast<double>(var) + eps));
+  float* yr = y + static_cast<size_t>(blockIdx.x) * n;
+  uint16_t* y16r = y16 + static_cast<size_t>(blockIdx.x) * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = fmaf((xr[i] - mean) * rstd, g[i], bta[i]);
+    yr[i] = v;
+    y16r[i] = f2h(v);
+  }
+}
+
+}  // namespace
+
+struct EncoderEngine {
+  gsvk_encoder_config cfg{};
+  void* wmem = nullptr;
+  void* amem = nullptr;
+  const uint16_t *wqkv = nullptr, *wo = nullptr, *wi = nullptr, *wf = nullptr;
+  const float *bqkv = nullptr, *bo = nullptr, *bi = nullptr, *bf = nullptr;
+  const float *ln1g = nullptr, *ln1b = nullptr, *ln2g = nullptr, *ln2b = nullptr;
+  uint16_t *x16 = nullptr, *qkv16 = nullptr, *p16 = nullptr, *vt16 = nullptr, *ctx16 = nullptr,
+           *x1_16 = nullptr, *mid16 = nullptr;
+  float *s32 = nullptr, *y32 = nullptr, *x1_32 = nullptr, *f32 = nullptr;
+  int launches = 0;
+};
+
+}  // namespace gsvk
+
+using namespace gsvk;
+
+struct gsvk_encoder : gsvk::EncoderEngine {};
+
+extern "C" {
+
+int gsvk_encoder_destroy(gsvk_encoder_t h) {
+  if (!h) return GSVK_OK;
+  if (h->wmem) cudaFree(h->wmem);
+  if (h->amem) cudaFree(h->amem);
+  delete h;
+  return GSVK_OK;
+}
+
+int gsvk_encoder_create(const gsvk_encoder_config* cfg, const gsvk_encoder_host_weights* w,
+                        gsvk_encoder_t* out) {
+  if (!cfg || !w || !out) return fail(GSVK_ERR_INVALID, "encoder_create: null argument");
+  *out = nullptr;
+  if (!gsvk_available()) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
+  const int L = cfg->layers, C = cfg->hidden, H = cfg->heads, F = cfg->ffn;
+  if (L <= 0 || C <= 0 || H <= 0 || F <= 0 || C % H || cfg->max_batch <= 0 || cfg->max_seq <= 0)
+    return fail(GSVK_ERR_INVALID, "encoder_create: bad dimensions");
+  const int dh = C / H;
+  if (dh % 64 || C % 64 || F % 64 || cfg->max_seq > 256)
+    return fail(GSVK_ERR_UNSUPPORTED,
+                "encoder_create: head_dim, hidden and ffn must be multiples of 64, seq <= 256");
+  auto* e = new gsvk_encoder();
+  e->cfg = *cfg;
+  auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+  const size_t nqkv = (size_t)L * 3 * C * C, no = (size_t)L * C * C, ni = (size_t)L * F * C,
+               nf = (size_t)L * C * F;
+  struct Up { size_t off; const void* src; size_t bytes; };
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += al(bytes); return o; };
+  const size_t o_wqkv = take(nqkv * 2), o_wo = take(no * 2), o_wi = take(ni * 2),
+               o_wf = take(nf * 2), o_bqkv = take((size_t)L * 3 * C * 4),
+               o_bo = take((size_t)L * C * 4), o_bi = take((size_t)L * F * 4),
+               o_bf = take((size_t)L * C * 4), o_l1g = take((size_t)L * C * 4),
+               o_l1b = take((size_t)L * C * 4), o_l2g = take((size_t)L * C * 4),
+               o_l2b = take((size_t)L * C * 4);
+  if (cudaMalloc(&e->wmem, off) != cudaSuccess) {
+    cudaGetLastError();
+    delete e;
+    return fail(GSVK_ERR_NOMEM, "encoder_create: weights");
+  }
+  uint8_t* base = static_cast<uint8_t*>(e->wmem);
+  const Up ups[] = {{o_wqkv, w->wqkv, nqkv * 2}, {o_wo, w->wo, no * 2}, {o_wi, w->wi, ni * 2},
+                    {o_wf, w->wf, nf * 2}, {o_bqkv, w->bqkv, (size_t)L * 3 * C * 4},
+                    {o_bo, w->bo, (size_t)L * C * 4}, {o_bi, w->bi, (size_t)L * F * 4},
+                    {o_bf, w->bf, (size_t)L * C * 4}, {o_l1g, w->ln1g, (size_t)L * C * 4},
+                    {o_l1b, w->ln1b, (size_t)L * C * 4}, {o_l2g, w->ln2g, (size_t)L * C * 4},
+                    {o_l2b, w->ln2b, (size_t)L * C * 4}};
+  for (const Up& u : ups) {
+    if (!u.src) {
+      gsvk_encoder_destroy(e);
+      return fail(GSVK_ERR_INVALID, "encoder_create: null weight");
+    }
+    int rc = check_cuda(cudaMemcpy(base + u.off, u.src, u.bytes, cudaMemcpyHostToDevice),
+                        "encoder upload");
+    if (rc) { gsvk_encoder_destroy(e); return rc; }
+  }
+  e->wqkv = reinterpret_cast<const uint16_t*>(base + o_wqkv);
+  e->wo = reinterpret_cast<const uint16_t*>(base + o_wo);
+  e->wi = reinterpret_cast<const uint16_t*>(base + o_wi);
+  e->wf = reinterpret_cast<const uint16_t*>(base + o_wf);
+  e->bqkv = reinterpret_cast<const float*>(base + o_bqkv);
+  e->bo = reinterpret_cast<const float*>(base + o_bo);
+  e->bi = reinterpret_cast<const float*>(base + o_bi);
+  e->bf = reinterpret_cast<const float*>(base + o_bf);
+  e->ln1g = reinterpret_cast<const float*>(base + o_l1g);
+  e->ln1b = reinterpret_cast<const float*>(base + o_l1b);
+  e->ln2g = reinterpret_cast<const float*>(base + o_l2g);
+  e->ln2b = reinterpret_cast<const float*>(base + o_l2b);
+  // activations for max_batch x max_seq tokens
+  const size_t M = (size_t)cfg->max_batch * cfg->max_seq;
+  const size_t Tp = ((size_t)cfg->max_seq + 63) / 64 * 64;
+  const size_t BHT = (size_t)cfg->max_batch * H * cfg->max_seq;
+  off = 0;
+  const size_t o_x16 = take(M * C * 2), o_qkv = take(M * 3 * C * 2), o_s = take(BHT * Tp * 4),
+               o_p = take(BHT * Tp * 2), o_vt = take((size_t)cfg->max_batch * H * dh * Tp * 2),
+               o_ctx = take(M * C * 2), o_y = take(M * C * 4), o_x1 = take(M * C * 4),
+               o_x116 = take(M * C * 2), o_mid = take(M * F * 2), o_f = take(M * C * 4);
+  if (cudaMalloc(&e->amem, off) != cudaSuccess) {
+    cudaGetLastError();
+    gsvk_encoder_destroy(e);
+    return fail(GSVK_ERR_NOMEM, "encoder_create: activations (%zu bytes)", off);
+  }
+  uint8_t* a = static_cast<uint8_t*>(e->amem);
+  e->x16 = reinterpret_cast<uint16_t*>(a + o_x16);
+  e->qkv16 = reinterpret_cast<uint16_t*>(a + o_qkv);
+  e->s32 = reinterpret_cast<float*>(a + o_s);
+  e->p16 = reinterpret_cast<uint16_t*>(a + o_p);
+  e->vt16 = reinterpret_cast<uint16_t*>(a + o_vt);
+  e->ctx16 = reinterpret_cast<uint16_t*>(a + o_ctx);
+  e->y32 = reinterpret_cast<float*>(a + o_y);
+  e->x1_32 = reinterpret_cast<float*>(a + o_x1);
+  e->x1_16 = reinterpret_cast<uint16_t*>(a + o_x116);
+  e->mid16 = reinterpret_cast<uint16_t*>(a + o_mid);
+  e->f32 = reinterpret_cast<float*>(a + o_f);
+  *out = e;
+  return GSVK_OK;
+}
+
+int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, const int* valid,
+                         gsvk_stream_t stream) {
+  if (!h || !x || batch == 0 || seq == 0) return fail(GSVK_ERR_INVALID, "encoder_forward: null");
+  if (batch > (size_t)h->cfg.max_batch || seq > (size_t)h->cfg.max_seq)
+    return fail(GSVK_ERR_INVALID, "encoder_forward: batch/seq exceed the handle's maxima");
+  const gsvk_encoder_config& c = h->cfg;
+  const int C = c.hidden, H = c.heads, F = c.ffn, dh = C / H, T = (int)seq, B = (int)batch;
+  const int M = B * T, Tp = (T + 63) / 64 * 64;
+  cudaStream_t st = as_cuda(stream);
+  int launches = 0;
+  int rc = gsvk_f32_to_f16(x, h->x16, (size_t)M * C, stream);
+  if (rc) return rc;
+  ++launches;
+  auto gemm = [&](const uint16_t* A, int lda, const uint16_t* W, int N, int K, const float* bias,
+                  int act, const float* res, float* c32, uint16_t* c16) -> int {
+    gsvk_gemm_args g{};
+    g.a = A;
+    g.lda = lda;
+    g.b = W;
+    g.ldb = K;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.bias = bias;
+    g.act = act;
+    g.residual = res;
+    g.ld_res = N;
+    g.c = c32;
+    g.ldc = N;
+    g.c_f16 = c16;
+    g.ldc_f16 = N;
+    g.alpha = 1.f;
+    ++launches;
+    return gsvk_gemm_f16_ex(&g, stream);
+  };
+  for (int l = 0; l < c.layers; ++l) {
+    // q|k|v
+    if ((rc = gemm(h->x16, C, h->wqkv + (size_t)l * 3 * C * C, 3 * C, C,
+                   h->bqkv + (size_t)l * 3 * C, GSVK_ACT_NONE, nullptr, nullptr, h->qkv16)))
+      return rc;
+    // S = Q K^T / sqrt(dh), batched over (utterance, head)
+    {
+      TcProblem p{};
+      p.M = T;
+      p.N = T;
+      p.kc = dh;
+      p.taps = 1;
+      p.dil = 1;
+      p.phases = B * H;
+      p.out_rows = T;
+      p.bh = H;
+      p.a_rb = T; p.a_rh = 0; p.a_ch = dh; p.a_c0 = 0;
+      p.b_rb = T; p.b_rh = 0; p.b_ch = dh; p.b_c0 = C;
+      p.c_rb = H * T; p.c_rh = T; p.c_ch = 0;
+      TcEpilogue e = make_epilogue();
+      e.alpha = 1.f / std::sqrt(static_cast<float>(dh));
+      e.c32 = h->s32;
+      e.ld_c32 = Tp;
+      if ((rc = tc_run(h->qkv16, M, 3 * C, h->qkv16, M, 3 * C, p, e, 0, st, 3 * C, 3 * C)))
+        return rc;
+      ++launches;
+    }
+    {
+      const int rows = B * H * T;
+      enc_softmax_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(h->s32, Tp, rows, T,
+                                                                            H, valid, h->p16);
+      if ((rc = check_launch("enc_softmax_kernel"))) return rc;
+      dim3 grid((unsigned)((Tp + 31) / 32), (unsigned)((dh + 31) / 32), (unsigned)(B * H));
+      enc_vt_kernel<<<grid, dim3(32, 8), 0, st>>>(h->qkv16, C, T, H, dh, Tp, h->vt16);
+      if ((rc = check_launch("enc_vt_kernel"))) return rc;
+      launches += 2;
+    }
+    // ctx = P V_h, written into the head's columns of ctx16
+    {
+      TcProblem p{};
+      p.M = T;
+      p.N = dh;
+      p.kc = Tp;
+      p.taps = 1;
+      p.dil = 1;
+      p.phases = B * H;
+      p.out_rows = T;
+      p.bh = H;
+      p.a_rb = H * T; p.a_rh = T; p.a_ch = 0; p.a_c0 = 0;
+      p.b_rb = H * dh; p.b_rh = dh; p.b_ch = 0; p.b_c0 = 0;
+      p.c_rb = T; p.c_rh = 0; p.c_ch = dh;
+      TcEpilogue e = make_epilogue();
+      e.c16 = h->ctx16;
+      e.ld_c16 = C;
+      if ((rc = tc_run(h->p16, (long long)B * H * T, Tp, h->vt16, (long long)B * H * dh, Tp, p, e,
+                       0, st)))
+        return rc;
+      ++launches;
+    }
+    // attn_out + b + x -> LN1
+    if ((rc = gemm(h->ctx16, C, h->wo + (size_t)l * C * C, C, C, h->bo + (size_t)l * C,
+                   GSVK_ACT_NONE, x, h->y32, nullptr)))
+      return rc;
+    enc_ln_kernel<<<(unsigned)M, 256, 0, st>>>(h->y32, h->ln1g + (size_t)l * C,
+                                               h->ln1b + (size_t)l * C, h->x1_32, h->x1_16, C, c.eps);
+    if ((rc = check_launch("enc_ln_kernel"))) return rc;
+    ++launches;
+    // FFN
+    if ((rc = gemm(h->x1_16, C, h->wi + (size_t)l * F * C, F, C, h->bi + (size_t)l * F,
+                   GSVK_ACT_GELU_ERF, nullptr, nullptr, h->mid16)))
+      return rc;
+    if ((rc = gemm(h->mid16, F, h->wf + (size_t)l * C * F, C, F, h->bf + (size_t)l * C,
+                   GSVK_ACT_NONE, h->x1_32, h->f32, nullptr)))
+      return rc;
+    enc_ln_kernel<<<(unsigned)M, 256, 0, st>>>(h->f32, h->ln2g + (size_t)l * C,
+                                               h->ln2b + (size_t)l * C, x, h->x16, C, c.eps);
+    if ((rc = check_launch("enc_ln_kernel"))) return rc;
+    ++launches;
+  }
+  h->launches = launches;
+  return GSVK_OK;
+}
+
+int gsvk_encoder_launches(gsvk_encoder_t h) { return h ? h->launches : 0; }
+
+}  // extern "C"

@@ -17,6 +17,7 @@ constexpr int kSmemBudget = 200 * 1024;
 
 struct TapPlan {
   int ntaps, q0, qmax, a_mul, a_off, b_first, b_step, o_mul, o_off;
+  int a_row0, a_col0, b_row0, b_col0, c_row0, c_col0;  // batched-mode offsets
 };
 
 __device__ __forceinline__ TapPlan plan_for(const TcProblem& p, int phase) {
@@ -31,6 +32,17 @@ __device__ __forceinline__ TapPlan plan_for(const TcProblem& p, int phase) {
     t.b_step = 1;
     t.o_mul = 1;
     t.o_off = 0;
+    if (p.bh > 0) {
+      const int b = phase / p.bh, h = phase - (phase / p.bh) * p.bh;
+      t.a_row0 = b * p.a_rb + h * p.a_rh;
+      t.a_col0 = p.a_c0 + h * p.a_ch;
+      t.b_row0 = b * p.b_rb + h * p.b_rh;
+      t.b_col0 = p.b_c0 + h * p.b_ch;
+      t.c_row0 = b * p.c_rb + h * p.c_rh;
+      t.c_col0 = h * p.c_ch;
+    } else {
+      t.a_row0 = t.a_col0 = t.b_row0 = t.b_col0 = t.c_row0 = t.c_col0 = 0;
+    }
   } else {
     const int u = p.dil, k = p.taps, r = phase;
     t.ntaps = (k - r + u - 1) / u;
@@ -44,12 +56,15 @@ __device__ __forceinline__ TapPlan plan_for(const TcProblem& p, int phase) {
     t.b_step = u;
     t.o_mul = u;
     t.o_off = r - p.pad;
+    t.a_row0 = t.a_col0 = t.b_row0 = t.b_col0 = t.c_row0 = t.c_col0 = 0;
   }
   return t;
 }
 
+// n0: column within the problem (bias index, N bound); oc: output column
+// offset (batched mode), added to n0 for the output and residual addresses.
 __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int n0, int N,
-                                        const uint32_t* r) {
+                                        const uint32_t* r, int oc = 0) {
   float v[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]) * e.alpha;
@@ -64,13 +79,13 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
     for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j], e.act, e.slope);
   }
   if (e.residual) {
-    const float* rr = e.residual + orow * e.ld_res + n0;
+    const float* rr = e.residual + orow * e.ld_res + oc + n0;
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (full || n0 + j < N) v[j] = fmaf(e.res_scale, rr[j], v[j]);
   }
   if (e.c32) {
-    float* dst = e.c32 + orow * e.ld_c32 + n0;
+    float* dst = e.c32 + orow * e.ld_c32 + oc + n0;
     if (full && aligned16(dst)) {
 #pragma unroll
       for (int j = 0; j < 16; j += 4)
@@ -81,7 +96,7 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
     }
   }
   if (e.c16) {
-    uint16_t* dst = e.c16 + orow * e.ld_c16 + n0;
+    uint16_t* dst = e.c16 + orow * e.ld_c16 + oc + n0;
     if (full && aligned16(dst)) {
       uint32_t pk[8];
 #pragma unroll
@@ -94,7 +109,7 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
     }
   }
   if (e.c16_act) {
-    uint16_t* dst = e.c16_act + orow * e.ld_c16_act + n0;
+    uint16_t* dst = e.c16_act + orow * e.ld_c16_act + oc + n0;
     if (full && aligned16(dst)) {
       uint32_t pk[8];
 #pragma unroll
@@ -172,8 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int mt = rem / n_tiles, nt = rem - (rem / n_tiles) * n_tiles;
         const TapPlan tp = plan_for(p, phase);
         for (int t = 0; t < tp.ntaps && ok; ++t) {
-          const int a_row = tp.q0 + mt * kBM + tp.a_mul * t + tp.a_off;
-          const int b_row = (tp.b_first + tp.b_step * t) * p.b_tap_rows + nt * BN;
+          const int a_row = tp.q0 + mt * kBM + tp.a_mul * t + tp.a_off + tp.a_row0;
+          const int b_row = (tp.b_first + tp.b_step * t) * p.b_tap_rows + nt * BN + tp.b_row0;
           for (int kb = 0; kb < kpt; ++kb, ++it) {
             const int s = it % stages;
             const uint32_t ph = static_cast<uint32_t>(it / stages) & 1u;
@@ -182,8 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
-            tma_load_2d(sA + static_cast<size_t>(s) * a_bytes, &tmA, &full[s], kb * bk, a_row);
-            tma_load_2d(sB + static_cast<size_t>(s) * b_bytes, &tmB, &full[s], kb * bk, b_row);
+            tma_load_2d(sA + static_cast<size_t>(s) * a_bytes, &tmA, &full[s], kb * bk + tp.a_col0,
+                        a_row);
+            tma_load_2d(sB + static_cast<size_t>(s) * b_bytes, &tmB, &full[s], kb * bk + tp.b_col0,
+                        b_row);
           }
         }
       }
@@ -239,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = mt * kBM + quarter * 32 + lane;
       const int q = tp.q0 + i;
       const bool row_ok = (i < p.M) && (q <= tp.qmax);
-      const long long orow = static_cast<long long>(q) * tp.o_mul + tp.o_off;
+      const long long orow = static_cast<long long>(q) * tp.o_mul + tp.o_off + tp.c_row0;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
@@ -247,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[16];
         tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
         tmem_ld_wait();
-        if (row_ok && nt * BN + c0 < p.N) store16(e, orow, nt * BN + c0, p.N, r);
+        if (row_ok && nt * BN + c0 < p.N) store16(e, orow, nt * BN + c0, p.N, r, tp.c_col0);
       }
       tc_fence_before();
       __syncwarp();
@@ -344,7 +361,7 @@ int tc_pick_bn(long long M, long long N) {
 
 int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b,
            long long b_rows, long long ldb, TcProblem p, const TcEpilogue& e, int bn,
-           cudaStream_t st) {
+           cudaStream_t st, long long a_cols, long long b_cols) {
   if (!gsvk_available()) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
   if (p.kc % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0)
     return fail(GSVK_ERR_ALIGN, "tensor-core path needs K and leading dims multiple of 8");
@@ -355,9 +372,9 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
   p.bk = pick_bk(p.kc);
   if (bn == 0) bn = tc_pick_bn(p.M, p.N);
   CUtensorMap ta, tb;
-  int rc = make_kmajor_map(&ta, a, a_rows, p.kc, lda, kBM, p.bk);
+  int rc = make_kmajor_map(&ta, a, a_rows, a_cols ? a_cols : p.kc, lda, kBM, p.bk);
   if (rc) return rc;
-  rc = make_kmajor_map(&tb, b, b_rows, p.kc, ldb, bn, p.bk);
+  rc = make_kmajor_map(&tb, b, b_rows, b_cols ? b_cols : p.kc, ldb, bn, p.bk);
   if (rc) return rc;
   switch (bn) {
     case 16: return launch_bn<16>(ta, tb, p, e, st);

@@ -49,8 +49,17 @@ struct TcProblem {
   int dil, pad;     // conv: a_shift(t) = t*dil - pad
   int b_tap_rows;   // rows of B per tap (Co)
   int convt;        // 1: ConvTranspose1d polyphase mode (taps = kernel k, dil = u)
-  int phases;       // ConvT: u phases; otherwise 1
+  int phases;       // ConvT: u phases; batched: batch * bh; otherwise 1
   int out_rows;     // valid output rows (ConvT: T*u; others: M)
+  // Batched mode (bh > 0, convt == 0): phase p = (b, h) with b = p / bh,
+  // h = p % bh solves an independent GEMM whose operands and output start at
+  //   A row b*a_rb + h*a_rh, A column h*a_ch;  B row b*b_rb + h*b_rh,
+  //   B column h*b_ch;  output row b*c_rb + h*c_rh, output column h*c_ch.
+  // (multi-head attention over a fused QKV buffer: one launch per product)
+  // (plus constant column offsets a_c0 / b_c0, e.g. the K block of QKV)
+  int bh;
+  int a_rb, a_rh, a_ch, b_rb, b_rh, b_ch, c_rb, c_rh, c_ch;
+  int a_c0, b_c0;
 };
 
 }  // namespace gsvk

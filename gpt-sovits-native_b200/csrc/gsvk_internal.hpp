@@ -18,9 +18,11 @@ int make_kmajor_map(CUtensorMap* map, const uint16_t* base, long long rows, long
                     long long ld, int box_rows, int bk);
 int tc_pick_bn(long long M, long long N);
 // Launches the tensor-core kernel for problem p (bn = 0 picks the tile width).
+// a_cols / b_cols: width of the A / B tensor maps when problems address
+// column windows of a wider matrix (batched mode); 0 = p.kc.
 int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b,
            long long b_rows, long long ldb, TcProblem p, const TcEpilogue& e, int bn,
-           cudaStream_t st);
+           cudaStream_t st, long long a_cols = 0, long long b_cols = 0);
 TcEpilogue make_epilogue();
 // CUDA-core fallback for shapes the TMA path cannot express (K or leading
 // dimensions not multiples of 8, unaligned bases).

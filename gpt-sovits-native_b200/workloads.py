@@ -98,6 +98,37 @@ ENCODERS = {
 }
 
 
+def encoder_model(name: str, layers=None, seed=0) -> dict:
+    """Encoder weights in the oracle / C-ABI layout: q, k, v rows fused as
+    [L][3C][C]; N(0,0.02) fp16 matrices, N(0,0.02) fp32 biases, LayerNorm gain
+    1+N(0,0.05), bias N(0,0.02)."""
+    e = ENCODERS[name]
+    rng = np.random.default_rng(seed)
+    L = layers or e["layers"]
+    C, F = e["hidden"], e["ffn"]
+    m = dict(layers=L, hidden=C, heads=e["heads"], ffn=F, eps=e["eps"])
+    m["wqkv"] = _f16(_normal(rng, (L, 3 * C, C), 0.02))
+    m["bqkv"] = _normal(rng, (L, 3 * C), 0.02)
+    m["wo"] = _f16(_normal(rng, (L, C, C), 0.02))
+    m["bo"] = _normal(rng, (L, C), 0.02)
+    m["ln1g"] = (1.0 + _normal(rng, (L, C), 0.05)).astype(np.float32)
+    m["ln1b"] = _normal(rng, (L, C), 0.02)
+    m["wi"] = _f16(_normal(rng, (L, F, C), 0.02))
+    m["bi"] = _normal(rng, (L, F), 0.02)
+    m["wf"] = _f16(_normal(rng, (L, C, F), 0.02))
+    m["bf"] = _normal(rng, (L, C), 0.02)
+    m["ln2g"] = (1.0 + _normal(rng, (L, C), 0.05)).astype(np.float32)
+    m["ln2b"] = _normal(rng, (L, C), 0.02)
+    return m
+
+
+def encoder_input(name: str, batch=None, seq=None, seed=0) -> np.ndarray:
+    """Activations N(0,1) fp32 [batch*seq, hidden]."""
+    e = ENCODERS[name]
+    rng = np.random.default_rng(seed + 5000)
+    return _normal(rng, ((batch or e["batch"]) * (seq or e["seq"]), e["hidden"]), 1.0)
+
+
 def encoder_gemm_flops(name: str) -> int:
     e = ENCODERS[name]
     M, H, Fd = e["batch"] * e["seq"], e["hidden"], e["ffn"]

@@ -181,6 +181,37 @@ int gsvk_decoder_forward(gsvk_decoder_t h, const float* z, size_t T, float* wav,
 /* Kernel launches issued by the last gsvk_decoder_forward. */
 int gsvk_decoder_launches(gsvk_decoder_t h);
 
+/* ---- encoder stacks: RoBERTa-large / HuBERT-base (a20, a21) -------------- */
+/* bert::BertLayer::forward (bert_ops.hpp:347-400) and the HuBERT layer loop
+ * (hubert.cpp:590-730), post-LN, GELU(erf) FFN, every product on the tensor
+ * cores (q/k/v fused into one GEMM, attention as batched GEMMs).  HOST
+ * weights: fp16 [L][3C][C] (q, k, v rows), [L][C][C], [L][F][C], [L][C][F];
+ * fp32 biases and LayerNorm parameters.  hidden, ffn and head_dim must be
+ * multiples of 64; seq <= 256. */
+typedef struct gsvk_encoder* gsvk_encoder_t;
+typedef struct {
+  int layers, hidden, heads, ffn;
+  double eps;            /* 1e-12 RoBERTa, 1e-5 HuBERT */
+  int max_batch, max_seq;
+} gsvk_encoder_config;
+typedef struct {
+  const uint16_t* wqkv; const float* bqkv;
+  const uint16_t* wo;   const float* bo;
+  const float* ln1g; const float* ln1b;
+  const uint16_t* wi;   const float* bi;
+  const uint16_t* wf;   const float* bf;
+  const float* ln2g; const float* ln2b;
+} gsvk_encoder_host_weights;
+int gsvk_encoder_create(const gsvk_encoder_config* cfg, const gsvk_encoder_host_weights* w,
+                        gsvk_encoder_t* out);
+int gsvk_encoder_destroy(gsvk_encoder_t h);
+/* x: DEVICE fp32 [batch*seq][hidden], replaced by the stack's output.
+ * valid (DEVICE int32 [batch], optional): keys >= valid[b] are masked with
+ * finfo.min as the reference's attention mask (bert_ops.hpp:373-374). */
+int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, const int* valid,
+                         gsvk_stream_t stream);
+int gsvk_encoder_launches(gsvk_encoder_t h);
+
 /* ---- support primitives (a22) ------------------------------------------ */
 /* kern::layernorm (kern.cpp:27) applied to `rows` rows of n. y may equal x. */
 int gsvk_layernorm_rows(const float* x, const float* g, const float* b, float* y,

@@ -42,6 +42,16 @@ class T2SWeights(ctypes.Structure):
         "n1g", "n1b", "n2g", "n2b", "wpred", "audio_emb")]
 
 
+class EncoderDims(ctypes.Structure):
+    _fields_ = [("layers", c_int), ("hidden", c_int), ("heads", c_int), ("ffn", c_int),
+                ("eps", c_double)]
+
+
+class EncoderWeights(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("wqkv", "bqkv", "wo", "bo", "ln1g", "ln1b", "wi", "bi",
+                                        "wf", "bf", "ln2g", "ln2b")]
+
+
 class DecoderCfg(ctypes.Structure):
     _fields_ = [("n_stages", c_int), ("in_ch", c_int), ("ch0", c_int), ("conv_pre_k", c_int),
                 ("conv_post_k", c_int), ("up_rate", c_int * 8), ("up_k", c_int * 8),
@@ -84,6 +94,7 @@ def lib():
             "ora_t2s_prefill_layer": (None, [vp, vp, c_int, vp, sz, sz, sz, vp, vp]),
             "ora_t2s_greedy_sample": (c_int, [vp, c_int, vp, sz, c_int, vp]),
             "ora_attention_decode": (None, [vp, vp, vp, sz, sz, sz, sz, c_float, vp]),
+            "ora_encoder_layer": (None, [vp, vp, c_int, vp, c_int, c_int, vp]),
             "ora_t2s_generate": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp, vp, vp]),
         }
         for name, (res, args) in sigs.items():
@@ -329,3 +340,12 @@ def t2s_generate(model: dict, kcache: np.ndarray, vcache: np.ndarray, prefix: in
     if with_logits:
         return toks[:n], margins, logits
     return toks[:n], margins
+
+
+def encoder_layer(model: dict, layer: int, x: np.ndarray, B: int, T: int, valid=None) -> None:
+    """x [B*T, C] fp32, updated in place (model: workloads.encoder_model)."""
+    d = EncoderDims(model["layers"], model["hidden"], model["heads"], model["ffn"], model["eps"])
+    w = EncoderWeights(*[_p(model[n]) for n in ("wqkv", "bqkv", "wo", "bo", "ln1g", "ln1b", "wi",
+                                                "bi", "wf", "bf", "ln2g", "ln2b")])
+    vd = None if valid is None else np.ascontiguousarray(valid, np.int32)
+    lib().ora_encoder_layer(ctypes.byref(d), ctypes.byref(w), layer, _p(x), B, T, _p(vd))

@@ -742,6 +742,75 @@ void ora_attention_decode(const float* q, const uint16_t* kc, const uint16_t* vc
                  head_dim, scale, out + h * head_dim);
 }
 
+// bert_ops.hpp:347-400 BertLayer::forward (and the HuBERT layer loop,
+// hubert.cpp:590-730, which has the same post-LN structure): q/k/v via the
+// DenseF16 view (fp16 activations, fp32 accumulation) + bias; per head
+// S = (Q K^T) / sqrt(dh) (+ key mask), softmax rows, ctx = S V in fp32;
+// attn_out + bias + residual, LN; inter + bias, GELU(erf); ffn_out + bias +
+// residual, LN.  x [B*T][C] in place; valid (optional) holds the number of
+// real tokens per utterance (mask value finfo.min on the rest, :373-374).
+void ora_encoder_layer(const ora_encoder_dims* d, const ora_encoder_weights* w, int l, float* x,
+                       int B, int T, const int* valid) {
+  const size_t C = d->hidden, H = d->heads, dh = C / H, F = d->ffn, M = (size_t)B * T;
+  std::vector<float> q(M * C), k(M * C), v(M * C), ctx(M * C), y(M * C), mid(M * F), f2(M * C);
+  const size_t oqkv = (size_t)l * 3 * C * C, ob = (size_t)l * 3 * C;
+  ora_linear_f16(x, M, C, w->wqkv + oqkv, C, w->bqkv + ob, ORA_ACT_NONE, 0.f, q.data());
+  ora_linear_f16(x, M, C, w->wqkv + oqkv + C * C, C, w->bqkv + ob + C, ORA_ACT_NONE, 0.f, k.data());
+  ora_linear_f16(x, M, C, w->wqkv + oqkv + 2 * C * C, C, w->bqkv + ob + 2 * C, ORA_ACT_NONE, 0.f,
+                 v.data());
+  const float alpha = 1.f / std::sqrt(static_cast<float>(dh));
+  pool().run((size_t)B * H, 1, [&](size_t ib, size_t ie) {
+    std::vector<float> S((size_t)T * T);
+    for (size_t item = ib; item < ie; ++item) {
+      const size_t b = item / H, h = item % H;
+      const int nv = valid ? valid[b] : T;
+      for (int i = 0; i < T; ++i)
+        for (int j = 0; j < T; ++j) {
+          float acc = 0.f;
+          const float* qi = q.data() + ((b * T + i) * C + h * dh);
+          const float* kj = k.data() + ((b * T + j) * C + h * dh);
+          for (size_t e = 0; e < dh; ++e) acc = std::fmaf(qi[e], kj[e], acc);
+          float s = alpha * acc;
+          if (j >= nv) s = s + -3.40282347e+38f;
+          S[(size_t)i * T + j] = s;
+        }
+      for (int i = 0; i < T; ++i) {  // bert_ops.hpp:28-43 softmax_rows
+        float* r = S.data() + (size_t)i * T;
+        float mx = r[0];
+        for (int j = 1; j < T; ++j) mx = mx > r[j] ? mx : r[j];
+        float sum = 0.f;
+        for (int j = 0; j < T; ++j) {
+          r[j] = std::exp(r[j] - mx);
+          sum = sum + r[j];
+        }
+        const float inv = 1.f / sum;
+        for (int j = 0; j < T; ++j) r[j] = r[j] * inv;
+      }
+      for (int i = 0; i < T; ++i)
+        for (size_t e = 0; e < dh; ++e) {
+          float acc = 0.f;
+          for (int j = 0; j < T; ++j)
+            acc = std::fmaf(S[(size_t)i * T + j], v[(b * T + j) * C + h * dh + e], acc);
+          ctx[(b * T + i) * C + h * dh + e] = acc;
+        }
+    }
+  });
+  ora_linear_f16(ctx.data(), M, C, w->wo + (size_t)l * C * C, C, w->bo + (size_t)l * C,
+                 ORA_ACT_NONE, 0.f, y.data());
+  for (size_t i = 0; i < M * C; ++i) y[i] = y[i] + x[i];
+  for (size_t r = 0; r < M; ++r)
+    ora_layernorm(y.data() + r * C, w->ln1g + (size_t)l * C, w->ln1b + (size_t)l * C,
+                  y.data() + r * C, C, d->eps);
+  ora_linear_f16(y.data(), M, C, w->wi + (size_t)l * F * C, F, w->bi + (size_t)l * F,
+                 ORA_ACT_GELU_ERF, 0.f, mid.data());
+  ora_linear_f16(mid.data(), M, F, w->wf + (size_t)l * C * F, C, w->bf + (size_t)l * C,
+                 ORA_ACT_NONE, 0.f, f2.data());
+  for (size_t i = 0; i < M * C; ++i) f2[i] = f2[i] + y[i];
+  for (size_t r = 0; r < M; ++r)
+    ora_layernorm(f2.data() + r * C, w->ln2g + (size_t)l * C, w->ln2b + (size_t)l * C,
+                  x + r * C, C, d->eps);
+}
+
 int ora_t2s_greedy_sample(float* lg, int V, const int32_t* hist, size_t n_hist,
                           int eos_allowed, int* raw_argmax) {
   const int limit = eos_allowed ? V : V - 1;

@@ -198,6 +198,26 @@ int ora_t2s_generate(const ora_t2s_dims* d, const ora_t2s_weights* w,
                      size_t max_steps, int stop_on_eos, int32_t* tokens_out,
                      float* margins_out, float* last_logits);
 
+/* ---- encoders (BERT / HuBERT post-LN layer) ---------------------------- */
+typedef struct {
+  int layers, hidden, heads, ffn;
+  double eps;  /* 1e-12 RoBERTa, 1e-5 HuBERT */
+} ora_encoder_dims;
+
+typedef struct {
+  const uint16_t* wqkv; const float* bqkv; /* [L][3C][C] (q, k, v rows), [L][3C] */
+  const uint16_t* wo;   const float* bo;   /* [L][C][C], [L][C] */
+  const float* ln1g; const float* ln1b;    /* [L][C] */
+  const uint16_t* wi;   const float* bi;   /* [L][F][C], [L][F] */
+  const uint16_t* wf;   const float* bf;   /* [L][C][F], [L][C] */
+  const float* ln2g; const float* ln2b;    /* [L][C] */
+} ora_encoder_weights;
+
+/* bert_ops.hpp:347-400 (see oracle.cpp): one layer over x [B*T][C] in place;
+ * valid (optional, B ints) masks keys >= valid[b]. */
+void ora_encoder_layer(const ora_encoder_dims* d, const ora_encoder_weights* w, int layer,
+                       float* x, int B, int T, const int* valid);
+
 #ifdef __cplusplus
 }
 #endif
