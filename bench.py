@@ -407,7 +407,101 @@ def run_decoder(args, rank, local, world):
     return line
 
 
-WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder": run_decoder}
+# ------------------------------------------------------ encoder prefill (4)
+def run_encoder(args, rank, local, world):
+    import numpy as np
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    name = args.encoder
+    e = g.workloads.ENCODERS[name]
+    B, T = e["batch"], e["seq"]
+    m = g.workloads.encoder_model(name, seed=0)
+    x = g.workloads.encoder_input(name, seed=rank)
+    enc = g.Encoder(m, max_batch=B, max_seq=T)
+    x0 = torch.from_numpy(x).to(dev)
+    xd = torch.empty_like(x0)
+    for _ in range(args.warmup):
+        xd.copy_(x0)
+        enc.forward(xd, B, T)
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler()
+    barrier(world)
+    clocks.start()
+    start.record(stream)
+    for _ in range(args.steps):
+        xd.copy_(x0)
+        enc.forward(xd, B, T)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    t = max_over_ranks(start.elapsed_time(end) * 1e-3 / args.steps, world)
+    # e2e: host activations in, host outputs out
+    x_pin = torch.from_numpy(x).pin_memory()
+    y_pin = torch.empty_like(x_pin).pin_memory()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        xd.copy_(x_pin, non_blocking=True)
+        enc.forward(xd, B, T)
+        y_pin.copy_(xd, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e-3 / args.steps, world)
+    # the dominant kernel alone: the stack's GEMM shapes back to back
+    C, F = e["hidden"], e["ffn"]
+    M = B * T
+    a16 = [torch.randn(M, k, device=dev).half() for k in (C, C, C, F)]
+    w16 = [(torch.randn(n, k, device=dev) * 0.02).half() for n, k in ((3 * C, C), (C, C), (F, C), (C, F))]
+    outs = [torch.empty(M, n, device=dev, dtype=torch.float16) for n in (3 * C, C, F, C)]
+    for _ in range(3):
+        for a, w_, o in zip(a16, w16, outs):
+            g.gemm_ex(a, w_, c_f16=o)
+    torch.cuda.synchronize(dev)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    g0.record(stream)
+    for _ in range(reps):
+        for a, w_, o in zip(a16, w16, outs):
+            g.gemm_ex(a, w_, c_f16=o)
+    g1.record(stream)
+    torch.cuda.synchronize(dev)
+    gemm_flops_layer = 2 * M * (3 * C * C + C * C + F * C + C * F)
+    t_gemm = g0.elapsed_time(g1) * 1e-3 / reps
+    launches = enc.launches()
+    enc.close()
+    flops = g.workloads.encoder_gemm_flops(name)
+    _, tf, kind = measured_peaks()
+    achieved = gemm_flops_layer / t_gemm / 1e12
+    line = {"metric": f"{name} encoder prefill GEMM TFLOP/s (batch {B} x {T})",
+            "value": flops * world / t / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulate", "data": "synthetic (N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": f"encoder_{name} (BASELINE configs[3])", "layers": e["layers"],
+                       "hidden": C, "ffn": F, "global_batch": B * world, "seq_len": T,
+                       "parallelism": f"replicas x{world}",
+                       "flops_counted": "the stack's GEMM FLOPs; time is the whole forward",
+                       "l2": "weights 0.2-0.6 GB and activations > L2 per step"},
+            "e2e": {"value": flops * world / t_e2e / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": x.nbytes, "d2h_bytes_per_step": x.nbytes},
+            "gpu_launches": launches * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel", "achieved": achieved,
+                         "peak": tf, "unit": "TFLOP/s", "frac": achieved / tf,
+                         "peak_source": kind, "traffic": None,
+                         "note": "the four layer GEMM shapes back to back, CUDA events"}}
+    if clk:
+        line["clocks"] = clk
+    return line
+
+
+WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder": run_decoder,
+             "encoder": run_encoder}
 
 
 def run_reference(args, rank, world):
@@ -445,6 +539,7 @@ def main():
     ap.add_argument("--impl", default="gsvk", choices=["gsvk", "reference"])
     ap.add_argument("--workload", default="t2s_decode_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--encoder", default="bert", choices=["bert", "hubert"])
     ap.add_argument("--decode-steps", type=int, default=T2S_STEPS,
                     help="tokens per utterance (default 500; smaller only for profiling captures)")
     args = ap.parse_args()
