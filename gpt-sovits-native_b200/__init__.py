@@ -82,6 +82,14 @@ SIGNATURES = {
     "gsvk_encoder_destroy": (c_int, [_vp]),
     "gsvk_encoder_forward": (c_int, [_vp, _vp, _sz, _sz, _vp, _vp]),
     "gsvk_encoder_launches": (c_int, [_vp]),
+    "gsvk_t2s_batch_create": (c_int, [_vp, _vp, c_int, c_int, _vp]),
+    "gsvk_t2s_batch_destroy": (c_int, [_vp]),
+    "gsvk_t2s_batch_load_kv": (c_int, [_vp, c_int, _vp, _vp, _sz, _sz, _vp]),
+    "gsvk_t2s_batch_begin": (c_int, [_vp, c_int, _vp, _vp, _vp, _vp, c_int, _vp]),
+    "gsvk_t2s_batch_run": (c_int, [_vp, c_int, c_int, _vp]),
+    "gsvk_t2s_batch_read": (c_int, [_vp, c_int, _vp, _vp]),
+    "gsvk_t2s_batch_read_logits": (c_int, [_vp, _vp]),
+    "gsvk_t2s_batch_launches_per_step": (c_int, [_vp]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -543,6 +551,77 @@ class Encoder:
     def close(self):
         if self.h:
             lib().gsvk_encoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------- config 3: batched T2S
+class T2SBatch:
+    """Batched greedy decode of concurrent utterances (gsvk_t2s_batch_*)."""
+
+    def __init__(self, model: dict, cap: int, max_batch: int, max_steps: int):
+        import numpy as np
+
+        self.model = model
+        self._keep = {k: np.ascontiguousarray(v) for k, v in model.items()
+                      if isinstance(v, np.ndarray)}
+        cfg = T2SConfig(model["n_layers"], model["d_model"], model["n_heads"], model["ffn"],
+                        model["vocab"], model["ln_eps"], model["alpha_audio"], cap)
+        w = T2SHostWeights(*[self._keep[n].ctypes.data for n in (
+            "wqkv", "bqkv", "wout", "bout", "w1", "b1", "w2", "b2", "n1g", "n1b", "n2g", "n2b",
+            "wpred", "audio_emb")])
+        h = c_void_p()
+        check(lib().gsvk_t2s_batch_create(ctypes.byref(cfg), ctypes.byref(w), max_batch,
+                                          max_steps, ctypes.byref(h)))
+        self.h = h
+        self.B = 0
+
+    def load_kv(self, b: int, k, v, length: int, stream=None):
+        check(lib().gsvk_t2s_batch_load_kv(self.h, b, k.ctypes.data, v.ctypes.data, length,
+                                           k.shape[1], _stream(stream)))
+
+    def begin(self, lengths, pe0, first_tok, hist=None, stream=None):
+        import numpy as np
+
+        B = len(lengths)
+        ln = np.ascontiguousarray(lengths, np.int32)
+        pe = np.ascontiguousarray(pe0, np.int32)
+        ft = np.ascontiguousarray(first_tok, np.int32)
+        hs = None if hist is None else np.ascontiguousarray(hist, np.int32)
+        check(lib().gsvk_t2s_batch_begin(self.h, B, ln.ctypes.data, pe.ctypes.data, ft.ctypes.data,
+                                         None if hs is None else hs.ctypes.data,
+                                         0 if hs is None else hs.shape[1], _stream(stream)))
+        self.B = B
+
+    def run(self, steps: int, use_graph: bool = True, stream=None):
+        check(lib().gsvk_t2s_batch_run(self.h, steps, int(use_graph), _stream(stream)))
+
+    def read(self, steps: int):
+        import numpy as np
+
+        toks = np.zeros((steps, self.B), np.int32)
+        marg = np.zeros((steps, self.B), np.float32)
+        check(lib().gsvk_t2s_batch_read(self.h, steps, toks.ctypes.data, marg.ctypes.data))
+        return toks, marg
+
+    def read_logits(self):
+        import numpy as np
+
+        out = np.zeros((self.B, self.model["vocab"]), np.float32)
+        check(lib().gsvk_t2s_batch_read_logits(self.h, out.ctypes.data))
+        return out
+
+    def launches_per_step(self) -> int:
+        return lib().gsvk_t2s_batch_launches_per_step(self.h)
+
+    def close(self):
+        if self.h:
+            lib().gsvk_t2s_batch_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -1,0 +1,594 @@
+// t2s_batch.cu — batched T2S greedy decode: B concurrent utterances, each
+// with its own KV cache and length (64 utterances,
+// lengths U{64..1024}).
+//
+// One decode step streams every weight matrix once for all B tokens: the
+// projections run as tensor-core GEMMs with M = B (gemm_tc.cuh, narrow
+// 32-column tiles so that enough CTAs pull weights from HBM), the attention
+// as one CTA per (utterance, head) over that utterance's ragged cache, and
+// sampling as one CTA per utterance (repetition penalty over its own
+// history, 11-step EOS mask, t2s_engine.cpp:1594-1636).  The per-step
+// positions come from a device step counter, so one captured CUDA graph
+// replays every step.
+//
+// Numerics: fp16 operands with fp32 accumulation on the tensor cores (the
+// W2 and logits activations are fp16 here, fp32 in the batch-1 path); parity
+// with the oracle is at GEMM tolerance, not bit-exact.
+#include <cmath>
+#include <vector>
+
+#include "gsvk_internal.hpp"
+
+struct gsvk_t2s_batch;
+
+namespace gsvk {
+
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kMaxKeys = 4096;  // per-utterance slots the attention kernel keeps in shared memory
+
+struct BatchDev {
+  int L, D, H, F, V, HD, cap, B, max_steps;
+  float eps, alpha, scale;
+  const uint16_t *wqkv, *wout, *w1, *w2, *wpred, *emb;
+  const float *bqkv, *bout, *b1, *b2, *n1g, *n1b, *n2g, *n2b, *pe;
+  uint16_t *kc, *vc;              // [B][L][cap][D]
+  const int32_t* base_len;        // [B] slots filled before step 0
+  const int32_t* base_pe;         // [B] PE index of step 0
+  int32_t* step;                  // device step counter
+  int32_t* tok;                   // [B] current input tokens
+  uint8_t* seen;                  // [B][V] history marks
+  int32_t* tokens_out;            // [max_steps][B]
+  float* margins;                 // [max_steps][B] (optional)
+};
+
+__global__ void batch_embed_kernel(BatchDev m, float* __restrict__ x32, uint16_t* __restrict__ x16) {
+  const int b = blockIdx.x, D = m.D;
+  const int s = *m.step;
+  if (s >= m.max_steps) return;  // past the buffers: no-op
+  const uint16_t* er = m.emb + static_cast<size_t>(m.tok[b]) * D;
+  const float* pr = m.pe + static_cast<size_t>(m.base_pe[b] + s) * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float v = fmaf(m.alpha, pr[i], h2f(er[i]));
+    x32[static_cast<size_t>(b) * D + i] = v;
+    x16[static_cast<size_t>(b) * D + i] = f2h(v);
+  }
+}
+
+// K/V append at slot base_len[b] + step and one-query attention over
+// [0, base_len[b] + step] for head h of utterance b.
+__global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(BatchDev m, int l,
+                                                                  const float* __restrict__ qkv,
+                                                                  uint16_t* __restrict__ out16) {
+  __shared__ float sc[kMaxKeys];
+  __shared__ float red[kAttnThreads / 32];
+  __shared__ float q[64];
+  __shared__ float part[kAttnThreads / 32][64];
+  const int b = blockIdx.x, h = blockIdx.y, HD = m.HD, D = m.D;
+  if (*m.step >= m.max_steps) return;
+  const int pos = m.base_len[b] + *m.step;
+  const int len = pos + 1;
+  const size_t slab = (static_cast<size_t>(b) * m.L + l) * m.cap;
+  uint16_t* kb = m.kc + slab * D + h * HD;
+  uint16_t* vb = m.vc + slab * D + h * HD;
+  const float* qrow = qkv + static_cast<size_t>(b) * 3 * D;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < HD) {
+    q[tid] = qrow[h * HD + tid];
+    kb[static_cast<size_t>(pos) * D + tid] = f2h(qrow[D + h * HD + tid]);
+    vb[static_cast<size_t>(pos) * D + tid] = f2h(qrow[2 * D + h * HD + tid]);
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int k = tid; k < len; k += kAttnThreads) {
+    const uint16_t* kr = kb + static_cast<size_t>(k) * D;
+    float d = 0.f;
+    for (int e = 0; e < HD; e += 8) {
+      float kf[8];
+      unpack8(*reinterpret_cast<const uint4*>(kr + e), kf);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d = fmaf(q[e + u], kf[u], d);
+    }
+    d *= m.scale;
+    sc[k] = d;
+    mx = fmaxf(mx, d);
+  }
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < kAttnThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int k = tid; k < len; k += kAttnThreads) {
+    const float e = expf(sc[k] - mx);
+    sc[k] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int w = 0; w < kAttnThreads / 32; ++w) sum += red[w];
+  // P . V: warp w takes keys w, w+4, ...; lane = dimension (and +32)
+  float o0 = 0.f, o1 = 0.f;
+  for (int k = warp; k < len; k += kAttnThreads / 32) {
+    const uint16_t* vr = vb + static_cast<size_t>(k) * D;
+    const float p = sc[k];
+    o0 = fmaf(p, h2f(vr[lane]), o0);
+    if (HD > 32) o1 = fmaf(p, h2f(vr[32 + lane]), o1);
+  }
+  part[warp][lane] = o0;
+  if (HD > 32) part[warp][32 + lane] = o1;
+  __syncthreads();
+  if (tid < HD) {
+    float o = 0.f;
+    for (int w = 0; w < kAttnThreads / 32; ++w) o += part[w][tid];
+    out16[static_cast<size_t>(b) * D + h * HD + tid] = f2h(o / sum);
+  }
+}
+
+__global__ void batch_ln_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                const float* __restrict__ bta, float* __restrict__ y,
+                                uint16_t* __restrict__ y16, int n, double eps) {
+  __shared__ double sh[64];
+  const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
+  float s = 0.f, q = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xr[i];
+    s += v;
+    q = fmaf(v, v, q);
+  }
+  double ds = warp_sum_d(static_cast<double>(s)), dq = warp_sum_d(static_cast<double>(q));
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sh[w] = ds;
+    sh[32 + w] = dq;
+  }
+  __syncthreads();
+  ds = lane < nw ? sh[lane] : 0.0;
+  dq = lane < nw ? sh[32 + lane] : 0.0;
+  ds = warp_sum_d(ds);
+  dq = warp_sum_d(dq);
+  const float mean = static_cast<float>(ds / n);
+  float var = static_cast<float>(dq / n - static_cast<double>(mean) * mean);
+  if (!(var >= 0.f)) var = 0.f;
+  const float rstd = static_cast<float>(1.0 / sqrt(static_cast<double>(var) + eps));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = fmaf((xr[i] - mean) * rstd, g[i], bta[i]);
+    y[static_cast<size_t>(blockIdx.x) * n + i] = v;
+    y16[static_cast<size_t>(blockIdx.x) * n + i] = f2h(v);
+  }
+}
+
+// Greedy sample of utterance b (penalty 1.35 once per distinct history
+// token, EOS excluded while step < 11), then advance: record the token, mark
+// it seen, make it the next input.  The last block bumps the step counter.
+__global__ void batch_sample_kernel(BatchDev m, const float* __restrict__ logits,
+                                    unsigned* __restrict__ done) {
+  __shared__ float rv[32];
+  __shared__ float rs[32];
+  __shared__ int ri[32];
+  const int b = blockIdx.x, V = m.V;
+  const int s = *m.step;
+  if (s >= m.max_steps) return;
+  const int limit = s >= 11 ? V : V - 1;
+  const float* lg = logits + static_cast<size_t>(b) * V;
+  const uint8_t* seen = m.seen + static_cast<size_t>(b) * V;
+  float bv = -INFINITY, sv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = threadIdx.x; c < limit; c += blockDim.x) {
+    float v = lg[c];
+    if (seen[c]) v = v < 0.f ? v * 1.35f : v / 1.35f;
+    if (v > bv || (v == bv && c < bi)) {
+      sv = bv;
+      bv = v;
+      bi = c;
+    } else if (v > sv) {
+      sv = v;
+    }
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o), os = __shfl_xor_sync(0xffffffffu, sv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      sv = fmaxf(os, bv);
+      bv = ov;
+      bi = oi;
+    } else {
+      sv = fmaxf(sv, ov);
+    }
+  }
+  if (lane == 0) {
+    rv[w] = bv;
+    rs[w] = sv;
+    ri[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float B = rv[0], S = rs[0];
+    int I = ri[0];
+    for (int k = 1; k < nw; ++k) {
+      if (rv[k] > B || (rv[k] == B && ri[k] < I)) {
+        S = fmaxf(rs[k], B);
+        B = rv[k];
+        I = ri[k];
+      } else {
+        S = fmaxf(S, rv[k]);
+      }
+    }
+    m.tokens_out[static_cast<size_t>(s) * m.B + b] = I;
+    if (m.margins) m.margins[static_cast<size_t>(s) * m.B + b] = B - S;
+    m.seen[static_cast<size_t>(b) * V + I] = 1;
+    m.tok[b] = I;
+    __threadfence();
+    if (atomicAdd(done, 1u) == static_cast<unsigned>(m.B) - 1) {
+      *done = 0;
+      *m.step = s + 1;
+    }
+  }
+}
+
+}  // namespace
+
+struct T2SBatchEngine {
+  BatchDev d{};
+  int max_batch = 0, cur_batch = 0;
+  void* wmem = nullptr;
+  void* amem = nullptr;
+  int32_t *base_len = nullptr, *base_pe = nullptr, *step = nullptr, *tok = nullptr,
+          *tokens_out = nullptr;
+  float* margins = nullptr;
+  unsigned* done = nullptr;
+  uint8_t* seen = nullptr;
+  float *x32 = nullptr, *qkv32 = nullptr, *hpre32 = nullptr, *h32 = nullptr, *xpre32 = nullptr,
+        *logits = nullptr;
+  uint16_t *x16 = nullptr, *attn16 = nullptr, *h16 = nullptr, *ff16 = nullptr;
+  int max_steps = 0;
+  int host_step = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int graph_batch = 0;
+  int launches_per_step = 0;
+};
+
+namespace {
+
+int gemm_m(const uint16_t* A, int M, int K, const uint16_t* W, int N, const float* bias, int act,
+           const float* res, float* c32, uint16_t* c16, cudaStream_t st) {
+  TcProblem p{};
+  p.M = M;
+  p.N = N;
+  p.kc = K;
+  p.taps = 1;
+  p.dil = 1;
+  p.phases = 1;
+  p.out_rows = M;
+  TcEpilogue e = make_epilogue();
+  e.bias = bias;
+  e.act = act;
+  e.residual = res;
+  e.ld_res = N;
+  e.c32 = c32;
+  e.ld_c32 = N;
+  e.c16 = c16;
+  e.ld_c16 = N;
+  // 32-column tiles: N/32 CTAs stream the weight matrix (M = batch <= 128)
+  return tc_run(A, M, K, W, N, K, p, e, 32, st);
+}
+
+int batch_step(T2SBatchEngine* e, int B, cudaStream_t st, int* launches) {
+  BatchDev& m = e->d;
+  const int D = m.D, F = m.F;
+  int n = 0, rc;
+  batch_embed_kernel<<<B, 256, 0, st>>>(m, e->x32, e->x16);
+  if ((rc = check_launch("batch_embed_kernel"))) return rc;
+  ++n;
+  for (int l = 0; l < m.L; ++l) {
+    if ((rc = gemm_m(e->x16, B, D, m.wqkv + (size_t)l * 3 * D * D, 3 * D,
+                     m.bqkv + (size_t)l * 3 * D, GSVK_ACT_NONE, nullptr, e->qkv32, nullptr, st)))
+      return rc;
+    batch_attn_kernel<<<dim3(B, m.H), kAttnThreads, 0, st>>>(m, l, e->qkv32, e->attn16);
+    if ((rc = check_launch("batch_attn_kernel"))) return rc;
+    if ((rc = gemm_m(e->attn16, B, D, m.wout + (size_t)l * D * D, D, m.bout + (size_t)l * D,
+                     GSVK_ACT_NONE, e->x32, e->hpre32, nullptr, st)))
+      return rc;
+    batch_ln_kernel<<<B, 256, 0, st>>>(e->hpre32, m.n1g + (size_t)l * D, m.n1b + (size_t)l * D,
+                                       e->h32, e->h16, D, m.eps);
+    if ((rc = check_launch("batch_ln_kernel"))) return rc;
+    if ((rc = gemm_m(e->h16, B, D, m.w1 + (size_t)l * F * D, F, m.b1 + (size_t)l * F,
+                     GSVK_ACT_RELU, nullptr, nullptr, e->ff16, st)))
+      return rc;
+    if ((rc = gemm_m(e->ff16, B, F, m.w2 + (size_t)l * D * F, D, m.b2 + (size_t)l * D,
+                     GSVK_ACT_NONE, e->h32, e->xpre32, nullptr, st)))
+      return rc;
+    batch_ln_kernel<<<B, 256, 0, st>>>(e->xpre32, m.n2g + (size_t)l * D, m.n2b + (size_t)l * D,
+                                       e->x32, e->x16, D, m.eps);
+    if ((rc = check_launch("batch_ln_kernel"))) return rc;
+    n += 7;
+  }
+  if ((rc = gemm_m(e->x16, B, D, m.wpred, m.V, nullptr, GSVK_ACT_NONE, nullptr, e->logits,
+                   nullptr, st)))
+    return rc;
+  batch_sample_kernel<<<B, 256, 0, st>>>(m, e->logits, e->done);
+  if ((rc = check_launch("batch_sample_kernel"))) return rc;
+  n += 2;
+  if (launches) *launches = n;
+  return GSVK_OK;
+}
+
+size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+void pe_rows(int D, int cap, float* pe) {
+  const float log_inc = static_cast<float>(-std::log(10000.0) / static_cast<double>(D));
+  for (int p = 0; p < cap; ++p) {
+    const float pf = static_cast<float>(p);
+    for (int d = 0; d < D; d += 2) {
+      const float div = std::exp(static_cast<float>(d) * log_inc);
+      pe[(size_t)p * D + d] = std::sin(pf * div);
+      pe[(size_t)p * D + d + 1] = std::cos(pf * div);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace gsvk
+
+using namespace gsvk;
+
+struct gsvk_t2s_batch : gsvk::T2SBatchEngine {};
+
+extern "C" {
+
+int gsvk_t2s_batch_destroy(gsvk_t2s_batch_t h) {
+  if (!h) return GSVK_OK;
+  if (h->exec) cudaGraphExecDestroy(h->exec);
+  if (h->graph) cudaGraphDestroy(h->graph);
+  if (h->wmem) cudaFree(h->wmem);
+  if (h->amem) cudaFree(h->amem);
+  delete h;
+  return GSVK_OK;
+}
+
+int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w,
+                          int max_batch, int max_steps, gsvk_t2s_batch_t* out) {
+  if (!cfg || !w || !out) return fail(GSVK_ERR_INVALID, "t2s_batch_create: null argument");
+  *out = nullptr;
+  if (!gsvk_available()) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
+  const int L = cfg->n_layers, D = cfg->d_model, H = cfg->n_heads, F = cfg->ffn, V = cfg->vocab;
+  const int cap = cfg->cap;
+  if (L <= 0 || D <= 0 || H <= 0 || F <= 0 || V <= 1 || cap <= 0 || D % H || max_batch <= 0 ||
+      max_batch > 128 || max_steps <= 0)
+    return fail(GSVK_ERR_INVALID, "t2s_batch_create: bad dimensions");
+  const int HD = D / H;
+  if ((HD != 32 && HD != 64) || D % 64 || F % 64 || cap > kMaxKeys)
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s_batch_create: head_dim 32/64, D and F multiples of 64, "
+                "cap <= %d", kMaxKeys);
+  if (!w->wqkv || !w->bqkv || !w->wout || !w->bout || !w->w1 || !w->b1 || !w->w2 || !w->b2 ||
+      !w->n1g || !w->n1b || !w->n2g || !w->n2b || !w->wpred || !w->audio_emb)
+    return fail(GSVK_ERR_INVALID, "t2s_batch_create: null weight");
+  auto* e = new gsvk_t2s_batch();
+  e->max_batch = max_batch;
+  e->max_steps = max_steps;
+  BatchDev& d = e->d;
+  d.max_steps = max_steps;
+  d.L = L; d.D = D; d.H = H; d.F = F; d.V = V; d.HD = HD; d.cap = cap;
+  d.eps = cfg->ln_eps; d.alpha = cfg->alpha_audio;
+  d.scale = 1.0f / std::sqrt(static_cast<float>(HD));
+  const size_t nq = (size_t)L * 3 * D * D, no = (size_t)L * D * D, n1 = (size_t)L * F * D,
+               n2 = (size_t)L * D * F, np = (size_t)V * D;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += al256(bytes); return o; };
+  struct Up { size_t o; const void* src; size_t bytes; };
+  std::vector<Up> ups;
+  auto up = [&](const void* src, size_t bytes) { ups.push_back({take(bytes), src, bytes}); return ups.back().o; };
+  std::vector<float> pe((size_t)cap * D);
+  pe_rows(D, cap, pe.data());
+  const size_t o_q = up(w->wqkv, nq * 2), o_o = up(w->wout, no * 2), o_1 = up(w->w1, n1 * 2),
+               o_2 = up(w->w2, n2 * 2), o_p = up(w->wpred, np * 2), o_e = up(w->audio_emb, np * 2),
+               o_bq = up(w->bqkv, (size_t)L * 3 * D * 4), o_bo = up(w->bout, (size_t)L * D * 4),
+               o_b1 = up(w->b1, (size_t)L * F * 4), o_b2 = up(w->b2, (size_t)L * D * 4),
+               o_n1g = up(w->n1g, (size_t)L * D * 4), o_n1b = up(w->n1b, (size_t)L * D * 4),
+               o_n2g = up(w->n2g, (size_t)L * D * 4), o_n2b = up(w->n2b, (size_t)L * D * 4),
+               o_pe = up(pe.data(), (size_t)cap * D * 4);
+  if (cudaMalloc(&e->wmem, off) != cudaSuccess) {
+    cudaGetLastError();
+    delete e;
+    return fail(GSVK_ERR_NOMEM, "t2s_batch_create: weights");
+  }
+  uint8_t* base = static_cast<uint8_t*>(e->wmem);
+  for (const Up& u : ups) {
+    int rc = check_cuda(cudaMemcpy(base + u.o, u.src, u.bytes, cudaMemcpyHostToDevice), "upload");
+    if (rc) { gsvk_t2s_batch_destroy(e); return rc; }
+  }
+  d.wqkv = reinterpret_cast<const uint16_t*>(base + o_q);
+  d.wout = reinterpret_cast<const uint16_t*>(base + o_o);
+  d.w1 = reinterpret_cast<const uint16_t*>(base + o_1);
+  d.w2 = reinterpret_cast<const uint16_t*>(base + o_2);
+  d.wpred = reinterpret_cast<const uint16_t*>(base + o_p);
+  d.emb = reinterpret_cast<const uint16_t*>(base + o_e);
+  d.bqkv = reinterpret_cast<const float*>(base + o_bq);
+  d.bout = reinterpret_cast<const float*>(base + o_bo);
+  d.b1 = reinterpret_cast<const float*>(base + o_b1);
+  d.b2 = reinterpret_cast<const float*>(base + o_b2);
+  d.n1g = reinterpret_cast<const float*>(base + o_n1g);
+  d.n1b = reinterpret_cast<const float*>(base + o_n1b);
+  d.n2g = reinterpret_cast<const float*>(base + o_n2g);
+  d.n2b = reinterpret_cast<const float*>(base + o_n2b);
+  d.pe = reinterpret_cast<const float*>(base + o_pe);
+  // KV caches + per-utterance state + activations
+  const size_t B = (size_t)max_batch;
+  off = 0;
+  const size_t o_kc = take(B * L * cap * D * 2), o_vc = take(B * L * cap * D * 2),
+               o_bl = take(B * 4), o_bp = take(B * 4), o_st = take(256), o_tok = take(B * 4),
+               o_out = take((size_t)max_steps * B * 4), o_mg = take((size_t)max_steps * B * 4),
+               o_dn = take(256), o_seen = take(B * V), o_x32 = take(B * D * 4),
+               o_qkv = take(B * 3 * D * 4), o_hp = take(B * D * 4), o_h32 = take(B * D * 4),
+               o_xp = take(B * D * 4), o_lg = take(B * V * 4), o_x16 = take(B * D * 2),
+               o_a16 = take(B * D * 2), o_h16 = take(B * D * 2), o_ff = take(B * F * 2);
+  if (cudaMalloc(&e->amem, off) != cudaSuccess) {
+    cudaGetLastError();
+    gsvk_t2s_batch_destroy(e);
+    return fail(GSVK_ERR_NOMEM, "t2s_batch_create: caches (%zu bytes)", off);
+  }
+  uint8_t* a = static_cast<uint8_t*>(e->amem);
+  if (int rc = check_cuda(cudaMemset(a, 0, off), "t2s_batch memset")) {
+    gsvk_t2s_batch_destroy(e);
+    return rc;
+  }
+  d.kc = reinterpret_cast<uint16_t*>(a + o_kc);
+  d.vc = reinterpret_cast<uint16_t*>(a + o_vc);
+  e->base_len = reinterpret_cast<int32_t*>(a + o_bl);
+  e->base_pe = reinterpret_cast<int32_t*>(a + o_bp);
+  e->step = reinterpret_cast<int32_t*>(a + o_st);
+  e->tok = reinterpret_cast<int32_t*>(a + o_tok);
+  e->tokens_out = reinterpret_cast<int32_t*>(a + o_out);
+  e->margins = reinterpret_cast<float*>(a + o_mg);
+  e->done = reinterpret_cast<unsigned*>(a + o_dn);
+  e->seen = a + o_seen;
+  e->x32 = reinterpret_cast<float*>(a + o_x32);
+  e->qkv32 = reinterpret_cast<float*>(a + o_qkv);
+  e->hpre32 = reinterpret_cast<float*>(a + o_hp);
+  e->h32 = reinterpret_cast<float*>(a + o_h32);
+  e->xpre32 = reinterpret_cast<float*>(a + o_xp);
+  e->logits = reinterpret_cast<float*>(a + o_lg);
+  e->x16 = reinterpret_cast<uint16_t*>(a + o_x16);
+  e->attn16 = reinterpret_cast<uint16_t*>(a + o_a16);
+  e->h16 = reinterpret_cast<uint16_t*>(a + o_h16);
+  e->ff16 = reinterpret_cast<uint16_t*>(a + o_ff);
+  d.base_len = e->base_len;
+  d.base_pe = e->base_pe;
+  d.step = e->step;
+  d.tok = e->tok;
+  d.seen = e->seen;
+  d.tokens_out = e->tokens_out;
+  d.margins = e->margins;
+  *out = e;
+  return GSVK_OK;
+}
+
+int gsvk_t2s_batch_load_kv(gsvk_t2s_batch_t h, int b, const uint16_t* k_host,
+                           const uint16_t* v_host, size_t len, size_t src_rows,
+                           gsvk_stream_t stream) {
+  if (!h || b < 0 || b >= h->max_batch || (len && (!k_host || !v_host)) || src_rows < len ||
+      len > (size_t)h->d.cap)
+    return fail(GSVK_ERR_INVALID, "t2s_batch_load_kv: bad arguments");
+  const BatchDev& d = h->d;
+  for (int l = 0; l < d.L && len; ++l) {
+    const size_t dst = (((size_t)b * d.L + l) * d.cap) * d.D;
+    int rc = check_cuda(cudaMemcpyAsync(d.kc + dst, k_host + (size_t)l * src_rows * d.D,
+                                        len * d.D * 2, cudaMemcpyHostToDevice, as_cuda(stream)),
+                        "batch kv k");
+    if (rc) return rc;
+    rc = check_cuda(cudaMemcpyAsync(d.vc + dst, v_host + (size_t)l * src_rows * d.D, len * d.D * 2,
+                                    cudaMemcpyHostToDevice, as_cuda(stream)),
+                    "batch kv v");
+    if (rc) return rc;
+  }
+  return GSVK_OK;
+}
+
+// Sets the B utterances' lengths, PE origins, first input tokens and
+// histories (HOST arrays; hist is [B][n_hist], -1 entries ignored) and
+// resets the step counter.
+int gsvk_t2s_batch_begin(gsvk_t2s_batch_t h, int B, const int32_t* len, const int32_t* pe0,
+                         const int32_t* first_tok, const int32_t* hist, int n_hist,
+                         gsvk_stream_t stream) {
+  if (!h || B <= 0 || B > h->max_batch || !len || !pe0 || !first_tok || (n_hist > 0 && !hist))
+    return fail(GSVK_ERR_INVALID, "t2s_batch_begin: bad arguments");
+  const BatchDev& d = h->d;
+  for (int b = 0; b < B; ++b)
+    if (len[b] < 0 || len[b] + h->max_steps > d.cap || pe0[b] < 0 || pe0[b] + h->max_steps > d.cap ||
+        first_tok[b] < 0 || first_tok[b] >= d.V)
+      return fail(GSVK_ERR_INVALID, "t2s_batch_begin: utterance %d out of range", b);
+  cudaStream_t st = as_cuda(stream);
+  std::vector<uint8_t> seen((size_t)B * d.V, 0);
+  for (int b = 0; b < B; ++b)
+    for (int i = 0; i < n_hist; ++i) {
+      const int t = hist[(size_t)b * n_hist + i];
+      if (t >= 0 && t < d.V) seen[(size_t)b * d.V + t] = 1;
+    }
+  // synchronous copies from pageable memory: the caller's arrays may be freed after return
+  int rc = check_cuda(cudaMemcpy(h->seen, seen.data(), seen.size(), cudaMemcpyHostToDevice), "seen");
+  if (!rc) rc = check_cuda(cudaMemcpy(h->base_len, len, B * 4, cudaMemcpyHostToDevice), "len");
+  if (!rc) rc = check_cuda(cudaMemcpy(h->base_pe, pe0, B * 4, cudaMemcpyHostToDevice), "pe0");
+  if (!rc) rc = check_cuda(cudaMemcpy(h->tok, first_tok, B * 4, cudaMemcpyHostToDevice), "tok");
+  if (!rc) rc = check_cuda(cudaMemsetAsync(h->step, 0, 4, st), "step");
+  if (!rc) rc = check_cuda(cudaMemsetAsync(h->done, 0, 4, st), "done");
+  h->cur_batch = B;
+  h->host_step = 0;
+  h->d.B = B;
+  return rc;
+}
+
+// Runs `steps` greedy steps (no EOS stop: fixed-length batches).  The first
+// call for a batch size records the step into a CUDA graph; later steps
+// replay it.  Outputs stay on the device until gsvk_t2s_batch_read.
+int gsvk_t2s_batch_run(gsvk_t2s_batch_t h, int steps, int use_graph, gsvk_stream_t stream) {
+  if (!h || h->cur_batch <= 0 || steps < 0) return fail(GSVK_ERR_INVALID, "t2s_batch_run: begin first");
+  if (h->host_step + steps > h->max_steps)
+    return fail(GSVK_ERR_INVALID, "t2s_batch_run: %d + %d steps exceed max_steps %d", h->host_step,
+                steps, h->max_steps);
+  h->host_step += steps;
+  cudaStream_t st = as_cuda(stream);
+  const int B = h->cur_batch;
+  if (!use_graph) {
+    for (int s = 0; s < steps; ++s)
+      if (int rc = batch_step(h, B, st, &h->launches_per_step)) return rc;
+    return GSVK_OK;
+  }
+  if (!h->exec || h->graph_batch != B) {
+    if (h->exec) cudaGraphExecDestroy(h->exec);
+    if (h->graph) cudaGraphDestroy(h->graph);
+    h->exec = nullptr;
+    h->graph = nullptr;
+    cudaStream_t cap;
+    int rc = check_cuda(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking), "capture stream");
+    if (rc) return rc;
+    rc = check_cuda(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "begin capture");
+    if (!rc) rc = batch_step(h, B, cap, &h->launches_per_step);
+    cudaGraph_t g = nullptr;
+    const int rc_end = check_cuda(cudaStreamEndCapture(cap, &g), "end capture");
+    cudaStreamDestroy(cap);
+    if (rc || rc_end) {
+      if (g) cudaGraphDestroy(g);
+      return rc ? rc : rc_end;
+    }
+    rc = check_cuda(cudaGraphInstantiate(&h->exec, g, 0), "graph instantiate");
+    if (rc) {
+      cudaGraphDestroy(g);
+      return rc;
+    }
+    h->graph = g;
+    h->graph_batch = B;
+  }
+  for (int s = 0; s < steps; ++s)
+    if (int rc = check_cuda(cudaGraphLaunch(h->exec, st), "graph launch")) return rc;
+  return GSVK_OK;
+}
+
+// tokens / margins: HOST [steps][B]; synchronous.
+int gsvk_t2s_batch_read(gsvk_t2s_batch_t h, int steps, int32_t* tokens, float* margins) {
+  if (!h || steps < 0 || steps > h->max_steps || !tokens)
+    return fail(GSVK_ERR_INVALID, "t2s_batch_read: bad arguments");
+  const size_t n = (size_t)steps * h->cur_batch;
+  int rc = check_cuda(cudaMemcpy(tokens, h->tokens_out, n * 4, cudaMemcpyDeviceToHost), "tokens");
+  if (!rc && margins)
+    rc = check_cuda(cudaMemcpy(margins, h->margins, n * 4, cudaMemcpyDeviceToHost), "margins");
+  return rc;
+}
+
+// Logits of the last step (HOST [B][V]); synchronous.
+int gsvk_t2s_batch_read_logits(gsvk_t2s_batch_t h, float* host_out) {
+  if (!h || !host_out) return fail(GSVK_ERR_INVALID, "t2s_batch_read_logits: null");
+  return check_cuda(cudaMemcpy(host_out, h->logits, (size_t)h->cur_batch * h->d.V * 4,
+                               cudaMemcpyDeviceToHost),
+                    "logits");
+}
+
+int gsvk_t2s_batch_launches_per_step(gsvk_t2s_batch_t h) { return h ? h->launches_per_step : 0; }
+
+}  // extern "C"

@@ -324,6 +324,34 @@ int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_
  * activation load.  read_trace is synchronous. */
 int gsvk_t2s_set_trace(gsvk_t2s_t h, int enable);
 int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n);
+/* ---- batched T2S decode (config 3: concurrent utterances) -------------- */
+/* B <= max_batch utterances decode together: every step streams the weights
+ * once for all B tokens through tensor-core GEMMs (M = B), attends each
+ * utterance over its own cache length and samples each greedily (penalty
+ * 1.35 over its own history, 11-step EOS mask, no EOS stop).  fp16 GEMM
+ * operands: parity with the batch-1 path is at GEMM tolerance.  Each
+ * utterance has cfg->cap KV slots. */
+typedef struct gsvk_t2s_batch* gsvk_t2s_batch_t;
+int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w,
+                          int max_batch, int max_steps, gsvk_t2s_batch_t* out);
+int gsvk_t2s_batch_destroy(gsvk_t2s_batch_t h);
+/* HOST fp16 [L][src_rows][D] K/V into slots [0, len) of utterance b. */
+int gsvk_t2s_batch_load_kv(gsvk_t2s_batch_t h, int b, const uint16_t* k_host,
+                           const uint16_t* v_host, size_t len, size_t src_rows,
+                           gsvk_stream_t stream);
+/* HOST per-utterance cache lengths, PE origins, first input tokens and
+ * histories ([B][n_hist], -1 ignored); resets the step counter. */
+int gsvk_t2s_batch_begin(gsvk_t2s_batch_t h, int B, const int32_t* len, const int32_t* pe0,
+                         const int32_t* first_tok, const int32_t* hist, int n_hist,
+                         gsvk_stream_t stream);
+/* Runs `steps` steps (asynchronous); use_graph captures one step as a CUDA
+ * graph the first time and replays it. */
+int gsvk_t2s_batch_run(gsvk_t2s_batch_t h, int steps, int use_graph, gsvk_stream_t stream);
+/* HOST tokens / margins [steps][B] of the steps run since begin; synchronous. */
+int gsvk_t2s_batch_read(gsvk_t2s_batch_t h, int steps, int32_t* tokens, float* margins);
+int gsvk_t2s_batch_read_logits(gsvk_t2s_batch_t h, float* host_out);
+int gsvk_t2s_batch_launches_per_step(gsvk_t2s_batch_t h);
+
 /* The logits the last step sampled from (raw, before the penalty); synchronous. */
 int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out);
 
