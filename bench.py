@@ -500,8 +500,93 @@ def run_encoder(args, rank, local, world):
     return line
 
 
+# ------------------------------------------------- batched T2S decode (3)
+def run_t2s_batch(args, rank, local, world):
+    import numpy as np
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    B, S = 64, 32
+    m = g.workloads.t2s_model(seed=1)
+    lens = g.workloads.t2s_batched_lengths(B, seed=1)
+    cap = int(lens.max()) + S
+    rng = np.random.default_rng(1 + rank)
+    first = rng.integers(0, m["vocab"] - 1, size=B).astype(np.int32)
+    hist = first[:, None].copy()
+    eng = g.T2SBatch(m, cap=cap, max_batch=B, max_steps=S)
+    gen = torch.Generator(device=dev).manual_seed(1 + rank)
+    L, D = m["n_layers"], m["d_model"]
+    for b in range(B):  # KV prefix N(0,1) fp16, drawn on the device
+        k = torch.randn(L, int(lens[b]), D, generator=gen, device=dev).half()
+        v = torch.randn(L, int(lens[b]), D, generator=gen, device=dev).half()
+        eng.load_kv(b, k, v, int(lens[b]))
+    torch.cuda.synchronize(dev)
+
+    def one():
+        eng.begin(lens, lens, first, hist)
+        eng.run(S, use_graph=True)
+
+    eng.begin(lens, lens, first, hist)
+    eng.run(S, use_graph=False)  # eager once (attributes, descriptors), then graphs
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clocks = ClockSampler()
+    barrier(world)
+    clocks.start()
+    for i in range(args.steps):
+        eng.begin(lens, lens, first, hist)
+        ev[i][0].record(stream)
+        eng.run(S, use_graph=True)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    t = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) * 1e-3 / args.steps, world)
+    # e2e: host token ids in, host tokens out (begin copies the per-utterance state)
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.begin(lens, lens, first, hist)
+        eng.run(S, use_graph=True)
+        toks, _ = eng.read(S)
+    t_e2e = max_over_ranks(time.perf_counter() - t0, world) / args.steps
+    launches = eng.launches_per_step()
+    eng.close()
+    w_bytes = L * (3 * D * D + D * D + 2 * m["ffn"] * D) * 2 + m["vocab"] * D * 2
+    kv = L * 2 * D * 2
+    alg = sum(w_bytes + kv * int(np.sum(lens + s + 1)) + kv * B for s in range(S))
+    hbm, _, kind = measured_peaks()
+    tokens = B * S
+    line = {"metric": "batched T2S decode tokens/s (64 utterances per GPU)",
+            "value": tokens * world / t, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulate",
+            "data": "synthetic (N(0,0.02) weights, N(0,1) KV, lengths U{64..1024} seed 1)",
+            "config": {"workload": "t2s_decode_b64 (BASELINE configs[2])", "batch": B,
+                       "decode_steps_per_step": S, "mean_kv_len": float(lens.mean()),
+                       "global_batch": B * world, "parallelism": f"replicas x{world}",
+                       "l2": "1.9 GB of weights + KV streamed per decode step"},
+            "e2e": {"value": tokens * world / t_e2e, "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(lens.nbytes * 2 + first.nbytes + hist.nbytes),
+                    "d2h_bytes_per_step": tokens * 8, "timing": "host wall clock"},
+            "gpu_launches": launches * S * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph)",
+                         "achieved": alg / t / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": alg / t / 1e9 / hbm, "peak_source": kind, "traffic": None,
+                         "algorithmic_bytes_per_step": alg}}
+    if clk:
+        line["clocks"] = clk
+    return line
+
+
 WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder": run_decoder,
-             "encoder": run_encoder}
+             "encoder": run_encoder, "t2s_decode_b64": run_t2s_batch}
 
 
 def run_reference(args, rank, world):

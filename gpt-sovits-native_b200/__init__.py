@@ -582,8 +582,11 @@ class T2SBatch:
         self.B = 0
 
     def load_kv(self, b: int, k, v, length: int, stream=None):
-        check(lib().gsvk_t2s_batch_load_kv(self.h, b, k.ctypes.data, v.ctypes.data, length,
-                                           k.shape[1], _stream(stream)))
+        """k, v: [L, rows, D] fp16 bits, numpy (host) or torch (host or CUDA)."""
+        kp = k.ctypes.data if hasattr(k, "ctypes") else k.data_ptr()
+        vp = v.ctypes.data if hasattr(v, "ctypes") else v.data_ptr()
+        check(lib().gsvk_t2s_batch_load_kv(self.h, b, kp, vp, length, k.shape[1],
+                                           _stream(stream)))
 
     def begin(self, lengths, pe0, first_tok, hist=None, stream=None):
         import numpy as np

@@ -21,12 +21,40 @@ int check_launch(const char* kernel);
 int sm_count();
 
 inline cudaStream_t as_cuda(gsvk_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+// Launches `kernel` with a programmatic dependency on the previous kernel in
+// `st` (it may start while that kernel drains; it must call griddep_wait()
+// before reading that kernel's results).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               const char* name, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), name);
+}
 __host__ __device__ inline bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 inline unsigned ceil_div(size_t a, size_t b) { return static_cast<unsigned>((a + b - 1) / b); }
 
 // ---------------------------------------------------------------- device side
+// Programmatic dependent launch.  griddep_wait() blocks until the kernels this
+// launch depends on have completed and their writes are visible (a no-op when
+// the launch carries no programmatic dependency); griddep_launch_dependents()
+// lets the next kernel in the stream begin its independent prologue.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
@@ -69,12 +97,18 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Epilogue activation (GSVK_ACT_*), identical expressions to the reference:
 // relu kern.cpp:85, gelu_erf bert_ops.hpp:25, leaky nn_ops.hpp:48, tanh dec.hpp:344.
+// The transcendental cases live in one out-of-line function: epilogues unroll
+// apply_act per element, and inlining erff / tanhf into every copy makes
+// those loops overflow the instruction cache.
+static __device__ __noinline__ float apply_act_transcendental(float v, int act) {
+  return act == GSVK_ACT_GELU_ERF ? 0.5f * v * (1.f + erff(v * 0.70710678118654752440f)) : tanhf(v);
+}
 __device__ __forceinline__ float apply_act(float v, int act, float slope) {
   switch (act) {
     case GSVK_ACT_RELU: return v > 0.f ? v : 0.f;
-    case GSVK_ACT_GELU_ERF: return 0.5f * v * (1.f + erff(v * 0.70710678118654752440f));
     case GSVK_ACT_LEAKY: return v < 0.f ? v * slope : v;
-    case GSVK_ACT_TANH: return tanhf(v);
+    case GSVK_ACT_GELU_ERF:
+    case GSVK_ACT_TANH: return apply_act_transcendental(v, act);
     default: return v;
   }
 }

@@ -128,7 +128,11 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const TcProblem p, const TcEpilogue e, int stages, uint32_t* status) {
+                   const TcProblem prob, const TcEpilogue epi, int stages, uint32_t* status) {
+  // Register copies of the parameter structs (see gemm_skinny.cu: references
+  // into parameter space are re-read after every global store).
+  const TcProblem p = prob;
+  const TcEpilogue e = epi;
   constexpr uint32_t kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
   const int bk = p.bk;
   const uint32_t swz_bytes = static_cast<uint32_t>(bk) * 2;          // 32, 64 or 128
@@ -308,7 +312,8 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
 // per (row, 16-column group), fp32 FMA over K, the same epilogue.
 __global__ void gemm_simt_kernel(const uint16_t* __restrict__ a, long long lda,
                                  const uint16_t* __restrict__ b, long long ldb, int M, int N, int K,
-                                 const TcEpilogue e) {
+                                 const TcEpilogue epi) {
+  const TcEpilogue e = epi;  // register copy (stores below must not re-read parameter space)
   const int groups = (N + 15) / 16;
   const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (idx >= static_cast<long long>(M) * groups) return;
@@ -444,6 +449,11 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   if (g->K % 8 != 0 || g->lda % 8 != 0 || g->ldb % 8 != 0 || !aligned16(g->a) ||
       !aligned16(g->b))
     return simt_gemm(g, e, as_cuda(stream));  // odd K (conv K=7/9, test shapes)
+  // few rows (decode steps, the FFN-up of one 128-token chunk): split-K cluster kernel
+  if (skinny_fits((long long)g->M, (long long)g->N, (long long)g->K, (long long)g->lda,
+                  (long long)g->ldb, g->a, g->b))
+    return skinny_run(g->a, (int)g->M, (long long)g->lda, g->b, (int)g->N, (long long)g->ldb,
+                      (int)g->K, e, as_cuda(stream), false);
   TcProblem p{};
   p.M = (int)g->M;
   p.N = (int)g->N;

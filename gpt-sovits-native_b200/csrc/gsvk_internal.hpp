@@ -24,6 +24,14 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
            long long b_rows, long long ldb, TcProblem p, const TcEpilogue& e, int bn,
            cudaStream_t st, long long a_cols = 0, long long b_cols = 0);
 TcEpilogue make_epilogue();
+// Split-K cluster GEMM for few-row activations (gemm_skinny.cu):
+// C[m, n] = epi(sum_k x[m, k] w[n, k]) for M <= 128; pdl = launch with a
+// programmatic dependency on the previous kernel in the stream; force_split
+// (a power of two <= 8) overrides the K split chosen from the shape.
+bool skinny_fits(long long M, long long N, long long K, long long ldx, long long ldw,
+                 const void* x, const void* w);
+int skinny_run(const uint16_t* x, int M, long long ldx, const uint16_t* w, int N, long long ldw,
+               int K, const TcEpilogue& e, cudaStream_t st, bool pdl, int force_split = 0);
 // CUDA-core fallback for shapes the TMA path cannot express (K or leading
 // dimensions not multiples of 8, unaligned bases).
 int simt_gemm(const gsvk_gemm_args* g, const TcEpilogue& e, cudaStream_t st);

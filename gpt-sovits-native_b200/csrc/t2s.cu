@@ -1071,12 +1071,12 @@ int gsvk_t2s_load_kv(gsvk_t2s_t h, const uint16_t* k_host, const uint16_t* v_hos
   for (int l = 0; l < h->L && prefix; ++l) {
     int rc = check_cuda(cudaMemcpyAsync(h->dev.kc + (size_t)l * h->cap * h->D,
                                         k_host + (size_t)l * src_rows * h->D, prefix * row,
-                                        cudaMemcpyHostToDevice, as_cuda(stream)),
+                                        cudaMemcpyDefault, as_cuda(stream)),
                         "t2s_load_kv k");
     if (rc) return rc;
     rc = check_cuda(cudaMemcpyAsync(h->dev.vc + (size_t)l * h->cap * h->D,
                                     v_host + (size_t)l * src_rows * h->D, prefix * row,
-                                    cudaMemcpyHostToDevice, as_cuda(stream)),
+                                    cudaMemcpyDefault, as_cuda(stream)),
                     "t2s_load_kv v");
     if (rc) return rc;
   }

@@ -5,7 +5,7 @@
 // One decode step streams every weight matrix once for all B tokens: the
 // projections run as tensor-core GEMMs with M = B (gemm_tc.cuh, narrow
 // 32-column tiles so that enough CTAs pull weights from HBM), the attention
-// as one CTA per (utterance, head) over that utterance's ragged cache, and
+// as split-KV chunks of 32 keys over each utterance's ragged cache, and
 // sampling as one CTA per utterance (repetition penalty over its own
 // history, 11-step EOS mask, t2s_engine.cpp:1594-1636).  The per-step
 // positions come from a device step counter, so one captured CUDA graph
@@ -25,8 +25,8 @@ namespace gsvk {
 
 namespace {
 
-constexpr int kAttnThreads = 128;
-constexpr int kMaxKeys = 4096;  // per-utterance slots the attention kernel keeps in shared memory
+constexpr int kAttnThreads = 256;
+constexpr int kAttnChunk = 32;  // keys per attention CTA (split-KV)
 
 struct BatchDev {
   int L, D, H, F, V, HD, cap, B, max_steps;
@@ -47,6 +47,7 @@ __global__ void batch_embed_kernel(BatchDev m, float* __restrict__ x32, uint16_t
   const int b = blockIdx.x, D = m.D;
   const int s = *m.step;
   if (s >= m.max_steps) return;  // past the buffers: no-op
+  griddep_launch_dependents();
   const uint16_t* er = m.emb + static_cast<size_t>(m.tok[b]) * D;
   const float* pr = m.pe + static_cast<size_t>(m.base_pe[b] + s) * D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -56,83 +57,185 @@ __global__ void batch_embed_kernel(BatchDev m, float* __restrict__ x32, uint16_t
   }
 }
 
-// K/V append at slot base_len[b] + step and one-query attention over
-// [0, base_len[b] + step] for head h of utterance b.
+// Split-KV one-query attention (flash-decoding).  CTA (c, b) takes keys
+// [32c, 32c + 32) of utterance b for ALL heads: the chunk's K and V rows are
+// contiguous in the [b][L][cap][D] cache, so two 1D bulk copies bring them
+// into shared memory at full HBM efficiency.  A warp reads 256 halves of a
+// row (16 bytes per lane, conflict-free); lanes sharing a head reduce with
+// shuffles.  The chunk that holds the new slot (base_len[b] + step) appends
+// the step's K/V row to the cache and to its shared copy.  Each chunk writes
+// (max, sum, unnormalised output) per head; the chunk that takes the last
+// ticket of its utterance merges them — no CTA waits on another.
 __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(BatchDev m, int l,
                                                                   const float* __restrict__ qkv,
-                                                                  uint16_t* __restrict__ out16) {
-  __shared__ float sc[kMaxKeys];
-  __shared__ float red[kAttnThreads / 32];
-  __shared__ float q[64];
-  __shared__ float part[kAttnThreads / 32][64];
-  const int b = blockIdx.x, h = blockIdx.y, HD = m.HD, D = m.D;
-  if (*m.step >= m.max_steps) return;
-  const int pos = m.base_len[b] + *m.step;
+                                                                  uint16_t* __restrict__ out16,
+                                                                  float* __restrict__ part_o,
+                                                                  float2* __restrict__ part_ml,
+                                                                  unsigned* __restrict__ ticket,
+                                                                  int max_chunks,
+                                                                  uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  __shared__ uint64_t bars[2];
+  __shared__ int is_last;
+  const int D = m.D, H = m.H, HD = m.HD;
+  const int b = blockIdx.y, c = blockIdx.x;
+  const int s = *m.step;
+  if (s >= m.max_steps) return;
+  const int pos = m.base_len[b] + s;
   const int len = pos + 1;
-  const size_t slab = (static_cast<size_t>(b) * m.L + l) * m.cap;
-  uint16_t* kb = m.kc + slab * D + h * HD;
-  uint16_t* vb = m.vc + slab * D + h * HD;
+  const int nchunks = (len + kAttnChunk - 1) / kAttnChunk;
+  if (c >= nchunks) return;
+  const int k0 = c * kAttnChunk;
+  const int rows = min(kAttnChunk, len - k0);
+  uint16_t* sK = reinterpret_cast<uint16_t*>(attn_smem);
+  uint16_t* sV = sK + kAttnChunk * D;
+  float* sP = reinterpret_cast<float*>(sV + kAttnChunk * D);  // [H][kAttnChunk + 1]
+  float* sM = sP + H * (kAttnChunk + 1);
+  float* sL = sM + H;
+  float* sPart = reinterpret_cast<float*>(sK);  // PV partials reuse the K buffer
+  const size_t slab = (static_cast<size_t>(b) * m.L + l) * m.cap + k0;
+  uint16_t* kg = m.kc + slab * D;
+  uint16_t* vg = m.vc + slab * D;
   const float* qrow = qkv + static_cast<size_t>(b) * 3 * D;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid < HD) {
-    q[tid] = qrow[h * HD + tid];
-    kb[static_cast<size_t>(pos) * D + tid] = f2h(qrow[D + h * HD + tid]);
-    vb[static_cast<size_t>(pos) * D + tid] = f2h(qrow[2 * D + h * HD + tid]);
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_barrier_init();
+    const uint32_t bytes = static_cast<uint32_t>(rows) * D * 2;
+    mbar_arrive_expect_tx(&bars[0], bytes);
+    bulk_load(sK, kg, bytes, &bars[0]);
+    mbar_arrive_expect_tx(&bars[1], bytes);
+    bulk_load(sV, vg, bytes, &bars[1]);
   }
+  griddep_wait();  // q and the new K/V row come from the QKV projection
+  griddep_launch_dependents();
+  // lane geometry: a warp covers segment `seg` (256 halves) of rows rg, rg + nrg, ...
+  const int nseg = D / 256, nrg = (kAttnThreads / 32) / nseg;
+  const int seg = warp % nseg, rg = warp / nseg;
+  const int e0 = seg * 256 + lane * 8;
+  const int lph = HD / 8, head = e0 / HD;
+  float q[8];
+  {
+    const float4 q0 = *reinterpret_cast<const float4*>(qrow + e0);
+    const float4 q1 = *reinterpret_cast<const float4*>(qrow + e0 + 4);
+    q[0] = q0.x * m.scale; q[1] = q0.y * m.scale; q[2] = q0.z * m.scale; q[3] = q0.w * m.scale;
+    q[4] = q1.x * m.scale; q[5] = q1.y * m.scale; q[6] = q1.z * m.scale; q[7] = q1.w * m.scale;
+  }
+  // the new slot pos = len - 1 is row rows - 1 of the last chunk; no other chunk touches it
+  const int r_new = (c == nchunks - 1) ? rows - 1 : -1;
   __syncthreads();
-  float mx = -INFINITY;
-  for (int k = tid; k < len; k += kAttnThreads) {
-    const uint16_t* kr = kb + static_cast<size_t>(k) * D;
-    float d = 0.f;
-    for (int e = 0; e < HD; e += 8) {
-      float kf[8];
-      unpack8(*reinterpret_cast<const uint4*>(kr + e), kf);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) d = fmaf(q[e + u], kf[u], d);
+  if (!__syncthreads_and(mbar_wait(&bars[0], 0, status))) return;
+  if (r_new >= 0) {
+    for (int i = tid; i < D; i += kAttnThreads) {
+      const uint16_t kv = f2h(qrow[D + i]);
+      sK[r_new * D + i] = kv;
+      kg[static_cast<size_t>(r_new) * D + i] = kv;
     }
-    d *= m.scale;
-    sc[k] = d;
-    mx = fmaxf(mx, d);
+    __syncthreads();
   }
-  mx = warp_max(mx);
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  mx = red[0];
-  for (int w = 1; w < kAttnThreads / 32; ++w) mx = fmaxf(mx, red[w]);
-  __syncthreads();
-  float sum = 0.f;
-  for (int k = tid; k < len; k += kAttnThreads) {
-    const float e = expf(sc[k] - mx);
-    sc[k] = e;
-    sum += e;
+  for (int r = rg; r < rows; r += nrg) {
+    float kf[8];
+    unpack8(*reinterpret_cast<const uint4*>(sK + r * D + e0), kf);
+    float d = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d = fmaf(q[j], kf[j], d);
+    for (int o = 1; o < lph; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if ((lane & (lph - 1)) == 0) sP[head * (kAttnChunk + 1) + r] = d;
   }
-  sum = warp_sum(sum);
-  if (lane == 0) red[warp] = sum;
   __syncthreads();
-  sum = 0.f;
-  for (int w = 0; w < kAttnThreads / 32; ++w) sum += red[w];
-  // P . V: warp w takes keys w, w+4, ...; lane = dimension (and +32)
-  float o0 = 0.f, o1 = 0.f;
-  for (int k = warp; k < len; k += kAttnThreads / 32) {
-    const uint16_t* vr = vb + static_cast<size_t>(k) * D;
-    const float p = sc[k];
-    o0 = fmaf(p, h2f(vr[lane]), o0);
-    if (HD > 32) o1 = fmaf(p, h2f(vr[32 + lane]), o1);
+  for (int h = warp; h < H; h += kAttnThreads / 32) {
+    float* ph = sP + h * (kAttnChunk + 1);
+    float mx = -INFINITY;
+    for (int r = lane; r < rows; r += 32) mx = fmaxf(mx, ph[r]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int r = lane; r < rows; r += 32) {
+      const float p = expf(ph[r] - mx);
+      ph[r] = p;
+      sum += p;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) {
+      sM[h] = mx;
+      sL[h] = sum;
+    }
   }
-  part[warp][lane] = o0;
-  if (HD > 32) part[warp][32 + lane] = o1;
+  if (!__syncthreads_and(mbar_wait(&bars[1], 0, status))) return;
+  if (r_new >= 0) {
+    for (int i = tid; i < D; i += kAttnThreads) {
+      const uint16_t vv = f2h(qrow[2 * D + i]);
+      sV[r_new * D + i] = vv;
+      vg[static_cast<size_t>(r_new) * D + i] = vv;
+    }
+    __syncthreads();
+  }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int r = rg; r < rows; r += nrg) {
+    const float p = sP[head * (kAttnChunk + 1) + r];
+    float vf[8];
+    unpack8(*reinterpret_cast<const uint4*>(sV + r * D + e0), vf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = fmaf(p, vf[j], acc[j]);
+  }
+  float4* pw = reinterpret_cast<float4*>(sPart + warp * 256 + lane * 8);
+  pw[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  pw[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   __syncthreads();
-  if (tid < HD) {
+  const size_t pc = static_cast<size_t>(b) * max_chunks;
+  for (int i = tid; i < D; i += kAttnThreads) {
+    const int sg = i >> 8, w = i & 255;
     float o = 0.f;
-    for (int w = 0; w < kAttnThreads / 32; ++w) o += part[w][tid];
-    out16[static_cast<size_t>(b) * D + h * HD + tid] = f2h(o / sum);
+    for (int g = 0; g < nrg; ++g) o += sPart[(g * nseg + sg) * 256 + w];
+    if (nchunks == 1)
+      out16[static_cast<size_t>(b) * D + i] = f2h(o / sL[i / HD]);
+    else
+      part_o[(pc + c) * D + i] = o;
   }
+  if (nchunks == 1) return;
+  if (tid < H) part_ml[(pc + c) * H + tid] = make_float2(sM[tid], sL[tid]);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(&ticket[b], 1u) == static_cast<unsigned>(nchunks - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // merge: out = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c, per head
+  if (tid < H) {
+    float M = -INFINITY;
+    for (int cc = 0; cc < nchunks; ++cc) M = fmaxf(M, __ldcg(&part_ml[(pc + cc) * H + tid]).x);
+    float den = 0.f;
+    for (int cc = 0; cc < nchunks; ++cc) {
+      const float2 ml = __ldcg(&part_ml[(pc + cc) * H + tid]);
+      den = fmaf(expf(ml.x - M), ml.y, den);
+    }
+    sM[tid] = M;
+    sL[tid] = den;
+  }
+  __syncthreads();
+  for (int i = tid; i < D; i += kAttnThreads) {
+    const int h = i / HD;
+    const float M = sM[h];
+    float num = 0.f;
+    for (int cc = 0; cc < nchunks; ++cc)
+      num = fmaf(expf(__ldcg(&part_ml[(pc + cc) * H + h]).x - M), __ldcg(&part_o[(pc + cc) * D + i]),
+                 num);
+    out16[static_cast<size_t>(b) * D + i] = f2h(num / sL[h]);
+  }
+  if (tid == 0) ticket[b] = 0;
+}
+
+size_t attn_smem_bytes(int D, int H) {
+  return static_cast<size_t>(kAttnChunk) * D * 2 * 2 +
+         (static_cast<size_t>(H) * (kAttnChunk + 1) + 2 * H) * 4;
 }
 
 __global__ void batch_ln_kernel(const float* __restrict__ x, const float* __restrict__ g,
                                 const float* __restrict__ bta, float* __restrict__ y,
                                 uint16_t* __restrict__ y16, int n, double eps) {
   __shared__ double sh[64];
+  griddep_wait();
+  griddep_launch_dependents();
   const float* xr = x + static_cast<size_t>(blockIdx.x) * n;
   float s = 0.f, q = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -171,6 +274,7 @@ __global__ void batch_sample_kernel(BatchDev m, const float* __restrict__ logits
   __shared__ float rs[32];
   __shared__ int ri[32];
   const int b = blockIdx.x, V = m.V;
+  griddep_wait();
   const int s = *m.step;
   if (s >= m.max_steps) return;
   const int limit = s >= 11 ? V : V - 1;
@@ -243,6 +347,10 @@ struct T2SBatchEngine {
           *tokens_out = nullptr;
   float* margins = nullptr;
   unsigned* done = nullptr;
+  unsigned* ticket = nullptr;  // [B] attention merge tickets (zero between launches)
+  float* part_o = nullptr;     // [B][max_chunks][D] per-chunk attention outputs
+  float2* part_ml = nullptr;   // [B][max_chunks][H] per-chunk (max, sum)
+  int max_chunks = 0;
   uint8_t* seen = nullptr;
   float *x32 = nullptr, *qkv32 = nullptr, *hpre32 = nullptr, *h32 = nullptr, *xpre32 = nullptr,
         *logits = nullptr;
@@ -276,7 +384,8 @@ int gemm_m(const uint16_t* A, int M, int K, const uint16_t* W, int N, const floa
   e.ld_c32 = N;
   e.c16 = c16;
   e.ld_c16 = N;
-  // 32-column tiles: N/32 CTAs stream the weight matrix (M = batch <= 128)
+  if (skinny_fits(M, N, K, K, K, A, W)) return skinny_run(A, M, K, W, N, K, K, e, st, true);
+  // 32-column tiles: N/32 CTAs stream the weight matrix
   return tc_run(A, M, K, W, N, K, p, e, 32, st);
 }
 
@@ -291,30 +400,36 @@ int batch_step(T2SBatchEngine* e, int B, cudaStream_t st, int* launches) {
     if ((rc = gemm_m(e->x16, B, D, m.wqkv + (size_t)l * 3 * D * D, 3 * D,
                      m.bqkv + (size_t)l * 3 * D, GSVK_ACT_NONE, nullptr, e->qkv32, nullptr, st)))
       return rc;
-    batch_attn_kernel<<<dim3(B, m.H), kAttnThreads, 0, st>>>(m, l, e->qkv32, e->attn16);
-    if ((rc = check_launch("batch_attn_kernel"))) return rc;
+    if ((rc = launch_pdl(batch_attn_kernel, dim3(e->max_chunks, B), dim3(kAttnThreads),
+                         attn_smem_bytes(D, m.H), st, "batch_attn_kernel", m, l, e->qkv32,
+                         e->attn16, e->part_o, e->part_ml, e->ticket, e->max_chunks,
+                         device_status())))
+      return rc;
     if ((rc = gemm_m(e->attn16, B, D, m.wout + (size_t)l * D * D, D, m.bout + (size_t)l * D,
                      GSVK_ACT_NONE, e->x32, e->hpre32, nullptr, st)))
       return rc;
-    batch_ln_kernel<<<B, 256, 0, st>>>(e->hpre32, m.n1g + (size_t)l * D, m.n1b + (size_t)l * D,
-                                       e->h32, e->h16, D, m.eps);
-    if ((rc = check_launch("batch_ln_kernel"))) return rc;
+    if ((rc = launch_pdl(batch_ln_kernel, dim3(B), dim3(256), 0, st, "batch_ln_kernel", e->hpre32,
+                         m.n1g + (size_t)l * D, m.n1b + (size_t)l * D, e->h32, e->h16, D,
+                         static_cast<double>(m.eps))))
+      return rc;
     if ((rc = gemm_m(e->h16, B, D, m.w1 + (size_t)l * F * D, F, m.b1 + (size_t)l * F,
                      GSVK_ACT_RELU, nullptr, nullptr, e->ff16, st)))
       return rc;
     if ((rc = gemm_m(e->ff16, B, F, m.w2 + (size_t)l * D * F, D, m.b2 + (size_t)l * D,
                      GSVK_ACT_NONE, e->h32, e->xpre32, nullptr, st)))
       return rc;
-    batch_ln_kernel<<<B, 256, 0, st>>>(e->xpre32, m.n2g + (size_t)l * D, m.n2b + (size_t)l * D,
-                                       e->x32, e->x16, D, m.eps);
-    if ((rc = check_launch("batch_ln_kernel"))) return rc;
+    if ((rc = launch_pdl(batch_ln_kernel, dim3(B), dim3(256), 0, st, "batch_ln_kernel", e->xpre32,
+                         m.n2g + (size_t)l * D, m.n2b + (size_t)l * D, e->x32, e->x16, D,
+                         static_cast<double>(m.eps))))
+      return rc;
     n += 7;
   }
   if ((rc = gemm_m(e->x16, B, D, m.wpred, m.V, nullptr, GSVK_ACT_NONE, nullptr, e->logits,
                    nullptr, st)))
     return rc;
-  batch_sample_kernel<<<B, 256, 0, st>>>(m, e->logits, e->done);
-  if ((rc = check_launch("batch_sample_kernel"))) return rc;
+  if ((rc = launch_pdl(batch_sample_kernel, dim3(B), dim3(256), 0, st, "batch_sample_kernel", m,
+                       e->logits, e->done)))
+    return rc;
   n += 2;
   if (launches) *launches = n;
   return GSVK_OK;
@@ -364,9 +479,11 @@ int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weight
       max_batch > 128 || max_steps <= 0)
     return fail(GSVK_ERR_INVALID, "t2s_batch_create: bad dimensions");
   const int HD = D / H;
-  if ((HD != 32 && HD != 64) || D % 64 || F % 64 || cap > kMaxKeys)
-    return fail(GSVK_ERR_UNSUPPORTED, "t2s_batch_create: head_dim 32/64, D and F multiples of 64, "
-                "cap <= %d", kMaxKeys);
+  if ((HD != 32 && HD != 64) || (D != 256 && D != 512 && D != 1024 && D != 2048) || F % 64)
+    return fail(GSVK_ERR_UNSUPPORTED,
+                "t2s_batch_create: head_dim 32/64, d_model 256/512/1024/2048, ffn multiple of 64");
+  if (attn_smem_bytes(D, H) > 200 * 1024)
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s_batch_create: attention chunk exceeds shared memory");
   if (!w->wqkv || !w->bqkv || !w->wout || !w->bout || !w->w1 || !w->b1 || !w->w2 || !w->b2 ||
       !w->n1g || !w->n1b || !w->n2g || !w->n2b || !w->wpred || !w->audio_emb)
     return fail(GSVK_ERR_INVALID, "t2s_batch_create: null weight");
@@ -429,6 +546,9 @@ int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weight
                o_qkv = take(B * 3 * D * 4), o_hp = take(B * D * 4), o_h32 = take(B * D * 4),
                o_xp = take(B * D * 4), o_lg = take(B * V * 4), o_x16 = take(B * D * 2),
                o_a16 = take(B * D * 2), o_h16 = take(B * D * 2), o_ff = take(B * F * 2);
+  const int max_chunks = (cap + kAttnChunk - 1) / kAttnChunk;
+  const size_t o_tk = take(B * 4), o_po = take(B * max_chunks * D * 4),
+               o_pm = take(B * max_chunks * H * 8);
   if (cudaMalloc(&e->amem, off) != cudaSuccess) {
     cudaGetLastError();
     gsvk_t2s_batch_destroy(e);
@@ -459,6 +579,17 @@ int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weight
   e->attn16 = reinterpret_cast<uint16_t*>(a + o_a16);
   e->h16 = reinterpret_cast<uint16_t*>(a + o_h16);
   e->ff16 = reinterpret_cast<uint16_t*>(a + o_ff);
+  e->ticket = reinterpret_cast<unsigned*>(a + o_tk);
+  e->part_o = reinterpret_cast<float*>(a + o_po);
+  e->part_ml = reinterpret_cast<float2*>(a + o_pm);
+  e->max_chunks = max_chunks;
+  if (int rc = check_cuda(cudaFuncSetAttribute(batch_attn_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(attn_smem_bytes(D, H))),
+                          "attention smem attribute")) {
+    gsvk_t2s_batch_destroy(e);
+    return rc;
+  }
   d.base_len = e->base_len;
   d.base_pe = e->base_pe;
   d.step = e->step;
@@ -480,11 +611,11 @@ int gsvk_t2s_batch_load_kv(gsvk_t2s_batch_t h, int b, const uint16_t* k_host,
   for (int l = 0; l < d.L && len; ++l) {
     const size_t dst = (((size_t)b * d.L + l) * d.cap) * d.D;
     int rc = check_cuda(cudaMemcpyAsync(d.kc + dst, k_host + (size_t)l * src_rows * d.D,
-                                        len * d.D * 2, cudaMemcpyHostToDevice, as_cuda(stream)),
+                                        len * d.D * 2, cudaMemcpyDefault, as_cuda(stream)),
                         "batch kv k");
     if (rc) return rc;
     rc = check_cuda(cudaMemcpyAsync(d.vc + dst, v_host + (size_t)l * src_rows * d.D, len * d.D * 2,
-                                    cudaMemcpyHostToDevice, as_cuda(stream)),
+                                    cudaMemcpyDefault, as_cuda(stream)),
                     "batch kv v");
     if (rc) return rc;
   }

@@ -281,8 +281,8 @@ typedef struct {
 } gsvk_t2s_host_weights;
 int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, gsvk_t2s_t* out);
 int gsvk_t2s_destroy(gsvk_t2s_t h);
-/* Copies a KV prefix (HOST, fp16 [L][src_rows][D] for K and V) into slots
- * [0, prefix) of every layer's cache. */
+/* Copies a KV prefix (fp16 [L][src_rows][D] for K and V, host or device
+ * memory) into slots [0, prefix) of every layer's cache. */
 int gsvk_t2s_load_kv(gsvk_t2s_t h, const uint16_t* k_host, const uint16_t* v_host, size_t prefix,
                      size_t src_rows, gsvk_stream_t stream);
 /* block_prefill (t2s_engine.cpp:881-1034) over all layers, in place on the
@@ -335,7 +335,8 @@ typedef struct gsvk_t2s_batch* gsvk_t2s_batch_t;
 int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w,
                           int max_batch, int max_steps, gsvk_t2s_batch_t* out);
 int gsvk_t2s_batch_destroy(gsvk_t2s_batch_t h);
-/* HOST fp16 [L][src_rows][D] K/V into slots [0, len) of utterance b. */
+/* fp16 [L][src_rows][D] K/V (host or device memory) into slots [0, len) of
+ * utterance b. */
 int gsvk_t2s_batch_load_kv(gsvk_t2s_batch_t h, int b, const uint16_t* k_host,
                            const uint16_t* v_host, size_t len, size_t src_rows,
                            gsvk_stream_t stream);

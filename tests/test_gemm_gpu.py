@@ -90,6 +90,25 @@ def test_gemm_fused_epilogue(dev, ora, act):
     np.testing.assert_array_equal(c16.cpu().numpy(), got.astype(np.float16))
 
 
+@pytest.mark.parametrize("M,N,K", [(64, 1536, 512), (64, 512, 2048), (7, 1025, 512),
+                                   (128, 2048, 512), (256, 640, 4096)])
+def test_gemm_few_rows_fused_epilogue(dev, ora, M, N, K):
+    """Decode-step shapes (M = batch): the split-K cluster kernel with bias,
+    ReLU, residual and both output precisions against the oracle."""
+    rng = np.random.default_rng(M + N + K)
+    a, w = rand16(rng, (M, K), 1.0), rand16(rng, (N, K), 0.05)
+    bias = rng.standard_normal(N).astype(np.float32) * 0.1
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    c = torch.empty(M, N, device="cuda")
+    c16 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    dev.gemm_ex(h(a), h(w), bias=f(bias), residual=f(res), act=1, c=c, c_f16=c16)
+    ref = ora.linear_f16(ora.f16_to_f32(a), w, bias, 1) + res
+    got = c.cpu().numpy()
+    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
+    np.testing.assert_array_equal(c16.cpu().numpy(), got.astype(np.float16))
+    assert dev.device_status() == 0
+
+
 def test_gemm_strided_operands(dev, ora):
     """Leading dimensions larger than K (sub-matrix views, e.g. per-head slices)."""
     rng = np.random.default_rng(5)
