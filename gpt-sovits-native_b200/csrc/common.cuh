@@ -113,4 +113,23 @@ __device__ __forceinline__ float apply_act(float v, int act, float slope) {
   }
 }
 
+// Activation over a small register array with the dispatch hoisted out of
+// the element loop (keeps unrolled epilogue bodies small).
+template <int NV>
+__device__ __forceinline__ void act_array(float* v, int act, float slope) {
+  switch (act) {
+    case GSVK_ACT_NONE: break;
+    case GSVK_ACT_RELU:
+#pragma unroll
+      for (int j = 0; j < NV; ++j) v[j] = v[j] > 0.f ? v[j] : 0.f;
+      break;
+    case GSVK_ACT_LEAKY:
+#pragma unroll
+      for (int j = 0; j < NV; ++j) v[j] = v[j] < 0.f ? v[j] * slope : v[j];
+      break;
+    default:
+      for (int j = 0; j < NV; ++j) v[j] = apply_act_transcendental(v[j], act);
+  }
+}
+
 }  // namespace gsvk

@@ -106,14 +106,14 @@ __device__ __forceinline__ SkOps sk_ops(const SkProblem& p, const TcEpilogue& e,
 }
 __device__ __forceinline__ void sk_store4(const SkProblem& p, const TcEpilogue& e, int m, int n0,
                                           float4 acc, const SkOps& o) {
-  float v[4] = {acc.x, acc.y, acc.z, acc.w};
-  const float* b = &o.bias.x;
-  const float* r = &o.res.x;
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    v[u] = v[u] * e.alpha + b[u];
-    if (e.act != GSVK_ACT_NONE) v[u] = apply_act(v[u], e.act, e.slope);
-    if (e.residual) v[u] = fmaf(e.res_scale, r[u], v[u]);
+  float v[4] = {fmaf(acc.x, e.alpha, o.bias.x), fmaf(acc.y, e.alpha, o.bias.y),
+                fmaf(acc.z, e.alpha, o.bias.z), fmaf(acc.w, e.alpha, o.bias.w)};
+  act_array<4>(v, e.act, e.slope);
+  if (e.residual) {
+    v[0] = fmaf(e.res_scale, o.res.x, v[0]);
+    v[1] = fmaf(e.res_scale, o.res.y, v[1]);
+    v[2] = fmaf(e.res_scale, o.res.z, v[2]);
+    v[3] = fmaf(e.res_scale, o.res.w, v[3]);
   }
   const bool full = n0 + 3 < p.N;
   if (e.c32) {
@@ -136,26 +136,51 @@ __device__ __forceinline__ void sk_store4(const SkProblem& p, const TcEpilogue& 
     }
   }
   if (e.c16_act) {
+    act_array<4>(v, e.act2, e.slope2);
     uint16_t* d = e.c16_act + m * e.ld_c16_act + n0;
-    uint16_t h[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) h[u] = f2h(apply_act(v[u], e.act2, e.slope2));
     if (full && p.v_c16a) {
-      *reinterpret_cast<uint2*>(d) = make_uint2(h[0] | (static_cast<uint32_t>(h[1]) << 16),
-                                                h[2] | (static_cast<uint32_t>(h[3]) << 16));
+      *reinterpret_cast<uint2*>(d) = make_uint2(f2h(v[0]) | (static_cast<uint32_t>(f2h(v[1])) << 16),
+                                                f2h(v[2]) | (static_cast<uint32_t>(f2h(v[3])) << 16));
     } else {
       for (int u = 0; u < 4; ++u)
-        if (n0 + u < p.N) d[u] = h[u];
+        if (n0 + u < p.N) d[u] = f2h(v[u]);
     }
   }
 }
-__device__ __forceinline__ void sk_store1(const TcEpilogue& e, int m, int n, float acc, float bias) {
-  float v = acc * e.alpha + bias;
-  if (e.act != GSVK_ACT_NONE) v = apply_act(v, e.act, e.slope);
-  if (e.residual) v = fmaf(e.res_scale, e.residual[m * e.ld_res + n], v);
-  if (e.c32) e.c32[m * e.ld_c32 + n] = v;
-  if (e.c16) e.c16[m * e.ld_c16 + n] = f2h(v);
-  if (e.c16_act) e.c16_act[m * e.ld_c16_act + n] = f2h(apply_act(v, e.act2, e.slope2));
+
+// Split-1 epilogue: output column n, rows m0 .. m0+15 (one TMEM chunk).
+__device__ __forceinline__ void sk_store_col16(const SkProblem& p, const TcEpilogue& e, int m0,
+                                               int n, const uint32_t* r, float bias) {
+  float v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = fmaf(__uint_as_float(r[j]), e.alpha, bias);
+  act_array<16>(v, e.act, e.slope);
+  const int nm = min(16, p.M - m0);
+  if (e.residual) {
+    const float* rr = e.residual + static_cast<long long>(m0) * e.ld_res + n;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nm) v[j] = fmaf(e.res_scale, rr[j * e.ld_res], v[j]);
+  }
+  if (e.c32) {
+    float* d = e.c32 + static_cast<long long>(m0) * e.ld_c32 + n;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nm) d[j * e.ld_c32] = v[j];
+  }
+  if (e.c16) {
+    uint16_t* d = e.c16 + static_cast<long long>(m0) * e.ld_c16 + n;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nm) d[j * e.ld_c16] = f2h(v[j]);
+  }
+  if (e.c16_act) {
+    act_array<16>(v, e.act2, e.slope2);
+    uint16_t* d = e.c16_act + static_cast<long long>(m0) * e.ld_c16_act + n;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nm) d[j * e.ld_c16_act] = f2h(v[j]);
+  }
 }
 
 // Shared memory (1 KB aligned): recv [split][Mp][rows_per] fp32 (filled by
@@ -172,9 +197,10 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   extern __shared__ uint8_t sk_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sk_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  __shared__ uint64_t full[8];
+  __shared__ uint64_t full[8], empty[8];
   __shared__ uint64_t done, recv_bar;
   __shared__ uint32_t tmem_slot;
+  __shared__ int ok_flag;
   constexpr uint32_t w_bytes = kSkTileN * kSkBK * 2;  // 16 KB
   const uint32_t x_bytes = static_cast<uint32_t>(p.Mp) * kSkBK * 2;
   const uint32_t stage_bytes = w_bytes + x_bytes;
@@ -191,11 +217,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   const int kb0 = static_cast<int>((static_cast<long long>(rank) * p.kb_total) / p.split);
   const int kb1 = static_cast<int>((static_cast<long long>(rank + 1) * p.kb_total) / p.split);
   const int nkb = kb1 - kb0;
+  const int nst = min(nkb, p.stages);  // stage buffers (a ring when nkb > nst)
   const int rows_per = kSkTileN / p.split;  // >= 16
   const uint32_t slice_bytes = tile_bytes / static_cast<uint32_t>(p.split);
 
   if (tid == 0) {
-    for (int s = 0; s < nkb; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
     mbar_init(&done, 1);
     mbar_init(&recv_bar, 1);
     fence_barrier_init();
@@ -219,30 +249,47 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     prefetch_tmap(&tmW);
     prefetch_tmap(&tmX);
     // W is constant: fetch it before the dependency on the producer of X resolves
-    for (int s = 0; s < nkb; ++s) {
+    for (int s = 0; s < nst; ++s) {
       mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_2d(stages + static_cast<size_t>(s) * stage_bytes, &tmW, &full[s], (kb0 + s) * kSkBK,
                   tile * kSkTileN);
     }
     griddep_wait();
-    for (int s = 0; s < nkb; ++s)
+    for (int s = 0; s < nst; ++s)
       tma_load_2d(stages + static_cast<size_t>(s) * stage_bytes + w_bytes, &tmX, &full[s],
                   (kb0 + s) * kSkBK, 0);
     const uint32_t idesc = idesc_f16_f32(kSkTileN, static_cast<uint32_t>(p.Mp));
-    for (int s = 0; s < nkb && ok; ++s) {
-      if (!mbar_wait(&full[s], 0, status)) {
+    for (int i = 0; i < nkb && ok; ++i) {
+      const int b = i % nst;
+      const uint32_t ph = static_cast<uint32_t>(i / nst) & 1u;
+      if (!mbar_wait(&full[b], ph, status)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t a_base = smem_u32(stages + static_cast<size_t>(s) * stage_bytes);
+      const uint32_t a_base = smem_u32(stages + static_cast<size_t>(b) * stage_bytes);
       const uint32_t b_base = a_base + w_bytes;
 #pragma unroll
       for (int j = 0; j < kSkBK / 16; ++j)
         tc_mma_f16(tmem, smem_desc(a_base + 32u * j, 1024, 2), smem_desc(b_base + 32u * j, 1024, 2),
-                   idesc, (s | j) ? 1u : 0u);
+                   idesc, (i | j) ? 1u : 0u);
+      if (i + nst < nkb) {  // refill buffer b with K block i + nst once its MMAs have read it
+        tc_commit(&empty[b]);
+        if (!mbar_wait(&empty[b], ph, status)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[b], stage_bytes);
+        uint8_t* dst = stages + static_cast<size_t>(b) * stage_bytes;
+        tma_load_2d(dst, &tmW, &full[b], (kb0 + i + nst) * kSkBK, tile * kSkTileN);
+        tma_load_2d(dst + w_bytes, &tmX, &full[b], (kb0 + i + nst) * kSkBK, 0);
+      }
     }
-    if (ok && nkb > 0) tc_commit(&done);
+    if (ok && nkb > 0) {
+      tc_commit(&done);
+      ok = mbar_wait(&done, 0, status);
+    }
+    ok_flag = ok ? 1 : 0;
     }
     __syncwarp();
   }
@@ -254,18 +301,18 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     // ------------------------------------------------ whole K in this CTA
     const int n = tile * kSkTileN + nl;
     const float bias = (e.bias && n < p.N) ? __ldg(e.bias + n) : 0.f;
-    if (nkb > 0) ok = mbar_wait(&done, 0, status) && ok;
+    __syncthreads();  // thread 0 has seen the MMAs complete (the others wait here, idle)
     tc_fence_after();
     const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    for (int c0 = 0; c0 < p.Mp; c0 += 16) {
-      uint32_t r[16];
-      tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
-      tmem_ld_wait();
-      if (n < p.N) {
+    for (int c0 = 0; c0 < p.Mp; c0 += 64) {  // up to four loads in flight per wait
+      uint32_t r[4][16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c0 + j < p.M) sk_store1(e, c0 + j, n, __uint_as_float(r[j]), bias);
-      }
+      for (int u = 0; u < 4; ++u)
+        if (c0 + 16 * u < p.Mp) tmem_ld16(t_row + static_cast<uint32_t>(c0 + 16 * u), r[u]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (n < p.N && c0 + 16 * u < p.M) sk_store_col16(p, e, c0 + 16 * u, n, r[u], bias);
     }
   } else {
     // ----------------------------------- split K: push slices, reduce own rows
@@ -284,8 +331,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     // TMEM -> send[q][m][row] with q = nl / rows_per, row = nl % rows_per
     const int q = nl / rows_per, row = nl - (nl / rows_per) * rows_per;
     float* my = send + static_cast<size_t>(q) * p.Mp * rows_per + row;
+    __syncthreads();  // thread 0 has seen the MMAs complete (the others wait here, idle)
     if (nkb > 0) {
-      ok = mbar_wait(&done, 0, status) && ok;
       tc_fence_after();
       const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
       for (int c0 = 0; c0 < p.Mp; c0 += 64) {  // up to four loads in flight per wait
@@ -314,7 +361,12 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         bulk_to_peer(dsmem_map(dst, static_cast<uint32_t>(d)), src + static_cast<uint32_t>(d) * slice_bytes,
                      slice_bytes, dsmem_map(bar, static_cast<uint32_t>(d)));
     }
-    ok = mbar_wait(&recv_bar, 0, status) && ok;
+    if (tid == 0) ok_flag = mbar_wait(&recv_bar, 0, status) && ok_flag;
+    __syncthreads();
+    // Every slice sent TO this CTA has landed.  Arriving now (waiting only at
+    // exit) keeps each CTA alive until all peers have received, i.e. until
+    // every copy OUT of its send buffer is complete.
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     // recv[src][m][row]: sum the split slices of rows [rank*rows_per, +rows_per)
     auto reduce_group = [&](int idx, const SkOps& o) {
       const int m = idx / g4, r4 = (idx % g4) * 4;
@@ -340,7 +392,6 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       reduce_group(idx, n0 < p.N ? sk_ops(p, e, m, n0)
                                  : SkOps{make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)});
     }
-    cluster_arrive();  // no CTA leaves while a peer's copy may still read its send buffer
     cluster_wait();
   }
   tc_fence_before();
@@ -366,9 +417,7 @@ bool skinny_fits(long long M, long long N, long long K, long long ldx, long long
       ldw % 8)
     return false;
   if (!aligned16(x) || !aligned16(w)) return false;
-  const int mp = static_cast<int>((M + 15) / 16 * 16);
-  const long long kb = (K + kSkBK - 1) / kSkBK;
-  return kb <= static_cast<long long>(sk_stage_cap(mp, kSkMaxSplit)) * kSkMaxSplit;
+  return true;  // any K: a CTA cycles its stage buffers as a ring
 }
 
 int skinny_run(const uint16_t* x, int M, long long ldx, const uint16_t* w, int N, long long ldw,
@@ -387,19 +436,16 @@ int skinny_run(const uint16_t* x, int M, long long ldx, const uint16_t* w, int N
   // smallest power-of-two split that fits the stages, then widen while the
   // GPU is under-filled and every CTA still gets a K block
   int split = 1;
-  while (split * sk_stage_cap(p.Mp, split) < p.kb_total) split *= 2;
   while (split < kSkMaxSplit && static_cast<long long>(n_tiles) * split < sm_count() &&
          split * 2 <= p.kb_total)
     split *= 2;
   if (force_split > 0) {
-    if (force_split > kSkMaxSplit || (force_split & (force_split - 1)) ||
-        force_split * sk_stage_cap(p.Mp, force_split) < p.kb_total || force_split > p.kb_total)
+    if (force_split > kSkMaxSplit || (force_split & (force_split - 1)) || force_split > p.kb_total)
       return fail(GSVK_ERR_INVALID, "skinny GEMM: split %d not usable for K %d", force_split, K);
     split = force_split;
   }
-  if (split > kSkMaxSplit) return fail(GSVK_ERR_UNSUPPORTED, "skinny GEMM: K %d too deep", K);
   p.split = split;
-  p.stages = (p.kb_total + split - 1) / split;
+  p.stages = std::min((p.kb_total + split - 1) / split, sk_stage_cap(p.Mp, split));
   p.v_bias = e.bias && aligned16(e.bias);
   p.v_res = e.residual && aligned16(e.residual) && e.ld_res % 4 == 0;
   p.v_c32 = e.c32 && aligned16(e.c32) && e.ld_c32 % 4 == 0;

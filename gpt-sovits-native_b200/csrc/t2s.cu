@@ -13,8 +13,9 @@
 // kernel runs every step of the generation.  Per layer it has five phases
 // separated by grid barriers:
 //   P1  x = LN2(prev) ; q|k|v = Wqkv . f16(x) + b ; k, v -> fp16 KV slot
-//   P2  attention partials per (head, key chunk)  (split-K softmax)
-//   P3  combine partials ; hpre = Wout . f16(attn) + b + x
+//   P2  attention partials per (head, key chunk)  (split-K softmax); the
+//       slot that finishes a head's last chunk merges that head's records
+//   P3  hpre = Wout . f16(attn) + b + x
 //   P4  h = LN1(hpre) ; ff = relu(W1 . f16(h) + b)
 //   P5  xpre = W2 . ff + b + h          (fp32 activations, as the reference)
 // then logits = Wpred . LN2(xpre) and every CTA redundantly applies the
@@ -50,6 +51,8 @@ struct T2SDev {
   const float *bqkv, *bout, *b1, *b2, *n1g, *n1b, *n2g, *n2b, *pe;
   uint16_t *kc, *vc;
   float *q, *part, *hpre, *ff, *xpre, *logits;
+  float* attn;       // [D] merged attention output (fp16-rounded), written by each head's merger
+  unsigned* ticket;  // [H] chunk records finished per head (zero between layers)
   unsigned* bar;
   uint32_t* status;
 };
@@ -67,7 +70,6 @@ struct DecodeArgs {
   // shared-memory plan (identical in every CTA)
   int mq, mo, m1, m2, ml;  // max rows per CTA of qkv / out / w1 / w2 / logits
   uint32_t layer_bytes;
-  int stage_floats;  // shared floats for chunk records (P3); 0 = read them from global
   // optional phase trace: CTA 0 writes %globaltimer (ns) at every phase
   // boundary of the first kTraceSteps steps, kTraceStride slots per step
   unsigned long long* trace;
@@ -101,8 +103,9 @@ __device__ bool grid_sync(unsigned* bar, unsigned& epoch, uint32_t* status, int*
   if (threadIdx.x == 0) {
     ++epoch;
     const unsigned target = epoch * gridDim.x;
-    __threadfence();
-    atomicAdd(bar, 1u);
+    // one release-add publishes this CTA's writes (made visible to thread 0
+    // by the CTA barrier above) and arrives
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
     int ok = 1;
     for (uint32_t i = 0;; ++i) {
       const unsigned v = ld_acquire(bar);
@@ -117,8 +120,7 @@ __device__ bool grid_sync(unsigned* bar, unsigned& epoch, uint32_t* status, int*
         break;
       }
     }
-    __threadfence();
-    *flag = ok;
+    *flag = ok;  // the acquire load above orders everything after it
   }
   __syncthreads();
   return *flag != 0;
@@ -307,8 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   uint8_t* wbuf[2] = {smem, smem + a.layer_bytes};
   uint16_t* wlog = reinterpret_cast<uint16_t*>(smem + 2 * static_cast<size_t>(a.layer_bytes));
   float* slots = reinterpret_cast<float*>(wlog + static_cast<size_t>(a.ml) * D);  // attention
-  float* stage = slots + kSlots * slot_floats<HD>();      // staged chunk records
-  float* xs = stage + a.stage_floats;                     // layer input x
+  float* xs = slots + kSlots * slot_floats<HD>();         // layer input x
   float* hs = xs + D;                                     // LN1 output h
   float* act = hs + D;                                    // operand, max(D, F)
   float* sc = act + (F > D ? F : D);                      // chunk scores / weights
@@ -507,56 +508,58 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
                               m.vc + static_cast<size_t>(l) * m.cap * D + h * HD, D, k0, k1, m.scale,
                               sm, 1 + slot,
                               m.part + (static_cast<size_t>(h) * kMaxChunks + c) * rec_floats<HD>());
+          // The slot that finishes the last record of head h merges the
+          // head's records (canonical chunk order) right away.  One
+          // acq_rel ticket per record: its release publishes the record the
+          // slot just wrote (ordered before it by the slot barrier inside
+          // attn_chunk_slot); its acquire, for the last ticket, makes every
+          // other record visible to this slot.
+          int* last = reinterpret_cast<int*>(sm + 128 + 4);
+          if ((tid & 63) == 0) {
+            unsigned old;
+            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                         : "=r"(old)
+                         : "l"(m.ticket + h)
+                         : "memory");
+            *last = old == static_cast<unsigned>(nch - 1);
+          }
+          slot_sync(1 + slot);
+          if (*last) {
+            const float* rec = m.part + static_cast<size_t>(h) * kMaxChunks * rec_floats<HD>();
+            const int n4 = nch * rec_floats<HD>() / 4;
+            // staged into the slot's V area (sm + 136), clear of the flag at sm[132]
+            float* stg = sm + 136;
+            const bool fits = n4 * 4 <= kChunk * HD / 2;
+            if (fits) {  // stage the records, every load in flight
+              constexpr int kPer = 4;
+              float4 r[kPer];
+              const int t64 = tid & 63;
+#pragma unroll
+              for (int u = 0; u < kPer; ++u)
+                if (t64 + 64 * u < n4) r[u] = __ldcg(reinterpret_cast<const float4*>(rec) + t64 + 64 * u);
+#pragma unroll
+              for (int u = 0; u < kPer; ++u)
+                if (t64 + 64 * u < n4) reinterpret_cast<float4*>(stg)[t64 + 64 * u] = r[u];
+              for (int i = t64 + 64 * kPer; i < n4; i += 64)
+                reinterpret_cast<float4*>(stg)[i] = __ldcg(reinterpret_cast<const float4*>(rec) + i);
+            }
+            slot_sync(1 + slot);
+            if ((tid & 63) < 32) {
+              float o0, o1;
+              attn_combine<HD>(fits ? stg : rec, nch, !fits, &o0, &o1);
+              m.attn[h * HD + lane] = h2f(f2h(o0));
+              if (HD > 32) m.attn[h * HD + 32 + lane] = h2f(f2h(o1));
+              if (lane == 0) m.ticket[h] = 0;
+            }
+          }
+          slot_sync(1 + slot);
         }
       }
       GSVK_TR(16 + 16 * l + 2);
       if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
       GSVK_TR(16 + 16 * l + 3);
       // ---------------------------------------------------------------- P3
-      {
-        // each warp stages the records of its own heads (all loads in flight at once)
-        const int rec4 = nch * rec_floats<HD>() / 4;
-        const bool staged = kWarps * 2 * rec4 * 4 <= a.stage_floats && H <= 2 * kWarps;
-        float* wst = stage + warp * 2 * rec4 * 4;
-        if (staged) {
-          constexpr int kMaxU = 16;
-          float4 r[kMaxU];
-          const int n4 = (H > kWarps ? 2 : 1) * rec4;
-#pragma unroll
-          for (int u = 0; u < kMaxU; ++u) {
-            const int i = lane + 32 * u;
-            if (i < n4) {
-              const int hh = warp + (i / rec4) * kWarps, j = i - (i / rec4) * rec4;
-              r[u] = hh < H ? __ldcg(reinterpret_cast<const float4*>(
-                                  m.part + static_cast<size_t>(hh) * kMaxChunks * rec_floats<HD>()) + j)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kMaxU; ++u) {
-            const int i = lane + 32 * u;
-            if (i < n4) reinterpret_cast<float4*>(wst)[i] = r[u];
-          }
-          for (int i = lane + 32 * kMaxU; i < n4; i += 32) {
-            const int hh = warp + (i / rec4) * kWarps, j = i - (i / rec4) * rec4;
-            reinterpret_cast<float4*>(wst)[i] =
-                hh < H ? __ldcg(reinterpret_cast<const float4*>(
-                             m.part + static_cast<size_t>(hh) * kMaxChunks * rec_floats<HD>()) + j)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-          __syncwarp();
-        }
-        for (int h = warp, k = 0; h < H; h += kWarps, ++k) {
-          float o0, o1;
-          if (staged)
-            attn_combine<HD>(wst + k * rec4 * 4, nch, false, &o0, &o1);
-          else
-            attn_combine<HD>(m.part + static_cast<size_t>(h) * kMaxChunks * rec_floats<HD>(), nch,
-                             true, &o0, &o1);
-          act[h * HD + lane] = h2f(f2h(o0));
-          if (HD > 32) act[h * HD + 32 + lane] = h2f(f2h(o1));
-        }
-      }
+      load_vec<2>(act, m.attn, D);
       __syncthreads();
       {
         const float* bo = m.bout + static_cast<size_t>(l) * D;
@@ -965,7 +968,8 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
                o_px = take((size_t)cap * D * 4), o_pqkv = take((size_t)cap * 3 * D * 4),
                o_phpre = take((size_t)cap * D * 4), o_px16 = take((size_t)cap * D * 2),
                o_pattn = take((size_t)cap * D * 2), o_pff = take((size_t)cap * F * 2),
-               o_trace = take((size_t)kTraceSteps * kTraceStride * 8);
+               o_trace = take((size_t)kTraceSteps * kTraceStride * 8),
+               o_attn = take((size_t)D * 4), o_ticket = take((size_t)H * 4);
   if (cudaMalloc(&e->scratch, off) != cudaSuccess) {
     cudaGetLastError();
     gsvk_t2s_destroy(e);
@@ -985,6 +989,8 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   d.xpre = reinterpret_cast<float*>(sb + o_xpre);
   d.logits = reinterpret_cast<float*>(sb + o_logits);
   d.bar = reinterpret_cast<unsigned*>(sb + o_bar);
+  d.attn = reinterpret_cast<float*>(sb + o_attn);
+  d.ticket = reinterpret_cast<unsigned*>(sb + o_ticket);
   d.status = device_status();
   e->d_prompt = reinterpret_cast<int32_t*>(sb + o_prompt);
   e->d_tokens = reinterpret_cast<int32_t*>(sb + o_tok);
@@ -1012,8 +1018,7 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
       ((size_t)a.mq * D + (size_t)a.mo * D + (size_t)a.m1 * D + (size_t)a.m2 * F) * 2, 128));
   const size_t slot_f = (size_t)kSlots * (HD == 32 ? slot_floats<32>() : slot_floats<64>());
   const size_t max_nch = ((size_t)cap + kChunk - 1) / kChunk;
-  a.stage_floats = (int)std::min<size_t>((size_t)2 * kWarps * max_nch * (HD + 4), 16384);
-  const size_t floats = slot_f + a.stage_floats + (size_t)D * 2 + std::max(D, F) + kChunk + 64;
+  const size_t floats = slot_f + (size_t)D * 2 + std::max(D, F) + kChunk + 64;
   e->decode_smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 + floats * 4 + 8 * 4 +
                    4 * 8 + align_up(V, 16) + 64;
   e->attn_smem = (slot_f + max_nch * (HD + 4)) * 4;
@@ -1164,6 +1169,8 @@ int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size
   cudaStream_t st = as_cuda(stream);
   int rc;
   if ((rc = check_cuda(cudaMemsetAsync(d.bar, 0, 4, st), "reset grid barrier"))) return rc;
+  if ((rc = check_cuda(cudaMemsetAsync(d.ticket, 0, (size_t)d.H * 4, st), "reset head tickets")))
+    return rc;
   if ((rc = check_cuda(cudaMemsetAsync(n_out_dev, 0, 4, st), "reset n_out"))) return rc;
   if (max_steps == 0) return GSVK_OK;
   DecodeArgs a = h->plan;
