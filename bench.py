@@ -357,6 +357,63 @@ def run_gemm1(args, rank, local, world):
     return line
 
 
+# ------------------------------------------- one GEMM shape, back to back
+def run_gemm_shape(args, rank, local, world):
+    """C = A B^T for --gemm-shape M,N,K (fp16 in, fp32 accumulate, fp16 out),
+    captured as 100 launches in a CUDA graph per step, rotating enough
+    operand copies that the working set exceeds L2."""
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    M, N, K = (int(v) for v in args.gemm_shape.split(","))
+    gen = torch.Generator(device=dev).manual_seed(1 + rank)
+    per = (M * K + N * K + M * N) * 2
+    copies = max(1, min(8, -(-256 * 2 ** 20 // per)))
+    a = [torch.randn(M, K, device=dev, generator=gen).half() for _ in range(copies)]
+    w = [(torch.randn(N, K, device=dev, generator=gen) * 0.02).half() for _ in range(copies)]
+    c = [torch.empty(M, N, device=dev, dtype=torch.float16) for _ in range(copies)]
+    iters = 100
+    for i in range(copies):
+        g.gemm_ex(a[i], w[i], c_f16=c[i])
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(iters):
+            g.gemm_ex(a[i % copies], w[i % copies], c_f16=c[i % copies])
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler()
+    barrier(world)
+    clocks.start()
+    start.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    t = max_over_ranks(start.elapsed_time(end) * 1e-3, world)
+    flops = 2.0 * M * N * K * iters * args.steps
+    _, tf, kind = measured_peaks()
+    achieved = flops / t / 1e12
+    line = {"metric": f"GEMM TFLOP/s ({M}x{N}x{K}, fp16 out)", "value": achieved * world,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 in, f32 accumulate, f16 out", "data": "synthetic N(0,1) x N(0,0.02)",
+            "config": {"workload": "gemm", "shape": [M, N, K], "iters_per_step": iters,
+                       "launch": "CUDA graph", "l2": f"{copies} rotated operand copies"},
+            "gpu_launches": iters * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel", "achieved": achieved, "peak": tf,
+                         "unit": "TFLOP/s", "frac": achieved / tf, "peak_source": kind, "traffic": None}}
+    if clk:
+        line["clocks"] = clk
+    return line
+
+
 # ------------------------------------------------------- SoVITS decoder (5)
 def run_decoder(args, rank, local, world):
     import numpy as np
@@ -604,7 +661,7 @@ def run_t2s_batch(args, rank, local, world):
 
 
 WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder": run_decoder,
-             "encoder": run_encoder, "t2s_decode_b64": run_t2s_batch}
+             "encoder": run_encoder, "t2s_decode_b64": run_t2s_batch, "gemm": run_gemm_shape}
 
 
 def run_reference(args, rank, world):
@@ -643,6 +700,8 @@ def main():
     ap.add_argument("--workload", default="t2s_decode_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--encoder", default="bert", choices=["bert", "hubert"])
+    ap.add_argument("--gemm-shape", default="4096,4096,1024",
+                    help="M,N,K of the gemm workload")
     ap.add_argument("--decode-steps", type=int, default=T2S_STEPS,
                     help="tokens per utterance (default 500; smaller only for profiling captures)")
     args = ap.parse_args()

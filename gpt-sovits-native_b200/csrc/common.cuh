@@ -57,6 +57,11 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
+// Two fp32 -> packed fp16 pair (low half = a), RNE, one conversion instruction.
+__device__ __forceinline__ uint32_t f2h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
 // Streaming 128-bit load that bypasses L1 allocation (weights are read once
 // per launch; keeping them out of L1 leaves it to the reused activations).
@@ -95,19 +100,38 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Epilogue activation (GSVK_ACT_*), identical expressions to the reference:
-// relu kern.cpp:85, gelu_erf bert_ops.hpp:25, leaky nn_ops.hpp:48, tanh dec.hpp:344.
-// The transcendental cases live in one out-of-line function: epilogues unroll
-// apply_act per element, and inlining erff / tanhf into every copy makes
-// those loops overflow the instruction cache.
+// Epilogue activation (GSVK_ACT_*), the reference's expressions:
+// relu kern.cpp:85, gelu_erf bert_ops.hpp:25 (its erf evaluated by the
+// approximation below, within 1.5e-7), leaky nn_ops.hpp:48, tanh dec.hpp:344.
+// erf(x) by Abramowitz & Stegun, Handbook of Mathematical Functions (1964),
+// eq. 7.1.26 (Hastings' approximation): for x >= 0,
+//   erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),
+//   t = 1 / (1 + p x),  |error| <= 1.5e-7;  erf(-x) = -erf(x).
+// Short enough to inline into unrolled epilogues.
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, ax, 1.0f));  // approximate reciprocal (2 ulp)
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  const float y = fmaf(-poly * t, __expf(-ax * ax), 1.0f);
+  return copysignf(y, x);
+}
+__device__ __forceinline__ float gelu_erf(float v) {
+  return 0.5f * v * (1.f + erf_as7126(v * 0.70710678118654752440f));
+}
+// tanh stays out of line: epilogues unroll apply_act per element, and
+// inlining tanhf into every copy makes those loops overflow the
+// instruction cache (it only runs in the decoder's last conv).
 static __device__ __noinline__ float apply_act_transcendental(float v, int act) {
-  return act == GSVK_ACT_GELU_ERF ? 0.5f * v * (1.f + erff(v * 0.70710678118654752440f)) : tanhf(v);
+  return act == GSVK_ACT_GELU_ERF ? gelu_erf(v) : tanhf(v);
 }
 __device__ __forceinline__ float apply_act(float v, int act, float slope) {
   switch (act) {
     case GSVK_ACT_RELU: return v > 0.f ? v : 0.f;
     case GSVK_ACT_LEAKY: return v < 0.f ? v * slope : v;
-    case GSVK_ACT_GELU_ERF:
+    case GSVK_ACT_GELU_ERF: return gelu_erf(v);
     case GSVK_ACT_TANH: return apply_act_transcendental(v, act);
     default: return v;
   }
@@ -126,6 +150,10 @@ __device__ __forceinline__ void act_array(float* v, int act, float slope) {
     case GSVK_ACT_LEAKY:
 #pragma unroll
       for (int j = 0; j < NV; ++j) v[j] = v[j] < 0.f ? v[j] * slope : v[j];
+      break;
+    case GSVK_ACT_GELU_ERF:
+#pragma unroll
+      for (int j = 0; j < NV; ++j) v[j] = gelu_erf(v[j]);
       break;
     default:
       for (int j = 0; j < NV; ++j) v[j] = apply_act_transcendental(v[j], act);

@@ -128,8 +128,8 @@ __device__ __forceinline__ void sk_store4(const SkProblem& p, const TcEpilogue& 
   if (e.c16) {
     uint16_t* d = e.c16 + m * e.ld_c16 + n0;
     if (full && p.v_c16) {
-      *reinterpret_cast<uint2*>(d) = make_uint2(f2h(v[0]) | (static_cast<uint32_t>(f2h(v[1])) << 16),
-                                                f2h(v[2]) | (static_cast<uint32_t>(f2h(v[3])) << 16));
+      *reinterpret_cast<uint2*>(d) = make_uint2(f2h2(v[0], v[1]),
+                                                f2h2(v[2], v[3]));
     } else {
       for (int u = 0; u < 4; ++u)
         if (n0 + u < p.N) d[u] = f2h(v[u]);
@@ -139,8 +139,8 @@ __device__ __forceinline__ void sk_store4(const SkProblem& p, const TcEpilogue& 
     act_array<4>(v, e.act2, e.slope2);
     uint16_t* d = e.c16_act + m * e.ld_c16_act + n0;
     if (full && p.v_c16a) {
-      *reinterpret_cast<uint2*>(d) = make_uint2(f2h(v[0]) | (static_cast<uint32_t>(f2h(v[1])) << 16),
-                                                f2h(v[2]) | (static_cast<uint32_t>(f2h(v[3])) << 16));
+      *reinterpret_cast<uint2*>(d) = make_uint2(f2h2(v[0], v[1]),
+                                                f2h2(v[2], v[3]));
     } else {
       for (int u = 0; u < 4; ++u)
         if (n0 + u < p.N) d[u] = f2h(v[u]);

@@ -12,7 +12,8 @@ namespace gsvk {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quadrant, each half of the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemBudget = 200 * 1024;
 
 struct TapPlan {
@@ -61,28 +62,66 @@ __device__ __forceinline__ TapPlan plan_for(const TcProblem& p, int phase) {
   return t;
 }
 
+// Bias and residual of one 16-column chunk, fetched one chunk ahead of its
+// use (loads stay in flight: values are assigned under branches, never
+// selected, so nothing waits for them until store16 consumes them).
+__device__ __forceinline__ void fetch16(const TcEpilogue& e, bool row_ok, long long orow, int n0,
+                                        int N, int oc, bool bias_vec, float* bb, float* rr) {
+  const bool full = (n0 + 16 <= N);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    bb[j] = 0.f;
+    rr[j] = 0.f;
+  }
+  if (e.bias) {
+    if (full && bias_vec) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(e.bias + n0 + j));
+        bb[j] = v.x;
+        bb[j + 1] = v.y;
+        bb[j + 2] = v.z;
+        bb[j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) bb[j] = __ldg(e.bias + n0 + j);
+    }
+  }
+  if (e.residual && row_ok) {
+    const float* src = e.residual + orow * e.ld_res + oc + n0;
+    if (full && aligned16(src)) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src + j);
+        rr[j] = v.x;
+        rr[j + 1] = v.y;
+        rr[j + 2] = v.z;
+        rr[j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) rr[j] = src[j];
+    }
+  }
+}
+
 // n0: column within the problem (bias index, N bound); oc: output column
 // offset (batched mode), added to n0 for the output and residual addresses.
+// bb / rr: this chunk's bias and residual (from fetch16).
 __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int n0, int N,
-                                        const uint32_t* r, int oc = 0) {
+                                        const uint32_t* r, int oc, const float* bb,
+                                        const float* rr) {
   float v[16];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]) * e.alpha;
+  for (int j = 0; j < 16; ++j) v[j] = fmaf(__uint_as_float(r[j]), e.alpha, bb[j]);
   const bool full = (n0 + 16 <= N);
-  if (e.bias) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (full || n0 + j < N) v[j] = v[j] + __ldg(e.bias + n0 + j);
-  }
-  if (e.act != GSVK_ACT_NONE) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = apply_act(v[j], e.act, e.slope);
-  }
+  act_array<16>(v, e.act, e.slope);
   if (e.residual) {
-    const float* rr = e.residual + orow * e.ld_res + oc + n0;
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (full || n0 + j < N) v[j] = fmaf(e.res_scale, rr[j], v[j]);
+    for (int j = 0; j < 16; ++j) v[j] = fmaf(e.res_scale, rr[j], v[j]);
   }
   if (e.c32) {
     float* dst = e.c32 + orow * e.ld_c32 + oc + n0;
@@ -100,7 +139,7 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
     if (full && aligned16(dst)) {
       uint32_t pk[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) pk[j] = f2h(v[2 * j]) | (static_cast<uint32_t>(f2h(v[2 * j + 1])) << 16);
+      for (int j = 0; j < 8; ++j) pk[j] = f2h2(v[2 * j], v[2 * j + 1]);
       reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
     } else {
@@ -109,18 +148,17 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
     }
   }
   if (e.c16_act) {
+    act_array<16>(v, e.act2, e.slope2);
     uint16_t* dst = e.c16_act + orow * e.ld_c16_act + oc + n0;
     if (full && aligned16(dst)) {
       uint32_t pk[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        pk[j] = f2h(apply_act(v[2 * j], e.act2, e.slope2)) |
-                (static_cast<uint32_t>(f2h(apply_act(v[2 * j + 1], e.act2, e.slope2))) << 16);
+      for (int j = 0; j < 8; ++j) pk[j] = f2h2(v[2 * j], v[2 * j + 1]);
       reinterpret_cast<uint4*>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       reinterpret_cast<uint4*>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
     } else {
       for (int j = 0; j < 16; ++j)
-        if (n0 + j < N) dst[j] = f2h(apply_act(v[j], e.act2, e.slope2));
+        if (n0 + j < N) dst[j] = f2h(v[j]);
     }
   }
 }
@@ -165,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     fence_barrier_init();
     prefetch_tmap(&tmA);
@@ -246,7 +284,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;            // TMEM lanes 32*quarter .. +31
+    const int half = (warp - 2) >> 2;        // column half of the tile
+    const int cw = BN >= 32 ? BN / 2 : BN;   // columns per warp
+    const int cbeg = BN >= 32 ? half * cw : 0;
+    const bool cols_ok = BN >= 32 || half == 0;
+    const bool bias_vec = e.bias && aligned16(e.bias);
     int tl = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tl) {
       const int phase = tile / (m_tiles * n_tiles);
@@ -255,20 +298,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TapPlan tp = plan_for(p, phase);
       const int acc = tl & 1;
       const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
-      if (!mbar_wait(&tfull[acc], aph, status)) break;
-      tc_fence_after();
       const int i = mt * kBM + quarter * 32 + lane;
       const int q = tp.q0 + i;
       const bool row_ok = (i < p.M) && (q <= tp.qmax);
       const long long orow = static_cast<long long>(q) * tp.o_mul + tp.o_off + tp.c_row0;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
+      float bnext[16], rnext[16];
+      fetch16(e, row_ok, orow, nt * BN + cbeg, p.N, tp.c_col0, bias_vec, bnext, rnext);
+      if (!mbar_wait(&tfull[acc], aph, status)) break;
+      tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = cbeg; c0 < cbeg + cw && cols_ok; c0 += 16) {
+        float bcur[16], rcur[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          bcur[j] = bnext[j];
+          rcur[j] = rnext[j];
+        }
+        if (c0 + 16 < cbeg + cw)
+          fetch16(e, row_ok, orow, nt * BN + c0 + 16, p.N, tp.c_col0, bias_vec, bnext, rnext);
         uint32_t r[16];
         tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
         tmem_ld_wait();
-        if (row_ok && nt * BN + c0 < p.N) store16(e, orow, nt * BN + c0, p.N, r, tp.c_col0);
+        if (row_ok && nt * BN + c0 < p.N)
+          store16(e, orow, nt * BN + c0, p.N, r, tp.c_col0, bcur, rcur);
       }
       tc_fence_before();
       __syncwarp();
@@ -329,7 +383,9 @@ __global__ void gemm_simt_kernel(const uint16_t* __restrict__ a, long long lda,
     }
     r[j] = __float_as_uint(acc);
   }
-  store16(e, m, g * 16, N, r);
+  float bb[16], rr[16];
+  fetch16(e, true, m, g * 16, N, 0, false, bb, rr);
+  store16(e, m, g * 16, N, r, 0, bb, rr);
 }
 
 int pick_bk(long long kc) {

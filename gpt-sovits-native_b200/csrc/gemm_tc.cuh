@@ -15,8 +15,10 @@
 //   ConvTranspose1d     phase r, tap m: a_shift = -m, b_row = (r + m*u)*Co,
 //                        output row = q*u + r - pad with q = i + q0(r)   (polyphase, no scatter)
 //
-// Roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and TMEM
-// owner, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer and TMEM
+// owner, warps 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31, warps
+// 2..5 the left half of the tile's columns, 6..9 the right half).  Bias and
+// residual chunks are fetched one chunk ahead of their use.
 // Two TMEM accumulators let the epilogue of tile i overlap the mainloop of
 // tile i+1.  Every mbarrier wait is bounded (see tma.cuh).
 #pragma once
