@@ -122,6 +122,275 @@ __global__ void enc_ln_kernel(const float* __restrict__ x, const float* __restri
   }
 }
 
+// Fused attention for one (utterance b, head h, 128-query block qb), head
+// dim 64, T <= 256 keys (Tp = T rounded up to 64):
+//   S = Q K^T on the tensor cores into TMEM (M = 128 queries, N = Tp keys);
+//   each thread owns one query row (its TMEM lane) and makes three passes
+//   over it — max, sum of exp, write — producing the same fp16
+//   P = softmax(S / sqrt(64)) as enc_softmax_kernel (keys >= valid[b] get
+//   finfo.min added; keys >= T are dropped) straight into shared memory in
+//   the 128-byte-swizzled K-major layout the MMA reads;
+//   O = P V (A = P, B = V^T from enc_vt_kernel) into TMEM; fp16 O rows go to
+//   the head's 64 columns of ctx.
+// One thread issues the TMA loads and the MMAs and alone polls their
+// mbarriers; the others wait at CTA barriers.
+constexpr int kAttnDh = 64;
+constexpr int kAttnQ = 128;
+
+__device__ __forceinline__ uint32_t sw128_offset(int row, int col) {
+  // byte offset of element (row, col) in a [rows][64] fp16 tile with the
+  // 128-byte swizzle: 16-byte chunk index XOR (row mod 8)
+  return static_cast<uint32_t>(row) * 128u +
+         ((static_cast<uint32_t>(col >> 3) ^ static_cast<uint32_t>(row & 7)) << 4) +
+         static_cast<uint32_t>(col & 7) * 2u;
+}
+
+constexpr int kAttnThreads = 512;  // 16 warps: four per TMEM lane quadrant
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    enc_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmVt, int T, int Tp, int H, int C,
+                    const int* __restrict__ valid, uint16_t* __restrict__ ctx, uint32_t* status) {
+  extern __shared__ uint8_t at_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  __shared__ uint64_t load_bar, s_bar, o_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ float red[8 * kAttnQ];  // per-group row max [4][128], row sum [4][128]
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nkc = Tp / 64;                       // 64-key regions
+  uint8_t* sVt = smem;                           // nkc x [64][64]   8 KB each
+  uint8_t* sQ = sVt + nkc * 64 * 128;            // [128][64]        16 KB
+  uint8_t* sK = sQ + kAttnQ * 128;               // [Tp][64]         Tp*128 B
+  uint8_t* sP = sQ;                              // nkc x [128][64]  16 KB each, over Q and K
+                                                 // (written once the S MMA has read them)
+  // S takes columns [0, Tp); O reuses [0, 64) after the softmax has read S
+  const uint32_t tmem_cols = Tp <= 64 ? 64u : (Tp <= 128 ? 128u : 256u);
+  const uint32_t o_col = 0;
+
+  if (tid == 0) {
+    mbar_init(&load_bar, 1);
+    mbar_init(&s_bar, 1);
+    mbar_init(&o_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const int row0 = b * T;  // first token row of utterance b
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmVt);
+      mbar_arrive_expect_tx(&load_bar,
+                            static_cast<uint32_t>(kAttnQ * 128 + Tp * 128 + nkc * 64 * 128));
+      tma_load_2d(sQ, &tmQ, &load_bar, h * kAttnDh, row0 + qb * kAttnQ);
+      tma_load_2d(sK, &tmK, &load_bar, C + h * kAttnDh, row0);
+      for (int kc = 0; kc < nkc; ++kc)
+        tma_load_2d(sVt + kc * 64 * 128, &tmVt, &load_bar, kc * 64, (b * H + h) * kAttnDh);
+      bool ok = mbar_wait(&load_bar, 0, status);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sQ), b0 = smem_u32(sK);
+        const uint32_t idesc = idesc_f16_f32(kAttnQ, static_cast<uint32_t>(Tp));
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc_mma_f16(tmem, smem_desc(a0 + 32u * j, 1024, 2), smem_desc(b0 + 32u * j, 1024, 2), idesc,
+                     j ? 1u : 0u);
+        tc_commit(&s_bar);
+        mbar_wait(&s_bar, 0, status);
+      }
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  tc_fence_after();
+  // ---------------------------------------------------------------- softmax
+  // Four warps per TMEM lane quadrant: warp w serves rows 32*(w%4) .. +31 and
+  // key columns [g*cw, (g+1)*cw) with g = w / 4; row max and sum are combined
+  // across the four groups through shared memory (in group order).
+  const int quad = warp & 3, grp = warp >> 2;
+  const int r = quad * 32 + lane;  // query row within the block (TMEM lane)
+  const int q = qb * kAttnQ + r;
+  const int cw = Tp / 4, cbeg = grp * cw;
+  const int nv = valid ? valid[b] : T;
+  const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+  constexpr float kScale = 0.125f;  // 1 / sqrt(64)
+  float mx = -INFINITY;
+  for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
+    uint32_t v[16];
+    tmem_ld16(t_row + static_cast<uint32_t>(c0), v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int k = c0 + j;
+      float x = __uint_as_float(v[j]) * kScale;
+      if (k >= nv) x = x + -3.40282347e+38f;
+      if (k < T) mx = fmaxf(mx, x);
+    }
+  }
+  red[grp * kAttnQ + r] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[r], red[kAttnQ + r]), fmaxf(red[2 * kAttnQ + r], red[3 * kAttnQ + r]));
+  float sum = 0.f;
+  for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
+    uint32_t v[16];
+    tmem_ld16(t_row + static_cast<uint32_t>(c0), v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int k = c0 + j;
+      float x = __uint_as_float(v[j]) * kScale;
+      if (k >= nv) x = x + -3.40282347e+38f;
+      if (k < T) sum += __expf(x - mx);
+    }
+  }
+  red[4 * kAttnQ + grp * kAttnQ + r] = sum;
+  __syncthreads();
+  const float* rs = red + 4 * kAttnQ;
+  const float inv = 1.f / (((rs[r] + rs[kAttnQ + r]) + rs[2 * kAttnQ + r]) + rs[3 * kAttnQ + r]);
+  for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
+    uint32_t v[16];
+    tmem_ld16(t_row + static_cast<uint32_t>(c0), v);
+    tmem_ld_wait();
+    uint32_t pk[8];
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      float e[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int k = c0 + j + u;
+        float x = __uint_as_float(v[j + u]) * kScale;
+        if (k >= nv) x = x + -3.40282347e+38f;
+        e[u] = k < T ? __expf(x - mx) * inv : 0.f;
+      }
+      pk[j / 2] = f2h2(e[0], e[1]);
+    }
+    uint8_t* region = sP + (c0 >> 6) * (kAttnQ * 128);
+    const int cc = c0 & 63;  // 16 keys = two 16-byte chunks
+    *reinterpret_cast<uint4*>(region + sw128_offset(r, cc)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    *reinterpret_cast<uint4*>(region + sw128_offset(r, cc + 8)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
+  fence_proxy_async_shared();  // P (generic writes) -> visible to the tensor core
+  tc_fence_before();
+  __syncthreads();
+  // ------------------------------------------------------------------ P . V
+  if (tid == 0) {
+    tc_fence_after();
+    const uint32_t idesc = idesc_f16_f32(kAttnQ, kAttnDh);
+    for (int kc = 0; kc < nkc; ++kc) {
+      const uint32_t a0 = smem_u32(sP + kc * kAttnQ * 128), b0 = smem_u32(sVt + kc * 64 * 128);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        tc_mma_f16(tmem + o_col, smem_desc(a0 + 32u * j, 1024, 2), smem_desc(b0 + 32u * j, 1024, 2),
+                   idesc, (kc | j) ? 1u : 0u);
+    }
+    tc_commit(&o_bar);
+    mbar_wait(&o_bar, 0, status);
+  }
+  __syncthreads();
+  tc_fence_after();
+  {  // group g stores O columns [16 g, 16 g + 16) of its rows
+    uint32_t v[16];
+    tmem_ld16(t_row + o_col + 16u * static_cast<uint32_t>(grp), v);
+    tmem_ld_wait();
+    if (q < T) {
+      uint4* dst = reinterpret_cast<uint4*>(ctx + static_cast<size_t>(row0 + q) * C + h * kAttnDh +
+                                            16 * grp);
+      uint32_t pk[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pk[j] = f2h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tmem_cols);
+  }
+}
+
+size_t enc_attn_smem(int Tp) {
+  const size_t qk = static_cast<size_t>(kAttnQ) * 128 + static_cast<size_t>(Tp) * 128;
+  const size_t p = static_cast<size_t>(Tp / 64) * kAttnQ * 128;
+  return 1024 + static_cast<size_t>(Tp / 64) * 64 * 128 + (qk > p ? qk : p);
+}
+
+// Row LayerNorm, one warp per row of n = 128 * NV4 values: every lane reads
+// its NV4 float4 slices once (coalesced), sums them in fp32, and the warp
+// combines the partial sums in fp64 (the reference's fp64 statistics);
+// normalised values go out as fp32 and fp16 from the same registers.
+template <int NV4>
+__global__ void __launch_bounds__(256) enc_ln_warp_kernel(const float* __restrict__ x,
+                                                          const float* __restrict__ g,
+                                                          const float* __restrict__ bta,
+                                                          float* __restrict__ y,
+                                                          uint16_t* __restrict__ y16, int rows,
+                                                          double eps) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int n = NV4 * 128;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * n);
+  float4 v[NV4];
+  float s = 0.f, q = 0.f;
+#pragma unroll
+  for (int u = 0; u < NV4; ++u) v[u] = xr[lane + 32 * u];
+#pragma unroll
+  for (int u = 0; u < NV4; ++u) {
+    s += (v[u].x + v[u].y) + (v[u].z + v[u].w);
+    q = fmaf(v[u].x, v[u].x, q);
+    q = fmaf(v[u].y, v[u].y, q);
+    q = fmaf(v[u].z, v[u].z, q);
+    q = fmaf(v[u].w, v[u].w, q);
+  }
+  const double ds = warp_sum_d(static_cast<double>(s)), dq = warp_sum_d(static_cast<double>(q));
+  const float mean = static_cast<float>(ds / n);
+  float var = static_cast<float>(dq / n - static_cast<double>(mean) * mean);
+  if (!(var >= 0.f)) var = 0.f;
+  const float rstd = static_cast<float>(1.0 / sqrt(static_cast<double>(var) + eps));
+  float4* yr = reinterpret_cast<float4*>(y + static_cast<size_t>(row) * n);
+  uint2* y16r = reinterpret_cast<uint2*>(y16 + static_cast<size_t>(row) * n);
+#pragma unroll
+  for (int u = 0; u < NV4; ++u) {
+    const int i = lane + 32 * u;
+    const float4 gg = __ldg(reinterpret_cast<const float4*>(g) + i);
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(bta) + i);
+    float4 o;
+    o.x = fmaf((v[u].x - mean) * rstd, gg.x, bb.x);
+    o.y = fmaf((v[u].y - mean) * rstd, gg.y, bb.y);
+    o.z = fmaf((v[u].z - mean) * rstd, gg.z, bb.z);
+    o.w = fmaf((v[u].w - mean) * rstd, gg.w, bb.w);
+    yr[i] = o;
+    y16r[i] = make_uint2(f2h2(o.x, o.y), f2h2(o.z, o.w));
+  }
+}
+
+int enc_layernorm(const float* x, const float* g, const float* b, float* y, uint16_t* y16, int rows,
+                  int n, double eps, cudaStream_t st) {
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  switch (n % 128 == 0 ? n / 128 : 0) {
+#define GSVK_LN_CASE(K)                                                                   \
+  case K:                                                                                 \
+    enc_ln_warp_kernel<K><<<blocks, 256, 0, st>>>(x, g, b, y, y16, rows, eps);            \
+    return check_launch("enc_ln_warp_kernel");
+    GSVK_LN_CASE(4) GSVK_LN_CASE(5) GSVK_LN_CASE(6) GSVK_LN_CASE(7) GSVK_LN_CASE(8)
+    GSVK_LN_CASE(10) GSVK_LN_CASE(12) GSVK_LN_CASE(16)
+#undef GSVK_LN_CASE
+    default:
+      enc_ln_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(x, g, b, y, y16, n, eps);
+      return check_launch("enc_ln_kernel");
+  }
+}
+
 }  // namespace
 
 struct EncoderEngine {
@@ -250,6 +519,21 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
   const gsvk_encoder_config& c = h->cfg;
   const int C = c.hidden, H = c.heads, F = c.ffn, dh = C / H, T = (int)seq, B = (int)batch;
   const int M = B * T, Tp = (T + 63) / 64 * 64;
+  // fused tensor-core attention covers head dim 64 and up to 256 keys
+  const bool fused = dh == kAttnDh && Tp <= 256;
+  if (fused) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+      if (int rc0 = check_cuda(cudaFuncSetAttribute(enc_attn_kernel,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    (int)enc_attn_smem(256)),
+                               "cudaFuncSetAttribute(enc_attn)"))
+        return rc0;
+      attr_set[dev] = true;
+    }
+  }
   cudaStream_t st = as_cuda(stream);
   int launches = 0;
   int rc = gsvk_f32_to_f16(x, h->x16, (size_t)M * C, stream);
@@ -282,67 +566,84 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
     if ((rc = gemm(h->x16, C, h->wqkv + (size_t)l * 3 * C * C, 3 * C, C,
                    h->bqkv + (size_t)l * 3 * C, GSVK_ACT_NONE, nullptr, nullptr, h->qkv16)))
       return rc;
-    // S = Q K^T / sqrt(dh), batched over (utterance, head)
-    {
-      TcProblem p{};
-      p.M = T;
-      p.N = T;
-      p.kc = dh;
-      p.taps = 1;
-      p.dil = 1;
-      p.phases = B * H;
-      p.out_rows = T;
-      p.bh = H;
-      p.a_rb = T; p.a_rh = 0; p.a_ch = dh; p.a_c0 = 0;
-      p.b_rb = T; p.b_rh = 0; p.b_ch = dh; p.b_c0 = C;
-      p.c_rb = H * T; p.c_rh = T; p.c_ch = 0;
-      TcEpilogue e = make_epilogue();
-      e.alpha = 1.f / std::sqrt(static_cast<float>(dh));
-      e.c32 = h->s32;
-      e.ld_c32 = Tp;
-      if ((rc = tc_run(h->qkv16, M, 3 * C, h->qkv16, M, 3 * C, p, e, 0, st, 3 * C, 3 * C)))
-        return rc;
-      ++launches;
-    }
-    {
-      const int rows = B * H * T;
-      enc_softmax_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(h->s32, Tp, rows, T,
-                                                                            H, valid, h->p16);
-      if ((rc = check_launch("enc_softmax_kernel"))) return rc;
+    if (fused) {
+      // V^T per (utterance, head), then S, softmax and P V in one kernel
       dim3 grid((unsigned)((Tp + 31) / 32), (unsigned)((dh + 31) / 32), (unsigned)(B * H));
       enc_vt_kernel<<<grid, dim3(32, 8), 0, st>>>(h->qkv16, C, T, H, dh, Tp, h->vt16);
       if ((rc = check_launch("enc_vt_kernel"))) return rc;
+      CUtensorMap tq, tk, tv;
+      if ((rc = make_kmajor_map(&tq, h->qkv16, M, 3 * C, 3 * C, kAttnQ, 64))) return rc;
+      if ((rc = make_kmajor_map(&tk, h->qkv16, M, 3 * C, 3 * C, Tp, 64))) return rc;
+      if ((rc = make_kmajor_map(&tv, h->vt16, (long long)B * H * dh, Tp, Tp, 64, 64))) return rc;
+      enc_attn_kernel<<<dim3((unsigned)((T + kAttnQ - 1) / kAttnQ), (unsigned)H, (unsigned)B),
+                        kAttnThreads,
+                        enc_attn_smem(Tp), st>>>(tq, tk, tv, T, Tp, H, C, valid, h->ctx16,
+                                                 device_status());
+      if ((rc = check_launch("enc_attn_kernel"))) return rc;
       launches += 2;
-    }
-    // ctx = P V_h, written into the head's columns of ctx16
-    {
-      TcProblem p{};
-      p.M = T;
-      p.N = dh;
-      p.kc = Tp;
-      p.taps = 1;
-      p.dil = 1;
-      p.phases = B * H;
-      p.out_rows = T;
-      p.bh = H;
-      p.a_rb = H * T; p.a_rh = T; p.a_ch = 0; p.a_c0 = 0;
-      p.b_rb = H * dh; p.b_rh = dh; p.b_ch = 0; p.b_c0 = 0;
-      p.c_rb = T; p.c_rh = 0; p.c_ch = dh;
-      TcEpilogue e = make_epilogue();
-      e.c16 = h->ctx16;
-      e.ld_c16 = C;
-      if ((rc = tc_run(h->p16, (long long)B * H * T, Tp, h->vt16, (long long)B * H * dh, Tp, p, e,
-                       0, st)))
-        return rc;
-      ++launches;
+    } else {
+      // S = Q K^T / sqrt(dh), batched over (utterance, head)
+      {
+        TcProblem p{};
+        p.M = T;
+        p.N = T;
+        p.kc = dh;
+        p.taps = 1;
+        p.dil = 1;
+        p.phases = B * H;
+        p.out_rows = T;
+        p.bh = H;
+        p.a_rb = T; p.a_rh = 0; p.a_ch = dh; p.a_c0 = 0;
+        p.b_rb = T; p.b_rh = 0; p.b_ch = dh; p.b_c0 = C;
+        p.c_rb = H * T; p.c_rh = T; p.c_ch = 0;
+        TcEpilogue e = make_epilogue();
+        e.alpha = 1.f / std::sqrt(static_cast<float>(dh));
+        e.c32 = h->s32;
+        e.ld_c32 = Tp;
+        if ((rc = tc_run(h->qkv16, M, 3 * C, h->qkv16, M, 3 * C, p, e, 0, st, 3 * C, 3 * C)))
+          return rc;
+        ++launches;
+      }
+      {
+        const int rows = B * H * T;
+        enc_softmax_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(h->s32, Tp, rows, T,
+                                                                              H, valid, h->p16);
+        if ((rc = check_launch("enc_softmax_kernel"))) return rc;
+        dim3 grid((unsigned)((Tp + 31) / 32), (unsigned)((dh + 31) / 32), (unsigned)(B * H));
+        enc_vt_kernel<<<grid, dim3(32, 8), 0, st>>>(h->qkv16, C, T, H, dh, Tp, h->vt16);
+        if ((rc = check_launch("enc_vt_kernel"))) return rc;
+        launches += 2;
+      }
+      // ctx = P V_h, written into the head's columns of ctx16
+      {
+        TcProblem p{};
+        p.M = T;
+        p.N = dh;
+        p.kc = Tp;
+        p.taps = 1;
+        p.dil = 1;
+        p.phases = B * H;
+        p.out_rows = T;
+        p.bh = H;
+        p.a_rb = H * T; p.a_rh = T; p.a_ch = 0; p.a_c0 = 0;
+        p.b_rb = H * dh; p.b_rh = dh; p.b_ch = 0; p.b_c0 = 0;
+        p.c_rb = T; p.c_rh = 0; p.c_ch = dh;
+        TcEpilogue e = make_epilogue();
+        e.c16 = h->ctx16;
+        e.ld_c16 = C;
+        if ((rc = tc_run(h->p16, (long long)B * H * T, Tp, h->vt16, (long long)B * H * dh, Tp, p, e,
+                         0, st)))
+          return rc;
+        ++launches;
+      }
     }
     // attn_out + b + x -> LN1
     if ((rc = gemm(h->ctx16, C, h->wo + (size_t)l * C * C, C, C, h->bo + (size_t)l * C,
                    GSVK_ACT_NONE, x, h->y32, nullptr)))
       return rc;
-    enc_ln_kernel<<<(unsigned)M, 256, 0, st>>>(h->y32, h->ln1g + (size_t)l * C,
-                                               h->ln1b + (size_t)l * C, h->x1_32, h->x1_16, C, c.eps);
-    if ((rc = check_launch("enc_ln_kernel"))) return rc;
+    if ((rc = enc_layernorm(h->y32, h->ln1g + (size_t)l * C, h->ln1b + (size_t)l * C, h->x1_32,
+                            h->x1_16, M, C, c.eps, st)))
+      return rc;
     ++launches;
     // FFN
     if ((rc = gemm(h->x1_16, C, h->wi + (size_t)l * F * C, F, C, h->bi + (size_t)l * F,
@@ -351,9 +652,9 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
     if ((rc = gemm(h->mid16, F, h->wf + (size_t)l * C * F, C, F, h->bf + (size_t)l * C,
                    GSVK_ACT_NONE, h->x1_32, h->f32, nullptr)))
       return rc;
-    enc_ln_kernel<<<(unsigned)M, 256, 0, st>>>(h->f32, h->ln2g + (size_t)l * C,
-                                               h->ln2b + (size_t)l * C, x, h->x16, C, c.eps);
-    if ((rc = check_launch("enc_ln_kernel"))) return rc;
+    if ((rc = enc_layernorm(h->f32, h->ln2g + (size_t)l * C, h->ln2b + (size_t)l * C, x, h->x16, M,
+                            C, c.eps, st)))
+      return rc;
     ++launches;
   }
   h->launches = launches;

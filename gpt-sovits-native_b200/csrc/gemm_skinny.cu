@@ -70,9 +70,6 @@ __device__ __forceinline__ void bulk_to_peer(uint32_t dst_cluster, uint32_t src_
       "r"(src_cta), "r"(bytes), "r"(bar_cluster)
       : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // Epilogue of four adjacent outputs (m, n0..n0+3): y = act(alpha*acc + bias)
 // + res_scale*residual, stored fp32 / fp16 / fp16(act2(y)), 16- or 8-byte
@@ -351,7 +348,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     } else {
       for (int m = 0; m < p.Mp; ++m) my[m * rows_per] = 0.f;
     }
-    fence_proxy_async_smem();  // generic writes of send -> visible to the bulk copies
+    fence_proxy_async_shared();  // generic writes of send -> visible to the bulk copies
     __syncthreads();
     cluster_wait();  // every rank's recv_bar is initialised
     if (tid == 0) {
