@@ -495,6 +495,12 @@ int gsvk_encoder_create(const gsvk_encoder_config* cfg, const gsvk_encoder_host_
     gsvk_encoder_destroy(e);
     return fail(GSVK_ERR_NOMEM, "encoder_create: activations (%zu bytes)", off);
   }
+  // zeroed once: the padding keys of V^T (columns T .. Tp of each row) are
+  // never written by the q|k|v epilogue, and P is exactly 0 there
+  if (int rc = check_cuda(cudaMemset(e->amem, 0, off), "encoder activations memset")) {
+    gsvk_encoder_destroy(e);
+    return rc;
+  }
   uint8_t* a = static_cast<uint8_t*>(e->amem);
   e->x16 = reinterpret_cast<uint16_t*>(a + o_x16);
   e->qkv16 = reinterpret_cast<uint16_t*>(a + o_qkv);
@@ -562,15 +568,36 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
     return gsvk_gemm_f16_ex(&g, stream);
   };
   for (int l = 0; l < c.layers; ++l) {
-    // q|k|v
-    if ((rc = gemm(h->x16, C, h->wqkv + (size_t)l * 3 * C * C, 3 * C, C,
-                   h->bqkv + (size_t)l * 3 * C, GSVK_ACT_NONE, nullptr, nullptr, h->qkv16)))
-      return rc;
+    // q|k|v (with the fused attention, V goes out transposed per head: V^T is
+    // the B operand of P.V)
     if (fused) {
-      // V^T per (utterance, head), then S, softmax and P V in one kernel
-      dim3 grid((unsigned)((Tp + 31) / 32), (unsigned)((dh + 31) / 32), (unsigned)(B * H));
-      enc_vt_kernel<<<grid, dim3(32, 8), 0, st>>>(h->qkv16, C, T, H, dh, Tp, h->vt16);
-      if ((rc = check_launch("enc_vt_kernel"))) return rc;
+      TcProblem p{};
+      p.M = M;
+      p.N = 3 * C;
+      p.kc = C;
+      p.taps = 1;
+      p.dil = 1;
+      p.phases = 1;
+      p.out_rows = M;
+      TcEpilogue e = make_epilogue();
+      e.bias = h->bqkv + (size_t)l * 3 * C;
+      e.c16 = h->qkv16;
+      e.ld_c16 = 3 * C;
+      e.vt = h->vt16;
+      e.vt_ld = Tp;
+      e.vt_c0 = 2 * C;
+      e.vt_T = T;
+      e.vt_dh = dh;
+      e.vt_H = H;
+      if ((rc = tc_run(h->x16, M, C, h->wqkv + (size_t)l * 3 * C * C, 3 * C, C, p, e, 0, st)))
+        return rc;
+      ++launches;
+    } else if ((rc = gemm(h->x16, C, h->wqkv + (size_t)l * 3 * C * C, 3 * C, C,
+                          h->bqkv + (size_t)l * 3 * C, GSVK_ACT_NONE, nullptr, nullptr, h->qkv16))) {
+      return rc;
+    }
+    if (fused) {
+      // S, softmax and P V in one kernel (V^T came from the q|k|v epilogue)
       CUtensorMap tq, tk, tv;
       if ((rc = make_kmajor_map(&tq, h->qkv16, M, 3 * C, 3 * C, kAttnQ, 64))) return rc;
       if ((rc = make_kmajor_map(&tk, h->qkv16, M, 3 * C, 3 * C, Tp, 64))) return rc;
@@ -580,7 +607,7 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
                         enc_attn_smem(Tp), st>>>(tq, tk, tv, T, Tp, H, C, valid, h->ctx16,
                                                  device_status());
       if ((rc = check_launch("enc_attn_kernel"))) return rc;
-      launches += 2;
+      ++launches;
     } else {
       // S = Q K^T / sqrt(dh), batched over (utterance, head)
       {

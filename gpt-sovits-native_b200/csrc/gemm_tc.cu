@@ -123,6 +123,15 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = fmaf(e.res_scale, rr[j], v[j]);
   }
+  if (e.vt && n0 >= e.vt_c0) {  // V columns: transposed per (utterance, head)
+    const long long b = orow / e.vt_T, t = orow - b * e.vt_T;
+    const int col = n0 - e.vt_c0, hh = col / e.vt_dh, d0 = col - (col / e.vt_dh) * e.vt_dh;
+    uint16_t* dst = e.vt + ((b * e.vt_H + hh) * e.vt_dh + d0) * e.vt_ld + t;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (full || n0 + j < N) dst[j * e.vt_ld] = f2h(v[j]);
+    return;
+  }
   if (e.c32) {
     float* dst = e.c32 + orow * e.ld_c32 + oc + n0;
     if (full && aligned16(dst)) {

@@ -40,6 +40,13 @@ struct TcEpilogue {
   float slope2;
   float alpha;
   float res_scale;        // y = act(alpha*acc + bias) + res_scale * residual
+  // Optional transposed output of the columns >= vt_c0 (the V block of a
+  // fused QKV projection): column vt_c0 + h*vt_dh + d of row b*vt_T + t goes
+  // to vt[((b*vt_H + h)*vt_dh + d)*vt_ld + t] as fp16, and those columns
+  // skip the other outputs.
+  uint16_t* vt;
+  long long vt_ld;
+  int vt_c0, vt_T, vt_dh, vt_H;
 };
 
 struct TcProblem {

@@ -39,6 +39,23 @@ def test_encoder_layers_match_oracle(dev, ora, name, B, T, masked):
     assert dev.device_status() == 0
 
 
+def test_encoder_handle_reused_with_shorter_sequences(dev, ora):
+    """One handle, a long batch then a shorter one: the shorter call's padding
+    keys hold the longer call's values and must not leak into its output."""
+    m = dev.workloads.encoder_model("hubert", layers=1, seed=6)
+    enc = dev.Encoder(m, max_batch=2, max_seq=250)
+    for B, T in ((2, 250), (2, 100)):
+        x = dev.workloads.encoder_input("hubert", batch=B, seq=T, seed=T)
+        valid = np.array([T - 5, T - 11], np.int32)
+        ref = x.copy()
+        ora.encoder_layer(m, 0, ref, B, T, valid)
+        xd = torch.from_numpy(x).cuda()
+        enc.forward(xd, B, T, torch.from_numpy(valid).cuda())
+        gate(xd.cpu().numpy(), ref)
+    enc.close()
+    assert dev.device_status() == 0
+
+
 def test_encoder_rejects_oversized(dev):
     m = dev.workloads.encoder_model("hubert", layers=1)
     enc = dev.Encoder(m, max_batch=1, max_seq=64)
