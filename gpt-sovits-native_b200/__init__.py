@@ -43,6 +43,12 @@ SIGNATURES = {
     "gsvk_device_status": (c_int, [c_int]),
     "gsvk_gemm_f16": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "gsvk_gemm_f16_ex": (c_int, [_vp, _vp]),
+    "gsvk_gemm_grouped_f16": (c_int, [_vp, _sz, _vp]),
+    "gsvk_weights_register": (c_int, [_vp, _sz, _sz, _vp]),
+    "gsvk_weights_release": (c_int, [_vp]),
+    "gsvk_weights_data": (_vp, [_vp]),
+    "gsvk_gemm_f16_w": (c_int, [_vp, _vp, _vp]),
+    "gsvk_gemv_f16w_f32acc_w": (c_int, [_vp, _vp, _vp, _vp]),
     "gsvk_f32_to_f16": (c_int, [_vp, _vp, _sz, _vp]),
     "gsvk_f16_to_f32": (c_int, [_vp, _vp, _sz, _vp]),
     "gsvk_gemv_f16w_f32acc": (c_int, [_vp, _vp, _vp, _sz, _sz, _vp]),
@@ -198,6 +204,67 @@ class GemmArgs(ctypes.Structure):
                 ("K", _sz), ("bias", _vp), ("residual", _vp), ("ld_res", _sz), ("c", _vp),
                 ("ldc", _sz), ("c_f16", _vp), ("ldc_f16", _sz), ("act", c_int), ("slope", c_float),
                 ("alpha", c_float)]
+
+
+def _gemm_args(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, c=None,
+               c_f16=None):
+    M, K = a.shape
+    N = b.shape[0]
+    return GemmArgs(_ptr(a), a.stride(0), _ptr(b), b.stride(0), M, N, K, _ptr(bias), _ptr(residual),
+                    0 if residual is None else residual.stride(0), _ptr(c),
+                    0 if c is None else c.stride(0), _ptr(c_f16),
+                    0 if c_f16 is None else c_f16.stride(0), act, slope, alpha)
+
+
+def gemm_grouped(problems, stream=None):
+    """Independent GEMMs submitted together: `problems` is a list of dicts of
+    gemm_ex keyword arguments (a, b, bias, residual, act, slope, alpha, c, c_f16)."""
+    arr = (GemmArgs * len(problems))(*[_gemm_args(**p) for p in problems])
+    check(lib().gsvk_gemm_grouped_f16(arr, len(problems), _stream(stream)))
+
+
+class Weights:
+    """A registered [rows, cols] fp16 weight (host numpy uint16 or a CUDA tensor)."""
+
+    def __init__(self, w, rows: int = None, cols: int = None):
+        if hasattr(w, "ctypes"):
+            rows, cols = w.shape
+            ptr = w.ctypes.data
+        else:
+            rows, cols = w.shape
+            ptr = w.data_ptr()
+        self.rows, self.cols = int(rows), int(cols)
+        h = ctypes.c_void_p()
+        check(lib().gsvk_weights_register(ptr, self.rows, self.cols, ctypes.byref(h)))
+        self.h = h
+
+    def data_ptr(self) -> int:
+        return lib().gsvk_weights_data(self.h)
+
+    def gemm(self, a, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, c=None,
+             c_f16=None, stream=None):
+        M, K = a.shape
+        g = GemmArgs(_ptr(a), a.stride(0), None, 0, M, self.rows, K, _ptr(bias), _ptr(residual),
+                     0 if residual is None else residual.stride(0), _ptr(c),
+                     0 if c is None else c.stride(0), _ptr(c_f16),
+                     0 if c_f16 is None else c_f16.stride(0), act, slope, alpha)
+        check(lib().gsvk_gemm_f16_w(ctypes.byref(g), self.h, _stream(stream)))
+        return c if c is not None else c_f16
+
+    def gemv(self, x, y, stream=None):
+        check(lib().gsvk_gemv_f16w_f32acc_w(self.h, _ptr(x), _ptr(y), _stream(stream)))
+        return y
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().gsvk_weights_release(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def device_status(reset: bool = True) -> int:

@@ -71,6 +71,59 @@ inline void relu(const float* x, float* y, size_t n) {
   check(gsvk_activation(x, y, n, GSVK_ACT_RELU, 0.f, current_stream()), "relu");
 }
 
+// AmxPanel / amx_pack (gemm_f16_amx.hpp:36-50): a weight uploaded once at
+// load time; the panel owns the device copy.  Move-only, like the CPU panel.
+class Panel {
+ public:
+  Panel() = default;
+  Panel(const uint16_t* w, size_t rows, size_t cols) {
+    check(gsvk_weights_register(w, rows, cols, &h_), "gsvk_weights_register");
+    rows_ = rows;
+    cols_ = cols;
+  }
+  Panel(const Panel&) = delete;
+  Panel& operator=(const Panel&) = delete;
+  Panel(Panel&& o) noexcept : h_(o.h_), rows_(o.rows_), cols_(o.cols_) { o.h_ = nullptr; }
+  Panel& operator=(Panel&& o) noexcept {
+    if (this != &o) {
+      gsvk_weights_release(h_);
+      h_ = o.h_;
+      rows_ = o.rows_;
+      cols_ = o.cols_;
+      o.h_ = nullptr;
+    }
+    return *this;
+  }
+  ~Panel() { gsvk_weights_release(h_); }
+  size_t rows() const { return rows_; }
+  size_t cols() const { return cols_; }
+  const uint16_t* data() const { return gsvk_weights_data(h_); }
+  gsvk_weights_t handle() const { return h_; }
+
+ private:
+  gsvk_weights_t h_ = nullptr;
+  size_t rows_ = 0, cols_ = 0;
+};
+// amx_pack (gemm_f16_amx.hpp:45): weights [rows, K] -> panel.
+inline Panel pack(const uint16_t* w, size_t rows, size_t K) { return Panel(w, rows, K); }
+// gemm_f16_amx_pp (gemm_f16_amx.hpp:56) with the weight panel as B: C = A . W^T.
+inline void gemm_panel(const uint16_t* a, const Panel& w, float* c, size_t M) {
+  gsvk_gemm_args g{};
+  g.a = a;
+  g.lda = w.cols();
+  g.M = M;
+  g.N = w.rows();
+  g.K = w.cols();
+  g.c = c;
+  g.ldc = w.rows();
+  g.alpha = 1.f;
+  check(gsvk_gemm_f16_w(&g, w.handle(), current_stream()), "gemm_panel");
+}
+// amx_batch_run (gemm_f16_amx.hpp:64-78): independent GEMMs, submitted together.
+inline void batch_run(const gsvk_gemm_args* nodes, size_t n) {
+  check(gsvk_gemm_grouped_f16(nodes, n, current_stream()), "batch_run");
+}
+
 namespace accel {
 
 // accel.hpp:27

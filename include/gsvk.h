@@ -112,6 +112,27 @@ typedef struct {
 } gsvk_gemm_args;
 int gsvk_gemm_f16_ex(const gsvk_gemm_args* args, gsvk_stream_t stream);
 
+/* Grouped GEMM: `count` independent problems (each with its own operands,
+ * shapes and epilogue) submitted together on one stream, in order.  Replaces
+ * AmxBatchNode + amx_batch_run (gemm_f16_amx.hpp:64-78).  Every group is
+ * validated before any is launched. */
+int gsvk_gemm_grouped_f16(const gsvk_gemm_args* groups, size_t count, gsvk_stream_t stream);
+
+/* ---- weight registration (a8) ------------------------------------------- */
+/* The analogue of amx_pack / AmxPanel (gemm_f16_amx.hpp:36-50): a one-off
+ * load-time upload of a row-major [rows, cols] fp16 weight (host or device
+ * memory) into a device copy the handle owns.  The row-major layout is what
+ * the TMA descriptors read, so no re-packing happens. */
+typedef struct gsvk_weights* gsvk_weights_t;
+int gsvk_weights_register(const uint16_t* w, size_t rows, size_t cols, gsvk_weights_t* out);
+int gsvk_weights_release(gsvk_weights_t w);
+const uint16_t* gsvk_weights_data(gsvk_weights_t w); /* device pointer, [rows, cols] */
+/* gsvk_gemm_f16_ex with B taken from the handle (args->b / ldb ignored;
+ * args->N, K must equal rows, cols). */
+int gsvk_gemm_f16_w(const gsvk_gemm_args* args, gsvk_weights_t w, gsvk_stream_t stream);
+/* gsvk_gemv_f16w_f32acc over a registered [out, in] weight. */
+int gsvk_gemv_f16w_f32acc_w(gsvk_weights_t w, const float* x, float* y, gsvk_stream_t stream);
+
 /* ---- fp32 GEMM (a5) ------------------------------------------------------ */
 /* accel::sgemm (accel.hpp:27): row-major C = alpha op(A) op(B) + beta C with
  * transa/transb 'N' or 'T'; beta == 0 never reads C.  fp32 on CUDA cores. */

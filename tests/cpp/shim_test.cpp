@@ -91,6 +91,39 @@ int main() {
         if (std::fabs(y[t * out + o] - yr[o]) > 1e-5f * peak) ++fails;
     }
   }
+  // pack + gemm_panel == gemm_f16x_fmlal on the same operands; batch_run runs
+  // each node like its own call (gemm_f16_amx.hpp:45-78)
+  {
+    const size_t M = 40, N = 96, K = 128;
+    std::vector<uint16_t> a(M * K), w(N * K);
+    for (auto& v : a) {
+      const _Float16 h = static_cast<_Float16>(rnd());
+      std::memcpy(&v, &h, 2);
+    }
+    for (auto& v : w) {
+      const _Float16 h = static_cast<_Float16>(rnd() * 0.05f);
+      std::memcpy(&v, &h, 2);
+    }
+    uint16_t* da = dev(a);
+    uint16_t* dw = dev(w);
+    float* c1 = dev(std::vector<float>(M * N));
+    float* c2 = dev(std::vector<float>(M * N));
+    float* c3 = dev(std::vector<float>(M * N));
+    gk::Panel panel = gk::pack(w.data(), N, K);  // host source: uploaded once
+    gk::gemm_panel(da, panel, c1, M);
+    gk::gemm_f16x_fmlal(da, dw, c2, M, N, K);
+    gsvk_gemm_args node{};
+    node.a = da;
+    node.b = panel.data();
+    node.M = M;
+    node.N = N;
+    node.K = K;
+    node.c = c3;
+    gk::batch_run(&node, 1);
+    auto h1 = host(c1, M * N), h2 = host(c2, M * N), h3 = host(c3, M * N);
+    for (size_t i = 0; i < M * N; ++i)
+      if (h1[i] != h2[i] || h3[i] != h2[i]) ++fails;
+  }
   // error path: a bad transpose flag throws
   try {
     gk::accel::sgemm('X', 'N', 1, 1, 1, 1.f, nullptr, 1, nullptr, 1, 0.f, nullptr, 1);

@@ -171,3 +171,60 @@ def test_sgemm_against_oracle(dev, ora, ta, tb, M, N, K):
     C = f(C0)
     dev.sgemm(ta, tb, M, N, K, 0.5, f(A), lda, f(B), ldb, 2.0, C, N)
     np.testing.assert_allclose(C.cpu().numpy(), ref, atol=1e-4, rtol=1e-5)
+
+
+# ------------------------------------------- grouped GEMM, registered weights
+def test_gemm_grouped_equals_individual_calls(dev, ora):
+    """gsvk_gemm_grouped_f16 (amx_batch_run's role): independent problems with
+    their own shapes and epilogues, each bit-identical to its own gemm_ex call."""
+    rng = np.random.default_rng(11)
+    shapes = [(64, 1536, 512, 0), (300, 384, 256, 1), (7, 1025, 512, 2), (129, 33, 72, 3)]
+    probs, singles = [], []
+    for M, N, K, act in shapes:
+        a, w = h(rand16(rng, (M, K), 1.0)), h(rand16(rng, (N, K), 0.05))
+        bias = f(rng.standard_normal(N).astype(np.float32) * 0.1)
+        c1 = torch.empty(M, N, device="cuda")
+        c2 = torch.empty(M, N, device="cuda")
+        probs.append(dict(a=a, b=w, bias=bias, act=act, slope=0.1, c=c1))
+        singles.append((a, w, bias, act, c2))
+    dev.gemm_grouped(probs)
+    for (a, w, bias, act, c2), p in zip(singles, probs):
+        dev.gemm_ex(a, w, bias=bias, act=act, slope=0.1, c=c2)
+        assert torch.equal(p["c"], c2)
+        ref = ora.linear_f16(ora.f16_to_f32(a.cpu().numpy().view(np.uint16)),
+                             w.cpu().numpy().view(np.uint16), bias.cpu().numpy(), act, 0.1)
+        assert np.abs(c2.cpu().numpy() - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max())
+    assert dev.device_status() == 0
+
+
+def test_gemm_grouped_rejects_a_bad_group_before_launching(dev):
+    a, w = h(np.zeros((8, 64), np.uint16)), h(np.zeros((16, 64), np.uint16))
+    c = torch.full((8, 16), 7.0, device="cuda")
+    with pytest.raises(dev.GsvkError):
+        dev.gemm_grouped([dict(a=a, b=w, c=c), dict(a=a, b=w)])  # second has no output
+    assert torch.all(c == 7.0)  # nothing ran
+
+
+def test_registered_weights_match_pointer_calls(dev):
+    """gsvk_weights_register (amx_pack's role): GEMM and GEMV through the handle
+    equal the pointer entry points bit for bit, for host and device sources."""
+    rng = np.random.default_rng(12)
+    N, K, M = 2048, 512, 64
+    w = rand16(rng, (N, K), 0.02)
+    x = h(rand16(rng, (M, K), 1.0))
+    bias = f(rng.standard_normal(N).astype(np.float32) * 0.01)
+    wd = h(w)
+    for src in (w, wd):
+        reg = dev.Weights(src)
+        c1 = torch.empty(M, N, device="cuda")
+        c2 = torch.empty(M, N, device="cuda")
+        reg.gemm(x, bias=bias, act=dev.ACT_RELU, c=c1)
+        dev.gemm_ex(x, wd, bias=bias, act=dev.ACT_RELU, c=c2)
+        assert torch.equal(c1, c2)
+        xv = torch.randn(K, device="cuda")
+        y1 = torch.empty(N, device="cuda")
+        reg.gemv(xv, y1)
+        y2 = dev.gemv_f16w_f32acc(wd, xv)
+        assert torch.equal(y1, y2)
+        reg.close()
+    assert dev.device_status() == 0
