@@ -70,6 +70,8 @@ struct DecodeArgs {
   // shared-memory plan (identical in every CTA)
   int mq, mo, m1, m2, ml;  // max rows per CTA of qkv / out / w1 / w2 / logits
   uint32_t layer_bytes;
+  uint32_t ln_off;   // LayerNorm parameters inside a layer buffer: n1g, n1b of the
+                     // layer, then n2g, n2b of the layer before it (fp32, D each)
   // optional phase trace: CTA 0 writes %globaltimer (ns) at every phase
   // boundary of the first kTraceSteps steps, kTraceStride slots per step
   unsigned long long* trace;
@@ -289,7 +291,10 @@ __device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slice
   const size_t D = m.D, F = m.F;
   const uint32_t bq = (s.q1 - s.q0) * D * 2, bo = (s.o1 - s.o0) * D * 2,
                  b1 = (s.a1 - s.a0) * D * 2, b2 = (s.b1 - s.b0) * F * 2;
-  mbar_arrive_expect_tx(bar, bq + bo + b1 + b2);
+  // every CTA normalises full rows, so it also takes the whole LayerNorm
+  // vectors (n1 of layer l, n2 of layer l - 1); one arrival for all bytes
+  const uint32_t vb = static_cast<uint32_t>(D) * 4;
+  mbar_arrive_expect_tx(bar, bq + bo + b1 + b2 + (l > 0 ? 4 * vb : 2 * vb));
   uint8_t* p = buf;
   if (bq) bulk_load(p, m.wqkv + (static_cast<size_t>(l) * 3 * D + s.q0) * D, bq, bar);
   p = buf + static_cast<size_t>(a.mq) * D * 2;
@@ -298,6 +303,13 @@ __device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slice
   if (b1) bulk_load(p, m.w1 + (static_cast<size_t>(l) * F + s.a0) * D, b1, bar);
   p += static_cast<size_t>(a.m1) * D * 2;
   if (b2) bulk_load(p, m.w2 + (static_cast<size_t>(l) * D + s.b0) * F, b2, bar);
+  float* ln = reinterpret_cast<float*>(buf + a.ln_off);
+  bulk_load(ln, m.n1g + static_cast<size_t>(l) * D, vb, bar);
+  bulk_load(ln + D, m.n1b + static_cast<size_t>(l) * D, vb, bar);
+  if (l > 0) {
+    bulk_load(ln + 2 * D, m.n2g + static_cast<size_t>(l - 1) * D, vb, bar);
+    bulk_load(ln + 3 * D, m.n2b + static_cast<size_t>(l - 1) * D, vb, bar);
+  }
 }
 
 template <int HD>
@@ -308,7 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   const int D = m.D, F = m.F, V = m.V, H = m.H, L = m.L;
   uint8_t* wbuf[2] = {smem, smem + a.layer_bytes};
   uint16_t* wlog = reinterpret_cast<uint16_t*>(smem + 2 * static_cast<size_t>(a.layer_bytes));
-  float* slots = reinterpret_cast<float*>(wlog + static_cast<size_t>(a.ml) * D);  // attention
+  float* lnf = reinterpret_cast<float*>(wlog + static_cast<size_t>(a.ml) * D);  // last LN2 g, b
+  float* slots = lnf + 2 * D;                                                  // attention
   float* xs = slots + kSlots * slot_floats<HD>();         // layer input x
   float* hs = xs + D;                                     // LN1 output h
   float* act = hs + D;                                    // operand, max(D, F)
@@ -341,8 +354,10 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   __syncthreads();
   if (tid == 0) {
     const uint32_t bl = (s.l1 - s.l0) * D * 2;
-    mbar_arrive_expect_tx(&mbar[2], bl);
+    mbar_arrive_expect_tx(&mbar[2], bl + 2u * D * 4);
     if (bl) bulk_load(wlog, m.wpred + static_cast<size_t>(s.l0) * D, bl, &mbar[2]);
+    bulk_load(lnf, m.n2g + static_cast<size_t>(L - 1) * D, D * 4, &mbar[2]);
+    bulk_load(lnf + D, m.n2b + static_cast<size_t>(L - 1) * D, D * 4, &mbar[2]);
     // the global layer sequence g = 0, 1, 2, ... runs layer g % L from buffer g & 1
     prefetch_layer(m, a, s, 0, wbuf[0], &mbar[0]);
     prefetch_layer(m, a, s, 1 % L, wbuf[1], &mbar[1]);
@@ -448,22 +463,25 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       const uint16_t* W1 = Wo + static_cast<size_t>(a.mo) * D;
       const uint16_t* W2 = W1 + static_cast<size_t>(a.m1) * D;
       // ---------------------------------------------------------------- P1
-      if (l > 0) {
-        load_vec<2>(xs, m.xpre, D);
-        __syncthreads();
-        ln_canon(xs, m.n2g + static_cast<size_t>(l - 1) * D, m.n2b + static_cast<size_t>(l - 1) * D,
-                 D, m.eps, red);
-      }
-      for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(xs[i]));
-      GSVK_TR(16 + 16 * l + 10);
+      // this layer's buffer: weight slices and the LayerNorm vectors
       if (!mbar_wait(&mbar[b], uses[b] & 1u, m.status)) {
         alive = false;
         break;
       }
       ++uses[b];
       pending[b] = 0;
-      __syncthreads();
+      const float* lnb = reinterpret_cast<const float*>(wbuf[b] + a.ln_off);
       GSVK_TR(16 + 16 * l + 11);
+      if (l > 0) {
+        load_vec<2>(xs, m.xpre, D);
+        __syncthreads();
+        GSVK_TR(16 + 16 * l + 14);
+        ln_canon(xs, lnb + 2 * D, lnb + 3 * D, D, m.eps, red);  // LN2 of layer l - 1
+        GSVK_TR(16 + 16 * l + 15);
+      }
+      for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(xs[i]));
+      __syncthreads();
+      GSVK_TR(16 + 16 * l + 10);
       {
         uint16_t* kl = m.kc + (static_cast<size_t>(l) * m.cap + pos) * D;
         uint16_t* vl = m.vc + (static_cast<size_t>(l) * m.cap + pos) * D;
@@ -574,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       // ---------------------------------------------------------------- P4
       load_vec<2>(hs, m.hpre, D);
       __syncthreads();
-      ln_canon(hs, m.n1g + static_cast<size_t>(l) * D, m.n1b + static_cast<size_t>(l) * D, D, m.eps,
+      ln_canon(hs, lnb, lnb + D, D, m.eps,
                red);
       for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(hs[i]));
       __syncthreads();
@@ -627,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
     // ---------------------------------------------------------------- logits
     load_vec<2>(xs, m.xpre, D);
     __syncthreads();
-    ln_canon(xs, m.n2g + static_cast<size_t>(L - 1) * D, m.n2b + static_cast<size_t>(L - 1) * D, D,
+    ln_canon(xs, lnf, lnf + D, D,
              m.eps, red);
     for (int r = s.l0 + warp; r < s.l1; r += kWarps) {
       const float acc = warp_dot32(wlog + static_cast<size_t>(r - s.l0) * D, xs, D);
@@ -1014,12 +1032,14 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   a.m1 = ceil_rows(F);
   a.m2 = ceil_rows(D);
   a.ml = ceil_rows(V);
-  a.layer_bytes = static_cast<uint32_t>(align_up(
-      ((size_t)a.mq * D + (size_t)a.mo * D + (size_t)a.m1 * D + (size_t)a.m2 * F) * 2, 128));
+  a.ln_off = static_cast<uint32_t>(align_up(
+      ((size_t)a.mq * D + (size_t)a.mo * D + (size_t)a.m1 * D + (size_t)a.m2 * F) * 2, 16));
+  a.layer_bytes = static_cast<uint32_t>(align_up((size_t)a.ln_off + (size_t)4 * D * 4, 128));
   const size_t slot_f = (size_t)kSlots * (HD == 32 ? slot_floats<32>() : slot_floats<64>());
   const size_t max_nch = ((size_t)cap + kChunk - 1) / kChunk;
   const size_t floats = slot_f + (size_t)D * 2 + std::max(D, F) + kChunk + 64;
-  e->decode_smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 + floats * 4 + 8 * 4 +
+  e->decode_smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 + (size_t)2 * D * 4 +
+                   floats * 4 + 8 * 4 +
                    4 * 8 + align_up(V, 16) + 64;
   e->attn_smem = (slot_f + max_nch * (HD + 4)) * 4;
   e->HD = HD;
