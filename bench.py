@@ -584,7 +584,7 @@ def run_t2s_batch(args, rank, local, world):
     g.device_init(local)
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
-    B, S = 64, 32
+    B, S = args.batch, 32
     m = g.workloads.t2s_model(seed=1)
     lens = g.workloads.t2s_batched_lengths(B, seed=1)
     cap = int(lens.max()) + S
@@ -637,7 +637,7 @@ def run_t2s_batch(args, rank, local, world):
     alg = sum(w_bytes + kv * int(np.sum(lens + s + 1)) + kv * B for s in range(S))
     hbm, _, kind = measured_peaks()
     tokens = B * S
-    line = {"metric": "batched T2S decode tokens/s (64 utterances per GPU)",
+    line = {"metric": f"batched T2S decode tokens/s ({B} utterances per GPU)",
             "value": tokens * world / t, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -702,6 +702,8 @@ def main():
     ap.add_argument("--encoder", default="bert", choices=["bert", "hubert"])
     ap.add_argument("--gemm-shape", default="4096,4096,1024",
                     help="M,N,K of the gemm workload")
+    ap.add_argument("--batch", type=int, default=64,
+                    help="utterances of the t2s_decode_b64 workload (64 = BASELINE config 3)")
     ap.add_argument("--decode-steps", type=int, default=T2S_STEPS,
                     help="tokens per utterance (default 500; smaller only for profiling captures)")
     args = ap.parse_args()

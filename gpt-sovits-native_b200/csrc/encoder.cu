@@ -223,61 +223,61 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int nv = valid ? valid[b] : T;
   const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
   constexpr float kScale = 0.125f;  // 1 / sqrt(64)
+  // pass 1: row max.  Chunks wholly inside the valid keys skip the masks.
+  const int kfull = nv < T ? nv : T;  // keys [0, kfull) need no mask
   float mx = -INFINITY;
   for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
     uint32_t v[16];
     tmem_ld16(t_row + static_cast<uint32_t>(c0), v);
     tmem_ld_wait();
+    if (c0 + 16 <= kfull) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int k = c0 + j;
-      float x = __uint_as_float(v[j]) * kScale;
-      if (k >= nv) x = x + -3.40282347e+38f;
-      if (k < T) mx = fmaxf(mx, x);
+      for (int j = 0; j < 16; ++j) mx = fmaxf(mx, __uint_as_float(v[j]) * kScale);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int k = c0 + j;
+        float x = __uint_as_float(v[j]) * kScale;
+        if (k >= nv) x = x + -3.40282347e+38f;
+        if (k < T) mx = fmaxf(mx, x);
+      }
     }
   }
   red[grp * kAttnQ + r] = mx;
   __syncthreads();
   mx = fmaxf(fmaxf(red[r], red[kAttnQ + r]), fmaxf(red[2 * kAttnQ + r], red[3 * kAttnQ + r]));
+  // pass 2: e = exp(x - max) written as fp16 P (unnormalised; O is scaled by
+  // 1 / sum in the epilogue) while the row sum accumulates
   float sum = 0.f;
   for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
     uint32_t v[16];
     tmem_ld16(t_row + static_cast<uint32_t>(c0), v);
     tmem_ld_wait();
+    float e[16];
+    if (c0 + 16 <= kfull) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int k = c0 + j;
-      float x = __uint_as_float(v[j]) * kScale;
-      if (k >= nv) x = x + -3.40282347e+38f;
-      if (k < T) sum += __expf(x - mx);
+      for (int j = 0; j < 16; ++j) e[j] = __expf(fmaf(__uint_as_float(v[j]), kScale, -mx));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int k = c0 + j;
+        float x = __uint_as_float(v[j]) * kScale;
+        if (k >= nv) x = x + -3.40282347e+38f;
+        e[j] = k < T ? __expf(x - mx) : 0.f;
+      }
     }
-  }
-  red[4 * kAttnQ + grp * kAttnQ + r] = sum;
-  __syncthreads();
-  const float* rs = red + 4 * kAttnQ;
-  const float inv = 1.f / (((rs[r] + rs[kAttnQ + r]) + rs[2 * kAttnQ + r]) + rs[3 * kAttnQ + r]);
-  for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
-    uint32_t v[16];
-    tmem_ld16(t_row + static_cast<uint32_t>(c0), v);
-    tmem_ld_wait();
     uint32_t pk[8];
 #pragma unroll
-    for (int j = 0; j < 16; j += 2) {
-      float e[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int k = c0 + j + u;
-        float x = __uint_as_float(v[j + u]) * kScale;
-        if (k >= nv) x = x + -3.40282347e+38f;
-        e[u] = k < T ? __expf(x - mx) * inv : 0.f;
-      }
-      pk[j / 2] = f2h2(e[0], e[1]);
+    for (int j = 0; j < 8; ++j) {
+      sum += e[2 * j] + e[2 * j + 1];
+      pk[j] = f2h2(e[2 * j], e[2 * j + 1]);
     }
     uint8_t* region = sP + (c0 >> 6) * (kAttnQ * 128);
     const int cc = c0 & 63;  // 16 keys = two 16-byte chunks
     *reinterpret_cast<uint4*>(region + sw128_offset(r, cc)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     *reinterpret_cast<uint4*>(region + sw128_offset(r, cc + 8)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
   }
+  red[4 * kAttnQ + grp * kAttnQ + r] = sum;
   fence_proxy_async_shared();  // P (generic writes) -> visible to the tensor core
   tc_fence_before();
   __syncthreads();
@@ -297,10 +297,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
   __syncthreads();
   tc_fence_after();
-  {  // group g stores O columns [16 g, 16 g + 16) of its rows
+  {  // group g stores O columns [16 g, 16 g + 16) of its rows, scaled by 1 / row sum
+    const float* rs = red + 4 * kAttnQ;
+    const float inv = 1.f / (((rs[r] + rs[kAttnQ + r]) + rs[2 * kAttnQ + r]) + rs[3 * kAttnQ + r]);
     uint32_t v[16];
     tmem_ld16(t_row + o_col + 16u * static_cast<uint32_t>(grp), v);
     tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * inv);
     if (q < T) {
       uint4* dst = reinterpret_cast<uint4*>(ctx + static_cast<size_t>(row0 + q) * C + h * kAttnDh +
                                             16 * grp);
