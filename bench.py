@@ -307,7 +307,7 @@ def run_gemm1(args, rank, local, world):
     # Steady state: `iters` launches per step captured in one CUDA graph as
     # `branches` independent streams of back-to-back GEMMs (independent
     # instances, each on its own rotating X/W/Y copies).
-    iters, branches = 1024, 4
+    iters, branches = 1024, 8
     for i in range(copies):
         g.gemm_ex(xs[i], ws[i], bias=bd, act=g.ACT_RELU, c_f16=ys[i])
     torch.cuda.synchronize(dev)

@@ -432,8 +432,11 @@ int skinny_run(const uint16_t* x, int M, long long ldx, const uint16_t* w, int N
   const int n_tiles = (N + kSkTileN - 1) / kSkTileN;
   // smallest power-of-two split that fits the stages, then widen while the
   // GPU is under-filled and every CTA still gets a K block
+  // Split K only for up to 64 activation rows: the exchanged partial tile
+  // grows with M (Mp x 128 fp32 per CTA), and from M = 65 up a whole-K CTA
+  // per 128-row weight tile is cheaper than the cluster exchange.
   int split = 1;
-  while (split < kSkMaxSplit && static_cast<long long>(n_tiles) * split < sm_count() &&
+  while (p.Mp <= 64 && split < kSkMaxSplit && static_cast<long long>(n_tiles) * split < sm_count() &&
          split * 2 <= p.kb_total)
     split *= 2;
   if (force_split > 0) {
