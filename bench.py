@@ -100,44 +100,34 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------- distributed
+# One process per GPU; the package's replicas module holds the host logic
+# (NCCL only for barriers, the max-over-ranks time and result gathering).
+def _replicas():
+    return __import__("__graft_entry__").package().replicas
+
+
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import torch
-        import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
+        _replicas().init("nccl", rank, world, device=torch.device("cuda", local))
     return rank, local, world
 
 
 def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
+    _replicas().barrier(world)
 
 
 def max_over_ranks(v, world):
-    if world <= 1:
-        return v
-    import torch
-    import torch.distributed as dist
-
-    t = torch.tensor([float(v)], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return t.item()
+    return _replicas().max_over_ranks(v, world, device="cuda" if world > 1 else None)
 
 
 def dist_close(world):
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    _replicas().close(world)
 
 
 # ----------------------------------------------------- CPU baseline (oracle)

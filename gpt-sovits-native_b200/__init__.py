@@ -15,6 +15,7 @@ import ctypes
 import os
 from ctypes import c_char, c_double, c_float, c_int, c_size_t, c_void_p
 
+from . import replicas  # noqa: F401  (multi-GPU host logic: shards, barriers, gathers)
 from . import workloads  # noqa: F401  (seeded synthetic inputs)
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
