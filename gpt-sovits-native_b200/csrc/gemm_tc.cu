@@ -180,11 +180,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   // into parameter space are re-read after every global store).
   const TcProblem p = prob;
   const TcEpilogue e = epi;
-  constexpr uint32_t kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+  // Narrow tiles (BN <= 64) have short, latency-bound epilogues: two groups of
+  // four epilogue warps take alternate tiles (each its tile's every column)
+  // and four TMEM accumulators let the MMAs run ahead.  Wide tiles: one group
+  // splitting the columns, two accumulators.
+  constexpr int kGroups = BN <= 64 ? 2 : 1;
+  constexpr int kAcc = BN <= 64 ? 4 : 2;
+  constexpr uint32_t kTmemCols = kAcc * BN <= 32 ? 32u : (kAcc * BN <= 64 ? 64u :
+                                 (kAcc * BN <= 128 ? 128u : (kAcc * BN <= 256 ? 256u : 512u)));
   const int bk = p.bk;
   const uint32_t swz_bytes = static_cast<uint32_t>(bk) * 2;          // 32, 64 or 128
   const uint32_t swz_code = swz_bytes == 128 ? 2u : (swz_bytes == 64 ? 4u : 6u);
-  const uint32_t a_bytes = kBM * swz_bytes, b_bytes = BN * swz_bytes;
+  const bool win = p.win > 0;
+  // stage sizes: a tap tile, or (window mode) a whole input window rounded to the 1 KB swizzle atom
+  const uint32_t a_bytes = win ? (static_cast<uint32_t>(p.win) * swz_bytes + 1023u) & ~1023u
+                               : kBM * swz_bytes;
+  const uint32_t b_bytes = BN * swz_bytes;
+  const uint32_t b_region = win ? static_cast<uint32_t>(p.taps) * b_bytes
+                                : static_cast<uint32_t>(stages) * b_bytes;
   const uint32_t sbo = 8 * swz_bytes;                                  // 8-row atom stride
   const int ksteps = bk / 16;
   constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
@@ -194,11 +207,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + static_cast<size_t>(stages) * a_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + static_cast<size_t>(stages) * b_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + b_region);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tempty = tfull + kAcc;
+  uint64_t* bbar = tempty + kAcc;  // window mode: all taps' weights landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bbar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (p.M + kBM - 1) / kBM, n_tiles = (p.N + BN - 1) / BN;
@@ -210,10 +224,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kAcc; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], kEpiWarps / kGroups);
     }
+    mbar_init(bbar, 1);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -232,7 +247,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------- producer
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      if (win) {
+        // every tap's weights once; then one input window per tile
+        mbar_arrive_expect_tx(bbar, b_region);
+        for (int t = 0; t < p.taps; ++t)
+          tma_load_2d(sB + static_cast<size_t>(t) * b_bytes, &tmB, bbar, 0, t * p.b_tap_rows);
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it) {
+          const int mt = tile;  // one column tile, one phase
+          const int s = it % stages;
+          const uint32_t ph = static_cast<uint32_t>(it / stages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(p.win) * swz_bytes);
+          tma_load_2d(sA + static_cast<size_t>(s) * a_bytes, &tmA, &full[s], 0, mt * kBM - p.pad);
+        }
+      }
+      for (int tile = blockIdx.x; tile < tiles && ok && !win; tile += gridDim.x) {
         const int phase = tile / (m_tiles * n_tiles);
         const int rem = tile - phase * m_tiles * n_tiles;
         const int mt = rem / n_tiles, nt = rem - (rem / n_tiles) * n_tiles;
@@ -260,15 +292,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // --------------------------------------------------------- MMA issuer
       int it = 0, tl = 0;
-      bool ok = true;
+      bool ok = !win || mbar_wait(bbar, 0, status);
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++tl) {
         const int phase = tile / (m_tiles * n_tiles);
         const TapPlan tp = plan_for(p, phase);
-        const int acc = tl & 1;
-        const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
+        const int acc = tl % kAcc;
+        const uint32_t aph = static_cast<uint32_t>(tl / kAcc) & 1u;
         if (!mbar_wait(&tempty[acc], aph ^ 1u, status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+        if (win) {
+          // tap t reads window rows [t*dil, t*dil + 128): a start-address shift
+          const int s = it % stages;
+          const uint32_t ph = static_cast<uint32_t>(it / stages) & 1u;
+          if (!mbar_wait(&full[s], ph, status)) break;
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + static_cast<size_t>(s) * a_bytes);
+          const uint32_t b_base = smem_u32(sB);
+          for (int t = 0; t < p.taps; ++t) {
+            const uint32_t a_t = a_base + static_cast<uint32_t>(t * p.dil) * swz_bytes;
+            const uint32_t b_t = b_base + static_cast<uint32_t>(t) * b_bytes;
+            for (int j = 0; j < ksteps; ++j)
+              tc_mma_f16(d_tmem, smem_desc(a_t + 32u * j, sbo, swz_code),
+                         smem_desc(b_t + 32u * j, sbo, swz_code), idesc, (t | j) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          ++it;
+          tc_commit(&tfull[acc]);
+          continue;
+        }
         const int nk = tp.ntaps * kpt;
         for (int kk = 0; kk < nk; ++kk, ++it) {
           const int s = it % stages;
@@ -294,19 +346,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;            // TMEM lanes 32*quarter .. +31
-    const int half = (warp - 2) >> 2;        // column half of the tile
-    const int cw = BN >= 32 ? BN / 2 : BN;   // columns per warp
-    const int cbeg = BN >= 32 ? half * cw : 0;
-    const bool cols_ok = BN >= 32 || half == 0;
+    const int half = (warp - 2) >> 2;        // epilogue group (two groups) or column half
+    const int cw = kGroups == 2 ? BN : BN / 2;  // columns per warp
+    const int cbeg = kGroups == 2 ? 0 : half * cw;
+    const bool cols_ok = true;
     const bool bias_vec = e.bias && aligned16(e.bias);
     int tl = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tl) {
+      if (kGroups == 2 && (tl & 1) != half) continue;  // the other group's tile
       const int phase = tile / (m_tiles * n_tiles);
       const int rem = tile - phase * m_tiles * n_tiles;
       const int mt = rem / n_tiles, nt = rem - (rem / n_tiles) * n_tiles;
       const TapPlan tp = plan_for(p, phase);
-      const int acc = tl & 1;
-      const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
+      const int acc = tl % kAcc;
+      const uint32_t aph = static_cast<uint32_t>(tl / kAcc) & 1u;
       const int i = mt * kBM + quarter * 32 + lane;
       const int q = tp.q0 + i;
       const bool row_ok = (i < p.M) && (q <= tp.qmax);
@@ -349,10 +402,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN>
 int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
               const TcEpilogue& e, cudaStream_t st) {
-  const int stage_bytes = (kBM + BN) * p.bk * 2;
-  int stages = kSmemBudget / stage_bytes;
-  stages = std::max(2, std::min(stages, 8));
-  const size_t smem = 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * stages + 4) * 8 + 16;
+  int stages;
+  size_t smem;
+  if (p.win) {  // window stages + every tap's weights (tc_run checked that two stages fit)
+    const size_t a_win = (static_cast<size_t>(p.win) * p.bk * 2 + 1023) & ~static_cast<size_t>(1023);
+    const size_t b_all = static_cast<size_t>(p.taps) * BN * p.bk * 2;
+    stages = static_cast<int>(std::min<size_t>(8, (kSmemBudget - b_all) / a_win));
+    smem = 1024 + stages * a_win + b_all + (2 * stages + 9) * 8 + 16;
+  } else {
+    const int stage_bytes = (kBM + BN) * p.bk * 2;
+    stages = std::max(2, std::min(kSmemBudget / stage_bytes, 8));
+    smem = 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * stages + 9) * 8 + 16;
+  }
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -441,8 +502,17 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
     return fail(GSVK_ERR_INVALID, "empty GEMM");
   p.bk = pick_bk(p.kc);
   if (bn == 0) bn = tc_pick_bn(p.M, p.N);
+  // window mode: a dilated conv with one K block per tap and one column tile,
+  // whose input window (<= 256 rows, the TMA box limit) and weights fit
+  p.win = 0;
+  if (!p.convt && p.bh == 0 && p.phases == 1 && p.taps > 1 && p.kc <= p.bk && bn >= p.N) {
+    const long long R = kBM + static_cast<long long>(p.taps - 1) * p.dil;
+    const long long a_win = (R * p.bk * 2 + 1023) & ~1023LL;
+    const long long b_all = static_cast<long long>(p.taps) * bn * p.bk * 2;
+    if (R <= 256 && b_all + 2 * a_win <= kSmemBudget) p.win = static_cast<int>(R);
+  }
   CUtensorMap ta, tb;
-  int rc = make_kmajor_map(&ta, a, a_rows, a_cols ? a_cols : p.kc, lda, kBM, p.bk);
+  int rc = make_kmajor_map(&ta, a, a_rows, a_cols ? a_cols : p.kc, lda, p.win ? p.win : kBM, p.bk);
   if (rc) return rc;
   rc = make_kmajor_map(&tb, b, b_rows, b_cols ? b_cols : p.kc, ldb, bn, p.bk);
   if (rc) return rc;

@@ -16,11 +16,13 @@
 //                        output row = q*u + r - pad with q = i + q0(r)   (polyphase, no scatter)
 //
 // Roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer and TMEM
-// owner, warps 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31, warps
-// 2..5 the left half of the tile's columns, 6..9 the right half).  Bias and
-// residual chunks are fetched one chunk ahead of their use.
-// Two TMEM accumulators let the epilogue of tile i overlap the mainloop of
-// tile i+1.  Every mbarrier wait is bounded (see tma.cuh).
+// owner, warps 2..9 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).  For
+// tiles wider than 64 columns warps 2..5 take the left half of the columns
+// and 6..9 the right half (two TMEM accumulators); for narrower tiles the two
+// groups take alternate tiles (four accumulators).  Bias and residual chunks
+// are fetched one chunk ahead of their use.
+// Several TMEM accumulators let the epilogue of tile i overlap the mainloop of
+// the following tiles.  Every mbarrier wait is bounded (see tma.cuh).
 #pragma once
 
 #include "tma.cuh"
@@ -69,6 +71,12 @@ struct TcProblem {
   int bh;
   int a_rb, a_rh, a_ch, b_rb, b_rh, b_ch, c_rb, c_rh, c_ch;
   int a_c0, b_c0;
+  // Window mode (win > 0, plain conv with one K block per tap and one column
+  // tile): one TMA load of win = 128 + (taps-1)*dil input rows per output tile
+  // serves every tap as a row-shifted operand descriptor (the swizzle follows
+  // absolute shared-memory addresses, so any row start is valid); all taps'
+  // weights are loaded once per CTA.
+  int win;
 };
 
 }  // namespace gsvk

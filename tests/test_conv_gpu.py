@@ -32,7 +32,10 @@ def gate(got, ref, rel=1e-3, min_cos=0.9999):
 
 CONV_CASES = [(192, 512, 37, 7, 1), (256, 256, 100, 3, 5), (128, 128, 150, 11, 3),
               (16, 16, 500, 7, 5), (32, 32, 300, 11, 1), (16, 1, 200, 7, 1), (64, 48, 129, 3, 1),
-              (24, 24, 64, 3, 3)]
+              (24, 24, 64, 3, 3),
+              # window mode (one input window per tile serves every tap): the largest
+              # weights (11 taps x 64 x 64), and more tiles than SMs (ring reuse)
+              (64, 64, 400, 11, 5), (16, 16, 40000, 11, 5)]
 
 
 @pytest.mark.parametrize("Ci,Co,T,k,dil", CONV_CASES)
