@@ -83,6 +83,7 @@ SIGNATURES = {
     "gsvk_decoder_destroy": (c_int, [_vp]),
     "gsvk_decoder_forward": (c_int, [_vp, _vp, _sz, _vp, _vp]),
     "gsvk_decoder_launches": (c_int, [_vp]),
+    "gsvk_decoder_set_graph": (c_int, [_vp, c_int]),
     "gsvk_sgemm": (c_int, [c_char, c_char, c_int, c_int, c_int, c_float, _vp, c_int, _vp, c_int,
                            c_float, _vp, c_int, _vp]),
     "gsvk_encoder_create": (c_int, [_vp, _vp, _vp]),
@@ -567,6 +568,11 @@ class Decoder:
 
     def launches(self) -> int:
         return lib().gsvk_decoder_launches(self.h)
+
+    def set_graph(self, enable: bool):
+        """Replay the layers as one CUDA graph per input length (default) or
+        launch them one by one; the results are identical."""
+        check(lib().gsvk_decoder_set_graph(self.h, int(bool(enable))))
 
     def close(self):
         if self.h:

@@ -87,18 +87,6 @@ __global__ void cl_to_cm32_kernel(const float* __restrict__ x, int T, int C, flo
 // Resblock mean (dec.hpp:323-334): j == 0: sum = cur * (1/3); else
 // sum = sum + cur * (1/3) (separately rounded multiply and add); after the
 // last resblock also emit the next stage's fp16 input lrelu(sum, slope).
-__global__ void res_mean_kernel(const float* __restrict__ cur, float* __restrict__ sum, size_t n,
-                                int first, uint16_t* __restrict__ next16, float slope) {
-  const float kinv = 1.f / 3.f;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const float t = __fmul_rn(cur[i], kinv);
-    const float s = first ? t : __fadd_rn(sum[i], t);
-    sum[i] = s;
-    if (next16) next16[i] = f2h(s < 0.f ? __fmul_rn(s, slope) : s);
-  }
-}
-
 unsigned grid_for(size_t n) {
   size_t g = (n + 255) / 256;
   const size_t cap = static_cast<size_t>(sm_count()) * 16;
@@ -121,9 +109,9 @@ TcEpilogue conv_epilogue(const gsvk_conv_args* c) {
   return e;
 }
 
-int check_conv(const gsvk_conv_args* c, const char* who) {
-  if (!c || !c->x || !c->w || (!c->y && !c->y_f16 && !c->y_f16_act) || c->T == 0 || c->ci == 0 ||
-      c->co == 0 || c->k == 0 || c->dil == 0)
+int check_conv(const gsvk_conv_args* c, const char* who, bool other_out) {
+  if (!c || !c->x || !c->w || (!c->y && !c->y_f16 && !c->y_f16_act && !other_out) || c->T == 0 ||
+      c->ci == 0 || c->co == 0 || c->k == 0 || c->dil == 0)
     return fail(GSVK_ERR_INVALID, "%s: null pointer or zero size", who);
   if (c->T > 0x3fffffff || c->ci > 65536 || c->co > 65536 || c->k > 64 || c->dil > 4096)
     return fail(GSVK_ERR_UNSUPPORTED, "%s: size outside the kernel envelope", who);
@@ -145,8 +133,24 @@ static void convt_phase_rows(long long T, int u, int pad, int r, long long* q0, 
   *qmax = top >= 0 ? top / u : -1;
 }
 
-int conv1d_run(const gsvk_conv_args* c, cudaStream_t st) {
-  if (int rc = check_conv(c, "conv1d")) return rc;
+// Engine-internal additions to a conv launch (not part of gsvk_conv_args).
+struct ConvFuse {
+  float* mean_sum = nullptr;  // TcEpilogue running mean
+  float mean_scale = 1.f;
+  int mean_first = 0;
+  int pdl = 0;                // TcProblem::pdl (the weights are immutable)
+};
+
+static void apply_fuse(const ConvFuse* f, TcProblem* p, TcEpilogue* e) {
+  if (!f) return;
+  e->mean_sum = f->mean_sum;
+  e->mean_scale = f->mean_scale;
+  e->mean_first = f->mean_first;
+  p->pdl = f->pdl;
+}
+
+int conv1d_run(const gsvk_conv_args* c, cudaStream_t st, const ConvFuse* f = nullptr) {
+  if (int rc = check_conv(c, "conv1d", f && f->mean_sum)) return rc;
   const long long dil = static_cast<long long>(c->dil), k = static_cast<long long>(c->k);
   TcProblem p{};
   p.M = static_cast<int>(c->T);
@@ -159,12 +163,14 @@ int conv1d_run(const gsvk_conv_args* c, cudaStream_t st) {
   p.convt = 0;
   p.phases = 1;
   p.out_rows = static_cast<int>(c->T);
+  TcEpilogue e = conv_epilogue(c);
+  apply_fuse(f, &p, &e);
   return tc_run(c->x, (long long)c->T, (long long)c->ci, c->w, k * (long long)c->co,
-                (long long)c->ci, p, conv_epilogue(c), 0, st);
+                (long long)c->ci, p, e, 0, st);
 }
 
-int convt1d_run(const gsvk_conv_args* c, cudaStream_t st) {
-  if (int rc = check_conv(c, "convt1d")) return rc;
+int convt1d_run(const gsvk_conv_args* c, cudaStream_t st, const ConvFuse* f = nullptr) {
+  if (int rc = check_conv(c, "convt1d", f && f->mean_sum)) return rc;
   const int u = static_cast<int>(c->dil), k = static_cast<int>(c->k);
   if (k < u || (k - u) % 2 != 0)
     return fail(GSVK_ERR_UNSUPPORTED, "convt1d: needs kernel >= stride and (kernel - stride) even");
@@ -186,8 +192,10 @@ int convt1d_run(const gsvk_conv_args* c, cudaStream_t st) {
   p.convt = 1;
   p.phases = u;
   p.out_rows = static_cast<int>(c->T * u);
+  TcEpilogue e = conv_epilogue(c);
+  apply_fuse(f, &p, &e);
   return tc_run(c->x, (long long)c->T, (long long)c->ci, c->w, (long long)k * (long long)c->co,
-                (long long)c->ci, p, conv_epilogue(c), 0, st);
+                (long long)c->ci, p, e, 0, st);
 }
 
 // ---------------------------------------------------------------- generator
@@ -203,6 +211,20 @@ struct DecoderEngine {
   uint16_t *in16 = nullptr, *a16 = nullptr, *xu16 = nullptr, *t16a = nullptr, *t16b = nullptr;
   float *xu32 = nullptr, *cur32 = nullptr, *sum32 = nullptr, *wav_cl = nullptr;
   int launches = 0;
+  // The layers between conv_pre and conv_post touch only the buffers above,
+  // so they are captured once per input length into a CUDA graph (on a
+  // private stream) and replayed on the caller's stream.
+  struct Graph {
+    size_t T;
+    cudaGraphExec_t exec;
+    int launches;
+    unsigned long long used;
+  };
+  static constexpr size_t kMaxGraphs = 8;
+  bool use_graph = true;
+  cudaStream_t capture = nullptr;
+  std::vector<Graph> graphs;
+  unsigned long long tick = 0;
 };
 
 }  // namespace gsvk
@@ -261,6 +283,9 @@ size_t gsvk_decoder_out_len(const gsvk_decoder_config* cfg, size_t T) {
 
 int gsvk_decoder_destroy(gsvk_decoder_t h) {
   if (!h) return GSVK_OK;
+  if (!h->graphs.empty()) cudaDeviceSynchronize();  // no replay may be in flight
+  for (auto& g : h->graphs) cudaGraphExecDestroy(g.exec);
+  if (h->capture) cudaStreamDestroy(h->capture);
   if (h->wmem) cudaFree(h->wmem);
   if (h->amem) cudaFree(h->amem);
   delete h;
@@ -375,9 +400,144 @@ int gsvk_decoder_create(const gsvk_decoder_config* cfg, const uint16_t* const* w
   e->cur32 = reinterpret_cast<float*>(a + n32);
   e->sum32 = reinterpret_cast<float*>(a + 2 * n32);
   e->wav_cl = reinterpret_cast<float*>(a + 3 * n32);
+  if (int rc = check_cuda(cudaStreamCreateWithFlags(&e->capture, cudaStreamNonBlocking),
+                          "decoder capture stream")) {
+    gsvk_decoder_destroy(e);
+    return rc;
+  }
   *out = e;
   return GSVK_OK;
 }
+
+}  // extern "C"
+
+namespace gsvk {
+
+// conv_pre and the upsampling stages (dec.hpp:267-300): reads in16, leaves
+// lrelu(conv_post input) in a16.  Every conv after the first is a
+// programmatic dependent of its predecessor; the last conv of each residual
+// block folds the block average into its epilogue (sum = cur * 1/3, then
+// sum += cur * 1/3 for the later blocks: mul_write / add_scaled_inplace,
+// dec.hpp:295-333).
+static int decoder_body(gsvk_decoder* h, size_t T, cudaStream_t st, int* launches) {
+  const gsvk_decoder_config& c = h->cfg;
+  auto conv = [&](int idx, const uint16_t* x, size_t Tin, int dil, bool convt,
+                  gsvk_conv_args& a, ConvFuse f) -> int {
+    a.x = x;
+    a.T = Tin;
+    a.ci = (size_t)h->ci[idx];
+    a.w = h->w[idx];
+    a.co = (size_t)h->co[idx];
+    a.k = (size_t)h->kk[idx];
+    a.dil = (size_t)dil;
+    a.bias = h->b[idx];
+    f.pdl = idx > 0;
+    ++*launches;
+    return convt ? convt1d_run(&a, st, &f) : conv1d_run(&a, st, &f);
+  };
+  int rc;
+  // conv_pre -> lrelu(0.1) as the first ConvT input (dec.hpp:267, 285)
+  {
+    gsvk_conv_args a{};
+    a.y_f16_act = h->a16;
+    a.act2 = GSVK_ACT_LEAKY;
+    a.slope2 = c.lrelu_slope;
+    if ((rc = conv(0, h->in16, T, 1, false, a, ConvFuse{}))) return rc;
+  }
+  size_t L = T;
+  for (int s = 0; s < c.n_stages; ++s) {
+    const int base = 1 + s * 19;
+    const size_t Ln = L * (size_t)c.up_rate[s];
+    const float next_slope = (s + 1 < c.n_stages) ? c.lrelu_slope : c.post_slope;
+    {  // ConvT: xu (fp32 resblock base) and lrelu(xu) fp16
+      gsvk_conv_args a{};
+      a.y = h->xu32;
+      a.y_f16_act = h->xu16;
+      a.act2 = GSVK_ACT_LEAKY;
+      a.slope2 = c.lrelu_slope;
+      if ((rc = conv(base, h->a16, L, c.up_rate[s], true, a, ConvFuse{}))) return rc;
+    }
+    for (int j = 0; j < 3; ++j) {
+      for (int p = 0; p < 3; ++p) {
+        const int i1 = base + 1 + j * 6 + p * 2;
+        {  // t_a = lrelu(c1(lrelu(cur)) + b) in fp16
+          gsvk_conv_args a{};
+          a.y_f16 = h->t16a;
+          a.act = GSVK_ACT_LEAKY;
+          a.slope = c.lrelu_slope;
+          if ((rc = conv(i1, p == 0 ? h->xu16 : h->t16b, Ln, c.res_dil[p], false, a, ConvFuse{})))
+            return rc;
+        }
+        {  // cur = cur + c2(t_a) + b ; next c1 input lrelu(cur) in fp16
+          gsvk_conv_args a{};
+          a.residual = p == 0 ? h->xu32 : h->cur32;
+          a.res_scale = 1.f;
+          ConvFuse f;
+          if (p < 2) {
+            a.y = h->cur32;
+            a.y_f16_act = h->t16b;
+            a.act2 = GSVK_ACT_LEAKY;
+            a.slope2 = c.lrelu_slope;
+          } else {
+            // block output: sum += cur / 3; after the last block the next
+            // stage's input lrelu(sum) in fp16
+            f.mean_sum = h->sum32;
+            f.mean_scale = 1.f / 3.f;
+            f.mean_first = j == 0;
+            if (j == 2) {
+              a.y_f16_act = h->a16;
+              a.act2 = GSVK_ACT_LEAKY;
+              a.slope2 = next_slope;
+            }
+          }
+          if ((rc = conv(i1 + 1, h->t16a, Ln, 1, false, a, f))) return rc;
+        }
+      }
+    }
+    L = Ln;
+  }
+  return GSVK_OK;
+}
+
+static int decoder_graph(gsvk_decoder* h, size_t T, cudaGraphExec_t* exec, int* launches) {
+  for (auto& g : h->graphs)
+    if (g.T == T) {
+      g.used = ++h->tick;
+      *exec = g.exec;
+      *launches = g.launches;
+      return GSVK_OK;
+    }
+  int n = 0;
+  if (int rc = check_cuda(cudaStreamBeginCapture(h->capture, cudaStreamCaptureModeRelaxed),
+                          "decoder capture"))
+    return rc;
+  const int rc_body = decoder_body(h, T, h->capture, &n);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(h->capture, &graph);
+  if (rc_body || ce != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return rc_body ? rc_body : check_cuda(ce, "decoder capture end");
+  }
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&ex, graph, 0);
+  cudaGraphDestroy(graph);
+  if (int rc = check_cuda(ie, "decoder graph instantiate")) return rc;
+  if (h->graphs.size() >= gsvk_decoder::kMaxGraphs) {  // evict the least recently used
+    auto lru = std::min_element(h->graphs.begin(), h->graphs.end(),
+                                [](const auto& a, const auto& b) { return a.used < b.used; });
+    cudaGraphExecDestroy(lru->exec);
+    h->graphs.erase(lru);
+  }
+  h->graphs.push_back({T, ex, n, ++h->tick});
+  *exec = ex;
+  *launches = n;
+  return GSVK_OK;
+}
+
+}  // namespace gsvk
+
+extern "C" {
 
 int gsvk_decoder_forward(gsvk_decoder_t h, const float* z, size_t T, float* wav,
                          gsvk_stream_t stream) {
@@ -388,80 +548,38 @@ int gsvk_decoder_forward(gsvk_decoder_t h, const float* z, size_t T, float* wav,
   cudaStream_t st = as_cuda(stream);
   int rc = gsvk_channels_to_rows_f16(z, c.in_ch, T, h->in16, stream);
   if (rc) return rc;
-  int launches = 1;
-  auto conv = [&](int idx, const uint16_t* x, size_t Tin, int dil, bool convt,
-                  gsvk_conv_args& a) -> int {
-    a.x = x;
-    a.T = Tin;
+  int launches = 1, body = 0;
+  if (h->use_graph) {
+    cudaGraphExec_t exec = nullptr;
+    if ((rc = decoder_graph(h, T, &exec, &body))) return rc;
+    if ((rc = check_cuda(cudaGraphLaunch(exec, st), "decoder graph launch"))) return rc;
+  } else if ((rc = decoder_body(h, T, st, &body))) {
+    return rc;
+  }
+  launches += body;
+  {  // conv_post (no bias) -> tanh, written as [T_out, 1] == wav
+    gsvk_conv_args a{};
+    a.x = h->a16;
+    a.T = gsvk_decoder_out_len(&c, T);
+    const int idx = 1 + 19 * c.n_stages;
     a.ci = (size_t)h->ci[idx];
     a.w = h->w[idx];
     a.co = (size_t)h->co[idx];
     a.k = (size_t)h->kk[idx];
-    a.dil = (size_t)dil;
+    a.dil = 1;
     a.bias = h->b[idx];
-    ++launches;
-    return convt ? convt1d_run(&a, st) : conv1d_run(&a, st);
-  };
-  // conv_pre -> lrelu(0.1) as the first ConvT input (dec.hpp:267, 285)
-  {
-    gsvk_conv_args a{};
-    a.y_f16_act = h->a16;
-    a.act2 = GSVK_ACT_LEAKY;
-    a.slope2 = c.lrelu_slope;
-    if ((rc = conv(0, h->in16, T, 1, false, a))) return rc;
-  }
-  size_t L = T;
-  for (int s = 0; s < c.n_stages; ++s) {
-    const int base = 1 + s * 19;
-    const size_t Ln = L * (size_t)c.up_rate[s];
-    const size_t n = Ln * (size_t)h->co[base];
-    {  // ConvT: xu (fp32 resblock base) and lrelu(xu) fp16
-      gsvk_conv_args a{};
-      a.y = h->xu32;
-      a.y_f16_act = h->xu16;
-      a.act2 = GSVK_ACT_LEAKY;
-      a.slope2 = c.lrelu_slope;
-      if ((rc = conv(base, h->a16, L, c.up_rate[s], true, a))) return rc;
-    }
-    for (int j = 0; j < 3; ++j) {
-      for (int p = 0; p < 3; ++p) {
-        const int i1 = base + 1 + j * 6 + p * 2;
-        {  // t_a = lrelu(c1(lrelu(cur)) + b) in fp16
-          gsvk_conv_args a{};
-          a.y_f16 = h->t16a;
-          a.act = GSVK_ACT_LEAKY;
-          a.slope = c.lrelu_slope;
-          if ((rc = conv(i1, p == 0 ? h->xu16 : h->t16b, Ln, c.res_dil[p], false, a))) return rc;
-        }
-        {  // cur = cur + c2(t_a) + b ; next c1 input lrelu(cur) in fp16
-          gsvk_conv_args a{};
-          a.residual = p == 0 ? h->xu32 : h->cur32;
-          a.res_scale = 1.f;
-          a.y = h->cur32;
-          if (p < 2) {
-            a.y_f16_act = h->t16b;
-            a.act2 = GSVK_ACT_LEAKY;
-            a.slope2 = c.lrelu_slope;
-          }
-          if ((rc = conv(i1 + 1, h->t16a, Ln, 1, false, a))) return rc;
-        }
-      }
-      const bool last = (j == 2);
-      const float next_slope = (s + 1 < c.n_stages) ? c.lrelu_slope : c.post_slope;
-      res_mean_kernel<<<grid_for(n), 256, 0, st>>>(h->cur32, h->sum32, n, j == 0,
-                                                   last ? h->a16 : nullptr, next_slope);
-      ++launches;
-      if ((rc = check_launch("res_mean_kernel"))) return rc;
-    }
-    L = Ln;
-  }
-  {  // conv_post (no bias) -> tanh, written as [T_out, 1] == wav
-    gsvk_conv_args a{};
     a.y = wav;
     a.act = GSVK_ACT_TANH;
-    if ((rc = conv(1 + 19 * c.n_stages, h->a16, L, 1, false, a))) return rc;
+    if ((rc = conv1d_run(&a, st))) return rc;
+    ++launches;
   }
   h->launches = launches;
+  return GSVK_OK;
+}
+
+int gsvk_decoder_set_graph(gsvk_decoder_t h, int enable) {
+  if (!h) return fail(GSVK_ERR_INVALID, "decoder_set_graph: null handle");
+  h->use_graph = enable != 0;
   return GSVK_OK;
 }
 

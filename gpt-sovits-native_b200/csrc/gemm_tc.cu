@@ -65,13 +65,32 @@ __device__ __forceinline__ TapPlan plan_for(const TcProblem& p, int phase) {
 // Bias and residual of one 16-column chunk, fetched one chunk ahead of its
 // use (loads stay in flight: values are assigned under branches, never
 // selected, so nothing waits for them until store16 consumes them).
+__device__ __forceinline__ void load16(const float* src, bool full, int n0, int N, float* out) {
+  if (full && aligned16(src)) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src + j);
+      out[j] = v.x;
+      out[j + 1] = v.y;
+      out[j + 2] = v.z;
+      out[j + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (n0 + j < N) out[j] = src[j];
+  }
+}
+
 __device__ __forceinline__ void fetch16(const TcEpilogue& e, bool row_ok, long long orow, int n0,
-                                        int N, int oc, bool bias_vec, float* bb, float* rr) {
+                                        int N, int oc, bool bias_vec, float* bb, float* rr,
+                                        float* ss) {
   const bool full = (n0 + 16 <= N);
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     bb[j] = 0.f;
     rr[j] = 0.f;
+    ss[j] = 0.f;
   }
   if (e.bias) {
     if (full && bias_vec) {
@@ -89,31 +108,17 @@ __device__ __forceinline__ void fetch16(const TcEpilogue& e, bool row_ok, long l
         if (n0 + j < N) bb[j] = __ldg(e.bias + n0 + j);
     }
   }
-  if (e.residual && row_ok) {
-    const float* src = e.residual + orow * e.ld_res + oc + n0;
-    if (full && aligned16(src)) {
-#pragma unroll
-      for (int j = 0; j < 16; j += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src + j);
-        rr[j] = v.x;
-        rr[j + 1] = v.y;
-        rr[j + 2] = v.z;
-        rr[j + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (n0 + j < N) rr[j] = src[j];
-    }
-  }
+  if (e.residual && row_ok) load16(e.residual + orow * e.ld_res + oc + n0, full, n0, N, rr);
+  if (e.mean_sum && !e.mean_first && row_ok)
+    load16(e.mean_sum + orow * e.ld_c32 + oc + n0, full, n0, N, ss);
 }
 
 // n0: column within the problem (bias index, N bound); oc: output column
 // offset (batched mode), added to n0 for the output and residual addresses.
-// bb / rr: this chunk's bias and residual (from fetch16).
+// bb / rr / ss: this chunk's bias, residual and running-mean sum (from fetch16).
 __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int n0, int N,
                                         const uint32_t* r, int oc, const float* bb,
-                                        const float* rr) {
+                                        const float* rr, const float* ss) {
   float v[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = fmaf(__uint_as_float(r[j]), e.alpha, bb[j]);
@@ -131,6 +136,22 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
     for (int j = 0; j < 16; ++j)
       if (full || n0 + j < N) dst[j * e.vt_ld] = f2h(v[j]);
     return;
+  }
+  if (e.mean_sum) {  // running mean: rounded multiply, then rounded add (no contraction)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float t = __fmul_rn(v[j], e.mean_scale);
+      v[j] = e.mean_first ? t : __fadd_rn(ss[j], t);
+    }
+    float* dst = e.mean_sum + orow * e.ld_c32 + oc + n0;
+    if (full && aligned16(dst)) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < N) dst[j] = v[j];
+    }
   }
   if (e.c32) {
     float* dst = e.c32 + orow * e.ld_c32 + oc + n0;
@@ -242,6 +263,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Programmatic dependent launch: everything above, and the weight loads of
+  // window mode, overlap the previous kernel; every access to activations and
+  // outputs comes after griddep_wait (a no-op for an ordinary launch).
+  const bool b_early = win && p.pdl;
+  if (b_early && threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bbar, b_region);
+    for (int t = 0; t < p.taps; ++t)
+      tma_load_2d(sB + static_cast<size_t>(t) * b_bytes, &tmB, bbar, 0, t * p.b_tap_rows);
+  }
+  griddep_wait();
+  griddep_launch_dependents();
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- producer
@@ -249,9 +282,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       if (win) {
         // every tap's weights once; then one input window per tile
-        mbar_arrive_expect_tx(bbar, b_region);
-        for (int t = 0; t < p.taps; ++t)
-          tma_load_2d(sB + static_cast<size_t>(t) * b_bytes, &tmB, bbar, 0, t * p.b_tap_rows);
+        if (!b_early) {
+          mbar_arrive_expect_tx(bbar, b_region);
+          for (int t = 0; t < p.taps; ++t)
+            tma_load_2d(sB + static_cast<size_t>(t) * b_bytes, &tmB, bbar, 0, t * p.b_tap_rows);
+        }
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it) {
           const int mt = tile;  // one column tile, one phase
           const int s = it % stages;
@@ -366,25 +401,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long orow = static_cast<long long>(q) * tp.o_mul + tp.o_off + tp.c_row0;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      float bnext[16], rnext[16];
-      fetch16(e, row_ok, orow, nt * BN + cbeg, p.N, tp.c_col0, bias_vec, bnext, rnext);
+      float bnext[16], rnext[16], snext[16];
+      fetch16(e, row_ok, orow, nt * BN + cbeg, p.N, tp.c_col0, bias_vec, bnext, rnext, snext);
       if (!mbar_wait(&tfull[acc], aph, status)) break;
       tc_fence_after();
 #pragma unroll 1
       for (int c0 = cbeg; c0 < cbeg + cw && cols_ok; c0 += 16) {
-        float bcur[16], rcur[16];
+        float bcur[16], rcur[16], scur[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           bcur[j] = bnext[j];
           rcur[j] = rnext[j];
+          scur[j] = snext[j];
         }
         if (c0 + 16 < cbeg + cw)
-          fetch16(e, row_ok, orow, nt * BN + c0 + 16, p.N, tp.c_col0, bias_vec, bnext, rnext);
+          fetch16(e, row_ok, orow, nt * BN + c0 + 16, p.N, tp.c_col0, bias_vec, bnext, rnext,
+                  snext);
         uint32_t r[16];
         tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
         tmem_ld_wait();
         if (row_ok && nt * BN + c0 < p.N)
-          store16(e, orow, nt * BN + c0, p.N, r, tp.c_col0, bcur, rcur);
+          store16(e, orow, nt * BN + c0, p.N, r, tp.c_col0, bcur, rcur, scur);
       }
       tc_fence_before();
       __syncwarp();
@@ -428,6 +465,9 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
   const long long tiles = static_cast<long long>((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) *
                           p.phases;
   const int grid = static_cast<int>(std::min<long long>(tiles, sm_count()));
+  if (p.pdl)
+    return launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kThreads), smem, st, "gemm_tc_kernel",
+                      ta, tb, p, e, stages, device_status());
   gemm_tc_kernel<BN><<<grid, kThreads, smem, st>>>(ta, tb, p, e, stages, device_status());
   return check_launch("gemm_tc_kernel");
 }
@@ -453,9 +493,9 @@ __global__ void gemm_simt_kernel(const uint16_t* __restrict__ a, long long lda,
     }
     r[j] = __float_as_uint(acc);
   }
-  float bb[16], rr[16];
-  fetch16(e, true, m, g * 16, N, 0, false, bb, rr);
-  store16(e, m, g * 16, N, r, 0, bb, rr);
+  float bb[16], rr[16], ss[16];
+  fetch16(e, true, m, g * 16, N, 0, false, bb, rr, ss);
+  store16(e, m, g * 16, N, r, 0, bb, rr, ss);
 }
 
 int pick_bk(long long kc) {

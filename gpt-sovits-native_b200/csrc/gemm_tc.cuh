@@ -49,6 +49,14 @@ struct TcEpilogue {
   uint16_t* vt;
   long long vt_ld;
   int vt_c0, vt_T, vt_dh, vt_H;
+  // Optional running mean (the average over the multi-receptive-field
+  // residual blocks): with mean_sum set, the value y above contributes
+  // t = y * mean_scale, s = mean_first ? t : mean_sum + t is stored back to
+  // mean_sum (same [rows, ld_c32] layout as c32), and the outputs written
+  // after it receive s in place of y (c32 / c16 = s, c16_act = act2(s)).
+  float* mean_sum;
+  float mean_scale;
+  int mean_first;
 };
 
 struct TcProblem {
@@ -77,6 +85,11 @@ struct TcProblem {
   // absolute shared-memory addresses, so any row start is valid); all taps'
   // weights are loaded once per CTA.
   int win;
+  // Launched as a programmatic dependent of the previous kernel in the
+  // stream: barrier set-up, TMEM allocation and (window mode) the weight
+  // loads overlap that kernel's tail, so B must not be written by the
+  // kernels this launch waits on.
+  int pdl;
 };
 
 }  // namespace gsvk

@@ -201,6 +201,10 @@ int gsvk_decoder_forward(gsvk_decoder_t h, const float* z, size_t T, float* wav,
                          gsvk_stream_t stream);
 /* Kernel launches issued by the last gsvk_decoder_forward. */
 int gsvk_decoder_launches(gsvk_decoder_t h);
+/* enable != 0 (the default): the layers between conv_pre's input and
+ * conv_post are captured once per input length T into a CUDA graph and
+ * replayed; 0: they are launched one by one.  The results are identical. */
+int gsvk_decoder_set_graph(gsvk_decoder_t h, int enable);
 
 /* ---- encoder stacks: RoBERTa-large / HuBERT-base (a20, a21) -------------- */
 /* bert::BertLayer::forward (bert_ops.hpp:347-400) and the HuBERT layer loop

@@ -117,3 +117,26 @@ def test_decoder_matches_oracle(dev, ora, which, T):
     assert wav.shape == ref.shape
     gate(wav, ref, rel=1e-2, min_cos=0.999)
     assert dev.device_status() == 0
+
+
+def test_decoder_graph_equals_eager(dev):
+    """Graph replay (one graph per input length, least recently used evicted
+    beyond eight) gives bit-identical waveforms to one-by-one launches."""
+    W = dev.workloads
+    cfg = W.DECODER
+    ws, bs = W.decoder_weights(cfg, seed=5)
+    dec = dev.Decoder(cfg, ws, bs, max_frames=24)
+    lengths = [24, 7, 13, 1, 2, 3, 4, 5, 6, 8, 24, 7]  # ten distinct: evictions, then re-capture
+    for T in lengths:
+        z = torch.from_numpy(W.decoder_latent(T, cfg, seed=T)).cuda()
+        dec.set_graph(True)
+        g = dec.forward(z).clone()
+        n_graph = dec.launches()
+        dec.set_graph(False)
+        e = dec.forward(z)
+        assert dec.launches() == n_graph
+        torch.cuda.synchronize()
+        assert torch.equal(g, e), f"T={T}"
+        assert bool(torch.isfinite(g).all())
+    dec.close()
+    assert dev.device_status() == 0
