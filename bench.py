@@ -291,15 +291,17 @@ def run_gemm1(args, rank, local, world):
     # rotate enough independent copies that the working set exceeds L2
     copies = 64
     xs = [torch.from_numpy(x.view(np.float16)).to(dev) for _ in range(copies)]
-    ws = [torch.from_numpy(w.view(np.float16)).to(dev) for _ in range(copies)]
+    # weights registered at load (gsvk_weights_register, the AmxPanel analogue):
+    # immutable, so each GEMM fetches its W tile while the previous one finishes
+    ws = [g.Weights(w.view(np.uint16)) for _ in range(copies)]
     bd = torch.from_numpy(b).to(dev)
     ys = [torch.empty(128, 2048, dtype=torch.float16, device=dev) for _ in range(copies)]
     # Steady state: `iters` launches per step captured in one CUDA graph as
     # `branches` independent streams of back-to-back GEMMs (independent
     # instances, each on its own rotating X/W/Y copies).
-    iters, branches = 1024, 8
+    iters, branches = 1024, 16
     for i in range(copies):
-        g.gemm_ex(xs[i], ws[i], bias=bd, act=g.ACT_RELU, c_f16=ys[i])
+        ws[i].gemm(xs[i], bias=bd, act=g.ACT_RELU, c_f16=ys[i])
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     side = [torch.cuda.Stream(dev) for _ in range(branches)]
@@ -311,7 +313,7 @@ def run_gemm1(args, rank, local, world):
             with torch.cuda.stream(s_):
                 for i in range(iters // branches):
                     j = bi * (copies // branches) + i % (copies // branches)  # own copies
-                    g.gemm_ex(xs[j], ws[j], bias=bd, act=g.ACT_RELU, c_f16=ys[j])
+                    ws[j].gemm(xs[j], bias=bd, act=g.ACT_RELU, c_f16=ys[j])
         for s_ in side:
             root.wait_stream(s_)
     for _ in range(args.warmup):
@@ -338,6 +340,7 @@ def run_gemm1(args, rank, local, world):
             "data": "synthetic", "config": {"workload": "gemm_ffn_up (BASELINE configs[0])",
                                             "iters_per_step": iters,
                                             "launch": f"CUDA graph, {branches} independent streams",
+                                            "weights": "registered (gsvk_gemm_f16_w)",
                                             "l2": f"{copies} rotated X/W copies (> L2)"},
             "gpu_launches": iters * args.steps,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf, "unit": "TFLOP/s",

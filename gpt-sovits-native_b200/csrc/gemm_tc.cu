@@ -604,6 +604,12 @@ int gsvk_gemm_f16(const uint16_t* a, const uint16_t* b, float* c, size_t M, size
 }
 
 int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
+  return gemm_ex_run(g, as_cuda(stream), false);
+}
+
+}  // extern "C"
+
+int gsvk::gemm_ex_run(const gsvk_gemm_args* g, cudaStream_t st, bool static_b) {
   if (!g || !g->a || !g->b || (!g->c && !g->c_f16) || g->M == 0 || g->N == 0 || g->K == 0)
     return fail(GSVK_ERR_INVALID, "gemm: null pointer or zero size");
   if (g->M > 0x7fffffff || g->N > 0x7fffffff || g->K > 0x7fffffff)
@@ -623,12 +629,12 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   e.alpha = g->alpha == 0.f ? 1.f : g->alpha;
   if (g->K % 8 != 0 || g->lda % 8 != 0 || g->ldb % 8 != 0 || !aligned16(g->a) ||
       !aligned16(g->b))
-    return simt_gemm(g, e, as_cuda(stream));  // odd K (conv K=7/9, test shapes)
+    return simt_gemm(g, e, st);  // odd K (conv K=7/9, test shapes)
   // few rows (decode steps, the FFN-up of one 128-token chunk): split-K cluster kernel
   if (skinny_fits((long long)g->M, (long long)g->N, (long long)g->K, (long long)g->lda,
                   (long long)g->ldb, g->a, g->b))
     return skinny_run(g->a, (int)g->M, (long long)g->lda, g->b, (int)g->N, (long long)g->ldb,
-                      (int)g->K, e, as_cuda(stream), false);
+                      (int)g->K, e, st, static_b);
   TcProblem p{};
   p.M = (int)g->M;
   p.N = (int)g->N;
@@ -641,7 +647,5 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   p.phases = 1;
   p.out_rows = (int)g->M;
   return tc_run(g->a, (long long)g->M, (long long)g->lda, g->b, (long long)g->N,
-                (long long)g->ldb, p, e, 0, as_cuda(stream));
+                (long long)g->ldb, p, e, 0, st);
 }
-
-}  // extern "C"

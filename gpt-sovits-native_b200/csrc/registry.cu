@@ -61,7 +61,7 @@ int gsvk_gemm_f16_w(const gsvk_gemm_args* args, gsvk_weights_t w, gsvk_stream_t 
   gsvk_gemm_args g = *args;
   g.b = w->dev;
   g.ldb = w->cols;
-  return gsvk_gemm_f16_ex(&g, stream);
+  return gemm_ex_run(&g, as_cuda(stream), true);  // registered weights are immutable
 }
 
 int gsvk_gemv_f16w_f32acc_w(gsvk_weights_t w, const float* x, float* y, gsvk_stream_t stream) {
