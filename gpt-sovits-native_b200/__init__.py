@@ -66,6 +66,10 @@ SIGNATURES = {
     "gsvk_t2s_decode": (c_int, [_vp, _sz, _vp, _sz, _sz, c_int, _vp, _vp, _vp, _vp]),
     "gsvk_t2s_launches_per_generate": (c_int, [_vp]),
     "gsvk_t2s_set_trace": (c_int, [_vp, c_int]),
+    "gsvk_t2s_set_decode_kernel": (c_int, [_vp, c_int]),
+    "gsvk_t2s_read_kv": (c_int, [_vp, _vp, _vp]),
+    "gsvk_t2s_set_decode_ctas": (c_int, [_vp, c_int]),
+    "gsvk_t2s_decode_kernel": (c_int, [_vp]),
     "gsvk_t2s_read_trace": (c_int, [_vp, _vp, _sz]),
     "gsvk_attention_workspace_floats": (_sz, [_sz, _sz, _sz]),
     "gsvk_attention_decode": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp, _vp, _vp]),
@@ -437,6 +441,30 @@ class T2S:
         check(lib().gsvk_t2s_decode(self.h, prefix, _ptr(prompt_dev), prompt_dev.numel(),
                                     max_steps, int(stop_on_eos), _ptr(tokens_dev), _ptr(n_out_dev),
                                     _ptr(margins_dev), _stream(stream)))
+
+    DECODE_GRID, DECODE_CLUSTER = 1, 2
+
+    def set_decode_kernel(self, kind: int):
+        """1 (or 0, the default): grid kernel (one CTA per SM, grid barriers,
+        phase trace); 2: single-cluster kernel (raises if unsupported).
+        Both give identical tokens, margins, logits and KV."""
+        check(lib().gsvk_t2s_set_decode_kernel(self.h, int(kind)))
+
+    def decode_kernel(self) -> int:
+        return lib().gsvk_t2s_decode_kernel(self.h)
+
+    def set_decode_ctas(self, ctas: int):
+        """CTAs of the grid decode kernel (0 = one per SM)."""
+        check(lib().gsvk_t2s_set_decode_ctas(self.h, int(ctas)))
+
+    def read_kv(self):
+        """(k, v) host uint16 [n_layers, cap, d_model]."""
+        import numpy as np
+
+        shape = (self.model["n_layers"], self.cap, self.model["d_model"])
+        k, v = np.zeros(shape, np.uint16), np.zeros(shape, np.uint16)
+        check(lib().gsvk_t2s_read_kv(self.h, k.ctypes.data, v.ctypes.data))
+        return k, v
 
     TRACE_STEPS, TRACE_STRIDE = 4, 16 + 16 * 64
 

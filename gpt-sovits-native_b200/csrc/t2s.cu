@@ -48,6 +48,7 @@ struct T2SDev {
   int L, D, H, F, V, cap, HD;
   float eps, alpha, scale;
   const uint16_t *wqkv, *wout, *w1, *w2, *wpred, *emb;
+  const uint16_t* w2p;  // W2 rows in the lane order of t2s_cluster_kernel (or null)
   const float *bqkv, *bout, *b1, *b2, *n1g, *n1b, *n2g, *n2b, *pe;
   uint16_t *kc, *vc;
   float *q, *part, *hpre, *ff, *xpre, *logits;
@@ -665,6 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   __syncthreads();
 }
 
+#include "t2s_cluster.cuh"
+
 // ------------------------------------------------------------ prefill kernels
 __global__ void embed_kernel(const int32_t* __restrict__ ids, int P, const uint16_t* __restrict__ emb,
                              const float* __restrict__ pe, int pe0, float alpha, int D,
@@ -866,8 +869,14 @@ struct T2SEngine {
   size_t attn_smem = 0;      // prefill attention dynamic shared memory
   const void* decode_fn = nullptr;
   const void* attn_fn = nullptr;
+  // single-cluster decode (t2s_cluster_kernel): usable on this shape / GPU,
+  // and which decode kernel gsvk_t2s_decode launches (1 grid, 2 cluster)
+  bool cluster_ok = false;
+  size_t cluster_smem = 0;
+  int decode_kind = 1;
   // device allocations
   void* weights = nullptr;   // one block: all fp16 weights + fp32 vectors + PE table
+  void* w2_lanes = nullptr;  // W2 permuted for the single-cluster decode
   void* scratch = nullptr;
   int32_t* d_prompt = nullptr;
   int32_t* d_tokens = nullptr;
@@ -902,6 +911,48 @@ void pe_row_host(int D, size_t pos, float* pe) {
 using namespace gsvk;
 
 struct gsvk_t2s : gsvk::T2SEngine {};
+
+namespace {
+
+// Decode launch plan for G persistent CTAs: weight slices sized for the
+// largest CTA (rows / G rounded up), two layer buffers and the persistent
+// logits slice in shared memory.  Sets e->G on success.
+int decode_plan(gsvk_t2s* e, int G) {
+  const int D = e->D, F = e->F, V = e->V, HD = e->HD;
+  auto ceil_rows = [&](int rows) { return (rows + G - 1) / G; };
+  DecodeArgs a = e->plan;
+  a.mq = ceil_rows(3 * D);
+  a.mo = ceil_rows(D);
+  a.m1 = ceil_rows(F);
+  a.m2 = ceil_rows(D);
+  a.ml = ceil_rows(V);
+  a.ln_off = static_cast<uint32_t>(align_up(
+      ((size_t)a.mq * D + (size_t)a.mo * D + (size_t)a.m1 * D + (size_t)a.m2 * F) * 2, 16));
+  a.layer_bytes = static_cast<uint32_t>(align_up((size_t)a.ln_off + (size_t)4 * D * 4, 128));
+  const size_t slot_f = (size_t)kSlots * (HD == 32 ? slot_floats<32>() : slot_floats<64>());
+  const size_t floats = slot_f + (size_t)D * 2 + std::max(D, F) + kChunk + 64;
+  const size_t smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 + (size_t)2 * D * 4 +
+                      floats * 4 + 8 * 4 + 4 * 8 + align_up(V, 16) + 64;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int max_optin = 0;
+  cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (smem > (size_t)max_optin)
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s decode on %d CTAs needs %zu B shared memory", G, smem);
+  if (int rc = check_cuda(cudaFuncSetAttribute(e->decode_fn,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                          "cudaFuncSetAttribute(t2s_decode)"))
+    return rc;
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->decode_fn, kThreads, smem);
+  if (per_sm < 1) return fail(GSVK_ERR_UNSUPPORTED, "t2s decode kernel does not fit an SM");
+  e->plan = a;
+  e->decode_smem = smem;
+  e->G = G;
+  return GSVK_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -1022,25 +1073,9 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   e->pff16 = reinterpret_cast<uint16_t*>(sb + o_pff);
   e->d_trace = reinterpret_cast<unsigned long long*>(sb + o_trace);
 
-  // ---- decode launch plan: one CTA per SM, weight slices sized for the
-  // largest CTA, two layer buffers + the persistent logits slice.
-  int G = sm_count();
-  auto ceil_rows = [&](int rows) { return (rows + G - 1) / G; };
-  DecodeArgs& a = e->plan;
-  a.mq = ceil_rows(3 * D);
-  a.mo = ceil_rows(D);
-  a.m1 = ceil_rows(F);
-  a.m2 = ceil_rows(D);
-  a.ml = ceil_rows(V);
-  a.ln_off = static_cast<uint32_t>(align_up(
-      ((size_t)a.mq * D + (size_t)a.mo * D + (size_t)a.m1 * D + (size_t)a.m2 * F) * 2, 16));
-  a.layer_bytes = static_cast<uint32_t>(align_up((size_t)a.ln_off + (size_t)4 * D * 4, 128));
+  // ---- decode launch plan (one CTA per SM by default) and prefill attention
   const size_t slot_f = (size_t)kSlots * (HD == 32 ? slot_floats<32>() : slot_floats<64>());
   const size_t max_nch = ((size_t)cap + kChunk - 1) / kChunk;
-  const size_t floats = slot_f + (size_t)D * 2 + std::max(D, F) + kChunk + 64;
-  e->decode_smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 + (size_t)2 * D * 4 +
-                   floats * 4 + 8 * 4 +
-                   4 * 8 + align_up(V, 16) + 64;
   e->attn_smem = (slot_f + max_nch * (HD + 4)) * 4;
   e->HD = HD;
   e->decode_fn = HD == 32 ? (const void*)t2s_decode_kernel<32> : (const void*)t2s_decode_kernel<64>;
@@ -1049,17 +1084,9 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   cudaGetDevice(&dev);
   int max_optin = 0;
   cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  if (e->decode_smem > (size_t)max_optin || e->attn_smem > (size_t)max_optin) {
+  if (e->attn_smem > (size_t)max_optin) {
     gsvk_t2s_destroy(e);
-    return fail(GSVK_ERR_UNSUPPORTED, "t2s kernels need %zu / %zu B shared memory",
-                e->decode_smem, e->attn_smem);
-  }
-  if (int rc = check_cuda(cudaFuncSetAttribute(e->decode_fn,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)e->decode_smem),
-                          "cudaFuncSetAttribute(t2s_decode)")) {
-    gsvk_t2s_destroy(e);
-    return rc;
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s prefill attention needs %zu B shared memory", e->attn_smem);
   }
   if (int rc = check_cuda(cudaFuncSetAttribute(e->attn_fn,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1068,13 +1095,47 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
     gsvk_t2s_destroy(e);
     return rc;
   }
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->decode_fn, kThreads, e->decode_smem);
-  if (per_sm < 1) {
+  if (int rc = decode_plan(e, sm_count())) {
     gsvk_t2s_destroy(e);
-    return fail(GSVK_ERR_UNSUPPORTED, "t2s decode kernel does not fit an SM");
+    return rc;
   }
-  e->G = G;
+  // single-cluster decode: the configuration's shape (d 512, head 32, ffn
+  // 2048), at most one head per CTA, chunk records for the whole cache in
+  // shared memory, and a GPU that can place a 16-CTA cluster of this size
+  if (HD == kClHD && D == kClD && F == kClF && H <= kClCS && cap <= kClMaxChunks * kChunk) {
+    const size_t smem = cl_layout(V).total;
+    const void* fn = (const void*)t2s_cluster_kernel;
+    if (smem <= (size_t)max_optin &&
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+            cudaSuccess &&
+        cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+      cudaLaunchConfig_t lc{};
+      lc.gridDim = dim3(kClCS);
+      lc.blockDim = dim3(kClThreads);
+      lc.dynamicSmemBytes = smem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = kClCS;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      lc.attrs = at;
+      lc.numAttrs = 1;
+      int clusters = 0;
+      const size_t w2_bytes = (size_t)L * D * F * 2;
+      if (cudaOccupancyMaxActiveClusters(&clusters, fn, &lc) == cudaSuccess && clusters >= 1 &&
+          cudaMalloc(&e->w2_lanes, w2_bytes) == cudaSuccess) {
+        uint16_t* dst = static_cast<uint16_t*>(e->w2_lanes);
+        w2_lane_order_kernel<<<(unsigned)((size_t)L * D), 256>>>(d.w2, dst);
+        if (cudaDeviceSynchronize() == cudaSuccess) {
+          d.w2p = dst;
+          e->cluster_ok = true;
+          e->cluster_smem = smem;
+        }
+      }
+    }
+    cudaGetLastError();  // a refused attribute, query or allocation only disables the variant
+  }
+  e->decode_kind = 1;
   *out = e;
   return GSVK_OK;
 }
@@ -1082,6 +1143,7 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
 int gsvk_t2s_destroy(gsvk_t2s_t h) {
   if (!h) return GSVK_OK;
   if (h->weights) cudaFree(h->weights);
+  if (h->w2_lanes) cudaFree(h->w2_lanes);
   if (h->scratch) cudaFree(h->scratch);
   delete h;
   return GSVK_OK;
@@ -1205,10 +1267,46 @@ int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size
   a.margins = margins_dev;
   a.trace = h->trace_on ? h->d_trace : nullptr;
   T2SDev dv = d;
+  if (h->decode_kind == 2) {
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(kClCS);
+    lc.blockDim = dim3(kClThreads);
+    lc.dynamicSmemBytes = h->cluster_smem;
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = kClCS;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&lc, t2s_cluster_kernel, dv, a),
+                      "t2s_cluster_kernel (cluster launch)");
+  }
   void* args[] = {&dv, &a};
   return check_cuda(cudaLaunchCooperativeKernel(h->decode_fn, dim3(h->G), dim3(kThreads),
                                                 args, h->decode_smem, st),
                     "t2s_decode_kernel (cooperative launch)");
+}
+
+int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind) {
+  if (!h) return fail(GSVK_ERR_INVALID, "t2s_set_decode_kernel: null handle");
+  if (kind < 0 || kind > 2) return fail(GSVK_ERR_INVALID, "t2s_set_decode_kernel: kind %d", kind);
+  if (kind == 2 && !h->cluster_ok)
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s_set_decode_kernel: the single-cluster decode does not "
+                                      "fit this model shape or GPU");
+  h->decode_kind = kind == 0 ? 1 : kind;
+  return GSVK_OK;
+}
+
+int gsvk_t2s_decode_kernel(gsvk_t2s_t h) { return h ? h->decode_kind : 0; }
+
+int gsvk_t2s_set_decode_ctas(gsvk_t2s_t h, int ctas) {
+  if (!h) return fail(GSVK_ERR_INVALID, "t2s_set_decode_ctas: null handle");
+  const int sms = sm_count();
+  if (ctas < 0 || ctas > sms)
+    return fail(GSVK_ERR_INVALID, "t2s_set_decode_ctas: %d CTAs (0 or 1..%d)", ctas, sms);
+  return decode_plan(h, ctas == 0 ? sms : ctas);
 }
 
 int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size_t P,
@@ -1274,6 +1372,14 @@ int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n) {
   return check_cuda(cudaMemcpy(host_out, h->d_trace, (n < total ? n : total) * 8,
                                cudaMemcpyDeviceToHost),
                     "trace download");
+}
+
+int gsvk_t2s_read_kv(gsvk_t2s_t h, uint16_t* k_host, uint16_t* v_host) {
+  if (!h || !k_host || !v_host) return fail(GSVK_ERR_INVALID, "t2s_read_kv: null");
+  const size_t bytes = (size_t)h->L * h->cap * h->D * 2;
+  int rc = check_cuda(cudaMemcpy(k_host, h->dev.kc, bytes, cudaMemcpyDeviceToHost), "kv download");
+  if (rc) return rc;
+  return check_cuda(cudaMemcpy(v_host, h->dev.vc, bytes, cudaMemcpyDeviceToHost), "kv download");
 }
 
 int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out) {

@@ -349,6 +349,18 @@ int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_
  * activation load.  read_trace is synchronous. */
 int gsvk_t2s_set_trace(gsvk_t2s_t h, int enable);
 int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n);
+/* Which decode kernel gsvk_t2s_decode launches: 1 = persistent CTAs (one
+ * per SM) with grid barriers (any shape; the default), 2 = one 16-CTA
+ * thread-block cluster with cluster barriers and distributed shared memory
+ * (d_model 512, head_dim 32, ffn 2048, <= 16 heads, cap <= 4096, and a GPU
+ * that places such a cluster; raises GSVK_ERR_UNSUPPORTED otherwise).
+ * 0 = the default.  Both produce identical tokens, margins, logits and KV.
+ * gsvk_t2s_decode_kernel returns the current choice (1 or 2). */
+int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind);
+int gsvk_t2s_decode_kernel(gsvk_t2s_t h);
+/* CTAs of the grid decode kernel (one per SM at most; 0 = every SM, the
+ * default).  Results are identical for any count. */
+int gsvk_t2s_set_decode_ctas(gsvk_t2s_t h, int ctas);
 /* ---- batched T2S decode (config 3: concurrent utterances) -------------- */
 /* B <= max_batch utterances decode together: every step streams the weights
  * once for all B tokens through tensor-core GEMMs (M = B), attends each
@@ -380,6 +392,9 @@ int gsvk_t2s_batch_launches_per_step(gsvk_t2s_batch_t h);
 
 /* The logits the last step sampled from (raw, before the penalty); synchronous. */
 int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out);
+/* The whole KV cache, fp16 [n_layers][cap][d_model] each (the layout of
+ * gsvk_t2s_load_kv with src_rows = cap); synchronous. */
+int gsvk_t2s_read_kv(gsvk_t2s_t h, uint16_t* k_host, uint16_t* v_host);
 
 #ifdef __cplusplus
 }

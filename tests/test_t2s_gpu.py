@@ -44,8 +44,9 @@ def test_prefill_matches_oracle(dev, ora, small):
     eng.close()
 
 
+@pytest.mark.parametrize("kernel", [1, 2], ids=["grid", "cluster"])
 @pytest.mark.parametrize("stop_on_eos", [False, True])
-def test_generate_small_token_identity(dev, ora, small, stop_on_eos):
+def test_generate_small_token_identity(dev, ora, small, stop_on_eos, kernel):
     m = dict(small)
     if stop_on_eos:
         # make EOS competitive so the stop path is exercised after the 11-step mask
@@ -59,6 +60,8 @@ def test_generate_small_token_identity(dev, ora, small, stop_on_eos):
     toks_ref, marg_ref, logits_ref = ora.t2s_generate(m, k0.copy(), v0.copy(), prefix, prompt,
                                                       steps, stop_on_eos, with_logits=True)
     eng = dev.T2S(m, cap)
+    eng.set_decode_kernel(kernel)
+    assert eng.decode_kernel() == kernel
     eng.load_kv(k0, v0, prefix)
     toks, marg = eng.generate(prefix, prompt, steps, stop_on_eos)
     logits = eng.read_logits()
@@ -84,14 +87,42 @@ def test_generate_config2_full_model_token_identity(dev, ora):
     steps = 500
     toks_ref, marg_ref = ora.t2s_generate(m, k0.copy(), v0.copy(), 256, prompt, steps, False)
     eng = dev.T2S(m, cap)
-    eng.load_kv(k0, v0, 256)
-    toks, marg = eng.generate(256, prompt, steps, False)
+    assert eng.decode_kernel() == eng.DECODE_GRID  # the default
+    for kernel in (eng.DECODE_CLUSTER, eng.DECODE_GRID):
+        eng.set_decode_kernel(kernel)
+        eng.load_kv(k0, v0, 256)
+        toks, marg = eng.generate(256, prompt, steps, False)
+        assert len(toks) == len(toks_ref) == steps
+        bad = np.nonzero(toks != toks_ref)[0]
+        assert bad.size == 0, (f"kernel {kernel}: first divergence at step {bad[0]}: oracle "
+                               f"margin {marg_ref[bad[0]]:.3e}, device margin {marg[bad[0]]:.3e}")
+        np.testing.assert_array_equal(marg, marg_ref)
     eng.close()
-    assert len(toks) == len(toks_ref) == steps
-    bad = np.nonzero(toks != toks_ref)[0]
-    assert bad.size == 0, (f"first divergence at step {bad[0]}: oracle margin "
-                           f"{marg_ref[bad[0]]:.3e}, device margin {marg[bad[0]]:.3e}")
-    np.testing.assert_array_equal(marg, marg_ref)
+
+
+def test_decode_kernels_write_identical_kv(dev, small):
+    """Both decode kernels leave the same KV cache and the same final logits."""
+    m = small
+    prefix, P, steps = 30, 8, 40
+    cap = prefix + P + steps
+    k0, v0 = dev.workloads.t2s_kv_prefix(m, cap, prefix, seed=2)
+    prompt = dev.workloads.t2s_prompt(P, m["vocab"], seed=6)
+    out = {}
+    for kernel in (1, 2):
+        eng = dev.T2S(m, cap)
+        eng.set_decode_kernel(kernel)
+        eng.load_kv(k0, v0, prefix)
+        toks, marg = eng.generate(prefix, prompt, steps, False)
+        kv = eng.read_kv()
+        out[kernel] = (toks, marg, eng.read_logits(), kv)
+        eng.close()
+    for a, b in zip(out[1], out[2]):
+        if isinstance(a, tuple):
+            for x, y in zip(a, b):
+                np.testing.assert_array_equal(x, y)
+        else:
+            np.testing.assert_array_equal(a, b)
+    assert dev.device_status() == 0
 
 
 def test_generate_rejects_oversized_request(dev, small):
@@ -99,3 +130,32 @@ def test_generate_rejects_oversized_request(dev, small):
     with pytest.raises(dev.GsvkError):
         eng.generate(40, np.zeros(16, np.int32), 20)
     eng.close()
+
+
+def test_decode_cta_count_does_not_change_results(dev, small):
+    """The grid decode kernel on fewer CTAs than SMs: identical tokens and margins."""
+    m = small
+    prefix, P, steps = 30, 8, 40
+    cap = prefix + P + steps
+    k0, v0 = dev.workloads.t2s_kv_prefix(m, cap, prefix, seed=7)
+    prompt = dev.workloads.t2s_prompt(P, m["vocab"], seed=9)
+    out = []
+    for ctas in (0, 100, 120):
+        eng = dev.T2S(m, cap)
+        eng.set_decode_ctas(ctas)
+        eng.load_kv(k0, v0, prefix)
+        out.append(eng.generate(prefix, prompt, steps, False))
+        eng.close()
+    for toks, marg in out[1:]:
+        np.testing.assert_array_equal(toks, out[0][0])
+        np.testing.assert_array_equal(marg, out[0][1])
+    # too few CTAs: their weight slices no longer fit shared memory; the plan is kept
+    eng = dev.T2S(m, cap)
+    with pytest.raises(dev.GsvkError) as ei:
+        eng.set_decode_ctas(37)
+    assert ei.value.code == -5
+    eng.load_kv(k0, v0, prefix)
+    toks, marg = eng.generate(prefix, prompt, steps, False)
+    np.testing.assert_array_equal(toks, out[0][0])
+    eng.close()
+    assert dev.device_status() == 0
