@@ -303,7 +303,8 @@ __device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slice
   p += static_cast<size_t>(a.mo) * D * 2;
   if (b1) bulk_load(p, m.w1 + (static_cast<size_t>(l) * F + s.a0) * D, b1, bar);
   p += static_cast<size_t>(a.m1) * D * 2;
-  if (b2) bulk_load(p, m.w2 + (static_cast<size_t>(l) * D + s.b0) * F, b2, bar);
+  const uint16_t* w2 = m.w2p ? m.w2p : m.w2;  // the lane-ordered copy when there is one
+  if (b2) bulk_load(p, w2 + (static_cast<size_t>(l) * D + s.b0) * F, b2, bar);
   float* ln = reinterpret_cast<float*>(buf + a.ln_off);
   bulk_load(ln, m.n1g + static_cast<size_t>(l) * D, vb, bar);
   bulk_load(ln + D, m.n1b + static_cast<size_t>(l) * D, vb, bar);
@@ -312,6 +313,8 @@ __device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slice
     bulk_load(ln + 3 * D, m.n2b + static_cast<size_t>(l - 1) * D, vb, bar);
   }
 }
+
+#include "t2s_cluster.cuh"
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m, const DecodeArgs a) {
@@ -331,11 +334,23 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   int* flag = reinterpret_cast<int*>(red + 64);
   int* tokp = flag + 4;
   uint64_t* mbar = reinterpret_cast<uint64_t*>(tokp + 4);
-  uint8_t* seen = reinterpret_cast<uint8_t*>(mbar + 4);
+  float* bsm = reinterpret_cast<float*>(mbar + 4);  // this layer's bias slices
+  uint8_t* seen = reinterpret_cast<uint8_t*>(bsm + ((a.mq + a.mo + a.m1 + a.m2 + 3) & ~3));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
   const Slices s = my_slices(m);
+  const int nq = s.q1 - s.q0, no = s.o1 - s.o0, na = s.a1 - s.a0, nb = s.b1 - s.b0;
+  // bias element `tid` of layer l's row slices (QKV, out, W1, W2 in order)
+  auto bias_of = [&](int l) -> float {
+    const size_t L_ = static_cast<size_t>(l);
+    if (tid < nq) return __ldg(m.bqkv + L_ * 3 * D + s.q0 + tid);
+    if (tid < nq + no) return __ldg(m.bout + L_ * D + s.o0 + tid - nq);
+    if (tid < nq + no + na) return __ldg(m.b1 + L_ * F + s.a0 + tid - nq - no);
+    if (tid < nq + no + na + nb) return __ldg(m.b2 + L_ * D + s.b0 + tid - nq - no - na);
+    return 0.f;
+  };
+  float bias_next = 0.f;
   unsigned epoch = 0;
   uint32_t uses[2] = {0, 0};
   const int eos = V - 1;
@@ -376,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   for (int idx = 0; idx < a.max_steps && alive; ++idx) {
     tr = (a.trace && blockIdx.x == 0 && idx < kTraceSteps) ? a.trace + idx * kTraceStride : nullptr;
     GSVK_TR(0);
+    bias_next = bias_of(0);  // in flight during the sampling
     // ------------------------------------------------ greedy sample (all CTAs)
     // t2s_engine.cpp:1594-1636: penalty once per distinct history token,
     // EOS excluded while idx < 11, first maximum wins.
@@ -473,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       pending[b] = 0;
       const float* lnb = reinterpret_cast<const float*>(wbuf[b] + a.ln_off);
       GSVK_TR(16 + 16 * l + 11);
+      if (tid < nq + no + na + nb) bsm[tid] = bias_next;  // loaded a phase ago
       if (l > 0) {
         load_vec<2>(xs, m.xpre, D);
         __syncthreads();
@@ -486,9 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       {
         uint16_t* kl = m.kc + (static_cast<size_t>(l) * m.cap + pos) * D;
         uint16_t* vl = m.vc + (static_cast<size_t>(l) * m.cap + pos) * D;
-        const float* bq = m.bqkv + static_cast<size_t>(l) * 3 * D;
         auto put = [&](int r, float acc) {
-          const float v = __fadd_rn(acc, bq[r]);
+          const float v = __fadd_rn(acc, bsm[r - s.q0]);
           if (r < D)
             m.q[r] = v;
           else if (r < 2 * D)
@@ -515,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
       GSVK_TR(16 + 16 * l + 1);
       // ---------------------------------------------------------------- P2
+      if (l + 1 < L) bias_next = bias_of(l + 1);  // the next layer's, a phase ahead
       {
         const int slot = tid >> 6;
         float* sm = slots + slot * slot_floats<HD>();
@@ -581,10 +598,9 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       load_vec<2>(act, m.attn, D);
       __syncthreads();
       {
-        const float* bo = m.bout + static_cast<size_t>(l) * D;
         for (int r = s.o0 + warp; r < s.o1; r += kWarps) {
           const float acc = warp_dot32(Wo + static_cast<size_t>(r - s.o0) * D, act, D);
-          if (lane == 0) m.hpre[r] = __fadd_rn(__fadd_rn(acc, bo[r]), xs[r]);
+          if (lane == 0) m.hpre[r] = __fadd_rn(__fadd_rn(acc, bsm[nq + r - s.o0]), xs[r]);
         }
       }
       GSVK_TR(16 + 16 * l + 4);
@@ -599,9 +615,8 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       __syncthreads();
       GSVK_TR(16 + 16 * l + 12);
       {
-        const float* bb = m.b1 + static_cast<size_t>(l) * F;
         auto put = [&](int r, float acc) {
-          const float v = __fadd_rn(acc, bb[r]);
+          const float v = __fadd_rn(acc, bsm[nq + no + r - s.a0]);
           m.ff[r] = v > 0.f ? v : 0.f;
         };
         for (int r = s.a0 + 2 * warp; r < s.a1; r += 2 * kWarps) {
@@ -626,11 +641,17 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       load_vec<4>(act, m.ff, F);
       __syncthreads();
       GSVK_TR(16 + 16 * l + 13);
-      {
-        const float* bb = m.b2 + static_cast<size_t>(l) * D;
+      if (m.w2p) {  // lane-ordered W2 slice (F = kClF), activations in registers
+        float xr[2 * kClFB];
+        lane_load_x(act, xr);
+        for (int r = s.b0 + warp; r < s.b1; r += kWarps) {
+          const float acc = lane_dot_ordered(W2 + static_cast<size_t>(r - s.b0) * F, xr);
+          if (lane == 0) m.xpre[r] = __fadd_rn(__fadd_rn(acc, bsm[nq + no + na + r - s.b0]), hs[r]);
+        }
+      } else {
         for (int r = s.b0 + warp; r < s.b1; r += kWarps) {
           const float acc = warp_dot32(W2 + static_cast<size_t>(r - s.b0) * F, act, F);
-          if (lane == 0) m.xpre[r] = __fadd_rn(__fadd_rn(acc, bb[r]), hs[r]);
+          if (lane == 0) m.xpre[r] = __fadd_rn(__fadd_rn(acc, bsm[nq + no + na + r - s.b0]), hs[r]);
         }
       }
       __syncthreads();  // every warp is done with wbuf[b]
@@ -665,8 +686,6 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
   }
   __syncthreads();
 }
-
-#include "t2s_cluster.cuh"
 
 // ------------------------------------------------------------ prefill kernels
 __global__ void embed_kernel(const int32_t* __restrict__ ids, int P, const uint16_t* __restrict__ emb,
@@ -931,8 +950,9 @@ int decode_plan(gsvk_t2s* e, int G) {
   a.layer_bytes = static_cast<uint32_t>(align_up((size_t)a.ln_off + (size_t)4 * D * 4, 128));
   const size_t slot_f = (size_t)kSlots * (HD == 32 ? slot_floats<32>() : slot_floats<64>());
   const size_t floats = slot_f + (size_t)D * 2 + std::max(D, F) + kChunk + 64;
+  const size_t bias_f = align_up((size_t)a.mq + a.mo + a.m1 + a.m2, 4);
   const size_t smem = 128 + 2 * (size_t)a.layer_bytes + (size_t)a.ml * D * 2 + (size_t)2 * D * 4 +
-                      floats * 4 + 8 * 4 + 4 * 8 + align_up(V, 16) + 64;
+                      floats * 4 + 8 * 4 + 4 * 8 + bias_f * 4 + align_up(V, 16) + 64;
   int dev = 0;
   cudaGetDevice(&dev);
   int max_optin = 0;
@@ -1099,6 +1119,22 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
     gsvk_t2s_destroy(e);
     return rc;
   }
+  // W2 in lane order (both decode kernels read it when F = kClF)
+  if (F == kClF) {
+    const size_t w2_bytes = (size_t)L * D * F * 2;
+    if (cudaMalloc(&e->w2_lanes, w2_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      gsvk_t2s_destroy(e);
+      return fail(GSVK_ERR_NOMEM, "t2s_create: lane-ordered W2 (%zu bytes)", w2_bytes);
+    }
+    uint16_t* dst = static_cast<uint16_t*>(e->w2_lanes);
+    w2_lane_order_kernel<<<(unsigned)((size_t)L * D), 256>>>(d.w2, dst);
+    if (int rc = check_cuda(cudaDeviceSynchronize(), "t2s_create: W2 lane order")) {
+      gsvk_t2s_destroy(e);
+      return rc;
+    }
+    d.w2p = dst;
+  }
   // single-cluster decode: the configuration's shape (d 512, head 32, ffn
   // 2048), at most one head per CTA, chunk records for the whole cache in
   // shared memory, and a GPU that can place a 16-CTA cluster of this size
@@ -1121,19 +1157,13 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
       lc.attrs = at;
       lc.numAttrs = 1;
       int clusters = 0;
-      const size_t w2_bytes = (size_t)L * D * F * 2;
       if (cudaOccupancyMaxActiveClusters(&clusters, fn, &lc) == cudaSuccess && clusters >= 1 &&
-          cudaMalloc(&e->w2_lanes, w2_bytes) == cudaSuccess) {
-        uint16_t* dst = static_cast<uint16_t*>(e->w2_lanes);
-        w2_lane_order_kernel<<<(unsigned)((size_t)L * D), 256>>>(d.w2, dst);
-        if (cudaDeviceSynchronize() == cudaSuccess) {
-          d.w2p = dst;
-          e->cluster_ok = true;
-          e->cluster_smem = smem;
-        }
+          d.w2p) {
+        e->cluster_ok = true;
+        e->cluster_smem = smem;
       }
     }
-    cudaGetLastError();  // a refused attribute, query or allocation only disables the variant
+    cudaGetLastError();  // a refused attribute or query only disables the variant
   }
   e->decode_kind = 1;
   *out = e;
