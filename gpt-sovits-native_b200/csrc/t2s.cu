@@ -101,7 +101,11 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 // Grid barrier on a monotonically increasing counter (reset by the host
 // before each launch).  Bounded: on timeout, or when another CTA has already
 // flagged one, it returns false and the kernel winds down.
-__device__ bool grid_sync(unsigned* bar, unsigned& epoch, uint32_t* status, int* flag) {
+// `during` runs on every other thread while thread 0 waits (work that needs
+// the CTA barrier but not the grid one, e.g. issuing the next prefetch).
+template <typename During>
+__device__ bool grid_sync_and(unsigned* bar, unsigned& epoch, uint32_t* status, int* flag,
+                              During&& during) {
   __syncthreads();
   if (threadIdx.x == 0) {
     ++epoch;
@@ -124,9 +128,14 @@ __device__ bool grid_sync(unsigned* bar, unsigned& epoch, uint32_t* status, int*
       }
     }
     *flag = ok;  // the acquire load above orders everything after it
+  } else {
+    during();
   }
   __syncthreads();
   return *flag != 0;
+}
+__device__ bool grid_sync(unsigned* bar, unsigned& epoch, uint32_t* status, int* flag) {
+  return grid_sync_and(bar, epoch, status, flag, [] {});
 }
 
 __device__ __forceinline__ void slot_sync(int id) {
@@ -286,32 +295,54 @@ __device__ Slices my_slices(const T2SDev& m) {
   return s;
 }
 
-// Thread 0 only: stream this CTA's slices of layer l into `buf`.
-__device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slices& s, int l,
-                               uint8_t* buf, uint64_t* bar) {
+// Part `part` (0..4) of streaming this CTA's slices of layer l into `buf`:
+// 0 posts the byte count of the whole layer (one arrival) and copies the QKV
+// slice, 1 the out slice, 2 the W1 slice, 3 the W2 slice, 4 the LayerNorm
+// vectors (every CTA normalises full rows: n1 of layer l, n2 of layer l - 1).
+// The parts may be issued by different threads, in any order (the copies'
+// bytes may land before the count is posted: the phase cannot complete
+// before the arrival).
+__device__ void prefetch_part(const T2SDev& m, const DecodeArgs& a, const Slices& s, int l,
+                              uint8_t* buf, uint64_t* bar, int part) {
   const size_t D = m.D, F = m.F;
   const uint32_t bq = (s.q1 - s.q0) * D * 2, bo = (s.o1 - s.o0) * D * 2,
                  b1 = (s.a1 - s.a0) * D * 2, b2 = (s.b1 - s.b0) * F * 2;
-  // every CTA normalises full rows, so it also takes the whole LayerNorm
-  // vectors (n1 of layer l, n2 of layer l - 1); one arrival for all bytes
   const uint32_t vb = static_cast<uint32_t>(D) * 4;
-  mbar_arrive_expect_tx(bar, bq + bo + b1 + b2 + (l > 0 ? 4 * vb : 2 * vb));
-  uint8_t* p = buf;
-  if (bq) bulk_load(p, m.wqkv + (static_cast<size_t>(l) * 3 * D + s.q0) * D, bq, bar);
-  p = buf + static_cast<size_t>(a.mq) * D * 2;
-  if (bo) bulk_load(p, m.wout + (static_cast<size_t>(l) * D + s.o0) * D, bo, bar);
-  p += static_cast<size_t>(a.mo) * D * 2;
-  if (b1) bulk_load(p, m.w1 + (static_cast<size_t>(l) * F + s.a0) * D, b1, bar);
-  p += static_cast<size_t>(a.m1) * D * 2;
-  const uint16_t* w2 = m.w2p ? m.w2p : m.w2;  // the lane-ordered copy when there is one
-  if (b2) bulk_load(p, w2 + (static_cast<size_t>(l) * D + s.b0) * F, b2, bar);
-  float* ln = reinterpret_cast<float*>(buf + a.ln_off);
-  bulk_load(ln, m.n1g + static_cast<size_t>(l) * D, vb, bar);
-  bulk_load(ln + D, m.n1b + static_cast<size_t>(l) * D, vb, bar);
-  if (l > 0) {
-    bulk_load(ln + 2 * D, m.n2g + static_cast<size_t>(l - 1) * D, vb, bar);
-    bulk_load(ln + 3 * D, m.n2b + static_cast<size_t>(l - 1) * D, vb, bar);
+  uint8_t* pq = buf;
+  uint8_t* po = pq + static_cast<size_t>(a.mq) * D * 2;
+  uint8_t* p1 = po + static_cast<size_t>(a.mo) * D * 2;
+  uint8_t* p2 = p1 + static_cast<size_t>(a.m1) * D * 2;
+  switch (part) {
+    case 0:
+      mbar_arrive_expect_tx(bar, bq + bo + b1 + b2 + (l > 0 ? 4 * vb : 2 * vb));
+      if (bq) bulk_load(pq, m.wqkv + (static_cast<size_t>(l) * 3 * D + s.q0) * D, bq, bar);
+      break;
+    case 1:
+      if (bo) bulk_load(po, m.wout + (static_cast<size_t>(l) * D + s.o0) * D, bo, bar);
+      break;
+    case 2:
+      if (b1) bulk_load(p1, m.w1 + (static_cast<size_t>(l) * F + s.a0) * D, b1, bar);
+      break;
+    case 3: {
+      const uint16_t* w2 = m.w2p ? m.w2p : m.w2;  // the lane-ordered copy when there is one
+      if (b2) bulk_load(p2, w2 + (static_cast<size_t>(l) * D + s.b0) * F, b2, bar);
+      break;
+    }
+    default: {
+      float* ln = reinterpret_cast<float*>(buf + a.ln_off);
+      bulk_load(ln, m.n1g + static_cast<size_t>(l) * D, vb, bar);
+      bulk_load(ln + D, m.n1b + static_cast<size_t>(l) * D, vb, bar);
+      if (l > 0) {
+        bulk_load(ln + 2 * D, m.n2g + static_cast<size_t>(l - 1) * D, vb, bar);
+        bulk_load(ln + 3 * D, m.n2b + static_cast<size_t>(l - 1) * D, vb, bar);
+      }
+    }
   }
+}
+// One thread: the whole layer.
+__device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slices& s, int l,
+                               uint8_t* buf, uint64_t* bar) {
+  for (int part = 0; part < 5; ++part) prefetch_part(m, a, s, l, buf, bar, part);
 }
 
 #include "t2s_cluster.cuh"
@@ -490,6 +521,17 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       const float* lnb = reinterpret_cast<const float*>(wbuf[b] + a.ln_off);
       GSVK_TR(16 + 16 * l + 11);
       if (tid < nq + no + na + nb) bsm[tid] = bias_next;  // loaded a phase ago
+      {  // warm L2 with the K / V rows this thread reads in P2 (all but the new key)
+        const uint16_t* kc_l = m.kc + static_cast<size_t>(l) * m.cap * D;
+        const uint16_t* vc_l = m.vc + static_cast<size_t>(l) * m.cap * D;
+        for (int it = blockIdx.x * kSlots + (tid >> 6); it < H * nch; it += G * kSlots) {
+          const int h = it / nch, k = (it - h * nch) * kChunk + (tid & 63);
+          if (k < len - 1) {
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(kc_l + static_cast<size_t>(k) * D + h * HD));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(vc_l + static_cast<size_t>(k) * D + h * HD));
+          }
+        }
+      }
       if (l > 0) {
         load_vec<2>(xs, m.xpre, D);
         __syncthreads();
@@ -654,13 +696,18 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
           if (lane == 0) m.xpre[r] = __fadd_rn(__fadd_rn(acc, bsm[nq + no + na + r - s.b0]), hs[r]);
         }
       }
-      __syncthreads();  // every warp is done with wbuf[b]
-      if (tid == 0) {
-        prefetch_layer(m, a, s, (l + 2) % L, wbuf[b], &mbar[b]);  // global layer gl + 2
-        pending[b] = 1;
-      }
+      pending[b] = 1;
       GSVK_TR(16 + 16 * l + 8);
-      if (!grid_sync(m.bar, epoch, m.status, flag)) { alive = false; break; }
+      // after the CTA barrier every warp is done with wbuf[b]: it is refilled
+      // with global layer gl + 2 while thread 0 waits at the grid barrier
+      if (!grid_sync_and(m.bar, epoch, m.status, flag, [&] {
+            // the five parts issued in parallel by lane 0 of warps 1..5
+            if (lane == 0 && warp >= 1 && warp <= 5)
+              prefetch_part(m, a, s, (l + 2) % L, wbuf[b], &mbar[b], warp - 1);
+          })) {
+        alive = false;
+        break;
+      }
       GSVK_TR(16 + 16 * l + 9);
     }
     if (!alive) break;
