@@ -45,6 +45,7 @@ SIGNATURES = {
     "gsvk_gemm_f16": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "gsvk_gemm_f16_ex": (c_int, [_vp, _vp]),
     "gsvk_gemm_grouped_f16": (c_int, [_vp, _sz, _vp]),
+    "gsvk_gemm_f16_batched": (c_int, [_vp, _sz, _sz, _sz, _sz, _vp]),
     "gsvk_weights_register": (c_int, [_vp, _sz, _sz, _vp]),
     "gsvk_weights_release": (c_int, [_vp]),
     "gsvk_weights_data": (_vp, [_vp]),
@@ -220,6 +221,24 @@ def _gemm_args(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.
                     0 if residual is None else residual.stride(0), _ptr(c),
                     0 if c is None else c.stride(0), _ptr(c_f16),
                     0 if c_f16 is None else c_f16.stride(0), act, slope, alpha)
+
+
+def gemm_batched(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, c=None,
+                 c_f16=None, stream=None):
+    """Strided batched C[i] = act(alpha * A[i].B[i]^T + bias) + residual[i]:
+    a [batch, M, K], b [batch, N, K] or [N, K] (shared), outputs and
+    residual [batch, M, N] (CUDA tensors, rows contiguous)."""
+    batch, M, K = a.shape
+    N = b.shape[-2]
+    out = c if c is not None else c_f16
+    g = GemmArgs(_ptr(a), a.stride(1), _ptr(b), b.stride(-2), M, N, K, _ptr(bias),
+                 _ptr(residual), 0 if residual is None else residual.stride(1), _ptr(c),
+                 0 if c is None else c.stride(1), _ptr(c_f16),
+                 0 if c_f16 is None else c_f16.stride(1), act, slope, alpha)
+    sb = b.stride(0) if b.dim() == 3 else 0
+    check(lib().gsvk_gemm_f16_batched(ctypes.byref(g), batch, a.stride(0), sb, out.stride(0),
+                                      _stream(stream)))
+    return out
 
 
 def gemm_grouped(problems, stream=None):

@@ -607,6 +607,74 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   return gemm_ex_run(g, as_cuda(stream), false);
 }
 
+int gsvk_gemm_f16_batched(const gsvk_gemm_args* g, size_t batch, size_t stride_a,
+                          size_t stride_b, size_t stride_c, gsvk_stream_t stream) {
+  if (!g || batch == 0) return fail(GSVK_ERR_INVALID, "gemm_batched: null arguments or zero batch");
+  if (!g->a || !g->b || (!g->c && !g->c_f16) || g->M == 0 || g->N == 0 || g->K == 0)
+    return fail(GSVK_ERR_INVALID, "gemm_batched: null pointer or zero size");
+  cudaStream_t st = as_cuda(stream);
+  const size_t lda = g->lda ? g->lda : g->K, ldb = g->ldb ? g->ldb : g->K;
+  const size_t ldc = g->ldc ? g->ldc : g->N, ldh = g->ldc_f16 ? g->ldc_f16 : g->N;
+  const size_t ldr = g->ld_res ? g->ld_res : g->N;
+  if (lda < g->K || ldb < g->K) return fail(GSVK_ERR_INVALID, "gemm_batched: lda/ldb < K");
+  if (g->act < GSVK_ACT_NONE || g->act > GSVK_ACT_TANH)
+    return fail(GSVK_ERR_INVALID, "gemm_batched: bad act");
+  // One persistent tensor-core launch over every (problem, tile) when the
+  // problems sit at whole-row strides of one tensor each and every output
+  // shares one row layout; otherwise one launch per problem.
+  const size_t ldo = g->c ? ldc : ldh;
+  bool one_launch = g->K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 && aligned16(g->a) &&
+                    aligned16(g->b) && stride_a % lda == 0 && stride_b % ldb == 0 &&
+                    stride_c % ldo == 0 && (!g->c || !g->c_f16 || ldc == ldh) &&
+                    (!g->residual || ldr == ldo);
+  const size_t a_rb = one_launch ? stride_a / lda : 0, b_rb = one_launch ? stride_b / ldb : 0,
+               c_rb = one_launch ? stride_c / ldo : 0;
+  one_launch = one_launch && (batch - 1) * a_rb + g->M < 0x7fffffffULL &&
+               (batch - 1) * b_rb + g->N < 0x7fffffffULL &&
+               (batch - 1) * c_rb + g->M < 0x7fffffffULL && batch < 0x7fffffffULL &&
+               c_rb >= g->M;  // outputs of different problems must not overlap
+  if (!one_launch) {
+    for (size_t i = 0; i < batch; ++i) {
+      gsvk_gemm_args gi = *g;
+      gi.a += i * stride_a;
+      gi.b += i * stride_b;
+      if (gi.c) gi.c += i * stride_c;
+      if (gi.c_f16) gi.c_f16 += i * stride_c;
+      if (gi.residual) gi.residual += i * stride_c;
+      if (int rc = gemm_ex_run(&gi, st, false)) return rc;
+    }
+    return GSVK_OK;
+  }
+  TcEpilogue e = make_epilogue();
+  e.bias = g->bias;
+  e.residual = g->residual;
+  e.ld_res = (long long)ldr;
+  e.c32 = g->c;
+  e.ld_c32 = (long long)ldc;
+  e.c16 = g->c_f16;
+  e.ld_c16 = (long long)ldh;
+  e.act = g->act;
+  e.slope = g->slope;
+  e.alpha = g->alpha == 0.f ? 1.f : g->alpha;
+  TcProblem p{};
+  p.M = (int)g->M;
+  p.N = (int)g->N;
+  p.kc = (int)g->K;
+  p.taps = 1;
+  p.dil = 1;
+  p.phases = (int)batch;
+  p.out_rows = (int)g->M;
+  p.bh = 1;  // phase = problem index
+  p.a_rb = (int)a_rb;
+  p.b_rb = (int)b_rb;
+  p.c_rb = (int)c_rb;
+  const long long m_tiles = (long long)((g->M + 127) / 128);
+  const int bn = g->N <= 128 ? 0 : (m_tiles * (long long)((g->N + 255) / 256) * (long long)batch >=
+                                            sm_count() ? 256 : 128);
+  return tc_run(g->a, (long long)((batch - 1) * a_rb + g->M), (long long)lda, g->b,
+                (long long)((batch - 1) * b_rb + g->N), (long long)ldb, p, e, bn, st);
+}
+
 }  // extern "C"
 
 int gsvk::gemm_ex_run(const gsvk_gemm_args* g, cudaStream_t st, bool static_b) {

@@ -112,6 +112,18 @@ typedef struct {
 } gsvk_gemm_args;
 int gsvk_gemm_f16_ex(const gsvk_gemm_args* args, gsvk_stream_t stream);
 
+/* Strided batched GEMM: `batch` independent problems of one shape and one
+ * epilogue, problem i reading A at args->a + i*stride_a and B at
+ * args->b + i*stride_b (stride_b = 0: shared weights) and writing C (and the
+ * residual it reads) at + i*stride_c; strides in elements.  When the strides
+ * are whole rows of their tensors (stride % leading dimension == 0) and the
+ * outputs share one row layout, all problems run as ONE persistent
+ * tensor-core launch over every (problem, tile); otherwise one launch per
+ * problem.  The batched form of AmxBatchNode / amx_batch_run for
+ * same-shape work (gemm_f16_amx.hpp:64-78). */
+int gsvk_gemm_f16_batched(const gsvk_gemm_args* args, size_t batch, size_t stride_a,
+                          size_t stride_b, size_t stride_c, gsvk_stream_t stream);
+
 /* Grouped GEMM: `count` independent problems (each with its own operands,
  * shapes and epilogue) submitted together on one stream, in order.  Replaces
  * AmxBatchNode + amx_batch_run (gemm_f16_amx.hpp:64-78).  Every group is

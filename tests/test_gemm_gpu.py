@@ -228,3 +228,28 @@ def test_registered_weights_match_pointer_calls(dev):
         assert torch.equal(y1, y2)
         reg.close()
     assert dev.device_status() == 0
+
+
+@pytest.mark.parametrize("batch,M,N,K,shared_w", [(16, 128, 2048, 512, False), (5, 100, 300, 72, False),
+                                                   (3, 1, 96, 64, True), (4, 257, 130, 136, True)])
+def test_gemm_batched_matches_reference(dev, ora, batch, M, N, K, shared_w):
+    """gsvk_gemm_f16_batched: independent problems in one launch (strided
+    batch), each within the GEMM tolerance of the fp64 reference; the
+    residual and fp16 output follow the problem stride."""
+    rng = np.random.default_rng(batch * 1000 + M)
+    a = h(rand16(rng, (batch, M, K), 1.0))
+    w = h(rand16(rng, (N, K) if shared_w else (batch, N, K), 0.05))
+    bias = f(rng.standard_normal(N).astype(np.float32) * 0.1)
+    res = f(rng.standard_normal((batch, M, N)).astype(np.float32))
+    c = torch.empty(batch, M, N, device="cuda")
+    c16 = torch.empty(batch, M, N, dtype=torch.float16, device="cuda")
+    dev.gemm_batched(a, w, bias=bias, residual=res, act=dev.ACT_RELU, c=c, c_f16=c16)
+    an = a.cpu().numpy().view(np.uint16)
+    wn = w.cpu().numpy().view(np.uint16)
+    for i in range(batch):
+        wi = wn if shared_w else wn[i]
+        ref = ora.linear_f16(ora.f16_to_f32(an[i]), wi, bias.cpu().numpy(), 1, 0.0) + res[i].cpu().numpy()
+        got = c[i].cpu().numpy()
+        assert np.abs(got - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max()), f"problem {i}"
+        np.testing.assert_array_equal(c16[i].cpu().numpy(), got.astype(np.float16))
+    assert dev.device_status() == 0
