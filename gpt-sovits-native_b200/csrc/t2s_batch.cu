@@ -43,11 +43,14 @@ struct BatchDev {
   float* margins;                 // [max_steps][B] (optional)
 };
 
-__global__ void batch_embed_kernel(BatchDev m, float* __restrict__ x32, uint16_t* __restrict__ x16) {
+__global__ void batch_embed_kernel(BatchDev m, float* __restrict__ x32, uint16_t* __restrict__ x16,
+                                   int* __restrict__ attn_work) {
   const int b = blockIdx.x, D = m.D;
   const int s = *m.step;
   if (s >= m.max_steps) return;  // past the buffers: no-op
   griddep_launch_dependents();
+  if (b == 0)  // the attention work counters of this step's layers
+    for (int i = threadIdx.x; i < m.L; i += blockDim.x) attn_work[i] = 0;
   const uint16_t* er = m.emb + static_cast<size_t>(m.tok[b]) * D;
   const float* pr = m.pe + static_cast<size_t>(m.base_pe[b] + s) * D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -225,6 +228,328 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(BatchDev m, in
   if (tid == 0) ticket[b] = 0;
 }
 
+// Streaming split-KV attention (d_model <= 512): one persistent CTA per SM
+// walks work items (utterance b, split sp) = keys [kAttnSplitKeys*sp,
+// +kAttnSplitKeys) of b, all heads.  Thread 0 keeps kAttnStages chunk
+// copies (16 keys of K and of V, two 1D bulk copies) in flight across items:
+// each CTA's first item is fixed (its block index), later ones come from a
+// per-layer work counter (zeroed by the step's embedding kernel).  Within an
+// item the softmax runs online over its chunks (running max / sum per head,
+// accumulator rescaled); a one-split utterance writes its output directly,
+// otherwise each split writes (max, sum, unnormalised output) per head and the
+// split that takes the utterance's last ticket merges them.
+constexpr int kAttnStages = 3;
+constexpr int kSChunk = 16;  // keys per streamed chunk (two CTAs per SM)
+constexpr int kAttnSplitChunks = 8;
+constexpr int kAttnSplitKeys = kSChunk * kAttnSplitChunks;
+
+size_t attn_stream_smem_bytes(int D, int H, int B) {
+  return static_cast<size_t>(kAttnStages) * kSChunk * D * 2 * 2 +  // K, V ring
+         static_cast<size_t>(kAttnThreads / 32) * 256 * 4 +            // PV partials
+         (static_cast<size_t>(H) * (kSChunk + 1) + 4 * H) * 4 +     // P, max/sum/scale
+         static_cast<size_t>(B + 1 + 2 * kAttnStages) * 4 + 64;        // item offsets, slots
+}
+
+template <int NSEG>
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    batch_attn_stream_kernel(BatchDev m, int l, const float* __restrict__ qkv,
+                             uint16_t* __restrict__ out16, float* __restrict__ part_o,
+                             float2* __restrict__ part_ml, unsigned* __restrict__ ticket,
+                             int* __restrict__ work, int max_chunks, uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t as_smem[];
+  __shared__ uint64_t full[kAttnStages];
+  __shared__ int is_last;
+  const int D = m.D, H = m.H, HD = m.HD, B = m.B;
+  const int s = *m.step;
+  if (s >= m.max_steps) return;
+  uint16_t* kbuf = reinterpret_cast<uint16_t*>(as_smem);
+  uint16_t* vbuf = kbuf + static_cast<size_t>(kAttnStages) * kSChunk * D;
+  float* sPart = reinterpret_cast<float*>(vbuf + static_cast<size_t>(kAttnStages) * kSChunk * D);
+  float* sP = sPart + (kAttnThreads / 32) * 256;  // [H][kSChunk + 1]
+  float* sMr = sP + H * (kSChunk + 1);          // running max per head
+  float* sLr = sMr + H;                            // running sum per head
+  float* sSc = sLr + H;                            // this chunk's rescale of the accumulator
+  int* sOff = reinterpret_cast<int*>(sSc + H);     // [B + 1] first item of each utterance
+  int* sItem = sOff + B + 1;                       // [kAttnStages] item of the slot's chunk (-1: none)
+  int* sChunk = sItem + kAttnStages;               // [kAttnStages] chunk index in its utterance
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  if (tid == 0) {
+    for (int i = 0; i < kAttnStages; ++i) mbar_init(&full[i], 1);
+    fence_barrier_init();
+    int acc = 0;
+    for (int b = 0; b < B; ++b) {
+      sOff[b] = acc;
+      acc += (m.base_len[b] + s + 1 + kAttnSplitKeys - 1) / kAttnSplitKeys;
+    }
+    sOff[B] = acc;
+  }
+  __syncthreads();
+  const int n_items = sOff[B];
+  auto item_utt = [&](int it) {  // the utterance of item `it` (binary search)
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sOff[mid] <= it) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  };
+  // ---- producer (thread 0): the CTA's chunk sequence, one slot at a time
+  int p_item = -1, p_c = 0, p_cend = 0, p_grab = 0, p_n = 0;
+  bool p_done = false;
+  auto produce = [&](bool dynamic) -> bool {  // false: nothing issued (needs the work counter)
+    const int sl = p_n % kAttnStages;
+    while (!p_done && p_c >= p_cend) {  // next item
+      int it;
+      if (p_grab == 0) {
+        it = blockIdx.x;
+      } else {
+        if (!dynamic) return false;
+        it = static_cast<int>(gridDim.x) + atomicAdd(work + l, 1);
+      }
+      ++p_grab;
+      if (it >= n_items) {
+        p_done = true;
+        break;
+      }
+      const int b = item_utt(it), sp = it - sOff[b];
+      const int nch = (m.base_len[b] + s + 1 + kSChunk - 1) / kSChunk;
+      p_item = it;
+      p_c = sp * kAttnSplitChunks;
+      p_cend = min(nch, p_c + kAttnSplitChunks);
+    }
+    if (p_done) {
+      sItem[sl] = -1;
+      mbar_arrive(&full[sl]);  // completes the phase with no copy: the consumers stop here
+    } else {
+      const int b = item_utt(p_item);
+      const int len = m.base_len[b] + s + 1;
+      const int k0 = p_c * kSChunk, rows = min(kSChunk, len - k0);
+      const size_t slab = (static_cast<size_t>(b) * m.L + l) * m.cap + k0;
+      const uint32_t bytes = static_cast<uint32_t>(rows) * D * 2;
+      sItem[sl] = p_item;
+      sChunk[sl] = p_c;
+      mbar_arrive_expect_tx(&full[sl], 2 * bytes);
+      bulk_load(kbuf + static_cast<size_t>(sl) * kSChunk * D, m.kc + slab * D, bytes, &full[sl]);
+      bulk_load(vbuf + static_cast<size_t>(sl) * kSChunk * D, m.vc + slab * D, bytes, &full[sl]);
+      ++p_c;
+    }
+    ++p_n;
+    return true;
+  };
+  if (tid == 0) {  // the fixed first item's chunks, before the dependency resolves
+    while (p_n < kAttnStages && produce(false)) {
+    }
+  }
+  griddep_wait();  // q and the new K/V rows come from the QKV projection
+  griddep_launch_dependents();
+  if (tid == 0) {
+    while (p_n < kAttnStages) produce(true);
+  }
+  // lane geometry: a warp covers segment `seg` (256 halves) of rows rg, rg + nrg, ...
+  constexpr int nrg = (kAttnThreads / 32) / NSEG;  // row groups
+  constexpr int kRows = kSChunk / nrg;          // rows per warp and chunk
+  const int seg = warp % NSEG, rg = warp / NSEG;
+  const int e0 = seg * 256 + lane * 8;
+  const int lph = HD / 8, head = e0 / HD;
+  float q[8], acc[8];
+  bool failed = false;
+  for (uint32_t ci = 0;; ++ci) {
+    const int sl = static_cast<int>(ci % kAttnStages);
+    // one lane per warp polls; the rest park at the warp barrier
+    if (!failed) {
+      bool ok = true;
+      if (lane == 0) {
+        ok = false;
+        for (uint32_t i = 0; i < kSpinLimit && !ok; ++i) ok = mbar_try_wait(&full[sl], (ci / kAttnStages) & 1u);
+        if (!ok) atomicExch(status, DEV_TIMEOUT);
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (ok) mbar_try_wait(&full[sl], (ci / kAttnStages) & 1u);  // this lane's acquire
+      failed = !ok;
+    }
+    if (!__syncthreads_and(!failed)) break;
+    const int it = sItem[sl];
+    if (it < 0) break;
+    const int c = sChunk[sl];
+    const int b = item_utt(it), sp = it - sOff[b];
+    const int len = m.base_len[b] + s + 1;
+    const int nch = (len + kSChunk - 1) / kSChunk;
+    const int nsplit = sOff[b + 1] - sOff[b];
+    const int k0 = c * kSChunk, rows = min(kSChunk, len - k0);
+    const bool first = c == sp * kAttnSplitChunks;
+    const bool last = c == min(nch, (sp + 1) * kAttnSplitChunks) - 1;
+    uint16_t* sK = kbuf + static_cast<size_t>(sl) * kSChunk * D;
+    uint16_t* sV = vbuf + static_cast<size_t>(sl) * kSChunk * D;
+    const float* qrow = qkv + static_cast<size_t>(b) * 3 * D;
+    if (first) {  // a new item: its query and a fresh running state
+      const float4 q0 = *reinterpret_cast<const float4*>(qrow + e0);
+      const float4 q1 = *reinterpret_cast<const float4*>(qrow + e0 + 4);
+      q[0] = q0.x * m.scale; q[1] = q0.y * m.scale; q[2] = q0.z * m.scale; q[3] = q0.w * m.scale;
+      q[4] = q1.x * m.scale; q[5] = q1.y * m.scale; q[6] = q1.z * m.scale; q[7] = q1.w * m.scale;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      if (tid < H) {
+        sMr[tid] = -INFINITY;
+        sLr[tid] = 0.f;
+      }
+    }
+    if (c == nch - 1) {  // the new slot pos = len - 1: append this step's K / V row
+      const size_t slab = (static_cast<size_t>(b) * m.L + l) * m.cap + k0;
+      const int r_new = rows - 1;
+      for (int i = tid; i < D; i += kAttnThreads) {
+        const uint16_t kv = f2h(qrow[D + i]), vv = f2h(qrow[2 * D + i]);
+        sK[r_new * D + i] = kv;
+        sV[r_new * D + i] = vv;
+        m.kc[(slab + r_new) * D + i] = kv;
+        m.vc[(slab + r_new) * D + i] = vv;
+      }
+    }
+    __syncthreads();
+    {  // scores of this warp's kRows rows: all loads first, independent chains
+      uint4 kr[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        const int r = rg + i * nrg;
+        kr[i] = r < rows ? *reinterpret_cast<const uint4*>(sK + r * D + e0) : make_uint4(0, 0, 0, 0);
+      }
+      float d[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        float kf[8];
+        unpack8(kr[i], kf);
+        d[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d[i] = fmaf(q[j], kf[j], d[i]);
+      }
+      for (int o = 1; o < lph; o <<= 1) {
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) d[i] += __shfl_xor_sync(0xffffffffu, d[i], o);
+      }
+      if ((lane & (lph - 1)) == 0) {
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) {
+          const int r = rg + i * nrg;
+          if (r < rows) sP[head * (kSChunk + 1) + r] = d[i];
+        }
+      }
+    }
+    __syncthreads();
+    {  // online softmax of heads warp and warp + 8 (both chains interleaved)
+      const int h0 = warp, h1 = warp + kAttnThreads / 32;
+      const bool one = h0 < H, two = h1 < H;
+      float* p0 = sP + (one ? h0 : 0) * (kSChunk + 1);
+      float* p1 = sP + (two ? h1 : 0) * (kSChunk + 1);
+      const bool in = lane < rows;
+      const float s0 = in && one ? p0[lane] : -INFINITY;
+      const float s1 = in && two ? p1[lane] : -INFINITY;
+      float mx0 = s0, mx1 = s1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      const float mo0 = one ? sMr[h0] : 0.f, mo1 = two ? sMr[h1] : 0.f;
+      const float mn0 = fmaxf(mo0, mx0), mn1 = fmaxf(mo1, mx1);
+      const float ev0 = in && one ? expf(s0 - mn0) : 0.f, ev1 = in && two ? expf(s1 - mn1) : 0.f;
+      if (in && one) p0[lane] = ev0;
+      if (in && two) p1[lane] = ev1;
+      float su0 = ev0, su1 = ev1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        su0 += __shfl_xor_sync(0xffffffffu, su0, o);
+        su1 += __shfl_xor_sync(0xffffffffu, su1, o);
+      }
+      if (lane == 0 && one) {
+        const float sc = mo0 == -INFINITY ? 0.f : expf(mo0 - mn0);
+        sSc[h0] = sc;
+        sLr[h0] = fmaf(sLr[h0], sc, su0);
+        sMr[h0] = mn0;
+      }
+      if (lane == 0 && two) {
+        const float sc = mo1 == -INFINITY ? 0.f : expf(mo1 - mn1);
+        sSc[h1] = sc;
+        sLr[h1] = fmaf(sLr[h1], sc, su1);
+        sMr[h1] = mn1;
+      }
+    }
+    __syncthreads();
+    {  // P.V of this warp's rows: all loads first
+      uint4 vr[kRows];
+      float pr[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        const int r = rg + i * nrg;
+        const bool ok = r < rows;
+        vr[i] = ok ? *reinterpret_cast<const uint4*>(sV + r * D + e0) : make_uint4(0, 0, 0, 0);
+        pr[i] = ok ? sP[head * (kSChunk + 1) + r] : 0.f;
+      }
+      const float sc = sSc[head];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] *= sc;
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        float vf[8];
+        unpack8(vr[i], vf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = fmaf(pr[i], vf[j], acc[j]);
+      }
+    }
+    __syncthreads();  // every thread is done with the slot
+    if (tid == 0) produce(true);
+    if (!last) continue;
+    // ---- the item is complete: reduce the row groups, then output / partial
+    float4* pw = reinterpret_cast<float4*>(sPart + warp * 256 + lane * 8);
+    pw[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    pw[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    __syncthreads();
+    const size_t pc = static_cast<size_t>(b) * max_chunks;
+    for (int i = tid; i < D; i += kAttnThreads) {
+      const int sg = i >> 8, w = i & 255;
+      float o = 0.f;
+      for (int g = 0; g < nrg; ++g) o += sPart[(g * NSEG + sg) * 256 + w];
+      if (nsplit == 1)
+        out16[static_cast<size_t>(b) * D + i] = f2h(o / sLr[i / HD]);
+      else
+        part_o[(pc + sp) * D + i] = o;
+    }
+    if (nsplit > 1) {
+      if (tid < H) part_ml[(pc + sp) * H + tid] = make_float2(sMr[tid], sLr[tid]);
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) is_last = atomicAdd(&ticket[b], 1u) == static_cast<unsigned>(nsplit - 1);
+      __syncthreads();
+      if (is_last) {
+        __threadfence();
+        // out = sum_sp e^(m_sp - M) o_sp / sum_sp e^(m_sp - M) l_sp, per head
+        if (tid < H) {
+          float M = -INFINITY;
+          for (int cc = 0; cc < nsplit; ++cc) M = fmaxf(M, __ldcg(&part_ml[(pc + cc) * H + tid]).x);
+          float den = 0.f;
+          for (int cc = 0; cc < nsplit; ++cc) {
+            const float2 ml = __ldcg(&part_ml[(pc + cc) * H + tid]);
+            den = fmaf(expf(ml.x - M), ml.y, den);
+          }
+          sSc[tid] = M;
+          sP[tid] = den;
+        }
+        __syncthreads();
+        for (int i = tid; i < D; i += kAttnThreads) {
+          const int h = i / HD;
+          const float M = sSc[h];
+          float num = 0.f;
+          for (int cc = 0; cc < nsplit; ++cc)
+            num = fmaf(expf(__ldcg(&part_ml[(pc + cc) * H + h]).x - M),
+                       __ldcg(&part_o[(pc + cc) * D + i]), num);
+          out16[static_cast<size_t>(b) * D + i] = f2h(num / sP[h]);
+        }
+        if (tid == 0) ticket[b] = 0;
+      }
+    }
+    __syncthreads();  // sPart / sP / sSc are reused by the next item
+  }
+}
+
 size_t attn_smem_bytes(int D, int H) {
   return static_cast<size_t>(kAttnChunk) * D * 2 * 2 +
          (static_cast<size_t>(H) * (kAttnChunk + 1) + 2 * H) * 4;
@@ -348,6 +673,8 @@ struct T2SBatchEngine {
   float* margins = nullptr;
   unsigned* done = nullptr;
   unsigned* ticket = nullptr;  // [B] attention merge tickets (zero between launches)
+  int* attn_work = nullptr;    // [L] streaming attention work counters (zeroed per step)
+  bool attn_stream = false;    // the streaming attention kernel (d_model <= 512)
   float* part_o = nullptr;     // [B][max_chunks][D] per-chunk attention outputs
   float2* part_ml = nullptr;   // [B][max_chunks][H] per-chunk (max, sum)
   int max_chunks = 0;
@@ -393,18 +720,26 @@ int batch_step(T2SBatchEngine* e, int B, cudaStream_t st, int* launches) {
   BatchDev& m = e->d;
   const int D = m.D, F = m.F;
   int n = 0, rc;
-  batch_embed_kernel<<<B, 256, 0, st>>>(m, e->x32, e->x16);
+  batch_embed_kernel<<<B, 256, 0, st>>>(m, e->x32, e->x16, e->attn_work);
   if ((rc = check_launch("batch_embed_kernel"))) return rc;
   ++n;
   for (int l = 0; l < m.L; ++l) {
     if ((rc = gemm_m(e->x16, B, D, m.wqkv + (size_t)l * 3 * D * D, 3 * D,
                      m.bqkv + (size_t)l * 3 * D, GSVK_ACT_NONE, nullptr, e->qkv32, nullptr, st)))
       return rc;
-    if ((rc = launch_pdl(batch_attn_kernel, dim3(e->max_chunks, B), dim3(kAttnThreads),
-                         attn_smem_bytes(D, m.H), st, "batch_attn_kernel", m, l, e->qkv32,
-                         e->attn16, e->part_o, e->part_ml, e->ticket, e->max_chunks,
-                         device_status())))
+    if (e->attn_stream) {
+      auto* fn = D == 512 ? batch_attn_stream_kernel<2> : batch_attn_stream_kernel<1>;
+      if ((rc = launch_pdl(fn, dim3(2 * sm_count()), dim3(kAttnThreads),
+                           attn_stream_smem_bytes(D, m.H, m.B), st, "batch_attn_stream_kernel", m,
+                           l, e->qkv32, e->attn16, e->part_o, e->part_ml, e->ticket, e->attn_work,
+                           e->max_chunks, device_status())))
+        return rc;
+    } else if ((rc = launch_pdl(batch_attn_kernel, dim3(e->max_chunks, B), dim3(kAttnThreads),
+                                attn_smem_bytes(D, m.H), st, "batch_attn_kernel", m, l, e->qkv32,
+                                e->attn16, e->part_o, e->part_ml, e->ticket, e->max_chunks,
+                                device_status()))) {
       return rc;
+    }
     if ((rc = gemm_m(e->attn16, B, D, m.wout + (size_t)l * D * D, D, m.bout + (size_t)l * D,
                      GSVK_ACT_NONE, e->x32, e->hpre32, nullptr, st)))
       return rc;
@@ -548,7 +883,7 @@ int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weight
                o_a16 = take(B * D * 2), o_h16 = take(B * D * 2), o_ff = take(B * F * 2);
   const int max_chunks = (cap + kAttnChunk - 1) / kAttnChunk;
   const size_t o_tk = take(B * 4), o_po = take(B * max_chunks * D * 4),
-               o_pm = take(B * max_chunks * H * 8);
+               o_pm = take(B * max_chunks * H * 8), o_wk = take((size_t)L * 4);
   if (cudaMalloc(&e->amem, off) != cudaSuccess) {
     cudaGetLastError();
     gsvk_t2s_batch_destroy(e);
@@ -583,6 +918,18 @@ int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weight
   e->part_o = reinterpret_cast<float*>(a + o_po);
   e->part_ml = reinterpret_cast<float2*>(a + o_pm);
   e->max_chunks = max_chunks;
+  e->attn_work = reinterpret_cast<int*>(a + o_wk);
+  e->attn_stream = D == 256 || D == 512;
+  if (e->attn_stream) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(D == 512 ? batch_attn_stream_kernel<2>
+                                                          : batch_attn_stream_kernel<1>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(attn_stream_smem_bytes(D, H, max_batch))),
+                            "streaming attention smem attribute")) {
+      gsvk_t2s_batch_destroy(e);
+      return rc;
+    }
+  }
   if (int rc = check_cuda(cudaFuncSetAttribute(batch_attn_kernel,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(attn_smem_bytes(D, H))),
