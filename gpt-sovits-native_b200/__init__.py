@@ -46,6 +46,7 @@ SIGNATURES = {
     "gsvk_gemm_f16_ex": (c_int, [_vp, _vp]),
     "gsvk_gemm_grouped_f16": (c_int, [_vp, _sz, _vp]),
     "gsvk_gemm_f16_batched": (c_int, [_vp, _sz, _sz, _sz, _sz, _vp]),
+    "gsvk_gemm_set_pair": (c_int, [c_int]),
     "gsvk_weights_register": (c_int, [_vp, _sz, _sz, _vp]),
     "gsvk_weights_release": (c_int, [_vp]),
     "gsvk_weights_data": (_vp, [_vp]),
@@ -221,6 +222,11 @@ def _gemm_args(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.
                     0 if residual is None else residual.stride(0), _ptr(c),
                     0 if c is None else c.stride(0), _ptr(c_f16),
                     0 if c_f16 is None else c_f16.stride(0), act, slope, alpha)
+
+
+def gemm_set_pair(enable: bool):
+    """Two-SM (cta_group::2) GEMM kernel for eligible plain problems."""
+    check(lib().gsvk_gemm_set_pair(int(bool(enable))))
 
 
 def gemm_batched(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, c=None,

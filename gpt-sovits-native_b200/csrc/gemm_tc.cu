@@ -436,6 +436,212 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Two-SM variant for plain GEMMs (one tap, one phase, K a multiple of 64):
+// a cluster of two CTAs computes 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2.  CTA r of the pair stages rows [128r, 128r+128)
+// of the tile's A rows and of its B rows (its half of N): 32 KB per 64-deep
+// K step, so six stages fit where the one-SM 128 x 256 tile fits four, and
+// every A and B byte a pair reads from L2 feeds 256 rows or columns instead
+// of 128.  CTA r holds rows [128r, +128) of the fp32 accumulator (two
+// accumulators of 256 columns: all 512 TMEM columns).  The leader (rank 0)
+// counts both CTAs' copy bytes on its barriers, issues the pair MMAs and
+// commits to both CTAs' barriers; both CTAs run the epilogue of their rows
+// and release an accumulator by arriving on the leader's barrier.
+constexpr int kPairBN = 256;
+constexpr int kPairBK = 64;
+constexpr int kPairStages = 6;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const TcProblem prob, const TcEpilogue epi, uint32_t* status) {
+  const TcProblem p = prob;
+  const TcEpilogue e = epi;
+  constexpr uint32_t kHalfBytes = 128u * kPairBK * 2u;  // 128 rows of A or of B, 16 KB
+  constexpr uint32_t sbo = 8u * 128u;                    // 8-row atom stride (128 B rows)
+  constexpr uint32_t idesc = idesc_f16_f32(256, kPairBN);
+  constexpr int kAcc = 2;
+  constexpr uint32_t kTmemCols = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kPairStages * kHalfBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kPairStages * kHalfBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;
+  uint64_t* tempty = tfull + kAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kAcc);
+
+  const uint32_t rank = cluster_rank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (p.M + 255) / 256, n_tiles = (p.N + kPairBN - 1) / kPairBN;
+  const int tiles = m_tiles * n_tiles;
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int kbn = p.kc / kPairBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < kAcc; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);  // the epilogue warps of both CTAs
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers and TMEM exist before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int mt = tile / n_tiles, nt = tile - (tile / n_tiles) * n_tiles;
+        for (int kb = 0; kb < kbn; ++kb, ++it) {
+          const int s = it % kPairStages;
+          const uint32_t ph = static_cast<uint32_t>(it / kPairStages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t lead_full = cluster_addr(&full[s], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 4u * kHalfBytes);  // both CTAs' A and B
+          tma_load_2d_pair(sA + static_cast<size_t>(s) * kHalfBytes, &tmA, lead_full, kb * kPairBK,
+                           mt * 256 + static_cast<int>(rank) * 128);
+          tma_load_2d_pair(sB + static_cast<size_t>(s) * kHalfBytes, &tmB, lead_full, kb * kPairBK,
+                           nt * kPairBN + static_cast<int>(rank) * 128);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------- MMA issuer (leader only)
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs, ++tl) {
+        const int acc = tl & 1;
+        const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * kPairBN);
+        for (int kb = 0; kb < kbn; ++kb, ++it) {
+          const int s = it % kPairStages;
+          const uint32_t ph = static_cast<uint32_t>(it / kPairStages) & 1u;
+          if (!mbar_wait(&full[s], ph, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + static_cast<size_t>(s) * kHalfBytes);
+          const uint32_t b_base = smem_u32(sB + static_cast<size_t>(s) * kHalfBytes);
+#pragma unroll
+          for (int j = 0; j < kPairBK / 16; ++j)
+            tc_mma_f16_pair(d_tmem, smem_desc(a_base + 32u * j, sbo, 2),
+                            smem_desc(b_base + 32u * j, sbo, 2), idesc, (kb | j) ? 1u : 0u);
+          tc_commit_pair(cluster_addr(&empty[s], 0));  // both CTAs may refill stage s
+          tc_commit_pair(cluster_addr(&empty[s], 1));
+        }
+        if (!ok) break;
+        tc_commit_pair(cluster_addr(&tfull[acc], 0));  // both CTAs' rows of the tile are done
+        tc_commit_pair(cluster_addr(&tfull[acc], 1));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;      // TMEM lanes 32*quarter .. +31
+    const int half = (warp - 2) >> 2;  // column half
+    const int cbeg = half * (kPairBN / 2);
+    const bool bias_vec = e.bias && aligned16(e.bias);
+    int tl = 0;
+    for (int tile = pair; tile < tiles; tile += npairs, ++tl) {
+      const int mt = tile / n_tiles, nt = tile - (tile / n_tiles) * n_tiles;
+      const int acc = tl & 1;
+      const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
+      const int i = mt * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+      const bool row_ok = i < p.M;
+      const long long orow = i;
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * kPairBN);
+      float bnext[16], rnext[16], snext[16];
+      fetch16(e, row_ok, orow, nt * kPairBN + cbeg, p.N, 0, bias_vec, bnext, rnext, snext);
+      if (!mbar_wait(&tfull[acc], aph, status)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c0 = cbeg; c0 < cbeg + kPairBN / 2; c0 += 16) {
+        float bcur[16], rcur[16], scur[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          bcur[j] = bnext[j];
+          rcur[j] = rnext[j];
+          scur[j] = snext[j];
+        }
+        if (c0 + 16 < cbeg + kPairBN / 2)
+          fetch16(e, row_ok, orow, nt * kPairBN + c0 + 16, p.N, 0, bias_vec, bnext, rnext, snext);
+        uint32_t r[16];
+        tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
+        tmem_ld_wait();
+        if (row_ok && nt * kPairBN + c0 < p.N)
+          store16(e, orow, nt * kPairBN + c0, p.N, r, 0, bcur, rcur, scur);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's last MMAs wrote this CTA's TMEM and read its tiles
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
+                const TcEpilogue& e, cudaStream_t st) {
+  const size_t smem = 1024 + static_cast<size_t>(kPairStages) * 2 * 128 * kPairBK * 2 +
+                      (2 * kPairStages + 4) * 8 + 16;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    int rc = check_cuda(cudaFuncSetAttribute(gemm_pair_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem)),
+                        "cudaFuncSetAttribute(gemm_pair)");
+    if (rc) return rc;
+    attr_set[dev] = true;
+  }
+  const long long tiles = static_cast<long long>((p.M + 255) / 256) * ((p.N + kPairBN - 1) / kPairBN);
+  const int pairs = static_cast<int>(std::min<long long>(tiles, sm_count() / 2));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ta, tb, p, e, device_status()),
+                    "gemm_pair_kernel launch");
+}
+
 template <int BN>
 int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
               const TcEpilogue& e, cudaStream_t st) {
@@ -530,6 +736,8 @@ int tc_pick_bn(long long M, long long N) {
   return (m_tiles * ((N + 255) / 256) >= sm_count()) ? 256 : 128;
 }
 
+static int g_pair_mode = 1;  // two-SM GEMM for eligible plain problems (gsvk_gemm_set_pair)
+
 int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b,
            long long b_rows, long long ldb, TcProblem p, const TcEpilogue& e, int bn,
            cudaStream_t st, long long a_cols, long long b_cols) {
@@ -552,6 +760,15 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
     if (R <= 256 && b_all + 2 * a_win <= kSmemBudget) p.win = static_cast<int>(R);
   }
   CUtensorMap ta, tb;
+  if (g_pair_mode && (bn == 0 || bn == 256) && !p.convt && p.bh == 0 && p.phases == 1 &&
+      p.taps == 1 && p.win == 0 && !p.pdl && p.kc % kPairBK == 0 && p.M >= 256 && p.N >= 256 &&
+      a_cols == 0 && b_cols == 0) {
+    p.bk = kPairBK;
+    int rc = make_kmajor_map(&ta, a, a_rows, p.kc, lda, 128, kPairBK);
+    if (!rc) rc = make_kmajor_map(&tb, b, b_rows, p.kc, ldb, 128, kPairBK);
+    if (rc) return rc;
+    return launch_pair(ta, tb, p, e, st);
+  }
   int rc = make_kmajor_map(&ta, a, a_rows, a_cols ? a_cols : p.kc, lda, p.win ? p.win : kBM, p.bk);
   if (rc) return rc;
   rc = make_kmajor_map(&tb, b, b_rows, b_cols ? b_cols : p.kc, ldb, bn, p.bk);
@@ -605,6 +822,11 @@ int gsvk_gemm_f16(const uint16_t* a, const uint16_t* b, float* c, size_t M, size
 
 int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   return gemm_ex_run(g, as_cuda(stream), false);
+}
+
+int gsvk_gemm_set_pair(int enable) {
+  g_pair_mode = enable != 0;
+  return GSVK_OK;
 }
 
 int gsvk_gemm_f16_batched(const gsvk_gemm_args* g, size_t batch, size_t stride_a,
