@@ -395,7 +395,7 @@ def run_gemm_shape(args, rank, local, world):
             "config": {"workload": "gemm", "shape": [M, N, K], "iters_per_step": iters,
                        "launch": "CUDA graph", "l2": f"{copies} rotated operand copies"},
             "gpu_launches": iters * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel", "achieved": achieved, "peak": tf,
+            "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel", "achieved": achieved, "peak": tf,
                          "unit": "TFLOP/s", "frac": achieved / tf, "peak_source": kind, "traffic": None}}
     if clk:
         line["clocks"] = clk
@@ -554,7 +554,7 @@ def run_encoder(args, rank, local, world):
             "e2e": {"value": flops * world / t_e2e / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": x.nbytes, "d2h_bytes_per_step": x.nbytes},
             "gpu_launches": launches * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel", "achieved": achieved,
+            "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel", "achieved": achieved,
                          "peak": tf, "unit": "TFLOP/s", "frac": achieved / tf,
                          "peak_source": kind, "traffic": None,
                          "note": "the four layer GEMM shapes back to back, CUDA events"}}

@@ -738,6 +738,21 @@ int tc_pick_bn(long long M, long long N) {
 
 static int g_pair_mode = 1;  // two-SM GEMM for eligible plain problems (gsvk_gemm_set_pair)
 
+// Whether the two-SM kernel beats the one-SM kernel with BN-wide tiles.  Both
+// are bound by each SM's L2 ingest (~64 B/clk) rather than by the tensor pipe:
+// per 64-deep K block a pair SM loads 32 KB for a 128x256 slice (512 clk), a
+// one-SM CTA 48 KB at BN = 256 (768 clk) or 32 KB at BN = 128 (512 clk for
+// half the work).  Cost = tile rounds x K-block cost; on a tie the pair wins
+// only for long K, where its larger unoverlapped epilogue is amortised.
+static bool pair_wins(long long M, long long N, long long K, int bn) {
+  const long long sms = sm_count(), pairs = sms / 2;
+  const long long t2 = ((M + 255) / 256) * ((N + 255) / 256);
+  const long long t1 = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+  const long long pair_cost = ((t2 + pairs - 1) / pairs) * 512;
+  const long long one_cost = ((t1 + sms - 1) / sms) * (bn >= 256 ? 768 : 512);
+  return pair_cost < one_cost || (pair_cost == one_cost && K >= 2048);
+}
+
 int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b,
            long long b_rows, long long ldb, TcProblem p, const TcEpilogue& e, int bn,
            cudaStream_t st, long long a_cols, long long b_cols) {
@@ -749,6 +764,7 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
   if (p.M <= 0 || p.N <= 0 || p.kc <= 0 || p.taps <= 0)
     return fail(GSVK_ERR_INVALID, "empty GEMM");
   p.bk = pick_bk(p.kc);
+  const bool bn_auto = bn == 0;
   if (bn == 0) bn = tc_pick_bn(p.M, p.N);
   // window mode: a dilated conv with one K block per tap and one column tile,
   // whose input window (<= 256 rows, the TMA box limit) and weights fit
@@ -760,9 +776,9 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
     if (R <= 256 && b_all + 2 * a_win <= kSmemBudget) p.win = static_cast<int>(R);
   }
   CUtensorMap ta, tb;
-  if (g_pair_mode && (bn == 0 || bn == 256) && !p.convt && p.bh == 0 && p.phases == 1 &&
+  if (g_pair_mode && (bn_auto || bn == 256) && !p.convt && p.bh == 0 && p.phases == 1 &&
       p.taps == 1 && p.win == 0 && !p.pdl && p.kc % kPairBK == 0 && p.M >= 256 && p.N >= 256 &&
-      a_cols == 0 && b_cols == 0) {
+      a_cols == 0 && b_cols == 0 && pair_wins(p.M, p.N, p.kc, bn)) {
     p.bk = kPairBK;
     int rc = make_kmajor_map(&ta, a, a_rows, p.kc, lda, 128, kPairBK);
     if (!rc) rc = make_kmajor_map(&tb, b, b_rows, p.kc, ldb, 128, kPairBK);
