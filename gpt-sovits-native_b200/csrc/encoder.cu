@@ -183,6 +183,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  griddep_wait();  // q|k|v and V^T come from the previous kernel (no-op for an ordinary launch)
+  griddep_launch_dependents();
   const int row0 = b * T;  // first token row of utterance b
   if (warp == 0) {
     if (lane == 0) {
@@ -341,6 +343,8 @@ __global__ void __launch_bounds__(256) enc_ln_warp_kernel(const float* __restric
                                                           uint16_t* __restrict__ y16, int rows,
                                                           double eps) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  griddep_wait();  // x comes from the previous kernel (no-op for an ordinary launch)
+  griddep_launch_dependents();
   if (row >= rows) return;
   constexpr int n = NV4 * 128;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * n);
@@ -378,12 +382,17 @@ __global__ void __launch_bounds__(256) enc_ln_warp_kernel(const float* __restric
   }
 }
 
+// pdl: launched as a programmatic dependent of the previous kernel (the warp
+// kernel waits for it before reading x).
 int enc_layernorm(const float* x, const float* g, const float* b, float* y, uint16_t* y16, int rows,
-                  int n, double eps, cudaStream_t st) {
+                  int n, double eps, cudaStream_t st, bool pdl) {
   const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
   switch (n % 128 == 0 ? n / 128 : 0) {
 #define GSVK_LN_CASE(K)                                                                   \
   case K:                                                                                 \
+    if (pdl)                                                                              \
+      return launch_pdl(enc_ln_warp_kernel<K>, dim3(blocks), dim3(256), 0, st,            \
+                        "enc_ln_warp_kernel", x, g, b, y, y16, rows, eps);                \
     enc_ln_warp_kernel<K><<<blocks, 256, 0, st>>>(x, g, b, y, y16, rows, eps);            \
     return check_launch("enc_ln_warp_kernel");
     GSVK_LN_CASE(4) GSVK_LN_CASE(5) GSVK_LN_CASE(6) GSVK_LN_CASE(7) GSVK_LN_CASE(8)
@@ -569,7 +578,7 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
     g.ldc_f16 = N;
     g.alpha = 1.f;
     ++launches;
-    return gsvk_gemm_f16_ex(&g, stream);
+    return gemm_ex_run(&g, st, fused);
   };
   for (int l = 0; l < c.layers; ++l) {
     // q|k|v (with the fused attention, V goes out transposed per head: V^T is
@@ -593,6 +602,7 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
       e.vt_T = T;
       e.vt_dh = dh;
       e.vt_H = H;
+      p.pdl = 1;
       if ((rc = tc_run(h->x16, M, C, h->wqkv + (size_t)l * 3 * C * C, 3 * C, C, p, e, 0, st)))
         return rc;
       ++launches;
@@ -606,11 +616,11 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
       if ((rc = make_kmajor_map(&tq, h->qkv16, M, 3 * C, 3 * C, kAttnQ, 64))) return rc;
       if ((rc = make_kmajor_map(&tk, h->qkv16, M, 3 * C, 3 * C, Tp, 64))) return rc;
       if ((rc = make_kmajor_map(&tv, h->vt16, (long long)B * H * dh, Tp, Tp, 64, 64))) return rc;
-      enc_attn_kernel<<<dim3((unsigned)((T + kAttnQ - 1) / kAttnQ), (unsigned)H, (unsigned)B),
-                        kAttnThreads,
-                        enc_attn_smem(Tp), st>>>(tq, tk, tv, T, Tp, H, C, valid, h->ctx16,
-                                                 device_status());
-      if ((rc = check_launch("enc_attn_kernel"))) return rc;
+      if ((rc = launch_pdl(enc_attn_kernel,
+                           dim3((unsigned)((T + kAttnQ - 1) / kAttnQ), (unsigned)H, (unsigned)B),
+                           dim3(kAttnThreads), enc_attn_smem(Tp), st, "enc_attn_kernel", tq, tk,
+                           tv, T, Tp, H, C, valid, h->ctx16, device_status())))
+        return rc;
       ++launches;
     } else {
       // S = Q K^T / sqrt(dh), batched over (utterance, head)
@@ -673,7 +683,7 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
                    GSVK_ACT_NONE, x, h->y32, nullptr)))
       return rc;
     if ((rc = enc_layernorm(h->y32, h->ln1g + (size_t)l * C, h->ln1b + (size_t)l * C, h->x1_32,
-                            h->x1_16, M, C, c.eps, st)))
+                            h->x1_16, M, C, c.eps, st, fused)))
       return rc;
     ++launches;
     // FFN
@@ -684,7 +694,7 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
                    GSVK_ACT_NONE, h->x1_32, h->f32, nullptr)))
       return rc;
     if ((rc = enc_layernorm(h->f32, h->ln2g + (size_t)l * C, h->ln2b + (size_t)l * C, x, h->x16, M,
-                            C, c.eps, st)))
+                            C, c.eps, st, fused)))
       return rc;
     ++launches;
   }

@@ -502,6 +502,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Programmatic dependent launch: the set-up above and (B being weights no
+  // kernel in the stream writes) the first stages' B loads overlap the
+  // previous kernel; activations, bias, residual and outputs are touched only
+  // after griddep_wait (a no-op for an ordinary launch).
+  const int pre = (p.pdl && pair < tiles) ? (kbn < kPairStages ? kbn : kPairStages) : 0;
+  if (warp == 0 && lane == 0 && pre > 0) {
+    const int nt0 = pair % n_tiles;
+    for (int s = 0; s < pre; ++s) {
+      if (rank == 0) mbar_arrive_expect_tx(&full[s], 4u * kHalfBytes);  // both CTAs' A and B
+      tma_load_2d_pair(sB + static_cast<size_t>(s) * kHalfBytes, &tmB, cluster_addr(&full[s], 0),
+                       s * kPairBK, nt0 * kPairBN + static_cast<int>(rank) * 128);
+    }
+  }
+  griddep_wait();
+  griddep_launch_dependents();
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- producer
@@ -512,11 +528,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < kbn; ++kb, ++it) {
           const int s = it % kPairStages;
           const uint32_t ph = static_cast<uint32_t>(it / kPairStages) & 1u;
+          const uint32_t lead_full = cluster_addr(&full[s], 0);
+          if (it < pre) {  // B and the expected bytes went out before griddep_wait
+            tma_load_2d_pair(sA + static_cast<size_t>(s) * kHalfBytes, &tmA, lead_full,
+                             kb * kPairBK, mt * 256 + static_cast<int>(rank) * 128);
+            continue;
+          }
           if (!mbar_wait(&empty[s], ph ^ 1u, status)) {
             ok = false;
             break;
           }
-          const uint32_t lead_full = cluster_addr(&full[s], 0);
           if (rank == 0) mbar_arrive_expect_tx(&full[s], 4u * kHalfBytes);  // both CTAs' A and B
           tma_load_2d_pair(sA + static_cast<size_t>(s) * kHalfBytes, &tmA, lead_full, kb * kPairBK,
                            mt * 256 + static_cast<int>(rank) * 128);
@@ -631,13 +652,15 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 2;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.pdl ? 2 : 1;
   return check_cuda(cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ta, tb, p, e, device_status()),
                     "gemm_pair_kernel launch");
 }
@@ -777,7 +800,7 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
   }
   CUtensorMap ta, tb;
   if (g_pair_mode && (bn_auto || bn == 256) && !p.convt && p.bh == 0 && p.phases == 1 &&
-      p.taps == 1 && p.win == 0 && !p.pdl && p.kc % kPairBK == 0 && p.M >= 256 && p.N >= 256 &&
+      p.taps == 1 && p.win == 0 && p.kc % kPairBK == 0 && p.M >= 256 && p.N >= 256 &&
       a_cols == 0 && b_cols == 0 && pair_wins(p.M, p.N, p.kc, bn)) {
     p.bk = kPairBK;
     int rc = make_kmajor_map(&ta, a, a_rows, p.kc, lda, 128, kPairBK);
@@ -952,6 +975,7 @@ int gsvk::gemm_ex_run(const gsvk_gemm_args* g, cudaStream_t st, bool static_b) {
   p.convt = 0;
   p.phases = 1;
   p.out_rows = (int)g->M;
+  p.pdl = static_b ? 1 : 0;
   return tc_run(g->a, (long long)g->M, (long long)g->lda, g->b, (long long)g->N,
                 (long long)g->ldb, p, e, 0, st);
 }

@@ -33,8 +33,8 @@ bool skinny_fits(long long M, long long N, long long K, long long ldx, long long
 int skinny_run(const uint16_t* x, int M, long long ldx, const uint16_t* w, int N, long long ldw,
                int K, const TcEpilogue& e, cudaStream_t st, bool pdl, int force_split = 0);
 // The gsvk_gemm_f16_ex dispatch.  static_b: B is registered weights, never
-// written by device work (few-row problems then run as programmatic
-// dependents of the previous kernel, fetching B before that kernel ends).
+// written by device work (the launch is then a programmatic dependent of the
+// previous kernel, whose set-up and first B loads overlap that kernel's end).
 int gemm_ex_run(const gsvk_gemm_args* g, cudaStream_t st, bool static_b);
 // CUDA-core fallback for shapes the TMA path cannot express (K or leading
 // dimensions not multiples of 8, unaligned bases).
