@@ -224,9 +224,16 @@ def _gemm_args(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.
                     0 if c_f16 is None else c_f16.stride(0), act, slope, alpha)
 
 
-def gemm_set_pair(enable: bool):
-    """Two-SM (cta_group::2) GEMM kernel for eligible plain problems."""
-    check(lib().gsvk_gemm_set_pair(int(bool(enable))))
+PAIR_NEVER, PAIR_AUTO, PAIR_ALWAYS = 0, 1, 2
+
+
+def gemm_set_pair(mode):
+    """Two-SM (cta_group::2) GEMM kernel for eligible plain problems: PAIR_AUTO
+    (the default, when its tile rounds cost no more), PAIR_ALWAYS or
+    PAIR_NEVER; True / False mean PAIR_AUTO / PAIR_NEVER."""
+    if mode is True or mode is False:
+        mode = PAIR_AUTO if mode else PAIR_NEVER
+    check(lib().gsvk_gemm_set_pair(int(mode)))
 
 
 def gemm_batched(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, c=None,

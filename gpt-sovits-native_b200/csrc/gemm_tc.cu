@@ -440,19 +440,52 @@ __global__ void __launch_bounds__(kThreads, 1)
 // a cluster of two CTAs computes 256 x 256 output tiles with
 // tcgen05.mma.cta_group::2.  CTA r of the pair stages rows [128r, 128r+128)
 // of the tile's A rows and of its B rows (its half of N): 32 KB per 64-deep
-// K step, so six stages fit where the one-SM 128 x 256 tile fits four, and
-// every A and B byte a pair reads from L2 feeds 256 rows or columns instead
-// of 128.  CTA r holds rows [128r, +128) of the fp32 accumulator (two
-// accumulators of 256 columns: all 512 TMEM columns).  The leader (rank 0)
-// counts both CTAs' copy bytes on its barriers, issues the pair MMAs and
-// commits to both CTAs' barriers; both CTAs run the epilogue of their rows
-// and release an accumulator by arriving on the leader's barrier.
+// K step, and every A and B byte a pair reads from L2 feeds 256 rows or
+// columns instead of 128.  CTA r holds rows [128r, +128) of the fp32
+// accumulator (two accumulators of 256 columns: all 512 TMEM columns).  The
+// leader (rank 0) counts both CTAs' copy bytes on its barriers, issues the
+// pair MMAs and commits to both CTAs' barriers; both CTAs run the epilogue
+// of their rows and release an accumulator by arriving on the leader's
+// barrier.
+//
+// Epilogue (tma_epi != 0): a lane holds one output row, so direct stores
+// touch 32 rows (32 cache lines) per instruction.  Instead each warp writes
+// its 32-row chunk into a 128-byte-row shared-memory tile in the 128-byte
+// swizzle (16-byte unit j of row r at unit j ^ (r & 7): conflict-free) and
+// one lane hands the tile to a TMA bulk store, which also clips the tile at
+// M and N.  Two 4 KB tiles per warp alternate; a tile is rewritten only after
+// the bulk store issued from it has read it.  An fp32 residual arrives the
+// same way, one chunk ahead, into the tile the result then overwrites.
 constexpr int kPairBN = 256;
 constexpr int kPairBK = 64;
-constexpr int kPairStages = 6;
+constexpr int kPairStages = 4;
+constexpr uint32_t kStageTile = 4096;  // 32 rows x 128 bytes
+
+// Bias of 16 output columns starting at n0 (0 past N or without bias).
+__device__ __forceinline__ void bias16(const TcEpilogue& e, int n0, int N, bool vec, float* bb) {
+  if (e.bias && vec && n0 + 16 <= N) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(e.bias + n0 + j));
+      bb[j] = v.x;
+      bb[j + 1] = v.y;
+      bb[j + 2] = v.z;
+      bb[j + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) bb[j] = (e.bias && n0 + j < N) ? __ldg(e.bias + n0 + j) : 0.f;
+  }
+}
+
+// Address of 16-byte unit j of row r in a 1024-byte-aligned swizzled tile.
+__device__ __forceinline__ uint8_t* swz_unit(uint8_t* tile, int r, int j) {
+  return tile + r * 128 + ((j ^ (r & 7)) << 4);
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
                      const TcProblem prob, const TcEpilogue epi, uint32_t* status) {
   const TcProblem p = prob;
   const TcEpilogue e = epi;
@@ -466,11 +499,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kPairStages * kHalfBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kPairStages * kHalfBytes);
+  uint8_t* sOut = sB + kPairStages * kHalfBytes;  // kEpiWarps x 2 staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kEpiWarps * 2 * kStageTile);
   uint64_t* empty = full + kPairStages;
   uint64_t* tfull = empty + kPairStages;
   uint64_t* tempty = tfull + kAcc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kAcc);
+  uint64_t* rbar = tempty + kAcc;  // kEpiWarps x 2: residual tile landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + kEpiWarps * 2);
 
   const uint32_t rank = cluster_rank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -488,9 +523,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * kEpiWarps);  // the epilogue warps of both CTAs
     }
+    for (int w = 0; w < 2 * kEpiWarps; ++w) mbar_init(&rbar[w], 1);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (p.tma_epi) prefetch_tmap(&tmC);
+    if (p.tma_epi == 2 && e.residual) prefetch_tmap(&tmR);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -585,41 +623,169 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;  // column half
     const int cbeg = half * (kPairBN / 2);
     const bool bias_vec = e.bias && aligned16(e.bias);
+    uint8_t* stile = sOut + static_cast<size_t>(warp - 2) * 2 * kStageTile;
+    uint64_t* rb = rbar + (warp - 2) * 2;
+    const bool res_tma = p.tma_epi == 2 && e.residual != nullptr;
+    int cc = 0;        // staging tiles used so far (tile cc & 1 next)
+    uint32_t rph = 0;  // residual barrier parities
     int tl = 0;
     for (int tile = pair; tile < tiles; tile += npairs, ++tl) {
       const int mt = tile / n_tiles, nt = tile - (tile / n_tiles) * n_tiles;
       const int acc = tl & 1;
       const uint32_t aph = static_cast<uint32_t>(tl >> 1) & 1u;
-      const int i = mt * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+      const int row0 = mt * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+      const int i = row0 + lane;
       const bool row_ok = i < p.M;
       const long long orow = i;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * kPairBN);
-      float bnext[16], rnext[16], snext[16];
-      fetch16(e, row_ok, orow, nt * kPairBN + cbeg, p.N, 0, bias_vec, bnext, rnext, snext);
-      if (!mbar_wait(&tfull[acc], aph, status)) break;
-      tc_fence_after();
+      if (p.tma_epi == 0) {
+        float bnext[16], rnext[16], snext[16];
+        fetch16(e, row_ok, orow, nt * kPairBN + cbeg, p.N, 0, bias_vec, bnext, rnext, snext);
+        if (!mbar_wait(&tfull[acc], aph, status)) break;
+        tc_fence_after();
 #pragma unroll 1
-      for (int c0 = cbeg; c0 < cbeg + kPairBN / 2; c0 += 16) {
-        float bcur[16], rcur[16], scur[16];
+        for (int c0 = cbeg; c0 < cbeg + kPairBN / 2; c0 += 16) {
+          float bcur[16], rcur[16], scur[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          bcur[j] = bnext[j];
-          rcur[j] = rnext[j];
-          scur[j] = snext[j];
+          for (int j = 0; j < 16; ++j) {
+            bcur[j] = bnext[j];
+            rcur[j] = rnext[j];
+            scur[j] = snext[j];
+          }
+          if (c0 + 16 < cbeg + kPairBN / 2)
+            fetch16(e, row_ok, orow, nt * kPairBN + c0 + 16, p.N, 0, bias_vec, bnext, rnext, snext);
+          uint32_t r[16];
+          tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
+          tmem_ld_wait();
+          if (row_ok && nt * kPairBN + c0 < p.N)
+            store16(e, orow, nt * kPairBN + c0, p.N, r, 0, bcur, rcur, scur);
         }
-        if (c0 + 16 < cbeg + kPairBN / 2)
-          fetch16(e, row_ok, orow, nt * kPairBN + c0 + 16, p.N, 0, bias_vec, bnext, rnext, snext);
-        uint32_t r[16];
-        tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
-        tmem_ld_wait();
-        if (row_ok && nt * kPairBN + c0 < p.N)
-          store16(e, orow, nt * kPairBN + c0, p.N, r, 0, bcur, rcur, scur);
+      } else if (p.tma_epi == 1) {
+        // fp16 output, 64-column chunks
+        if (!mbar_wait(&tfull[acc], aph, status)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c0 = cbeg; c0 < cbeg + kPairBN / 2; c0 += 64) {
+          const int n0 = nt * kPairBN + c0;
+          if (n0 >= p.N) break;
+          if (e.vt && n0 + 64 > e.vt_c0) {  // V^T columns: scattered per-head stores
+#pragma unroll 1
+            for (int q = 0; q < 4; ++q) {
+              float bb[16], rr[16], ss[16];
+              fetch16(e, row_ok, orow, n0 + 16 * q, p.N, 0, bias_vec, bb, rr, ss);
+              uint32_t r[16];
+              tmem_ld16(t_row + static_cast<uint32_t>(c0 + 16 * q), r);
+              tmem_ld_wait();
+              if (row_ok && n0 + 16 * q < p.N) store16(e, orow, n0 + 16 * q, p.N, r, 0, bb, rr, ss);
+            }
+            continue;
+          }
+          uint8_t* st = stile + (cc & 1) * kStageTile;
+          if (lane == 0) bulk_wait_read<1>();  // the store issued from `st` has read it
+          __syncwarp();
+#pragma unroll 1
+          for (int q = 0; q < 4; ++q) {
+            uint32_t r[16];
+            float v[16], bb[16];
+            tmem_ld16(t_row + static_cast<uint32_t>(c0 + 16 * q), r);
+            bias16(e, n0 + 16 * q, p.N, bias_vec, bb);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = fmaf(__uint_as_float(r[j]), e.alpha, bb[j]);
+            act_array<16>(v, e.act, e.slope);
+            uint32_t pk[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pk[j] = f2h2(v[2 * j], v[2 * j + 1]);
+            *reinterpret_cast<uint4*>(swz_unit(st, lane, 2 * q)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(swz_unit(st, lane, 2 * q + 1)) =
+                make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, st, n0, row0);
+            bulk_commit();
+          }
+          ++cc;
+        }
+      } else {
+        // fp32 output (+ fp32 residual), 32-column chunks
+        const int nfirst = nt * kPairBN + cbeg;
+        if (res_tma && lane == 0 && nfirst < p.N) {
+          bulk_wait_read<1>();  // the store issued from tile cc & 1 has read it
+          mbar_arrive_expect_tx(&rb[cc & 1], kStageTile);
+          tma_load_2d(stile + (cc & 1) * kStageTile, &tmR, &rb[cc & 1], nfirst, row0);
+        }
+        if (!mbar_wait(&tfull[acc], aph, status)) break;
+        tc_fence_after();
+        bool ok = true;
+#pragma unroll 1
+        for (int c0 = cbeg; c0 < cbeg + kPairBN / 2 && ok; c0 += 32) {
+          const int n0 = nt * kPairBN + c0;
+          if (n0 >= p.N) break;
+          const int b = cc & 1;
+          uint8_t* st = stile + b * kStageTile;
+          if (res_tma) {
+            if (lane == 0 && c0 + 32 < cbeg + kPairBN / 2 && n0 + 32 < p.N) {
+              bulk_wait_read<0>();  // the previous chunk's store has read tile b ^ 1
+              mbar_arrive_expect_tx(&rb[b ^ 1], kStageTile);
+              tma_load_2d(stile + (b ^ 1) * kStageTile, &tmR, &rb[b ^ 1], n0 + 32, row0);
+            }
+            const uint32_t par = (rph >> b) & 1u;
+            bool got = true;
+            if (lane == 0) got = mbar_wait(&rb[b], par, status);
+            got = __shfl_sync(0xffffffffu, got, 0) != 0;
+            if (!got) {
+              ok = false;
+              break;
+            }
+            mbar_wait(&rb[b], par, status);  // complete: each lane's own acquire of the tile
+            rph ^= 1u << b;
+          } else {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+          }
+#pragma unroll 1
+          for (int q = 0; q < 2; ++q) {
+            uint32_t r[16];
+            float v[16], bb[16];
+            tmem_ld16(t_row + static_cast<uint32_t>(c0 + 16 * q), r);
+            bias16(e, n0 + 16 * q, p.N, bias_vec, bb);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = fmaf(__uint_as_float(r[j]), e.alpha, bb[j]);
+            act_array<16>(v, e.act, e.slope);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              float4* u = reinterpret_cast<float4*>(swz_unit(st, lane, 4 * q + k));
+              float4 o = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+              if (res_tma) {
+                const float4 rv = *u;
+                o.x = fmaf(e.res_scale, rv.x, o.x);
+                o.y = fmaf(e.res_scale, rv.y, o.y);
+                o.z = fmaf(e.res_scale, rv.z, o.z);
+                o.w = fmaf(e.res_scale, rv.w, o.w);
+              }
+              *u = o;
+            }
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, st, n0, row0);
+            bulk_commit();
+          }
+          ++cc;
+        }
+        if (!ok) break;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
     }
+    if (lane == 0) bulk_wait<0>();  // every bulk store of this warp written
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -630,10 +796,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
-                const TcEpilogue& e, cudaStream_t st) {
-  const size_t smem = 1024 + static_cast<size_t>(kPairStages) * 2 * 128 * kPairBK * 2 +
-                      (2 * kPairStages + 4) * 8 + 16;
+size_t pair_smem_bytes() {
+  return 1024 + static_cast<size_t>(kPairStages) * 2 * 128 * kPairBK * 2 +
+         static_cast<size_t>(kEpiWarps) * 2 * kStageTile +
+         (2 * kPairStages + 4 + 2 * kEpiWarps) * 8 + 16;
+}
+
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                const CUtensorMap& tr, const TcProblem& p, const TcEpilogue& e, cudaStream_t st) {
+  const size_t smem = pair_smem_bytes();
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -661,7 +832,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = p.pdl ? 2 : 1;
-  return check_cuda(cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ta, tb, p, e, device_status()),
+  return check_cuda(cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ta, tb, tc, tr, p, e, device_status()),
                     "gemm_pair_kernel launch");
 }
 
@@ -759,7 +930,9 @@ int tc_pick_bn(long long M, long long N) {
   return (m_tiles * ((N + 255) / 256) >= sm_count()) ? 256 : 128;
 }
 
-static int g_pair_mode = 1;  // two-SM GEMM for eligible plain problems (gsvk_gemm_set_pair)
+// Two-SM GEMM for eligible plain problems (gsvk_gemm_set_pair): 0 never,
+// 1 when pair_wins, 2 always.
+static int g_pair_mode = 1;
 
 // Whether the two-SM kernel beats the one-SM kernel with BN-wide tiles.  Both
 // are bound by each SM's L2 ingest (~64 B/clk) rather than by the tensor pipe:
@@ -801,12 +974,40 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
   CUtensorMap ta, tb;
   if (g_pair_mode && (bn_auto || bn == 256) && !p.convt && p.bh == 0 && p.phases == 1 &&
       p.taps == 1 && p.win == 0 && p.kc % kPairBK == 0 && p.M >= 256 && p.N >= 256 &&
-      a_cols == 0 && b_cols == 0 && pair_wins(p.M, p.N, p.kc, bn)) {
+      a_cols == 0 && b_cols == 0 && (g_pair_mode == 2 || pair_wins(p.M, p.N, p.kc, bn))) {
     p.bk = kPairBK;
     int rc = make_kmajor_map(&ta, a, a_rows, p.kc, lda, 128, kPairBK);
     if (!rc) rc = make_kmajor_map(&tb, b, b_rows, p.kc, ldb, 128, kPairBK);
     if (rc) return rc;
-    return launch_pair(ta, tb, p, e, st);
+    // bulk-copy epilogue for a single fp16 or fp32 output (32-row tiles of
+    // 128-byte rows: 64 fp16 or 32 fp32 columns)
+    CUtensorMap tc{}, tr{};
+    p.tma_epi = 0;
+    const uint64_t odims[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M)};
+    if (e.c16 && !e.c32 && !e.c16_act && !e.mean_sum && !e.residual && aligned16(e.c16) &&
+        e.ld_c16 % 8 == 0) {
+      const uint64_t str[1] = {static_cast<uint64_t>(e.ld_c16) * 2};
+      const uint32_t box[2] = {64, 32};
+      rc = encode_tiled(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e.c16, odims, str, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      p.tma_epi = 1;
+    } else if (e.c32 && !e.c16 && !e.c16_act && !e.mean_sum && !e.vt && aligned16(e.c32) &&
+               e.ld_c32 % 4 == 0 &&
+               (!e.residual || (aligned16(e.residual) && e.ld_res % 4 == 0))) {
+      const uint32_t box[2] = {32, 32};
+      const uint64_t str[1] = {static_cast<uint64_t>(e.ld_c32) * 4};
+      rc = encode_tiled(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, e.c32, odims, str, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+      if (!rc && e.residual) {
+        const uint64_t rstr[1] = {static_cast<uint64_t>(e.ld_res) * 4};
+        rc = encode_tiled(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(e.residual),
+                          odims, rstr, box, CU_TENSOR_MAP_SWIZZLE_128B);
+      }
+      if (rc) return rc;
+      p.tma_epi = 2;
+    }
+    return launch_pair(ta, tb, tc, tr, p, e, st);
   }
   int rc = make_kmajor_map(&ta, a, a_rows, a_cols ? a_cols : p.kc, lda, p.win ? p.win : kBM, p.bk);
   if (rc) return rc;
@@ -863,8 +1064,9 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   return gemm_ex_run(g, as_cuda(stream), false);
 }
 
-int gsvk_gemm_set_pair(int enable) {
-  g_pair_mode = enable != 0;
+int gsvk_gemm_set_pair(int mode) {
+  if (mode < 0 || mode > 2) return gsvk::fail(GSVK_ERR_INVALID, "gemm_set_pair: mode %d", mode);
+  g_pair_mode = mode;
   return GSVK_OK;
 }
 

@@ -90,6 +90,10 @@ struct TcProblem {
   // loads overlap that kernel's tail, so B must not be written by the
   // kernels this launch waits on.
   int pdl;
+  // Two-SM kernel only: 0 = per-lane row stores; 1 = the fp16 output (c16)
+  // and 2 = the fp32 output (c32, its fp32 residual loaded the same way) go
+  // through swizzled shared-memory tiles and TMA bulk copies.
+  int tma_epi;
 };
 
 }  // namespace gsvk

@@ -98,6 +98,31 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// 2D tiled store this CTA's shared memory -> global (rows and columns outside
+// the tensor map's extent are not written), tracked in this thread's bulk
+// async-group.  c0 = innermost coordinate (elements), c1 = row; c0 times the
+// element size must be a multiple of 16 bytes and neither may be negative.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Until at most N of this thread's committed bulk groups still read their
+// shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Until at most N of this thread's committed bulk groups are incomplete
+// (their global writes done).
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (tcgen05.mma operands, bulk copies) of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_shared() {

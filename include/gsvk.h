@@ -111,12 +111,12 @@ typedef struct {
   float alpha;                       /* 0 is read as 1 */
 } gsvk_gemm_args;
 int gsvk_gemm_f16_ex(const gsvk_gemm_args* args, gsvk_stream_t stream);
-/* enable != 0 (the default): plain GEMMs with M, N >= 256 and K a multiple
- * of 64 (here and in the engines built on this library) run on the two-SM
- * kernel (256 x 256 tiles over a CTA pair, tcgen05.mma.cta_group::2) when
- * its tile rounds cost no more than the one-SM kernel's; 0: always the
- * one-SM kernel.  Process-wide. */
-int gsvk_gemm_set_pair(int enable);
+/* Plain GEMMs with M, N >= 256 and K a multiple of 64 (here and in the
+ * engines built on this library) may run on the two-SM kernel (256 x 256
+ * tiles over a CTA pair, tcgen05.mma.cta_group::2).  mode 1 (the default):
+ * when its tile rounds cost no more than the one-SM kernel's; 2: always;
+ * 0: never.  Process-wide; GSVK_ERR_INVALID for another mode. */
+int gsvk_gemm_set_pair(int mode);
 
 /* Strided batched GEMM: `batch` independent problems of one shape and one
  * epilogue, problem i reading A at args->a + i*stride_a and B at

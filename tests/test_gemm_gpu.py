@@ -267,18 +267,63 @@ def test_gemm_pair_kernel_matches_one_sm(dev, ora, M, N, K):
     res = f(rng.standard_normal((M, N)).astype(np.float32))
     out = {}
     try:
-        for pair in (False, True):
-            dev.gemm_set_pair(pair)
+        for mode in (dev.PAIR_NEVER, dev.PAIR_ALWAYS):
+            dev.gemm_set_pair(mode)
             c = torch.empty(M, N, device="cuda")
             c16 = torch.empty(M, N, dtype=torch.float16, device="cuda")
             dev.gemm_ex(a, w, bias=bias, residual=res, act=dev.ACT_GELU_ERF, c=c, c_f16=c16)
-            out[pair] = (c.cpu().numpy(), c16.cpu().numpy())
+            out[mode] = (c.cpu().numpy(), c16.cpu().numpy())
     finally:
-        dev.gemm_set_pair(True)
+        dev.gemm_set_pair(dev.PAIR_AUTO)
     ref = ora.linear_f16(ora.f16_to_f32(a.cpu().numpy().view(np.uint16)), w.cpu().numpy().view(np.uint16),
                          bias.cpu().numpy(), dev.ACT_GELU_ERF, 0.0) + res.cpu().numpy()
-    for pair in (False, True):
-        c, c16 = out[pair]
-        assert np.abs(c - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max()), f"pair={pair}"
+    for mode, (c, c16) in out.items():
+        assert np.abs(c - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max()), f"mode={mode}"
         np.testing.assert_array_equal(c16, c.astype(np.float16))
     assert dev.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 520, 128), (517, 2304, 768), (1000, 776, 256), (260, 1002, 64)])
+def test_gemm_pair_bulk_copy_epilogue(dev, ora, M, N, K):
+    """A single fp16 output (bias + GELU) or a single fp32 output (bias +
+    residual, alpha) leaves the two-SM kernel through swizzled shared-memory
+    tiles and TMA bulk stores, which clip at M and N.  Those outputs are
+    bit-identical to the same kernel's per-lane stores (taken when both
+    outputs are requested) and within the GEMM tolerance of the oracle.
+    N = 1002 has row pitches that are not 16-byte multiples: per-lane stores."""
+    rng = np.random.default_rng(3 * M + N + K)
+    a = h(rand16(rng, (M, K), 1.0))
+    w = h(rand16(rng, (N, K), 0.05))
+    bias = f(rng.standard_normal(N).astype(np.float32) * 0.1)
+    res = f(rng.standard_normal((M, N)).astype(np.float32))
+    a_np = ora.f16_to_f32(a.cpu().numpy().view(np.uint16))
+    w_np = w.cpu().numpy().view(np.uint16)
+    dev.gemm_set_pair(dev.PAIR_ALWAYS)
+    try:
+        # fp16 output alone vs both outputs
+        c16 = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        dev.gemm_ex(a, w, bias=bias, act=dev.ACT_GELU_ERF, c_f16=c16)
+        both32 = torch.empty(M, N, device="cuda")
+        both16 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        dev.gemm_ex(a, w, bias=bias, act=dev.ACT_GELU_ERF, c=both32, c_f16=both16)
+        # fp32 output alone (+ residual, alpha) vs both outputs
+        c32 = torch.full((M, N), float("nan"), device="cuda")
+        dev.gemm_ex(a, w, bias=bias, residual=res, alpha=0.5, c=c32)
+        r32 = torch.empty(M, N, device="cuda")
+        r16 = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        dev.gemm_ex(a, w, bias=bias, residual=res, alpha=0.5, c=r32, c_f16=r16)
+        # fp32 output alone, no residual
+        p32 = torch.full((M, N), float("nan"), device="cuda")
+        dev.gemm_ex(a, w, c=p32)
+        torch.cuda.synchronize()
+    finally:
+        dev.gemm_set_pair(dev.PAIR_AUTO)
+    assert dev.device_status() == 0
+    np.testing.assert_array_equal(c16.cpu().numpy(), both16.cpu().numpy())
+    np.testing.assert_array_equal(c32.cpu().numpy(), r32.cpu().numpy())
+    gelu = ora.linear_f16(a_np, w_np, bias.cpu().numpy(), dev.ACT_GELU_ERF, 0.0)
+    assert np.abs(c16.cpu().numpy().astype(np.float32) - gelu).max() <= 1e-2 * max(1.0, np.abs(gelu).max())
+    lin = ora.linear_f16(a_np, w_np, None, dev.ACT_NONE, 0.0)
+    ref = 0.5 * lin + bias.cpu().numpy() + res.cpu().numpy()
+    assert np.abs(c32.cpu().numpy() - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max())
+    assert np.abs(p32.cpu().numpy() - lin).max() <= 1e-4 * max(1.0, np.abs(lin).max())
