@@ -126,6 +126,20 @@ def test_softmax_golden(dev, golden):
     np.testing.assert_allclose(got.astype(np.float64).sum(-1), 1.0, atol=1e-6)
 
 
+def test_gelu_dense_grid_vs_exact(dev):
+    """The device GELU over [-9, 9] against the exact x Phi(x) (fp64):
+    within 6e-7 absolute and 6e-6 relative where |GELU| > 1e-6 (the fp32 fit
+    is within 3.9e-7 and 2.4e-6; ex2.approx adds at most 2^-22 relative)."""
+    from scipy.special import ndtr
+    x = np.linspace(-9, 9, 200_001).astype(np.float32)
+    got = dev.activation(dev_f32(x), 2).cpu().numpy().astype(np.float64)
+    ref = x.astype(np.float64) * ndtr(x.astype(np.float64))
+    err = np.abs(got - ref)
+    assert err.max() <= 6e-7
+    big = np.abs(ref) > 1e-6
+    assert (err[big] / np.abs(ref[big])).max() <= 6e-6
+
+
 def test_activations(dev, ora, golden):
     v = golden["act_v"]
     assert np.array_equal(dev.activation(dev_f32(v), 1).cpu().numpy(), golden["act_relu"])
