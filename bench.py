@@ -395,7 +395,9 @@ def run_gemm_shape(args, rank, local, world):
             "config": {"workload": "gemm", "shape": [M, N, K], "iters_per_step": iters,
                        "launch": "CUDA graph", "l2": f"{copies} rotated operand copies"},
             "gpu_launches": iters * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel", "achieved": achieved, "peak": tf,
+            "roofline": {"bound": "tensor",
+                         "kernel": "gemm_pair_kernel" if g.gemm_uses_pair(M, N, K) else "gemm_tc_kernel",
+                         "achieved": achieved, "peak": tf,
                          "unit": "TFLOP/s", "frac": achieved / tf, "peak_source": kind, "traffic": None}}
     if clk:
         line["clocks"] = clk

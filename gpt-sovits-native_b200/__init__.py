@@ -47,6 +47,7 @@ SIGNATURES = {
     "gsvk_gemm_grouped_f16": (c_int, [_vp, _sz, _vp]),
     "gsvk_gemm_f16_batched": (c_int, [_vp, _sz, _sz, _sz, _sz, _vp]),
     "gsvk_gemm_set_pair": (c_int, [c_int]),
+    "gsvk_gemm_uses_pair": (c_int, [c_size_t, c_size_t, c_size_t]),
     "gsvk_weights_register": (c_int, [_vp, _sz, _sz, _vp]),
     "gsvk_weights_release": (c_int, [_vp]),
     "gsvk_weights_data": (_vp, [_vp]),
@@ -234,6 +235,11 @@ def gemm_set_pair(mode):
     if mode is True or mode is False:
         mode = PAIR_AUTO if mode else PAIR_NEVER
     check(lib().gsvk_gemm_set_pair(int(mode)))
+
+
+def gemm_uses_pair(M: int, N: int, K: int) -> bool:
+    """Whether an M x N x K gemm_ex call runs on the two-SM kernel."""
+    return bool(lib().gsvk_gemm_uses_pair(int(M), int(N), int(K)))
 
 
 def gemm_batched(a, b, bias=None, residual=None, act=ACT_NONE, slope=0.0, alpha=1.0, c=None,

@@ -1064,6 +1064,21 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* g, gsvk_stream_t stream) {
   return gemm_ex_run(g, as_cuda(stream), false);
 }
 
+int gsvk_gemm_uses_pair(size_t M, size_t N, size_t K) {
+  if (M == 0 || N == 0 || K == 0 || M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff || K % 8)
+    return 0;
+  const void* aligned = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+  if (gsvk::skinny_fits((long long)M, (long long)N, (long long)K, (long long)K, (long long)K,
+                        aligned, aligned))
+    return 0;  // few rows: the split-K kernel
+  if (!g_pair_mode || K % gsvk::kPairBK != 0 || M < 256 || N < 256) return 0;
+  return (g_pair_mode == 2 ||
+          gsvk::pair_wins((long long)M, (long long)N, (long long)K,
+                          gsvk::tc_pick_bn((long long)M, (long long)N)))
+             ? 1
+             : 0;
+}
+
 int gsvk_gemm_set_pair(int mode) {
   if (mode < 0 || mode > 2) return gsvk::fail(GSVK_ERR_INVALID, "gemm_set_pair: mode %d", mode);
   g_pair_mode = mode;

@@ -117,6 +117,10 @@ int gsvk_gemm_f16_ex(const gsvk_gemm_args* args, gsvk_stream_t stream);
  * when its tile rounds cost no more than the one-SM kernel's; 2: always;
  * 0: never.  Process-wide; GSVK_ERR_INVALID for another mode. */
 int gsvk_gemm_set_pair(int mode);
+/* 1 if gsvk_gemm_f16_ex of an M x N x K problem (16-byte aligned operands,
+ * leading dimensions K) runs on the two-SM kernel under the current mode,
+ * 0 otherwise.  A query only: launches nothing. */
+int gsvk_gemm_uses_pair(size_t M, size_t N, size_t K);
 
 /* Strided batched GEMM: `batch` independent problems of one shape and one
  * epilogue, problem i reading A at args->a + i*stride_a and B at

@@ -327,3 +327,20 @@ def test_gemm_pair_bulk_copy_epilogue(dev, ora, M, N, K):
     ref = 0.5 * lin + bias.cpu().numpy() + res.cpu().numpy()
     assert np.abs(c32.cpu().numpy() - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max())
     assert np.abs(p32.cpu().numpy() - lin).max() <= 1e-4 * max(1.0, np.abs(lin).max())
+
+
+def test_gemm_uses_pair_follows_the_mode(dev):
+    """The kernel query: encoder-sized problems take the two-SM kernel under
+    the default rule, few-row and short problems do not; the mode switch
+    forces either way (the query launches nothing)."""
+    try:
+        assert dev.gemm_uses_pair(4096, 1024, 4096) and dev.gemm_uses_pair(8000, 3072, 768)
+        assert not dev.gemm_uses_pair(2048, 1024, 1024)  # tile rounds tie, short K
+        assert not dev.gemm_uses_pair(64, 4096, 1024)    # few rows: split-K kernel
+        assert not dev.gemm_uses_pair(4096, 4096, 1000)  # K not a multiple of 64
+        dev.gemm_set_pair(dev.PAIR_ALWAYS)
+        assert dev.gemm_uses_pair(2048, 1024, 1024)
+        dev.gemm_set_pair(dev.PAIR_NEVER)
+        assert not dev.gemm_uses_pair(4096, 1024, 4096)
+    finally:
+        dev.gemm_set_pair(dev.PAIR_AUTO)
