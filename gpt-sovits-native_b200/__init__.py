@@ -105,6 +105,8 @@ SIGNATURES = {
     "gsvk_t2s_batch_read": (c_int, [_vp, c_int, _vp, _vp]),
     "gsvk_t2s_batch_read_logits": (c_int, [_vp, _vp]),
     "gsvk_t2s_batch_launches_per_step": (c_int, [_vp]),
+    "gsvk_t2s_batch_set_attention": (c_int, [c_void_p, c_int]),
+    "gsvk_t2s_batch_attention": (c_int, [c_void_p]),
     "gsvk_layernorm_rows": (c_int, [_vp, _vp, _vp, _vp, _sz, _sz, c_double, _vp]),
     "gsvk_softmax_rows": (c_int, [_vp, _vp, _sz, _sz, _vp]),
     "gsvk_activation": (c_int, [_vp, _vp, _sz, c_int, c_float, _vp]),
@@ -751,6 +753,15 @@ class T2SBatch:
         marg = np.zeros((steps, self.B), np.float32)
         check(lib().gsvk_t2s_batch_read(self.h, steps, toks.ctypes.data, marg.ctypes.data))
         return toks, marg
+
+    ATTN_CHUNK, ATTN_STREAM = 0, 1
+
+    def set_attention(self, kind: int):
+        """Attention kernel of the step (ATTN_CHUNK / ATTN_STREAM)."""
+        check(lib().gsvk_t2s_batch_set_attention(self.h, int(kind)))
+
+    def attention(self) -> int:
+        return lib().gsvk_t2s_batch_attention(self.h)
 
     def read_logits(self):
         import numpy as np

@@ -675,6 +675,7 @@ struct T2SBatchEngine {
   unsigned* ticket = nullptr;  // [B] attention merge tickets (zero between launches)
   int* attn_work = nullptr;    // [L] streaming attention work counters (zeroed per step)
   bool attn_stream = false;    // the streaming attention kernel (d_model <= 512)
+  int attn_kind = 0;           // 0 per-chunk CTAs, 1 streaming CTAs
   float* part_o = nullptr;     // [B][max_chunks][D] per-chunk attention outputs
   float2* part_ml = nullptr;   // [B][max_chunks][H] per-chunk (max, sum)
   int max_chunks = 0;
@@ -727,7 +728,7 @@ int batch_step(T2SBatchEngine* e, int B, cudaStream_t st, int* launches) {
     if ((rc = gemm_m(e->x16, B, D, m.wqkv + (size_t)l * 3 * D * D, 3 * D,
                      m.bqkv + (size_t)l * 3 * D, GSVK_ACT_NONE, nullptr, e->qkv32, nullptr, st)))
       return rc;
-    if (e->attn_stream) {
+    if (e->attn_kind == 1) {
       auto* fn = D == 512 ? batch_attn_stream_kernel<2> : batch_attn_stream_kernel<1>;
       if ((rc = launch_pdl(fn, dim3(2 * sm_count()), dim3(kAttnThreads),
                            attn_stream_smem_bytes(D, m.H, m.B), st, "batch_attn_stream_kernel", m,
@@ -920,6 +921,7 @@ int gsvk_t2s_batch_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weight
   e->max_chunks = max_chunks;
   e->attn_work = reinterpret_cast<int*>(a + o_wk);
   e->attn_stream = D == 256 || D == 512;
+  e->attn_kind = e->attn_stream ? 1 : 0;
   if (e->attn_stream) {
     if (int rc = check_cuda(cudaFuncSetAttribute(D == 512 ? batch_attn_stream_kernel<2>
                                                           : batch_attn_stream_kernel<1>,
@@ -1068,5 +1070,22 @@ int gsvk_t2s_batch_read_logits(gsvk_t2s_batch_t h, float* host_out) {
 }
 
 int gsvk_t2s_batch_launches_per_step(gsvk_t2s_batch_t h) { return h ? h->launches_per_step : 0; }
+
+int gsvk_t2s_batch_set_attention(gsvk_t2s_batch_t h, int kind) {
+  if (!h) return fail(GSVK_ERR_INVALID, "t2s_batch_set_attention: null handle");
+  if (kind < 0 || kind > 1 || (kind == 1 && !h->attn_stream))
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s_batch_set_attention: kernel %d not available for this model",
+                kind);
+  if (kind != h->attn_kind) {  // the captured step holds the previous kernel
+    if (h->exec) cudaGraphExecDestroy(h->exec);
+    if (h->graph) cudaGraphDestroy(h->graph);
+    h->exec = nullptr;
+    h->graph = nullptr;
+    h->attn_kind = kind;
+  }
+  return GSVK_OK;
+}
+
+int gsvk_t2s_batch_attention(gsvk_t2s_batch_t h) { return h ? h->attn_kind : -1; }
 
 }  // extern "C"

@@ -411,6 +411,13 @@ int gsvk_t2s_batch_run(gsvk_t2s_batch_t h, int steps, int use_graph, gsvk_stream
 int gsvk_t2s_batch_read(gsvk_t2s_batch_t h, int steps, int32_t* tokens, float* margins);
 int gsvk_t2s_batch_read_logits(gsvk_t2s_batch_t h, float* host_out);
 int gsvk_t2s_batch_launches_per_step(gsvk_t2s_batch_t h);
+/* Attention kernel of the batched step: 0 = one CTA per (utterance, 32-key
+ * chunk), any supported d_model; 1 = persistent CTAs streaming 16-key chunks
+ * of 128-key splits (d_model 256 / 512, the default there).  Both agree at
+ * the batched path's GEMM tolerance.  Changing it drops the captured step
+ * graph.  GSVK_ERR_UNSUPPORTED for a kernel the model cannot use. */
+int gsvk_t2s_batch_set_attention(gsvk_t2s_batch_t h, int kind);
+int gsvk_t2s_batch_attention(gsvk_t2s_batch_t h);
 
 /* The logits the last step sampled from (raw, before the penalty); synchronous. */
 int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out);

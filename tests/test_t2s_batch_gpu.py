@@ -13,11 +13,14 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _setup(dev, n_layers, B, seed):
+def _setup(dev, n_layers, B, seed, d_model=512, lens=None):
     W = dev.workloads
-    m = W.t2s_model(n_layers=n_layers, seed=seed)
+    m = W.t2s_model(n_layers=n_layers, d_model=d_model, n_heads=d_model // 32, ffn=4 * d_model,
+                    seed=seed)
     rng = np.random.default_rng(seed + 7)
-    lens = rng.integers(10, 200, size=B).astype(np.int32)
+    if lens is None:
+        lens = rng.integers(10, 200, size=B)
+    lens = np.asarray(lens, np.int32)
     pe0 = lens.copy()
     first = rng.integers(0, m["vocab"] - 1, size=B).astype(np.int32)
     hist = np.stack([np.concatenate([[first[b]], rng.integers(0, 1024, size=7)])
@@ -37,25 +40,63 @@ def _oracle_embed(ora, m, tok, pe_idx):
     return (np.float32(m["alpha_audio"]) * pe + e).astype(np.float32)
 
 
-def test_batched_step_logits_match_oracle(dev, ora):
-    B, L = 8, 3
-    m, lens, pe0, first, hist, cap, caches = _setup(dev, L, B, seed=21)
+def _check_steps_vs_oracle(dev, ora, m, L, lens, pe0, first, hist, cap, caches, kind, steps):
+    """`steps` eager steps with attention kernel `kind`; the last step's logits
+    against the oracle's per-utterance decode (which appends the same rows)."""
+    B = len(lens)
     eng = dev.T2SBatch(m, cap=cap, max_batch=B, max_steps=8)
+    eng.set_attention(kind)
+    assert eng.attention() == kind
     for b in range(B):
         eng.load_kv(b, caches[b][0], caches[b][1], int(lens[b]))
     eng.begin(lens, pe0, first, hist)
-    eng.run(1, use_graph=False)
+    eng.run(steps, use_graph=False)
+    toks, _ = eng.read(steps)
     got = eng.read_logits()
     eng.close()
+    assert dev.device_status() == 0
     for b in range(B):
-        x = _oracle_embed(ora, m, first[b], pe0[b])
         kc, vc = caches[b][0].copy(), caches[b][1].copy()
-        for layer in range(L):
-            ora.t2s_decode_layer(m, layer, x, int(lens[b]), kc[layer], vc[layer])
+        tok = int(first[b])
+        for s in range(steps):
+            x = _oracle_embed(ora, m, tok, pe0[b] + s)
+            for layer in range(L):
+                ora.t2s_decode_layer(m, layer, x, int(lens[b]) + s, kc[layer], vc[layer])
+            tok = int(toks[s, b])  # follow the batched stream (its tokens are checked elsewhere)
         ref = _oracle_logits(ora, m, x)
         d = np.abs(got[b] - ref).max() / np.abs(ref).max()
         c = float(got[b].astype(np.float64) @ ref / np.linalg.norm(got[b]) / np.linalg.norm(ref))
-        assert d <= 1e-2 and c >= 0.9999, f"utterance {b}: max rel {d:.3e} cos {c:.8f}"
+        assert d <= 1e-2 and c >= 0.9999, f"kind {kind} utterance {b}: max rel {d:.3e} cos {c:.8f}"
+
+
+@pytest.mark.parametrize("d_model,kind", [(512, 0), (512, 1), (256, 0), (256, 1)])
+def test_batched_step_logits_match_oracle(dev, ora, d_model, kind):
+    """Both attention kernels of the batched step (per-chunk CTAs, streaming
+    CTAs) at both streaming model widths."""
+    B, L = 8, 3
+    m, lens, pe0, first, hist, cap, caches = _setup(dev, L, B, seed=21, d_model=d_model)
+    _check_steps_vs_oracle(dev, ora, m, L, lens, pe0, first, hist, cap, caches, kind, 1)
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_batched_attention_ragged_lengths(dev, ora, kind):
+    """Cache lengths at the kernels' chunk and split edges (one key, one
+    32-key chunk, exact multiples, one key past them) over two steps, so the
+    second step also reads the K/V rows the first step appended."""
+    L = 2
+    m, lens, pe0, first, hist, cap, caches = _setup(dev, L, 8, seed=33,
+                                                    lens=[1, 3, 31, 32, 63, 64, 127, 129])
+    _check_steps_vs_oracle(dev, ora, m, L, lens, pe0, first, hist, cap, caches, kind, 2)
+
+
+def test_batched_attention_rejects_unavailable_kernels(dev):
+    m = dev.workloads.t2s_model(n_layers=1, d_model=1024, n_heads=16, ffn=4096, seed=2)
+    eng = dev.T2SBatch(m, cap=64, max_batch=2, max_steps=2)
+    assert eng.attention() == 0  # d_model 1024: the per-chunk kernel only
+    for kind in (1, 2):
+        with pytest.raises(dev.GsvkError):
+            eng.set_attention(kind)
+    eng.close()
 
 
 def test_batched_streams_match_oracle_until_a_near_tie(dev, ora):
