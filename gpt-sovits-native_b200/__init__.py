@@ -48,6 +48,7 @@ SIGNATURES = {
     "gsvk_gemm_f16_batched": (c_int, [_vp, _sz, _sz, _sz, _sz, _vp]),
     "gsvk_gemm_set_pair": (c_int, [c_int]),
     "gsvk_gemm_uses_pair": (c_int, [c_size_t, c_size_t, c_size_t]),
+    "gsvk_gemm_set_bulk_epilogue": (c_int, [c_int]),
     "gsvk_weights_register": (c_int, [_vp, _sz, _sz, _vp]),
     "gsvk_weights_release": (c_int, [_vp]),
     "gsvk_weights_data": (_vp, [_vp]),
@@ -237,6 +238,12 @@ def gemm_set_pair(mode):
     if mode is True or mode is False:
         mode = PAIR_AUTO if mode else PAIR_NEVER
     check(lib().gsvk_gemm_set_pair(int(mode)))
+
+
+def gemm_set_bulk_epilogue(enable: bool):
+    """One-SM kernel: bulk-copy epilogue where possible (default) or per-row
+    stores everywhere (identical results)."""
+    check(lib().gsvk_gemm_set_bulk_epilogue(int(bool(enable))))
 
 
 def gemm_uses_pair(M: int, N: int, K: int) -> bool:

@@ -193,10 +193,28 @@ __device__ __forceinline__ void store16(const TcEpilogue& e, long long orow, int
   }
 }
 
+// Bulk-copy epilogue of the one-SM kernel: per epilogue warp two 4 KB
+// buffers, each [fp32 32 x 16 | fp16 32 x 16 | activated fp16 32 x 16]; the
+// fp32 tile has 64-byte rows in the 64-byte swizzle (16-byte unit j of row r
+// at j ^ ((r >> 1) & 3)), the fp16 tiles 32-byte rows in the 32-byte swizzle
+// (unit j at j ^ ((r >> 2) & 1)): a lane writing its own row hits eight
+// distinct bank groups per eight lanes.
+constexpr uint32_t kBulkBuf = 4096;
+constexpr size_t kBulkStgBytes = static_cast<size_t>(kEpiWarps) * 2 * kBulkBuf;
+__device__ __forceinline__ uint8_t* sw64_unit(uint8_t* t, int r, int j) {
+  return t + r * 64 + ((j ^ ((r >> 1) & 3)) << 4);
+}
+__device__ __forceinline__ uint8_t* sw32_unit(uint8_t* t, int r, int j) {
+  return t + r * 32 + ((j ^ ((r >> 2) & 1)) << 4);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const TcProblem prob, const TcEpilogue epi, int stages, uint32_t* status) {
+                   const __grid_constant__ CUtensorMap tmO32, const __grid_constant__ CUtensorMap tmO16,
+                   const __grid_constant__ CUtensorMap tmO16a,
+                   const __grid_constant__ CUtensorMap tmMean, const TcProblem prob,
+                   const TcEpilogue epi, int stages, uint32_t* status) {
   // Register copies of the parameter structs (see gemm_skinny.cu: references
   // into parameter space are re-read after every global store).
   const TcProblem p = prob;
@@ -234,6 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + kAcc;
   uint64_t* bbar = tempty + kAcc;  // window mode: all taps' weights landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bbar + 1);
+  uint8_t* bulk_stg = reinterpret_cast<uint8_t*>(  // bulk-copy epilogue buffers, 1 KB aligned
+      (reinterpret_cast<uintptr_t>(bbar + 2) + 1023) & ~static_cast<uintptr_t>(1023));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (p.M + kBM - 1) / kBM, n_tiles = (p.N + BN - 1) / BN;
@@ -253,6 +273,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (p.bulk_epi) {
+      if (e.c32) prefetch_tmap(&tmO32);
+      if (e.c16) prefetch_tmap(&tmO16);
+      if (e.c16_act) prefetch_tmap(&tmO16a);
+      if (e.mean_sum) prefetch_tmap(&tmMean);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -386,6 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cbeg = kGroups == 2 ? 0 : half * cw;
     const bool cols_ok = true;
     const bool bias_vec = e.bias && aligned16(e.bias);
+    int bulk_n = 0;  // bulk-copy epilogue chunks issued by this warp
     int tl = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tl) {
       if (kGroups == 2 && (tl & 1) != half) continue;  // the other group's tile
@@ -405,6 +432,82 @@ __global__ void __launch_bounds__(kThreads, 1)
       fetch16(e, row_ok, orow, nt * BN + cbeg, p.N, tp.c_col0, bias_vec, bnext, rnext, snext);
       if (!mbar_wait(&tfull[acc], aph, status)) break;
       tc_fence_after();
+      if (p.bulk_epi) {
+        // bulk-copy epilogue: the per-row arithmetic of store16, results staged
+        // in this warp's swizzled tiles, one bulk group per 16-column chunk
+        const int row0 = mt * kBM + quarter * 32;
+#pragma unroll 1
+        for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
+          if (nt * BN + c0 >= p.N) break;
+          float bcur[16], rcur[16], scur[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            bcur[j] = bnext[j];
+            rcur[j] = rnext[j];
+            scur[j] = snext[j];
+          }
+          if (c0 + 16 < cbeg + cw)
+            fetch16(e, row_ok, orow, nt * BN + c0 + 16, p.N, tp.c_col0, bias_vec, bnext, rnext,
+                    snext);
+          uint32_t r[16];
+          tmem_ld16(t_row + static_cast<uint32_t>(c0), r);
+          uint8_t* buf = bulk_stg + (static_cast<size_t>(warp - 2) * 2 + (bulk_n & 1)) * kBulkBuf;
+          if (lane == 0) bulk_wait_read<1>();  // the store issued from `buf` has read it
+          __syncwarp();
+          tmem_ld_wait();
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = fmaf(__uint_as_float(r[j]), e.alpha, bcur[j]);
+          act_array<16>(v, e.act, e.slope);
+          if (e.residual) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = fmaf(e.res_scale, rcur[j], v[j]);
+          }
+          if (e.mean_sum) {  // running mean: rounded multiply, then rounded add (no contraction)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float t = __fmul_rn(v[j], e.mean_scale);
+              v[j] = e.mean_first ? t : __fadd_rn(scur[j], t);
+            }
+          }
+          if (e.c32 || e.mean_sum) {  // one fp32 tile serves both (the same values)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              *reinterpret_cast<float4*>(sw64_unit(buf, lane, k)) =
+                  make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          }
+          if (e.c16) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pk[j] = f2h2(v[2 * j], v[2 * j + 1]);
+            *reinterpret_cast<uint4*>(sw32_unit(buf + 2048, lane, 0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(sw32_unit(buf + 2048, lane, 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+          if (e.c16_act) {
+            act_array<16>(v, e.act2, e.slope2);
+            uint32_t pk[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pk[j] = f2h2(v[2 * j], v[2 * j + 1]);
+            *reinterpret_cast<uint4*>(sw32_unit(buf + 3072, lane, 0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(sw32_unit(buf + 3072, lane, 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            const int x = nt * BN + c0;
+            if (e.mean_sum) tma_store_2d(&tmMean, buf, x, row0);
+            if (e.c32) tma_store_2d(&tmO32, buf, x, row0);
+            if (e.c16) tma_store_2d(&tmO16, buf + 2048, x, row0);
+            if (e.c16_act) tma_store_2d(&tmO16a, buf + 3072, x, row0);
+            bulk_commit();
+          }
+          ++bulk_n;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int c0 = cbeg; c0 < cbeg + cw && cols_ok; c0 += 16) {
         float bcur[16], rcur[16], scur[16];
@@ -427,6 +530,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (p.bulk_epi && lane == 0) bulk_wait<0>();  // every bulk store of this warp written
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -837,27 +942,31 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 }
 
 template <int BN>
-int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
-              const TcEpilogue& e, cudaStream_t st) {
+int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to32,
+              const CUtensorMap& to16, const CUtensorMap& to16a, const CUtensorMap& tmean,
+              const TcProblem& p, const TcEpilogue& e, cudaStream_t st) {
   int stages;
   size_t smem;
+  // the bulk-copy epilogue's buffers come out of the stage budget
+  const size_t budget = kSmemBudget - (p.bulk_epi ? kBulkStgBytes + 1024 : 0);
   if (p.win) {  // window stages + every tap's weights (tc_run checked that two stages fit)
     const size_t a_win = (static_cast<size_t>(p.win) * p.bk * 2 + 1023) & ~static_cast<size_t>(1023);
     const size_t b_all = static_cast<size_t>(p.taps) * BN * p.bk * 2;
-    stages = static_cast<int>(std::min<size_t>(8, (kSmemBudget - b_all) / a_win));
+    stages = static_cast<int>(std::min<size_t>(8, (budget - b_all) / a_win));
     smem = 1024 + stages * a_win + b_all + (2 * stages + 9) * 8 + 16;
   } else {
     const int stage_bytes = (kBM + BN) * p.bk * 2;
-    stages = std::max(2, std::min(kSmemBudget / stage_bytes, 8));
+    stages = std::max(2, std::min(static_cast<int>(budget) / stage_bytes, 8));
     smem = 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * stages + 9) * 8 + 16;
   }
+  if (p.bulk_epi) smem += 1024 + kBulkStgBytes;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
     int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<BN>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemBudget + 4096),
+                                             kSmemBudget + 8192),
                         "cudaFuncSetAttribute(gemm_tc)");
     if (rc) return rc;
     attr_set[dev] = true;
@@ -867,8 +976,9 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const TcProblem& p,
   const int grid = static_cast<int>(std::min<long long>(tiles, sm_count()));
   if (p.pdl)
     return launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kThreads), smem, st, "gemm_tc_kernel",
-                      ta, tb, p, e, stages, device_status());
-  gemm_tc_kernel<BN><<<grid, kThreads, smem, st>>>(ta, tb, p, e, stages, device_status());
+                      ta, tb, to32, to16, to16a, tmean, p, e, stages, device_status());
+  gemm_tc_kernel<BN><<<grid, kThreads, smem, st>>>(ta, tb, to32, to16, to16a, tmean, p, e, stages,
+                                                   device_status());
   return check_launch("gemm_tc_kernel");
 }
 
@@ -930,6 +1040,9 @@ int tc_pick_bn(long long M, long long N) {
   return (m_tiles * ((N + 255) / 256) >= sm_count()) ? 256 : 128;
 }
 
+// One-SM kernel's bulk-copy epilogue where the outputs allow it
+// (gsvk_gemm_set_bulk_epilogue).
+static int g_bulk_epi = 1;
 // Two-SM GEMM for eligible plain problems (gsvk_gemm_set_pair): 0 never,
 // 1 when pair_wins, 2 always.
 static int g_pair_mode = 1;
@@ -1013,12 +1126,56 @@ int tc_run(const uint16_t* a, long long a_rows, long long lda, const uint16_t* b
   if (rc) return rc;
   rc = make_kmajor_map(&tb, b, b_rows, b_cols ? b_cols : p.kc, ldb, bn, p.bk);
   if (rc) return rc;
+  // bulk-copy epilogue: contiguous output rows (no ConvT interleave, no
+  // batched offsets), no transposed-V output, 16-byte aligned outputs, and
+  // the stage ring still two deep in the smaller budget
+  CUtensorMap to32{}, to16{}, to16a{}, tmean{};
+  p.bulk_epi = 0;
+  if (g_bulk_epi && !p.convt && p.bh == 0 && p.phases == 1 && !e.vt &&
+      (e.c32 || e.c16 || e.c16_act || e.mean_sum) &&
+      (!e.c32 || (aligned16(e.c32) && e.ld_c32 % 4 == 0)) &&
+      (!e.mean_sum || (aligned16(e.mean_sum) && e.ld_c32 % 4 == 0)) &&
+      (!e.c16 || (aligned16(e.c16) && e.ld_c16 % 8 == 0)) &&
+      (!e.c16_act || (aligned16(e.c16_act) && e.ld_c16_act % 8 == 0))) {
+    const long long budget = kSmemBudget - static_cast<long long>(kBulkStgBytes) - 1024;
+    long long need = 2LL * (kBM + bn) * p.bk * 2;
+    if (p.win) {
+      const long long a_win = (static_cast<long long>(p.win) * p.bk * 2 + 1023) & ~1023LL;
+      need = static_cast<long long>(p.taps) * bn * p.bk * 2 + 2 * a_win;
+    }
+    if (need <= budget) {
+      const uint64_t odims[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M)};
+      const uint32_t box[2] = {16, 32};
+      if (e.c32) {
+        const uint64_t str[1] = {static_cast<uint64_t>(e.ld_c32) * 4};
+        rc = encode_tiled(&to32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, e.c32, odims, str, box,
+                          CU_TENSOR_MAP_SWIZZLE_64B);
+      }
+      if (!rc && e.c16) {
+        const uint64_t str[1] = {static_cast<uint64_t>(e.ld_c16) * 2};
+        rc = encode_tiled(&to16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e.c16, odims, str, box,
+                          CU_TENSOR_MAP_SWIZZLE_32B);
+      }
+      if (!rc && e.c16_act) {
+        const uint64_t str[1] = {static_cast<uint64_t>(e.ld_c16_act) * 2};
+        rc = encode_tiled(&to16a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e.c16_act, odims, str, box,
+                          CU_TENSOR_MAP_SWIZZLE_32B);
+      }
+      if (!rc && e.mean_sum) {  // the running mean shares the fp32 output's layout
+        const uint64_t str[1] = {static_cast<uint64_t>(e.ld_c32) * 4};
+        rc = encode_tiled(&tmean, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, e.mean_sum, odims, str, box,
+                          CU_TENSOR_MAP_SWIZZLE_64B);
+      }
+      if (rc) return rc;
+      p.bulk_epi = 1;
+    }
+  }
   switch (bn) {
-    case 16: return launch_bn<16>(ta, tb, p, e, st);
-    case 32: return launch_bn<32>(ta, tb, p, e, st);
-    case 64: return launch_bn<64>(ta, tb, p, e, st);
-    case 128: return launch_bn<128>(ta, tb, p, e, st);
-    case 256: return launch_bn<256>(ta, tb, p, e, st);
+    case 16: return launch_bn<16>(ta, tb, to32, to16, to16a, tmean, p, e, st);
+    case 32: return launch_bn<32>(ta, tb, to32, to16, to16a, tmean, p, e, st);
+    case 64: return launch_bn<64>(ta, tb, to32, to16, to16a, tmean, p, e, st);
+    case 128: return launch_bn<128>(ta, tb, to32, to16, to16a, tmean, p, e, st);
+    case 256: return launch_bn<256>(ta, tb, to32, to16, to16a, tmean, p, e, st);
     default: return fail(GSVK_ERR_INVALID, "bad BN %d", bn);
   }
 }
@@ -1077,6 +1234,11 @@ int gsvk_gemm_uses_pair(size_t M, size_t N, size_t K) {
                           gsvk::tc_pick_bn((long long)M, (long long)N)))
              ? 1
              : 0;
+}
+
+int gsvk_gemm_set_bulk_epilogue(int enable) {
+  g_bulk_epi = enable != 0;
+  return GSVK_OK;
 }
 
 int gsvk_gemm_set_pair(int mode) {

@@ -94,6 +94,10 @@ struct TcProblem {
   // and 2 = the fp32 output (c32, its fp32 residual loaded the same way) go
   // through swizzled shared-memory tiles and TMA bulk copies.
   int tma_epi;
+  // One-SM kernel: 1 = the fp32 / running-mean / fp16 / activated-fp16 outputs leave through
+  // swizzled shared-memory tiles (32 rows x 16 columns per warp) and TMA bulk
+  // stores (plain and conv problems: contiguous output rows).
+  int bulk_epi;
 };
 
 }  // namespace gsvk

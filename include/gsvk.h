@@ -121,6 +121,13 @@ int gsvk_gemm_set_pair(int mode);
  * leading dimensions K) runs on the two-SM kernel under the current mode,
  * 0 otherwise.  A query only: launches nothing. */
 int gsvk_gemm_uses_pair(size_t M, size_t N, size_t K);
+/* enable != 0 (the default): the one-SM tensor-core kernel (convolutions and
+ * the GEMMs kept off the two-SM kernel) writes its fp32 / fp16 / activated
+ * fp16 outputs through shared-memory tiles and TMA bulk stores where the
+ * problem allows (contiguous output rows, 16-byte aligned outputs, no
+ * transposed-V output); 0: per-row stores everywhere.
+ * Results are identical either way.  Process-wide. */
+int gsvk_gemm_set_bulk_epilogue(int enable);
 
 /* Strided batched GEMM: `batch` independent problems of one shape and one
  * epilogue, problem i reading A at args->a + i*stride_a and B at

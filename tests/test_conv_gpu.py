@@ -140,3 +140,28 @@ def test_decoder_graph_equals_eager(dev):
         assert bool(torch.isfinite(g).all())
     dec.close()
     assert dev.device_status() == 0
+
+
+def test_decoder_bulk_copy_epilogue_is_bit_identical(dev):
+    """The one-SM kernel's bulk-copy epilogue (swizzled shared-memory tiles,
+    TMA bulk stores) against its per-row stores on whole generator passes:
+    every conv output, ConvT phase and running mean agrees bit for bit."""
+    W = dev.workloads
+    cfg = W.DECODER
+    ws, bs = W.decoder_weights(cfg, seed=9)
+    dec = dev.Decoder(cfg, ws, bs, max_frames=40)
+    dec.set_graph(False)
+    try:
+        for T in (40, 17, 3):
+            z = torch.from_numpy(W.decoder_latent(T, cfg, seed=T + 1)).cuda()
+            dev.gemm_set_bulk_epilogue(False)
+            ref = dec.forward(z).clone()
+            dev.gemm_set_bulk_epilogue(True)
+            got = dec.forward(z)
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref), f"T={T}"
+            assert bool(torch.isfinite(got).all())
+    finally:
+        dev.gemm_set_bulk_epilogue(True)
+        dec.close()
+    assert dev.device_status() == 0

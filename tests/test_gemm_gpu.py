@@ -344,3 +344,35 @@ def test_gemm_uses_pair_follows_the_mode(dev):
         assert not dev.gemm_uses_pair(4096, 1024, 4096)
     finally:
         dev.gemm_set_pair(dev.PAIR_AUTO)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 520, 128), (1000, 64, 256), (517, 136, 64), (300, 16, 32),
+                                   (4100, 1000, 64), (260, 68, 64)])
+def test_one_sm_bulk_copy_epilogue_matches_per_row_stores(dev, M, N, K):
+    """The one-SM kernel's bulk-copy epilogue writes the same bits as its
+    per-row stores (bias, GELU, residual, fp32 and fp16 outputs; wide and
+    narrow tiles, ragged M and N).  N = 68 has an fp16 row pitch that is not a
+    16-byte multiple: per-row stores in both runs."""
+    rng = np.random.default_rng(M * 5 + N + K)
+    a = h(rand16(rng, (M, K), 1.0))
+    w = h(rand16(rng, (N, K), 0.05))
+    bias = f(rng.standard_normal(N).astype(np.float32) * 0.1)
+    res = f(rng.standard_normal((M, N)).astype(np.float32))
+    out = {}
+    dev.gemm_set_pair(dev.PAIR_NEVER)
+    try:
+        for bulk in (False, True):
+            dev.gemm_set_bulk_epilogue(bulk)
+            c = torch.full((M, N), float("nan"), device="cuda")
+            c16 = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+            dev.gemm_ex(a, w, bias=bias, residual=res, act=dev.ACT_GELU_ERF, alpha=0.75, c=c, c_f16=c16)
+            o16 = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+            dev.gemm_ex(a, w, bias=bias, act=dev.ACT_GELU_ERF, c_f16=o16)
+            out[bulk] = (c.cpu().numpy(), c16.cpu().numpy(), o16.cpu().numpy())
+    finally:
+        dev.gemm_set_bulk_epilogue(True)
+        dev.gemm_set_pair(dev.PAIR_AUTO)
+    for i in range(3):
+        np.testing.assert_array_equal(out[True][i], out[False][i])
+    assert np.isfinite(out[True][0]).all()
+    assert dev.device_status() == 0
