@@ -68,6 +68,13 @@ class ClockSampler:
                  "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # sampling is running once the first row is out (bounded: 3 s)
+        deadline = time.time() + 3.0
+        while time.time() < deadline and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
@@ -321,6 +328,21 @@ def run_gemm1(args, rank, local, world):
     torch.cuda.synchronize(dev)
     clk = clocks.stop()
     t = max_over_ranks(start.elapsed_time(end) * 1e-3, world)
+    # e2e: every launch's activations from pinned host memory and its outputs
+    # back to the host (weights stay resident)
+    x_pin = xs[0].cpu().pin_memory()
+    y_pin = torch.empty(ys[0].shape, dtype=torch.float16).pin_memory()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        for j in range(iters // batch):
+            xs[0].copy_(x_pin, non_blocking=True)
+            g.gemm_batched(xs[0], ws[0], bias=bd, act=g.ACT_RELU, c_f16=ys[0])
+            y_pin.copy_(ys[0], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
     flops = 2 * 128 * 2048 * 512 * iters * args.steps * world
     hbm, tf, kind = measured_peaks()
     alg_bytes = 2760704  # X 131,072 + W 2,097,152 + b 8,192 + Y 524,288 per GEMM
@@ -333,6 +355,10 @@ def run_gemm1(args, rank, local, world):
                                             "iters_per_step": iters,
                                             "launch": f"CUDA graph of {iters // batch} strided-batched launches of {batch} independent GEMMs (gsvk_gemm_f16_batched)",
                                             "l2": f"{batch} X/W/Y copies per launch (weights 268 MB > L2)"},
+            "e2e": {"value": flops / t_e2e / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": x_pin.numel() * 2 * (iters // batch),
+                    "d2h_bytes_per_step": y_pin.numel() * 2 * (iters // batch),
+                    "note": "bound by the host link: 134 MB in and 537 MB out per 1024 GEMMs"},
             "gpu_launches": iters // batch * args.steps,
             "roofline": {"bound": "hbm", "kernel": "gemm_tc_kernel (strided batch)",
                          "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
