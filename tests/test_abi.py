@@ -53,3 +53,24 @@ def test_device_init_without_gpu_fails_cleanly(gsv):
     rc = gsv.lib().gsvk_device_init(0)
     assert rc == -7  # GSVK_ERR_NODEV
     assert gsv.lib().gsvk_available() == 0
+
+
+def test_two_sm_gemm_choice_is_host_logic(gsv):
+    """The cost rule that picks the two-SM GEMM runs on the host (148 SMs
+    when no device is visible): encoder-sized problems take it, few-row,
+    short and misaligned ones do not, and the mode switch forces either way.
+    The query launches nothing."""
+    try:
+        assert gsv.gemm_uses_pair(4096, 1024, 4096)      # one round of pair tiles vs two
+        assert gsv.gemm_uses_pair(8000, 3072, 768)
+        assert not gsv.gemm_uses_pair(2048, 1024, 1024)  # tie with short K: one-SM kernel
+        assert not gsv.gemm_uses_pair(64, 4096, 1024)    # few rows: split-K cluster kernel
+        assert not gsv.gemm_uses_pair(4096, 4096, 1000)  # K not a multiple of 64
+        gsv.gemm_set_pair(gsv.PAIR_ALWAYS)
+        assert gsv.gemm_uses_pair(2048, 1024, 1024)
+        gsv.gemm_set_pair(gsv.PAIR_NEVER)
+        assert not gsv.gemm_uses_pair(4096, 1024, 4096)
+        with pytest.raises(gsv.GsvkError):
+            gsv.gemm_set_pair(3)
+    finally:
+        gsv.gemm_set_pair(gsv.PAIR_AUTO)
