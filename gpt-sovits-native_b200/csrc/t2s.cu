@@ -1476,6 +1476,10 @@ int gsvk_attention_decode(const float* q, const uint16_t* kcache, const uint16_t
     return fail(GSVK_ERR_INVALID, "attention_decode: null pointer or zero size");
   if (head_dim != 32 && head_dim != 64)
     return fail(GSVK_ERR_UNSUPPORTED, "attention_decode: head_dim must be 32 or 64");
+  // n_heads and row_stride are narrowed to int below: reject anything that
+  // would not survive the cast (and keep n_heads * head_dim from wrapping).
+  if (n_heads > (1u << 20) || row_stride > static_cast<size_t>(INT32_MAX))
+    return fail(GSVK_ERR_INVALID, "attention_decode: n_heads or row stride out of range");
   if (row_stride < n_heads * head_dim || row_stride % 8 != 0 || len > (1u << 24))
     return fail(GSVK_ERR_INVALID, "attention_decode: bad row stride or length");
   if (!aligned16(q) || !aligned16(kcache) || !aligned16(vcache))
@@ -1518,7 +1522,17 @@ constexpr size_t kNoAllocAttnFloats = 262144;  // 1 MiB of fp32 chunk records
 static __device__ __align__(256) float g_noalloc_attn_scratch[kNoAllocAttnFloats];
 
 std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[64] = {};  // device address of the array, per device
+// Device address of the array, per device, and the driver context it was
+// resolved in: an address is only valid in its own context, so a caller that
+// switches to another context (or resets the device, which makes a new
+// primary context) gets the address resolved again.
+struct NoAllocSlot {
+  void* ctx = nullptr;
+  float* ptr = nullptr;
+};
+NoAllocSlot g_noalloc_slot[64];
+using CtxGetCurrentFn = int (*)(void**);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
 
 }  // namespace
 
@@ -1529,13 +1543,14 @@ size_t gsvk_attention_decode_noalloc_max_floats(void) { return kNoAllocAttnFloat
 int gsvk_attention_decode_noalloc(const float* q, const uint16_t* kcache, const uint16_t* vcache,
                                   size_t len, size_t n_heads, size_t head_dim, size_t row_stride,
                                   float scale, float* out, gsvk_stream_t stream) {
-  if (head_dim == 32 || head_dim == 64) {
-    const size_t need = gsvk_attention_workspace_floats(len, n_heads, head_dim);
-    if (need > kNoAllocAttnFloats)
+  if ((head_dim == 32 || head_dim == 64) && n_heads > 0) {
+    // Compared by division so that no product can wrap past the limit.
+    const size_t per_head = (len / kChunk + (len % kChunk != 0)) * (head_dim + 4);
+    if (per_head > kNoAllocAttnFloats || n_heads > kNoAllocAttnFloats / per_head)
       return fail(GSVK_ERR_UNSUPPORTED,
-                  "attention_decode_noalloc: needs %zu scratch floats, the static array holds "
-                  "%zu (n_heads * ceil(len/64) * (head_dim+4) must not exceed it)",
-                  need, kNoAllocAttnFloats);
+                  "attention_decode_noalloc: needs more scratch than the static array holds "
+                  "(%zu floats; n_heads * ceil(len/64) * (head_dim+4) must not exceed it)",
+                  kNoAllocAttnFloats);
   }
   int dev = -1;
   int rc = check_cuda(cudaGetDevice(&dev), "attention_decode_noalloc: cudaGetDevice");
@@ -1546,14 +1561,29 @@ int gsvk_attention_decode_noalloc(const float* q, const uint16_t* kcache, const 
     // One-time set-up per device, with that device current: host code cannot
     // use the array's name as a device address, so resolve it here.
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
+    if (!g_ctx_get_current) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult qr;
+      rc = check_cuda(cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &qr),
+                      "attention_decode_noalloc: cudaGetDriverEntryPoint");
+      if (rc) return rc;
+      if (qr != cudaDriverEntryPointSuccess || !fn)
+        return fail(GSVK_ERR_NODEV, "attention_decode_noalloc: driver lacks cuCtxGetCurrent");
+      g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    }
+    void* ctx = nullptr;
+    if (g_ctx_get_current(&ctx) != 0 || !ctx)
+      return fail(GSVK_ERR_NODEV, "attention_decode_noalloc: no current CUDA context");
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    if (!slot.ptr || slot.ctx != ctx) {
       void* p = nullptr;
       rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_attn_scratch),
                       "attention_decode_noalloc: cudaGetSymbolAddress");
       if (rc) return rc;
-      g_noalloc_ptr[dev] = static_cast<float*>(p);
+      slot.ptr = static_cast<float*>(p);
+      slot.ctx = ctx;
     }
-    scratch = g_noalloc_ptr[dev];
+    scratch = slot.ptr;
   }
   // Same kernels as gsvk_attention_decode; the records it reads are all
   // written earlier in the same call, so nothing needs clearing between calls.

@@ -299,7 +299,9 @@ int gsvk_attention_decode(const float* q, const uint16_t* kcache, const uint16_t
  * held by every GPU that loads the library until the process exits; requests
  * needing more (n_heads * ceil(len/64) * (head_dim+4) floats) return
  * GSVK_ERR_UNSUPPORTED.  The first call on a device resolves the array's
- * device address; make that first call before any stream capture.  All calls
+ * device address in the current driver context (and a call made from a
+ * different context, e.g. after a device reset, resolves it again); make that
+ * first call before any stream capture.  All calls
  * on a device share the array: calls that overlap on the GPU (other streams,
  * other host threads) race and must be serialised by the caller.  Results
  * are bit-identical to gsvk_attention_decode. */

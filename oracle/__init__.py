@@ -96,6 +96,9 @@ def lib():
             "ora_attention_decode": (None, [vp, vp, vp, sz, sz, sz, sz, c_float, vp]),
             "ora_encoder_layer": (None, [vp, vp, c_int, vp, c_int, c_int, vp]),
             "ora_t2s_generate": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp, vp, vp]),
+            "ora_t2s_decode_layer_literal": (None, [vp, vp, c_int, vp, sz, vp, vp]),
+            "ora_t2s_generate_ex": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, c_int, vp,
+                                            vp, vp]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(L, name)
@@ -340,6 +343,32 @@ def t2s_generate(model: dict, kcache: np.ndarray, vcache: np.ndarray, prefix: in
     if with_logits:
         return toks[:n], margins, logits
     return toks[:n], margins
+
+
+def t2s_generate_ex(model: dict, kcache: np.ndarray, vcache: np.ndarray, prefix: int,
+                    prompt: np.ndarray, max_steps: int, stop_on_eos: bool = False,
+                    literal: bool = False):
+    """ora_t2s_generate_ex: (tokens, margins, logits [steps, vocab]).  literal
+    selects the line-by-line restatement of the reference's decode layer."""
+    d, w = t2s_structs(model)
+    cap = kcache.shape[1]
+    pr = np.ascontiguousarray(prompt, np.int32)
+    toks = np.zeros(max_steps, dtype=np.int32)
+    margins = np.zeros(max_steps, dtype=np.float32)
+    logits = np.zeros((max_steps, model["vocab"]), dtype=np.float32)
+    n = lib().ora_t2s_generate_ex(ctypes.byref(d), ctypes.byref(w), _p(kcache), _p(vcache), cap,
+                                  prefix, _p(pr), pr.size, max_steps, int(stop_on_eos),
+                                  int(literal), _p(toks), _p(margins), _p(logits))
+    if n < 0:
+        raise ValueError("ora_t2s_generate_ex: cache too small")
+    return toks[:n], margins, logits
+
+
+def t2s_decode_layer_literal(model: dict, layer: int, x: np.ndarray, pos: int, kc: np.ndarray,
+                             vc: np.ndarray) -> None:
+    d, w = t2s_structs(model)
+    lib().ora_t2s_decode_layer_literal(ctypes.byref(d), ctypes.byref(w), layer, _p(x), pos,
+                                       _p(kc), _p(vc))
 
 
 def encoder_layer(model: dict, layer: int, x: np.ndarray, B: int, T: int, valid=None) -> None:

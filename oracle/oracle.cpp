@@ -669,10 +669,37 @@ void ora_t2s_pe_row(int d_model, size_t pos, float* pe) {
   }
 }
 
+// Attention of one head exactly as t2s_engine.cpp:1062-1087 writes it
+// (KV16): scores dot_f16kv * scale over [0, n), kern::softmax over all n
+// (kern.cpp:62-73: sequential max, std::exp, sequential sum, multiply by
+// 1/sum), then ov += p * v (accum_f16kv) slot by slot from ov = 0.
+void attend_literal(const float* q, const uint16_t* kc, const uint16_t* vc, size_t D, size_t n,
+                    size_t HD, float scale, float* out) {
+  std::vector<float> sc(n);
+  for (size_t k = 0; k < n; ++k) sc[k] = dot_f16kv(q, kc + k * D, HD) * scale;
+  ora_softmax(sc.data(), sc.data(), n);
+  for (size_t e = 0; e < HD; ++e) out[e] = 0.f;
+  for (size_t k = 0; k < n; ++k) accum_f16kv(out, vc + k * D, sc[k], HD);
+}
+
+// y[r] = W[r] . x with fp32 activations and widened fp16 weights in one FMA
+// chain per row: the resident fp32 DenseF16 (accel.hpp:85-92) through
+// sgemm at M = 1, restated in this oracle's sgemm order (ora_sgemm; the
+// Accelerate kernel's own blocking is closed).
+void gemv_sgemm_order(const uint16_t* w, const float* x, float* y, size_t out, size_t in) {
+  row_bands(out, [&](size_t r0, size_t r1) {
+    for (size_t r = r0; r < r1; ++r) y[r] = dot_f32_f16w(w + r * in, x, in);
+  });
+}
+
 // T2S layers.  Every dot product uses the canonical dot32 association and
 // attention the chunked softmax of attend_canon; LayerNorm is kern.cpp:27-58.
-void ora_t2s_decode_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l, float* x,
-                          size_t pos, uint16_t* kc, uint16_t* vc) {
+// literal != 0 instead follows t2s_engine.cpp:1036-1119 line by line where the
+// canonical order departs from it: attention per attend_literal, and W2 (and,
+// in ora_t2s_generate_literal, the logits head) through the fp32 DenseF16
+// order of gemv_sgemm_order.
+static void t2s_decode_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l, float* x,
+                             size_t pos, uint16_t* kc, uint16_t* vc, bool literal) {
   const size_t D = dm->d_model, H = dm->n_heads, HD = D / H, F = dm->ffn;
   const size_t len = pos + 1;
   const float scale = 1.0f / std::sqrt(static_cast<float>(HD));
@@ -684,8 +711,8 @@ void ora_t2s_decode_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int 
   ora_f32_to_f16(qkv.data() + D, kc + pos * D, D);       // :1053-1055
   ora_f32_to_f16(qkv.data() + 2 * D, vc + pos * D, D);
   for (size_t hh = 0; hh < H; ++hh)  // :1062-1087
-    attend_canon(qkv.data() + hh * HD, kc + hh * HD, vc + hh * HD, D, len, HD, scale,
-                 attn.data() + hh * HD);
+    (literal ? attend_literal : attend_canon)(qkv.data() + hh * HD, kc + hh * HD, vc + hh * HD, D,
+                                              len, HD, scale, attn.data() + hh * HD);
   // out proj on fp16(attn) + bias + residual, LN1 (:1089-1099)
   for (size_t i = 0; i < D; ++i) xr[i] = round_f16(attn[i]);
   gemv32(w->wout + l * D * D, xr.data(), xb.data(), D, D);
@@ -698,9 +725,19 @@ void ora_t2s_decode_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int 
     const float v = ff[i] + w->b1[l * F + i];
     ff[i] = v > 0.f ? v : 0.f;
   }
-  gemv32(w->w2 + l * D * F, ff.data(), xb.data(), D, F);
+  (literal ? gemv_sgemm_order : gemv32)(w->w2 + l * D * F, ff.data(), xb.data(), D, F);
   for (size_t i = 0; i < D; ++i) xb[i] = (xb[i] + w->b2[l * D + i]) + h[i];
   ora_layernorm(xb.data(), w->n2g + l * D, w->n2b + l * D, x, D, dm->ln_eps);
+}
+
+void ora_t2s_decode_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l, float* x,
+                          size_t pos, uint16_t* kc, uint16_t* vc) {
+  t2s_decode_layer(dm, w, l, x, pos, kc, vc, false);
+}
+
+void ora_t2s_decode_layer_literal(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l,
+                                  float* x, size_t pos, uint16_t* kc, uint16_t* vc) {
+  t2s_decode_layer(dm, w, l, x, pos, kc, vc, true);
 }
 
 void ora_t2s_prefill_layer(const ora_t2s_dims* dm, const ora_t2s_weights* w, int l, float* x,
@@ -842,10 +879,11 @@ int ora_t2s_greedy_sample(float* lg, int V, const int32_t* hist, size_t n_hist,
   return best;
 }
 
-int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
-                     uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt, size_t P,
-                     size_t max_steps, int stop_on_eos, int32_t* tokens_out,
-                     float* margins_out, float* last_logits) {
+static int t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
+                        uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt, size_t P,
+                        size_t max_steps, int stop_on_eos, int32_t* tokens_out,
+                        float* margins_out, float* last_logits, float* all_logits, bool literal) {
+  auto logits_head = literal ? gemv_sgemm_order : gemv32;  // predict_layer_fp, :704-708
   const size_t D = dm->d_model, L = dm->n_layers, V = dm->vocab;
   const int eos = static_cast<int>(V) - 1;
   if (P == 0 || prefix + P + max_steps > cap) return -1;
@@ -858,13 +896,14 @@ int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t*
   for (size_t l = 0; l < L; ++l)
     ora_t2s_prefill_layer(dm, w, static_cast<int>(l), xy.data(), P, prefix, 0, kc + l * cap * D,
                           vc + l * cap * D);
-  gemv32(w->wpred, xy.data() + (P - 1) * D, logits.data(), V, D);  // fp32 activations
+  logits_head(w->wpred, xy.data() + (P - 1) * D, logits.data(), V, D);  // fp32 activations
   std::vector<int32_t> hist(prompt, prompt + P);
   size_t cur = prefix + P;
   int n_out = 0;
   for (size_t idx = 0; idx < max_steps; ++idx) {
     const bool eos_allowed = idx >= 11;  // kEosMaskSteps
     if (last_logits) std::memcpy(last_logits, logits.data(), V * sizeof(float));
+    if (all_logits) std::memcpy(all_logits + idx * V, logits.data(), V * sizeof(float));
     int raw = -1;
     const int s = ora_t2s_greedy_sample(logits.data(), static_cast<int>(V), hist.data(),
                                         hist.size(), eos_allowed, &raw);
@@ -888,12 +927,28 @@ int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t*
     const uint16_t* er = w->audio_emb + static_cast<size_t>(s) * D;
     for (size_t d = 0; d < D; ++d) x1[d] = std::fmaf(dm->alpha_audio, pe[d], h2f(er[d]));
     for (size_t l = 0; l < L; ++l)
-      ora_t2s_decode_layer(dm, w, static_cast<int>(l), x1.data(), cur, kc + l * cap * D,
-                           vc + l * cap * D);
-    gemv32(w->wpred, x1.data(), logits.data(), V, D);
+      t2s_decode_layer(dm, w, static_cast<int>(l), x1.data(), cur, kc + l * cap * D,
+                       vc + l * cap * D, literal);
+    logits_head(w->wpred, x1.data(), logits.data(), V, D);
     ++cur;
   }
   return n_out;
+}
+
+int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
+                     uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt, size_t P,
+                     size_t max_steps, int stop_on_eos, int32_t* tokens_out,
+                     float* margins_out, float* last_logits) {
+  return t2s_generate(dm, w, kc, vc, cap, prefix, prompt, P, max_steps, stop_on_eos, tokens_out,
+                      margins_out, last_logits, nullptr, false);
+}
+
+int ora_t2s_generate_ex(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
+                        uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt, size_t P,
+                        size_t max_steps, int stop_on_eos, int literal, int32_t* tokens_out,
+                        float* margins_out, float* all_logits) {
+  return t2s_generate(dm, w, kc, vc, cap, prefix, prompt, P, max_steps, stop_on_eos, tokens_out,
+                      margins_out, nullptr, all_logits, literal != 0);
 }
 
 }  // extern "C"

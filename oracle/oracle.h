@@ -161,6 +161,18 @@ void ora_t2s_decode_layer(const ora_t2s_dims* d, const ora_t2s_weights* w,
                           int layer, float* x, size_t pos, uint16_t* kcache,
                           uint16_t* vcache);
 
+/* The same layer written line by line as t2s_engine.cpp:1036-1119 (KV16 &&
+ * GEMV16) where the canonical order above departs from it: attention takes
+ * kern::softmax over all len slots (kern.cpp:62-73: sequential max, libm
+ * expf, sequential sum, multiply by 1/sum) and accumulates normalised p * v
+ * slot by slot (accum_f16kv); W2 is the resident fp32 DenseF16 (accel.hpp:
+ * 85-92), i.e. sgemm at M = 1, restated as one FMA chain per row (ora_sgemm's
+ * order: Accelerate's blocking is closed).  QKV, out-proj, W1 (gemv_fmlal),
+ * the scores (dot_f16kv) and LayerNorm are the same in both. */
+void ora_t2s_decode_layer_literal(const ora_t2s_dims* d, const ora_t2s_weights* w,
+                                  int layer, float* x, size_t pos, uint16_t* kcache,
+                                  uint16_t* vcache);
+
 /* t2s_engine.cpp:881-1034 with KV16: S rows x[S][D] at absolute slots
  * pos..pos+S-1.  Query q sees every slot below pos, the first text_len
  * slots of the block, and block slots <= q (pos == 0 reproduces the
@@ -197,6 +209,18 @@ int ora_t2s_generate(const ora_t2s_dims* d, const ora_t2s_weights* w,
                      size_t prefix, const int32_t* prompt, size_t P,
                      size_t max_steps, int stop_on_eos, int32_t* tokens_out,
                      float* margins_out, float* last_logits);
+
+/* ora_t2s_generate with the decode layers and logits head selectable:
+ * literal = 0 is ora_t2s_generate; literal != 0 decodes through
+ * ora_t2s_decode_layer_literal and takes the logits through the fp32 DenseF16
+ * order (predict_layer_fp, t2s_engine.cpp:704-708).  The prompt prefill is
+ * the canonical one in both.  all_logits (optional, max_steps x vocab)
+ * receives the raw logits every step sampled from. */
+int ora_t2s_generate_ex(const ora_t2s_dims* d, const ora_t2s_weights* w,
+                        uint16_t* kcache, uint16_t* vcache, size_t cap,
+                        size_t prefix, const int32_t* prompt, size_t P,
+                        size_t max_steps, int stop_on_eos, int literal,
+                        int32_t* tokens_out, float* margins_out, float* all_logits);
 
 /* ---- encoders (BERT / HuBERT post-LN layer) ---------------------------- */
 typedef struct {
