@@ -137,30 +137,205 @@ def dist_close(world):
     _replicas().close(world)
 
 
+# --------------------------------------------- workload identity (both arms)
+# metric, unit and config of every workload: the GPU arm and the reference
+# arm print the same ones.
+def workload_meta(args, world):
+    import numpy as np
+
+    W = __import__("__graft_entry__").package().workloads
+    wl = args.workload
+    if wl == "t2s_decode_b1":
+        return dict(metric="T2S decode tokens/s (batch 1 per GPU, 500 greedy tokens per utterance)",
+                    unit="tokens/s", dtype="f16 weights/KV, f32 accumulate",
+                    data="synthetic (seeded N(0,0.02) weights, N(0,1) KV prefix, uniform prompt ids)",
+                    config={"workload": "t2s_decode_b1 (BASELINE configs[1])",
+                            "model": "T2S 24L d512 16h ffn2048 vocab1025 post-LN",
+                            "global_batch": world, "seq_len": T2S_STEPS, "kv_prefix": T2S_PREFIX,
+                            "prompt": T2S_PROMPT, "parallelism": f"replicas x{world}",
+                            "l2": "inputs larger than L2: 152 MB of weights streamed per token"})
+    if wl == "gemm_ffn_up":
+        return dict(metric="GEMM TFLOP/s (Y = ReLU(X W^T + b), 128x2048x512, fp16 out)",
+                    unit="TFLOP/s", dtype="f16 in, f32 accumulate, f16 out", data="synthetic",
+                    config={"workload": "gemm_ffn_up (BASELINE configs[0])", "shape": [128, 2048, 512],
+                            "epilogue": "bias + ReLU, fp16 out", "global_batch": world,
+                            "parallelism": f"replicas x{world}",
+                            "l2": "128 X/W/Y copies per launch (weights 268 MB > L2)"})
+    if wl == "gemm":
+        M, N, K = (int(v) for v in args.gemm_shape.split(","))
+        return dict(metric=f"GEMM TFLOP/s ({M}x{N}x{K}, fp16 out)", unit="TFLOP/s",
+                    dtype="f16 in, f32 accumulate, f16 out", data="synthetic N(0,1) x N(0,0.02)",
+                    config={"workload": "gemm", "shape": [M, N, K], "global_batch": world,
+                            "parallelism": f"replicas x{world}",
+                            "l2": "rotated operand copies > L2"})
+    if wl == "sovits_decoder":
+        cfg = W.DECODER
+        return dict(metric="SoVITS decoder TFLOP/s (192x500 latent -> 320,000 samples per utterance)",
+                    unit="TFLOP/s", dtype="f16 activations/weights, f32 accumulate and residual",
+                    data="synthetic (N(0,0.01) weights, N(0,1) latent)",
+                    config={"workload": "sovits_decoder (BASELINE configs[4])", "frames": 500,
+                            "samples": 500 * int(np.prod(cfg["up_rate"])), "global_batch": world,
+                            "parallelism": f"replicas x{world}",
+                            "l2": "activations 20-40 MB per layer at the late stages, > L2 per step"})
+    if wl == "encoder":
+        e = W.ENCODERS[args.encoder]
+        return dict(metric=f"{args.encoder} encoder prefill GEMM TFLOP/s (batch {e['batch']} x {e['seq']})",
+                    unit="TFLOP/s", dtype="f16 operands, f32 accumulate",
+                    data="synthetic (N(0,0.02) weights, N(0,1) activations)",
+                    config={"workload": f"encoder_{args.encoder} (BASELINE configs[3])",
+                            "layers": e["layers"], "hidden": e["hidden"], "ffn": e["ffn"],
+                            "global_batch": e["batch"] * world, "seq_len": e["seq"],
+                            "parallelism": f"replicas x{world}",
+                            "flops_counted": "the stack's GEMM FLOPs; time is the whole forward",
+                            "l2": "weights 0.2-0.6 GB and activations > L2 per step"})
+    if wl == "t2s_decode_b64":
+        B = args.batch
+        lens = W.t2s_batched_lengths(B, seed=1)
+        return dict(metric=f"batched T2S decode tokens/s ({B} utterances per GPU)", unit="tokens/s",
+                    dtype="f16 operands, f32 accumulate",
+                    data="synthetic (N(0,0.02) weights, N(0,1) KV, lengths U{64..1024} seed 1)",
+                    config={"workload": "t2s_decode_b64 (BASELINE configs[2])", "batch": B,
+                            "decode_steps_per_step": 32, "mean_kv_len": float(lens.mean()),
+                            "global_batch": B * world, "parallelism": f"replicas x{world}",
+                            "l2": "1.9 GB of weights + KV streamed per decode step"})
+    raise ValueError(wl)
+
+
 # ----------------------------------------------------- CPU baseline (oracle)
-def t2s_cpu_sample(n_decode=12, threads=None):
-    """Time the oracle restatement of the T2S generate on the host cores:
-    the 64-token prompt prefill, then n_decode decode steps; extrapolate to the
-    500-token utterance.  Returns (tokens_per_s, ms_per_utterance, threads, sample)."""
+# The reference is Apple-only (NEON, Accelerate, AArch64 AMX) and does not
+# build here, so its CPU arithmetic is timed through the oracle restatement
+# (kind "port"), threaded over the host cores.  Every workload has a bounded
+# sample of its own work; a sample is timed whole and reported as the
+# workload's unit.
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_sampler(args, threads):
+    """(fn, units_per_call, description): fn() runs one bounded sample of the
+    workload on the oracle; units_per_call is in the workload's unit
+    numerator (tokens, or FLOPs for TFLOP/s)."""
+    import numpy as np
     import oracle
 
-    g = __import__("__graft_entry__").package()
-    threads = threads or (os.cpu_count() or 1)
+    W = __import__("__graft_entry__").package().workloads
     oracle.build()
     oracle.set_threads(threads)
-    m, k0, v0, prompt = g.workloads.t2s_decode_b1(steps=n_decode + 1)
-    t0 = time.perf_counter()
-    oracle.t2s_generate(m, k0.copy(), v0.copy(), T2S_PREFIX, prompt, 1, False)
-    t_pf = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    oracle.t2s_generate(m, k0.copy(), v0.copy(), T2S_PREFIX, prompt, n_decode + 1, False)
-    t_all = time.perf_counter() - t0
-    per_tok = max(1e-9, (t_all - t_pf) / n_decode)
-    full = t_pf + (T2S_STEPS - 1) * per_tok
-    sample = (f"oracle T2S generate, 24 layers: 64-token prompt prefill ({t_pf*1e3:.0f} ms) + "
-              f"{n_decode} decode steps ({per_tok*1e3:.1f} ms/token), extrapolated to the "
-              f"500-token utterance; {threads} threads")
-    return T2S_STEPS / full, full * 1e3, threads, sample
+    wl = args.workload
+    if wl == "t2s_decode_b1":
+        m = W.t2s_model(seed=0)
+        L, D = m["n_layers"], m["d_model"]
+        top = T2S_PREFIX + T2S_PROMPT + T2S_STEPS
+        kc, vc = W.t2s_kv_prefix(m, top + 1, top, seed=5)
+        ctxs = [int(c) for c in np.linspace(T2S_PREFIX + T2S_PROMPT + 1, top, 10)]
+        hist = np.arange(64, dtype=np.int32)
+
+        def fn():
+            tok = 7
+            for c in ctxs:  # one decode token at each of 10 context lengths over 321..820
+                pe = oracle.t2s_pe_row(D, c - T2S_PREFIX)
+                x = (pe + m["audio_emb"][tok].view(np.float16).astype(np.float32)).astype(np.float32)
+                for layer in range(L):
+                    oracle.t2s_decode_layer(m, layer, x, c, kc[layer], vc[layer])
+                lg = oracle.gemv_f16w_f32acc(m["wpred"], x)
+                tok, _ = oracle.t2s_greedy_sample(lg, hist, True)
+        return fn, len(ctxs), ("oracle T2S decode: one token (24 layers, logits, sampling) at each of "
+                               f"10 context lengths evenly spaced over {ctxs[0]}..{ctxs[-1]}; the "
+                               "64-token prompt prefill is not in the sample")
+    if wl in ("gemm_ffn_up", "gemm"):
+        if wl == "gemm_ffn_up":
+            x, w, b = W.gemm_ffn_up(seed=0)
+            M, N, K = 128, 2048, 512
+            act = oracle.ACT_RELU
+        else:
+            M, N, K = (int(v) for v in args.gemm_shape.split(","))
+            M = min(M, 256)  # row band sample of a large shape
+            rng = np.random.default_rng(0)
+            x = W._f16(rng.standard_normal((M, K), dtype=np.float32))
+            w = W._f16(rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+            b, act = None, oracle.ACT_NONE
+        xf = x.view(np.float16).astype(np.float32)
+        reps = 4
+
+        def fn():
+            for _ in range(reps):
+                oracle.linear_f16(xf, w, b, act)
+        return fn, 2 * M * N * K * reps, (f"oracle gemm_f16x_fmlal order, {reps} x "
+                                         f"{M}x{N}x{K} with the fused epilogue")
+    if wl == "encoder":
+        e = W.ENCODERS[args.encoder]
+        ub, T = 4, e["seq"]
+        m = W.encoder_model(args.encoder, layers=1, seed=0)
+        x = W.encoder_input(args.encoder, batch=ub, seq=T, seed=0)
+        C, F = e["hidden"], e["ffn"]
+
+        def fn():
+            oracle.encoder_layer(m, 0, x.copy(), ub, T, None)
+        return fn, 2 * ub * T * (4 * C * C + 2 * C * F), (
+            f"oracle {args.encoder} layer (full post-LN layer) on {ub} of the {e['batch']} "
+            f"utterances x {T}; FLOPs counted as the layer's GEMMs")
+    if wl == "sovits_decoder":
+        cfg = W.DECODER
+        ws, bs = W.decoder_weights(cfg, seed=0)
+        T = 40
+        z = W.decoder_latent(T, cfg, seed=0)
+        dc = oracle.decoder_cfg(**cfg)
+
+        def fn():
+            oracle.decoder_forward(dc, ws, bs, z, round_in=True)
+        return fn, 2 * W.decoder_macs(cfg, T), f"oracle generator on a {T}-frame latent (of 500)"
+    if wl == "t2s_decode_b64":
+        m = W.t2s_model(seed=1)
+        L, D = m["n_layers"], m["d_model"]
+        lens = W.t2s_batched_lengths(args.batch, seed=1)[:8]
+        caches = [W.t2s_kv_prefix(m, int(n) + 1, int(n), seed=600 + i) for i, n in enumerate(lens)]
+        hist = np.arange(8, dtype=np.int32)
+
+        def fn():
+            for (kc, vc), n in zip(caches, lens):
+                x = m["audio_emb"][3].view(np.float16).astype(np.float32)
+                for layer in range(L):
+                    oracle.t2s_decode_layer(m, layer, x, int(n), kc[layer], vc[layer])
+                lg = oracle.gemv_f16w_f32acc(m["wpred"], x)
+                oracle.t2s_greedy_sample(lg, hist, True)
+        return fn, len(lens), (f"oracle T2S decode: one token for each of the first {len(lens)} "
+                               f"utterances (KV lengths {', '.join(str(int(v)) for v in lens)})")
+    raise ValueError(wl)
+
+
+def cpu_measure(args, warmup=2, samples=7, threads=None):
+    """Median of `samples` timed samples after `warmup`; returns the
+    cpu_baseline dict (value in the workload's unit)."""
+    threads = threads or (os.cpu_count() or 1)
+    fn, units, desc = cpu_sampler(args, threads)
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(samples):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return cpu_result(args, units, desc, times, threads)
+
+
+def cpu_result(args, units, desc, times, threads):
+    meta = workload_meta(args, 1)
+    med = statistics.median(times)
+    scale = 1e-12 if meta["unit"] == "TFLOP/s" else 1.0
+    cv = statistics.pstdev(times) / statistics.mean(times) * 100 if len(times) > 1 else 0.0
+    return {"value": units / med * scale, "unit": meta["unit"], "cores": threads, "kind": "port",
+            "sample": f"{desc}; median of {len(times)} samples ({med * 1e3:.1f} ms each, "
+                      f"CV {cv:.1f} %)",
+            "median_ms": med * 1e3, "cv_pct": cv, "n_samples": len(times),
+            "nproc": os.cpu_count(), "cpu_model": cpu_model()}
 
 
 # ------------------------------------------------------------ T2S workload
@@ -190,6 +365,8 @@ def run_t2s(args, rank, local, world):
     prompt = g.workloads.t2s_prompt(T2S_PROMPT, m["vocab"], seed=rank)  # one utterance per rank
     cap = T2S_PREFIX + T2S_PROMPT + T2S_STEPS
     eng = g.T2S(m, cap)
+    if args.decode_kernel:
+        eng.set_decode_kernel(args.decode_kernel)
     k_pin = torch.from_numpy(k0[:, :T2S_PREFIX].copy()).pin_memory()
     v_pin = torch.from_numpy(v0[:, :T2S_PREFIX].copy()).pin_memory()
     eng.load_kv(k_pin.numpy(), v_pin.numpy(), T2S_PREFIX)
@@ -246,6 +423,8 @@ def run_t2s(args, rank, local, world):
     torch.cuda.synchronize(dev)
     t_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
     launches = eng.launches_per_generate() * args.steps
+    kernel_name = {1: "t2s_decode_kernel", 2: "t2s_cluster_kernel",
+                   3: "t2s_flow_kernel"}[eng.decode_kernel()]
     eng.close()
 
     tokens = T2S_STEPS * args.steps * world
@@ -273,7 +452,7 @@ def run_t2s(args, rank, local, world):
         "e2e": {"value": tokens / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "t2s_decode_kernel", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": kernel_name, "achieved": achieved,
                      "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": peak_kind, "traffic": T2S_TRAFFIC_RATIO * alg,
                      "traffic_note": "ncu DRAM bytes of a 20-step launch, scaled per pass",
@@ -681,28 +860,28 @@ WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder
 
 
 def run_reference(args, rank, world):
-    """The reference's CPU arithmetic (oracle restatement) on the host cores."""
+    """The reference's CPU arithmetic (the oracle restatement) on the host
+    cores: each step is one bounded sample of the workload, timed whole; the
+    line's value is the median step in the workload's unit."""
     if rank != 0:
         return None
-    if args.workload != "t2s_decode_b1":
-        return {"impl": "reference", "unavailable": "reference arm implemented for t2s_decode_b1"}
-    vals, mss = [], []
+    threads = os.cpu_count() or 1
+    fn, units, desc = cpu_sampler(args, threads)
     for _ in range(args.warmup):
-        t2s_cpu_sample(n_decode=4)
+        fn()
+    times = []
     for _ in range(args.steps):
-        v, ms, threads, sample = t2s_cpu_sample(n_decode=8)
-        vals.append(v)
-        mss.append(ms)
-    v = statistics.mean(vals)
-    return {"metric": "T2S decode tokens/s (batch 1 per GPU, 500 greedy tokens per utterance)",
-            "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(mss),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 weights/KV, f32 accumulate", "data": "synthetic",
-            "config": {"workload": "t2s_decode_b1 (BASELINE configs[1])"},
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    meta = workload_meta(args, 1)
+    cb = cpu_result(args, units, desc, times, threads)
+    return {"metric": meta["metric"], "value": cb["value"], "unit": meta["unit"],
+            "impl": "reference", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.median(times) * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": meta["dtype"], "data": meta["data"],
+            "config": meta["config"], "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": meta["unit"], "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
 
@@ -720,6 +899,8 @@ def main():
                     help="M,N,K of the gemm workload")
     ap.add_argument("--batch", type=int, default=64,
                     help="utterances of the t2s_decode_b64 workload (64 = BASELINE config 3)")
+    ap.add_argument("--decode-kernel", type=int, default=0,
+                    help="t2s_decode_b1 decode kernel (gsvk_t2s_set_decode_kernel; 0 = default)")
     ap.add_argument("--decode-steps", type=int, default=T2S_STEPS,
                     help="tokens per utterance (default 500; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -737,10 +918,15 @@ def main():
         line = WORKLOADS[args.workload](args, rank, local, world)
     finally:
         pass
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "t2s_decode_b1":
-        v, ms, threads, sample = t2s_cpu_sample()
-        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": sample}
+    if rank == 0:
+        # every arm prints the same metric, unit and config for the workload
+        meta = workload_meta(args, world)
+        extra = {k: v for k, v in line.get("config", {}).items() if k not in meta["config"]}
+        line.update(metric=meta["metric"], unit=meta["unit"], config=meta["config"])
+        if extra:
+            line["run"] = extra
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_measure(args)
     dist_close(world)
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -489,7 +489,7 @@ class T2S:
                                     max_steps, int(stop_on_eos), _ptr(tokens_dev), _ptr(n_out_dev),
                                     _ptr(margins_dev), _stream(stream)))
 
-    DECODE_GRID, DECODE_CLUSTER = 1, 2
+    DECODE_GRID, DECODE_CLUSTER, DECODE_FLOW = 1, 2, 3
 
     def set_decode_kernel(self, kind: int):
         """1 (or 0, the default): grid kernel (one CTA per SM, grid barriers,

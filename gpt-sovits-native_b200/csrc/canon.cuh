@@ -46,10 +46,23 @@ __device__ __forceinline__ float warp_dot32(const uint16_t* w, const float* x, i
   const int o0 = 8 * (lane >> 2) + (lane & 3);
   const int vec_end = n & ~63;
   float acc = 0.f;
+  if (n == 512) {  // the T2S width: every load ahead of the chain
+    float wv[16], xv[16];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      wv[2 * b] = h2f(w[64 * b + o0]);
+      wv[2 * b + 1] = h2f(w[64 * b + o0 + 4]);
+      xv[2 * b] = x[64 * b + o0];
+      xv[2 * b + 1] = x[64 * b + o0 + 4];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc = fmaf(wv[j], xv[j], acc);
+  } else {
 #pragma unroll 4
-  for (int i = 0; i < vec_end; i += 64) {
-    acc = fmaf(h2f(w[i + o0]), x[i + o0], acc);
-    acc = fmaf(h2f(w[i + o0 + 4]), x[i + o0 + 4], acc);
+    for (int i = 0; i < vec_end; i += 64) {
+      acc = fmaf(h2f(w[i + o0]), x[i + o0], acc);
+      acc = fmaf(h2f(w[i + o0 + 4]), x[i + o0 + 4], acc);
+    }
   }
   const float t = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
   const float u = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
@@ -75,70 +88,106 @@ __device__ __forceinline__ float group16_dot_kv(const float* q_reg, const uint16
   return __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
 }
 
+// 1 / sqrt(v) rounded to float exactly as (float)(1.0 / sqrt(v)) with both
+// double operations correctly rounded (kern.cpp:55).  Fast path: CUDA's
+// double rsqrt (within a few ulp of 1/sqrt(v)), rounded to float; the
+// reference value lies within 2^-40 * y of y, so when no float rounding
+// boundary (midpoint of two adjacent floats) lies that close to y both round
+// to the same float.  Otherwise (about one call in 2^15) the exact
+// sqrt-then-divide path decides.
+__device__ __forceinline__ float rstd_f32(double v) {
+  const double y = rsqrt(v);
+  const float r = __double2float_rn(y);
+  const double rd = static_cast<double>(r);
+  const double up = static_cast<double>(nextafterf(r, INFINITY));
+  const double dn = static_cast<double>(nextafterf(r, 0.0f));
+  const double tol = y * 0x1p-40;
+  if (fabs(y - 0.5 * (rd + up)) <= tol || fabs(y - 0.5 * (rd + dn)) <= tol)
+    return static_cast<float>(__ddiv_rn(1.0, __dsqrt_rn(v)));
+  return r;
+}
+
+// Sum chains of ln_canon for thread l (0..7: sum of x[l], x[l+8], ...;
+// 8..15: the same chains of squares, fused multiply-add), element order.
+template <int N>
+__device__ __forceinline__ float ln_chain_fixed(const float* buf, int l, bool sq) {
+  float v[N / 8];
+#pragma unroll
+  for (int u = 0; u < N / 8; ++u) v[u] = buf[l + 8 * u];
+  float a = 0.f;
+#pragma unroll
+  for (int u = 0; u < N / 8; ++u) a = sq ? fmaf(v[u], v[u], a) : __fadd_rn(a, v[u]);
+  return a;
+}
+
 // LayerNorm of n values held in shared memory `buf`, in place, whole block.
 // scratch: >= 18 floats of shared memory.  Threads 0-7 run the 8 sum chains,
-// 8-15 the 8 sum-of-squares chains (each in element order, loads hoisted 8
-// at a time); thread 0 then forms mean / variance / rstd in fp64.
+// 8-15 the 8 sum-of-squares chains (each in element order); thread 0 then
+// forms mean / variance / rstd in fp64.  rounded (optional) receives
+// f16-rounded copies of the outputs (the next GEMV's fp16 activations).
 __device__ __forceinline__ void ln_canon(float* buf, const float* g, const float* b, int n,
-                                         double eps, float* scratch) {
+                                         double eps, float* scratch, float* rounded = nullptr) {
   const int tid = threadIdx.x;
   const int vec_end = n & ~7;
   if (tid < 16) {
     const int l = tid & 7;
     const bool sq = tid >= 8;
     float a = 0.f;
-    int i = l;
-    for (; i + 56 < vec_end; i += 64) {
-      float v[8];
+    if (n == 512) {
+      a = ln_chain_fixed<512>(buf, l, sq);
+    } else {
+      int i = l;
+      for (; i + 56 < vec_end; i += 64) {
+        float v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = buf[i + 8 * u];
+        for (int u = 0; u < 8; ++u) v[u] = buf[i + 8 * u];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) a = sq ? fmaf(v[u], v[u], a) : __fadd_rn(a, v[u]);
-    }
-    for (; i < vec_end; i += 8) {
-      const float v = buf[i];
-      a = sq ? fmaf(v, v, a) : __fadd_rn(a, v);
-    }
-    scratch[tid] = a;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    const float* f = scratch;
-    const float s = __fadd_rn(__fadd_rn(__fadd_rn(f[0], f[1]), __fadd_rn(f[2], f[3])),
-                              __fadd_rn(__fadd_rn(f[4], f[5]), __fadd_rn(f[6], f[7])));
-    const float q = __fadd_rn(__fadd_rn(__fadd_rn(f[8], f[9]), __fadd_rn(f[10], f[11])),
-                              __fadd_rn(__fadd_rn(f[12], f[13]), __fadd_rn(f[14], f[15])));
-    double sum = static_cast<double>(s), sq = static_cast<double>(q);
-    for (int i = vec_end; i < n; ++i) {
-      const double xv = static_cast<double>(buf[i]);
-      sum = __dadd_rn(sum, xv);
-      sq = __dadd_rn(sq, __dmul_rn(xv, xv));
-    }
-    const double dn = static_cast<double>(n);
-    // x / 2^k == x * 2^-k exactly: skip the fp64 divide for power-of-two n
-    const bool pow2 = (n & (n - 1)) == 0;
-    const double inv_n = pow2 ? 1.0 / dn : 0.0;
-    const float mean = static_cast<float>(pow2 ? __dmul_rn(sum, inv_n) : __ddiv_rn(sum, dn));
-    const double md = static_cast<double>(mean);
-    const double ex2 = pow2 ? __dmul_rn(sq, inv_n) : __ddiv_rn(sq, dn);
-    float var = static_cast<float>(__dsub_rn(ex2, __dmul_rn(md, md)));
-    if (!(var >= 0.0f)) {
-      double s2 = 0.0;
-      for (int i = 0; i < n; ++i) {
-        const double d = __dsub_rn(static_cast<double>(buf[i]), md);
-        s2 = __dadd_rn(s2, __dmul_rn(d, d));
+        for (int u = 0; u < 8; ++u) a = sq ? fmaf(v[u], v[u], a) : __fadd_rn(a, v[u]);
       }
-      var = static_cast<float>(pow2 ? __dmul_rn(s2, inv_n) : __ddiv_rn(s2, dn));
+      for (; i < vec_end; i += 8) {
+        const float v = buf[i];
+        a = sq ? fmaf(v, v, a) : __fadd_rn(a, v);
+      }
     }
-    const float rstd = static_cast<float>(
-        __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(static_cast<double>(var), eps))));
-    scratch[16] = mean;
-    scratch[17] = rstd;
+      // lanes 0-7 and 8-15 combine as ((0+1)+(2+3))+((4+5)+(6+7))
+    float t = __fadd_rn(a, __shfl_xor_sync(0x0000ffffu, a, 1));
+    t = __fadd_rn(t, __shfl_xor_sync(0x0000ffffu, t, 2));
+    t = __fadd_rn(t, __shfl_xor_sync(0x0000ffffu, t, 4));
+    const float qsum = __shfl_sync(0x0000ffffu, t, 8);
+      if (tid == 0) {
+      double sum = static_cast<double>(t), sqs = static_cast<double>(qsum);
+      for (int i = vec_end; i < n; ++i) {
+        const double xv = static_cast<double>(buf[i]);
+        sum = __dadd_rn(sum, xv);
+        sqs = __dadd_rn(sqs, __dmul_rn(xv, xv));
+      }
+      const double dn = static_cast<double>(n);
+      // x / 2^k == x * 2^-k exactly: skip the fp64 divide for power-of-two n
+      const bool pow2 = (n & (n - 1)) == 0;
+      const double inv_n = pow2 ? 1.0 / dn : 0.0;
+      const float mean = static_cast<float>(pow2 ? __dmul_rn(sum, inv_n) : __ddiv_rn(sum, dn));
+      const double md = static_cast<double>(mean);
+      const double ex2 = pow2 ? __dmul_rn(sqs, inv_n) : __ddiv_rn(sqs, dn);
+      float var = static_cast<float>(__dsub_rn(ex2, __dmul_rn(md, md)));
+      if (!(var >= 0.0f)) {
+        double s2 = 0.0;
+        for (int i = 0; i < n; ++i) {
+          const double d = __dsub_rn(static_cast<double>(buf[i]), md);
+          s2 = __dadd_rn(s2, __dmul_rn(d, d));
+        }
+        var = static_cast<float>(pow2 ? __dmul_rn(s2, inv_n) : __ddiv_rn(s2, dn));
+      }
+          scratch[16] = mean;
+      scratch[17] = rstd_f32(__dadd_rn(static_cast<double>(var), eps));
+        }
   }
   __syncthreads();
   const float mean = scratch[16], rstd = scratch[17];
-  for (int i = tid; i < n; i += blockDim.x)
-    buf[i] = fmaf(__fmul_rn(__fsub_rn(buf[i], mean), rstd), g[i], b[i]);
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float v = fmaf(__fmul_rn(__fsub_rn(buf[i], mean), rstd), g[i], b[i]);
+    buf[i] = v;
+    if (rounded) rounded[i] = h2f(f2h(v));
+  }
   __syncthreads();
 }
 
@@ -149,13 +198,31 @@ __device__ __forceinline__ void warp_dot32x2(const uint16_t* w0, const uint16_t*
   const int o0 = 8 * (lane >> 2) + (lane & 3);
   const int vec_end = n & ~63;
   float a0 = 0.f, a1 = 0.f;
+  if (n == 512) {  // the T2S width: every load ahead of the chains
+    float u0[16], u1[16], xv[16];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      xv[2 * b] = x[64 * b + o0];
+      xv[2 * b + 1] = x[64 * b + o0 + 4];
+      u0[2 * b] = h2f(w0[64 * b + o0]);
+      u0[2 * b + 1] = h2f(w0[64 * b + o0 + 4]);
+      u1[2 * b] = h2f(w1[64 * b + o0]);
+      u1[2 * b + 1] = h2f(w1[64 * b + o0 + 4]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      a0 = fmaf(u0[j], xv[j], a0);
+      a1 = fmaf(u1[j], xv[j], a1);
+    }
+  } else {
 #pragma unroll 4
-  for (int i = 0; i < vec_end; i += 64) {
-    const float xl = x[i + o0], xh = x[i + o0 + 4];
-    a0 = fmaf(h2f(w0[i + o0]), xl, a0);
-    a1 = fmaf(h2f(w1[i + o0]), xl, a1);
-    a0 = fmaf(h2f(w0[i + o0 + 4]), xh, a0);
-    a1 = fmaf(h2f(w1[i + o0 + 4]), xh, a1);
+    for (int i = 0; i < vec_end; i += 64) {
+      const float xl = x[i + o0], xh = x[i + o0 + 4];
+      a0 = fmaf(h2f(w0[i + o0]), xl, a0);
+      a1 = fmaf(h2f(w1[i + o0]), xl, a1);
+      a0 = fmaf(h2f(w0[i + o0 + 4]), xh, a0);
+      a1 = fmaf(h2f(w1[i + o0 + 4]), xh, a1);
+    }
   }
   float t0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
   float t1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));

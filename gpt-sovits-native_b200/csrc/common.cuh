@@ -55,6 +55,15 @@ __device__ __forceinline__ void griddep_wait() {
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Aligns a dynamic shared-memory base to A bytes by pointer arithmetic on the
+// shared array itself, so that the compiler keeps every access derived from
+// it in the shared address space (a round trip through an integer would turn
+// them all into generic loads and stores).
+template <unsigned A>
+__device__ __forceinline__ uint8_t* align_smem(uint8_t* base) {
+  const unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(base));
+  return base + ((A - (a & (A - 1u))) & (A - 1u));
+}
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 // Two fp32 -> packed fp16 pair (low half = a), RNE, one conversion instruction.

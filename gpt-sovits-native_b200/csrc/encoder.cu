@@ -152,8 +152,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     const __grid_constant__ CUtensorMap tmVt, int T, int Tp, int H, int C,
                     const int* __restrict__ valid, uint16_t* __restrict__ ctx, uint32_t* status) {
   extern __shared__ uint8_t at_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(at_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(at_raw);
   __shared__ uint64_t load_bar, s_bar, o_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ float red[8 * kAttnQ];  // per-group row max [4][128], row sum [4][128]

@@ -192,8 +192,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   const SkProblem p = prob;
   const TcEpilogue e = epi;
   extern __shared__ uint8_t sk_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sk_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(sk_raw);
   __shared__ uint64_t full[8], empty[8];
   __shared__ uint64_t done, recv_bar;
   __shared__ uint32_t tmem_slot;

@@ -242,8 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idesc = idesc_f16_f32(kBM, BN);
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + static_cast<size_t>(stages) * a_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + b_region);
@@ -600,8 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kAcc = 2;
   constexpr uint32_t kTmemCols = 512;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + kPairStages * kHalfBytes;
   uint8_t* sOut = sB + kPairStages * kHalfBytes;  // kEpiWarps x 2 staging tiles

@@ -346,12 +346,12 @@ __device__ void prefetch_layer(const T2SDev& m, const DecodeArgs& a, const Slice
 }
 
 #include "t2s_cluster.cuh"
+#include "t2s_flow.cuh"
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m, const DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                             ~static_cast<uintptr_t>(127));
+  uint8_t* smem = align_smem<128>(smem_raw);
   const int D = m.D, F = m.F, V = m.V, H = m.H, L = m.L;
   uint8_t* wbuf[2] = {smem, smem + a.layer_bytes};
   uint16_t* wlog = reinterpret_cast<uint16_t*>(smem + 2 * static_cast<size_t>(a.layer_bytes));
@@ -536,11 +536,12 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
         load_vec<2>(xs, m.xpre, D);
         __syncthreads();
         GSVK_TR(16 + 16 * l + 14);
-        ln_canon(xs, lnb + 2 * D, lnb + 3 * D, D, m.eps, red);  // LN2 of layer l - 1
+        ln_canon(xs, lnb + 2 * D, lnb + 3 * D, D, m.eps, red, act);  // LN2 of layer l - 1
         GSVK_TR(16 + 16 * l + 15);
+      } else {
+        for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(xs[i]));
+        __syncthreads();
       }
-      for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(xs[i]));
-      __syncthreads();
       GSVK_TR(16 + 16 * l + 10);
       {
         uint16_t* kl = m.kc + (static_cast<size_t>(l) * m.cap + pos) * D;
@@ -651,10 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1) t2s_decode_kernel(const T2SDev m,
       // ---------------------------------------------------------------- P4
       load_vec<2>(hs, m.hpre, D);
       __syncthreads();
-      ln_canon(hs, lnb, lnb + D, D, m.eps,
-               red);
-      for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(hs[i]));
-      __syncthreads();
+      ln_canon(hs, lnb, lnb + D, D, m.eps, red, act);
       GSVK_TR(16 + 16 * l + 12);
       {
         auto put = [&](int r, float acc) {
@@ -940,6 +938,14 @@ struct T2SEngine {
   bool cluster_ok = false;
   size_t cluster_smem = 0;
   int decode_kind = 1;
+  // per-head cluster data-flow decode (t2s_flow_kernel): kind 3
+  bool flow_ok = false;
+  const void* flow_fn = nullptr;
+  size_t flow_smem = 0;
+  FlowArgs flow{};
+  CUtensorMap flow_tk{}, flow_tv{};
+  uint32_t flow_epoch = 1;   // exchange epochs used so far (never reused)
+  size_t flow_xbytes = 0;    // exchange words (zeroed at create)
   // device allocations
   void* weights = nullptr;   // one block: all fp16 weights + fp32 vectors + PE table
   void* w2_lanes = nullptr;  // W2 permuted for the single-cluster decode
@@ -1017,6 +1023,60 @@ int decode_plan(gsvk_t2s* e, int G) {
   e->decode_smem = smem;
   e->G = G;
   return GSVK_OK;
+}
+
+// Per-head cluster decode (t2s_flow_kernel): one cluster of cs CTAs per
+// head, cs the largest of 8..1 whose grid of H * cs CTAs the GPU can hold at
+// once (every cluster resident: the kernel's waits need co-resident CTAs) and
+// whose shared-memory plan fits.  Leaves flow_ok false when no size fits.
+void flow_plan(gsvk_t2s* e, int max_optin) {
+  const int D = e->D, F = e->F, V = e->V, H = e->H, HD = e->HD, sms = sm_count();
+  const int vp = (V + 1) & ~1;
+  if (D % 2 || F % 2 || std::max(std::max(D, F), vp) > 2 * kThreads * kFlMaxPairs) return;
+  const void* fn = HD == 32 ? (const void*)t2s_flow_kernel<32> : (const void*)t2s_flow_kernel<64>;
+  for (int cs = std::min(8, sms / H); cs >= 1; --cs) {
+    const int G = H * cs;
+    if (G > D) continue;  // every CTA must own rows of every exchanged vector
+    const FlLayout y = fl_layout(D, F, V, HD, cs, G, e->cap);
+    if (y.total > (uint32_t)max_optin || y.mq + y.mo + y.m1 + y.m2 > kThreads) continue;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)y.total) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(G);
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = y.total;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cs;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, fn, &lc) != cudaSuccess || clusters < H) {
+      cudaGetLastError();
+      continue;
+    }
+    // K and V caches as 2-D tensors [L * cap rows][D] fp16; a box is one
+    // head's HD columns of 64 consecutive slots (one softmax chunk)
+    const uint64_t dims[2] = {(uint64_t)D, (uint64_t)e->L * e->cap};
+    const uint64_t strides[1] = {(uint64_t)D * 2};
+    const uint32_t box[2] = {(uint32_t)HD, (uint32_t)kChunk};
+    if (encode_tiled(&e->flow_tk, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, e->dev.kc, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        encode_tiled(&e->flow_tv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, e->dev.vc, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return;
+    e->flow.cs = cs;
+    e->flow.y = y;
+    e->flow_fn = fn;
+    e->flow_smem = y.total;
+    e->flow_ok = true;
+    return;
+  }
 }
 
 }  // namespace
@@ -1106,6 +1166,10 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
                o_pattn = take((size_t)cap * D * 2), o_pff = take((size_t)cap * F * 2),
                o_trace = take((size_t)kTraceSteps * kTraceStride * 8),
                o_attn = take((size_t)D * 4), o_ticket = take((size_t)H * 4);
+  const int vp = (V + 1) & ~1;
+  const size_t o_xattn = take((size_t)2 * D * 8), o_xhpre = take((size_t)2 * D * 8),
+               o_xff = take((size_t)2 * F * 8), o_xxpre = take((size_t)2 * D * 8),
+               o_xlog = take((size_t)2 * vp * 8);
   if (cudaMalloc(&e->scratch, off) != cudaSuccess) {
     cudaGetLastError();
     gsvk_t2s_destroy(e);
@@ -1139,6 +1203,13 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
   e->pattn16 = reinterpret_cast<uint16_t*>(sb + o_pattn);
   e->pff16 = reinterpret_cast<uint16_t*>(sb + o_pff);
   e->d_trace = reinterpret_cast<unsigned long long*>(sb + o_trace);
+  e->flow.xattn = reinterpret_cast<uint64_t*>(sb + o_xattn);
+  e->flow.xhpre = reinterpret_cast<uint64_t*>(sb + o_xhpre);
+  e->flow.xff = reinterpret_cast<uint64_t*>(sb + o_xff);
+  e->flow.xxpre = reinterpret_cast<uint64_t*>(sb + o_xxpre);
+  e->flow.xlog = reinterpret_cast<uint64_t*>(sb + o_xlog);
+  e->flow.vp = vp;
+  e->flow_xbytes = o_xlog + (size_t)2 * vp * 8 - o_xattn;
 
   // ---- decode launch plan (one CTA per SM by default) and prefill attention
   const size_t slot_f = (size_t)kSlots * (HD == 32 ? slot_floats<32>() : slot_floats<64>());
@@ -1212,7 +1283,9 @@ int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, 
     }
     cudaGetLastError();  // a refused attribute or query only disables the variant
   }
-  e->decode_kind = 1;
+  flow_plan(e, max_optin);
+  // the per-head cluster decode when this shape and GPU can run it
+  e->decode_kind = e->flow_ok ? 3 : 1;
   *out = e;
   return GSVK_OK;
 }
@@ -1344,6 +1417,37 @@ int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size
   a.margins = margins_dev;
   a.trace = h->trace_on ? h->d_trace : nullptr;
   T2SDev dv = d;
+  if (h->decode_kind == 3) {
+    // this launch's exchange epochs: epoch0 + 1 .. epoch0 + steps * (L + 1);
+    // near the end of the 32-bit range the words are cleared and epochs restart
+    const uint64_t need = (uint64_t)max_steps * (h->L + 1) + 2;
+    if ((uint64_t)h->flow_epoch + need >= 0xFFFFFFF0ull) {
+      if ((rc = check_cuda(cudaMemsetAsync(h->flow.xattn, 0, h->flow_xbytes, st),
+                           "reset exchange words")))
+        return rc;
+      h->flow_epoch = 1;
+    }
+    FlowArgs fa = h->flow;
+    fa.epoch0 = h->flow_epoch;
+    h->flow_epoch += (uint32_t)need;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(h->H * fa.cs);
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = h->flow_smem;
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = fa.cs;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    if (h->HD == 32)
+      return check_cuda(cudaLaunchKernelEx(&lc, t2s_flow_kernel<32>, dv, a, fa, h->flow_tk, h->flow_tv),
+                        "t2s_flow_kernel (cluster launch)");
+    return check_cuda(cudaLaunchKernelEx(&lc, t2s_flow_kernel<64>, dv, a, fa, h->flow_tk, h->flow_tv),
+                      "t2s_flow_kernel (cluster launch)");
+  }
   if (h->decode_kind == 2) {
     cudaLaunchConfig_t lc{};
     lc.gridDim = dim3(kClCS);
@@ -1368,11 +1472,14 @@ int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size
 
 int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind) {
   if (!h) return fail(GSVK_ERR_INVALID, "t2s_set_decode_kernel: null handle");
-  if (kind < 0 || kind > 2) return fail(GSVK_ERR_INVALID, "t2s_set_decode_kernel: kind %d", kind);
+  if (kind < 0 || kind > 3) return fail(GSVK_ERR_INVALID, "t2s_set_decode_kernel: kind %d", kind);
   if (kind == 2 && !h->cluster_ok)
     return fail(GSVK_ERR_UNSUPPORTED, "t2s_set_decode_kernel: the single-cluster decode does not "
                                       "fit this model shape or GPU");
-  h->decode_kind = kind == 0 ? 1 : kind;
+  if (kind == 3 && !h->flow_ok)
+    return fail(GSVK_ERR_UNSUPPORTED, "t2s_set_decode_kernel: the per-head cluster decode does not "
+                                      "fit this model shape or GPU");
+  h->decode_kind = kind == 0 ? (h->flow_ok ? 3 : 1) : kind;
   return GSVK_OK;
 }
 

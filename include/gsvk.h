@@ -381,12 +381,19 @@ int gsvk_t2s_generate_device(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_
 int gsvk_t2s_set_trace(gsvk_t2s_t h, int enable);
 int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n);
 /* Which decode kernel gsvk_t2s_decode launches: 1 = persistent CTAs (one
- * per SM) with grid barriers (any shape; the default), 2 = one 16-CTA
+ * per SM) with grid barriers (any shape), 2 = one 16-CTA
  * thread-block cluster with cluster barriers and distributed shared memory
  * (d_model 512, head_dim 32, ffn 2048, <= 16 heads, cap <= 4096, and a GPU
- * that places such a cluster; raises GSVK_ERR_UNSUPPORTED otherwise).
- * 0 = the default.  Both produce identical tokens, margins, logits and KV.
- * gsvk_t2s_decode_kernel returns the current choice (1 or 2). */
+ * that places such a cluster), 3 = one thread-block cluster per attention
+ * head with K/V tiles loaded by TMA, and vectors exchanged between clusters
+ * through {value, epoch} words polled in global memory instead of grid
+ * barriers (needs every cluster resident at once and its shared-memory plan
+ * to fit; d_model, ffn and vocab up to 4096).  A kind the handle's shape or
+ * GPU cannot run raises GSVK_ERR_UNSUPPORTED.  0 = the default: 3 where the
+ * handle's shape and GPU can run it, 1 otherwise (the choice made at
+ * gsvk_t2s_create).  All produce
+ * identical tokens, margins, logits and KV.  gsvk_t2s_decode_kernel returns
+ * the current choice (1, 2 or 3). */
 int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind);
 int gsvk_t2s_decode_kernel(gsvk_t2s_t h);
 /* CTAs of the grid decode kernel (one per SM at most; 0 = every SM, the

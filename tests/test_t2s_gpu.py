@@ -44,7 +44,7 @@ def test_prefill_matches_oracle(dev, ora, small):
     eng.close()
 
 
-@pytest.mark.parametrize("kernel", [1, 2], ids=["grid", "cluster"])
+@pytest.mark.parametrize("kernel", [1, 2, 3], ids=["grid", "cluster", "flow"])
 @pytest.mark.parametrize("stop_on_eos", [False, True])
 def test_generate_small_token_identity(dev, ora, small, stop_on_eos, kernel):
     m = dict(small)
@@ -87,8 +87,8 @@ def test_generate_config2_full_model_token_identity(dev, ora):
     steps = 500
     toks_ref, marg_ref = ora.t2s_generate(m, k0.copy(), v0.copy(), 256, prompt, steps, False)
     eng = dev.T2S(m, cap)
-    assert eng.decode_kernel() == eng.DECODE_GRID  # the default
-    for kernel in (eng.DECODE_CLUSTER, eng.DECODE_GRID):
+    assert eng.decode_kernel() == eng.DECODE_FLOW  # the default on a B200
+    for kernel in (eng.DECODE_FLOW, eng.DECODE_CLUSTER, eng.DECODE_GRID):
         eng.set_decode_kernel(kernel)
         eng.load_kv(k0, v0, 256)
         toks, marg = eng.generate(256, prompt, steps, False)
@@ -101,14 +101,14 @@ def test_generate_config2_full_model_token_identity(dev, ora):
 
 
 def test_decode_kernels_write_identical_kv(dev, small):
-    """Both decode kernels leave the same KV cache and the same final logits."""
+    """All decode kernels leave the same KV cache and the same final logits."""
     m = small
     prefix, P, steps = 30, 8, 40
     cap = prefix + P + steps
     k0, v0 = dev.workloads.t2s_kv_prefix(m, cap, prefix, seed=2)
     prompt = dev.workloads.t2s_prompt(P, m["vocab"], seed=6)
     out = {}
-    for kernel in (1, 2):
+    for kernel in (1, 2, 3):
         eng = dev.T2S(m, cap)
         eng.set_decode_kernel(kernel)
         eng.load_kv(k0, v0, prefix)
@@ -116,12 +116,13 @@ def test_decode_kernels_write_identical_kv(dev, small):
         kv = eng.read_kv()
         out[kernel] = (toks, marg, eng.read_logits(), kv)
         eng.close()
-    for a, b in zip(out[1], out[2]):
-        if isinstance(a, tuple):
-            for x, y in zip(a, b):
-                np.testing.assert_array_equal(x, y)
-        else:
-            np.testing.assert_array_equal(a, b)
+    for other in (2, 3):
+        for a, b in zip(out[1], out[other]):
+            if isinstance(a, tuple):
+                for x, y in zip(a, b):
+                    np.testing.assert_array_equal(x, y)
+            else:
+                np.testing.assert_array_equal(a, b)
     assert dev.device_status() == 0
 
 
