@@ -942,6 +942,7 @@ struct T2SEngine {
   bool flow_ok = false;
   const void* flow_fn = nullptr;
   size_t flow_smem = 0;
+  int flow_grid = 0;         // clusters x CTAs per cluster
   FlowArgs flow{};
   CUtensorMap flow_tk{}, flow_tv{};
   uint32_t flow_epoch = 1;   // exchange epochs used so far (never reused)
@@ -1025,19 +1026,26 @@ int decode_plan(gsvk_t2s* e, int G) {
   return GSVK_OK;
 }
 
-// Per-head cluster decode (t2s_flow_kernel): one cluster of cs CTAs per
-// head, cs the largest of 8..1 whose grid of H * cs CTAs the GPU can hold at
-// once (every cluster resident: the kernel's waits need co-resident CTAs) and
-// whose shared-memory plan fits.  Leaves flow_ok false when no size fits.
+// Per-head cluster decode (t2s_flow_kernel): one cluster of cs CTAs per head
+// plus helper clusters of the same size for the grid-wide rows.  All clusters
+// must be resident at once (the kernel's waits need co-resident CTAs), so for
+// each cluster size the GPU's own count of simultaneously active clusters
+// bounds the grid.  Among the sizes whose shared-memory plan fits, the one
+// whose clusters cover a full cache's softmax chunks in the fewest rounds is
+// taken, then the one with the most CTAs, then the largest (fewer q/k/v rows
+// per CTA).  Leaves flow_ok false when none fits.
 void flow_plan(gsvk_t2s* e, int max_optin) {
   const int D = e->D, F = e->F, V = e->V, H = e->H, HD = e->HD, sms = sm_count();
   const int vp = (V + 1) & ~1;
   if (D % 2 || F % 2 || std::max(std::max(D, F), vp) > 2 * kThreads * kFlMaxPairs) return;
   const void* fn = HD == 32 ? (const void*)t2s_flow_kernel<32> : (const void*)t2s_flow_kernel<64>;
-  for (int cs = std::min(8, sms / H); cs >= 1; --cs) {
-    const int G = H * cs;
-    if (G > D) continue;  // every CTA must own rows of every exchanged vector
-    const FlLayout y = fl_layout(D, F, V, HD, cs, G, e->cap);
+  int best_cs = 0, best_g = 0, best_rounds = 0;
+  FlLayout best_y{};
+  for (int cs = 8; cs >= 1; --cs) {
+    if (cs * H > sms) continue;
+    int nclust = std::min(sms / cs, D / cs);  // every CTA must own rows of every exchanged vector
+    if (nclust < H) continue;
+    FlLayout y = fl_layout(D, F, V, HD, cs, nclust * cs, e->cap);
     if (y.total > (uint32_t)max_optin || y.mq + y.mo + y.m1 + y.m2 > kThreads) continue;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)y.total) !=
         cudaSuccess) {
@@ -1045,7 +1053,7 @@ void flow_plan(gsvk_t2s* e, int max_optin) {
       continue;
     }
     cudaLaunchConfig_t lc{};
-    lc.gridDim = dim3(G);
+    lc.gridDim = dim3(nclust * cs);
     lc.blockDim = dim3(kThreads);
     lc.dynamicSmemBytes = y.total;
     cudaLaunchAttribute at[1];
@@ -1055,28 +1063,48 @@ void flow_plan(gsvk_t2s* e, int max_optin) {
     at[0].val.clusterDim.z = 1;
     lc.attrs = at;
     lc.numAttrs = 1;
-    int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, fn, &lc) != cudaSuccess || clusters < H) {
+    int active = 0;
+    if (cudaOccupancyMaxActiveClusters(&active, fn, &lc) != cudaSuccess) {
       cudaGetLastError();
       continue;
     }
-    // K and V caches as 2-D tensors [L * cap rows][D] fp16; a box is one
-    // head's HD columns of 64 consecutive slots (one softmax chunk)
-    const uint64_t dims[2] = {(uint64_t)D, (uint64_t)e->L * e->cap};
-    const uint64_t strides[1] = {(uint64_t)D * 2};
-    const uint32_t box[2] = {(uint32_t)HD, (uint32_t)kChunk};
-    if (encode_tiled(&e->flow_tk, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, e->dev.kc, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        encode_tiled(&e->flow_tv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, e->dev.vc, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
-      return;
-    e->flow.cs = cs;
-    e->flow.y = y;
-    e->flow_fn = fn;
-    e->flow_smem = y.total;
-    e->flow_ok = true;
+    nclust = std::min(nclust, active);
+    if (nclust < H) continue;
+    // fewer clusters: the rows per CTA grow, so re-plan at the final grid
+    y = fl_layout(D, F, V, HD, cs, nclust * cs, e->cap);
+    if (y.total > (uint32_t)max_optin || y.mq + y.mo + y.m1 + y.m2 > kThreads) continue;
+    // fewest attention rounds over a full cache first, then the most CTAs
+    // (sizes are tried largest first, so ties keep the larger cluster)
+    const int rounds = ((e->cap + kChunk - 1) / kChunk + cs * kSlots - 1) / (cs * kSlots);
+    if (!best_cs || rounds < best_rounds || (rounds == best_rounds && nclust * cs > best_g)) {
+      best_rounds = rounds;
+      best_g = nclust * cs;
+      best_cs = cs;
+      best_y = y;
+    }
+  }
+  if (!best_cs) return;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)best_y.total) !=
+      cudaSuccess) {
+    cudaGetLastError();
     return;
   }
+  // K and V caches as 2-D tensors [L * cap rows][D] fp16; a box is one
+  // head's HD columns of 64 consecutive slots (one softmax chunk)
+  const uint64_t dims[2] = {(uint64_t)D, (uint64_t)e->L * e->cap};
+  const uint64_t strides[1] = {(uint64_t)D * 2};
+  const uint32_t box[2] = {(uint32_t)HD, (uint32_t)kChunk};
+  if (encode_tiled(&e->flow_tk, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, e->dev.kc, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      encode_tiled(&e->flow_tv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, e->dev.vc, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+    return;
+  e->flow.cs = best_cs;
+  e->flow.y = best_y;
+  e->flow_grid = best_g;
+  e->flow_fn = fn;
+  e->flow_smem = best_y.total;
+  e->flow_ok = true;
 }
 
 }  // namespace
@@ -1431,7 +1459,7 @@ int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size
     fa.epoch0 = h->flow_epoch;
     h->flow_epoch += (uint32_t)need;
     cudaLaunchConfig_t lc{};
-    lc.gridDim = dim3(h->H * fa.cs);
+    lc.gridDim = dim3(h->flow_grid);
     lc.blockDim = dim3(kThreads);
     lc.dynamicSmemBytes = h->flow_smem;
     lc.stream = st;

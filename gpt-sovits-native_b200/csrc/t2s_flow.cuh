@@ -90,7 +90,7 @@ struct FlowArgs {
   uint64_t* xxpre;  // [2][D]
   uint64_t* xlog;   // [2][vp]
   int vp;           // V rounded up to even
-  int cs;           // CTAs per cluster (per head)
+  int cs;           // CTAs per cluster (the first H clusters each own a head)
   uint32_t epoch0;  // this launch's epochs are epoch0 + 1 ...
   FlLayout y;
 };
@@ -331,6 +331,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, c = blockIdx.x, cs = f.cs;
   const int head = c / cs;
+  // clusters past the heads help with the grid-wide rows only (no q/k/v rows,
+  // no attention): the GPU holds fewer clusters of a given size than it has
+  // SMs for, so the grid is H head clusters plus as many helpers as fit
+  const bool is_head = head < m.H;
   const int rank = static_cast<int>(cluster_rank());
 
   uint8_t* const wbuf0 = smem + Y.wbuf;  // layer buffer b at wbuf0 + b * layer_bytes
@@ -352,7 +356,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // row ownership: qkv rows of this cluster's head (local index j: group
   // j / HD = q, k, v; element j % HD), the other matrices over the grid
-  const int j0 = row_lo(3 * HD, cs, rank), j1 = row_lo(3 * HD, cs, rank + 1);
+  const int j0 = is_head ? row_lo(3 * HD, cs, rank) : 0;
+  const int j1 = is_head ? row_lo(3 * HD, cs, rank + 1) : 0;
   const int o0 = row_lo(D, G, c), o1 = row_lo(D, G, c + 1);
   const int a0 = row_lo(F, G, c), a1 = row_lo(F, G, c + 1);
   const int b0 = row_lo(D, G, c), b1 = row_lo(D, G, c + 1);
@@ -447,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool tiles_armed;
   {
     const int nch0 = (a.pos0 + 1 + kChunk - 1) / kChunk;
-    tiles_armed = tiles_issued(nch0, 0);
+    tiles_armed = is_head && tiles_issued(nch0, 0);
   }
 
   for (int cc = tid; cc < V; cc += kThreads) seen[cc] = 0;
@@ -469,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bulk_load(lnf + D, m.n2b + static_cast<size_t>(L - 1) * D, D * 4, &mbar[2]);
     for (int part = 0; part < 5; ++part) prefetch(0, wbuf0, &mbar[0], part);
     for (int part = 0; part < 5; ++part) prefetch(1 % L, wbuf0 + Y.layer_bytes, &mbar[1], part);
-    issue_tiles(0, (a.pos0 + 1 + kChunk - 1) / kChunk, 0);
+    if (is_head) issue_tiles(0, (a.pos0 + 1 + kChunk - 1) / kChunk, 0);
   }
   // every member of the cluster is running before any distributed
   // shared-memory store
@@ -641,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       GSVK_FTR(16 + 16 * l + 0);
       fl_cluster_sync();
       GSVK_FTR(16 + 16 * l + 1);
-      if (rank == cs - 1 && warp == kWarps - 1) {
+      if (is_head && rank == cs - 1 && warp == kWarps - 1) {
         // the head's new K and V rows (fp16) into the cache by bulk copy (the
         // same async proxy as the TMA tile loads that read them later), by
         // the member and warp with the least attention work
@@ -664,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const int slot = tid >> 6;
         float* ew = slots + slot * (kChunk + 8);
-        for (int rd = 0; rd < rounds; ++rd) {
+        for (int rd = 0; rd < (is_head ? rounds : 0); ++rd) {
           if (rd > 0) {  // later rounds: refill the tiles (all slots are done with them)
             __syncthreads();
             if (tid == 0 && !failed) issue_tiles(l, nch, rd);
@@ -695,10 +700,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tiles_armed = false;
       }
       GSVK_FTR(16 + 16 * l + 2);
-      if (rank == cs - 1 && tid == kThreads - 32) bulk_wait<0>();  // the K/V row is in the cache before anyone reads it
+      if (is_head && rank == cs - 1 && tid == kThreads - 32) bulk_wait<0>();  // the K/V row is in the cache before anyone reads it
       fl_cluster_sync();
       GSVK_FTR(16 + 16 * l + 3);
-      if (rank == 0 && warp == 0) {  // merge the head's chunk records, canonical order
+      if (is_head && rank == 0 && warp == 0) {  // merge the head's chunk records, canonical order
         float r0, r1;
         fl_combine<HD>(rec, nch, &r0, &r1);
         uint64_t* xa = f.xattn + static_cast<size_t>(par) * D + head * HD;
@@ -709,8 +714,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       {  // the next attention's tiles (this step's next layer, or the next step's first)
         const int nl = l + 1 < L ? l + 1 : 0;
         const int nn = l + 1 < L ? nch : (len + 1 + kChunk - 1) / kChunk;
-        if (tid == 0 && !failed) issue_tiles(nl, nn, 0);
-        tiles_armed = !failed && tiles_issued(nn, 0);
+        if (is_head && tid == 0 && !failed) issue_tiles(nl, nn, 0);
+        tiles_armed = is_head && !failed && tiles_issued(nn, 0);
       }
       // ------------------------------------------------ out-proj rows
       if (!fl_poll(f.xattn + static_cast<size_t>(par) * D, D, ep, act, m.status, failed)) failed = true;
