@@ -94,6 +94,10 @@ SIGNATURES = {
     "gsvk_decoder_set_graph": (c_int, [_vp, c_int]),
     "gsvk_sgemm": (c_int, [c_char, c_char, c_int, c_int, c_int, c_float, _vp, c_int, _vp, c_int,
                            c_float, _vp, c_int, _vp]),
+    "gsvk_gemm_nt_f16w": (c_int, [_vp, _sz, _sz, _vp, _sz, _vp, _vp]),
+    "gsvk_device_alloc_copy": (c_int, [_vp, _sz, _vp]),
+    "gsvk_device_free": (c_int, [_vp]),
+    "gsvk_gemm_chain_run": (c_int, [_vp, _sz, _vp]),
     "gsvk_encoder_create": (c_int, [_vp, _vp, _vp]),
     "gsvk_encoder_destroy": (c_int, [_vp]),
     "gsvk_encoder_forward": (c_int, [_vp, _vp, _sz, _sz, _vp, _vp]),
@@ -274,6 +278,30 @@ def gemm_grouped(problems, stream=None):
     gemm_ex keyword arguments (a, b, bias, residual, act, slope, alpha, c, c_f16)."""
     arr = (GemmArgs * len(problems))(*[_gemm_args(**p) for p in problems])
     check(lib().gsvk_gemm_grouped_f16(arr, len(problems), _stream(stream)))
+
+
+class GemmChainLink(ctypes.Structure):
+    _fields_ = [("chain_id", c_int), ("depth", c_int), ("gemm", GemmArgs)]
+
+
+def gemm_chain_run(links, stream=None):
+    """AmxChainLink / amx_chain_run: `links` is a list of (chain_id, depth,
+    dict of gemm_ex keyword arguments); links of one chain run in depth
+    order, chains are independent."""
+    arr = (GemmChainLink * len(links))(*[GemmChainLink(c, d, _gemm_args(**g)) for c, d, g in links])
+    check(lib().gsvk_gemm_chain_run(arr, len(links), _stream(stream)))
+
+
+def gemm_nt_f16w(x, w, y=None, stream=None):
+    """accel::gemm_nt_f16w: y[T, out] = x[T, in] (fp32) . W[out, in]^T (fp16,
+    widened exactly), fp32 accumulation."""
+    import torch
+
+    T, in_ = x.shape
+    out_ = w.shape[0]
+    y = y if y is not None else torch.empty(T, out_, dtype=torch.float32, device=x.device)
+    check(lib().gsvk_gemm_nt_f16w(_ptr(x), T, in_, _ptr(w), out_, _ptr(y), _stream(stream)))
+    return y
 
 
 class Weights:

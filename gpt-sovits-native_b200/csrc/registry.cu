@@ -7,6 +7,7 @@
 // weight — the layout the TMA descriptors read directly, so no re-packing is
 // needed (the conv weights' tap-major packing has its own entry points).
 #include <cstring>
+#include <vector>
 
 #include "gsvk_internal.hpp"
 
@@ -67,6 +68,62 @@ int gsvk_gemm_f16_w(const gsvk_gemm_args* args, gsvk_weights_t w, gsvk_stream_t 
 int gsvk_gemv_f16w_f32acc_w(gsvk_weights_t w, const float* x, float* y, gsvk_stream_t stream) {
   if (!w) return fail(GSVK_ERR_INVALID, "gemv_f16w_f32acc_w: null weights");
   return gsvk_gemv_f16w_f32acc(w->dev, x, y, w->rows, w->cols, stream);
+}
+
+int gsvk_device_alloc_copy(const void* src, size_t bytes, void** out) {
+  if (!out || bytes == 0) return fail(GSVK_ERR_INVALID, "device_alloc_copy: null out or empty");
+  *out = nullptr;
+  if (!gsvk_available()) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(GSVK_ERR_NOMEM, "device_alloc_copy: %zu bytes", bytes);
+  }
+  const int rc = src ? check_cuda(cudaMemcpy(p, src, bytes, cudaMemcpyDefault), "device upload")
+                     : check_cuda(cudaMemset(p, 0, bytes), "device memset");
+  if (rc) {
+    cudaFree(p);
+    return rc;
+  }
+  *out = p;
+  return GSVK_OK;
+}
+
+int gsvk_device_free(void* p) {
+  if (!p) return GSVK_OK;
+  return check_cuda(cudaFree(p), "device_free");
+}
+
+int gsvk_gemm_chain_run(const gsvk_gemm_chain_link* links, size_t n, gsvk_stream_t stream) {
+  if (n && !links) return fail(GSVK_ERR_INVALID, "gemm_chain_run: null link list");
+  // validate everything first: a bad link launches nothing
+  int max_depth = -1;
+  for (size_t i = 0; i < n; ++i) {
+    const gsvk_gemm_chain_link& k = links[i];
+    if (k.depth < 0 || k.depth > 4095)
+      return fail(GSVK_ERR_INVALID, "gemm_chain_run: link %zu has depth %d", i, k.depth);
+    for (size_t j = 0; j < i; ++j)
+      if (links[j].chain_id == k.chain_id && links[j].depth == k.depth)
+        return fail(GSVK_ERR_INVALID, "gemm_chain_run: links %zu and %zu share chain %d depth %d",
+                    j, i, k.chain_id, k.depth);
+    const gsvk_gemm_args& g = k.gemm;
+    if (!g.a || !g.b || (!g.c && !g.c_f16) || g.M == 0 || g.N == 0 || g.K == 0 ||
+        (g.lda && g.lda < g.K) || (g.ldb && g.ldb < g.K))
+      return fail(GSVK_ERR_INVALID, "gemm_chain_run: link %zu is invalid", i);
+    if (k.depth > max_depth) max_depth = k.depth;
+  }
+  // Depth level by level on the stream: every link of depth d follows every
+  // link of depth d - 1 (so each chain runs in order), and the links of one
+  // level are independent problems launched back to back.
+  std::vector<gsvk_gemm_args> level;
+  for (int d = 0; d <= max_depth; ++d) {
+    level.clear();
+    for (size_t i = 0; i < n; ++i)
+      if (links[i].depth == d) level.push_back(links[i].gemm);
+    if (!level.empty())
+      if (int rc = gsvk_gemm_grouped_f16(level.data(), level.size(), stream)) return rc;
+  }
+  return GSVK_OK;
 }
 
 int gsvk_gemm_grouped_f16(const gsvk_gemm_args* groups, size_t count, gsvk_stream_t stream) {

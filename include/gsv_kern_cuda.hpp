@@ -9,14 +9,19 @@
 //    current stream (set_stream), so calls return before the GPU finishes;
 //  - errors throw std::runtime_error (the reference throws at load time and
 //    returns silently on bad GEMM shapes, gemm_f16_amx.cpp:551-553);
-//  - DenseF16 has only the view form (fp16 weights stay fp16 on the device;
-//    the fp32 up-cast copy of accel.hpp:56 would double the HBM traffic).
+//  - the resident DenseF16 built from fp16 weights (accel.hpp:53) keeps them
+//    fp16 on the device and widens them exactly inside the GEMM
+//    (gemm_nt_f16w), which gives the sgemm results of the reference's fp32
+//    up-cast copy without storing (and streaming) twice the bytes;
+//  - AmxChainLink's host-side `prepare` hook has no counterpart (operands are
+//    device tensors written by the previous link's epilogue).
 #pragma once
 
 #include <cstddef>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #include "gsvk.h"
 
@@ -123,6 +128,24 @@ inline void gemm_panel(const uint16_t* a, const Panel& w, float* c, size_t M) {
 inline void batch_run(const gsvk_gemm_args* nodes, size_t n) {
   check(gsvk_gemm_grouped_f16(nodes, n, current_stream()), "batch_run");
 }
+// AmxChainLink / amx_chain_run (gemm_f16_amx.hpp:90-102): links of one chain
+// run in depth order, chains are independent.
+struct ChainLink {
+  int chain_id = 0;
+  int depth = 0;
+  gsvk_gemm_args gemm{};
+};
+inline void chain_run(const ChainLink* links, size_t n) {
+  static_assert(sizeof(ChainLink) == sizeof(gsvk_gemm_chain_link), "ChainLink layout");
+  check(gsvk_gemm_chain_run(reinterpret_cast<const gsvk_gemm_chain_link*>(links), n,
+                            current_stream()),
+        "chain_run");
+}
+// AmxTileChainLink / amx_tile_chain_run (gemm_f16_amx.hpp:104-124): the
+// reference's per-tile prepare overlap is the TMA / MMA pipeline inside each
+// link's kernel, so the same submission serves both.
+using TileChainLink = ChainLink;
+inline void tile_chain_run(const TileChainLink* links, size_t n) { chain_run(links, n); }
 
 namespace accel {
 
@@ -137,12 +160,35 @@ inline void f16_to_f32(const uint16_t* src, float* dst, size_t n) {
   check(gsvk_f16_to_f32(src, dst, n, current_stream()), "f16_to_f32");
 }
 
-// accel.hpp:47-98, view form: y[T,out] = f16(x)[T,in] . W[out,in]^T with the
-// fp16 activations staged in the caller's device buffer xh (>= T*in halves),
-// the role the reference's std::vector<uint16_t>& xh plays.
+// accel.hpp:38-41  y[T,out] = x[T,in] . W[out,in]^T, W fp16 widened exactly.
+inline void gemm_nt_f16w(const float* x, size_t T, size_t in, const uint16_t* w, size_t out,
+                         float* y) {
+  check(gsvk_gemm_nt_f16w(x, T, in, w, out, y, current_stream()), "gemm_nt_f16w");
+}
+
+// accel.hpp:47-98.  Three forms, as in the reference:
+//  - view (view_f16): borrows fp16 weights; forward = f16(x) . W^T on the
+//    tensor cores, the fp16 activations staged in the caller's device buffer
+//    xh (>= T*in halves, the role of the reference's std::vector xh);
+//  - resident from fp16 weights (accel.hpp:53): owns a device copy of the
+//    fp16 weights; forward = gemm_nt_f16w (fp32 activations);
+//  - resident from fp32 weights (accel.hpp:54): owns a device fp32 copy;
+//    forward = sgemm.
+// Source pointers of the owning constructors may be host or device memory.
+// The 3-argument forward of a view stages its fp16 activations in a device
+// buffer the object grows on first use (the reference allocates a vector on
+// every such call).  Move-only.
 class DenseF16 {
  public:
   DenseF16() = default;
+  DenseF16(const uint16_t* w16, size_t out, size_t in) : out_(out), in_(in) {
+    check(gsvk_weights_register(w16, out, in, &panel_), "DenseF16(w16)");
+  }
+  DenseF16(const float* w32_src, size_t out, size_t in) : out_(out), in_(in) {
+    void* p = nullptr;
+    check(gsvk_device_alloc_copy(w32_src, out * in * sizeof(float), &p), "DenseF16(w32)");
+    w32_ = static_cast<float*>(p);
+  }
   static DenseF16 view_f16(const uint16_t* w16_dev, size_t out, size_t in) {
     DenseF16 d;
     d.w16_ = w16_dev;
@@ -150,17 +196,85 @@ class DenseF16 {
     d.in_ = in;
     return d;
   }
+  DenseF16(const DenseF16&) = delete;
+  DenseF16& operator=(const DenseF16&) = delete;
+  DenseF16(DenseF16&& o) noexcept { *this = std::move(o); }
+  DenseF16& operator=(DenseF16&& o) noexcept {
+    if (this != &o) {
+      release();
+      w16_ = o.w16_;
+      panel_ = o.panel_;
+      w32_ = o.w32_;
+      xh_ = o.xh_;
+      xh_cap_ = o.xh_cap_;
+      out_ = o.out_;
+      in_ = o.in_;
+      o.w16_ = nullptr;
+      o.panel_ = nullptr;
+      o.w32_ = nullptr;
+      o.xh_ = nullptr;
+      o.xh_cap_ = 0;
+    }
+    return *this;
+  }
+  ~DenseF16() { release(); }
+
   bool is_view() const { return w16_ != nullptr; }
-  const uint16_t* data_f16() const { return w16_; }
+  const uint16_t* data_f16() const { return w16_ ? w16_ : (panel_ ? gsvk_weights_data(panel_) : nullptr); }
   size_t rows() const { return out_; }
   size_t cols() const { return in_; }
+
+  // y[T,out] = x[T,in] . W^T; y is overwritten.
   void forward(const float* x, size_t T, float* y, uint16_t* xh) const {
+    if (!w16_) {
+      forward(x, T, y);
+      return;
+    }
     check(gsvk_f32_to_f16(x, xh, T * in_, current_stream()), "DenseF16 f32_to_f16");
     check(gsvk_gemm_f16(xh, w16_, y, T, out_, in_, current_stream()), "DenseF16 gemm");
   }
+  void forward(const float* x, size_t T, float* y) {
+    if (w16_) {
+      if (xh_cap_ < T * in_) {
+        gsvk_device_free(xh_);
+        xh_ = nullptr;
+        xh_cap_ = 0;
+        void* p = nullptr;
+        check(gsvk_device_alloc_copy(nullptr, T * in_ * 2, &p), "DenseF16 activation buffer");
+        xh_ = static_cast<uint16_t*>(p);
+        xh_cap_ = T * in_;
+      }
+      forward(x, T, y, xh_);
+      return;
+    }
+    if (panel_) {
+      gemm_nt_f16w(x, T, in_, gsvk_weights_data(panel_), out_, y);
+      return;
+    }
+    if (!w32_) throw std::runtime_error("DenseF16::forward on an empty object");
+    sgemm('N', 'T', static_cast<int>(T), static_cast<int>(out_), static_cast<int>(in_), 1.0f, x,
+          static_cast<int>(in_), w32_, static_cast<int>(in_), 0.0f, y, static_cast<int>(out_));
+  }
+  void forward(const float* x, size_t T, float* y) const {
+    if (w16_) throw std::runtime_error("DenseF16::forward (const view) needs an xh buffer");
+    const_cast<DenseF16*>(this)->forward(x, T, y);
+  }
 
  private:
-  const uint16_t* w16_ = nullptr;
+  void release() {
+    if (panel_) gsvk_weights_release(panel_);
+    if (w32_) gsvk_device_free(w32_);
+    if (xh_) gsvk_device_free(xh_);
+    panel_ = nullptr;
+    w32_ = nullptr;
+    xh_ = nullptr;
+    xh_cap_ = 0;
+  }
+  const uint16_t* w16_ = nullptr;  // view
+  gsvk_weights_t panel_ = nullptr; // resident fp16
+  float* w32_ = nullptr;           // resident fp32
+  uint16_t* xh_ = nullptr;         // view: staged activations of the 3-argument forward
+  size_t xh_cap_ = 0;
   size_t out_ = 0, in_ = 0;
 };
 

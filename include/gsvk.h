@@ -147,6 +147,24 @@ int gsvk_gemm_f16_batched(const gsvk_gemm_args* args, size_t batch, size_t strid
  * validated before any is launched. */
 int gsvk_gemm_grouped_f16(const gsvk_gemm_args* groups, size_t count, gsvk_stream_t stream);
 
+/* Chained GEMMs: the analogue of AmxChainLink + amx_chain_run and
+ * AmxTileChainLink + amx_tile_chain_run (gemm_f16_amx.hpp:90-124).  Links of
+ * one chain_id run in depth order (depth d after depth d - 1, so a link may
+ * read the output of the link before it); links of different chains are
+ * independent.  Each link computes exactly what gsvk_gemm_f16_ex computes
+ * for its arguments.  The reference's host-side `prepare` hook (im2col into
+ * a packed panel) has no counterpart: a link's operands are device tensors
+ * the previous link's epilogue writes directly (convolutions take their
+ * taps by TMA coordinate shifts, gsvk_conv1d_f16).  Depths 0..4095; a
+ * repeated (chain_id, depth) pair or an invalid GEMM fails before anything
+ * is launched.  Work is queued on `stream` level by level. */
+typedef struct {
+  int chain_id;
+  int depth;
+  gsvk_gemm_args gemm;
+} gsvk_gemm_chain_link;
+int gsvk_gemm_chain_run(const gsvk_gemm_chain_link* links, size_t n, gsvk_stream_t stream);
+
 /* ---- weight registration (a8) ------------------------------------------- */
 /* The analogue of amx_pack / AmxPanel (gemm_f16_amx.hpp:36-50): a one-off
  * load-time upload of a row-major [rows, cols] fp16 weight (host or device
@@ -168,6 +186,21 @@ int gsvk_gemv_f16w_f32acc_w(gsvk_weights_t w, const float* x, float* y, gsvk_str
 int gsvk_sgemm(char transa, char transb, int M, int N, int K, float alpha, const float* A,
                int lda, const float* B, int ldb, float beta, float* C, int ldc,
                gsvk_stream_t stream);
+
+/* accel::gemm_nt_f16w (accel.hpp:38-41): y[T, out] = x[T, in] . W[out, in]^T
+ * with fp32 activations and fp16 weights widened exactly, one fp32 FMA chain
+ * per output in k order on CUDA cores -- bit-identical to gsvk_sgemm on an
+ * fp32 up-cast copy of W (which is how the reference computes it, and how
+ * its resident DenseF16 forward runs, accel.hpp:85-92).  Device pointers. */
+int gsvk_gemm_nt_f16w(const float* x, size_t T, size_t in, const uint16_t* w, size_t out,
+                      float* y, gsvk_stream_t stream);
+
+/* Device buffers for host code that does not link the CUDA runtime (the
+ * C++ shim's resident DenseF16 keeps its fp32 weights in one): allocates
+ * `bytes` of device memory and fills it from `src` (host or device memory),
+ * or with zeros when src is NULL.  Load-time helpers, not for the hot path. */
+int gsvk_device_alloc_copy(const void* src, size_t bytes, void** out);
+int gsvk_device_free(void* p);
 
 /* ---- SoVITS convolutions (a12-a14) -------------------------------------- */
 /* Activations are channels-last rows: x[T][ci] fp16 (the transpose of the

@@ -124,6 +124,106 @@ int main() {
     for (size_t i = 0; i < M * N; ++i)
       if (h1[i] != h2[i] || h3[i] != h2[i]) ++fails;
   }
+  // gemm_nt_f16w_and_dense_match_gemv_rows (test_accel.cpp:120-143): a
+  // [128, 96] fp16 weight, 17 rows of fp32 activations; gemm_nt_f16w and the
+  // resident DenseF16 (fp16 and fp32 constructors) against GEMV rows at
+  // 1e-5 of the row peak, and bit for bit against each other.
+  {
+    const size_t out = 128, in = 96, T = 17;
+    std::vector<uint16_t> w(out * in);
+    std::vector<float> w32(out * in);
+    for (size_t i = 0; i < w.size(); ++i) {
+      const _Float16 h = static_cast<_Float16>(rnd() * 0.05f);
+      std::memcpy(&w[i], &h, 2);
+      w32[i] = static_cast<float>(h);
+    }
+    std::vector<float> x(T * in);
+    for (auto& v : x) v = rnd();
+    uint16_t* dw = dev(w);
+    float* dx = dev(x);
+    float* dy = dev(std::vector<float>(T * out));
+    float* dyd = dev(std::vector<float>(T * out));
+    float* dy32 = dev(std::vector<float>(T * out));
+    float* dyv = dev(std::vector<float>(T * out));
+    float* dyr = dev(std::vector<float>(out));
+    gk::accel::gemm_nt_f16w(dx, T, in, dw, out, dy);
+    gk::accel::DenseF16 dense(w.data(), out, in);   // host fp16 source
+    dense.forward(dx, T, dyd);
+    gk::accel::DenseF16 dense32(w32.data(), out, in);  // host fp32 source
+    dense32.forward(dx, T, dy32);
+    gk::accel::DenseF16 view = gk::accel::DenseF16::view_f16(dw, out, in);
+    view.forward(dx, T, dyv);  // 3-argument view forward: f16 activations staged inside
+    auto y = host(dy, T * out), yd = host(dyd, T * out), y32 = host(dy32, T * out),
+         yv = host(dyv, T * out);
+    for (size_t t = 0; t < T; ++t) {
+      gk::gemv_f16w_f32acc(dw, dx + t * in, dyr, out, in);
+      auto yr = host(dyr, out);
+      float peak = 0;
+      for (float v : yr) peak = std::fmax(peak, std::fabs(v));
+      for (size_t o = 0; o < out; ++o) {
+        const size_t i = t * out + o;
+        if (std::fabs(y[i] - yr[o]) > 1e-5f * peak) ++fails;
+        if (yd[i] != y[i] || y32[i] != y[i]) ++fails;           // exact widening: same bits
+        if (std::fabs(yv[i] - yr[o]) > 2e-3f * peak) ++fails;   // view: fp16 activations
+      }
+    }
+    gk::accel::DenseF16 moved = std::move(dense);
+    moved.forward(dx, T, dyd);
+    if (host(dyd, T * out) != y) ++fails;
+  }
+  // amx_chain_run (gemm_f16_amx.hpp:90-102): two chains of three links, each
+  // link reading the fp16 output of the link before it; the chain submission
+  // gives the same bits as the links called one by one in order
+  {
+    const size_t M = 32, N = 64, K = 64;
+    std::vector<uint16_t> a(M * K), w(3 * N * K);
+    for (auto& v : a) {
+      const _Float16 h = static_cast<_Float16>(rnd());
+      std::memcpy(&v, &h, 2);
+    }
+    for (auto& v : w) {
+      const _Float16 h = static_cast<_Float16>(rnd() * 0.1f);
+      std::memcpy(&v, &h, 2);
+    }
+    uint16_t* da = dev(a);
+    uint16_t* dw = dev(w);
+    std::vector<uint16_t*> act(12);
+    for (auto& p : act) p = dev(std::vector<uint16_t>(M * N));
+    std::vector<float*> out(12);
+    for (auto& p : out) p = dev(std::vector<float>(M * N));
+    auto link = [&](int chain, int depth, int set) {
+      gk::ChainLink k;
+      k.chain_id = chain;
+      k.depth = depth;
+      k.gemm.a = depth == 0 ? da : act[set * 6 + chain * 3 + depth - 1];
+      k.gemm.b = dw + static_cast<size_t>(depth) * N * K;
+      k.gemm.M = M;
+      k.gemm.N = N;
+      k.gemm.K = K;
+      k.gemm.c = out[set * 6 + chain * 3 + depth];
+      k.gemm.c_f16 = act[set * 6 + chain * 3 + depth];
+      k.gemm.act = chain == 0 ? GSVK_ACT_RELU : GSVK_ACT_NONE;
+      return k;
+    };
+    std::vector<gk::ChainLink> links;
+    for (int d = 2; d >= 0; --d)  // any order in the list
+      for (int c = 0; c < 2; ++c) links.push_back(link(c, d, 0));
+    gk::chain_run(links.data(), links.size());
+    for (int c = 0; c < 2; ++c)
+      for (int d = 0; d < 3; ++d) {
+        const gk::ChainLink k = link(c, d, 1);
+        if (gsvk_gemm_f16_ex(&k.gemm, gk::current_stream()) != GSVK_OK) ++fails;
+      }
+    for (int i = 0; i < 6; ++i)
+      if (host(out[i], M * N) != host(out[6 + i], M * N)) ++fails;
+    // a repeated (chain, depth) pair is refused before anything runs
+    std::vector<gk::ChainLink> bad = {link(0, 0, 0), link(0, 0, 0)};
+    try {
+      gk::chain_run(bad.data(), bad.size());
+      ++fails;
+    } catch (const std::runtime_error&) {
+    }
+  }
   // error path: a bad transpose flag throws
   try {
     gk::accel::sgemm('X', 'N', 1, 1, 1, 1.f, nullptr, 1, nullptr, 1, 0.f, nullptr, 1);

@@ -376,3 +376,59 @@ def test_one_sm_bulk_copy_epilogue_matches_per_row_stores(dev, M, N, K):
         np.testing.assert_array_equal(out[True][i], out[False][i])
     assert np.isfinite(out[True][0]).all()
     assert dev.device_status() == 0
+
+
+# ------------------------------------------------- a7 gemm_nt_f16w, a11 chains
+@pytest.mark.parametrize("T,out_,in_", [(17, 128, 96), (1, 1536, 512), (64, 2048, 512),
+                                        (5, 33, 131), (300, 512, 2048)])
+def test_gemm_nt_f16w_matches_oracle_sgemm(dev, ora, T, out_, in_):
+    """accel::gemm_nt_f16w: bit-identical to the oracle's sgemm on the exactly
+    widened weights (one fp32 FMA chain per output in k order), and within
+    1e-5 of the row peak of the GEMV rows (test_accel.cpp:120-143)."""
+    rng = np.random.default_rng(T * 7 + out_)
+    w = (rng.standard_normal((out_, in_), dtype=np.float32) * 0.05).astype(np.float16).view(np.uint16)
+    x = rng.standard_normal((T, in_), dtype=np.float32)
+    y = dev.gemm_nt_f16w(torch.from_numpy(x).cuda(),
+                         torch.from_numpy(w.view(np.float16)).cuda()).cpu().numpy()
+    w32 = ora.f16_to_f32(w)
+    ref = np.zeros((T, out_), np.float32)
+    ora.sgemm("N", "T", T, out_, in_, 1.0, x, in_, w32, in_, 0.0, ref, out_)
+    np.testing.assert_array_equal(y, ref)
+    for t in range(min(T, 4)):
+        row = ora.gemv_f16w_f32acc(w, x[t])
+        assert np.abs(y[t] - row).max() <= 1e-5 * np.abs(row).max()
+
+
+def test_gemm_chain_matches_links_one_by_one(dev):
+    """amx_chain_run analogue: three chains of four links, each link reading
+    the fp16 output of the link before it, listed out of order: the chain
+    submission gives the same bits as calling the links in order."""
+    M, N, K = 48, 128, 128
+    rng = np.random.default_rng(3)
+    a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda().half()
+    ws = [torch.from_numpy(rng.standard_normal((N, K), dtype=np.float32) * 0.08).cuda().half()
+          for _ in range(4)]
+
+    def build():
+        acts = [[torch.empty(M, N, dtype=torch.float16, device="cuda") for _ in range(4)]
+                for _ in range(3)]
+        outs = [[torch.empty(M, N, device="cuda") for _ in range(4)] for _ in range(3)]
+        links = []
+        for d in (3, 1, 0, 2):
+            for c in range(3):
+                links.append((c, d, dict(a=a if d == 0 else acts[c][d - 1], b=ws[d],
+                                          act=dev.ACT_RELU if c == 1 else dev.ACT_NONE,
+                                          c=outs[c][d], c_f16=acts[c][d])))
+        return links, outs
+
+    links, outs = build()
+    dev.gemm_chain_run(links)
+    ref_links, ref_outs = build()
+    for c, d, g in sorted(ref_links, key=lambda t: (t[0], t[1])):
+        dev.gemm_ex(**g)
+    torch.cuda.synchronize()
+    for c in range(3):
+        for d in range(4):
+            assert torch.equal(outs[c][d], ref_outs[c][d]), (c, d)
+    with pytest.raises(dev.GsvkError):
+        dev.gemm_chain_run([links[0], links[0]])
