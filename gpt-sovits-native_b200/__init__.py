@@ -74,6 +74,7 @@ SIGNATURES = {
     "gsvk_t2s_read_kv": (c_int, [_vp, _vp, _vp]),
     "gsvk_t2s_set_decode_ctas": (c_int, [_vp, c_int]),
     "gsvk_t2s_decode_kernel": (c_int, [_vp]),
+    "gsvk_t2s_set_sampling": (c_int, [_vp, _vp]),
     "gsvk_t2s_read_trace": (c_int, [_vp, _vp, _sz]),
     "gsvk_attention_workspace_floats": (_sz, [_sz, _sz, _sz]),
     "gsvk_attention_decode": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp, _vp, _vp]),
@@ -445,6 +446,11 @@ class T2SHostWeights(ctypes.Structure):
                                    "n1g", "n1b", "n2g", "n2b", "wpred", "audio_emb")]
 
 
+class T2SSampling(ctypes.Structure):
+    _fields_ = [("mode", c_int), ("top_k", c_int), ("top_p", c_float), ("temperature", c_float),
+                ("rep_penalty", c_float), ("seed", ctypes.c_ulonglong)]
+
+
 class T2S:
     """Device T2S engine (ar::T2SEngine).  `model` is a dict of numpy arrays in
     the reference layouts (see workloads.t2s_model)."""
@@ -524,6 +530,15 @@ class T2S:
         phase trace); 2: single-cluster kernel (raises if unsupported).
         Both give identical tokens, margins, logits and KV."""
         check(lib().gsvk_t2s_set_decode_kernel(self.h, int(kind)))
+
+    def set_sampling(self, mode=1, top_k=15, top_p=1.0, temperature=1.0, rep_penalty=1.35,
+                     seed=1):
+        """gsvk_t2s_set_sampling; mode 0 (or None) restores greedy."""
+        if mode is None or mode == 0:
+            check(lib().gsvk_t2s_set_sampling(self.h, None))
+            return
+        sp = T2SSampling(mode, top_k, top_p, temperature, rep_penalty, seed)
+        check(lib().gsvk_t2s_set_sampling(self.h, ctypes.byref(sp)))
 
     def decode_kernel(self) -> int:
         return lib().gsvk_t2s_decode_kernel(self.h)

@@ -1315,8 +1315,13 @@ int gsvk_gemm_f16_batched(const gsvk_gemm_args* g, size_t batch, size_t stride_a
 
 }  // extern "C"
 
-int gsvk::gemm_ex_run(const gsvk_gemm_args* g, cudaStream_t st, bool static_b) {
-  if (!g || !g->a || !g->b || (!g->c && !g->c_f16) || g->M == 0 || g->N == 0 || g->K == 0)
+int gsvk::gemm_ex_run(const gsvk_gemm_args* args, cudaStream_t st, bool static_b) {
+  if (!args) return fail(GSVK_ERR_INVALID, "gemm: null arguments");
+  gsvk_gemm_args norm = *args;  // zero leading dimensions mean dense rows
+  if (!norm.lda) norm.lda = norm.K;
+  if (!norm.ldb) norm.ldb = norm.K;
+  const gsvk_gemm_args* g = &norm;
+  if (!g->a || !g->b || (!g->c && !g->c_f16) || g->M == 0 || g->N == 0 || g->K == 0)
     return fail(GSVK_ERR_INVALID, "gemm: null pointer or zero size");
   if (g->M > 0x7fffffff || g->N > 0x7fffffff || g->K > 0x7fffffff)
     return fail(GSVK_ERR_UNSUPPORTED, "gemm: size > 2^31");

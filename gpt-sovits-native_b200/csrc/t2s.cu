@@ -23,6 +23,7 @@
 // needs no extra barrier.  Each CTA owns fixed row slices of every weight
 // matrix and streams them into shared memory one layer ahead with bulk
 // copies, so HBM streaming overlaps the barrier latency chain.
+#include <chrono>
 #include <cmath>
 #include <mutex>
 #include <cstring>
@@ -73,6 +74,10 @@ struct DecodeArgs {
   uint32_t layer_bytes;
   uint32_t ln_off;   // LayerNorm parameters inside a layer buffer: n1g, n1b of the
                      // layer, then n2g, n2b of the layer before it (fp32, D each)
+  // sampling (SamplingParams, t2s_engine.hpp:69-77): mode 0 greedy, 1 top-k
+  int samp_mode, samp_top_k;
+  float samp_top_p, samp_temp, samp_pen;
+  unsigned long long samp_seed;
   // optional phase trace: CTA 0 writes %globaltimer (ns) at every phase
   // boundary of the first kTraceSteps steps, kTraceStride slots per step
   unsigned long long* trace;
@@ -946,6 +951,7 @@ struct T2SEngine {
   FlowArgs flow{};
   CUtensorMap flow_tk{}, flow_tv{};
   uint32_t flow_epoch = 1;   // exchange epochs used so far (never reused)
+  gsvk_t2s_sampling sampling{};  // mode 0: greedy
   size_t flow_xbytes = 0;    // exchange words (zeroed at create)
   // device allocations
   void* weights = nullptr;   // one block: all fp16 weights + fp32 vectors + PE table
@@ -1444,6 +1450,19 @@ int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size
   a.n_out = n_out_dev;
   a.margins = margins_dev;
   a.trace = h->trace_on ? h->d_trace : nullptr;
+  a.samp_mode = h->sampling.mode;
+  a.samp_top_k = h->sampling.top_k;
+  a.samp_top_p = h->sampling.top_p;
+  a.samp_temp = h->sampling.temperature;
+  a.samp_pen = h->sampling.rep_penalty;
+  a.samp_seed = h->sampling.seed;
+  if (a.samp_mode == 1) {
+    if (h->decode_kind != 3)
+      return fail(GSVK_ERR_UNSUPPORTED, "t2s_decode: top-k sampling runs on decode kernel 3 only");
+    if (a.samp_seed == 0)  // the reference draws a fresh seed (std::random_device)
+      a.samp_seed = static_cast<unsigned long long>(
+          std::chrono::high_resolution_clock::now().time_since_epoch().count()) | 1ull;
+  }
   T2SDev dv = d;
   if (h->decode_kind == 3) {
     // this launch's exchange epochs: epoch0 + 1 .. epoch0 + steps * (L + 1);
@@ -1512,6 +1531,27 @@ int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind) {
 }
 
 int gsvk_t2s_decode_kernel(gsvk_t2s_t h) { return h ? h->decode_kind : 0; }
+
+int gsvk_t2s_set_sampling(gsvk_t2s_t h, const gsvk_t2s_sampling* sp) {
+  if (!h) return fail(GSVK_ERR_INVALID, "t2s_set_sampling: null handle");
+  if (!sp) {
+    h->sampling = gsvk_t2s_sampling{};
+    return GSVK_OK;
+  }
+  if (sp->mode != 0 && sp->mode != 1)
+    return fail(GSVK_ERR_INVALID, "t2s_set_sampling: mode %d (0 greedy, 1 top-k)", sp->mode);
+  if (sp->mode == 1) {
+    if (sp->top_k < 1 || !(sp->top_p > 0.f && sp->top_p <= 1.f) || !(sp->rep_penalty > 0.f) ||
+        sp->temperature != sp->temperature)
+      return fail(GSVK_ERR_INVALID, "t2s_set_sampling: top_k >= 1, 0 < top_p <= 1, "
+                                    "rep_penalty > 0 and a temperature are required");
+    if (!h->flow_ok)
+      return fail(GSVK_ERR_UNSUPPORTED, "t2s_set_sampling: top-k sampling runs on decode kernel "
+                                        "3, which this shape or GPU cannot run");
+  }
+  h->sampling = *sp;
+  return GSVK_OK;
+}
 
 int gsvk_t2s_set_decode_ctas(gsvk_t2s_t h, int ctas) {
   if (!h) return fail(GSVK_ERR_INVALID, "t2s_set_decode_ctas: null handle");

@@ -43,7 +43,7 @@ struct FlLayout {
   int mq, mo, m1, m2, ml;     // max rows per CTA: qkv (per cluster member), out, W1, W2, logits
   uint32_t ln_off, layer_bytes;
   uint32_t wbuf, wlog, lnf, ktile, vtile, rec, slots, qkv, xs, hs, act, red, bsm, ctl, kvstage,
-      mbar, seen, total;
+      mbar, seen, svals, sidx, mt, total;
 };
 
 __host__ __device__ inline uint32_t fl_al(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
@@ -79,6 +79,9 @@ __host__ __device__ inline FlLayout fl_layout(int D, int F, int V, int HD, int c
   Y.kvstage = o; o = fl_al(o + 4u * HD, 16);
   Y.mbar = o;  o += 8 * 8;
   Y.seen = o;  o = fl_al(o + V, 16);
+  Y.svals = o; o = fl_al(o + 4u * V, 16);   // top-k sampling: penalised values
+  Y.sidx = o;  o = fl_al(o + 4u * V, 16);   // ... and their token ids
+  Y.mt = o;    o = fl_al(o + 8u * 313, 16); // mt19937_64 state + index
   Y.total = o + 128;  // alignment slack of the dynamic shared-memory base
   return Y;
 }
@@ -320,6 +323,137 @@ __device__ __forceinline__ void fl_chunk(const float* q, const uint16_t* kt, con
   slot_sync(bar_id);
 }
 
+// ---------------------------------------------------------- top-k sampling
+// std::mt19937_64 (Matsumoto-Nishimura 64-bit Mersenne Twister with the
+// parameters the C++ standard fixes for it), one thread: state[0..311],
+// state[312] = index of the next word.
+constexpr int kMtN = 312, kMtM = 156;
+__device__ void mt_seed(uint64_t* st, uint64_t seed) {
+  st[0] = seed;
+  for (int i = 1; i < kMtN; ++i)
+    st[i] = 6364136223846793005ull * (st[i - 1] ^ (st[i - 1] >> 62)) + static_cast<uint64_t>(i);
+  st[kMtN] = kMtN;
+}
+__device__ uint64_t mt_next(uint64_t* st) {
+  if (st[kMtN] >= static_cast<uint64_t>(kMtN)) {
+    constexpr uint64_t kUpper = 0xFFFFFFFF80000000ull, kLower = 0x7FFFFFFFull;
+    constexpr uint64_t kA = 0xB5026F5AA96619E9ull;
+    for (int i = 0; i < kMtN; ++i) {
+      const uint64_t y = (st[i] & kUpper) | (st[(i + 1) % kMtN] & kLower);
+      st[i] = st[(i + kMtM) % kMtN] ^ (y >> 1) ^ ((y & 1ull) ? kA : 0ull);
+    }
+    st[kMtN] = 0;
+  }
+  uint64_t x = st[st[kMtN]++];
+  x ^= (x >> 29) & 0x5555555555555555ull;
+  x ^= (x << 17) & 0x71D67FFFEDA60000ull;
+  x ^= (x << 37) & 0xFFF7EEE000000000ull;
+  x ^= x >> 43;
+  return x;
+}
+
+// topk_sample (t2s_engine.cpp:1640-1737) after the penalty: vals / idx hold
+// the penalised logits of tokens [0, limit) and their ids.  The top-k
+// selection sort runs round by round on the whole CTA (each round the first
+// position holding the maximum of positions [i, limit) -- the reference's
+// strict '>' scan -- is swapped into position i); thread 0 then applies the
+// temperature, the softmax (exp_det), top-p and the multinomial draw.
+// Returns the token on thread 0.
+__device__ int fl_topk_sample(float* vals, int* idx, int limit, int top_k, float top_p,
+                              float temperature, uint64_t* mt, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k = top_k > limit ? limit : (top_k < 1 ? 1 : top_k);
+  for (int i = 0; i < k; ++i) {
+    float bv = -INFINITY;
+    int bp = 0x7fffffff;
+    for (int p = i + tid; p < limit; p += kThreads) {
+      const float v = vals[p];
+      if (v > bv || (v == bv && p < bp)) {
+        bv = v;
+        bp = p;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+      if (ov > bv || (ov == bv && op < bp)) {
+        bv = ov;
+        bp = op;
+      }
+    }
+    if (lane == 0) {
+      red[warp] = bv;
+      reinterpret_cast<int*>(red + kWarps)[warp] = bp;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float B = red[0];
+      int P = reinterpret_cast<int*>(red + kWarps)[0];
+      for (int w = 1; w < kWarps; ++w) {
+        const float ov = red[w];
+        const int op = reinterpret_cast<int*>(red + kWarps)[w];
+        if (ov > B || (ov == B && op < P)) {
+          B = ov;
+          P = op;
+        }
+      }
+      if (vals[i] != vals[i] || P >= limit) P = i;  // a NaN at i: nothing compares greater
+      if (P != i) {
+        const float tv = vals[i];
+        vals[i] = vals[P];
+        vals[P] = tv;
+        const int ti = idx[i];
+        idx[i] = idx[P];
+        idx[P] = ti;
+      }
+    }
+    __syncthreads();
+  }
+  int tok = idx[0];
+  if (tid == 0 && temperature > 0.f) {
+    if (temperature != 1.0f)
+      for (int i = 0; i < k; ++i) vals[i] = __fdiv_rn(vals[i], temperature);
+    float mx = vals[0];
+    for (int i = 1; i < k; ++i)
+      if (vals[i] > mx) mx = vals[i];
+    float sum = 0.f;
+    for (int i = 0; i < k; ++i) {
+      vals[i] = exp_det(__fsub_rn(vals[i], mx));
+      sum = __fadd_rn(sum, vals[i]);
+    }
+    int keep = k;
+    if (top_p < 1.0f) {
+      const float threshold = __fmul_rn(__fsub_rn(1.f, top_p), sum);
+      float cum = 0.f;
+      for (int i = k - 1; i >= 0; --i) {
+        cum = __fadd_rn(cum, vals[i]);
+        if (cum >= threshold) {
+          keep = i + 1;
+          break;
+        }
+      }
+      if (keep < k) {
+        sum = 0.f;
+        for (int i = 0; i < keep; ++i) sum = __fadd_rn(sum, vals[i]);
+      }
+    }
+    // uniform_real_distribution<float>(0, 1) on the 64-bit engine (libc++
+    // generate_canonical<float, 24>): one draw, as float, times 2^-64
+    const float u = __fmul_rn(__fmul_rn(__ull2float_rn(mt_next(mt)), 0x1p-64f), sum);
+    float cdf = 0.f;
+    tok = idx[keep - 1];
+    for (int i = 0; i < keep; ++i) {
+      cdf = __fadd_rn(cdf, vals[i]);
+      if (u <= cdf) {
+        tok = idx[i];
+        break;
+      }
+    }
+  }
+  return tok;
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     t2s_flow_kernel(const T2SDev m, const DecodeArgs a, const FlowArgs f,
@@ -353,6 +487,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* ctl = reinterpret_cast<int*>(smem + Y.ctl);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + Y.mbar);
   uint8_t* seen = smem + Y.seen;
+  float* svals = reinterpret_cast<float*>(smem + Y.svals);
+  int* sidx = reinterpret_cast<int*>(smem + Y.sidx);
+  uint64_t* mt = reinterpret_cast<uint64_t*>(smem + Y.mt);
+  const bool topk = a.samp_mode == 1;
+  const float pen = topk ? a.samp_pen : 1.35f;
 
   // row ownership: qkv rows of this cluster's head (local index j: group
   // j / HD = q, k, v; element j % HD), the other matrices over the grid
@@ -464,6 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&mbar[i], 1);
     fence_barrier_init();
+    if (topk) mt_seed(mt, a.samp_seed);  // t2s_engine.cpp:1814-1818, one engine per generate
   }
   __syncthreads();
   if (tid == 0) {
@@ -512,7 +652,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int bi = 0x7fffffff;
     for (int cc = tid; cc < limit; cc += kThreads) {
       float v = idx > 0 ? lg[cc] : __ldcg(lg + cc);
-      if (seen[cc]) v = v < 0.f ? __fmul_rn(v, 1.35f) : __fdiv_rn(v, 1.35f);
+      if (seen[cc]) v = v < 0.f ? __fmul_rn(v, pen) : __fdiv_rn(v, pen);
+      if (topk) {
+        svals[cc] = v;
+        sidx[cc] = cc;
+      }
       if (v > bv || (v == bv && cc < bi)) {
         sv = bv;
         bv = v;
@@ -541,6 +685,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<int*>(red + 2 * kWarps)[warp] = bi;
     }
     __syncthreads();
+    // top-k sampling replaces the argmax (the margins below stay top1 - top2)
+    const int sampled = topk ? fl_topk_sample(svals, sidx, limit, a.samp_top_k, a.samp_top_p,
+                                              a.samp_temp, mt, red + 3 * kWarps)
+                             : 0;
     if (tid == 0) {
       float B = red[0], S = red[kWarps];
       int I = reinterpret_cast<int*>(red + 2 * kWarps)[0];
@@ -556,6 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (c == 0 && a.margins) a.margins[idx] = __fsub_rn(B, S);
+      if (topk) I = sampled;
       // the cluster follows its first member's token and abort decision
       if (rank == 0) {
         const int abort = failed || I < 0 || I >= V ||

@@ -429,6 +429,27 @@ int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n);
  * the current choice (1, 2 or 3). */
 int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind);
 int gsvk_t2s_decode_kernel(gsvk_t2s_t h);
+/* Sampling of the decode steps: SamplingParams (t2s_engine.hpp:69-77) and
+ * topk_sample (t2s_engine.cpp:1640-1737).  mode 0 (the default) is greedy;
+ * mode 1 applies the repetition penalty rep_penalty once per distinct history
+ * token, keeps the top_k logits (the reference's selection sort), divides by
+ * temperature (<= 0: the best of the top k), takes a softmax (a fixed
+ * Cody-Waite/Taylor exp in place of libm expf), cuts to the nucleus top_p
+ * and draws from std::mt19937_64 seeded with seed for each generate call
+ * (uniform = one 64-bit draw as float times 2^-64, as libc++'s
+ * uniform_real_distribution<float> computes it).  seed 0 takes a seed from
+ * the host clock (the reference uses std::random_device).  Top-k sampling
+ * runs on decode kernel 3 only (GSVK_ERR_UNSUPPORTED otherwise).  Margins
+ * stay top1 - top2 of the penalised logits.  NULL restores greedy. */
+typedef struct {
+  int mode;
+  int top_k;
+  float top_p;
+  float temperature;
+  float rep_penalty;
+  unsigned long long seed;
+} gsvk_t2s_sampling;
+int gsvk_t2s_set_sampling(gsvk_t2s_t h, const gsvk_t2s_sampling* sp);
 /* CTAs of the grid decode kernel (one per SM at most; 0 = every SM, the
  * default).  Results are identical for any count. */
 int gsvk_t2s_set_decode_ctas(gsvk_t2s_t h, int ctas);

@@ -97,6 +97,8 @@ def lib():
             "ora_encoder_layer": (None, [vp, vp, c_int, vp, c_int, c_int, vp]),
             "ora_t2s_generate": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp, vp, vp]),
             "ora_t2s_decode_layer_literal": (None, [vp, vp, c_int, vp, sz, vp, vp]),
+            "ora_t2s_generate_sampled": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp,
+                                                 vp, vp]),
             "ora_t2s_generate_ex": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, c_int, vp,
                                             vp, vp]),
         }
@@ -362,6 +364,30 @@ def t2s_generate_ex(model: dict, kcache: np.ndarray, vcache: np.ndarray, prefix:
     if n < 0:
         raise ValueError("ora_t2s_generate_ex: cache too small")
     return toks[:n], margins, logits
+
+
+class Sampling(ctypes.Structure):
+    """SamplingParams (t2s_engine.hpp:69-77); mode 0 greedy, 1 top-k."""
+    _fields_ = [("mode", c_int), ("top_k", c_int), ("top_p", ctypes.c_float),
+                ("temperature", ctypes.c_float), ("rep_penalty", ctypes.c_float),
+                ("seed", ctypes.c_ulonglong)]
+
+
+def t2s_generate_sampled(model: dict, kcache: np.ndarray, vcache: np.ndarray, prefix: int,
+                         prompt: np.ndarray, max_steps: int, sampling: "Sampling",
+                         stop_on_eos: bool = True):
+    """(tokens, margins) of a generate that samples with `sampling`."""
+    d, w = t2s_structs(model)
+    cap = kcache.shape[1]
+    pr = np.ascontiguousarray(prompt, np.int32)
+    toks = np.zeros(max_steps, dtype=np.int32)
+    margins = np.zeros(max_steps, dtype=np.float32)
+    n = lib().ora_t2s_generate_sampled(ctypes.byref(d), ctypes.byref(w), _p(kcache), _p(vcache),
+                                       cap, prefix, _p(pr), pr.size, max_steps, int(stop_on_eos),
+                                       ctypes.byref(sampling), _p(toks), _p(margins))
+    if n < 0:
+        raise ValueError("ora_t2s_generate_sampled: cache too small")
+    return toks[:n], margins
 
 
 def t2s_decode_layer_literal(model: dict, layer: int, x: np.ndarray, pos: int, kc: np.ndarray,

@@ -19,6 +19,7 @@
 #include <functional>
 #include <mutex>
 #include <thread>
+#include <random>
 #include <vector>
 
 namespace {
@@ -879,10 +880,112 @@ int ora_t2s_greedy_sample(float* lg, int V, const int32_t* hist, size_t n_hist,
   return best;
 }
 
+// t2s_engine.cpp:1640-1737 topk_sample: repetition penalty (once per distinct
+// history token below `limit`), top-k by the reference's selection sort
+// (strict '>' over the current positions, swapping into place), temperature,
+// softmax over the k values (exp_det in place of libm expf, as in the
+// canonical attention), top-p from the tail, then a multinomial draw
+// u = uniform(rng) * sum: uniform_real_distribution<float>(0, 1) on
+// std::mt19937_64, which the reference's libc++ evaluates as one 64-bit draw
+// converted to float and scaled by 2^-64 (generate_canonical<float, 24>).
+// Returns the sampled token; *margin receives top1 - top2 of the penalised
+// logits over [0, limit).
+static int ora_t2s_topk_sample(float* lg, int V, const int32_t* hist, size_t n_hist, int eos_allowed,
+                               const ora_sampling* sp, std::mt19937_64* rng, float* margin) {
+  const int limit = eos_allowed ? V : V - 1;
+  std::vector<unsigned char> mark(static_cast<size_t>(V), 0);
+  for (size_t i = 0; i < n_hist; ++i) {
+    const int c = hist[i];
+    if (c < 0 || c >= limit || mark[c]) continue;
+    mark[c] = 1;
+    float& v = lg[c];
+    v = v < 0.f ? v * sp->rep_penalty : v / sp->rep_penalty;
+  }
+  if (margin) {
+    float b = -INFINITY, s2 = -INFINITY;
+    int bi = -1;
+    for (int c = 0; c < limit; ++c)
+      if (lg[c] > b) {
+        b = lg[c];
+        bi = c;
+      }
+    for (int c = 0; c < limit; ++c)
+      if (c != bi && lg[c] > s2) s2 = lg[c];
+    *margin = b - s2;
+  }
+  const int k = sp->top_k > limit ? limit : (sp->top_k < 1 ? 1 : sp->top_k);
+  std::vector<int> idxs(static_cast<size_t>(limit));
+  std::vector<float> vals(static_cast<size_t>(limit));
+  for (int c = 0; c < limit; ++c) {
+    idxs[c] = c;
+    vals[c] = lg[c];
+  }
+  for (int i = 0; i < k; ++i) {
+    int max_j = i;
+    float max_v = vals[i];
+    for (int j = i + 1; j < limit; ++j)
+      if (vals[j] > max_v) {
+        max_v = vals[j];
+        max_j = j;
+      }
+    if (max_j != i) {
+      std::swap(vals[i], vals[max_j]);
+      std::swap(idxs[i], idxs[max_j]);
+    }
+  }
+  if (sp->temperature <= 0.f) {
+    int best = idxs[0];
+    float bv = vals[0];
+    for (int i = 1; i < k; ++i)
+      if (vals[i] > bv) {
+        bv = vals[i];
+        best = idxs[i];
+      }
+    return best;
+  }
+  if (sp->temperature != 1.0f)
+    for (int i = 0; i < k; ++i) vals[i] = vals[i] / sp->temperature;
+  float max_logit = vals[0];
+  for (int i = 1; i < k; ++i)
+    if (vals[i] > max_logit) max_logit = vals[i];
+  float sum_exp = 0.f;
+  for (int i = 0; i < k; ++i) {
+    vals[i] = exp_det(vals[i] - max_logit);
+    sum_exp = sum_exp + vals[i];
+  }
+  int keep = k;
+  if (sp->top_p < 1.0f) {
+    const float threshold = (1.f - sp->top_p) * sum_exp;
+    float cum = 0.f;
+    for (int i = k - 1; i >= 0; --i) {
+      cum = cum + vals[i];
+      if (cum >= threshold) {
+        keep = i + 1;
+        break;
+      }
+    }
+    if (keep < k) {
+      sum_exp = 0.f;
+      for (int i = 0; i < keep; ++i) sum_exp = sum_exp + vals[i];
+    }
+  }
+  const float u01 = static_cast<float>((*rng)()) * 0x1p-64f;
+  const float u = u01 * sum_exp;
+  float cdf = 0.f;
+  for (int i = 0; i < keep; ++i) {
+    cdf = cdf + vals[i];
+    if (u <= cdf) return idxs[i];
+  }
+  return idxs[keep - 1];
+}
+
 static int t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
                         uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt, size_t P,
                         size_t max_steps, int stop_on_eos, int32_t* tokens_out,
-                        float* margins_out, float* last_logits, float* all_logits, bool literal) {
+                        float* margins_out, float* last_logits, float* all_logits, bool literal,
+                        const ora_sampling* sp = nullptr) {
+  const bool topk = sp && sp->mode == 1;
+  std::mt19937_64 rng(sp ? sp->seed : 0);  // t2s_engine.cpp:1814-1818
   auto logits_head = literal ? gemv_sgemm_order : gemv32;  // predict_layer_fp, :704-708
   const size_t D = dm->d_model, L = dm->n_layers, V = dm->vocab;
   const int eos = static_cast<int>(V) - 1;
@@ -905,9 +1008,13 @@ static int t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16
     if (last_logits) std::memcpy(last_logits, logits.data(), V * sizeof(float));
     if (all_logits) std::memcpy(all_logits + idx * V, logits.data(), V * sizeof(float));
     int raw = -1;
-    const int s = ora_t2s_greedy_sample(logits.data(), static_cast<int>(V), hist.data(),
-                                        hist.size(), eos_allowed, &raw);
-    if (margins_out) {
+    float tk_margin = 0.f;
+    const int s = topk ? ora_t2s_topk_sample(logits.data(), static_cast<int>(V), hist.data(),
+                                             hist.size(), eos_allowed, sp, &rng, &tk_margin)
+                       : ora_t2s_greedy_sample(logits.data(), static_cast<int>(V), hist.data(),
+                                               hist.size(), eos_allowed, &raw);
+    if (topk && margins_out) margins_out[idx] = tk_margin;
+    if (!topk && margins_out) {
       const int limit = eos_allowed ? static_cast<int>(V) : static_cast<int>(V) - 1;
       float second = -INFINITY;
       for (int c = 0; c < limit; ++c)
@@ -941,6 +1048,14 @@ int ora_t2s_generate(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t*
                      float* margins_out, float* last_logits) {
   return t2s_generate(dm, w, kc, vc, cap, prefix, prompt, P, max_steps, stop_on_eos, tokens_out,
                       margins_out, last_logits, nullptr, false);
+}
+
+int ora_t2s_generate_sampled(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,
+                             uint16_t* vc, size_t cap, size_t prefix, const int32_t* prompt,
+                             size_t P, size_t max_steps, int stop_on_eos, const ora_sampling* sp,
+                             int32_t* tokens_out, float* margins_out) {
+  return t2s_generate(dm, w, kc, vc, cap, prefix, prompt, P, max_steps, stop_on_eos, tokens_out,
+                      margins_out, nullptr, nullptr, false, sp);
 }
 
 int ora_t2s_generate_ex(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16_t* kc,

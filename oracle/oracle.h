@@ -222,6 +222,26 @@ int ora_t2s_generate_ex(const ora_t2s_dims* d, const ora_t2s_weights* w,
                         size_t max_steps, int stop_on_eos, int literal,
                         int32_t* tokens_out, float* margins_out, float* all_logits);
 
+/* SamplingParams (t2s_engine.hpp:69-77): mode 0 greedy, 1 top-k. */
+typedef struct {
+  int mode;
+  int top_k;
+  float top_p;
+  float temperature;
+  float rep_penalty;
+  unsigned long long seed;
+} ora_sampling;
+
+/* ora_t2s_generate with sampling params: mode 1 samples every step with
+ * topk_sample (t2s_engine.cpp:1640-1737) from a std::mt19937_64 seeded with
+ * sp->seed (t2s_engine.cpp:1814-1818); margins_out receives top1 - top2 of
+ * the penalised logits. */
+int ora_t2s_generate_sampled(const ora_t2s_dims* d, const ora_t2s_weights* w,
+                             uint16_t* kcache, uint16_t* vcache, size_t cap,
+                             size_t prefix, const int32_t* prompt, size_t P,
+                             size_t max_steps, int stop_on_eos, const ora_sampling* sp,
+                             int32_t* tokens_out, float* margins_out);
+
 /* ---- encoders (BERT / HuBERT post-LN layer) ---------------------------- */
 typedef struct {
   int layers, hidden, heads, ffn;
