@@ -75,6 +75,14 @@ SIGNATURES = {
     "gsvk_t2s_set_decode_ctas": (c_int, [_vp, c_int]),
     "gsvk_t2s_decode_kernel": (c_int, [_vp]),
     "gsvk_t2s_set_sampling": (c_int, [_vp, _vp]),
+    "gsvk_gsv_open": (c_int, [ctypes.c_char_p, _vp]),
+    "gsvk_gsv_close": (c_int, [_vp]),
+    "gsvk_gsv_count": (_sz, [_vp]),
+    "gsvk_gsv_model_name": (ctypes.c_char_p, [_vp]),
+    "gsvk_gsv_config": (ctypes.c_char_p, [_vp, _vp]),
+    "gsvk_gsv_tensor_at": (c_int, [_vp, _sz, _vp]),
+    "gsvk_gsv_find": (c_int, [_vp, ctypes.c_char_p, _vp]),
+    "gsvk_t2s_create_from_gsv": (c_int, [_vp, c_int, _vp]),
     "gsvk_t2s_read_trace": (c_int, [_vp, _vp, _sz]),
     "gsvk_attention_workspace_floats": (_sz, [_sz, _sz, _sz]),
     "gsvk_attention_decode": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp, _vp, _vp]),
@@ -446,6 +454,71 @@ class T2SHostWeights(ctypes.Structure):
                                    "n1g", "n1b", "n2g", "n2b", "wpred", "audio_emb")]
 
 
+class GsvTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("rank", ctypes.c_uint32),
+                ("dims", ctypes.c_uint32 * 8), ("src_dtype", c_int), ("numel", ctypes.c_uint64),
+                ("f32", _vp), ("f16", _vp)]
+
+
+class GsvFile:
+    """A GSV1 weight container opened through gsvk_gsv_open (host memory)."""
+
+    def __init__(self, path: str):
+        h = c_void_p()
+        check(lib().gsvk_gsv_open(os.fsencode(path), ctypes.byref(h)))
+        self.h = h
+
+    def __len__(self):
+        return lib().gsvk_gsv_count(self.h)
+
+    @property
+    def model_name(self) -> str:
+        return lib().gsvk_gsv_model_name(self.h).decode()
+
+    @property
+    def config(self) -> str:
+        n = ctypes.c_size_t()
+        return lib().gsvk_gsv_config(self.h, ctypes.byref(n)).decode()
+
+    def _arrays(self, t):
+        import numpy as np
+
+        shape = tuple(t.dims[:t.rank])
+        f32 = f16 = None
+        if t.f32:
+            f32 = np.ctypeslib.as_array(ctypes.cast(t.f32, ctypes.POINTER(c_float)),
+                                        shape=(t.numel,)).reshape(shape).copy()
+        if t.f16:
+            f16 = np.ctypeslib.as_array(ctypes.cast(t.f16, ctypes.POINTER(ctypes.c_uint16)),
+                                        shape=(t.numel,)).reshape(shape).copy()
+        return t.name.decode(), shape, t.src_dtype, f32, f16
+
+    def tensor(self, name: str):
+        """(name, shape, src_dtype, fp32 array or None, fp16 bits or None)."""
+        t = GsvTensor()
+        check(lib().gsvk_gsv_find(self.h, name.encode(), ctypes.byref(t)))
+        return self._arrays(t)
+
+    def tensors(self):
+        out = []
+        for i in range(len(self)):
+            t = GsvTensor()
+            check(lib().gsvk_gsv_tensor_at(self.h, i, ctypes.byref(t)))
+            out.append(self._arrays(t))
+        return out
+
+    def close(self):
+        if self.h:
+            lib().gsvk_gsv_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class T2SSampling(ctypes.Structure):
     _fields_ = [("mode", c_int), ("top_k", c_int), ("top_p", c_float), ("temperature", c_float),
                 ("rep_penalty", c_float), ("seed", ctypes.c_ulonglong)]
@@ -454,6 +527,22 @@ class T2SSampling(ctypes.Structure):
 class T2S:
     """Device T2S engine (ar::T2SEngine).  `model` is a dict of numpy arrays in
     the reference layouts (see workloads.t2s_model)."""
+
+    @classmethod
+    def from_gsv(cls, gsv: "GsvFile", cap: int):
+        """T2SEngine(const GsvFile&) on the device (gsvk_t2s_create_from_gsv)."""
+        import json
+
+        self = cls.__new__(cls)
+        mc = json.loads(gsv.config)["model_config"]["model"]
+        self.model = dict(n_layers=int(mc["n_layer"]), d_model=int(mc["hidden_dim"]),
+                          vocab=int(mc["vocab_size"]))
+        self._keep = {}
+        h = c_void_p()
+        check(lib().gsvk_t2s_create_from_gsv(gsv.h, cap, ctypes.byref(h)))
+        self.h = h
+        self.cap = cap
+        return self
 
     def __init__(self, model: dict, cap: int):
         import numpy as np

@@ -369,6 +369,38 @@ typedef struct {
   const uint16_t* audio_emb;
 } gsvk_t2s_host_weights;
 int gsvk_t2s_create(const gsvk_t2s_config* cfg, const gsvk_t2s_host_weights* w, gsvk_t2s_t* out);
+
+/* ---- .gsv weight container (GsvFile, src/runtime/gsv_loader.hpp:50-114;
+ * GSV1 format per tools/convert.py:3-28) -------------------------------- */
+/* Opens and validates a GSV1 file (mapped read-only; the rules of the
+ * reference loader: magic, version, truncation, rank <= 8, known dtype,
+ * segment sizes matching the shape, 64-byte aligned in-file segments, flag
+ * bit 0 equal to the presence of fp16 segments).  Host-only: needs no GPU. */
+typedef struct gsvk_gsv* gsvk_gsv_t;
+typedef struct {
+  const char* name;
+  uint32_t rank;
+  uint32_t dims[8];
+  int src_dtype;          /* 1 fp32, 2 fp16 (the checkpoint's type) */
+  uint64_t numel;
+  const float* f32;       /* fp32 copy (host, in the mapping) or NULL (slim fp16-only) */
+  const uint16_t* f16;    /* fp16 copy or NULL */
+} gsvk_gsv_tensor;
+int gsvk_gsv_open(const char* path, gsvk_gsv_t* out);
+int gsvk_gsv_close(gsvk_gsv_t f);
+size_t gsvk_gsv_count(gsvk_gsv_t f);
+const char* gsvk_gsv_model_name(gsvk_gsv_t f);
+const char* gsvk_gsv_config(gsvk_gsv_t f, size_t* len); /* the embedded JSON */
+int gsvk_gsv_tensor_at(gsvk_gsv_t f, size_t i, gsvk_gsv_tensor* out);
+int gsvk_gsv_find(gsvk_gsv_t f, const char* name, gsvk_gsv_tensor* out);
+/* T2SEngine(const GsvFile&) (t2s_engine.cpp:544-630) on the device: the
+ * dimensions from the embedded config (model_config.model hidden_dim, head,
+ * linear_units, n_layer, vocab_size; embedding_dim == hidden_dim and EOS ==
+ * vocab_size - 1 when present), the per-layer h.layers.<l>.* tensors,
+ * ar_predict_layer.weight, ar_audio_embedding and ar_audio_position.alpha,
+ * uploaded into a gsvk_t2s handle with `cap` KV slots.  The file may be
+ * closed afterwards. */
+int gsvk_t2s_create_from_gsv(gsvk_gsv_t f, int cap, gsvk_t2s_t* out);
 int gsvk_t2s_destroy(gsvk_t2s_t h);
 /* Copies a KV prefix (fp16 [L][src_rows][D] for K and V, host or device
  * memory) into slots [0, prefix) of every layer's cache. */
