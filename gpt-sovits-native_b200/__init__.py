@@ -75,6 +75,7 @@ SIGNATURES = {
     "gsvk_t2s_set_decode_ctas": (c_int, [_vp, c_int]),
     "gsvk_t2s_decode_kernel": (c_int, [_vp]),
     "gsvk_t2s_set_sampling": (c_int, [_vp, _vp]),
+    "gsvk_set_spin_limit_for_test": (c_int, [ctypes.c_uint32]),
     "gsvk_gsv_open": (c_int, [ctypes.c_char_p, _vp]),
     "gsvk_gsv_close": (c_int, [_vp]),
     "gsvk_gsv_count": (_sz, [_vp]),

@@ -992,6 +992,14 @@ using namespace gsvk;
 struct gsvk_t2s : gsvk::T2SEngine {};
 
 namespace {
+// gsvk_set_spin_limit_for_test: 0 = the kernels' own budgets.
+uint32_t& test_spin_limit() {
+  static uint32_t v = 0;
+  return v;
+}
+}  // namespace
+
+namespace {
 
 // Decode launch plan for G persistent CTAs: weight slices sized for the
 // largest CTA (rows / G rounded up), two layer buffers and the persistent
@@ -1476,6 +1484,7 @@ int gsvk_t2s_decode(gsvk_t2s_t h, size_t prefix, const int32_t* prompt_dev, size
     }
     FlowArgs fa = h->flow;
     fa.epoch0 = h->flow_epoch;
+    fa.spin = test_spin_limit() ? test_spin_limit() : kFlSpin;
     h->flow_epoch += (uint32_t)need;
     cudaLaunchConfig_t lc{};
     lc.gridDim = dim3(h->flow_grid);
@@ -1531,6 +1540,11 @@ int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind) {
 }
 
 int gsvk_t2s_decode_kernel(gsvk_t2s_t h) { return h ? h->decode_kind : 0; }
+
+int gsvk_set_spin_limit_for_test(uint32_t polls) {
+  test_spin_limit() = polls;
+  return GSVK_OK;
+}
 
 int gsvk_t2s_set_sampling(gsvk_t2s_t h, const gsvk_t2s_sampling* sp) {
   if (!h) return fail(GSVK_ERR_INVALID, "t2s_set_sampling: null handle");

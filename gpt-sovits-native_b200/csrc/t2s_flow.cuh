@@ -95,6 +95,7 @@ struct FlowArgs {
   int vp;           // V rounded up to even
   int cs;           // CTAs per cluster (the first H clusters each own a head)
   uint32_t epoch0;  // this launch's epochs are epoch0 + 1 ...
+  uint32_t spin;    // polls of one exchange word pair before it gives up
   FlLayout y;
 };
 
@@ -118,7 +119,7 @@ __device__ __forceinline__ bool xw_ready(uint64_t a, uint64_t b, uint32_t ep) {
 // recorded a failure in the status word, or the spin budget ran out (which
 // records GSVK_ERR_TIMEOUT).  Ends with a CTA barrier.
 __device__ __forceinline__ bool fl_poll(const uint64_t* X, int n, uint32_t ep, float* dst,
-                                        uint32_t* status, bool failed) {
+                                        uint32_t* status, bool failed, uint32_t spin) {
   const int np = n >> 1;
   uint64_t a[kFlMaxPairs], b[kFlMaxPairs];
   bool ok = !failed;
@@ -141,16 +142,14 @@ __device__ __forceinline__ bool fl_poll(const uint64_t* X, int n, uint32_t ep, f
         if (p < np && !xw_ready(a[u], b[u], ep)) all = false;
       }
       if (all) break;
-      if ((it & 255u) == 255u) {
-        if (*reinterpret_cast<volatile uint32_t*>(status) != 0) {
-          ok = false;
-          break;
-        }
-        if (it > kFlSpin) {
-          atomicExch(status, DEV_TIMEOUT);
-          ok = false;
-          break;
-        }
+      if (it >= spin) {
+        atomicExch(status, DEV_TIMEOUT);
+        ok = false;
+        break;
+      }
+      if ((it & 255u) == 255u && *reinterpret_cast<volatile uint32_t*>(status) != 0) {
+        ok = false;
+        break;
       }
 #pragma unroll
       for (int u = 0; u < kFlMaxPairs; ++u) {
@@ -619,7 +618,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // every member of the cluster is running before any distributed
   // shared-memory store
   fl_cluster_sync();
-  if (!mbar_wait(&mbar[2], 0, m.status)) failed = true;
+  bool logits_pending = true;
+  if (mbar_wait(&mbar[2], 0, m.status))
+    logits_pending = false;
+  else
+    failed = true;
   failed = __syncthreads_or(failed ? 1 : 0) != 0;
 
   const uint32_t rec_remote = cluster_addr(rec, 0);  // the merger's chunk records
@@ -639,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* lg = m.logits;  // step 0: the prompt's logits (an earlier launch)
     if (idx > 0) {
       const uint32_t ep = ep_step;  // the previous step's logits epoch
-      if (!fl_poll(f.xlog + static_cast<size_t>(ep & 1u) * f.vp, f.vp, ep, act, m.status, failed))
+      if (!fl_poll(f.xlog + static_cast<size_t>(ep & 1u) * f.vp, f.vp, ep, act, m.status, failed, f.spin))
         failed = true;
       lg = act;
     }
@@ -756,14 +759,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint16_t* W2 = W1 + static_cast<size_t>(Y.m1) * D;
       const float* lnb = reinterpret_cast<const float*>(wb + Y.ln_off);
       // ---------------------------------------------- layer input, QKV rows
-      if (!failed && !mbar_wait(&mbar[b], (phase >> b) & 1u, m.status)) failed = true;
-      phase ^= 1u << b;
-      pending &= ~(1u << b);
+      // a copy that was not waited for (after a failure) stays pending: the
+      // exit drain waits for it, so no bulk copy outlives the CTA
+      if (!failed) {
+        if (mbar_wait(&mbar[b], (phase >> b) & 1u, m.status)) {
+          phase ^= 1u << b;
+          pending &= ~(1u << b);
+        } else {
+          failed = true;
+        }
+      }
       if (tid < nq + no + na + nb) bsm[tid] = bias_next;
       if (l > 0) {
         GSVK_FTR(16 + 16 * l + 14);
         if (!fl_poll(f.xxpre + static_cast<size_t>((ep - 1) & 1u) * D, D, ep - 1, xs, m.status,
-                     failed))
+                     failed, f.spin))
           failed = true;
         GSVK_FTR(16 + 16 * l + 15);
         fl_ln(xs, lnb + 2 * D, lnb + 3 * D, D, m.eps, red, act);  // LN2 of layer l - 1
@@ -819,14 +829,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int slot = tid >> 6;
         float* ew = slots + slot * (kChunk + 8);
         for (int rd = 0; rd < (is_head ? rounds : 0); ++rd) {
-          if (rd > 0) {  // later rounds: refill the tiles (all slots are done with them)
-            __syncthreads();
-            if (tid == 0 && !failed) issue_tiles(l, nch, rd);
+          if (rd > 0 && !failed && !tiles_armed) {  // later rounds: refill the tiles
+            __syncthreads();                           // (all slots are done with them)
+            if (tid == 0) issue_tiles(l, nch, rd);
+            tiles_armed = tiles_issued(nch, rd);
           }
-          const bool armed = rd == 0 ? tiles_armed : tiles_issued(nch, rd);
-          if (armed) {
-            if (!failed && !mbar_wait(&mbar[3], tile_uses & 1u, m.status)) failed = true;
-            ++tile_uses;
+          // tiles_armed: a tile copy in flight; one that was not waited for
+          // (after a failure) stays armed for the exit drain
+          if (tiles_armed && !failed) {
+            if (mbar_wait(&mbar[3], tile_uses & 1u, m.status)) {
+              ++tile_uses;
+              tiles_armed = false;
+            } else {
+              failed = true;
+            }
           }
           failed = __syncthreads_or(failed ? 1 : 0) != 0;
           if (rd == 0) GSVK_FTR(16 + 16 * l + 11);
@@ -846,7 +862,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                          rec_remote + static_cast<uint32_t>(ch) * rec_floats<HD>() * 4u);
           }
         }
-        tiles_armed = false;
       }
       GSVK_FTR(16 + 16 * l + 2);
       if (is_head && rank == cs - 1 && tid == kThreads - 32) bulk_wait<0>();  // the K/V row is in the cache before anyone reads it
@@ -863,11 +878,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       {  // the next attention's tiles (this step's next layer, or the next step's first)
         const int nl = l + 1 < L ? l + 1 : 0;
         const int nn = l + 1 < L ? nch : (len + 1 + kChunk - 1) / kChunk;
-        if (is_head && tid == 0 && !failed) issue_tiles(nl, nn, 0);
-        tiles_armed = is_head && !failed && tiles_issued(nn, 0);
+        if (is_head && !failed && !tiles_armed) {
+          if (tid == 0) issue_tiles(nl, nn, 0);
+          tiles_armed = tiles_issued(nn, 0);
+        }
       }
       // ------------------------------------------------ out-proj rows
-      if (!fl_poll(f.xattn + static_cast<size_t>(par) * D, D, ep, act, m.status, failed)) failed = true;
+      if (!fl_poll(f.xattn + static_cast<size_t>(par) * D, D, ep, act, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 4);
       for (int r = o0 + warp; r < o1; r += kWarps) {
         const float acc = warp_dot32(Wo + static_cast<size_t>(r - o0) * D, act, D);
@@ -876,14 +893,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                  __fadd_rn(__fadd_rn(acc, bsm[nq + r - o0]), xs[r]), ep);
       }
       // ------------------------------------------- LN1, W1 rows + ReLU
-      if (!fl_poll(f.xhpre + static_cast<size_t>(par) * D, D, ep, hs, m.status, failed)) failed = true;
+      if (!fl_poll(f.xhpre + static_cast<size_t>(par) * D, D, ep, hs, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 5);
       fl_ln(hs, lnb, lnb + D, D, m.eps, red, act);
       GSVK_FTR(16 + 16 * l + 12);
       fl_w1_rows(W1, act, a0, a1, D, bsm + nq + no, f.xff + static_cast<size_t>(par) * F, ep);
       GSVK_FTR(16 + 16 * l + 6);
       // ------------------------------------------------------- W2 rows
-      if (!fl_poll(f.xff + static_cast<size_t>(par) * F, F, ep, act, m.status, failed)) failed = true;
+      if (!fl_poll(f.xff + static_cast<size_t>(par) * F, F, ep, act, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 7);
       {
         uint64_t* xx = f.xxpre + static_cast<size_t>(par) * D;
@@ -914,7 +931,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       const uint32_t ep_x = ep_step + static_cast<uint32_t>(L);  // layer L - 1
       const uint32_t ep_l = ep_step + static_cast<uint32_t>(L) + 1;
-      if (!fl_poll(f.xxpre + static_cast<size_t>(ep_x & 1u) * D, D, ep_x, xs, m.status, failed))
+      if (!fl_poll(f.xxpre + static_cast<size_t>(ep_x & 1u) * D, D, ep_x, xs, m.status, failed, f.spin))
         failed = true;
       fl_ln(xs, lnf, lnf + D, D, m.eps, red, nullptr);
       uint64_t* xl = f.xlog + static_cast<size_t>(ep_l & 1u) * f.vp;
@@ -937,6 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int bb = 0; bb < 2; ++bb)
       if ((pending >> bb) & 1u) mbar_wait(&mbar[bb], (phase >> bb) & 1u, m.status);
     if (tiles_armed) mbar_wait(&mbar[3], tile_uses & 1u, m.status);
+    if (logits_pending) mbar_wait(&mbar[2], 0, m.status);
     if (c == 0 && a.n_out) *a.n_out = n_out;
   }
   bulk_wait<0>();  // the K/V row stores of the thread that issued them

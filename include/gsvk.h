@@ -461,6 +461,13 @@ int gsvk_t2s_read_trace(gsvk_t2s_t h, unsigned long long* host_out, size_t n);
  * the current choice (1, 2 or 3). */
 int gsvk_t2s_set_decode_kernel(gsvk_t2s_t h, int kind);
 int gsvk_t2s_decode_kernel(gsvk_t2s_t h);
+/* Failure injection for tests (no counterpart in the reference): every
+ * exchange poll of decode kernel 3 gives up after `polls` polls instead of
+ * its own budget (seconds), records GSVK_ERR_TIMEOUT in the device status and
+ * winds the launch down (no wait, every bulk copy drained before exit), so a
+ * test can make a real device wait run out without faulting or hanging the
+ * GPU.  0 restores the default.  Process-wide. */
+int gsvk_set_spin_limit_for_test(uint32_t polls);
 /* Sampling of the decode steps: SamplingParams (t2s_engine.hpp:69-77) and
  * topk_sample (t2s_engine.cpp:1640-1737).  mode 0 (the default) is greedy;
  * mode 1 applies the repetition penalty rep_penalty once per distinct history

@@ -160,3 +160,35 @@ def test_decode_cta_count_does_not_change_results(dev, small):
     np.testing.assert_array_equal(toks, out[0][0])
     eng.close()
     assert dev.device_status() == 0
+
+
+def test_exchange_wait_timeout_is_reported_and_recovers(dev, ora, small):
+    """Failure detection without a fault: with the test spin limit every
+    exchange poll of the per-head cluster decode gives up after a few polls,
+    so the launch records GSVK_ERR_TIMEOUT, winds down (no wait, every bulk
+    copy drained) and the host call reports it; the next healthy generate on
+    the same handle and context matches the oracle bit for bit."""
+    m = small
+    prefix, P, steps = 30, 8, 40
+    cap = prefix + P + steps
+    k0, v0 = dev.workloads.t2s_kv_prefix(m, cap, prefix, seed=12)
+    prompt = dev.workloads.t2s_prompt(P, m["vocab"], seed=13)
+    eng = dev.T2S(m, cap)
+    if eng.decode_kernel() != eng.DECODE_FLOW:
+        pytest.skip("the per-head cluster decode kernel does not fit this GPU")
+    lib = dev.lib()
+    try:
+        assert lib.gsvk_set_spin_limit_for_test(1) == 0
+        eng.load_kv(k0, v0, prefix)
+        with pytest.raises(dev.GsvkError) as ei:
+            eng.generate(prefix, prompt, steps, False)
+        assert ei.value.code == -4, ei.value  # GSVK_ERR_TIMEOUT
+    finally:
+        lib.gsvk_set_spin_limit_for_test(0)
+    assert dev.device_status() == 0  # the failing call read and cleared the status
+    eng.load_kv(k0, v0, prefix)
+    toks, marg = eng.generate(prefix, prompt, steps, False)
+    eng.close()
+    ref, ref_marg = ora.t2s_generate(m, k0.copy(), v0.copy(), prefix, prompt, steps, False)
+    np.testing.assert_array_equal(toks, ref)
+    np.testing.assert_array_equal(marg, ref_marg)
