@@ -33,8 +33,9 @@ sys.path.insert(0, ROOT)
 T2S_STEPS = 500
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one decode
 # launch divided by its algorithmic bytes, measured on a 20-step launch of the
-# same kernel; traffic grows in proportion to the decode passes.
-T2S_TRAFFIC_RATIO = 0.986
+# default decode kernel (t2s_flow_kernel: 3.1665 GB against 3.1980 GB);
+# traffic grows in proportion to the decode passes.
+T2S_TRAFFIC_RATIO = 0.990
 T2S_PREFIX = 256
 T2S_PROMPT = 64
 L2_BYTES = 126 * 1024 * 1024
@@ -455,7 +456,8 @@ def run_t2s(args, rank, local, world):
         "roofline": {"bound": "hbm", "kernel": kernel_name, "achieved": achieved,
                      "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": peak_kind, "traffic": T2S_TRAFFIC_RATIO * alg,
-                     "traffic_note": "ncu DRAM bytes of a 20-step launch, scaled per pass",
+                     "traffic_note": "ncu DRAM bytes of a 20-step launch of the same kernel, "
+                                     "scaled per pass (profiles/t2s_flow_kernel_config2.md)",
                      "algorithmic_bytes_per_launch": alg,
                      "launch_ms": t_dec_max * 1e3},
     }
