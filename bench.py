@@ -199,6 +199,15 @@ def workload_meta(args, world):
                             "decode_steps_per_step": 32, "mean_kv_len": float(lens.mean()),
                             "global_batch": B * world, "parallelism": f"replicas x{world}",
                             "l2": "1.9 GB of weights + KV streamed per decode step"})
+    if wl == "gemv_t2s":
+        return dict(metric="T2S GEMV GB/s (one token's 97 GEMVs: 24 x {1536x512, 512x512, "
+                           "2048x512, 512x2048} + 1025x512)",
+                    unit="GB/s", dtype="f16 weights, f32 x and accumulate",
+                    data="synthetic (seeded N(0,0.02) weights, N(0,1) x)",
+                    config={"workload": "gemv_t2s (the T2S decode GEMV shapes, SURVEY 8d)",
+                            "launch": "CUDA graph of one token's 97 gemv_f16w_f32acc launches",
+                            "global_batch": world, "parallelism": f"replicas x{world}",
+                            "l2": f"{GEMV_SETS} rotated copies of the 152 MB weight set (> L2)"})
     raise ValueError(wl)
 
 
@@ -309,6 +318,17 @@ def cpu_sampler(args, threads):
                 oracle.t2s_greedy_sample(lg, hist, True)
         return fn, len(lens), (f"oracle T2S decode: one token for each of the first {len(lens)} "
                                f"utterances (KV lengths {', '.join(str(int(v)) for v in lens)})")
+    if wl == "gemv_t2s":
+        m = W.t2s_model(seed=0)
+        x = np.random.default_rng(0).standard_normal(2048).astype(np.float32)
+        mats = [m[k][i] for i in range(m["n_layers"]) for k in ("wqkv", "wout", "w1", "w2")]
+        mats.append(m["wpred"])
+
+        def fn():
+            for w in mats:
+                oracle.gemv_f16w_f32acc(w, x[:w.shape[1]])
+        return fn, sum(w.nbytes for w in mats) / 1e9, (
+            "oracle gemv_f16w_f32acc over one token's 97 weight matrices (152 MB)")
     raise ValueError(wl)
 
 
@@ -547,6 +567,145 @@ def run_gemm1(args, rank, local, world):
                          "algorithmic_bytes_per_gemm": alg_bytes,
                          "tensor_frac": flops / world / t / 1e12 / tf,
                          "note": "AI 97 flop/B is below the ridge: HBM-bound"}}
+    if clk:
+        line["clocks"] = clk
+    return line
+
+
+# ------------------------------------------------ T2S GEMV shapes (a1, a2)
+GEMV_SETS = 4
+GEMV_SHAPES = ((1536, 512), (512, 512), (2048, 512), (512, 2048), (1025, 512))
+
+
+def run_gemv_t2s(args, rank, local, world):
+    """One token's GEMVs as standalone gemv_f16w_f32acc launches (the a1
+    kernel at the five T2S shapes), GEMV_SETS rotated weight sets so every
+    launch streams its weights from HBM; then, per shape, the same kernel on
+    its own over >= 256 MB of rotated copies, and the M=64 product through
+    the tensor-core skinny GEMM against 64 fp16-x GEMV launches."""
+    import numpy as np
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    m = g.workloads.t2s_model(seed=rank)
+    L = m["n_layers"]
+    names = ("wqkv", "wout", "w1", "w2")
+    base = [torch.from_numpy(m[k][i].view(np.float16)).to(dev) for i in range(L) for k in names]
+    base.append(torch.from_numpy(m["wpred"].view(np.float16)).to(dev))
+    sets = [[w.clone() for w in base] for _ in range(GEMV_SETS)]
+    x = torch.randn(2048, device=dev)
+    ys = [torch.empty(w.shape[0], device=dev) for w in base]
+    tok_bytes = sum(w.numel() * 2 + w.shape[1] * 4 + w.shape[0] * 4 for w in base)
+
+    def token(ws):
+        for w, y in zip(ws, ys):
+            g.gemv_f16w_f32acc(w, x[:w.shape[1]], y)
+
+    token(sets[0])
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for ws in sets:
+            token(ws)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler()
+    barrier(world)
+    clocks.start()
+    start.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    t = max_over_ranks(start.elapsed_time(end) * 1e-3, world)
+    launches = len(base) * GEMV_SETS * args.steps
+    value = tok_bytes * GEMV_SETS * args.steps * world / t / 1e9
+    # e2e: x from pinned host memory and every y back to it, per token
+    x_pin = x.cpu().pin_memory()
+    y_pin = torch.empty(sum(y.numel() for y in ys)).pin_memory()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        for ws in sets:
+            x.copy_(x_pin, non_blocking=True)
+            token(ws)
+            o = 0
+            for y in ys:
+                y_pin[o:o + y.numel()].copy_(y, non_blocking=True)
+                o += y.numel()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e-3, world)
+    del graph, sets
+    torch.cuda.empty_cache()
+    hbm, tf, kind = measured_peaks()
+    shapes = {}
+    for N, K in GEMV_SHAPES:
+        wb = N * K * 2
+        R = max(4, -(-(256 << 20) // wb))
+        ws = torch.randn(R, N, K, device=dev).mul_(0.02).half()
+        xv, xh = torch.randn(K, device=dev), torch.randn(64, K, device=dev).half()
+        y, y64 = torch.empty(N, device=dev), torch.empty(64, N, device=dev)
+        reps = 256
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for j in range(reps):
+                g.gemv_f16w_f32acc(ws[j % R], xv, y)
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(4):
+            gr.replay()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        us1 = a.elapsed_time(b) * 1e3 / (4 * reps)
+        gb1 = (wb + K * 4 + N * 4) / us1 / 1e3
+        # M = 64: one skinny tensor-core GEMM vs 64 fp16-x GEMV launches
+        tc = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(tc):
+            for j in range(64):
+                g.gemm_ex(xh, ws[j % R], c=y64)
+        gv = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gv):
+            for j in range(8):
+                for r in range(64):
+                    g.gemv_f16x_fmlal(ws[j % R], xh[r], y64[r])
+        res = []
+        for gg, n in ((tc, 64), (gv, 8)):
+            gg.replay()
+            torch.cuda.synchronize(dev)
+            a.record(stream)
+            for _ in range(4):
+                gg.replay()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            res.append(a.elapsed_time(b) * 1e3 / (4 * n))
+        shapes[f"{N}x{K}"] = {"copies": R, "gemv_us": round(us1, 3), "gemv_gbs": round(gb1, 1),
+                              "gemv_frac": round(gb1 / hbm, 4),
+                              "m64_tensor_us": round(res[0], 3), "m64_gemv_x64_us": round(res[1], 3)}
+        del ws, gr, tc, gv
+        torch.cuda.empty_cache()
+    line = {"metric": workload_meta(args, world)["metric"], "value": value, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "e2e": {"value": tok_bytes * GEMV_SETS * args.steps * world / t_e2e / 1e9,
+                    "unit": "GB/s", "h2d_bytes_per_step": x_pin.numel() * 4 * GEMV_SETS,
+                    "d2h_bytes_per_step": y_pin.numel() * 4 * GEMV_SETS},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": "gemv_vec_kernel", "achieved": value / world,
+                         "peak": hbm, "unit": "GB/s", "frac": value / world / hbm,
+                         "peak_source": kind, "traffic": None,
+                         "algorithmic_bytes_per_token": tok_bytes},
+            "shapes": shapes}
     if clk:
         line["clocks"] = clk
     return line
@@ -858,7 +1017,7 @@ def run_t2s_batch(args, rank, local, world):
 
 
 WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder": run_decoder,
-             "encoder": run_encoder, "t2s_decode_b64": run_t2s_batch, "gemm": run_gemm_shape}
+             "gemv_t2s": run_gemv_t2s, "encoder": run_encoder, "t2s_decode_b64": run_t2s_batch, "gemm": run_gemm_shape}
 
 
 def run_reference(args, rank, world):
@@ -925,6 +1084,8 @@ def main():
         meta = workload_meta(args, world)
         extra = {k: v for k, v in line.get("config", {}).items() if k not in meta["config"]}
         line.update(metric=meta["metric"], unit=meta["unit"], config=meta["config"])
+        line.setdefault("dtype", meta["dtype"])
+        line.setdefault("data", meta["data"])
         if extra:
             line["run"] = extra
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

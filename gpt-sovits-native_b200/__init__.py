@@ -76,6 +76,10 @@ SIGNATURES = {
     "gsvk_t2s_decode_kernel": (c_int, [_vp]),
     "gsvk_t2s_set_sampling": (c_int, [_vp, _vp]),
     "gsvk_set_spin_limit_for_test": (c_int, [ctypes.c_uint32]),
+    "gsvk_hubert_front_create": (c_int, [_vp, _vp, _vp]),
+    "gsvk_hubert_front_destroy": (c_int, [_vp]),
+    "gsvk_hubert_front_frames": (_sz, [_vp, _sz]),
+    "gsvk_hubert_front_forward": (c_int, [_vp, _vp, _sz, _vp, _vp]),
     "gsvk_gsv_open": (c_int, [ctypes.c_char_p, _vp]),
     "gsvk_gsv_close": (c_int, [_vp]),
     "gsvk_gsv_count": (_sz, [_vp]),
@@ -453,6 +457,62 @@ class T2SConfig(ctypes.Structure):
 class T2SHostWeights(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("wqkv", "bqkv", "wout", "bout", "w1", "b1", "w2", "b2",
                                    "n1g", "n1b", "n2g", "n2b", "wpred", "audio_emb")]
+
+
+class HubertFrontConfig(ctypes.Structure):
+    _fields_ = [("conv_dim", c_int * 7), ("conv_kernel", c_int * 7), ("conv_stride", c_int * 7),
+                ("hidden", c_int), ("pos_k", c_int), ("pos_groups", c_int), ("ln_eps", c_float),
+                ("max_samples", _sz)]
+
+
+class HubertFrontWeights(ctypes.Structure):
+    _fields_ = [("conv_w", _vp * 7)] + [(n, _vp) for n in (
+        "gn_g", "gn_b", "proj_ln_g", "proj_ln_b", "proj_w", "proj_b", "pos_w", "pos_b",
+        "enc_ln_g", "enc_ln_b")]
+
+
+class HubertFront:
+    """HuBERT feature front-end (gsvk_hubert_front_*): waveform -> encoder input."""
+
+    NAMES = ("gn_g", "gn_b", "proj_ln_g", "proj_ln_b", "proj_w", "proj_b", "pos_w", "pos_b",
+             "enc_ln_g", "enc_ln_b")
+
+    def __init__(self, model: dict, max_samples: int):
+        import numpy as np
+
+        self.hidden = model["hidden"]
+        conv = [np.ascontiguousarray(w) for w in model["conv_w"]]
+        keep = {n: np.ascontiguousarray(model[n]) for n in self.NAMES}
+        cfg = HubertFrontConfig((c_int * 7)(*model["conv_dim"]), (c_int * 7)(*model["conv_kernel"]),
+                                (c_int * 7)(*model["conv_stride"]), model["hidden"],
+                                model["pos_k"], model["pos_groups"], model["ln_eps"], max_samples)
+        w = HubertFrontWeights((_vp * 7)(*[a.ctypes.data for a in conv]),
+                               *[keep[n].ctypes.data for n in self.NAMES])
+        h = c_void_p()
+        check(lib().gsvk_hubert_front_create(ctypes.byref(cfg), ctypes.byref(w), ctypes.byref(h)))
+        self.h = h
+
+    def frames(self, n: int) -> int:
+        return lib().gsvk_hubert_front_frames(self.h, n)
+
+    def forward(self, wav, x=None, stream=None):
+        import torch
+
+        n = wav.numel()
+        x = x if x is not None else torch.empty(self.frames(n), self.hidden, device=wav.device)
+        check(lib().gsvk_hubert_front_forward(self.h, _ptr(wav), n, _ptr(x), _stream(stream)))
+        return x
+
+    def close(self):
+        if self.h:
+            lib().gsvk_hubert_front_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class GsvTensor(ctypes.Structure):

@@ -98,6 +98,118 @@ ENCODERS = {
 }
 
 
+HUBERT_FRONT = dict(conv_dim=(512,) * 7, conv_kernel=(10, 3, 3, 3, 3, 2, 2),
+                    conv_stride=(5, 2, 2, 2, 2, 2, 2), hidden=768, pos_k=128, pos_groups=16,
+                    ln_eps=1e-5)
+
+
+def hubert_front_model(seed=0, cfg=HUBERT_FRONT) -> dict:
+    """HuBERT feature front-end weights (hubert.cpp:93-160 layouts): conv
+    weights fp16 [512][in][k] ~ N(0, 1/fan_in), GroupNorm / LayerNorm gains
+    1+N(0,0.05) and biases N(0,0.02), projection fp16 [768][512] N(0,0.02)
+    and bias, positional conv fp32 [768][48][128] N(0, 1/fan_in) and bias."""
+    rng = np.random.default_rng(seed)
+    m = dict(cfg)
+    m["conv_w"] = []
+    ci = 1
+    for co, k in zip(cfg["conv_dim"], cfg["conv_kernel"]):
+        m["conv_w"].append(_f16(_normal(rng, (co, ci, k), 1.0 / np.sqrt(ci * k))))
+        ci = co
+    C0, C6, H = cfg["conv_dim"][0], cfg["conv_dim"][6], cfg["hidden"]
+    cg = H // cfg["pos_groups"]
+    m["gn_g"] = (1.0 + _normal(rng, (C0,), 0.05)).astype(np.float32)
+    m["gn_b"] = _normal(rng, (C0,), 0.02)
+    m["proj_ln_g"] = (1.0 + _normal(rng, (C6,), 0.05)).astype(np.float32)
+    m["proj_ln_b"] = _normal(rng, (C6,), 0.02)
+    m["proj_w"] = _f16(_normal(rng, (H, C6), 0.02))
+    m["proj_b"] = _normal(rng, (H,), 0.02)
+    m["pos_w"] = _normal(rng, (H, cg, cfg["pos_k"]), 1.0 / np.sqrt(cg * cfg["pos_k"]))
+    m["pos_b"] = _normal(rng, (H,), 0.02)
+    m["enc_ln_g"] = (1.0 + _normal(rng, (H,), 0.05)).astype(np.float32)
+    m["enc_ln_b"] = _normal(rng, (H,), 0.02)
+    return m
+
+
+def hubert_waveform(n=16000, seed=0):
+    """A waveform stand-in ~ N(0, 0.1) (the reference feeds 16 kHz audio)."""
+    return _normal(np.random.default_rng(seed + 7000), (n,), 0.1)
+
+
+SOVITS_LATENT = dict(ssl_dim=768, hidden=192, filter=768, heads=2, kernel=3, window=4,
+                     layers_ssl=3, layers_text=6, layers_2=3, mrte_hidden=512, mrte_heads=4,
+                     gin=1024, flows=4, wn_layers=4, wn_kernel=5, noise_scale=0.5,
+                     n_symbols=732, codebook=1024)
+
+
+def sovits_latent_model(seed=0, cfg=SOVITS_LATENT) -> dict:
+    """The SoVITS latent path's tensors under their .gsv names (enc_p.hpp,
+    enc_p_parts.hpp, mha.hpp, flow.hpp, quantizer.hpp): conv weights fp16
+    [out][in][k] ~ N(0, 1/fan_in), biases N(0, 0.02), LayerNorm gains
+    1+N(0,0.05), relative tables N(0, dk^-1/2) [1][2W+1][dk], text embedding
+    N(0, hidden^-1/2), codebook N(0,1) - the torch initialisers' scales."""
+    rng = np.random.default_rng(seed)
+    c = dict(cfg)
+    C, H, F, K = c["hidden"], c["heads"], c["filter"], c["kernel"]
+    t = {}
+
+    def conv(name, co, ci, k, wscale=1.0):
+        t[name + ".weight"] = _f16(_normal(rng, (co, ci, k), wscale / np.sqrt(ci * k)))
+        t[name + ".bias"] = _normal(rng, (co,), 0.02)
+
+    def mha(p, ch, heads, rel):
+        for n in ("q", "k", "v", "o"):
+            conv(f"{p}.conv_{n}", ch, ch, 1)
+        if rel:
+            dk = ch // heads
+            for n in ("k", "v"):
+                t[f"{p}.emb_rel_{n}"] = _normal(rng, (1, 2 * c["window"] + 1, dk), dk ** -0.5)
+
+    def encoder(p, nl):
+        for i in range(nl):
+            mha(f"{p}.attn_layers.{i}", C, H, True)
+            for j in (1, 2):
+                t[f"{p}.norm_layers_{j}.{i}.gamma"] = (1 + _normal(rng, (C,), 0.05)).astype(np.float32)
+                t[f"{p}.norm_layers_{j}.{i}.beta"] = _normal(rng, (C,), 0.02)
+            conv(f"{p}.ffn_layers.{i}.conv_1", F, C, K)
+            conv(f"{p}.ffn_layers.{i}.conv_2", C, F, K)
+
+    t["quantizer.vq.layers.0._codebook.embed"] = _normal(rng, (c["codebook"], c["ssl_dim"]), 1.0)
+    conv("enc_p.ssl_proj", C, c["ssl_dim"], 1)
+    encoder("enc_p.encoder_ssl", c["layers_ssl"])
+    encoder("enc_p.encoder_text", c["layers_text"])
+    encoder("enc_p.encoder2", c["layers_2"])
+    t["enc_p.text_embedding.weight"] = _normal(rng, (c["n_symbols"], C), C ** -0.5)
+    MH = c["mrte_hidden"]
+    mha("enc_p.mrte.cross_attention", MH, c["mrte_heads"], False)
+    conv("enc_p.mrte.c_pre", MH, C, 1)
+    conv("enc_p.mrte.text_pre", MH, C, 1)
+    conv("enc_p.mrte.c_post", C, MH, 1)
+    conv("enc_p.proj", 2 * C, C, 1)
+    nl = c["wn_layers"]
+    for f in range(c["flows"]):
+        p = f"flow.flows.{2 * f}"
+        conv(p + ".pre", C, C // 2, 1)
+        conv(p + ".enc.cond_layer", 2 * C * nl, c["gin"], 1)
+        for i in range(nl):
+            conv(f"{p}.enc.in_layers.{i}", 2 * C, C, c["wn_kernel"])
+            conv(f"{p}.enc.res_skip_layers.{i}", 2 * C if i + 1 < nl else C, C, 1)
+        conv(p + ".post", C // 2, C, 1, wscale=0.5)
+    c["tensors"] = t
+    return c
+
+
+def sovits_latent_inputs(n_codes, n_phones, cfg=SOVITS_LATENT, seed=0, noise=True):
+    """codes U[0, codebook), phones U[0, n_symbols), ge N(0,1) [gin],
+    ge_text N(0,1) [mrte_hidden], noise N(0,1) [hidden][2 n_codes]."""
+    rng = np.random.default_rng(seed + 9000)
+    codes = rng.integers(0, cfg["codebook"], n_codes).astype(np.int64)
+    phones = rng.integers(0, cfg["n_symbols"], n_phones).astype(np.int64)
+    ge = _normal(rng, (cfg["gin"],), 1.0)
+    ge_text = _normal(rng, (cfg["mrte_hidden"],), 1.0)
+    nz = _normal(rng, (cfg["hidden"], 2 * n_codes), 1.0) if noise else None
+    return codes, phones, ge, ge_text, nz
+
+
 def encoder_model(name: str, layers=None, seed=0) -> dict:
     """Encoder weights in the oracle / C-ABI layout: q, k, v rows fused as
     [L][3C][C]; N(0,0.02) fp16 matrices, N(0,0.02) fp32 biases, LayerNorm gain

@@ -299,6 +299,49 @@ int gsvk_encoder_forward(gsvk_encoder_t h, float* x, size_t batch, size_t seq, c
                          gsvk_stream_t stream);
 int gsvk_encoder_launches(gsvk_encoder_t h);
 
+/* ---- HuBERT feature front-end (hubert.cpp:439-580) ---------------------- */
+/* The 7-layer strided CNN feature extractor (valid convolutions, no bias;
+ * layer 0 with a per-channel GroupNorm: fp64 mean and biased variance over
+ * time; GELU after every layer), the feature projection (LayerNorm,
+ * Linear + bias on fp16 activations), the grouped positional convolution
+ * (pad pos_k/2, the first T of its T + 1 outputs, + bias, GELU, added to the
+ * projected features) and the encoder LayerNorm: waveform -> the input of
+ * the transformer layers (gsvk_encoder_forward).  Convolutions round their
+ * activations to fp16 and accumulate in fp32 on the tensor cores, as the
+ * reference's im2col + gemm_f16x_fmlal / AMX path does. */
+typedef struct gsvk_hubert_front* gsvk_hubert_front_t;
+typedef struct {
+  int conv_dim[7];      /* 512 x 7 */
+  int conv_kernel[7];   /* 10, 3, 3, 3, 3, 2, 2 */
+  int conv_stride[7];   /* 5, 2, 2, 2, 2, 2, 2 */
+  int hidden;           /* 768 */
+  int pos_k;            /* num_conv_pos_embeddings, 128 */
+  int pos_groups;       /* num_conv_pos_embedding_groups, 16 */
+  float ln_eps;         /* layer_norm_eps, 1e-5 */
+  size_t max_samples;   /* longest waveform a forward may take */
+} gsvk_hubert_front_config;
+/* HOST pointers, the reference's tensor layouts: conv_w[i] fp16
+ * [conv_dim[i]][in][k]; gn_* [conv_dim[0]]; proj_ln_* [conv_dim[6]];
+ * proj_w fp16 [hidden][conv_dim[6]], proj_b [hidden]; pos_w fp32
+ * [hidden][hidden/pos_groups][pos_k] (the weight-norm product, rounded to
+ * fp16 once at create, hubert.cpp:538-539), pos_b [hidden]; enc_ln_* [hidden]. */
+typedef struct {
+  const uint16_t* conv_w[7];
+  const float* gn_g; const float* gn_b;
+  const float* proj_ln_g; const float* proj_ln_b;
+  const uint16_t* proj_w; const float* proj_b;
+  const float* pos_w; const float* pos_b;
+  const float* enc_ln_g; const float* enc_ln_b;
+} gsvk_hubert_front_weights;
+int gsvk_hubert_front_create(const gsvk_hubert_front_config* cfg,
+                             const gsvk_hubert_front_weights* w, gsvk_hubert_front_t* out);
+int gsvk_hubert_front_destroy(gsvk_hubert_front_t h);
+/* Frames the CNN makes of n samples (0 when too short). */
+size_t gsvk_hubert_front_frames(gsvk_hubert_front_t h, size_t n);
+/* wav: DEVICE fp32 [n]; x: DEVICE fp32 [frames][hidden]. */
+int gsvk_hubert_front_forward(gsvk_hubert_front_t h, const float* wav, size_t n, float* x,
+                              gsvk_stream_t stream);
+
 /* ---- support primitives (a22) ------------------------------------------ */
 /* kern::layernorm (kern.cpp:27) applied to `rows` rows of n. y may equal x. */
 int gsvk_layernorm_rows(const float* x, const float* g, const float* b, float* y,

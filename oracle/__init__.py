@@ -99,6 +99,9 @@ def lib():
             "ora_t2s_decode_layer_literal": (None, [vp, vp, c_int, vp, sz, vp, vp]),
             "ora_t2s_generate_sampled": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp,
                                                  vp, vp]),
+            "ora_sovits_latent": (c_int, [vp, vp, sz, vp, sz, vp, sz, vp, vp, vp, vp, vp, vp]),
+            "ora_hubert_front_frames": (sz, [vp, sz]),
+            "ora_hubert_front": (None, [vp, vp, vp, sz, vp]),
             "ora_t2s_generate_ex": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, c_int, vp,
                                             vp, vp]),
         }
@@ -404,3 +407,76 @@ def encoder_layer(model: dict, layer: int, x: np.ndarray, B: int, T: int, valid=
                                                 "bi", "wf", "bf", "ln2g", "ln2b")])
     vd = None if valid is None else np.ascontiguousarray(valid, np.int32)
     lib().ora_encoder_layer(ctypes.byref(d), ctypes.byref(w), layer, _p(x), B, T, _p(vd))
+
+
+class HubertFrontCfg(ctypes.Structure):
+    _fields_ = [("conv_dim", c_int * 7), ("conv_kernel", c_int * 7), ("conv_stride", c_int * 7),
+                ("hidden", c_int), ("pos_k", c_int), ("pos_groups", c_int),
+                ("ln_eps", ctypes.c_double)]
+
+
+class HubertFrontWeights(ctypes.Structure):
+    _fields_ = [("conv_w", c_void_p * 7)] + [(n, c_void_p) for n in (
+        "gn_g", "gn_b", "proj_ln_g", "proj_ln_b", "proj_w", "proj_b", "pos_w", "pos_b",
+        "enc_ln_g", "enc_ln_b")]
+
+
+def hubert_front(model: dict, wav: np.ndarray) -> np.ndarray:
+    """hubert.cpp:476-580 on the CPU: waveform -> [frames][hidden]."""
+    c = HubertFrontCfg((c_int * 7)(*model["conv_dim"]), (c_int * 7)(*model["conv_kernel"]),
+                       (c_int * 7)(*model["conv_stride"]), model["hidden"], model["pos_k"],
+                       model["pos_groups"], model["ln_eps"])
+    w = HubertFrontWeights((c_void_p * 7)(*[_p(a) for a in model["conv_w"]]),
+                           *[_p(model[n]) for n in ("gn_g", "gn_b", "proj_ln_g", "proj_ln_b",
+                                                    "proj_w", "proj_b", "pos_w", "pos_b",
+                                                    "enc_ln_g", "enc_ln_b")])
+    wav = np.ascontiguousarray(wav, np.float32)
+    T = lib().ora_hubert_front_frames(ctypes.byref(c), wav.size)
+    out = np.zeros((T, model["hidden"]), np.float32)
+    lib().ora_hubert_front(ctypes.byref(c), ctypes.byref(w), _p(wav), wav.size, _p(out))
+    return out
+
+
+class Named(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("f32", c_void_p), ("f16", c_void_p),
+                ("numel", ctypes.c_uint64)]
+
+
+class SovitsLatentCfg(ctypes.Structure):
+    _fields_ = [(n, c_int) for n in (
+        "ssl_dim", "hidden", "filter", "heads", "kernel", "window", "layers_ssl", "layers_text",
+        "layers_2", "mrte_hidden", "mrte_heads", "gin", "flows", "wn_layers", "wn_kernel")] + [
+        ("noise_scale", c_float)]
+
+
+def named_tensors(tensors: dict):
+    """(ctypes array, keep-alive list) of ora_named for a name -> array dict:
+    uint16 arrays are fp16 bits, float32 arrays fp32."""
+    keep, arr = [], (Named * len(tensors))()
+    for i, (k, a) in enumerate(tensors.items()):
+        a = np.ascontiguousarray(a)
+        keep.append(a)
+        f16 = a.dtype == np.uint16
+        arr[i] = Named(k.encode(), None if f16 else a.ctypes.data, a.ctypes.data if f16 else None,
+                       a.size)
+    return arr, keep
+
+
+def sovits_latent(model: dict, codes, phones, ge, ge_text, noise=None):
+    """sovits_engine.hpp:48-93 steps 1-5 on the CPU: (m_p, logs_p, z), each
+    [hidden][2 * len(codes)]; raises ValueError on the oracle's error codes."""
+    c = SovitsLatentCfg(*[model[f[0]] for f in SovitsLatentCfg._fields_])
+    arr, keep = named_tensors(model["tensors"])
+    codes = np.ascontiguousarray(codes, np.int64)
+    phones = np.ascontiguousarray(phones, np.int64)
+    ge = np.ascontiguousarray(ge, np.float32)
+    ge_text = np.ascontiguousarray(ge_text, np.float32)
+    Tq = 2 * codes.size
+    outs = [np.zeros((model["hidden"], Tq), np.float32) for _ in range(3)]
+    nz = None if noise is None else np.ascontiguousarray(noise, np.float32)
+    rc = lib().ora_sovits_latent(ctypes.byref(c), arr, len(keep), _p(codes), codes.size,
+                                 _p(phones), phones.size, _p(ge), _p(ge_text), _p(nz),
+                                 *[_p(o) for o in outs])
+    if rc:
+        raise ValueError(f"ora_sovits_latent: {rc}")
+    return tuple(outs)

@@ -17,6 +17,8 @@
 #include <condition_variable>
 #include <cstring>
 #include <functional>
+#include <map>
+#include <string>
 #include <mutex>
 #include <thread>
 #include <random>
@@ -780,6 +782,90 @@ void ora_attention_decode(const float* q, const uint16_t* kc, const uint16_t* vc
                  head_dim, scale, out + h * head_dim);
 }
 
+size_t ora_hubert_front_frames(const ora_hubert_front_cfg* c, size_t n) {
+  size_t t = n;
+  for (int i = 0; i < 7; ++i)
+    t = t < static_cast<size_t>(c->conv_kernel[i]) ? 0 : (t - c->conv_kernel[i]) / c->conv_stride[i] + 1;
+  return t;
+}
+
+// hubert.cpp:476-580 (HubertEngine::run up to the transformer layers).
+void ora_hubert_front(const ora_hubert_front_cfg* c, const ora_hubert_front_weights* w,
+                      const float* wav, size_t n, float* out) {
+  int ch = 1;
+  size_t len = n;
+  std::vector<float> cur(wav, wav + n), nxt;  // channel-major [ch][len]
+  std::vector<uint16_t> cols;
+  for (int li = 0; li < 7; ++li) {  // conv_layer, hubert.cpp:439-473
+    const int k = c->conv_kernel[li], st = c->conv_stride[li], oc = c->conv_dim[li];
+    const size_t T = (len - static_cast<size_t>(k)) / static_cast<size_t>(st) + 1;
+    const size_t KK = static_cast<size_t>(ch) * k;
+    cols.assign(T * KK, 0);
+    for (size_t t = 0; t < T; ++t)
+      for (int cc = 0; cc < ch; ++cc)
+        for (int kk = 0; kk < k; ++kk)
+          cols[t * KK + static_cast<size_t>(cc) * k + kk] = f2h(cur[static_cast<size_t>(cc) * len + t * st + kk]);
+    nxt.assign(static_cast<size_t>(oc) * T, 0.f);
+    ora_gemm_f16x_fmlal(w->conv_w[li], cols.data(), nxt.data(), static_cast<size_t>(oc), T, KK);
+    if (li == 0) {  // GroupNorm(groups = C), hubert.cpp:485-500
+      const double inv = 1.0 / static_cast<double>(T);
+      for (int cc = 0; cc < oc; ++cc) {
+        float* p = nxt.data() + static_cast<size_t>(cc) * T;
+        double mu = 0.0, var = 0.0;
+        for (size_t t = 0; t < T; ++t) mu += p[t];
+        mu *= inv;
+        for (size_t t = 0; t < T; ++t) var += (p[t] - mu) * (p[t] - mu);
+        var *= inv;
+        const double rstd = 1.0 / std::sqrt(var + c->ln_eps);
+        const double g = w->gn_g[cc], b = w->gn_b[cc];
+        for (size_t t = 0; t < T; ++t) p[t] = static_cast<float>((p[t] - mu) * rstd * g + b);
+      }
+    }
+    ora_gelu_erf(nxt.data(), nxt.data(), nxt.size());
+    cur.swap(nxt);
+    len = T;
+    ch = oc;
+  }
+  // feature_projection: [C6][T] -> [T][C6], LayerNorm, Linear + bias (hubert.cpp:508-529)
+  const size_t T = len;
+  const int C6 = c->conv_dim[6], H = c->hidden;
+  std::vector<float> tmp(T * C6), x(T * H);
+  for (size_t t = 0; t < T; ++t)
+    for (int cc = 0; cc < C6; ++cc) tmp[t * C6 + cc] = cur[static_cast<size_t>(cc) * T + t];
+  for (size_t t = 0; t < T; ++t)
+    ora_layernorm(tmp.data() + t * C6, w->proj_ln_g, w->proj_ln_b, tmp.data() + t * C6, C6, c->ln_eps);
+  ora_linear_f16(tmp.data(), T, C6, w->proj_w, H, w->proj_b, ORA_ACT_NONE, 0.f, x.data());
+  // pos_conv (hubert.cpp:531-577): grouped conv, pad K/2, T + 1 outputs, + bias,
+  // GELU, SamePad drops the last frame, x += it
+  const int G = c->pos_groups, cg = H / G, K = c->pos_k;
+  const size_t P = static_cast<size_t>(K) / 2, Tp = T + 1, KK = static_cast<size_t>(cg) * K;
+  std::vector<uint16_t> w16(static_cast<size_t>(H) * cg * K);
+  ora_f32_to_f16(w->pos_w, w16.data(), w16.size());
+  std::vector<float> pos(Tp * H), gt(static_cast<size_t>(cg) * Tp);
+  cols.assign(Tp * KK, 0);
+  for (int g = 0; g < G; ++g) {
+    for (size_t t = 0; t < Tp; ++t)
+      for (int j = 0; j < cg; ++j)
+        for (int kk = 0; kk < K; ++kk) {
+          const size_t src = t + kk;
+          const float v = (src >= P && src < P + T) ? x[(src - P) * H + static_cast<size_t>(g) * cg + j] : 0.f;
+          cols[t * KK + static_cast<size_t>(j) * K + kk] = f2h(v);
+        }
+    ora_gemm_f16x_fmlal(w16.data() + static_cast<size_t>(g) * cg * KK, cols.data(), gt.data(),
+                        static_cast<size_t>(cg), Tp, KK);
+    for (size_t t = 0; t < Tp; ++t)
+      for (int i = 0; i < cg; ++i)
+        pos[t * H + static_cast<size_t>(g) * cg + i] = gt[static_cast<size_t>(i) * Tp + t];
+  }
+  for (size_t t = 0; t < Tp; ++t)
+    for (int i = 0; i < H; ++i) pos[t * H + i] = pos[t * H + i] + w->pos_b[i];
+  ora_gelu_erf(pos.data(), pos.data(), pos.size());
+  for (size_t t = 0; t < T; ++t)
+    for (int i = 0; i < H; ++i) x[t * H + i] = x[t * H + i] + pos[t * H + i];
+  for (size_t t = 0; t < T; ++t)  // encoder.layer_norm
+    ora_layernorm(x.data() + t * H, w->enc_ln_g, w->enc_ln_b, out + t * H, H, c->ln_eps);
+}
+
 // bert_ops.hpp:347-400 BertLayer::forward (and the HuBERT layer loop,
 // hubert.cpp:590-730, which has the same post-LN structure): q/k/v via the
 // DenseF16 view (fp16 activations, fp32 accumulation) + bias; per head
@@ -1067,3 +1153,356 @@ int ora_t2s_generate_ex(const ora_t2s_dims* dm, const ora_t2s_weights* w, uint16
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------- SoVITS latent path
+// sovits_engine.hpp:48-93 steps 1-5, channel-major [C][T] as the reference's
+// Tensor2D (sovits_types.hpp:21-35).
+namespace {
+
+struct LatentError {
+  int code;
+};
+
+class Named {
+ public:
+  Named(const ora_named* t, size_t n) {
+    for (size_t i = 0; i < n; ++i) by_[t[i].name] = &t[i];
+  }
+  bool has(const std::string& n) const { return by_.count(n) != 0; }
+  const ora_named& get(const std::string& n, uint64_t numel) const {
+    auto it = by_.find(n);
+    if (it == by_.end() || (numel && it->second->numel != numel) ||
+        (!it->second->f32 && !it->second->f16))
+      throw LatentError{-1};
+    return *it->second;
+  }
+  // load_tensor_f32 (sovits_types.hpp:38-48): the fp16 copy, widened, when
+  // the file holds one; else the fp32 copy.
+  std::vector<float> f32(const std::string& n, uint64_t numel = 0) const {
+    const ora_named& t = get(n, numel);
+    std::vector<float> v(t.numel);
+    if (t.f16)
+      ora_f16_to_f32(t.f16, v.data(), t.numel);
+    else
+      std::copy(t.f32, t.f32 + t.numel, v.begin());
+    return v;
+  }
+  // load_tensor_f16 (sovits_types.hpp:76-87): the fp16 copy, else the fp32
+  // copy rounded once.
+  std::vector<uint16_t> f16(const std::string& n, uint64_t numel = 0) const {
+    const ora_named& t = get(n, numel);
+    std::vector<uint16_t> v(t.numel);
+    if (t.f16)
+      std::copy(t.f16, t.f16 + t.numel, v.begin());
+    else
+      ora_f32_to_f16(t.f32, v.data(), t.numel);
+    return v;
+  }
+
+ private:
+  std::map<std::string, const ora_named*> by_;
+};
+
+using Vec = std::vector<float>;
+
+// sovits::Conv1d (conv1d.hpp:57-82, forward :109-194).
+struct LConv {
+  size_t co = 0, ci = 0, k = 1;
+  std::vector<uint16_t> w;
+  Vec b;
+  void load(const Named& T, const std::string& p, size_t o, size_t i, size_t kk) {
+    co = o, ci = i, k = kk;
+    w = T.f16(p + ".weight", o * i * kk);
+    b = T.has(p + ".bias") ? T.f32(p + ".bias", o) : Vec(o, 0.f);
+  }
+  Vec operator()(const Vec& x, size_t T, bool round_in = true) const {
+    Vec y(co * T);
+    ora_conv1d(x.data(), ci, T, w.data(), b.data(), co, k, 1, round_in ? 1 : 0, y.data());
+    return y;
+  }
+};
+
+// sovits::MultiHeadAttention (mha.hpp:16-202) with an all-ones mask.
+struct LMha {
+  size_t C = 0, H = 0, dk = 0, table = 0;
+  LConv q, k, v, o;
+  Vec relk, relv;
+  void load(const Named& T, const std::string& p, size_t ch, size_t heads, size_t tab) {
+    C = ch, H = heads, dk = ch / heads, table = tab;
+    q.load(T, p + ".conv_q", ch, ch, 1);
+    k.load(T, p + ".conv_k", ch, ch, 1);
+    v.load(T, p + ".conv_v", ch, ch, 1);
+    o.load(T, p + ".conv_o", ch, ch, 1);
+    if (tab) {
+      relk = T.f32(p + ".emb_rel_k", tab * dk);
+      relv = T.f32(p + ".emb_rel_v", tab * dk);
+    }
+  }
+  // _get_relative_embeddings (mha.hpp:45-58).
+  Vec slice(const Vec& emb, size_t L) const {
+    const size_t hw = table / 2;
+    const size_t pad_len = L > hw + 1 ? L - (hw + 1) : 0;
+    const size_t start = hw + 1 > L ? hw + 1 - L : 0;
+    Vec used((2 * L - 1) * dk, 0.f);
+    for (size_t m = 0; m < 2 * L - 1; ++m) {
+      const long long src = static_cast<long long>(m + start) - static_cast<long long>(pad_len);
+      if (src >= 0 && src < static_cast<long long>(table))
+        for (size_t d = 0; d < dk; ++d) used[m * dk + d] = emb[src * dk + d];
+    }
+    return used;
+  }
+  Vec operator()(const Vec& xq, size_t Tq, const Vec& xkv, size_t Tk) const {
+    const Vec qb = q(xq, Tq), kb = k(xkv, Tk), vb = v(xkv, Tk);
+    const float scale = 1.f / std::sqrt(static_cast<float>(dk));
+    Vec sc(H * Tq * Tk);
+    Vec usedk, usedv, rl;
+    const size_t L = Tq;
+    if (table) {
+      usedk = slice(relk, L);
+      usedv = slice(relv, L);
+      rl.assign(H * L * (2 * L - 1), 0.f);
+    }
+    pool().run(H * Tq, 1, [&](size_t rb, size_t re) {
+      for (size_t r = rb; r < re; ++r) {
+        const size_t h = r / Tq, i = r % Tq;
+        // scores = scale * Q[h]^T K[h] (mha.hpp:80-90, an sgemm with alpha)
+        for (size_t j = 0; j < Tk; ++j) {
+          float acc = 0.f;
+          for (size_t d = 0; d < dk; ++d)
+            acc = std::fmaf(qb[(h * dk + d) * Tq + i], kb[(h * dk + d) * Tk + j], acc);
+          sc[(h * Tq + i) * Tk + j] = scale * acc;
+        }
+        if (table)  // rel_logits = scale * Q[h]^T usedk^T (mha.hpp:105-113)
+          for (size_t m = 0; m < 2 * L - 1; ++m) {
+            float acc = 0.f;
+            for (size_t d = 0; d < dk; ++d)
+              acc = std::fmaf(qb[(h * dk + d) * Tq + i], usedk[m * dk + d], acc);
+            rl[(h * L + i) * (2 * L - 1) + m] = scale * acc;
+          }
+      }
+    });
+    if (table)  // relative -> absolute (mha.hpp:122-135)
+      for (size_t h = 0; h < H; ++h)
+        for (size_t i = 0; i < L; ++i)
+          for (size_t j = 0; j < L; ++j) {
+            const size_t nn = i * (2 * L - 1) + j + L - 1;
+            float val = 0.f;
+            if (nn < 2 * L * L) {
+              const size_t a = nn / (2 * L), bb = nn % (2 * L);
+              if (bb != 2 * L - 1) val = rl[(h * L + a) * (2 * L - 1) + bb];
+            }
+            sc[(h * L + i) * Tk + j] += val;
+          }
+    // softmax_row_inplace (nn_ops.hpp:12-22)
+    for (size_t r = 0; r < H * Tq; ++r) {
+      float* x = &sc[r * Tk];
+      float mx = x[0];
+      for (size_t s = 1; s < Tk; ++s) mx = std::max(mx, x[s]);
+      float sum = 0.f;
+      for (size_t s = 0; s < Tk; ++s) {
+        x[s] = std::exp(x[s] - mx);
+        sum += x[s];
+      }
+      const float inv = 1.f / sum;
+      for (size_t s = 0; s < Tk; ++s) x[s] *= inv;
+    }
+    // out = sum_s p v (mha.hpp:164-175), then the relative values (:176-196)
+    Vec out(C * Tq, 0.f);
+    for (size_t h = 0; h < H; ++h)
+      for (size_t t = 0; t < Tq; ++t) {
+        const float* pr = &sc[(h * Tq + t) * Tk];
+        for (size_t s = 0; s < Tk; ++s) {
+          const float p = pr[s];
+          if (p == 0.f) continue;
+          for (size_t d = 0; d < dk; ++d)
+            out[(h * dk + d) * Tq + t] += p * vb[(h * dk + d) * Tk + s];
+        }
+      }
+    if (table)
+      for (size_t h = 0; h < H; ++h)
+        for (size_t i = 0; i < L; ++i)
+          for (size_t m = 0; m < 2 * L - 1; ++m) {
+            const size_t nn = i * 2 * L + m + 1;
+            float w = 0.f;
+            if (nn >= L) {
+              const size_t mm = nn - L;
+              const size_t a = mm / (2 * L - 1), bb = mm % (2 * L - 1);
+              w = bb < L ? sc[(h * L + a) * L + bb] : 0.f;
+            }
+            if (w == 0.f) continue;
+            for (size_t d = 0; d < dk; ++d) out[(h * dk + d) * Tq + i] += w * usedv[m * dk + d];
+          }
+    return o(out, Tq);
+  }
+};
+
+// layernorm_ct (nn_ops.hpp:26-45): per frame over the channels, eps 1e-5.
+Vec layernorm_ct(const Vec& x, const Vec& g, const Vec& b, size_t C, size_t T) {
+  Vec y(C * T);
+  for (size_t t = 0; t < T; ++t) {
+    float mu = 0.f;
+    for (size_t c = 0; c < C; ++c) mu += x[c * T + t];
+    mu /= static_cast<float>(C);
+    float var = 0.f;
+    for (size_t c = 0; c < C; ++c) {
+      const float d = x[c * T + t] - mu;
+      var += d * d;
+    }
+    var /= static_cast<float>(C);
+    const float inv = 1.f / std::sqrt(var + 1e-5f);
+    for (size_t c = 0; c < C; ++c) y[c * T + t] = (x[c * T + t] - mu) * inv * g[c] + b[c];
+  }
+  return y;
+}
+
+// sovits::Encoder (enc_p_parts.hpp:34-95): rel-MHA, LN, FFN(k, ReLU), LN.
+struct LEncoder {
+  struct Layer {
+    LMha attn;
+    Vec g1, b1, g2, b2;
+    LConv f1, f2;
+  };
+  size_t C = 0;
+  std::vector<Layer> layers;
+  void load(const Named& T, const std::string& p, size_t ch, size_t heads, size_t nl,
+            size_t filt, size_t k, size_t table) {
+    C = ch;
+    layers.resize(nl);
+    for (size_t i = 0; i < nl; ++i) {
+      const std::string ix = "." + std::to_string(i);
+      Layer& L = layers[i];
+      L.attn.load(T, p + ".attn_layers" + ix, ch, heads, table);
+      L.g1 = T.f32(p + ".norm_layers_1" + ix + ".gamma", ch);
+      L.b1 = T.f32(p + ".norm_layers_1" + ix + ".beta", ch);
+      L.g2 = T.f32(p + ".norm_layers_2" + ix + ".gamma", ch);
+      L.b2 = T.f32(p + ".norm_layers_2" + ix + ".beta", ch);
+      L.f1.load(T, p + ".ffn_layers" + ix + ".conv_1", filt, ch, k);
+      L.f2.load(T, p + ".ffn_layers" + ix + ".conv_2", ch, filt, k);
+    }
+  }
+  void forward(Vec& x, size_t T) const {
+    Vec s(C * T);
+    for (const Layer& L : layers) {
+      const Vec y = L.attn(x, T, x, T);
+      for (size_t i = 0; i < C * T; ++i) s[i] = x[i] + y[i];
+      x = layernorm_ct(s, L.g1, L.b1, C, T);
+      Vec h = L.f1(x, T);
+      for (float& v : h) v = v > 0.f ? v : 0.f;
+      const Vec f = L.f2(h, T);
+      for (size_t i = 0; i < C * T; ++i) s[i] = x[i] + f[i];
+      x = layernorm_ct(s, L.g2, L.b2, C, T);
+    }
+  }
+};
+
+int sovits_latent(const ora_sovits_latent_cfg* c, const Named& N, const int64_t* codes, size_t Tc,
+                  const int64_t* phones, size_t Tt, const float* ge, const float* ge_text,
+                  const float* noise, float* m_p_out, float* logs_p_out, float* z_out) {
+  const size_t D = c->ssl_dim, C = c->hidden, Tq = 2 * Tc, half = C / 2, nl = c->wn_layers;
+  const size_t table = 2 * c->window + 1, MH = c->mrte_hidden;
+  // 1-2. RVQ decode (quantizer.hpp:26-38) and nearest x2 (sovits_engine.hpp:57-64)
+  const ora_named& cb = N.get("quantizer.vq.layers.0._codebook.embed", 0);
+  const Vec embed = N.f32(cb.name);
+  const size_t n_codes = embed.size() / D;
+  Vec up(D * Tq);
+  for (size_t t = 0; t < Tc; ++t) {
+    if (codes[t] < 0 || static_cast<size_t>(codes[t]) >= n_codes) throw LatentError{-2};
+    for (size_t d = 0; d < D; ++d)
+      up[d * Tq + 2 * t] = up[d * Tq + 2 * t + 1] = embed[codes[t] * D + d];
+  }
+  // 3. TextEncoder (enc_p.hpp:45-91)
+  LConv ssl_proj, c_pre, text_pre, c_post, proj;
+  ssl_proj.load(N, "enc_p.ssl_proj", C, D, 1);
+  LEncoder e_ssl, e_text, e2;
+  e_ssl.load(N, "enc_p.encoder_ssl", C, c->heads, c->layers_ssl, c->filter, c->kernel, table);
+  e_text.load(N, "enc_p.encoder_text", C, c->heads, c->layers_text, c->filter, c->kernel, table);
+  e2.load(N, "enc_p.encoder2", C, c->heads, c->layers_2, c->filter, c->kernel, table);
+  const Vec temb_w = N.f32("enc_p.text_embedding.weight");
+  const size_t n_sym = temb_w.size() / C;
+  LMha cross;
+  cross.load(N, "enc_p.mrte.cross_attention", MH, c->mrte_heads, 0);
+  c_pre.load(N, "enc_p.mrte.c_pre", MH, C, 1);
+  text_pre.load(N, "enc_p.mrte.text_pre", MH, C, 1);
+  c_post.load(N, "enc_p.mrte.c_post", C, MH, 1);
+  proj.load(N, "enc_p.proj", 2 * C, C, 1);
+
+  Vec y = ssl_proj(up, Tq);
+  e_ssl.forward(y, Tq);
+  Vec temb(C * Tt);
+  for (size_t t = 0; t < Tt; ++t) {
+    if (phones[t] < 0 || static_cast<size_t>(phones[t]) >= n_sym) throw LatentError{-2};
+    for (size_t ch = 0; ch < C; ++ch) temb[ch * Tt + t] = temb_w[phones[t] * C + ch];
+  }
+  e_text.forward(temb, Tt);
+  // MRTE (enc_p_parts.hpp:111-129)
+  const Vec c512 = c_pre(y, Tq), t512 = text_pre(temb, Tt);
+  const Vec att = cross(c512, Tq, t512, Tt);
+  Vec sum(MH * Tq);
+  for (size_t ch = 0; ch < MH; ++ch)
+    for (size_t t = 0; t < Tq; ++t)
+      sum[ch * Tq + t] = att[ch * Tq + t] + c512[ch * Tq + t] + ge_text[ch];
+  Vec m = c_post(sum, Tq);
+  e2.forward(m, Tq);
+  const Vec stats = proj(m, Tq);
+  // 4. z_p = m_p + noise * exp(logs_p) * noise_scale (sovits_engine.hpp:74-79)
+  Vec x(C * Tq);
+  for (size_t i = 0; i < C * Tq; ++i) {
+    const float mp = stats[i], lp = stats[C * Tq + i];
+    if (m_p_out) m_p_out[i] = mp;
+    if (logs_p_out) logs_p_out[i] = lp;
+    x[i] = mp + (noise ? noise[i] : 0.f) * std::exp(lp) * c->noise_scale;
+  }
+  // 5. reverse flow (flow.hpp:136-170): flip, then the coupling layer
+  const Vec gev(ge, ge + c->gin);
+  for (int f = c->flows - 1; f >= 0; --f) {
+    for (size_t ch = 0; ch < C / 2; ++ch)
+      for (size_t t = 0; t < Tq; ++t) std::swap(x[ch * Tq + t], x[(C - 1 - ch) * Tq + t]);
+    const std::string p = "flow.flows." + std::to_string(2 * f);
+    LConv pre, cond, post;
+    pre.load(N, p + ".pre", C, half, 1);
+    cond.load(N, p + ".enc.cond_layer", 2 * C * nl, c->gin, 1);
+    post.load(N, p + ".post", half, C, 1);
+    const Vec x0(x.begin(), x.begin() + half * Tq);
+    Vec h = pre(x0, Tq);
+    // FlowWN::forward (flow.hpp:38-106); the cond layer sees one frame and
+    // takes the fp32 path
+    const Vec g = cond(gev, 1, false);
+    Vec out(C * Tq, 0.f), acts(C * Tq);
+    for (size_t l = 0; l < nl; ++l) {
+      LConv in, rs;
+      in.load(N, p + ".enc.in_layers." + std::to_string(l), 2 * C, C, c->wn_kernel);
+      rs.load(N, p + ".enc.res_skip_layers." + std::to_string(l), l + 1 < nl ? 2 * C : C, C, 1);
+      const Vec a = in(h, Tq);
+      for (size_t ch = 0; ch < C; ++ch)
+        for (size_t t = 0; t < Tq; ++t)
+          acts[ch * Tq + t] =
+              std::tanh(a[ch * Tq + t] + g[l * 2 * C + ch]) *
+              (1.f / (1.f + std::exp(-(a[(C + ch) * Tq + t] + g[l * 2 * C + C + ch]))));
+      const Vec r = rs(acts, Tq);
+      if (l + 1 < nl) {
+        for (size_t i = 0; i < C * Tq; ++i) h[i] = (h[i] + r[i]) * 1.f;
+        for (size_t i = 0; i < C * Tq; ++i) out[i] += r[C * Tq + i];
+      } else {
+        for (size_t i = 0; i < C * Tq; ++i) out[i] += r[i];
+      }
+    }
+    const Vec mm = post(out, Tq);
+    for (size_t i = 0; i < half * Tq; ++i) x[half * Tq + i] -= mm[i];
+  }
+  std::copy(x.begin(), x.end(), z_out);
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int ora_sovits_latent(const ora_sovits_latent_cfg* c, const ora_named* t, size_t n,
+                                 const int64_t* codes, size_t Tc, const int64_t* phones,
+                                 size_t Tt, const float* ge, const float* ge_text,
+                                 const float* noise, float* m_p, float* logs_p, float* z) {
+  try {
+    const Named N(t, n);
+    return sovits_latent(c, N, codes, Tc, phones, Tt, ge, ge_text, noise, m_p, logs_p, z);
+  } catch (const LatentError& e) {
+    return e.code;
+  }
+}

@@ -242,6 +242,65 @@ int ora_t2s_generate_sampled(const ora_t2s_dims* d, const ora_t2s_weights* w,
                              size_t max_steps, int stop_on_eos, const ora_sampling* sp,
                              int32_t* tokens_out, float* margins_out);
 
+/* ---- HuBERT feature front-end (hubert.cpp:476-580) ----------------------- */
+typedef struct {
+  int conv_dim[7], conv_kernel[7], conv_stride[7];
+  int hidden, pos_k, pos_groups;
+  double ln_eps;
+} ora_hubert_front_cfg;
+typedef struct {
+  const uint16_t* conv_w[7];      /* fp16 [conv_dim][in][k] */
+  const float* gn_g; const float* gn_b;
+  const float* proj_ln_g; const float* proj_ln_b;
+  const uint16_t* proj_w; const float* proj_b;
+  const float* pos_w; const float* pos_b;   /* fp32 [hidden][hidden/groups][pos_k] */
+  const float* enc_ln_g; const float* enc_ln_b;
+} ora_hubert_front_weights;
+/* Frames of n samples. */
+size_t ora_hubert_front_frames(const ora_hubert_front_cfg* c, size_t n);
+/* The CNN stack (im2col rounded to fp16, gemm_f16x_fmlal, GroupNorm in fp64
+ * on layer 0, GELU), the feature projection (LayerNorm, DenseF16 view +
+ * bias), the grouped positional conv (fp16-rounded weights, + bias, GELU,
+ * SamePad, residual) and the encoder LayerNorm: out [frames][hidden]. */
+void ora_hubert_front(const ora_hubert_front_cfg* c, const ora_hubert_front_weights* w,
+                      const float* wav, size_t n, float* out);
+
+/* ---- SoVITS latent path (sovits_engine.hpp:48-93 steps 1-5) ------------ */
+/* Named tensors, the .gsv names and layouts (sovits_types.hpp:38-95): a
+ * tensor offers an fp16 copy, an fp32 copy or both. */
+typedef struct {
+  const char* name;
+  const float* f32;
+  const uint16_t* f16;
+  uint64_t numel;
+} ora_named;
+typedef struct {
+  int ssl_dim;          /* 768 */
+  int hidden;           /* 192 */
+  int filter;           /* 768 */
+  int heads;            /* 2 */
+  int kernel;           /* 3 */
+  int window;           /* 4 (relative tables of 2W+1 rows) */
+  int layers_ssl, layers_text, layers_2;   /* 3, 6, 3 */
+  int mrte_hidden, mrte_heads;             /* 512, 4 */
+  int gin;              /* 1024 */
+  int flows;            /* 4 */
+  int wn_layers;        /* 4 */
+  int wn_kernel;        /* 5 */
+  float noise_scale;    /* 0.5 */
+} ora_sovits_latent_cfg;
+/* codes[Tc] -> RVQ decode, nearest x2, TextEncoder (ssl_proj, rel-MHA
+ * encoders, text embedding, MRTE, proj) -> m_p, logs_p [hidden][2Tc];
+ * z_p = m_p + noise * exp(logs_p) * noise_scale (noise [hidden][2Tc] or
+ * NULL); reverse flow (4 x flip + mean-only coupling with a WaveNet) -> z.
+ * Conv1d inputs are rounded to fp16 (the accelerated path); the cond layer
+ * (one frame) stays fp32.  Returns 0, -1 for a missing / mis-sized tensor,
+ * -2 for a code or phone id out of range. */
+int ora_sovits_latent(const ora_sovits_latent_cfg* c, const ora_named* t, size_t n,
+                      const int64_t* codes, size_t Tc, const int64_t* phones, size_t Tt,
+                      const float* ge, const float* ge_text, const float* noise,
+                      float* m_p, float* logs_p, float* z);
+
 /* ---- encoders (BERT / HuBERT post-LN layer) ---------------------------- */
 typedef struct {
   int layers, hidden, heads, ffn;

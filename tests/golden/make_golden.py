@@ -13,7 +13,7 @@ Run once on a machine that has the reference tree; the .npz it writes
 (kern_golden.npz next to this script) is the committed fixture, so nothing
 at test time reads the reference tree.
 
-    python tests/golden/make_golden.py [path/to/reference]
+    python tests/golden/make_golden.py path/to/reference
 """
 import os
 import struct
@@ -45,7 +45,9 @@ def load(path: str, ext: str) -> np.ndarray:
 
 
 def main() -> None:
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py path/to/reference")
+    ref = sys.argv[1]
     src = os.path.join(ref, "tests", "kern_golden")
     out = {}
     for name, ext in NAMES:
