@@ -88,6 +88,11 @@ SIGNATURES = {
     "gsvk_gsv_tensor_at": (c_int, [_vp, _sz, _vp]),
     "gsvk_gsv_find": (c_int, [_vp, ctypes.c_char_p, _vp]),
     "gsvk_t2s_create_from_gsv": (c_int, [_vp, c_int, _vp]),
+    "gsvk_sovits_latent_create": (c_int, [_vp, _vp, _sz, _vp]),
+    "gsvk_sovits_latent_create_from_gsv": (c_int, [_vp, _vp, _vp]),
+    "gsvk_sovits_latent_destroy": (c_int, [_vp]),
+    "gsvk_sovits_latent_forward": (c_int, [_vp, _vp, _sz, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp,
+                                           _vp]),
     "gsvk_t2s_read_trace": (c_int, [_vp, _vp, _sz]),
     "gsvk_attention_workspace_floats": (_sz, [_sz, _sz, _sz]),
     "gsvk_attention_decode": (c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, c_float, _vp, _vp, _vp]),
@@ -519,6 +524,77 @@ class GsvTensor(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char_p), ("rank", ctypes.c_uint32),
                 ("dims", ctypes.c_uint32 * 8), ("src_dtype", c_int), ("numel", ctypes.c_uint64),
                 ("f32", _vp), ("f16", _vp)]
+
+
+def gsv_tensors(tensors: dict):
+    """(ctypes array of GsvTensor, keep-alive list) for a name -> array dict:
+    uint16 arrays are fp16 bits, float32 arrays fp32 (the .gsv tensor view)."""
+    import numpy as np
+
+    keep, arr = [], (GsvTensor * len(tensors))()
+    for i, (k, a) in enumerate(tensors.items()):
+        a = np.ascontiguousarray(a)
+        name = k.encode()
+        keep += [a, name]
+        f16 = a.dtype == np.uint16
+        dims = (ctypes.c_uint32 * 8)(*a.shape)
+        arr[i] = GsvTensor(name, a.ndim, dims, 2 if f16 else 1, a.size,
+                           None if f16 else a.ctypes.data, a.ctypes.data if f16 else None)
+    return arr, keep
+
+
+class SovitsLatentConfig(ctypes.Structure):
+    _fields_ = [(n, c_int) for n in (
+        "ssl_dim", "hidden", "filter", "heads", "kernel", "window", "layers_ssl", "layers_text",
+        "layers_2", "mrte_hidden", "mrte_heads", "gin", "flows", "wn_layers", "wn_kernel")] + [
+        ("noise_scale", c_float), ("max_codes", _sz), ("max_phones", _sz)]
+
+
+class SovitsLatent:
+    """SoVITS latent path (gsvk_sovits_latent_*): codes + phones + speaker
+    embeddings -> z [hidden][2 n_codes], the generator's input."""
+
+    def __init__(self, model: dict, max_codes: int, max_phones: int, gsv: "GsvFile" = None):
+        self.hidden = model["hidden"]
+        names = [f[0] for f in SovitsLatentConfig._fields_[:-2]]
+        self.cfg = SovitsLatentConfig(*[model[n] for n in names], max_codes, max_phones)
+        h = c_void_p()
+        if gsv is not None:
+            check(lib().gsvk_sovits_latent_create_from_gsv(gsv.h, ctypes.byref(self.cfg),
+                                                          ctypes.byref(h)))
+        else:
+            arr, keep = gsv_tensors(model["tensors"])
+            check(lib().gsvk_sovits_latent_create(ctypes.byref(self.cfg), arr, len(arr),
+                                                  ctypes.byref(h)))
+        self.h = h
+
+    def forward(self, codes, phones, ge, ge_text, noise=None, z=None, m_p=None, logs_p=None,
+                stream=None):
+        """codes, phones: host int64 arrays; ge, ge_text, noise: device fp32."""
+        import numpy as np
+        import torch
+
+        codes = np.ascontiguousarray(codes, np.int64)
+        phones = np.ascontiguousarray(phones, np.int64)
+        Tq = 2 * codes.size
+        if z is None:
+            z = torch.empty(self.hidden, Tq, device=ge.device)
+        check(lib().gsvk_sovits_latent_forward(self.h, codes.ctypes.data, codes.size,
+                                               phones.ctypes.data, phones.size, _ptr(ge),
+                                               _ptr(ge_text), _ptr(noise), _ptr(z), _ptr(m_p),
+                                               _ptr(logs_p), _stream(stream)))
+        return z
+
+    def close(self):
+        if self.h:
+            lib().gsvk_sovits_latent_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class GsvFile:

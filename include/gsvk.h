@@ -444,6 +444,54 @@ int gsvk_gsv_find(gsvk_gsv_t f, const char* name, gsvk_gsv_tensor* out);
  * uploaded into a gsvk_t2s handle with `cap` KV slots.  The file may be
  * closed afterwards. */
 int gsvk_t2s_create_from_gsv(gsvk_gsv_t f, int cap, gsvk_t2s_t* out);
+
+/* ---- SoVITS latent path (sovits_engine.hpp:48-93 steps 1-5) ------------- */
+/* codes -> RVQ decode (quantizer.hpp:26-38) -> nearest x2 -> TextEncoder
+ * (enc_p.hpp: ssl_proj, relative-position encoders, text embedding, MRTE,
+ * proj) -> m_p, logs_p -> z_p = m_p + noise * exp(logs_p) * noise_scale ->
+ * reverse ResidualCouplingBlock (flow.hpp) -> z, the generator's input.
+ * Convolutions run on the tensor cores with fp16 activations (the
+ * reference's accelerated Conv1d path); attention is fp32. */
+typedef struct gsvk_sovits_latent* gsvk_sovits_latent_t;
+typedef struct {
+  int ssl_dim;          /* 768 */
+  int hidden;           /* 192; a multiple of 16, <= 512 */
+  int filter;           /* 768 (FFN width) */
+  int heads;            /* 2; hidden / heads a multiple of 32, <= 128 */
+  int kernel;           /* 3 (FFN conv kernel, odd) */
+  int window;           /* 4: relative tables of 2*window + 1 rows */
+  int layers_ssl, layers_text, layers_2;   /* 3, 6, 3 */
+  int mrte_hidden, mrte_heads;             /* 512, 4 */
+  int gin;              /* 1024: speaker embedding width (flow condition) */
+  int flows;            /* 4 coupling layers */
+  int wn_layers;        /* 4 WaveNet layers per coupling layer */
+  int wn_kernel;        /* 5 (odd) */
+  float noise_scale;    /* 0.5 */
+  size_t max_codes;     /* longest code sequence (frames = 2 x codes, <= 4096) */
+  size_t max_phones;    /* longest phone sequence (<= 4096) */
+} gsvk_sovits_latent_config;
+/* Weights from named tensors with the .gsv names and shapes
+ * (enc_p.*, flow.flows.*, quantizer.vq.layers.0._codebook.embed), read as
+ * the reference's load_tensor_f16 / load_tensor_f32 do: a tensor's fp16 copy
+ * when present, else its fp32 copy (rounded once for conv weights).  HOST
+ * data; the codebook and text-embedding sizes come from the tensors.  A
+ * missing or mis-sized tensor is GSVK_ERR_INVALID. */
+int gsvk_sovits_latent_create(const gsvk_sovits_latent_config* cfg,
+                              const gsvk_gsv_tensor* tensors, size_t n,
+                              gsvk_sovits_latent_t* out);
+/* The same from every tensor of an opened .gsv file. */
+int gsvk_sovits_latent_create_from_gsv(gsvk_gsv_t f, const gsvk_sovits_latent_config* cfg,
+                                       gsvk_sovits_latent_t* out);
+int gsvk_sovits_latent_destroy(gsvk_sovits_latent_t h);
+/* codes [n_codes], phones [n_phones]: HOST int64, checked against the
+ * codebook / symbol table (GSVK_ERR_INVALID, as the reference throws).
+ * ge [gin], ge_text [mrte_hidden], noise [hidden][2 n_codes] or NULL (no
+ * noise: z_p = m_p): DEVICE fp32.  z, and m_p / logs_p unless NULL: DEVICE
+ * fp32 [hidden][2 n_codes], channel-major like the reference's Tensor2D. */
+int gsvk_sovits_latent_forward(gsvk_sovits_latent_t h, const int64_t* codes, size_t n_codes,
+                               const int64_t* phones, size_t n_phones, const float* ge,
+                               const float* ge_text, const float* noise, float* z, float* m_p,
+                               float* logs_p, gsvk_stream_t stream);
 int gsvk_t2s_destroy(gsvk_t2s_t h);
 /* Copies a KV prefix (fp16 [L][src_rows][D] for K and V, host or device
  * memory) into slots [0, prefix) of every layer's cache. */
