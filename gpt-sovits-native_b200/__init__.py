@@ -88,6 +88,11 @@ SIGNATURES = {
     "gsvk_gsv_tensor_at": (c_int, [_vp, _sz, _vp]),
     "gsvk_gsv_find": (c_int, [_vp, ctypes.c_char_p, _vp]),
     "gsvk_t2s_create_from_gsv": (c_int, [_vp, c_int, _vp]),
+    "gsvk_sv_create": (c_int, [_vp, _vp, _sz, _vp]),
+    "gsvk_sv_create_from_gsv": (c_int, [_vp, _vp, _vp]),
+    "gsvk_sv_destroy": (c_int, [_vp]),
+    "gsvk_sv_embedding_size": (_sz, [_vp]),
+    "gsvk_sv_forward": (c_int, [_vp, _vp, _sz, _vp, _vp]),
     "gsvk_sovits_latent_create": (c_int, [_vp, _vp, _sz, _vp]),
     "gsvk_sovits_latent_create_from_gsv": (c_int, [_vp, _vp, _vp]),
     "gsvk_sovits_latent_destroy": (c_int, [_vp]),
@@ -588,6 +593,47 @@ class SovitsLatent:
     def close(self):
         if self.h:
             lib().gsvk_sovits_latent_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class SvConfig(ctypes.Structure):
+    _fields_ = [("n_mels", c_int), ("max_frames", _sz)]
+
+
+class SvEncoder:
+    """SV speaker encoder (gsvk_sv_*): fbank [frames][n_mels] -> embedding."""
+
+    def __init__(self, model: dict, max_frames: int, n_mels: int = 80, gsv: "GsvFile" = None):
+        self.cfg = SvConfig(n_mels, max_frames)
+        h = c_void_p()
+        if gsv is not None:
+            check(lib().gsvk_sv_create_from_gsv(gsv.h, ctypes.byref(self.cfg), ctypes.byref(h)))
+        else:
+            arr, keep = gsv_tensors(model["tensors"])
+            check(lib().gsvk_sv_create(ctypes.byref(self.cfg), arr, len(arr), ctypes.byref(h)))
+        self.h = h
+
+    def embedding_size(self) -> int:
+        return lib().gsvk_sv_embedding_size(self.h)
+
+    def forward(self, fbank, emb=None, stream=None):
+        import torch
+
+        if emb is None:
+            emb = torch.empty(self.embedding_size(), device=fbank.device)
+        check(lib().gsvk_sv_forward(self.h, _ptr(fbank), fbank.shape[0], _ptr(emb),
+                                    _stream(stream)))
+        return emb
+
+    def close(self):
+        if self.h:
+            lib().gsvk_sv_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -210,6 +210,73 @@ def sovits_latent_inputs(n_codes, n_phones, cfg=SOVITS_LATENT, seed=0, noise=Tru
     return codes, phones, ge, ge_text, nz
 
 
+SV_STAGES = ((3, 1, False), (4, 2, False), (6, 2, True), (3, 2, True))  # blocks, stride, AFF
+
+
+def sv_model(seed=0, m_ch=64, base_width=24, scale=4, expansion=4) -> dict:
+    """ERes2NetV2 w24 s4 e4 tensors under their .gsv names (sv.cpp:660-760):
+    convs fp16 [out][in][kh][kw] ~ N(0, 2/fan_in) (He; the residual-branch
+    conv3 and the shortcuts x0.25, which keeps relu20 mostly unsaturated),
+    the stem conv fp32, BatchNorm gamma 1+N(0,0.1), beta N(0,0.1), running
+    mean N(0,0.1), running var U(0.5,1.5); the AFF second convs fp32 only
+    (the reference rounds those once)."""
+    rng = np.random.default_rng(seed)
+    t = {}
+
+    def conv(name, co, ci, k, gain=1.0, f32=False):
+        w = _normal(rng, (co, ci, k, k), gain * np.sqrt(2.0 / (ci * k * k)))
+        t[name] = w if f32 else _f16(w)
+
+    def bn(p, c):
+        t[p + ".weight"] = (1 + _normal(rng, (c,), 0.1)).astype(np.float32)
+        t[p + ".bias"] = _normal(rng, (c,), 0.1)
+        t[p + ".running_mean"] = _normal(rng, (c,), 0.1)
+        t[p + ".running_var"] = rng.uniform(0.5, 1.5, c).astype(np.float32)
+
+    def aff(p, ch, r=4):
+        inter = ch // r
+        conv(p + "0.weight", inter, 2 * ch, 1)
+        t[p + "0.bias"] = _normal(rng, (inter,), 0.1)
+        bn(p + "1", inter)
+        conv(p + "3.weight", ch, inter, 1, gain=0.5, f32=True)
+        t[p + "3.bias"] = _normal(rng, (ch,), 0.1)
+        bn(p + "4", ch)
+
+    conv("conv1.weight", m_ch, 1, 3, f32=True)
+    bn("bn1", m_ch)
+    c_in = m_ch
+    for l, (blocks, stride, with_aff) in enumerate(SV_STAGES, 1):
+        planes = m_ch * 2 ** (l - 1)
+        width = planes * base_width // 64
+        exp = planes * expansion
+        for i in range(blocks):
+            p = f"layer{l}.{i}."
+            conv(p + "conv1.weight", width * scale, c_in, 1)
+            bn(p + "bn1", width * scale)
+            for j in range(scale):
+                conv(p + f"convs.{j}.weight", width, width, 3)
+                bn(p + f"bns.{j}", width)
+            conv(p + "conv3.weight", exp, width * scale, 1, gain=0.25)
+            bn(p + "bn3", exp)
+            if with_aff:
+                for j in range(scale - 1):
+                    aff(p + f"fuse_models.{j}.local_att.", width)
+            if i == 0 and (stride != 1 or c_in != exp):
+                conv(p + "shortcut.0.weight", exp, c_in, 1, gain=0.25)
+                bn(p + "shortcut.1", exp)
+            c_in = exp
+        if l == 3:
+            c3 = exp
+    conv("layer3_ds.weight", c_in, c3, 3, gain=0.5)
+    aff("fuse34.local_att.", c_in)
+    return {"tensors": t, "m_ch": m_ch, "emb_channels": c_in}
+
+
+def sv_fbank(frames=64, n_mels=80, seed=0):
+    """A log-mel stand-in: N(0,1) [frames][n_mels] (fbank.cpp output shape)."""
+    return _normal(np.random.default_rng(seed + 11000), (frames, n_mels), 1.0)
+
+
 def encoder_model(name: str, layers=None, seed=0) -> dict:
     """Encoder weights in the oracle / C-ABI layout: q, k, v rows fused as
     [L][3C][C]; N(0,0.02) fp16 matrices, N(0,0.02) fp32 biases, LayerNorm gain

@@ -492,6 +492,28 @@ int gsvk_sovits_latent_forward(gsvk_sovits_latent_t h, const int64_t* codes, siz
                                const int64_t* phones, size_t n_phones, const float* ge,
                                const float* ge_text, const float* noise, float* z, float* m_p,
                                float* logs_p, gsvk_stream_t stream);
+
+/* ---- SV speaker encoder, ERes2NetV2 w24 s4 e4 (sv.cpp:130-885) ---------- */
+/* fbank [frames][n_mels] -> embedding [C4 * F4] (C4 = 2048 channels, F4 =
+ * n_mels after the three stride-2 stages): stem conv (fp32), 16 Res2Net
+ * blocks, layer3_ds, fuse34 AFF, mean over time.  Convs are im2col + tensor
+ * core GEMMs with fp16 operands (the reference's conv2d_f16); BatchNorm
+ * runs in the reference's fp64 chain.  Weights by .gsv names (conv1.*,
+ * bn1.*, layer{1..4}.{i}.*, layer3_ds.*, fuse34.*), HOST data. */
+typedef struct gsvk_sv* gsvk_sv_t;
+typedef struct {
+  int n_mels;          /* 80 */
+  size_t max_frames;   /* longest fbank a forward may take */
+} gsvk_sv_config;
+int gsvk_sv_create(const gsvk_sv_config* cfg, const gsvk_gsv_tensor* tensors, size_t n,
+                   gsvk_sv_t* out);
+int gsvk_sv_create_from_gsv(gsvk_gsv_t f, const gsvk_sv_config* cfg, gsvk_sv_t* out);
+int gsvk_sv_destroy(gsvk_sv_t h);
+size_t gsvk_sv_embedding_size(gsvk_sv_t h);
+/* fbank: DEVICE fp32 [frames][n_mels]; emb: DEVICE fp32 [embedding_size]
+ * (channel-major [C4][F4], SvEngine::emb_out). */
+int gsvk_sv_forward(gsvk_sv_t h, const float* fbank, size_t frames, float* emb,
+                    gsvk_stream_t stream);
 int gsvk_t2s_destroy(gsvk_t2s_t h);
 /* Copies a KV prefix (fp16 [L][src_rows][D] for K and V, host or device
  * memory) into slots [0, prefix) of every layer's cache. */

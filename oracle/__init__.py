@@ -100,6 +100,9 @@ def lib():
             "ora_t2s_generate_sampled": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, vp,
                                                  vp, vp]),
             "ora_sovits_latent": (c_int, [vp, vp, sz, vp, sz, vp, sz, vp, vp, vp, vp, vp, vp]),
+            "ora_sv_forward": (sz, [vp, sz, vp, sz, c_int, vp]),
+            "ora_sv_conv2d_f16": (None, [vp, c_int, c_int, c_int, vp, c_int, c_int, c_int, c_int,
+                                         c_int, vp]),
             "ora_hubert_front_frames": (sz, [vp, sz]),
             "ora_hubert_front": (None, [vp, vp, vp, sz, vp]),
             "ora_t2s_generate_ex": (c_int, [vp, vp, vp, vp, sz, sz, vp, sz, sz, c_int, c_int, vp,
@@ -480,3 +483,27 @@ def sovits_latent(model: dict, codes, phones, ge, ge_text, noise=None):
     if rc:
         raise ValueError(f"ora_sovits_latent: {rc}")
     return tuple(outs)
+
+
+def sv_forward(model: dict, fbank: np.ndarray) -> np.ndarray:
+    """sv.cpp forward3 on the CPU: fbank [frames][n_mels] -> embedding."""
+    arr, keep = named_tensors(model["tensors"])
+    fb = np.ascontiguousarray(fbank, np.float32)
+    frames, n_mels = fb.shape
+    emb = np.zeros(model["emb_channels"] * (n_mels // 8 + 1), np.float32)
+    n = lib().ora_sv_forward(arr, len(keep), _p(fb), frames, n_mels, _p(emb))
+    if n == 0:
+        raise ValueError("ora_sv_forward: missing tensor")
+    return emb[:n].copy()
+
+
+def sv_conv2d_f16(x: np.ndarray, w16: np.ndarray, stride: int, pad: int) -> np.ndarray:
+    """conv2d_f16: x [c_in][h][w] fp32, w16 [c_out][c_in][kh][kw] fp16 bits."""
+    x = np.ascontiguousarray(x, np.float32)
+    w16 = np.ascontiguousarray(w16, np.uint16)
+    c_in, h, w = x.shape
+    c_out, _, kh, kw = w16.shape
+    oh, ow = (h + 2 * pad - kh) // stride + 1, (w + 2 * pad - kw) // stride + 1
+    out = np.zeros((c_out, oh, ow), np.float32)
+    lib().ora_sv_conv2d_f16(_p(x), c_in, h, w, _p(w16), c_out, kh, kw, stride, pad, _p(out))
+    return out

@@ -1506,3 +1506,297 @@ extern "C" int ora_sovits_latent(const ora_sovits_latent_cfg* c, const ora_named
     return e.code;
   }
 }
+
+// ------------------------------------------------- SV speaker encoder
+// sv.cpp:130-885 (the default, non --amx-enc path), channel-major
+// [C][H][W] like the reference.
+namespace {
+
+struct SvMissing {};
+
+const ora_named* sv_find(const std::map<std::string, const ora_named*>& by, const std::string& n) {
+  auto it = by.find(n);
+  return it == by.end() ? nullptr : it->second;
+}
+
+// vec_any (sv.cpp:74-84): the fp16 copy widened when present, else fp32.
+std::vector<float> sv_vec(const std::map<std::string, const ora_named*>& by, const std::string& n) {
+  const ora_named* t = sv_find(by, n);
+  if (!t || (!t->f16 && !t->f32)) throw SvMissing{};
+  std::vector<float> v(t->numel);
+  if (t->f16)
+    ora_f16_to_f32(t->f16, v.data(), t->numel);
+  else
+    std::copy(t->f32, t->f32 + t->numel, v.begin());
+  return v;
+}
+
+// load_conv_w (sv.cpp:97-128): the fp16 copy, else the fp32 copy rounded.
+std::vector<uint16_t> sv_w16(const std::map<std::string, const ora_named*>& by,
+                             const std::string& n) {
+  const ora_named* t = sv_find(by, n);
+  if (!t || (!t->f16 && !t->f32)) throw SvMissing{};
+  std::vector<uint16_t> v(t->numel);
+  if (t->f16)
+    std::copy(t->f16, t->f16 + t->numel, v.begin());
+  else
+    ora_f32_to_f16(t->f32, v.data(), t->numel);
+  return v;
+}
+
+struct SvBn {
+  std::vector<float> g, b, mean, var;
+  void load(const std::map<std::string, const ora_named*>& by, const std::string& p) {
+    g = sv_vec(by, p + ".weight");
+    b = sv_vec(by, p + ".bias");
+    mean = sv_vec(by, p + ".running_mean");
+    var = sv_vec(by, p + ".running_var");
+  }
+  // Bn::apply (sv.cpp:132-145), the fp64 chain.
+  void apply(float* x, int c, size_t s) const {
+    for (int ci = 0; ci < c; ++ci) {
+      const double a0 = static_cast<double>(g[ci]) / std::sqrt(static_cast<double>(var[ci]) + 1e-5);
+      const double beta0 = static_cast<double>(b[ci]), mu0 = static_cast<double>(mean[ci]);
+      float* row = x + static_cast<size_t>(ci) * s;
+      for (size_t i = 0; i < s; ++i)
+        row[i] = static_cast<float>((static_cast<double>(row[i]) - mu0) * a0 + beta0);
+    }
+  }
+};
+
+inline float relu20f(float v) { return v < 0.f ? 0.f : (v > 20.f ? 20.f : v); }
+
+// conv2d (sv.cpp:171-194): im2col in fp32, sgemm('N','T').
+std::vector<float> sv_conv2d_f32(const float* in, int c_in, int h, int w, const float* wt,
+                                 int c_out, int kh, int kw, int stride, int pad) {
+  const int oh = (h + 2 * pad - kh) / stride + 1, ow = (w + 2 * pad - kw) / stride + 1;
+  const size_t S = static_cast<size_t>(oh) * ow;
+  const int K = c_in * kh * kw;
+  std::vector<float> cols(S * K);
+  for (int oy = 0; oy < oh; ++oy)
+    for (int ox = 0; ox < ow; ++ox) {
+      float* row = cols.data() + (static_cast<size_t>(oy) * ow + ox) * K;
+      for (int c = 0; c < c_in; ++c)
+        for (int ky = 0; ky < kh; ++ky)
+          for (int kx = 0; kx < kw; ++kx) {
+            const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+            row[(c * kh + ky) * kw + kx] = (iy >= 0 && iy < h && ix >= 0 && ix < w)
+                                               ? in[(static_cast<size_t>(c) * h + iy) * w + ix]
+                                               : 0.f;
+          }
+    }
+  std::vector<float> out(static_cast<size_t>(c_out) * S, 0.f);
+  ora_sgemm('N', 'T', c_out, static_cast<int>(S), K, 1.f, wt, K, cols.data(), K, 0.f, out.data(),
+            static_cast<int>(S));
+  return out;
+}
+
+// conv2d_f16 (sv.cpp:196-258): im2col rounded to fp16, gemm_f16x_fmlal.
+std::vector<float> sv_conv2d_f16(const float* in, int c_in, int h, int w, const uint16_t* w16,
+                                 int c_out, int kh, int kw, int stride, int pad) {
+  const int oh = (h + 2 * pad - kh) / stride + 1, ow = (w + 2 * pad - kw) / stride + 1;
+  const size_t S = static_cast<size_t>(oh) * ow, K = static_cast<size_t>(c_in) * kh * kw;
+  std::vector<uint16_t> cols(S * K);
+  for (int oy = 0; oy < oh; ++oy)
+    for (int ox = 0; ox < ow; ++ox) {
+      uint16_t* row = cols.data() + (static_cast<size_t>(oy) * ow + ox) * K;
+      for (int c = 0; c < c_in; ++c)
+        for (int ky = 0; ky < kh; ++ky)
+          for (int kx = 0; kx < kw; ++kx) {
+            const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+            row[(static_cast<size_t>(c) * kh + ky) * kw + kx] =
+                f2h((iy >= 0 && iy < h && ix >= 0 && ix < w)
+                        ? in[(static_cast<size_t>(c) * h + iy) * w + ix]
+                        : 0.f);
+          }
+    }
+  std::vector<float> out(static_cast<size_t>(c_out) * S, 0.f);
+  ora_gemm_f16x_fmlal(w16, cols.data(), out.data(), static_cast<size_t>(c_out), S, K);
+  return out;
+}
+
+using Named2 = std::map<std::string, const ora_named*>;
+
+// Aff::apply (sv.cpp:445-521): att = BN2(W2 SiLU(BN1(W1 [x; ds] + b1)) + b2),
+// out = x (1 + tanh att) + ds (1 - tanh att).  out may alias x.
+struct SvAff {
+  std::vector<uint16_t> w1, w2;
+  std::vector<float> b1, b2;
+  SvBn bn1, bn2;
+  int inter = 0, ch = 0;
+  void load(const Named2& by, const std::string& p, int c) {
+    ch = c;
+    w1 = sv_w16(by, p + "0.weight");
+    inter = static_cast<int>(w1.size() / (2 * static_cast<size_t>(c)));
+    w2 = sv_w16(by, p + "3.weight");
+    b1 = sv_vec(by, p + "0.bias");
+    b2 = sv_vec(by, p + "3.bias");
+    bn1.load(by, p + "1");
+    bn2.load(by, p + "4");
+  }
+  void apply(const float* x, const float* ds, float* out, size_t s) const {
+    std::vector<uint16_t> xh(2 * static_cast<size_t>(ch) * s);
+    for (size_t i = 0; i < s; ++i)  // f32_trans_to_f16 of cat [2ch][s] -> [s][2ch]
+      for (int c = 0; c < 2 * ch; ++c)
+        xh[i * 2 * ch + c] = f2h(c < ch ? x[static_cast<size_t>(c) * s + i]
+                                        : ds[static_cast<size_t>(c - ch) * s + i]);
+    std::vector<float> att(static_cast<size_t>(inter) * s);
+    ora_gemm_f16x_fmlal(w1.data(), xh.data(), att.data(), inter, s, 2 * static_cast<size_t>(ch));
+    for (int e = 0; e < inter; ++e)
+      for (size_t i = 0; i < s; ++i) att[e * s + i] += b1[e];
+    bn1.apply(att.data(), inter, s);
+    ora_silu(att.data(), att.data(), att.size());
+    std::vector<uint16_t> xh2(static_cast<size_t>(inter) * s);
+    for (size_t i = 0; i < s; ++i)
+      for (int e = 0; e < inter; ++e) xh2[i * inter + e] = f2h(att[static_cast<size_t>(e) * s + i]);
+    std::vector<float> at(static_cast<size_t>(ch) * s);
+    ora_gemm_f16x_fmlal(w2.data(), xh2.data(), at.data(), ch, s, inter);
+    for (int e = 0; e < ch; ++e)
+      for (size_t i = 0; i < s; ++i) at[e * s + i] += b2[e];
+    bn2.apply(at.data(), ch, s);
+    for (size_t i = 0; i < static_cast<size_t>(ch) * s; ++i) {
+      const float t = std::tanh(at[i]);
+      out[i] = x[i] * (1.0f + t) + ds[i] * (1.0f - t);
+    }
+  }
+};
+
+// Block::apply (sv.cpp:523-644).
+struct SvBlock {
+  bool aff = false, has_sc = false;
+  int width = 0, scale = 4, exp = 0, stride = 1;
+  std::vector<uint16_t> conv1, conv3, sc;
+  std::vector<std::vector<uint16_t>> convs;
+  SvBn bn1, bn3, sc_bn;
+  std::vector<SvBn> bns;
+  std::vector<SvAff> fuses;
+  void load(const Named2& by, int l, int i, bool with_aff, int st) {
+    const std::string p = "layer" + std::to_string(l) + "." + std::to_string(i) + ".";
+    aff = with_aff;
+    stride = st;
+    bn3.load(by, p + "bn3");
+    exp = static_cast<int>(bn3.g.size());
+    conv1 = sv_w16(by, p + "conv1.weight");
+    bn1.load(by, p + "bn1");
+    width = static_cast<int>(bn1.g.size()) / scale;
+    for (int j = 0; j < scale; ++j) {
+      convs.push_back(sv_w16(by, p + "convs." + std::to_string(j) + ".weight"));
+      bns.emplace_back();
+      bns.back().load(by, p + "bns." + std::to_string(j));
+    }
+    conv3 = sv_w16(by, p + "conv3.weight");
+    if (aff)
+      for (int j = 0; j < scale - 1; ++j) {
+        fuses.emplace_back();
+        fuses.back().load(by, p + "fuse_models." + std::to_string(j) + ".local_att.", width);
+      }
+    has_sc = sv_find(by, p + "shortcut.0.weight") != nullptr;
+    if (has_sc) {
+      sc = sv_w16(by, p + "shortcut.0.weight");
+      sc_bn.load(by, p + "shortcut.1");
+    }
+  }
+  std::vector<float> apply(const std::vector<float>& in, int c_in, int& h, int& w) const {
+    const int co1 = width * scale, h_in = h, w_in = w;
+    std::vector<float> c1 = sv_conv2d_f16(in.data(), c_in, h, w, conv1.data(), co1, 1, 1, stride, 0);
+    h = (h - 1) / stride + 1;
+    w = (w - 1) / stride + 1;
+    const size_t s = static_cast<size_t>(h) * w;
+    bn1.apply(c1.data(), co1, s);
+    for (float& v : c1) v = relu20f(v);
+    std::vector<float> tmp2(static_cast<size_t>(co1) * s), sp(static_cast<size_t>(width) * s);
+    for (int i = 0; i < scale; ++i) {
+      const float* chunk = c1.data() + static_cast<size_t>(i) * width * s;
+      if (i > 0) {
+        if (aff)
+          fuses[i - 1].apply(sp.data(), chunk, sp.data(), s);
+        else
+          for (size_t j = 0; j < sp.size(); ++j) sp[j] += chunk[j];
+      }
+      std::vector<float> nx = sv_conv2d_f16(i == 0 ? chunk : sp.data(), width, h, w,
+                                            convs[i].data(), width, 3, 3, 1, 1);
+      bns[i].apply(nx.data(), width, s);
+      for (float& v : nx) v = relu20f(v);
+      std::copy(nx.begin(), nx.end(), tmp2.begin() + static_cast<size_t>(i) * width * s);
+      sp = nx;
+    }
+    std::vector<float> out = sv_conv2d_f16(tmp2.data(), co1, h, w, conv3.data(), exp, 1, 1, 1, 0);
+    bn3.apply(out.data(), exp, s);
+    if (!has_sc) {
+      for (size_t j = 0; j < out.size(); ++j) out[j] += in[j];
+    } else {
+      std::vector<float> t = sv_conv2d_f16(in.data(), c_in, h_in, w_in, sc.data(), exp, 1, 1,
+                                           stride, 0);
+      sc_bn.apply(t.data(), exp, s);
+      for (size_t j = 0; j < out.size(); ++j) out[j] += t[j];
+    }
+    for (float& v : out) v = relu20f(v);
+    return out;
+  }
+};
+
+size_t sv_forward(const Named2& by, const float* fbk, size_t frames, int F, float* emb_out) {
+  const int T = static_cast<int>(frames);
+  std::vector<float> cur(static_cast<size_t>(F) * T);
+  for (int t = 0; t < T; ++t)
+    for (int f = 0; f < F; ++f) cur[static_cast<size_t>(f) * T + t] = fbk[static_cast<size_t>(t) * F + f];
+  const std::vector<float> w0 = sv_vec(by, "conv1.weight");
+  SvBn bn1;
+  bn1.load(by, "bn1");
+  const int m_ch = static_cast<int>(bn1.g.size());
+  std::vector<float> x = sv_conv2d_f32(cur.data(), 1, F, T, w0.data(), m_ch, 3, 3, 1, 1);
+  bn1.apply(x.data(), m_ch, static_cast<size_t>(F) * T);
+  for (float& v : x) v = v < 0.f ? 0.f : v;
+  struct Def {
+    int blocks, stride;
+    bool aff;
+  };
+  const Def defs[4] = {{3, 1, false}, {4, 2, false}, {6, 2, true}, {3, 2, true}};
+  int h = F, w = T, c = m_ch, h3 = 0, w3 = 0, c3 = 0;
+  std::vector<float> o3;
+  for (int l = 1; l <= 4; ++l) {
+    for (int i = 0; i < defs[l - 1].blocks; ++i) {
+      SvBlock b;
+      b.load(by, l, i, defs[l - 1].aff, i == 0 ? defs[l - 1].stride : 1);
+      x = b.apply(x, c, h, w);
+      c = b.exp;
+    }
+    if (l == 3) {
+      o3 = x;
+      h3 = h, w3 = w, c3 = c;
+    }
+  }
+  const std::vector<uint16_t> l3ds = sv_w16(by, "layer3_ds.weight");
+  const std::vector<float> ds = sv_conv2d_f16(o3.data(), c3, h3, w3, l3ds.data(), c, 3, 3, 2, 1);
+  SvAff f34;
+  f34.load(by, "fuse34.local_att.", c);
+  std::vector<float> fused(ds.size());
+  f34.apply(x.data(), ds.data(), fused.data(), static_cast<size_t>(h) * w);
+  for (int ci = 0; ci < c; ++ci)  // flatten (C x F) and mean over T (sv.cpp:870-879)
+    for (int fy = 0; fy < h; ++fy) {
+      const float* row = fused.data() + (static_cast<size_t>(ci) * h + fy) * w;
+      double acc = 0.0;
+      for (int t = 0; t < w; ++t) acc += row[t];
+      emb_out[static_cast<size_t>(ci) * h + fy] = static_cast<float>(acc / w);
+    }
+  return static_cast<size_t>(c) * h;
+}
+
+}  // namespace
+
+extern "C" size_t ora_sv_forward(const ora_named* t, size_t n, const float* fbank, size_t frames,
+                                 int n_mels, float* emb) {
+  Named2 by;
+  for (size_t i = 0; i < n; ++i) by[t[i].name] = &t[i];
+  try {
+    return sv_forward(by, fbank, frames, n_mels, emb);
+  } catch (const SvMissing&) {
+    return 0;
+  }
+}
+
+extern "C" void ora_sv_conv2d_f16(const float* in, int c_in, int h, int w, const uint16_t* w16,
+                                  int c_out, int kh, int kw, int stride, int pad, float* out) {
+  const std::vector<float> y = sv_conv2d_f16(in, c_in, h, w, w16, c_out, kh, kw, stride, pad);
+  std::copy(y.begin(), y.end(), out);
+}

@@ -301,6 +301,19 @@ int ora_sovits_latent(const ora_sovits_latent_cfg* c, const ora_named* t, size_t
                       const float* ge, const float* ge_text, const float* noise,
                       float* m_p, float* logs_p, float* z);
 
+/* ---- SV speaker encoder, ERes2NetV2 w24 s4 e4 (sv.cpp:130-885) --------- */
+/* fbank [frames][n_mels] -> embedding [C4 * n_mels / 8] (C4 = 2048): the
+ * fp32 stem conv (sgemm), four Res2Net stages (conv2d_f16: im2col rounded
+ * to fp16, gemm_f16x_fmlal), BatchNorm in the fp64 chain, relu20, AFF
+ * fusions, layer3_ds, fuse34 and the mean over time.  Named tensors as in
+ * the .gsv.  Returns the embedding size, 0 for a missing tensor. */
+size_t ora_sv_forward(const ora_named* t, size_t n, const float* fbank, size_t frames,
+                      int n_mels, float* emb);
+/* conv2d_f16 (sv.cpp:196-258) on its own: in [c_in][h][w] fp32, w16
+ * [c_out][c_in*kh*kw] -> out [c_out][oh*ow]. */
+void ora_sv_conv2d_f16(const float* in, int c_in, int h, int w, const uint16_t* w16, int c_out,
+                       int kh, int kw, int stride, int pad, float* out);
+
 /* ---- encoders (BERT / HuBERT post-LN layer) ---------------------------- */
 typedef struct {
   int layers, hidden, heads, ffn;
