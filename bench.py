@@ -199,6 +199,14 @@ def workload_meta(args, world):
                             "decode_steps_per_step": 32, "mean_kv_len": float(lens.mean()),
                             "global_batch": B * world, "parallelism": f"replicas x{world}",
                             "l2": "1.9 GB of weights + KV streamed per decode step"})
+    if wl in ENGINE_WORKLOADS:
+        d = ENGINE_WORKLOADS[wl]
+        return dict(metric=d["metric"], unit="TFLOP/s", dtype=d["dtype"], data=d["data"],
+                    config={"workload": wl, **d["shape"], "global_batch": world,
+                            "parallelism": f"replicas x{world}",
+                            "l2": "a 256 MB buffer written between timed forwards (L2 flushed)",
+                            "flops_counted": "conv / GEMM / attention products; time is the "
+                                             "whole forward"})
     if wl == "gemv_t2s":
         return dict(metric="T2S GEMV GB/s (one token's 97 GEMVs: 24 x {1536x512, 512x512, "
                            "2048x512, 512x2048} + 1025x512)",
@@ -318,6 +326,9 @@ def cpu_sampler(args, threads):
                 oracle.t2s_greedy_sample(lg, hist, True)
         return fn, len(lens), (f"oracle T2S decode: one token for each of the first {len(lens)} "
                                f"utterances (KV lengths {', '.join(str(int(v)) for v in lens)})")
+    if wl in ENGINE_WORKLOADS:
+        fn, flops, desc = engine_cpu_sample(wl, W, oracle)
+        return fn, flops, desc
     if wl == "gemv_t2s":
         m = W.t2s_model(seed=0)
         x = np.random.default_rng(0).standard_normal(2048).astype(np.float32)
@@ -569,6 +580,225 @@ def run_gemm1(args, rank, local, world):
                          "note": "AI 97 flop/B is below the ridge: HBM-bound"}}
     if clk:
         line["clocks"] = clk
+    return line
+
+
+# ---------------------------------- SoVITS latent path, SV, HuBERT front-end
+ENGINE_WORKLOADS = {
+    "hubert_front": dict(
+        metric="HuBERT front-end TFLOP/s (10 s of 16 kHz audio per forward)",
+        dtype="f16 operands, f32 accumulate", shape={"samples": 160000},
+        data="synthetic (N(0,0.1) waveform, N(0,1/fan_in) conv weights)"),
+    "sovits_latent": dict(
+        metric="SoVITS latent path TFLOP/s (250 codes = 500 frames, 100 phones per forward)",
+        dtype="f16 conv operands, f32 accumulate and attention", shape={"codes": 250, "phones": 100},
+        data="synthetic (uniform codes / phones, N(0,1/fan_in) conv weights, N(0,1) noise)"),
+    "sv": dict(
+        metric="SV encoder TFLOP/s (500 fbank frames per forward)",
+        dtype="f16 conv operands, f32 accumulate, fp64 BatchNorm", shape={"frames": 500},
+        data="synthetic (N(0,1) fbank, He-initialised convs)"),
+}
+
+
+def hubert_front_flops(cfg, n):
+    t, ci, f = n, 1, 0
+    for co, k, s in zip(cfg["conv_dim"], cfg["conv_kernel"], cfg["conv_stride"]):
+        t = (t - k) // s + 1
+        f += 2 * t * co * ci * k
+        ci = co
+    H = cfg["hidden"]
+    return f + 2 * t * H * ci + 2 * t * H * (H // cfg["pos_groups"]) * cfg["pos_k"]
+
+
+def sovits_latent_flops(c, n_codes, n_phones):
+    Tq, Tt, C, F, MH = 2 * n_codes, n_phones, c["hidden"], c["filter"], c["mrte_hidden"]
+    K = c["kernel"]
+
+    def enc(T, L):
+        return L * (2 * T * 3 * C * C + 4 * T * T * C + 2 * T * C * C + 4 * T * F * C * K)
+
+    f = 2 * Tq * C * c["ssl_dim"] + enc(Tq, c["layers_ssl"]) + enc(Tt, c["layers_text"])
+    f += enc(Tq, c["layers_2"])
+    f += 2 * Tq * MH * C + 2 * Tt * MH * C + 2 * Tq * MH * MH + 4 * Tt * MH * MH
+    f += 4 * Tq * Tt * MH + 2 * Tq * MH * MH + 2 * Tq * C * MH + 4 * Tq * C * C
+    nl = c["wn_layers"]
+    per_flow = 2 * Tq * C * (C // 2) + 4 * C * nl * c["gin"] + 2 * Tq * (C // 2) * C
+    per_flow += sum(2 * Tq * 2 * C * C * c["wn_kernel"] + 2 * Tq * (2 * C if l + 1 < nl else C) * C
+                    for l in range(nl))
+    return f + c["flows"] * per_flow
+
+
+def sv_flops(frames, n_mels=80, m_ch=64, base_width=24, scale=4, expansion=4, stages=None):
+    stages = stages or __import__("__graft_entry__").package().workloads.SV_STAGES
+    h, w = n_mels, frames
+    f = 2 * h * w * m_ch * 9
+    c = m_ch
+    for l, (blocks, stride, aff) in enumerate(stages, 1):
+        planes = m_ch * 2 ** (l - 1)
+        width, exp = planes * base_width // 64, planes * expansion
+        for i in range(blocks):
+            st = stride if i == 0 else 1
+            h, w = (h - 1) // st + 1, (w - 1) // st + 1
+            S, co1 = h * w, width * scale
+            f += 2 * S * co1 * c + scale * 2 * S * width * width * 9 + 2 * S * exp * co1
+            if aff:
+                inter = width // 4
+                f += (scale - 1) * (2 * S * inter * 2 * width + 2 * S * width * inter)
+            if i == 0 and (st != 1 or c != exp):
+                f += 2 * S * exp * c
+            c = exp
+        if l == 3:
+            c3 = c
+    S4 = h * w
+    return f + 2 * S4 * c * c3 * 9 + 2 * S4 * (c // 4) * 2 * c + 2 * S4 * c * (c // 4)
+
+
+def engine_setup(wl, g, dev):
+    """(forward(), e2e_step(), flops, h2d_bytes, d2h_bytes) for one engine
+    workload; inputs resident on `dev`, pinned host copies for e2e."""
+    import numpy as np
+    import torch
+
+    W = g.workloads
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()  # noqa: E731
+    if wl == "hubert_front":
+        n = ENGINE_WORKLOADS[wl]["shape"]["samples"]
+        m = W.hubert_front_model(seed=0)
+        fe = g.HubertFront(m, max_samples=n)
+        wav_h = pin(W.hubert_waveform(n, seed=0))
+        wav = wav_h.to(dev)
+        x = torch.empty(fe.frames(n), m["hidden"], device=dev)
+        x_h = torch.empty(x.shape).pin_memory()
+
+        def e2e():
+            wav.copy_(wav_h, non_blocking=True)
+            fe.forward(wav, x)
+            x_h.copy_(x, non_blocking=True)
+        return (lambda: fe.forward(wav, x)), e2e, hubert_front_flops(m, n), n * 4, x.numel() * 4, fe
+    if wl == "sovits_latent":
+        sh = ENGINE_WORKLOADS[wl]["shape"]
+        m = W.sovits_latent_model(seed=0)
+        eng = g.SovitsLatent(m, sh["codes"], sh["phones"])
+        codes, phones, ge, ge_text, nz = W.sovits_latent_inputs(sh["codes"], sh["phones"], seed=0)
+        hs = [pin(a) for a in (ge, ge_text, nz)]
+        ds = [h.to(dev) for h in hs]
+        z = torch.empty(m["hidden"], 2 * sh["codes"], device=dev)
+        z_h = torch.empty(z.shape).pin_memory()
+
+        def e2e():
+            for d_, h_ in zip(ds, hs):
+                d_.copy_(h_, non_blocking=True)
+            eng.forward(codes, phones, *ds, z=z)
+            z_h.copy_(z, non_blocking=True)
+        h2d = sum(h.numel() * 4 for h in hs) + codes.nbytes + phones.nbytes
+        return ((lambda: eng.forward(codes, phones, *ds, z=z)), e2e,
+                sovits_latent_flops(m, sh["codes"], sh["phones"]), h2d, z.numel() * 4, eng)
+    if wl == "sv":
+        T = ENGINE_WORKLOADS[wl]["shape"]["frames"]
+        m = W.sv_model(seed=0)
+        enc = g.SvEncoder(m, max_frames=T)
+        fb_h = pin(W.sv_fbank(T, seed=0))
+        fb = fb_h.to(dev)
+        emb = torch.empty(enc.embedding_size(), device=dev)
+        emb_h = torch.empty(emb.shape).pin_memory()
+
+        def e2e():
+            fb.copy_(fb_h, non_blocking=True)
+            enc.forward(fb, emb)
+            emb_h.copy_(emb, non_blocking=True)
+        return (lambda: enc.forward(fb, emb)), e2e, sv_flops(T), fb.numel() * 4, emb.numel() * 4, enc
+    raise ValueError(wl)
+
+
+def engine_cpu_sample(wl, W, oracle):
+    """A bounded oracle sample of an engine workload: (fn, flops, description)."""
+    if wl == "hubert_front":
+        m = W.hubert_front_model(seed=0)
+        wav = W.hubert_waveform(16000, seed=0)
+        return (lambda: oracle.hubert_front(m, wav)), hubert_front_flops(m, 16000), \
+            "oracle HuBERT front-end on 1 s of audio (of 10 s)"
+    if wl == "sovits_latent":
+        m = W.sovits_latent_model(seed=0)
+        inp = W.sovits_latent_inputs(50, 40, seed=0)
+        return (lambda: oracle.sovits_latent(m, *inp)), sovits_latent_flops(m, 50, 40), \
+            "oracle SoVITS latent path on 50 codes / 40 phones (of 250 / 100)"
+    if wl == "sv":
+        m = W.sv_model(seed=0)
+        fb = W.sv_fbank(16, seed=0)
+        return (lambda: oracle.sv_forward(m, fb)), sv_flops(16), \
+            "oracle SV encoder on 16 fbank frames (of 500)"
+    raise ValueError(wl)
+
+
+def count_kernels(fn):
+    """Kernels one call of fn launches, from the CUDA profiler's activity
+    records (None when the profiler is unavailable)."""
+    import torch
+
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        return sum(1 for e in prof.events() if e.device_type.name == "CUDA" and
+                   not e.name.lower().startswith(("memcpy", "memset")))
+    except Exception:
+        return None
+
+
+def run_engine(args, rank, local, world):
+    import torch
+
+    g = __import__("__graft_entry__").package()
+    g.device_init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    fwd, e2e, flops, h2d, d2h, keep = engine_setup(args.workload, g, dev)
+    flush = torch.empty(64 << 20, device=dev)  # 256 MB > L2
+    for _ in range(args.warmup):
+        fwd()
+    torch.cuda.synchronize(dev)
+    launches = None if args.no_launch_count else count_kernels(fwd)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clocks = ClockSampler()
+    barrier(world)
+    clocks.start()
+    for a, b in ev:
+        flush.zero_()
+        a.record(stream)
+        fwd()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    t = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) * 1e-3 / args.steps, world)
+    barrier(world)
+    for a, b in ev:
+        flush.zero_()
+        a.record(stream)
+        e2e()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) * 1e-3 / args.steps, world)
+    hbm, tf, kind = measured_peaks()
+    value = flops * world / t / 1e12
+    line = {"metric": ENGINE_WORKLOADS[args.workload]["metric"], "value": value,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "e2e": {"value": flops * world / t_e2e / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": t_e2e * 1e3},
+            "gpu_launches": None if launches is None else launches * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "whole forward (conv GEMMs dominate)",
+                         "achieved": value / world, "peak": tf, "unit": "TFLOP/s",
+                         "frac": value / world / tf, "peak_source": kind, "traffic": None,
+                         "flops_per_forward": flops,
+                         "note": "small per-utterance shapes: launch- and latency-bound"}}
+    if clk:
+        line["clocks"] = clk
+    del keep
     return line
 
 
@@ -1017,7 +1247,8 @@ def run_t2s_batch(args, rank, local, world):
 
 
 WORKLOADS = {"t2s_decode_b1": run_t2s, "gemm_ffn_up": run_gemm1, "sovits_decoder": run_decoder,
-             "gemv_t2s": run_gemv_t2s, "encoder": run_encoder, "t2s_decode_b64": run_t2s_batch, "gemm": run_gemm_shape}
+             "gemv_t2s": run_gemv_t2s, "encoder": run_encoder, "hubert_front": run_engine,
+             "sovits_latent": run_engine, "sv": run_engine, "t2s_decode_b64": run_t2s_batch, "gemm": run_gemm_shape}
 
 
 def run_reference(args, rank, world):
@@ -1055,6 +1286,8 @@ def main():
     ap.add_argument("--impl", default="gsvk", choices=["gsvk", "reference"])
     ap.add_argument("--workload", default="t2s_decode_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-launch-count", action="store_true",
+                    help="skip the profiler-based kernel count (e.g. under ncu)")
     ap.add_argument("--encoder", default="bert", choices=["bert", "hubert"])
     ap.add_argument("--gemm-shape", default="4096,4096,1024",
                     help="M,N,K of the gemm workload")

@@ -23,10 +23,11 @@ struct gsvk_hubert_front;
 namespace gsvk {
 namespace {
 
-// cols[t][c*k + kk] = f16(x[(t*stride + kk - pad) * x_ld + c]) for c < ci,
-// kk < k, zero outside [0, t_in) and in the padding columns [ci*k, kp).  One
-// thread per (t, column); consecutive threads take consecutive channels of
-// one tap (coalesced reads of a channels-last row).
+// cols[t][kk*ci + c] = f16(x[(t*stride + kk - pad) * x_ld + c]) for c < ci,
+// kk < k, zero outside [0, t_in) and in the padding columns [ci*k, kp): tap-
+// major columns, so that a tap's columns are one contiguous channels-last
+// row of x (coalesced reads and writes); the weights are permuted to the same
+// column order once at create.  One thread per (t, column).
 __global__ void im2col_f16_kernel(const float* __restrict__ x, int x_ld, int t_in, int ci, int k,
                                   int stride, int pad, int t_out, int kp,
                                   uint16_t* __restrict__ cols) {
@@ -40,7 +41,7 @@ __global__ void im2col_f16_kernel(const float* __restrict__ x, int x_ld, int t_i
       const int kk = r / ci, c = r - kk * ci;
       const int src = t * stride + kk - pad;
       const float v = (src >= 0 && src < t_in) ? x[static_cast<size_t>(src) * x_ld + c] : 0.f;
-      row[c * k + kk] = f2h(v);
+      row[r] = f2h(v);
     } else {
       row[r] = 0;
     }
@@ -50,48 +51,60 @@ __global__ void im2col_f16_kernel(const float* __restrict__ x, int x_ld, int t_i
 // GroupNorm with one group per channel (hubert.cpp:485-500): per channel the
 // mean and the biased variance over T in fp64 (the reference's two passes),
 // rstd = 1/sqrt(var + eps) in fp64, y = float((x - mu) * rstd * g + b), then
-// GELU.  Block: 32 channels x 8 row groups; partial sums combined in a fixed
-// order.
-__global__ void __launch_bounds__(256) group_norm_gelu_kernel(float* __restrict__ y, int T, int C,
-                                                             const float* __restrict__ g,
-                                                             const float* __restrict__ b,
-                                                             double eps) {
-  __shared__ double part[8][33];
-  __shared__ double stat[2][32];
+// GELU.  Three passes spread over the whole GPU: per (32-channel, row-chunk)
+// block a partial sum (x, or (x - mu)^2 once mu is known) combined in a fixed
+// order; per channel the chunk partials summed in chunk order; then the
+// element-wise apply.
+constexpr int kGnChunks = 64;
+
+__global__ void __launch_bounds__(256) gn_partial_kernel(const float* __restrict__ y, int T, int C,
+                                                         int rows, const double* __restrict__ mu,
+                                                         double* __restrict__ part) {
+  __shared__ double sp[8][33];
   const int cl = threadIdx.x & 31, rg = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + cl;
+  const int t0 = blockIdx.y * rows, t1 = min(T, t0 + rows);
   double s = 0.0;
-  if (c < C)
-    for (int t = rg; t < T; t += 8) s += static_cast<double>(y[static_cast<size_t>(t) * C + c]);
-  part[rg][cl] = s;
-  __syncthreads();
-  if (rg == 0) {
-    double m = 0.0;
-    for (int r = 0; r < 8; ++r) m += part[r][cl];
-    stat[0][cl] = m / static_cast<double>(T);
-  }
-  __syncthreads();
-  const double mu = stat[0][cl];
-  double v = 0.0;
-  if (c < C)
-    for (int t = rg; t < T; t += 8) {
-      const double d = static_cast<double>(y[static_cast<size_t>(t) * C + c]) - mu;
-      v += d * d;
+  if (c < C) {
+    const double m = mu ? mu[c] : 0.0;
+    for (int t = t0 + rg; t < t1; t += 8) {
+      const double v = static_cast<double>(y[static_cast<size_t>(t) * C + c]);
+      s += mu ? (v - m) * (v - m) : v;
     }
-  part[rg][cl] = v;
-  __syncthreads();
-  if (rg == 0) {
-    double var = 0.0;
-    for (int r = 0; r < 8; ++r) var += part[r][cl];
-    var /= static_cast<double>(T);
-    stat[1][cl] = 1.0 / sqrt(var + eps);
   }
+  sp[rg][cl] = s;
   __syncthreads();
+  if (rg == 0 && c < C) {
+    double a = 0.0;
+    for (int r = 0; r < 8; ++r) a += sp[r][cl];
+    part[static_cast<size_t>(blockIdx.y) * C + c] = a;
+  }
+}
+
+// stat[c] = sum_r part[r][c] / T, then (rstd) 1 / sqrt(stat + eps).
+__global__ void gn_stat_kernel(const double* __restrict__ part, int chunks, int T, int C,
+                               double eps, int rstd, double* __restrict__ stat) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
-  const double rstd = stat[1][cl], gg = g[c], bb = b[c];
-  for (int t = rg; t < T; t += 8) {
-    float& p = y[static_cast<size_t>(t) * C + c];
-    p = gelu_erf(static_cast<float>((static_cast<double>(p) - mu) * rstd * gg + bb));
+  double a = 0.0;
+  for (int r = 0; r < chunks; ++r) a += part[static_cast<size_t>(r) * C + c];
+  a /= static_cast<double>(T);
+  stat[c] = rstd ? 1.0 / sqrt(a + eps) : a;
+}
+
+__global__ void gn_apply_gelu_kernel(float* __restrict__ y, int T, int C,
+                                     const double* __restrict__ mu,
+                                     const double* __restrict__ rstd,
+                                     const float* __restrict__ g, const float* __restrict__ b) {
+  const long long n = static_cast<long long>(T) * C;
+  for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < n;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(e % C);
+    const double v = __dadd_rn(
+        __dmul_rn(__dmul_rn(__dsub_rn(static_cast<double>(y[e]), mu[c]), rstd[c]),
+                  static_cast<double>(g[c])),
+        static_cast<double>(b[c]));
+    y[e] = gelu_erf(static_cast<float>(v));
   }
 }
 
@@ -113,6 +126,7 @@ struct gsvk_hubert_front {
   float *act0 = nullptr, *act1 = nullptr, *feat = nullptr, *pos_out = nullptr;
   uint16_t* cols = nullptr;
   uint16_t* feat16 = nullptr;
+  double* gn_ws = nullptr;  // [kGnChunks][C] partials, then mu [C] and rstd [C]
   std::vector<void*> allocs;
 };
 
@@ -155,6 +169,12 @@ int run_gemm(const uint16_t* a, size_t lda, const uint16_t* b, size_t ldb, size_
   g.act = act;
   g.alpha = 1.f;
   return gemm_ex_run(&g, st, true);
+}
+
+unsigned grid_cap(long long n) {
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  long long b = (n + 255) / 256;
+  return static_cast<unsigned>(b < 1 ? 1 : (b > cap ? cap : b));
 }
 
 int launch_im2col(const float* x, int x_ld, int t_in, int ci, int k, int stride, int pad,
@@ -219,11 +239,14 @@ int gsvk_hubert_front_create(const gsvk_hubert_front_config* cfg,
     }
     max_cols = std::max(max_cols, t * h->kp[i]);
     max_act = std::max(max_act, t * static_cast<size_t>(co));
-    // weights [co][ci][k] -> [co][kp] (zero padding columns)
+    // weights [co][ci][k] -> [co][kp] in the tap-major column order kk*ci + c
+    // of the im2col (zero padding columns)
     std::vector<uint16_t> wp(static_cast<size_t>(co) * h->kp[i], 0);
     for (int o = 0; o < co; ++o)
-      for (int j = 0; j < ci * k; ++j)
-        wp[static_cast<size_t>(o) * h->kp[i] + j] = w->conv_w[i][static_cast<size_t>(o) * ci * k + j];
+      for (int c = 0; c < ci; ++c)
+        for (int kk = 0; kk < k; ++kk)
+          wp[static_cast<size_t>(o) * h->kp[i] + kk * ci + c] =
+              w->conv_w[i][(static_cast<size_t>(o) * ci + c) * k + kk];
     rc = upload(h, &h->conv_w[i], wp.data(), wp.size());
     ci = co;
   }
@@ -239,11 +262,13 @@ int gsvk_hubert_front_create(const gsvk_hubert_front_config* cfg,
   if (!rc) {
     // the weight-normed fp32 positional weights, rounded to fp16 once
     // (hubert.cpp:538-539), [H][cg][PK] = group g's rows [g*cg, (g+1)*cg)
+    // in the im2col's tap-major column order kk*cg + c
     std::vector<uint16_t> p16(static_cast<size_t>(H) * cg * PK);
-    for (size_t i = 0; i < p16.size(); ++i) {
-      const __half hv = __float2half_rn(w->pos_w[i]);
-      p16[i] = *reinterpret_cast<const uint16_t*>(&hv);
-    }
+    for (int o = 0; o < H; ++o)
+      for (int c = 0; c < cg; ++c)
+        for (int kk = 0; kk < PK; ++kk)
+          p16[static_cast<size_t>(o) * cg * PK + kk * cg + c] = __half_as_ushort(
+              __float2half_rn(w->pos_w[(static_cast<size_t>(o) * cg + c) * PK + kk]));
     rc = upload(h, &h->pos_w, p16.data(), p16.size());
   }
   if (!rc) rc = upload(h, &h->pos_b, w->pos_b, H);
@@ -255,6 +280,9 @@ int gsvk_hubert_front_create(const gsvk_hubert_front_config* cfg,
   if (!rc) rc = dev_alloc(h, reinterpret_cast<void**>(&h->feat), T * H * 4);
   if (!rc) rc = dev_alloc(h, reinterpret_cast<void**>(&h->pos_out), T * H * 4);
   if (!rc) rc = dev_alloc(h, reinterpret_cast<void**>(&h->feat16), T * std::max(C6, H) * 2);
+  if (!rc)
+    rc = dev_alloc(h, reinterpret_cast<void**>(&h->gn_ws),
+                   (static_cast<size_t>(kGnChunks) + 2) * cfg->conv_dim[0] * sizeof(double));
   if (rc) {
     gsvk_hubert_front_destroy(h);
     return rc;
@@ -288,9 +316,20 @@ int gsvk_hubert_front_forward(gsvk_hubert_front_t h, const float* wav, size_t n,
                        nullptr, 0, y, co, i == 0 ? GSVK_ACT_NONE : GSVK_ACT_GELU_ERF, st)))
       return rc;
     if (i == 0) {
-      group_norm_gelu_kernel<<<(unsigned)((co + 31) / 32), 256, 0, st>>>(y, (int)t_out, co, h->gn_g,
-                                                                        h->gn_b, (double)c.ln_eps);
-      if ((rc = check_launch("group_norm_gelu_kernel"))) return rc;
+      const int T = static_cast<int>(t_out);
+      const int rows = (T + kGnChunks - 1) / kGnChunks, chunks = (T + rows - 1) / rows;
+      double* part = h->gn_ws;
+      double* mu = part + static_cast<size_t>(kGnChunks) * co;
+      double* rstd = mu + co;
+      const dim3 pg((co + 31) / 32, chunks);
+      gn_partial_kernel<<<pg, 256, 0, st>>>(y, T, co, rows, nullptr, part);
+      gn_stat_kernel<<<(co + 255) / 256, 256, 0, st>>>(part, chunks, T, co, 0.0, 0, mu);
+      gn_partial_kernel<<<pg, 256, 0, st>>>(y, T, co, rows, mu, part);
+      gn_stat_kernel<<<(co + 255) / 256, 256, 0, st>>>(part, chunks, T, co, (double)c.ln_eps, 1,
+                                                        rstd);
+      gn_apply_gelu_kernel<<<grid_cap(static_cast<long long>(T) * co), 256, 0, st>>>(
+          y, T, co, mu, rstd, h->gn_g, h->gn_b);
+      if ((rc = check_launch("group norm kernels"))) return rc;
     }
     in = y;
     t_in = t_out;
@@ -303,7 +342,7 @@ int gsvk_hubert_front_forward(gsvk_hubert_front_t h, const float* wav, size_t n,
   if ((rc = run_gemm(h->feat16, C6, h->proj_w, C6, T, H, C6, h->proj_b, nullptr, 0, h->feat, H,
                      GSVK_ACT_NONE, st)))
     return rc;
-  // positional conv: per group, cols[g][t][j*PK + kk] = f16(feat[t + kk - PK/2][g*cg + j]);
+  // positional conv: per group, cols[g][t][kk*cg + j] = f16(feat[t + kk - PK/2][g*cg + j]);
   // out = GELU(conv + b) + feat (the first T of the T + 1 outputs: SamePad)
   for (int g = 0; g < G; ++g)  // group g's channels start at g*cg of a row of H
     if ((rc = launch_im2col(h->feat + g * cg, H, (int)T, cg, PK, 1, PK / 2, (int)T, cg * PK,

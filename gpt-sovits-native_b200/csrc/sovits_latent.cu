@@ -50,25 +50,63 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// 16-byte asynchronous global -> shared copy (cp.async, L2 only), zero-
+// filling the destination when `valid` is false (the source is then not
+// read).
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Multi-head attention for one head and kAttRows query rows per CTA
 // (mha.hpp:62-202 with an all-ones mask): scores = scale * q.k (fp32 FMA
-// chain over d, then the scale), plus, with relative tables, scale *
-// q.relk[j - i + W] for |j - i| <= W (the reference's
+// chain over d in order, then the scale), plus, with relative tables, scale
+// * q.relk[j - i + W] for |j - i| <= W (the reference's
 // _relative_position_to_absolute_position gather reduces to that index);
 // softmax; out = sum_j p_j v_j in key order, then sum_r p_(i+r-W) relv[r].
-// Shared memory: Q [8][dk] | K or V tile [64][dk+1] | scores [8][Tk].
+// The K tiles and then the V tiles of 64 keys stream through two shared
+// buffers by cp.async, the next tile in flight while the current one is
+// used.  Rows of a tile are dk + 4 floats: 16-byte aligned, and a quarter
+// warp's float4 reads of 8 rows fall in distinct banks.
+// Shared memory: Q [8][dk] | 2 x tile [64][dk+4] | scores [8][Tk].
 __global__ void __launch_bounds__(256) rel_attention_kernel(
     const float* __restrict__ q, int ldq, const float* __restrict__ k, int ldk,
     const float* __restrict__ v, int ldv, int Tq, int Tk, int dk, float scale,
     const float* __restrict__ relk, const float* __restrict__ relv, int window,
     uint16_t* __restrict__ out, int ldo) {
-  extern __shared__ float sm[];
+  extern __shared__ float4 sm4[];
+  float* sm = reinterpret_cast<float*>(sm4);
   const int h = blockIdx.y, i0 = blockIdx.x * kAttRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ldt = dk + 1;
+  const int ldt = dk + 4, dk4 = dk >> 2;
   float* Qs = sm;
-  float* KV = Qs + kAttRows * dk;
-  float* S = KV + kAttTile * ldt;
+  float* buf0 = Qs + kAttRows * dk;  // two tiles, kAttTile * ldt floats apart
+  float* S = buf0 + 2 * kAttTile * ldt;
+  const int nt = (Tk + kAttTile - 1) / kAttTile;
+  // tile t < nt: keys of K; nt <= t < 2 nt: values of V
+  auto issue = [&](int t) {
+    const bool isk = t < nt;
+    const float* src = isk ? k : v;
+    const int ld = isk ? ldk : ldv, j0 = (isk ? t : t - nt) * kAttTile;
+    float* dst = buf0 + (t & 1) * kAttTile * ldt;
+    for (int e = threadIdx.x; e < kAttTile * dk4; e += blockDim.x) {
+      const int jj = e / dk4, c = e - jj * dk4, j = j0 + jj;
+      const bool ok = j < Tk;
+      cp_async16(dst + jj * ldt + 4 * c,
+                 src + static_cast<size_t>(ok ? j : 0) * ld + h * dk + 4 * c, ok);
+    }
+    cp_async_commit();
+  };
+  issue(0);
   for (int e = threadIdx.x; e < kAttRows * dk; e += blockDim.x) {
     const int r = e / dk, d = e - r * dk, i = i0 + r;
     Qs[e] = i < Tq ? q[static_cast<size_t>(i) * ldq + h * dk + d] : 0.f;
@@ -76,67 +114,86 @@ __global__ void __launch_bounds__(256) rel_attention_kernel(
   const int i = i0 + warp;
   const bool live = i < Tq;
   float* Sr = S + static_cast<size_t>(warp) * Tk;
-  const float* Qr = Qs + warp * dk;
-  for (int j0 = 0; j0 < Tk; j0 += kAttTile) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < kAttTile * dk; e += blockDim.x) {
-      const int jj = e / dk, d = e - jj * dk, j = j0 + jj;
-      KV[jj * ldt + d] = j < Tk ? k[static_cast<size_t>(j) * ldk + h * dk + d] : 0.f;
-    }
-    __syncthreads();
-    if (live)
-      for (int jj = lane; jj < kAttTile && j0 + jj < Tk; jj += 32) {
-        const float* kr = KV + jj * ldt;
-        float acc = 0.f;
-        for (int d = 0; d < dk; ++d) acc = fmaf(Qr[d], kr[d], acc);
-        Sr[j0 + jj] = scale * acc;
-      }
-  }
-  __syncwarp();
-  if (live && relk && lane <= 2 * window) {
-    const int j = i + lane - window;
-    if (j >= 0 && j < Tk) {
-      const float* rk = relk + lane * dk;
-      float acc = 0.f;
-      for (int d = 0; d < dk; ++d) acc = fmaf(Qr[d], rk[d], acc);
-      Sr[j] += scale * acc;
-    }
-  }
-  __syncwarp();
-  if (live) {
-    float mx = -INFINITY;
-    for (int j = lane; j < Tk; j += 32) mx = fmaxf(mx, Sr[j]);
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int j = lane; j < Tk; j += 32) {
-      const float e = expf(Sr[j] - mx);
-      Sr[j] = e;
-      sum += e;
-    }
-    const float inv = 1.f / warp_sum(sum);
-    for (int j = lane; j < Tk; j += 32) Sr[j] *= inv;
-  }
-  __syncwarp();
+  const float4* Q4 = reinterpret_cast<const float4*>(Qs + warp * dk);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   const int nd = dk >> 5;
-  for (int j0 = 0; j0 < Tk; j0 += kAttTile) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < kAttTile * dk; e += blockDim.x) {
-      const int jj = e / dk, d = e - jj * dk, j = j0 + jj;
-      KV[jj * ldt + d] = j < Tk ? v[static_cast<size_t>(j) * ldv + h * dk + d] : 0.f;
+  for (int t = 0; t < 2 * nt; ++t) {
+    if (t + 1 < 2 * nt) {
+      issue(t + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
-    if (live) {
-      const int n = min(kAttTile, Tk - j0);
-      for (int jj = 0; jj < n; ++jj) {
-        const float p = Sr[j0 + jj];
-        if (p == 0.f) continue;
-        const float* vr = KV + jj * ldt + lane;
+    const float* tile = buf0 + (t & 1) * kAttTile * ldt;
+    if (t < nt) {
+      // scores of keys j0 + lane and j0 + lane + 32
+      const int j0 = t * kAttTile;
+      if (live) {
+        const float4* ka = reinterpret_cast<const float4*>(tile + lane * ldt);
+        const float4* kb = reinterpret_cast<const float4*>(tile + (lane + 32) * ldt);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < dk4; ++c) {
+          const float4 qv = Q4[c], x = ka[c], y = kb[c];
+          a0 = fmaf(qv.x, x.x, a0);
+          a0 = fmaf(qv.y, x.y, a0);
+          a0 = fmaf(qv.z, x.z, a0);
+          a0 = fmaf(qv.w, x.w, a0);
+          a1 = fmaf(qv.x, y.x, a1);
+          a1 = fmaf(qv.y, y.y, a1);
+          a1 = fmaf(qv.z, y.z, a1);
+          a1 = fmaf(qv.w, y.w, a1);
+        }
+        if (j0 + lane < Tk) Sr[j0 + lane] = scale * a0;
+        if (j0 + lane + 32 < Tk) Sr[j0 + lane + 32] = scale * a1;
+      }
+    } else {
+      if (t == nt && live) {
+        __syncwarp();
+        if (relk && lane <= 2 * window) {
+          const int j = i + lane - window;
+          if (j >= 0 && j < Tk) {
+            const float4* rk = reinterpret_cast<const float4*>(relk + lane * dk);
+            float a0 = 0.f;
+            for (int c = 0; c < dk4; ++c) {
+              const float4 qv = Q4[c], x = rk[c];
+              a0 = fmaf(qv.x, x.x, a0);
+              a0 = fmaf(qv.y, x.y, a0);
+              a0 = fmaf(qv.z, x.z, a0);
+              a0 = fmaf(qv.w, x.w, a0);
+            }
+            Sr[j] += scale * a0;
+          }
+        }
+        __syncwarp();
+        float mx = -INFINITY;
+        for (int j = lane; j < Tk; j += 32) mx = fmaxf(mx, Sr[j]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int j = lane; j < Tk; j += 32) {
+          const float e = expf(Sr[j] - mx);
+          Sr[j] = e;
+          sum += e;
+        }
+        const float inv = 1.f / warp_sum(sum);
+        for (int j = lane; j < Tk; j += 32) Sr[j] *= inv;
+        __syncwarp();
+      }
+      if (live) {
+        const int j0 = (t - nt) * kAttTile, n = min(kAttTile, Tk - j0);
+        const float* vr = tile + lane;
+#pragma unroll 4
+        for (int jj = 0; jj < n; ++jj) {
+          const float p = Sr[j0 + jj];
+          if (p == 0.f) continue;
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (u < nd) acc[u] = __fadd_rn(acc[u], __fmul_rn(p, vr[32 * u]));
+          for (int u = 0; u < 4; ++u)
+            if (u < nd) acc[u] = __fadd_rn(acc[u], __fmul_rn(p, vr[jj * ldt + 32 * u]));
+        }
       }
     }
+    __syncthreads();
   }
   if (!live) return;
   if (relv)
@@ -488,13 +545,18 @@ int conv(const DConv& c, const uint16_t* x, int T, float* y, uint16_t* y16, cons
 }
 
 size_t att_smem(int dk, int Tk) {
-  return (static_cast<size_t>(kAttRows) * dk + static_cast<size_t>(kAttTile) * (dk + 1) +
+  return (static_cast<size_t>(kAttRows) * dk + 2 * static_cast<size_t>(kAttTile) * (dk + 4) +
           static_cast<size_t>(kAttRows) * Tk) * sizeof(float);
 }
 
 int attention(const float* q, int ldq, const float* k, int ldk,
               const float* v, int ldv, int Tq, int Tk, int heads, int dk, const float* relk,
               const float* relv, int window, uint16_t* out, int ldo, cudaStream_t st) {
+  // the kernel's 16-byte copies need 16-byte rows and bases
+  if (ldq % 4 || ldk % 4 || ldv % 4 || dk % 32 || dk > 128 ||
+      (reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(relk) | reinterpret_cast<uintptr_t>(relv)) % 16)
+    return fail(GSVK_ERR_ALIGN, "sovits attention: unaligned operands");
   const size_t smem = att_smem(dk, Tk);
   dim3 grid((Tq + kAttRows - 1) / kAttRows, heads);
   rel_attention_kernel<<<grid, 256, smem, st>>>(q, ldq, k, ldk, v, ldv, Tq, Tk, dk,
@@ -587,7 +649,8 @@ int load_flow(gsvk_sovits_latent* h, const Src& S) {
       HConv t = pre;
       for (int o = 0; o < C; ++o)
         for (int j = 0; j < half; ++j)
-          t.w[static_cast<size_t>(o) * half + j] = pre.w[static_cast<size_t>(o) * half + half - 1 - j];
+          t.w[static_cast<size_t>(o) * half + j] =
+              pre.w[static_cast<size_t>(o) * half + half - 1 - j];
       pre = t;
     }
     {  // x1 -= m as (-W) h + (-b) + x1, rows in physical order
@@ -608,7 +671,8 @@ int load_flow(gsvk_sovits_latent* h, const Src& S) {
     L.res.resize(nl);
     L.skip.resize(nl);
     for (int l = 0; l < nl && !rc; ++l) {
-      HConv in = load_conv(S, p + ".enc.in_layers." + std::to_string(l), 2 * C, C, c.wn_kernel, &rc);
+      HConv in =
+          load_conv(S, p + ".enc.in_layers." + std::to_string(l), 2 * C, C, c.wn_kernel, &rc);
       const bool last = l + 1 == nl;
       HConv rs = load_conv(S, p + ".enc.res_skip_layers." + std::to_string(l), last ? C : 2 * C,
                            C, 1, &rc);
@@ -632,7 +696,8 @@ int create_impl(gsvk_sovits_latent* h, const Src& S) {
   if (!rc && (embed.empty() || embed.size() % D))
     rc = fail(GSVK_ERR_INVALID, "sovits_latent_create: codebook is not [n][%d]", D);
   if (!rc) h->n_codebook = embed.size() / D;
-  std::vector<float> temb = rc ? std::vector<float>() : S.f32("enc_p.text_embedding.weight", 0, &rc);
+  std::vector<float> temb;
+  if (!rc) temb = S.f32("enc_p.text_embedding.weight", 0, &rc);
   if (!rc && (temb.empty() || temb.size() % C))
     rc = fail(GSVK_ERR_INVALID, "sovits_latent_create: text embedding is not [n][%d]", C);
   if (!rc) h->n_symbols = temb.size() / C;
@@ -716,7 +781,8 @@ int gsvk_sovits_latent_destroy(gsvk_sovits_latent_t h) {
 
 int gsvk_sovits_latent_create(const gsvk_sovits_latent_config* cfg, const gsvk_gsv_tensor* tensors,
                               size_t n, gsvk_sovits_latent_t* out) {
-  if (!cfg || !tensors || !out) return fail(GSVK_ERR_INVALID, "sovits_latent_create: null argument");
+  if (!cfg || !tensors || !out)
+    return fail(GSVK_ERR_INVALID, "sovits_latent_create: null argument");
   *out = nullptr;
   if (!gsvk_available()) return fail(GSVK_ERR_NODEV, "gsvk_device_init() not called");
   const auto& c = *cfg;
@@ -732,7 +798,9 @@ int gsvk_sovits_latent_create(const gsvk_sovits_latent_config* cfg, const gsvk_g
       c.wn_kernel % 2 == 1 && c.max_codes > 0 && c.max_phones > 0 &&
       2 * c.max_codes <= static_cast<size_t>(kMaxFrames) &&
       c.max_phones <= static_cast<size_t>(kMaxFrames);
-  if (!ok) return fail(GSVK_ERR_INVALID, "sovits_latent_create: configuration outside the supported envelope");
+  if (!ok)
+    return fail(GSVK_ERR_INVALID,
+                "sovits_latent_create: configuration outside the supported envelope");
   auto* h = new gsvk_sovits_latent();
   h->cfg = c;
   h->Tq_max = static_cast<int>(2 * c.max_codes);
@@ -763,7 +831,8 @@ int gsvk_sovits_latent_forward(gsvk_sovits_latent_t h, const int64_t* codes, siz
   if (!h || !codes || !phones || !ge || !ge_text || !z)
     return fail(GSVK_ERR_INVALID, "sovits_latent_forward: null argument");
   if (n_codes == 0 || n_phones == 0 || n_codes > h->cfg.max_codes || n_phones > h->cfg.max_phones)
-    return fail(GSVK_ERR_INVALID, "sovits_latent_forward: %zu codes / %zu phones outside 1..%zu / 1..%zu",
+    return fail(GSVK_ERR_INVALID,
+                "sovits_latent_forward: %zu codes / %zu phones outside 1..%zu / 1..%zu",
                 n_codes, n_phones, h->cfg.max_codes, h->cfg.max_phones);
   for (size_t i = 0; i < n_codes; ++i)  // quantizer.hpp:30-31
     if (codes[i] < 0 || static_cast<size_t>(codes[i]) >= h->n_codebook)
@@ -806,7 +875,8 @@ int gsvk_sovits_latent_forward(gsvk_sovits_latent_t h, const int64_t* codes, siz
     add_vec_kernel<<<(MH + 255) / 256, 256, 0, st>>>(h->mo.b, ge_text, MH, h->bias_eff);
     rc = check_launch("add_vec_kernel");
   }
-  if (!rc) rc = conv(h->mo, h->att16, Tq, nullptr, h->sum16, h->c512, GSVK_ACT_NONE, st, h->bias_eff);
+  if (!rc)
+    rc = conv(h->mo, h->att16, Tq, nullptr, h->sum16, h->c512, GSVK_ACT_NONE, st, h->bias_eff);
   if (!rc) rc = conv(h->c_post, h->sum16, Tq, h->y, h->y16, nullptr, GSVK_ACT_NONE, st);
   if (!rc) rc = encoder_forward(h, h->enc[2], h->y, h->y16, Tq, st);
   if (!rc) rc = conv(h->proj, h->y16, Tq, h->stats, nullptr, nullptr, GSVK_ACT_NONE, st);
