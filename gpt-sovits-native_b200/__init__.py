@@ -76,6 +76,7 @@ SIGNATURES = {
     "gsvk_t2s_decode_kernel": (c_int, [_vp]),
     "gsvk_t2s_set_sampling": (c_int, [_vp, _vp]),
     "gsvk_set_spin_limit_for_test": (c_int, [ctypes.c_uint32]),
+    "gsvk_test_rstd": (c_int, [_vp, _vp, _sz, _vp]),
     "gsvk_hubert_front_create": (c_int, [_vp, _vp, _vp]),
     "gsvk_hubert_front_destroy": (c_int, [_vp]),
     "gsvk_hubert_front_frames": (_sz, [_vp, _sz]),

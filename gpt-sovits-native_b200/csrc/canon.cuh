@@ -89,22 +89,37 @@ __device__ __forceinline__ float group16_dot_kv(const float* q_reg, const uint16
 }
 
 // 1 / sqrt(v) rounded to float exactly as (float)(1.0 / sqrt(v)) with both
-// double operations correctly rounded (kern.cpp:55).  Fast path: CUDA's
-// double rsqrt (within a few ulp of 1/sqrt(v)), rounded to float; the
-// reference value lies within 2^-40 * y of y, so when no float rounding
-// boundary (midpoint of two adjacent floats) lies that close to y both round
-// to the same float.  Otherwise (about one call in 2^15) the exact
-// sqrt-then-divide path decides.
+// double operations correctly rounded (kern.cpp:55).
+//
+// Fast path: a float candidate r (the float reciprocal square root, then
+// moved an ulp at a time) is accepted when y = 1/sqrt(v) lies strictly inside
+// (m_lo, m_hi), the midpoints between r and its float neighbours, with a
+// relative margin of at least 2^-48.  The test is exact: m has at most 25
+// significant bits, so m*m is exact in double, and y < m <=> m^2 v > 1, whose
+// sign one fused multiply-add m^2 v - 1 gives exactly (its value s is also
+// accurate: (m - y) / y ~ s / 2).  The reference value (two correctly rounded
+// double operations) lies within 2^-51 * y of y, so it rounds to r as well.
+// Otherwise (y within the margin of a midpoint, about one call in 2^23, or a
+// non-finite or zero candidate) the exact sqrt-then-divide path decides.
 __device__ __forceinline__ float rstd_f32(double v) {
-  const double y = rsqrt(v);
-  const float r = __double2float_rn(y);
-  const double rd = static_cast<double>(r);
-  const double up = static_cast<double>(nextafterf(r, INFINITY));
-  const double dn = static_cast<double>(nextafterf(r, 0.0f));
-  const double tol = y * 0x1p-40;
-  if (fabs(y - 0.5 * (rd + up)) <= tol || fabs(y - 0.5 * (rd + dn)) <= tol)
-    return static_cast<float>(__ddiv_rn(1.0, __dsqrt_rn(v)));
-  return r;
+  float r = rsqrtf(__double2float_rn(v));
+#pragma unroll 1
+  for (int step = 0; step < 4; ++step) {
+    if (!(r > 0.0f) || isinf(r)) break;
+    const double rd = static_cast<double>(r);
+    const double mhi = 0.5 * (rd + static_cast<double>(nextafterf(r, INFINITY)));
+    const double mlo = 0.5 * (rd + static_cast<double>(nextafterf(r, 0.0f)));
+    const double shi = fma(mhi * mhi, v, -1.0);  // > 0  <=>  y < mhi
+    const double slo = fma(mlo * mlo, v, -1.0);  // < 0  <=>  y > mlo
+    if (shi > 0x1p-46 && slo < -0x1p-46) return r;
+    if (shi <= 0.0)
+      r = nextafterf(r, INFINITY);
+    else if (slo >= 0.0)
+      r = nextafterf(r, 0.0f);
+    else
+      break;  // y within the margin of a midpoint
+  }
+  return static_cast<float>(__ddiv_rn(1.0, __dsqrt_rn(v)));
 }
 
 // Sum chains of ln_canon for thread l (0..7: sum of x[l], x[l+8], ...;
@@ -189,6 +204,131 @@ __device__ __forceinline__ void ln_canon(float* buf, const float* g, const float
     if (rounded) rounded[i] = h2f(f2h(v));
   }
   __syncthreads();
+}
+
+// ln_canon's mean and rstd computed by ONE warp (any warp; several warps may
+// compute the same statistics concurrently): lanes (l & 15) run ln_canon's 16
+// chains (lanes 16-31 repeat them), every lane then holds both sums and forms
+// mean / variance / rstd itself in fp64.  Same values as ln_canon.
+__device__ __forceinline__ void warp_ln_stats(const float* buf, int n, double eps, float* mean_out,
+                                              float* rstd_out) {
+  const int lane = threadIdx.x & 31;
+  const int l = lane & 7;
+  const bool sq = (lane & 8) != 0;
+  const int vec_end = n & ~7;
+  float a = 0.f;
+  if (n == 512) {
+    a = ln_chain_fixed<512>(buf, l, sq);
+  } else {
+    for (int i = l; i < vec_end; i += 8) {
+      const float v = buf[i];
+      a = sq ? fmaf(v, v, a) : __fadd_rn(a, v);
+    }
+  }
+  // lanes 0-7 and 8-15 combine as ((0+1)+(2+3))+((4+5)+(6+7))
+  float t = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+  t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+  t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
+  const float ssum = __shfl_sync(0xffffffffu, t, 0);
+  const float qsum = __shfl_sync(0xffffffffu, t, 8);
+  double sum = static_cast<double>(ssum), sqs = static_cast<double>(qsum);
+  for (int i = vec_end; i < n; ++i) {
+    const double xv = static_cast<double>(buf[i]);
+    sum = __dadd_rn(sum, xv);
+    sqs = __dadd_rn(sqs, __dmul_rn(xv, xv));
+  }
+  const double dn = static_cast<double>(n);
+  const bool pow2 = (n & (n - 1)) == 0;
+  const double inv_n = pow2 ? 1.0 / dn : 0.0;
+  const float mean = static_cast<float>(pow2 ? __dmul_rn(sum, inv_n) : __ddiv_rn(sum, dn));
+  const double md = static_cast<double>(mean);
+  const double ex2 = pow2 ? __dmul_rn(sqs, inv_n) : __ddiv_rn(sqs, dn);
+  float var = static_cast<float>(__dsub_rn(ex2, __dmul_rn(md, md)));
+  if (!(var >= 0.0f)) {
+    double s2 = 0.0;
+    for (int i = 0; i < n; ++i) {
+      const double d = __dsub_rn(static_cast<double>(buf[i]), md);
+      s2 = __dadd_rn(s2, __dmul_rn(d, d));
+    }
+    var = static_cast<float>(pow2 ? __dmul_rn(s2, inv_n) : __ddiv_rn(s2, dn));
+  }
+  *mean_out = mean;
+  *rstd_out = rstd_f32(__dadd_rn(static_cast<double>(var), eps));
+}
+
+// One LayerNorm output element, ln_canon's arithmetic.
+__device__ __forceinline__ float ln_val(float x, float mean, float rstd, float g, float b) {
+  return fmaf(__fmul_rn(__fsub_rn(x, mean), rstd), g, b);
+}
+
+// This lane's 16 activations of the 512-wide canonical dot (xr[2b] = element
+// 64b + o0, xr[2b + 1] = 64b + o0 + 4), optionally through a LayerNorm
+// (mean, rstd, g, b) and/or rounded to fp16 values.
+__device__ __forceinline__ void lane_act512(const float* x, bool ln, float mean, float rstd, const float* g,
+                                            const float* b, bool round16, float* xr) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int i = 64 * (k >> 1) + o0 + 4 * (k & 1);
+    float v = x[i];
+    if (ln) v = ln_val(v, mean, rstd, g[i], b[i]);
+    xr[k] = round16 ? h2f(f2h(v)) : v;
+  }
+}
+
+// warp_dot32 (n = 512) with the activations in registers (lane_act512 layout).
+__device__ __forceinline__ float warp_dot512_r(const uint16_t* w, const float* xr) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+  float wv[16];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    wv[2 * b] = h2f(w[64 * b + o0]);
+    wv[2 * b + 1] = h2f(w[64 * b + o0 + 4]);
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc = fmaf(wv[j], xr[j], acc);
+  const float t = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+  const float u = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+  float s = __shfl_sync(0xffffffffu, u, 0);
+#pragma unroll
+  for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __shfl_sync(0xffffffffu, u, 4 * j));
+  return s;
+}
+
+// Two of them sharing the activations (chains interleaved).
+__device__ __forceinline__ void warp_dot512x2_r(const uint16_t* w0, const uint16_t* w1, const float* xr,
+                                                float* r0, float* r1) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+  float u0[16], u1[16];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    u0[2 * b] = h2f(w0[64 * b + o0]);
+    u0[2 * b + 1] = h2f(w0[64 * b + o0 + 4]);
+    u1[2 * b] = h2f(w1[64 * b + o0]);
+    u1[2 * b + 1] = h2f(w1[64 * b + o0 + 4]);
+  }
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    a0 = fmaf(u0[j], xr[j], a0);
+    a1 = fmaf(u1[j], xr[j], a1);
+  }
+  float t0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
+  float t1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+  t0 = __fadd_rn(t0, __shfl_xor_sync(0xffffffffu, t0, 2));
+  t1 = __fadd_rn(t1, __shfl_xor_sync(0xffffffffu, t1, 2));
+  float s0 = __shfl_sync(0xffffffffu, t0, 0), s1 = __shfl_sync(0xffffffffu, t1, 0);
+#pragma unroll
+  for (int j = 1; j < 8; ++j) {
+    s0 = __fadd_rn(s0, __shfl_sync(0xffffffffu, t0, 4 * j));
+    s1 = __fadd_rn(s1, __shfl_sync(0xffffffffu, t1, 4 * j));
+  }
+  *r0 = s0;
+  *r1 = s1;
 }
 
 // Two canonical dots sharing x (independent chains interleaved for ILP).

@@ -924,6 +924,11 @@ int canon_gemm(const uint16_t* A, int lda, const uint16_t* B, int ldb, int M, in
       A, lda, B, ldb, M, N, K, bias, relu, res, ldr, c32, ldc, c16, ldc16);
   return check_launch("canon_gemm_kernel");
 }
+__global__ void rstd_check_kernel(const double* __restrict__ v, float* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = rstd_f32(v[i]);
+}
+
 }  // namespace
 
 // --------------------------------------------------------------- host engine
@@ -1051,7 +1056,7 @@ int decode_plan(gsvk_t2s* e, int G) {
 void flow_plan(gsvk_t2s* e, int max_optin) {
   const int D = e->D, F = e->F, V = e->V, H = e->H, HD = e->HD, sms = sm_count();
   const int vp = (V + 1) & ~1;
-  if (D % 2 || F % 2 || std::max(std::max(D, F), vp) > 2 * kThreads * kFlMaxPairs) return;
+  if (D != kFlD || F % 2 || std::max(std::max(D, F), vp) > 2 * kThreads * kFlMaxPairs) return;
   const void* fn = HD == 32 ? (const void*)t2s_flow_kernel<32> : (const void*)t2s_flow_kernel<64>;
   int best_cs = 0, best_g = 0, best_rounds = 0;
   FlLayout best_y{};
@@ -1544,6 +1549,15 @@ int gsvk_t2s_decode_kernel(gsvk_t2s_t h) { return h ? h->decode_kind : 0; }
 int gsvk_set_spin_limit_for_test(uint32_t polls) {
   test_spin_limit() = polls;
   return GSVK_OK;
+}
+
+int gsvk_test_rstd(const double* v, float* out, size_t n, gsvk_stream_t stream) {
+  if (!v || !out || !n) return fail(GSVK_ERR_INVALID, "test_rstd: null pointer or zero size");
+  if (n > 0x7fffffffu) return fail(GSVK_ERR_UNSUPPORTED, "test_rstd: n too large");
+  const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
+  rstd_check_kernel<<<blocks, 256, 0, as_cuda(stream)>>>(v, out, static_cast<int>(n));
+  if (int rc = check_launch("rstd_check_kernel")) return rc;
+  return check_cuda(cudaStreamSynchronize(as_cuda(stream)), "test_rstd");
 }
 
 int gsvk_t2s_set_sampling(gsvk_t2s_t h, const gsvk_t2s_sampling* sp) {

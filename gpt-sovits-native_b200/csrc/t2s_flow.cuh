@@ -37,6 +37,7 @@
 
 constexpr uint32_t kFlSpin = 1u << 22;  // polls of one exchange word pair (seconds)
 constexpr int kFlMaxPairs = 8;          // exchange vectors up to 8 x 2 x 256 = 4096 words
+constexpr int kFlD = 512;               // model width: the dots keep their activations in registers
 
 // Shared-memory plan (byte offsets), identical on host and device.
 struct FlLayout {
@@ -104,6 +105,11 @@ __device__ __forceinline__ void xw_put(uint64_t* p, float v, uint32_t ep) {
   const uint64_t w = (static_cast<uint64_t>(ep) << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+// After a thread's last exchange store of a phase: wait until its stores are
+// performed at GPU scope, which pushes them out of the SM at once instead of
+// whenever the store path drains (measured: a 132-CTA exchange round of
+// 1.38 us becomes 1.06 us).
+__device__ __forceinline__ void xw_flush() { __threadfence(); }
 __device__ __forceinline__ void xw_get2(const uint64_t* p, uint64_t& a, uint64_t& b) {
   asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
@@ -169,35 +175,34 @@ __device__ __forceinline__ bool fl_poll(const uint64_t* X, int n, uint32_t ep, f
   return __syncthreads_or(ok ? 0 : 1) == 0;
 }
 
-// One out-of-line copy of the LayerNorm for every call site (instruction
-// cache footprint of the per-layer loop).
-__device__ __forceinline__ void fl_ln(float* buf, const float* g, const float* b, int n, double eps,
-                                   float* scratch, float* rounded) {
-  ln_canon(buf, g, b, n, eps, scratch, rounded);
-}
-
-// W1 rows r in [a0, a1) of this CTA: relu(dot32(W1[r], act) + bias) -> xf.
-__device__ __forceinline__ void fl_w1_rows(const uint16_t* W1, const float* act, int a0, int a1, int D,
+// W1 rows r in [a0, a1) of this CTA: relu(dot32(W1[r], x) + bias) -> xf,
+// x = fp16-rounded LN1(h) formed per lane from the raw rows h.
+__device__ __forceinline__ void fl_w1_rows(const uint16_t* W1, const float* h, float mean, float rstd,
+                                        const float* g, const float* b, int a0, int a1, int D,
                                         const float* bias, uint64_t* xf, uint32_t ep) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (a0 + 2 * warp >= a1) return;
   auto put = [&](int r, float acc) {
     const float v = __fadd_rn(acc, bias[r - a0]);
     xw_put(xf + r, v > 0.f ? v : 0.f, ep);
   };
+  float xr[16];
+  lane_act512(h, true, mean, rstd, g, b, true, xr);
   for (int r = a0 + 2 * warp; r < a1; r += 2 * kWarps) {
     if (r + 1 < a1) {
       float r0, r1;
-      warp_dot32x2(W1 + static_cast<size_t>(r - a0) * D, W1 + static_cast<size_t>(r + 1 - a0) * D,
-                   act, D, &r0, &r1);
+      warp_dot512x2_r(W1 + static_cast<size_t>(r - a0) * D, W1 + static_cast<size_t>(r + 1 - a0) * D, xr,
+                      &r0, &r1);
       if (lane == 0) {
         put(r, r0);
         put(r + 1, r1);
       }
     } else {
-      const float r0 = warp_dot32(W1 + static_cast<size_t>(r - a0) * D, act, D);
+      const float r0 = warp_dot512_r(W1 + static_cast<size_t>(r - a0) * D, xr);
       if (lane == 0) put(r, r0);
     }
   }
+  if (lane == 0) xw_flush();
 }
 
 // attn_combine's arithmetic with the per-record work in parallel: lane c
@@ -216,12 +221,25 @@ __device__ __forceinline__ void fl_combine(const float* rec, int nch, float* out
   for (int c0 = 0; c0 < nch; c0 += 32) {
     const float wl = c0 + lane < nch ? exp_det(__fsub_rn(rec[(c0 + lane) * R], M)) : 0.f;
     const int n = min(32, nch - c0);
-    for (int j = 0; j < n; ++j) {
-      const float w = __shfl_sync(0xffffffffu, wl, j);
-      const float* r = rec + (c0 + j) * R;
-      L = __fadd_rn(L, __fmul_rn(r[1], w));
-      O0 = __fadd_rn(O0, __fmul_rn(r[4 + lane], w));
-      if (HD > 32) O1 = __fadd_rn(O1, __fmul_rn(r[4 + 32 + lane], w));
+    // eight records at a time: every load and weight ahead of the chains
+    for (int j0 = 0; j0 < n; j0 += 8) {
+      float w[8], rl[8], r0[8], r1[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        w[u] = __shfl_sync(0xffffffffu, wl, j0 + u);
+        const float* r = rec + (c0 + min(j0 + u, n - 1)) * R;  // in bounds; unused past n
+        rl[u] = r[1];
+        r0[u] = r[4 + lane];
+        r1[u] = HD > 32 ? r[4 + 32 + lane] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (j0 + u < n) {
+          L = __fadd_rn(L, __fmul_rn(rl[u], w[u]));
+          O0 = __fadd_rn(O0, __fmul_rn(r0[u], w[u]));
+          if (HD > 32) O1 = __fadd_rn(O1, __fmul_rn(r1[u], w[u]));
+        }
+      }
     }
   }
   const float inv = __fdiv_rn(1.0f, L);
@@ -502,13 +520,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int l0 = row_lo(V, G, c), l1 = row_lo(V, G, c + 1);
   const int nq = j1 - j0, no = o1 - o0, na = a1 - a0, nb = b1 - b0;
   auto qkv_row = [&](int j) { return (j / HD) * D + head * HD + (j % HD); };
+  // The bias this thread stages for layer l: the address is chosen first and
+  // loaded once (a select between loaded values would wait for the loads).
+  // Threads without a row load any valid word; bsm ignores it.
   auto bias_of = [&](int l) -> float {
     const size_t L_ = static_cast<size_t>(l);
-    if (tid < nq) return __ldg(m.bqkv + L_ * 3 * D + qkv_row(j0 + tid));
-    if (tid < nq + no) return __ldg(m.bout + L_ * D + o0 + tid - nq);
-    if (tid < nq + no + na) return __ldg(m.b1 + L_ * F + a0 + tid - nq - no);
-    if (tid < nq + no + na + nb) return __ldg(m.b2 + L_ * D + b0 + tid - nq - no - na);
-    return 0.f;
+    const float* p = m.bout;
+    if (tid < nq)
+      p = m.bqkv + L_ * 3 * D + qkv_row(j0 + tid);
+    else if (tid < nq + no)
+      p = m.bout + L_ * D + o0 + tid - nq;
+    else if (tid < nq + no + na)
+      p = m.b1 + L_ * F + a0 + tid - nq - no;
+    else if (tid < nq + no + na + nb)
+      p = m.b2 + L_ * D + b0 + tid - nq - no - na;
+    return __ldg(p);
   };
   // Part `part` (0..4) of layer l's weight slices into buffer `buf`; part 0
   // posts the whole layer's byte count.
@@ -776,11 +802,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                      failed, f.spin))
           failed = true;
         GSVK_FTR(16 + 16 * l + 15);
-        fl_ln(xs, lnb + 2 * D, lnb + 3 * D, D, m.eps, red, act);  // LN2 of layer l - 1
-      } else {
-        for (int i = tid; i < D; i += kThreads) act[i] = h2f(f2h(xs[i]));
       }
       failed = __syncthreads_or(failed ? 1 : 0) != 0;  // one decision for the whole CTA
+      // LN2 of layer l - 1 (layer 0 takes its input as it is): every warp
+      // forms the statistics itself and normalises the elements it reads, so
+      // xs keeps the raw rows and no CTA barrier separates LN2 from the dots
+      const bool ln2 = l > 0;
+      float mu2 = 0.f, rs2 = 0.f;
+      if (ln2) warp_ln_stats(xs, kFlD, m.eps, &mu2, &rs2);
       GSVK_FTR(16 + 16 * l + 10);
       {
         auto put = [&](int j, float acc) {
@@ -790,15 +819,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float val = j < HD ? v : h2f(f2h(v));
           if (lane < cs) st_cluster_f32(cluster_addr(qkv + j, lane), val);
         };
+        float xr[16];  // fp16-rounded activations (the reference's fp16 x)
+        lane_act512(xs, ln2, mu2, rs2, lnb + 2 * D, lnb + 3 * D, true, xr);
         for (int j = j0 + 2 * warp; j < j1; j += 2 * kWarps) {
           if (j + 1 < j1) {
             float r0, r1;
-            warp_dot32x2(Wq + static_cast<size_t>(j - j0) * D, Wq + static_cast<size_t>(j + 1 - j0) * D,
-                         act, D, &r0, &r1);
+            warp_dot512x2_r(Wq + static_cast<size_t>(j - j0) * D, Wq + static_cast<size_t>(j + 1 - j0) * D,
+                            xr, &r0, &r1);
             put(j, r0);
             put(j + 1, r1);
           } else {
-            put(j, warp_dot32(Wq + static_cast<size_t>(j - j0) * D, act, D));
+            put(j, warp_dot512_r(Wq + static_cast<size_t>(j - j0) * D, xr));
           }
         }
       }
@@ -873,6 +904,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t* xa = f.xattn + static_cast<size_t>(par) * D + head * HD;
         xw_put(xa + lane, h2f(f2h(r0)), ep);
         if (HD > 32) xw_put(xa + 32 + lane, h2f(f2h(r1)), ep);
+        xw_flush();
       }
       GSVK_FTR(16 + 16 * l + 13);
       {  // the next attention's tiles (this step's next layer, or the next step's first)
@@ -886,18 +918,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------------ out-proj rows
       if (!fl_poll(f.xattn + static_cast<size_t>(par) * D, D, ep, act, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 4);
-      for (int r = o0 + warp; r < o1; r += kWarps) {
-        const float acc = warp_dot32(Wo + static_cast<size_t>(r - o0) * D, act, D);
-        if (lane == 0)
-          xw_put(f.xhpre + static_cast<size_t>(par) * D + r,
-                 __fadd_rn(__fadd_rn(acc, bsm[nq + r - o0]), xs[r]), ep);
+      if (o0 + warp < o1) {
+        float xr[16];
+        lane_act512(act, false, 0.f, 0.f, nullptr, nullptr, false, xr);
+        for (int r = o0 + warp; r < o1; r += kWarps) {
+          const float acc = warp_dot512_r(Wo + static_cast<size_t>(r - o0) * D, xr);
+          if (lane == 0) {
+            // the residual: this layer's input row (LN2 output of layer l - 1)
+            const float xin = ln2 ? ln_val(xs[r], mu2, rs2, lnb[2 * D + r], lnb[3 * D + r]) : xs[r];
+            xw_put(f.xhpre + static_cast<size_t>(par) * D + r, __fadd_rn(__fadd_rn(acc, bsm[nq + r - o0]), xin),
+                   ep);
+          }
+        }
+        if (lane == 0) xw_flush();
       }
       // ------------------------------------------- LN1, W1 rows + ReLU
       if (!fl_poll(f.xhpre + static_cast<size_t>(par) * D, D, ep, hs, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 5);
-      fl_ln(hs, lnb, lnb + D, D, m.eps, red, act);
+      // LN1 per warp as LN2 above: hs keeps the raw rows
+      float mu1, rs1;
+      warp_ln_stats(hs, kFlD, m.eps, &mu1, &rs1);
       GSVK_FTR(16 + 16 * l + 12);
-      fl_w1_rows(W1, act, a0, a1, D, bsm + nq + no, f.xff + static_cast<size_t>(par) * F, ep);
+      fl_w1_rows(W1, hs, mu1, rs1, lnb, lnb + D, a0, a1, D, bsm + nq + no, f.xff + static_cast<size_t>(par) * F,
+                 ep);
       GSVK_FTR(16 + 16 * l + 6);
       // ------------------------------------------------------- W2 rows
       if (!fl_poll(f.xff + static_cast<size_t>(par) * F, F, ep, act, m.status, failed, f.spin)) failed = true;
@@ -909,13 +952,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           lane_load_x(act, xr);
           for (int r = b0 + warp; r < b1; r += kWarps) {
             const float acc = lane_dot_ordered(W2 + static_cast<size_t>(r - b0) * F, xr);
-            if (lane == 0) xw_put(xx + r, __fadd_rn(__fadd_rn(acc, bsm[nq + no + na + r - b0]), hs[r]), ep);
+            if (lane == 0)
+              xw_put(xx + r, __fadd_rn(__fadd_rn(acc, bsm[nq + no + na + r - b0]),
+                                       ln_val(hs[r], mu1, rs1, lnb[r], lnb[D + r])), ep);
           }
+          if (lane == 0 && b0 + warp < b1) xw_flush();
         } else {
           for (int r = b0 + warp; r < b1; r += kWarps) {
             const float acc = warp_dot32(W2 + static_cast<size_t>(r - b0) * F, act, F);
-            if (lane == 0) xw_put(xx + r, __fadd_rn(__fadd_rn(acc, bsm[nq + no + na + r - b0]), hs[r]), ep);
+            if (lane == 0)
+              xw_put(xx + r, __fadd_rn(__fadd_rn(acc, bsm[nq + no + na + r - b0]),
+                                       ln_val(hs[r], mu1, rs1, lnb[r], lnb[D + r])), ep);
           }
+          if (lane == 0 && b0 + warp < b1) xw_flush();
         }
       }
       GSVK_FTR(16 + 16 * l + 8);
@@ -933,16 +982,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ep_l = ep_step + static_cast<uint32_t>(L) + 1;
       if (!fl_poll(f.xxpre + static_cast<size_t>(ep_x & 1u) * D, D, ep_x, xs, m.status, failed, f.spin))
         failed = true;
-      fl_ln(xs, lnf, lnf + D, D, m.eps, red, nullptr);
+      // the final LayerNorm per warp, fp32 activations
+      float muf, rsf, xr[16];
+      warp_ln_stats(xs, kFlD, m.eps, &muf, &rsf);
+      lane_act512(xs, true, muf, rsf, lnf, lnf + D, false, xr);
       uint64_t* xl = f.xlog + static_cast<size_t>(ep_l & 1u) * f.vp;
       for (int r = l0 + warp; r < l1; r += kWarps) {
-        const float acc = warp_dot32(wlog + static_cast<size_t>(r - l0) * D, xs, D);
+        const float acc = warp_dot512_r(wlog + static_cast<size_t>(r - l0) * D, xr);
         if (lane == 0) {
           xw_put(xl + r, acc, ep_l);
           m.logits[r] = acc;
           if (r == V - 1 && f.vp > V) xw_put(xl + V, 0.f, ep_l);  // the padding word
         }
       }
+      if (lane == 0 && l0 + warp < l1) xw_flush();
       GSVK_FTR(2);
     }
   }

@@ -581,6 +581,12 @@ int gsvk_t2s_decode_kernel(gsvk_t2s_t h);
  * test can make a real device wait run out without faulting or hanging the
  * GPU.  0 restores the default.  Process-wide. */
 int gsvk_set_spin_limit_for_test(uint32_t polls);
+/* Check of the LayerNorm's reciprocal square root for tests (no counterpart
+ * in the reference; the value it reproduces is kern.cpp:55's
+ * (float)(1.0 / std::sqrt(v)) with correctly rounded double operations):
+ * out[i] = the device routine every T2S LayerNorm uses, for n device doubles
+ * v.  Synchronous on the stream. */
+int gsvk_test_rstd(const double* v, float* out, size_t n, gsvk_stream_t stream);
 /* Sampling of the decode steps: SamplingParams (t2s_engine.hpp:69-77) and
  * topk_sample (t2s_engine.cpp:1640-1737).  mode 0 (the default) is greedy;
  * mode 1 applies the repetition penalty rep_penalty once per distinct history
