@@ -43,7 +43,7 @@ constexpr int kFlD = 512;               // model width: the dots keep their acti
 struct FlLayout {
   int mq, mo, m1, m2, ml;     // max rows per CTA: qkv (per cluster member), out, W1, W2, logits
   uint32_t ln_off, layer_bytes;
-  uint32_t wbuf, wlog, lnf, ktile, vtile, rec, slots, qkv, xs, hs, act, red, bsm, ctl, kvstage,
+  uint32_t wbuf, wlog, lnf, ktile, vtile, rec, slots, qkv, qkvw, xs, hs, act, red, bsm, ctl, kvstage,
       mbar, seen, svals, sidx, mt, total;
 };
 
@@ -71,6 +71,7 @@ __host__ __device__ inline FlLayout fl_layout(int D, int F, int V, int HD, int c
   Y.rec = o;   o = fl_al(o + static_cast<uint32_t>(nmax) * (HD + 4) * 4, 128);
   Y.slots = o; o = fl_al(o + static_cast<uint32_t>(kSlots) * (kChunk + 8) * 4, 128);
   Y.qkv = o;   o = fl_al(o + 3u * HD * 4, 128);
+  Y.qkvw = o;  o = fl_al(o + 2u * 3u * HD * 8, 128);  // {value, epoch} words, by layer parity
   Y.xs = o;    o = fl_al(o + 4u * D, 128);
   Y.hs = o;    o = fl_al(o + 4u * D, 128);
   Y.act = o;   o = fl_al(o + 4u * act, 128);
@@ -250,6 +251,14 @@ __device__ __forceinline__ void fl_combine(const float* rec, int nch, float* out
 // --------------------------------------------------------------- cluster ops
 __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u64(uint32_t addr, uint64_t v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_volatile_shared_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
 }
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
@@ -496,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* rec = reinterpret_cast<float*>(smem + Y.rec);
   float* slots = reinterpret_cast<float*>(smem + Y.slots);
   float* qkv = reinterpret_cast<float*>(smem + Y.qkv);
+  uint64_t* qkvw = reinterpret_cast<uint64_t*>(smem + Y.qkvw);
   float* xs = reinterpret_cast<float*>(smem + Y.xs);
   float* hs = reinterpret_cast<float*>(smem + Y.hs);
   float* act = reinterpret_cast<float*>(smem + Y.act);
@@ -620,6 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   for (int cc = tid; cc < V; cc += kThreads) seen[cc] = 0;
+  for (int i = tid; i < 2 * 3 * HD; i += kThreads) qkvw[i] = 0;  // epoch 0 is never used
   __syncthreads();
   for (int i = tid; i < a.n_hist; i += kThreads) {
     const int t = a.hist[i];
@@ -817,7 +828,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           // (k and v as their fp16 cache values)
           const float v = __fadd_rn(acc, bsm[j - j0]);
           const float val = j < HD ? v : h2f(f2h(v));
-          if (lane < cs) st_cluster_f32(cluster_addr(qkv + j, lane), val);
+          if (lane < cs)
+            st_cluster_u64(cluster_addr(qkvw + par * 3 * HD + j, lane),
+                           (static_cast<uint64_t>(ep) << 32) | __float_as_uint(val));
         };
         float xr[16];  // fp16-rounded activations (the reference's fp16 x)
         lane_act512(xs, ln2, mu2, rs2, lnb + 2 * D, lnb + 3 * D, true, xr);
@@ -834,7 +847,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       GSVK_FTR(16 + 16 * l + 0);
-      fl_cluster_sync();
+      // this head's q, k and v from every member: each word carries this
+      // layer's epoch, so the CTA polls its own shared memory (no cluster
+      // barrier) and keeps a plain copy for the chunks
+      if (is_head) {
+        if (tid < 3 * HD && !failed) {
+          const uint64_t* w = qkvw + par * 3 * HD + tid;
+          uint64_t v = ld_volatile_shared_u64(w);
+          for (uint32_t it = 0; static_cast<uint32_t>(v >> 32) != ep; ++it) {
+            if (it >= f.spin) {
+              atomicExch(m.status, DEV_TIMEOUT);
+              failed = true;
+              break;
+            }
+            if ((it & 255u) == 255u && *reinterpret_cast<volatile uint32_t*>(m.status) != 0) {
+              failed = true;
+              break;
+            }
+            v = ld_volatile_shared_u64(w);
+          }
+          qkv[tid] = __uint_as_float(static_cast<uint32_t>(v));
+        }
+        failed = __syncthreads_or(failed ? 1 : 0) != 0;
+      }
       GSVK_FTR(16 + 16 * l + 1);
       if (is_head && rank == cs - 1 && warp == kWarps - 1) {
         // the head's new K and V rows (fp16) into the cache by bulk copy (the
