@@ -43,7 +43,7 @@ constexpr int kFlD = 512;               // model width: the dots keep their acti
 struct FlLayout {
   int mq, mo, m1, m2, ml;     // max rows per CTA: qkv (per cluster member), out, W1, W2, logits
   uint32_t ln_off, layer_bytes;
-  uint32_t wbuf, wlog, lnf, ktile, vtile, rec, slots, qkv, qkvw, xs, hs, act, red, bsm, ctl, kvstage,
+  uint32_t wbuf, wlog, lnf, ktile, vtile, rec, recw, slots, qkv, qkvw, xs, hs, act, red, bsm, ctl, kvstage,
       mbar, seen, svals, sidx, mt, total;
 };
 
@@ -69,6 +69,7 @@ __host__ __device__ inline FlLayout fl_layout(int D, int F, int V, int HD, int c
   Y.ktile = o; o = fl_al(o + static_cast<uint32_t>(kSlots) * kChunk * HD * 2, 128);
   Y.vtile = o; o = fl_al(o + static_cast<uint32_t>(kSlots) * kChunk * HD * 2, 128);
   Y.rec = o;   o = fl_al(o + static_cast<uint32_t>(nmax) * (HD + 4) * 4, 128);
+  Y.recw = o;  o = fl_al(o + static_cast<uint32_t>(nmax) * (HD + 2) * 8, 128);  // {value, epoch} records
   Y.slots = o; o = fl_al(o + static_cast<uint32_t>(kSlots) * (kChunk + 8) * 4, 128);
   Y.qkv = o;   o = fl_al(o + 3u * HD * 4, 128);
   Y.qkvw = o;  o = fl_al(o + 2u * 3u * HD * 8, 128);  // {value, epoch} words, by layer parity
@@ -279,11 +280,11 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // One 64-slot chunk of the canonical softmax for one head, by a slot of 64
 // threads (named barrier bar_id), from K/V tiles in shared memory (row t =
 // key k0 + t, HD halves per row): the arithmetic of attn_chunk_slot.  The
-// record {m, l, 0, 0, o[HD]} goes to shared memory address `dst` (any CTA of
-// the cluster).
+// record {m, l, o[HD]}, each a {value, epoch ep} word, goes to shared memory
+// address `dst` (any CTA of the cluster).
 template <int HD>
 __device__ __forceinline__ void fl_chunk(const float* q, const uint16_t* kt, const uint16_t* vt, int nk, float scale,
-                         float* ew, int bar_id, uint32_t dst) {
+                         float* ew, int bar_id, uint32_t dst, uint32_t ep) {
   float* red = ew + kChunk;
   const int t = threadIdx.x & 63, lane = t & 31, w = t >> 5;
   constexpr int kV = HD / 8;
@@ -341,10 +342,11 @@ __device__ __forceinline__ void fl_chunk(const float* q, const uint16_t* kt, con
   }
   const bool do_o = (HD == 64) || (w == 0);
   const bool do_l = (w == 1 && lane == 0);
-  if (do_o) st_cluster_f32(dst + 4u * (4 + d), o);
+  const uint64_t tag = static_cast<uint64_t>(ep) << 32;
+  if (do_o) st_cluster_u64(dst + 8u * (2 + d), tag | __float_as_uint(o));
   if (do_l) {
-    st_cluster_f32(dst, mx);
-    st_cluster_f32(dst + 4u, l);
+    st_cluster_u64(dst, tag | __float_as_uint(mx));
+    st_cluster_u64(dst + 8u, tag | __float_as_uint(l));
   }
   slot_sync(bar_id);
 }
@@ -503,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint16_t* ktile = reinterpret_cast<uint16_t*>(smem + Y.ktile);
   uint16_t* vtile = reinterpret_cast<uint16_t*>(smem + Y.vtile);
   float* rec = reinterpret_cast<float*>(smem + Y.rec);
+  uint64_t* recw = reinterpret_cast<uint64_t*>(smem + Y.recw);
   float* slots = reinterpret_cast<float*>(smem + Y.slots);
   float* qkv = reinterpret_cast<float*>(smem + Y.qkv);
   uint64_t* qkvw = reinterpret_cast<uint64_t*>(smem + Y.qkvw);
@@ -631,6 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   for (int cc = tid; cc < V; cc += kThreads) seen[cc] = 0;
   for (int i = tid; i < 2 * 3 * HD; i += kThreads) qkvw[i] = 0;  // epoch 0 is never used
+  for (int i = tid; i < (cap + kChunk - 1) / kChunk * (HD + 2); i += kThreads) recw[i] = 0;
   __syncthreads();
   for (int i = tid; i < a.n_hist; i += kThreads) {
     const int t = a.hist[i];
@@ -662,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     failed = true;
   failed = __syncthreads_or(failed ? 1 : 0) != 0;
 
-  const uint32_t rec_remote = cluster_addr(rec, 0);  // the merger's chunk records
+  const uint32_t rec_remote = cluster_addr(recw, 0);  // the merger's chunk record words
   unsigned gl = 0;
   int n_out = 0;
   unsigned long long* tr = nullptr;
@@ -784,6 +788,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     const int nch = (len + kChunk - 1) / kChunk;
     const int rounds = (nch + kSlots * cs - 1) / (kSlots * cs);
+    // layer 0's tiles (the first step's were issued before the loop): after
+    // the step's cluster barrier, which orders every K/V row the previous
+    // step stored before these loads
+    if (is_head && !failed && !tiles_armed) {
+      if (tid == 0) issue_tiles(0, nch, 0);
+      tiles_armed = tiles_issued(nch, 0);
+    }
 
     for (int l = 0; l < L; ++l, ++gl) {
       const uint32_t ep = ep_step + 1 + static_cast<uint32_t>(l);
@@ -925,31 +936,58 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             slot_sync(1 + slot);
             fl_chunk<HD>(qkv, kt, vt, min(len - k0, kChunk), m.scale, ew, 1 + slot,
-                         rec_remote + static_cast<uint32_t>(ch) * rec_floats<HD>() * 4u);
+                         rec_remote + static_cast<uint32_t>(ch) * (HD + 2) * 8u, ep);
           }
         }
       }
       GSVK_FTR(16 + 16 * l + 2);
-      if (is_head && rank == cs - 1 && tid == kThreads - 32) bulk_wait<0>();  // the K/V row is in the cache before anyone reads it
-      fl_cluster_sync();
-      GSVK_FTR(16 + 16 * l + 3);
-      if (is_head && rank == 0 && warp == 0) {  // merge the head's chunk records, canonical order
-        float r0, r1;
-        fl_combine<HD>(rec, nch, &r0, &r1);
-        uint64_t* xa = f.xattn + static_cast<size_t>(par) * D + head * HD;
-        xw_put(xa + lane, h2f(f2h(r0)), ep);
-        if (HD > 32) xw_put(xa + 32 + lane, h2f(f2h(r1)), ep);
-        xw_flush();
-      }
-      GSVK_FTR(16 + 16 * l + 13);
-      {  // the next attention's tiles (this step's next layer, or the next step's first)
-        const int nl = l + 1 < L ? l + 1 : 0;
-        const int nn = l + 1 < L ? nch : (len + 1 + kChunk - 1) / kChunk;
-        if (is_head && !failed && !tiles_armed) {
-          if (tid == 0) issue_tiles(nl, nn, 0);
-          tiles_armed = tiles_issued(nn, 0);
+      // the K/V row is in the cache before the next step's cluster barrier,
+      // after which the tiles that read it are issued
+      if (is_head && rank == cs - 1 && tid == kThreads - 32) bulk_wait<0>();
+      if (is_head) {
+        if (rank == 0) {
+          // every member's chunk records ({value, epoch} words in this CTA's
+          // shared memory), polled locally instead of a cluster barrier
+          constexpr int RW = HD + 2, R = rec_floats<HD>();
+          for (int i = tid; i < nch * RW && !failed; i += kThreads) {
+            const uint64_t* w = recw + i;
+            uint64_t v = ld_volatile_shared_u64(w);
+            for (uint32_t it = 0; static_cast<uint32_t>(v >> 32) != ep; ++it) {
+              if (it >= f.spin) {
+                atomicExch(m.status, DEV_TIMEOUT);
+                failed = true;
+                break;
+              }
+              if ((it & 255u) == 255u && *reinterpret_cast<volatile uint32_t*>(m.status) != 0) {
+                failed = true;
+                break;
+              }
+              v = ld_volatile_shared_u64(w);
+            }
+            const int cr = i / RW, k = i - cr * RW;
+            rec[cr * R + (k < 2 ? k : k + 2)] = __uint_as_float(static_cast<uint32_t>(v));
+          }
+          failed = __syncthreads_or(failed ? 1 : 0) != 0;
+          GSVK_FTR(16 + 16 * l + 3);
+          if (warp == 0) {  // merge the head's chunk records, canonical order
+            float r0, r1;
+            fl_combine<HD>(rec, nch, &r0, &r1);
+            uint64_t* xa = f.xattn + static_cast<size_t>(par) * D + head * HD;
+            xw_put(xa + lane, h2f(f2h(r0)), ep);
+            if (HD > 32) xw_put(xa + 32 + lane, h2f(f2h(r1)), ep);
+            xw_flush();
+          }
+        } else {
+          __syncthreads();  // every slot is done with the tiles before they are refilled
+        }
+        // the next layer's tiles (the next step's first layer: after that
+        // step's cluster barrier)
+        if (l + 1 < L && !failed && !tiles_armed) {
+          if (tid == 0) issue_tiles(l + 1, nch, 0);
+          tiles_armed = tiles_issued(nch, 0);
         }
       }
+      GSVK_FTR(16 + 16 * l + 13);
       // ------------------------------------------------ out-proj rows
       if (!fl_poll(f.xattn + static_cast<size_t>(par) * D, D, ep, act, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 4);
