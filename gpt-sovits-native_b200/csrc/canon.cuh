@@ -91,31 +91,37 @@ __device__ __forceinline__ float group16_dot_kv(const float* q_reg, const uint16
 // 1 / sqrt(v) rounded to float exactly as (float)(1.0 / sqrt(v)) with both
 // double operations correctly rounded (kern.cpp:55).
 //
-// Fast path: a float candidate r (the float reciprocal square root, then
-// moved an ulp at a time) is accepted when y = 1/sqrt(v) lies strictly inside
+// A float candidate r is accepted when y = 1/sqrt(v) lies strictly inside
 // (m_lo, m_hi), the midpoints between r and its float neighbours, with a
 // relative margin of at least 2^-48.  The test is exact: m has at most 25
 // significant bits, so m*m is exact in double, and y < m <=> m^2 v > 1, whose
 // sign one fused multiply-add m^2 v - 1 gives exactly (its value s is also
 // accurate: (m - y) / y ~ s / 2).  The reference value (two correctly rounded
 // double operations) lies within 2^-51 * y of y, so it rounds to r as well.
-// Otherwise (y within the margin of a midpoint, about one call in 2^23, or a
-// non-finite or zero candidate) the exact sqrt-then-divide path decides.
+// The candidate is the float reciprocal square root refined by one Newton
+// step in double (then almost always the nearest float, so one test
+// suffices); a failed test moves it one ulp and tests again, and a y within
+// the margin of a midpoint (about one call in 2^23), or a non-finite or zero
+// candidate, takes the exact sqrt-then-divide path.  The test alone decides
+// correctness: the candidate's accuracy only decides the speed.
 __device__ __forceinline__ float rstd_f32(double v) {
-  float r = rsqrtf(__double2float_rn(v));
+  const double y0 = static_cast<double>(rsqrtf(__double2float_rn(v)));
+  const double y1 = y0 * fma(-0.5 * v * y0, y0, 1.5);
+  float r = __double2float_rn(y1);
 #pragma unroll 1
-  for (int step = 0; step < 4; ++step) {
+  for (int step = 0; step < 3; ++step) {
     if (!(r > 0.0f) || isinf(r)) break;
+    const int bits = __float_as_int(r);  // r positive and finite: neighbours by integer steps
     const double rd = static_cast<double>(r);
-    const double mhi = 0.5 * (rd + static_cast<double>(nextafterf(r, INFINITY)));
-    const double mlo = 0.5 * (rd + static_cast<double>(nextafterf(r, 0.0f)));
+    const double mhi = 0.5 * (rd + static_cast<double>(__int_as_float(bits + 1)));
+    const double mlo = 0.5 * (rd + static_cast<double>(__int_as_float(bits - 1)));
     const double shi = fma(mhi * mhi, v, -1.0);  // > 0  <=>  y < mhi
     const double slo = fma(mlo * mlo, v, -1.0);  // < 0  <=>  y > mlo
     if (shi > 0x1p-46 && slo < -0x1p-46) return r;
     if (shi <= 0.0)
-      r = nextafterf(r, INFINITY);
+      r = __int_as_float(bits + 1);
     else if (slo >= 0.0)
-      r = nextafterf(r, 0.0f);
+      r = __int_as_float(bits - 1);
     else
       break;  // y within the margin of a midpoint
   }
