@@ -304,6 +304,90 @@ __device__ __forceinline__ float warp_dot512_r(const uint16_t* w, const float* x
   return s;
 }
 
+// fp32(a) * fp32(b) + c rounded once, a and b fp16 bits: the product of two
+// fp16 values is exact in fp32, so this equals fmaf(h2f(a), h2f(b), c)
+// without the two conversions (mixed-precision fma).
+__device__ __forceinline__ float fma_hh(uint16_t a, uint16_t b, float c) {
+  float d;
+  asm("{\n\t.reg .f16 ha, hb;\n\tmov.b16 ha, %1;\n\tmov.b16 hb, %2;\n\t"
+      "fma.rn.f32.f16 %0, ha, hb, %3;\n\t}"
+      : "=f"(d)
+      : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+
+// This lane's 16 activations (lane_act512 layout) as fp16 bits, rounded to
+// nearest even from the fp32 values (optionally through a LayerNorm).
+__device__ __forceinline__ void lane_act512_h(const float* x, bool ln, float mean, float rstd, const float* g,
+                                              const float* b, uint16_t* xh) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+#pragma unroll
+  for (int k = 0; k < 16; k += 2) {
+    const int i = 64 * (k >> 1) + o0;
+    float v0 = x[i], v1 = x[i + 4];
+    if (ln) {
+      v0 = ln_val(v0, mean, rstd, g[i], b[i]);
+      v1 = ln_val(v1, mean, rstd, g[i + 4], b[i + 4]);
+    }
+    const uint32_t p = f2h2(v0, v1);  // one conversion for both
+    xh[k] = static_cast<uint16_t>(p & 0xffffu);
+    xh[k + 1] = static_cast<uint16_t>(p >> 16);
+  }
+}
+
+// warp_dot512_r for fp16 activations xh (bits): the same chain and result.
+__device__ __forceinline__ float warp_dot512_h(const uint16_t* w, const uint16_t* xh) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+  uint16_t wv[16];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    wv[2 * b] = w[64 * b + o0];
+    wv[2 * b + 1] = w[64 * b + o0 + 4];
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc = fma_hh(wv[j], xh[j], acc);
+  const float t = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+  const float u = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+  float s = __shfl_sync(0xffffffffu, u, 0);
+#pragma unroll
+  for (int j = 1; j < 8; ++j) s = __fadd_rn(s, __shfl_sync(0xffffffffu, u, 4 * j));
+  return s;
+}
+__device__ __forceinline__ void warp_dot512x2_h(const uint16_t* w0, const uint16_t* w1, const uint16_t* xh,
+                                                float* r0, float* r1) {
+  const int lane = threadIdx.x & 31;
+  const int o0 = 8 * (lane >> 2) + (lane & 3);
+  uint16_t u0[16], u1[16];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    u0[2 * b] = w0[64 * b + o0];
+    u0[2 * b + 1] = w0[64 * b + o0 + 4];
+    u1[2 * b] = w1[64 * b + o0];
+    u1[2 * b + 1] = w1[64 * b + o0 + 4];
+  }
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    a0 = fma_hh(u0[j], xh[j], a0);
+    a1 = fma_hh(u1[j], xh[j], a1);
+  }
+  float t0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
+  float t1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+  t0 = __fadd_rn(t0, __shfl_xor_sync(0xffffffffu, t0, 2));
+  t1 = __fadd_rn(t1, __shfl_xor_sync(0xffffffffu, t1, 2));
+  float s0 = __shfl_sync(0xffffffffu, t0, 0), s1 = __shfl_sync(0xffffffffu, t1, 0);
+#pragma unroll
+  for (int j = 1; j < 8; ++j) {
+    s0 = __fadd_rn(s0, __shfl_sync(0xffffffffu, t0, 4 * j));
+    s1 = __fadd_rn(s1, __shfl_sync(0xffffffffu, t1, 4 * j));
+  }
+  *r0 = s0;
+  *r1 = s1;
+}
+
 // Two of them sharing the activations (chains interleaved).
 __device__ __forceinline__ void warp_dot512x2_r(const uint16_t* w0, const uint16_t* w1, const float* xr,
                                                 float* r0, float* r1) {

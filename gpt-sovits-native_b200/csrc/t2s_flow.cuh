@@ -188,19 +188,19 @@ __device__ __forceinline__ void fl_w1_rows(const uint16_t* W1, const float* h, f
     const float v = __fadd_rn(acc, bias[r - a0]);
     xw_put(xf + r, v > 0.f ? v : 0.f, ep);
   };
-  float xr[16];
-  lane_act512(h, true, mean, rstd, g, b, true, xr);
+  uint16_t xh[16];  // fp16 activations: mixed-precision fma, no conversions
+  lane_act512_h(h, true, mean, rstd, g, b, xh);
   for (int r = a0 + 2 * warp; r < a1; r += 2 * kWarps) {
     if (r + 1 < a1) {
       float r0, r1;
-      warp_dot512x2_r(W1 + static_cast<size_t>(r - a0) * D, W1 + static_cast<size_t>(r + 1 - a0) * D, xr,
+      warp_dot512x2_h(W1 + static_cast<size_t>(r - a0) * D, W1 + static_cast<size_t>(r + 1 - a0) * D, xh,
                       &r0, &r1);
       if (lane == 0) {
         put(r, r0);
         put(r + 1, r1);
       }
     } else {
-      const float r0 = warp_dot512_r(W1 + static_cast<size_t>(r - a0) * D, xr);
+      const float r0 = warp_dot512_h(W1 + static_cast<size_t>(r - a0) * D, xh);
       if (lane == 0) put(r, r0);
     }
   }
@@ -843,17 +843,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             st_cluster_u64(cluster_addr(qkvw + par * 3 * HD + j, lane),
                            (static_cast<uint64_t>(ep) << 32) | __float_as_uint(val));
         };
-        float xr[16];  // fp16-rounded activations (the reference's fp16 x)
-        lane_act512(xs, ln2, mu2, rs2, lnb + 2 * D, lnb + 3 * D, true, xr);
+        uint16_t xh[16];  // fp16 activations (the reference's fp16 x)
+        lane_act512_h(xs, ln2, mu2, rs2, lnb + 2 * D, lnb + 3 * D, xh);
         for (int j = j0 + 2 * warp; j < j1; j += 2 * kWarps) {
           if (j + 1 < j1) {
             float r0, r1;
-            warp_dot512x2_r(Wq + static_cast<size_t>(j - j0) * D, Wq + static_cast<size_t>(j + 1 - j0) * D,
-                            xr, &r0, &r1);
+            warp_dot512x2_h(Wq + static_cast<size_t>(j - j0) * D, Wq + static_cast<size_t>(j + 1 - j0) * D,
+                            xh, &r0, &r1);
             put(j, r0);
             put(j + 1, r1);
           } else {
-            put(j, warp_dot512_r(Wq + static_cast<size_t>(j - j0) * D, xr));
+            put(j, warp_dot512_h(Wq + static_cast<size_t>(j - j0) * D, xh));
           }
         }
       }
@@ -992,10 +992,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!fl_poll(f.xattn + static_cast<size_t>(par) * D, D, ep, act, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 4);
       if (o0 + warp < o1) {
-        float xr[16];
-        lane_act512(act, false, 0.f, 0.f, nullptr, nullptr, false, xr);
+        uint16_t xh[16];  // the attention output: fp16 values, exact as fp16 bits
+        lane_act512_h(act, false, 0.f, 0.f, nullptr, nullptr, xh);
         for (int r = o0 + warp; r < o1; r += kWarps) {
-          const float acc = warp_dot512_r(Wo + static_cast<size_t>(r - o0) * D, xr);
+          const float acc = warp_dot512_h(Wo + static_cast<size_t>(r - o0) * D, xh);
           if (lane == 0) {
             // the residual: this layer's input row (LN2 output of layer l - 1)
             const float xin = ln2 ? ln_val(xs[r], mu2, rs2, lnb[2 * D + r], lnb[3 * D + r]) : xs[r];
