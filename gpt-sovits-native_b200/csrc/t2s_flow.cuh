@@ -826,12 +826,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         GSVK_FTR(16 + 16 * l + 15);
       }
       failed = __syncthreads_or(failed ? 1 : 0) != 0;  // one decision for the whole CTA
-      // LN2 of layer l - 1 (layer 0 takes its input as it is): every warp
-      // forms the statistics itself and normalises the elements it reads, so
-      // xs keeps the raw rows and no CTA barrier separates LN2 from the dots
+      // LN2 of layer l - 1 (layer 0 takes its input as it is): warp 0 forms
+      // the statistics (one warp's chain loads instead of eight warps'
+      // competing for shared memory), the CTA reads them after one barrier,
+      // and every lane normalises only the elements its dots read, so xs
+      // keeps the raw rows
       const bool ln2 = l > 0;
       float mu2 = 0.f, rs2 = 0.f;
-      if (ln2) warp_ln_stats(xs, kFlD, m.eps, &mu2, &rs2);
+      if (ln2) {  // warp 0 forms the statistics, the CTA reads them
+        if (warp == 0) {
+          warp_ln_stats(xs, kFlD, m.eps, &mu2, &rs2);
+          if (lane == 0) {
+            red[48] = mu2;
+            red[49] = rs2;
+          }
+        }
+        __syncthreads();
+        mu2 = red[48];
+        rs2 = red[49];
+      }
       GSVK_FTR(16 + 16 * l + 10);
       {
         auto put = [&](int j, float acc) {
@@ -1008,9 +1021,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------- LN1, W1 rows + ReLU
       if (!fl_poll(f.xhpre + static_cast<size_t>(par) * D, D, ep, hs, m.status, failed, f.spin)) failed = true;
       GSVK_FTR(16 + 16 * l + 5);
-      // LN1 per warp as LN2 above: hs keeps the raw rows
+      // LN1 as LN2 above: hs keeps the raw rows
       float mu1, rs1;
-      warp_ln_stats(hs, kFlD, m.eps, &mu1, &rs1);
+      if (warp == 0) {
+        warp_ln_stats(hs, kFlD, m.eps, &mu1, &rs1);
+        if (lane == 0) {
+          red[50] = mu1;
+          red[51] = rs1;
+        }
+      }
+      __syncthreads();
+      mu1 = red[50];
+      rs1 = red[51];
       GSVK_FTR(16 + 16 * l + 12);
       fl_w1_rows(W1, hs, mu1, rs1, lnb, lnb + D, a0, a1, D, bsm + nq + no, f.xff + static_cast<size_t>(par) * F,
                  ep);
