@@ -247,7 +247,7 @@ size_t attn_stream_smem_bytes(int D, int H, int B) {
   return static_cast<size_t>(kAttnStages) * kSChunk * D * 2 * 2 +  // K, V ring
          static_cast<size_t>(kAttnThreads / 32) * 256 * 4 +            // PV partials
          (static_cast<size_t>(H) * (kSChunk + 1) + 4 * H) * 4 +     // P, max/sum/scale
-         static_cast<size_t>(B + 1 + 2 * kAttnStages) * 4 + 64;        // item offsets, slots
+         static_cast<size_t>(2 * B + 1 + 2 * kAttnStages) * 4 + 64;    // item offsets, lengths, slots
 }
 
 template <int NSEG>
@@ -272,6 +272,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   int* sOff = reinterpret_cast<int*>(sSc + H);     // [B + 1] first item of each utterance
   int* sItem = sOff + B + 1;                       // [kAttnStages] item of the slot's chunk (-1: none)
   int* sChunk = sItem + kAttnStages;               // [kAttnStages] chunk index in its utterance
+  int* sLen = sChunk + kAttnStages;                // [B] keys of each utterance this step (the
+                                                   // per-chunk paths read it, not global memory)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   if (tid == 0) {
@@ -279,8 +281,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     fence_barrier_init();
     int acc = 0;
     for (int b = 0; b < B; ++b) {
+      const int len = m.base_len[b] + s + 1;
+      sLen[b] = len;
       sOff[b] = acc;
-      acc += (m.base_len[b] + s + 1 + kAttnSplitKeys - 1) / kAttnSplitKeys;
+      acc += (len + kAttnSplitKeys - 1) / kAttnSplitKeys;
     }
     sOff[B] = acc;
   }
@@ -313,7 +317,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         break;
       }
       const int b = item_utt(it), sp = it - sOff[b];
-      const int nch = (m.base_len[b] + s + 1 + kSChunk - 1) / kSChunk;
+      const int nch = (sLen[b] + kSChunk - 1) / kSChunk;
       p_item = it;
       p_c = sp * kAttnSplitChunks;
       p_cend = min(nch, p_c + kAttnSplitChunks);
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       mbar_arrive(&full[sl]);  // completes the phase with no copy: the consumers stop here
     } else {
       const int b = item_utt(p_item);
-      const int len = m.base_len[b] + s + 1;
+      const int len = sLen[b];
       const int k0 = p_c * kSChunk, rows = min(kSChunk, len - k0);
       const size_t slab = (static_cast<size_t>(b) * m.L + l) * m.cap + k0;
       const uint32_t bytes = static_cast<uint32_t>(rows) * D * 2;
@@ -373,7 +377,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     if (it < 0) break;
     const int c = sChunk[sl];
     const int b = item_utt(it), sp = it - sOff[b];
-    const int len = m.base_len[b] + s + 1;
+    const int len = sLen[b];
     const int nch = (len + kSChunk - 1) / kSChunk;
     const int nsplit = sOff[b + 1] - sOff[b];
     const int k0 = c * kSChunk, rows = min(kSChunk, len - k0);
