@@ -233,7 +233,10 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attn_kernel(BatchDev m, in
 // +kAttnSplitKeys) of b, all heads.  Thread 0 keeps kAttnStages chunk
 // copies (16 keys of K and of V, two 1D bulk copies) in flight across items:
 // each CTA's first item is fixed (its block index), later ones come from a
-// per-layer work counter (zeroed by the step's embedding kernel).  Within an
+// per-layer work counter (zeroed by the step's embedding kernel).  Items are
+// handed out longest first: every full split (kAttnSplitChunks chunks), then
+// each utterance's shorter last split by decreasing length, so the CTAs that
+// take a second item take short ones and finish together.  Within an
 // item the softmax runs online over its chunks (running max / sum per head,
 // accumulator rescaled); a one-split utterance writes its output directly,
 // otherwise each split writes (max, sum, unnormalised output) per head and the
@@ -247,7 +250,7 @@ size_t attn_stream_smem_bytes(int D, int H, int B) {
   return static_cast<size_t>(kAttnStages) * kSChunk * D * 2 * 2 +  // K, V ring
          static_cast<size_t>(kAttnThreads / 32) * 256 * 4 +            // PV partials
          (static_cast<size_t>(H) * (kSChunk + 1) + 4 * H) * 4 +     // P, max/sum/scale
-         static_cast<size_t>(2 * B + 1 + 2 * kAttnStages) * 4 + 64;    // item offsets, lengths, slots
+         static_cast<size_t>(4 * B + 2 + 2 * kAttnStages) * 4 + 64;    // item offsets, lengths, order, slots
 }
 
 template <int NSEG>
@@ -274,22 +277,41 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   int* sChunk = sItem + kAttnStages;               // [kAttnStages] chunk index in its utterance
   int* sLen = sChunk + kAttnStages;                // [B] keys of each utterance this step (the
                                                    // per-chunk paths read it, not global memory)
+  int* sFull = sLen + B;                           // [B + 1] first full split of each utterance,
+                                                   // in dispatch order
+  int* sShort = sFull + B + 1;                     // [B] utterances with a short last split,
+                                                   // longest first
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   if (tid == 0) {
     for (int i = 0; i < kAttnStages; ++i) mbar_init(&full[i], 1);
     fence_barrier_init();
-    int acc = 0;
+    int acc = 0, full = 0;
     for (int b = 0; b < B; ++b) {
       const int len = m.base_len[b] + s + 1;
       sLen[b] = len;
       sOff[b] = acc;
+      sFull[b] = full;
       acc += (len + kAttnSplitKeys - 1) / kAttnSplitKeys;
+      full += len / kAttnSplitKeys;
     }
     sOff[B] = acc;
+    sFull[B] = full;
   }
   __syncthreads();
-  const int n_items = sOff[B];
+  const int n_items = sOff[B], n_full = sFull[B];
+  // rank of each short last split: longer first, then by utterance
+  for (int b = tid; b < B; b += kAttnThreads) {
+    const int rb = sLen[b] % kAttnSplitKeys;
+    if (rb == 0) continue;
+    int rank = 0;
+    for (int o = 0; o < B; ++o) {
+      const int ro = sLen[o] % kAttnSplitKeys;
+      rank += (ro > rb || (ro == rb && o < b)) ? 1 : 0;
+    }
+    sShort[rank] = b;
+  }
+  __syncthreads();
   auto item_utt = [&](int it) {  // the utterance of item `it` (binary search)
     int lo = 0, hi = B - 1;
     while (lo < hi) {
@@ -297,6 +319,20 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       if (sOff[mid] <= it) lo = mid; else hi = mid - 1;
     }
     return lo;
+  };
+  // the item handed out d-th: full splits in utterance order, then the short
+  // last splits as ranked above
+  auto dispatch_item = [&](int d) {
+    if (d >= n_full) {
+      const int b = sShort[d - n_full];
+      return sOff[b + 1] - 1;
+    }
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sFull[mid] <= d) lo = mid; else hi = mid - 1;
+    }
+    return sOff[lo] + (d - sFull[lo]);
   };
   // ---- producer (thread 0): the CTA's chunk sequence, one slot at a time
   int p_item = -1, p_c = 0, p_cend = 0, p_grab = 0, p_n = 0;
@@ -316,6 +352,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         p_done = true;
         break;
       }
+      it = dispatch_item(it);
       const int b = item_utt(it), sp = it - sOff[b];
       const int nch = (sLen[b] + kSChunk - 1) / kSChunk;
       p_item = it;
