@@ -250,7 +250,15 @@ size_t attn_stream_smem_bytes(int D, int H, int B) {
   return static_cast<size_t>(kAttnStages) * kSChunk * D * 2 * 2 +  // K, V ring
          static_cast<size_t>(kAttnThreads / 32) * 256 * 4 +            // PV partials
          (static_cast<size_t>(H) * (kSChunk + 1) + 4 * H) * 4 +     // P, max/sum/scale
-         static_cast<size_t>(4 * B + 2 + 2 * kAttnStages) * 4 + 64;    // item offsets, lengths, order, slots
+         static_cast<size_t>(4 * B + 2 + 3 * kAttnStages) * 4 + 64;    // item offsets, lengths, order, slots
+}
+
+// Maximum over the warp in one instruction (sm_100a's floating-point
+// redux); exact, like the fmaxf butterfly it replaces.
+__device__ __forceinline__ float warp_max_redux(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
 }
 
 template <int NSEG>
@@ -281,6 +289,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
                                                    // in dispatch order
   int* sShort = sFull + B + 1;                     // [B] utterances with a short last split,
                                                    // longest first
+  int* sUtt = sShort + B;                          // [kAttnStages] utterance of the slot's chunk
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   if (tid == 0) {
@@ -335,7 +344,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     return sOff[lo] + (d - sFull[lo]);
   };
   // ---- producer (thread 0): the CTA's chunk sequence, one slot at a time
-  int p_item = -1, p_c = 0, p_cend = 0, p_grab = 0, p_n = 0;
+  int p_item = -1, p_b = 0, p_c = 0, p_cend = 0, p_grab = 0, p_n = 0;
   bool p_done = false;
   auto produce = [&](bool dynamic) -> bool {  // false: nothing issued (needs the work counter)
     const int sl = p_n % kAttnStages;
@@ -356,6 +365,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       const int b = item_utt(it), sp = it - sOff[b];
       const int nch = (sLen[b] + kSChunk - 1) / kSChunk;
       p_item = it;
+      p_b = b;
       p_c = sp * kAttnSplitChunks;
       p_cend = min(nch, p_c + kAttnSplitChunks);
     }
@@ -363,12 +373,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       sItem[sl] = -1;
       mbar_arrive(&full[sl]);  // completes the phase with no copy: the consumers stop here
     } else {
-      const int b = item_utt(p_item);
+      const int b = p_b;
       const int len = sLen[b];
       const int k0 = p_c * kSChunk, rows = min(kSChunk, len - k0);
       const size_t slab = (static_cast<size_t>(b) * m.L + l) * m.cap + k0;
       const uint32_t bytes = static_cast<uint32_t>(rows) * D * 2;
       sItem[sl] = p_item;
+      sUtt[sl] = p_b;
       sChunk[sl] = p_c;
       mbar_arrive_expect_tx(&full[sl], 2 * bytes);
       bulk_load(kbuf + static_cast<size_t>(sl) * kSChunk * D, m.kc + slab * D, bytes, &full[sl]);
@@ -413,7 +424,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const int it = sItem[sl];
     if (it < 0) break;
     const int c = sChunk[sl];
-    const int b = item_utt(it), sp = it - sOff[b];
+    const int b = sUtt[sl], sp = it - sOff[b];
     const int len = sLen[b];
     const int nch = (len + kSChunk - 1) / kSChunk;
     const int nsplit = sOff[b + 1] - sOff[b];
@@ -484,12 +495,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       const bool in = lane < rows;
       const float s0 = in && one ? p0[lane] : -INFINITY;
       const float s1 = in && two ? p1[lane] : -INFINITY;
-      float mx0 = s0, mx1 = s1;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-      }
+      const float mx0 = warp_max_redux(s0), mx1 = warp_max_redux(s1);
       const float mo0 = one ? sMr[h0] : 0.f, mo1 = two ? sMr[h1] : 0.f;
       const float mn0 = fmaxf(mo0, mx0), mn1 = fmaxf(mo1, mx1);
       const float ev0 = in && one ? expf(s0 - mn0) : 0.f, ev1 = in && two ? expf(s1 - mn1) : 0.f;
