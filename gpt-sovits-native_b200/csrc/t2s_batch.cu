@@ -487,37 +487,27 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       }
     }
     __syncthreads();
-    {  // online softmax of heads warp and warp + 8 (both chains interleaved)
-      const int h0 = warp, h1 = warp + kAttnThreads / 32;
-      const bool one = h0 < H, two = h1 < H;
-      float* p0 = sP + (one ? h0 : 0) * (kSChunk + 1);
-      float* p1 = sP + (two ? h1 : 0) * (kSChunk + 1);
-      const bool in = lane < rows;
-      const float s0 = in && one ? p0[lane] : -INFINITY;
-      const float s1 = in && two ? p1[lane] : -INFINITY;
-      const float mx0 = warp_max_redux(s0), mx1 = warp_max_redux(s1);
-      const float mo0 = one ? sMr[h0] : 0.f, mo1 = two ? sMr[h1] : 0.f;
-      const float mn0 = fmaxf(mo0, mx0), mn1 = fmaxf(mo1, mx1);
-      const float ev0 = in && one ? expf(s0 - mn0) : 0.f, ev1 = in && two ? expf(s1 - mn1) : 0.f;
-      if (in && one) p0[lane] = ev0;
-      if (in && two) p1[lane] = ev1;
-      float su0 = ev0, su1 = ev1;
+    {  // online softmax: lanes 0-15 take head `warp`, lanes 16-31 head
+       // `warp + 8`, one key per lane (the sums are the same butterflies)
+      static_assert(kSChunk == 16, "one key per half-warp lane");
+      const int hh = warp + (lane >> 4) * (kAttnThreads / 32), r = lane & 15;
+      const bool ok = hh < H, in = ok && r < rows;
+      float* ph = sP + (ok ? hh : 0) * (kSChunk + 1);
+      const float sv = in ? ph[r] : -INFINITY;
+      const float mx0 = warp_max_redux(lane < 16 ? sv : -INFINITY);
+      const float mx1 = warp_max_redux(lane < 16 ? -INFINITY : sv);
+      const float mo = ok ? sMr[hh] : 0.f;
+      const float mn = fmaxf(mo, lane < 16 ? mx0 : mx1);
+      const float ev = in ? expf(sv - mn) : 0.f;
+      if (in) ph[r] = ev;
+      float su = ev;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        su0 += __shfl_xor_sync(0xffffffffu, su0, o);
-        su1 += __shfl_xor_sync(0xffffffffu, su1, o);
-      }
-      if (lane == 0 && one) {
-        const float sc = mo0 == -INFINITY ? 0.f : expf(mo0 - mn0);
-        sSc[h0] = sc;
-        sLr[h0] = fmaf(sLr[h0], sc, su0);
-        sMr[h0] = mn0;
-      }
-      if (lane == 0 && two) {
-        const float sc = mo1 == -INFINITY ? 0.f : expf(mo1 - mn1);
-        sSc[h1] = sc;
-        sLr[h1] = fmaf(sLr[h1], sc, su1);
-        sMr[h1] = mn1;
+      for (int o = 8; o > 0; o >>= 1) su += __shfl_xor_sync(0xffffffffu, su, o);
+      if (r == 0 && ok) {
+        const float sc = mo == -INFINITY ? 0.f : expf(mo - mn);
+        sSc[hh] = sc;
+        sLr[hh] = fmaf(sLr[hh], sc, su);
+        sMr[hh] = mn;
       }
     }
     __syncthreads();
