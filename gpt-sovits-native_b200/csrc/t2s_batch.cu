@@ -253,14 +253,6 @@ size_t attn_stream_smem_bytes(int D, int H, int B) {
          static_cast<size_t>(4 * B + 2 + 3 * kAttnStages) * 4 + 64;    // item offsets, lengths, order, slots
 }
 
-// Maximum over the warp in one instruction (sm_100a's floating-point
-// redux); exact, like the fmaxf butterfly it replaces.
-__device__ __forceinline__ float warp_max_redux(float v) {
-  float r;
-  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
-  return r;
-}
-
 template <int NSEG>
 __global__ void __launch_bounds__(kAttnThreads, 2)
     batch_attn_stream_kernel(BatchDev m, int l, const float* __restrict__ qkv,
@@ -494,8 +486,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       const bool ok = hh < H, in = ok && r < rows;
       float* ph = sP + (ok ? hh : 0) * (kSChunk + 1);
       const float sv = in ? ph[r] : -INFINITY;
-      const float mx0 = warp_max_redux(lane < 16 ? sv : -INFINITY);
-      const float mx1 = warp_max_redux(lane < 16 ? -INFINITY : sv);
+      const float mx0 = warp_max(lane < 16 ? sv : -INFINITY);
+      const float mx1 = warp_max(lane < 16 ? -INFINITY : sv);
       const float mo = ok ? sMr[hh] : 0.f;
       const float mn = fmaxf(mo, lane < 16 ? mx0 : mx1);
       const float ev = in ? expf(sv - mn) : 0.f;
