@@ -212,7 +212,7 @@ def workload_meta(args, world):
                            "2048x512, 512x2048} + 1025x512)",
                     unit="GB/s", dtype="f16 weights, f32 x and accumulate",
                     data="synthetic (seeded N(0,0.02) weights, N(0,1) x)",
-                    config={"workload": "gemv_t2s (the T2S decode GEMV shapes, SURVEY 8d)",
+                    config={"workload": "gemv_t2s (the T2S decode GEMV shapes)",
                             "launch": "CUDA graph of one token's 97 gemv_f16w_f32acc launches",
                             "global_batch": world, "parallelism": f"replicas x{world}",
                             "l2": f"{GEMV_SETS} rotated copies of the 152 MB weight set (> L2)"})
