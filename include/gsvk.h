@@ -514,6 +514,8 @@ size_t gsvk_sv_embedding_size(gsvk_sv_t h);
  * (channel-major [C4][F4], SvEngine::emb_out). */
 int gsvk_sv_forward(gsvk_sv_t h, const float* fbank, size_t frames, float* emb,
                     gsvk_stream_t stream);
+
+/* ---- T2S autoregressive transformer: lifetime, generation, switches ----- */
 int gsvk_t2s_destroy(gsvk_t2s_t h);
 /* Copies a KV prefix (fp16 [L][src_rows][D] for K and V, host or device
  * memory) into slots [0, prefix) of every layer's cache. */
@@ -647,6 +649,7 @@ int gsvk_t2s_batch_launches_per_step(gsvk_t2s_batch_t h);
 int gsvk_t2s_batch_set_attention(gsvk_t2s_batch_t h, int kind);
 int gsvk_t2s_batch_attention(gsvk_t2s_batch_t h);
 
+/* ---- T2S inspection (synchronous reads of the batch-1 engine) ----------- */
 /* The logits the last step sampled from (raw, before the penalty); synchronous. */
 int gsvk_t2s_read_logits(gsvk_t2s_t h, float* host_out);
 /* The whole KV cache, fp16 [n_layers][cap][d_model] each (the layout of
